@@ -1,0 +1,513 @@
+#!/usr/bin/env python
+"""Benchmark: the QORA-4B 32-layer token-mixer stack in decode (workload 4).
+
+One step = one new token for each of B=64 independent sequences per GPU
+through all 32 mixer layers (3 x DeltaNet + 1 x GQA, 8 times), at context
+32768: 24 fp32 DeltaNet states [32,128,128] and 8 bf16 KV caches
+[4,32768,256] per sequence, seeded N(0, 0.02); per-layer inputs N(0, 1)
+with the value distributions of workloads 0 and 1 (synthetic; random-init
+layer parameters).  Sequences are sharded across GPUs with no collective,
+so every rank carries its own 64 sequences (weak scaling; --strong keeps
+64 sequences in total).
+
+value  = tokens/s of the whole job with inputs resident in HBM.
+e2e    = the same through the C ABI's _host entry points: every layer call
+         copies its inputs from pinned host memory and its output back.
+roofline = the dominant kernel (split-KV GQA attention) against the
+         measured HBM copy bandwidth.
+cpu_baseline = the CPU restatement of the reference mixer path on a bounded
+         sample (rank 0, N=1 only).
+
+--impl reference times that CPU restatement as the reference arm (the
+reference is Rust and cannot be built here).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "qora-llm-4b_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = json.load(open(os.path.join(ROOT, "BASELINE.json")))["metric"]
+UNIT = "tok/s"
+CTX = 32768
+B_PER_GPU = 64
+LAYERS = ["dn", "dn", "dn", "attn"] * 8
+WORKLOAD = "mixer-stack decode: 32 layers (24 DeltaNet + 8 GQA), ctx 32768"
+
+# algorithmic bytes (reference algorithm, minimal traffic)
+DN_BYTES_TOKEN = 2 * 32 * 128 * 128 * 4 + 2 * 8192 * 3 * 4 + 8192 * 4 + 2 * 32 * 4 + 2 * 4096 * 4
+
+
+def attn_bytes(B, L):
+    """K and V of L cached positions, 4 KV heads x 256 dims bf16, per sequence."""
+    return B * 2 * 4 * L * 256 * 2
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        return json.load(open(p))
+    return {}
+
+
+# ----------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ----------------------------------------------------------------------------
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# distributed plumbing
+# ----------------------------------------------------------------------------
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def init_dist(ws, local):
+    import torch
+
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x, ws):
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------
+# the stack
+# ----------------------------------------------------------------------------
+class Stack:
+    """24 DeltaNet states + 8 KV caches for B sequences, with per-layer params and inputs."""
+
+    def __init__(self, ctx, B, cap, seed):
+        import numpy as np
+        import torch
+
+        import qora_mixer as qm
+        from qora_mixer import inputs as I
+
+        self.qm, self.B = qm, B
+        self.ctx, self.mx = ctx, qm.Mixer(ctx)
+        g = I.rng(4, stream=seed)
+        cos, sin = qm.rope_table(1.0e7, 64, cap + 1)
+        self.rope = (torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda())
+        self.layers = []
+        dseed = 0x51A4 * 1000 + seed * 100
+        for li, kind in enumerate(LAYERS):
+            L = {}
+            if kind == "dn":
+                p = I.dn_layer_params(g)
+                L["keep"] = [torch.from_numpy(p[k]).cuda() for k in ("conv_w", "a_log", "dt_bias", "norm_gamma")]
+                L["prm"] = qm.dn_params(*L["keep"])
+                s = I.device_normal_f32((B, 32, 128, 128), dseed + li, 0.02)
+                cv = torch.zeros(B, 4, 8192, device="cuda")
+                cv[:, 1:] = I.device_normal_f32((B, 3, 8192), dseed + 50 + li, 0.02)
+                L["store"] = (s, cv)
+                L["st"] = qm.DnState(ctx, B, s, cv)
+                L["st"].conv_pos = CTX  # slots (CTX-3..CTX-1) % 4 = 1..3 hold the history
+                tok = I.dn_token_inputs(g, 1, B)
+                L["in"] = [torch.from_numpy(np.ascontiguousarray(tok[k][:, 0])).cuda()
+                           for k in ("qkv", "a", "b", "z")]
+                L["out"] = torch.empty(B, 4096, device="cuda")
+            else:
+                p = I.gqa_layer_params(g, cap + 1)
+                L["keep"] = [torch.from_numpy(p["q_norm"]).cuda(), torch.from_numpy(p["k_norm"]).cuda(), *self.rope]
+                L["prm"] = qm.gqa_params(*L["keep"])
+                K = I.device_normal_bf16((B, 4, cap, 256), dseed + li, 0.02).view(torch.int16)
+                V = I.device_normal_bf16((B, 4, cap, 256), dseed + 70 + li, 0.02).view(torch.int16)
+                L["store"] = (K, V)
+                L["kv"] = qm.KvCache(ctx, B, cap, K, V)
+                L["kv"].seq_len = CTX
+                tok = I.gqa_token_inputs(g, B)
+                L["in"] = [torch.from_numpy(tok[k]).cuda() for k in ("q_gate", "k_new", "v_new")]
+                L["out"] = torch.empty(B, 16, 256, device="cuda")
+            L["kind"] = kind
+            self.layers.append(L)
+        torch.cuda.synchronize()
+
+    def step(self):
+        mx = self.mx
+        for L in self.layers:
+            if L["kind"] == "dn":
+                qkv, a, b, z = L["in"]
+                mx.dn_decode(L["prm"], L["st"], qkv, a, b, None, z, L["out"])
+            else:
+                mx.gqa_decode(L["prm"], L["kv"], *L["in"], L["out"])
+
+    def make_host_io(self):
+        """Pinned host copies of every layer's inputs and outputs (for e2e)."""
+        import torch
+
+        for L in self.layers:
+            L["hin"] = [t.cpu().pin_memory() for t in L["in"]]
+            L["hout"] = torch.empty(L["out"].shape, dtype=torch.float32).pin_memory()
+        h2d = sum(t.numel() * 4 for L in self.layers for t in L["hin"])
+        d2h = sum(L["hout"].numel() * 4 for L in self.layers)
+        return h2d, d2h
+
+    def step_host(self):
+        mx = self.mx
+        for L in self.layers:
+            hin = [t.numpy() for t in L["hin"]]
+            if L["kind"] == "dn":
+                qkv, a, b, z = hin
+                mx.dn_decode_host(L["prm"], L["st"], qkv, a, b, None, z, L["hout"].numpy())
+            else:
+                mx.gqa_decode_host(L["prm"], L["kv"], *hin, L["hout"].numpy())
+
+    def seq_len(self):
+        return self.layers[3]["kv"].seq_len
+
+
+def run_ours(args):
+    import torch
+
+    import qora_mixer as qm
+
+    ws, rank, local = dist_env()
+    init_dist(ws, local)
+    torch.cuda.set_device(local)
+    B = B_PER_GPU if not args.strong else max(1, B_PER_GPU // ws)
+    cap = CTX + 2 * (args.warmup + args.steps) + 16
+    ctx = qm.Ctx(local, stream=torch.cuda.current_stream())
+    stack = Stack(ctx, B, cap, seed=rank)
+    stream = torch.cuda.current_stream()
+
+    # ---- device-resident run ----
+    for _ in range(args.warmup):
+        stack.step()
+    ctx.sync()
+    barrier(ws)
+    clocks = Clocks(local)
+    clocks.start()
+    ctx.set_timing(True)
+    L0 = stack.seq_len()
+    n0 = ctx.launch_count()
+    torch.cuda.synchronize()
+    barrier(ws)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        stack.step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    launches = ctx.launch_count() - n0
+    ms_local = ev0.elapsed_time(ev1)
+    ktimes = {k: ctx.kernel_time(k) for k in ("dn_decode", "gqa_prep", "gqa_attn", "gqa_combine")}
+    ctx.set_timing(False)
+    clk = clocks.stop()
+    ctx.sync()
+    ms = max_over_ranks(ms_local, ws)
+    ms_step = ms / args.steps
+    tokens = B * ws * args.steps
+    value = tokens / (ms / 1e3)
+
+    # ---- roofline of the dominant kernel (split-KV attention) ----
+    peak, peak_kind = load_peaks()
+    att_ms, att_n = ktimes["gqa_attn"]
+    L_avg = L0 + (args.steps - 1) / 2.0
+    att_bytes = attn_bytes(B, L_avg)
+    att_achieved = att_bytes / (att_ms / att_n / 1e3) / 1e9
+    dn_ms, dn_n = ktimes["dn_decode"]
+    dn_achieved = B * DN_BYTES_TOKEN / (dn_ms / dn_n / 1e3) / 1e9
+    traffic = load_traffic().get("gqa_attn_bytes_per_seq_pos")
+    att_traffic = traffic * B * L_avg if traffic else None
+    step_kernel_ms = sum(v[0] for v in ktimes.values()) / args.steps
+
+    # ---- e2e through the _host entry points ----
+    h2d, d2h = stack.make_host_io()
+    for _ in range(min(2, args.warmup)):
+        stack.step_host()
+    torch.cuda.synchronize()
+    barrier(ws)
+    t0 = time.perf_counter()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        stack.step_host()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) * 1e3
+    e2e_ms = max_over_ranks(max(e0.elapsed_time(e1), wall), ws)
+    e2e_value = tokens / (e2e_ms / 1e3)
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "strong" if args.strong else "weak",
+        "vs_baseline": None, "dtype": "f32 state / bf16 KV (f32 math)",
+        "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) states/caches, random-init params)",
+        "config": {"workload": WORKLOAD, "global_batch": B * ws, "batch_per_gpu": B,
+                   "context": CTX, "layers": "24 DeltaNet + 8 GQA",
+                   "parallelism": f"sequence-sharded x{ws}, no collective",
+                   "l2": "inputs larger than L2 (68.7 GB of KV per GPU)"},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "kernel": "gqa_attn (split-KV attention)",
+                     "achieved": round(att_achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(att_achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": att_traffic,
+                     "algorithmic_bytes_per_launch": att_bytes,
+                     "avg_launch_us": round(att_ms / att_n * 1e3, 2)},
+        "kernels": {
+            k: {"launches_per_step": v[1] / args.steps, "ms_per_step": round(v[0] / args.steps, 4)}
+            for k, v in ktimes.items()},
+        "dn_decode_roofline": {"achieved": round(dn_achieved, 1), "peak": peak, "unit": "GB/s",
+                               "frac": round(dn_achieved / peak, 4),
+                               "algorithmic_bytes_per_launch": B * DN_BYTES_TOKEN},
+        "kernel_ms_per_step": round(step_kernel_ms, 4),
+        "clocks": clk,
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_sample(args.cpu_tokens)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for L in stack.layers:
+        for k in ("st", "kv"):
+            if k in L:
+                L[k].close()
+    ctx.close()
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------
+# CPU restatement on a bounded sample (reference arm and cpu_baseline)
+# ----------------------------------------------------------------------------
+class CpuStack:
+    """One sequence of workload 4 on the CPU restatement: 24 DeltaNet states and
+    8 GQA layers; the 8 layers' caches share one storage block (same shape and
+    traffic per layer, 1/8 of the host memory)."""
+
+    def __init__(self, ntok):
+        import numpy as np
+
+        from oracle import oracle as orc
+        from qora_mixer import inputs as I
+
+        self.orc, self.I = orc, I
+        self.c = orc.cfg_4b()
+        g = I.rng(4, stream=99)
+        cap = CTX + ntok + 4
+        self.cos, self.sin = orc.rope_table(1.0e7, 64, cap + 1)
+        self.dn = []
+        for li in range(24):
+            p = I.dn_layer_params(g)
+            st = orc.DnState(self.c)
+            st.s[:] = (g.standard_normal(st.s.shape, dtype=np.float32) * np.float32(0.02))
+            st.conv_buf[:] = (g.standard_normal(st.conv_buf.shape, dtype=np.float32) * np.float32(0.02))
+            tok = I.dn_token_inputs(g, 1, 1)
+            self.dn.append((p, st, tok))
+        kb = I.f32_to_bf16_bits(g.standard_normal((CTX, 4, 256), dtype=np.float32) * np.float32(0.02))
+        vb = I.f32_to_bf16_bits(g.standard_normal((CTX, 4, 256), dtype=np.float32) * np.float32(0.02))
+        self.kv = orc.KvCache(self.c, cap, I.bf16_bits_to_f32(kb).reshape(CTX, -1),
+                              I.bf16_bits_to_f32(vb).reshape(CTX, -1))
+        self.att = []
+        for li in range(8):
+            pr = I.gqa_layer_params(g, cap + 1)
+            tok = I.gqa_token_inputs(g, 1)
+            self.att.append((pr, tok))
+        self.avx = orc.has_avx512()
+
+    def token(self):
+        """One decode token through all 32 layers (3 DeltaNet + 1 GQA, x8)."""
+        orc = self.orc
+        di = ai = 0
+        for kind in LAYERS:
+            if kind == "dn":
+                p, st, tok = self.dn[di]
+                di += 1
+                orc.dn_decode(self.c, st, tok["qkv"][0, 0], tok["a"][0, 0], tok["b"][0, 0],
+                              p["conv_w"], p["a_log"], p["dt_bias"], use_avx512=self.avx,
+                              z=tok["z"][0, 0], norm_gamma=p["norm_gamma"])
+            else:
+                pr, tok = self.att[ai]
+                ai += 1
+                L = int(self.kv.seq_len[0])
+                orc.gqa_decode(self.c, self.kv, tok["q_gate"][0], tok["k_new"][0], tok["v_new"][0],
+                               pr["q_norm"], pr["k_norm"], self.cos, self.sin)
+                self.kv.seq_len[0] = L  # all 8 layers attend over the same 32768+1 positions
+
+
+def cpu_sample(ntok):
+    from oracle import oracle as orc
+
+    cs = CpuStack(ntok)
+    cs.token()  # warm
+    t0 = time.perf_counter()
+    for _ in range(ntok):
+        cs.token()
+    dt = time.perf_counter() - t0
+    return {"value": round(ntok / dt, 4), "unit": UNIT, "cores": min(16, orc.num_threads()),
+            "kind": "port",
+            "sample": (f"{ntok} decode tokens of one sequence through all 32 mixer layers at context "
+                       f"{CTX}; GQA heads on an OpenMP pool (rayon over 16 heads, gemv.rs:963), "
+                       "DeltaNet heads serial with the AVX-512 update (gemv.rs:817, simd.rs:292)"),
+            "cpu": cpu_model()}
+
+
+def cpu_model():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+
+    per_step = args.cpu_tokens_per_step
+    cs = CpuStack(per_step * (args.warmup + args.steps) + 1)
+    for _ in range(args.warmup):
+        for _ in range(per_step):
+            cs.token()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        for _ in range(per_step):
+            cs.token()
+        times.append(time.perf_counter() - t0)
+    tot = sum(times)
+    value = per_step * args.steps / tot
+    sample = (f"{per_step} decode token(s) of one sequence per step through all 32 mixer layers at "
+              f"context {CTX} (the reference processes sequences one at a time); GQA heads on an "
+              "OpenMP pool as rayon does (gemv.rs:963), DeltaNet heads serial with the AVX-512 "
+              "head update (gemv.rs:817, simd.rs:292-362)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(tot / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD, "global_batch": 1, "context": CTX,
+                   "parallelism": "CPU restatement of the reference (Rust not buildable here)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": min(16, orc.num_threads()),
+                         "kind": "port", "sample": sample, "cpu": cpu_model()},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--strong", action="store_true", help="64 sequences in total instead of per GPU")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-tokens", type=int, default=4)
+    ap.add_argument("--cpu-tokens-per-step", type=int, default=1)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,247 @@
+/*
+ * qora_mixer.h — C ABI of the B200 (sm_100a) QORA-4B token-mixer library.
+ *
+ * The library replaces the mixer regions of the reference engine
+ * (qora-protocol/QORA-LLM-4B, Rust): the Gated-DeltaNet layers and the
+ * full-attention GQA layers, for decode and prefill.  Projections, MLP and
+ * residual stay with the caller, exactly where the reference keeps them.
+ *
+ * Conventions
+ *  - Every function returns int: QM_OK (0) or a QM_E_* code; nothing aborts
+ *    or throws across this boundary.  qm_last_error(ctx) describes the last
+ *    failure on that context.
+ *  - Tensors passed to the non-_host entry points are DEVICE pointers on
+ *    the context's device; _host variants take host pointers (pinned or
+ *    pageable), copy in, run, copy out and return after the results are in
+ *    host memory, like the reference's Vec<f32>-returning functions.
+ *  - A context binds one device and one CUDA stream; calls on it are
+ *    asynchronous and must be serialised by the caller (the reference
+ *    drives its GPU from one dedicated thread, gpu_inference.rs:946-953).
+ *  - A state/cache handle holds B sequences that advance together: one
+ *    decode call adds one token to each of the B sequences (a batch of B
+ *    reference caches stepped in lockstep).
+ *  - Shapes are those of Qor4bConfig::default_4b (src/config.rs:42-79);
+ *    qm_shape_get reports them.  Kernels are specialised for them.
+ *  - bf16 tensors are passed as uint16_t bit patterns.
+ */
+#ifndef QORA_MIXER_H
+#define QORA_MIXER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ */
+/* Status codes.  The reference panics on a layer/cache type mismatch   */
+/* (src/gemv.rs:1049,228; src/gpu_inference.rs:418); here that is       */
+/* QM_E_MISMATCH.                                                       */
+/* ------------------------------------------------------------------ */
+#define QM_OK 0
+#define QM_E_ARG 1          /* null pointer or invalid value             */
+#define QM_E_SHAPE 2        /* batch/size/capacity does not fit          */
+#define QM_E_OOM 3          /* device allocation failed                  */
+#define QM_E_CUDA 4         /* CUDA runtime/driver error                 */
+#define QM_E_NCCL 5         /* NCCL error                                */
+#define QM_E_TIMEOUT 6      /* a bounded device-side wait gave up        */
+#define QM_E_RANGE 7        /* position beyond the RoPE table or cache   */
+#define QM_E_MISMATCH 8     /* handle belongs to another ctx / wrong kind*/
+#define QM_E_UNSUPPORTED 9  /* device is not sm_100 (B200)               */
+#define QM_E_CAPTURE 10     /* would allocate during CUDA-graph capture  */
+
+typedef struct qm_ctx qm_ctx;
+typedef struct qm_dn_state qm_dn_state;
+typedef struct qm_kv qm_kv;
+
+/* Mixer shape (fields of Qor4bConfig used by the mixers, src/config.rs:4-32). */
+typedef struct qm_shape {
+    int num_qk_heads;    /* 16 */
+    int num_v_heads;     /* 32 */
+    int dn_head_dim;     /* 128 */
+    int conv_kernel;     /* 4 */
+    int num_attn_heads;  /* 16 */
+    int num_kv_heads;    /* 4 */
+    int attn_head_dim;   /* 256 */
+    int rope_dim;        /* 64 (config.rs:82-84) */
+    float rope_theta;    /* 1e7 */
+    float rms_eps;       /* 1e-6 */
+} qm_shape;
+
+/* Replaces Qor4bConfig::default_4b (src/config.rs:42-79) for the mixer fields. */
+int qm_shape_get(qm_shape* out);
+const char* qm_status_string(int status);
+
+/* ------------------------------------------------------------------ */
+/* Context                                                              */
+/* ------------------------------------------------------------------ */
+/* Replaces the backend/device set-up of generate_gpu_inner
+ * (src/gpu_inference.rs:981-1004).  Fails with QM_E_UNSUPPORTED unless the
+ * device is compute capability 10.x. */
+int qm_ctx_create(int device, qm_ctx** out);
+int qm_ctx_destroy(qm_ctx* ctx);
+/* Run subsequent calls on `stream` (a cudaStream_t); NULL restores the
+ * context's own stream. */
+int qm_ctx_set_stream(qm_ctx* ctx, void* stream);
+void* qm_ctx_get_stream(const qm_ctx* ctx);
+/* Waits for the context's stream, then reports any device-side error word
+ * (a bounded wait that gave up) as QM_E_TIMEOUT. */
+int qm_sync(qm_ctx* ctx);
+const char* qm_last_error(const qm_ctx* ctx);
+/* Grows the context workspace to `bytes` now, so later calls never
+ * allocate (needed before capturing calls into a CUDA graph). */
+int qm_ctx_reserve(qm_ctx* ctx, size_t bytes);
+/* Kernels this context launched since creation (for launch accounting). */
+int64_t qm_ctx_launch_count(const qm_ctx* ctx);
+/* Per-kernel timing: when on, every launch is bracketed by CUDA events on the
+ * context stream.  qm_ctx_kernel_time waits for the recorded events and
+ * returns the summed device time (ms) and launch count of kernel `name`
+ * ("dn_decode", "gqa_prep", "gqa_attn", "gqa_combine", "gqa_prefill",
+ * "dn_prefill", ...).  qm_ctx_set_timing(ctx, 0) discards the records. */
+int qm_ctx_set_timing(qm_ctx* ctx, int on);
+int qm_ctx_kernel_time(qm_ctx* ctx, const char* name, double* total_ms, int64_t* launches);
+
+/* ------------------------------------------------------------------ */
+/* RoPE tables                                                           */
+/* ------------------------------------------------------------------ */
+/* Replaces the table precompute of src/convert.rs:161-176 (loaded at
+ * src/save.rs:345-346, uploaded at src/gpu_loader.rs:174-184), with the
+ * same f32 formula, for any max_pos (the reference stops at 8192).
+ * Host buffers [max_pos, rope_dim/2]. */
+int qm_rope_table(float theta, int rope_dim, int max_pos, float* cos_host, float* sin_host);
+
+/* ------------------------------------------------------------------ */
+/* DeltaNet recurrent state                                              */
+/* ------------------------------------------------------------------ */
+/* Replaces DeltaNetState::new (src/gemv.rs:144-157) / GpuDeltaNetState
+ * (src/gpu_inference.rs:30-36,49-58) for B sequences: S [B,32,128,128] f32
+ * (row = v-dim, as the reference stores it), the causal-conv history and
+ * conv_pos, all zero. */
+int qm_dn_state_create(qm_ctx* ctx, int batch, qm_dn_state** out);
+/* Same over caller-owned device memory (not freed by destroy):
+ * s [B,32,128,128] f32 and conv [B,4,8192] f32 (see qm_dn_state_data). */
+int qm_dn_state_wrap(qm_ctx* ctx, int batch, float* s, float* conv, qm_dn_state** out);
+int qm_dn_state_destroy(qm_dn_state* st);
+/* Zero S, the conv history and conv_pos (DeltaNetState::new). */
+int qm_dn_state_reset(qm_ctx* ctx, qm_dn_state* st);
+/* Deep copy (HybridCache::snapshot, src/gemv.rs:198-212). */
+int qm_dn_state_snapshot(qm_ctx* ctx, const qm_dn_state* src, qm_dn_state** out);
+/* Copy src into dst (HybridCache::restore_from, src/gemv.rs:215-231);
+ * QM_E_MISMATCH when the batch sizes differ. */
+int qm_dn_state_restore(qm_ctx* ctx, qm_dn_state* dst, const qm_dn_state* src);
+/* Sequence b of the state in the reference layout (synchronous):
+ * s [32,128,128] and conv_buf [8192,3] (oldest first, gemv.rs:137-139). */
+int qm_dn_state_read(qm_ctx* ctx, const qm_dn_state* st, int b, float* s_host, float* conv_buf_host);
+int qm_dn_state_write(qm_ctx* ctx, qm_dn_state* st, int b, const float* s_host, const float* conv_buf_host);
+int64_t qm_dn_state_conv_pos(const qm_dn_state* st);
+int qm_dn_state_set_conv_pos(qm_dn_state* st, int64_t conv_pos);
+int qm_dn_state_batch(const qm_dn_state* st);
+/* Raw device storage: S [B,32,128,128] f32; conv history [B,4,8192] f32 as a
+ * ring of 4 slots, token t stored in slot t % 4. */
+int qm_dn_state_data(const qm_dn_state* st, float** s, float** conv);
+
+/* DeltaNet layer parameters (device pointers). */
+typedef struct qm_dn_params {
+    const float* conv_w;     /* [8192, 4] conv1d_weight (gemv.rs:68)        */
+    const float* a_log;      /* [32]  A_log (gemv.rs:69)                    */
+    const float* dt_bias;    /* [32]  dt_bias (gemv.rs:70)                  */
+    const float* norm_gamma; /* [128] attn_norm_weight widened from f16
+                                (gemv.rs:71); only read when z != NULL      */
+} qm_dn_params;
+
+/*
+ * DeltaNet decode, one token per sequence.  Replaces the mixer region
+ * src/gemv.rs:744-883 of forward_deltanet_decode (gemv.rs:719) and
+ * src/gpu_inference.rs:149-227 of forward_deltanet_decode_gpu (125):
+ * causal conv1d + SiLU, per-head L2 norm (q scaled by 1/sqrt(128)),
+ * alpha/beta gates, the gated delta-rule update of S and y = S q.
+ *   qkv [B,8192] f32  in_proj_qkv output (Q 0..2047, K 2048..4095, V 4096..)
+ *   a,b [B,32]   f32  in_proj_a / in_proj_b outputs
+ *   y   [B,32,128] f32 raw per-head output (gemv.rs:814-862); may be NULL
+ *       when out is given
+ *   z   [B,4096] f32 or NULL: in_proj_z output; when given, out [B,4096]
+ *       receives RMSNorm(y)*gamma*SiLU(z) (gemv.rs:864-883), the input of
+ *       out_proj.
+ */
+int qm_dn_decode(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, const float* qkv,
+                 const float* a, const float* b, float* y, const float* z, float* out);
+/* Host-buffer variant of qm_dn_decode (params stay device pointers). */
+int qm_dn_decode_host(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, const float* qkv,
+                      const float* a, const float* b, float* y, const float* z, float* out);
+
+/*
+ * DeltaNet prefill of T tokens per sequence (chunked WY form on the tensor
+ * cores).  Replaces the sequential loop src/gemv.rs:1119-1219 of
+ * prefill_deltanet_layer (1086) and the CPU recurrence that
+ * prefill_deltanet_layer_gpu runs between device round trips
+ * (src/gpu_inference.rs:464-604).
+ *   qkv [B,T,8192] bf16, a,b [B,T,32] f32, y [B,T,32,128] f32,
+ *   z [B,T,4096] f32 or NULL, out [B,T,4096] f32 or NULL.
+ * The state continues from its current contents (conv history included).
+ */
+int qm_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, int T, const uint16_t* qkv,
+                  const float* a, const float* b, float* y, const float* z, float* out);
+
+/* ------------------------------------------------------------------ */
+/* GQA KV cache                                                          */
+/* ------------------------------------------------------------------ */
+/* Replaces KvCacheEntry (src/gemv.rs:164-168, f32 [seq,4,256] grown per
+ * token) and GpuKvCacheEntry (src/gpu_inference.rs:38-42, re-concatenated
+ * every token, 303-310) with a preallocated bf16 cache
+ * K,V [B,4,capacity,256], appended in place. */
+int qm_kv_create(qm_ctx* ctx, int batch, int capacity, qm_kv** out);
+/* Same over caller-owned device memory k, v (bf16 [B,4,capacity,256]). */
+int qm_kv_wrap(qm_ctx* ctx, int batch, int capacity, uint16_t* k, uint16_t* v, qm_kv** out);
+int qm_kv_destroy(qm_kv* kv);
+int qm_kv_snapshot(qm_ctx* ctx, const qm_kv* src, qm_kv** out);    /* gemv.rs:198-212 */
+int qm_kv_restore(qm_ctx* ctx, qm_kv* dst, const qm_kv* src);      /* gemv.rs:215-231 */
+int64_t qm_kv_seq_len(const qm_kv* kv);
+/* Declare how many positions the cache holds (after filling it directly). */
+int qm_kv_set_seq_len(qm_kv* kv, int64_t seq_len);
+int qm_kv_capacity(const qm_kv* kv);
+int qm_kv_batch(const qm_kv* kv);
+int qm_kv_data(const qm_kv* kv, uint16_t** k, uint16_t** v);
+
+/* GQA layer parameters (device pointers). */
+typedef struct qm_gqa_params {
+    const float* q_norm;   /* [256] q_norm widened from f16, applied as 1+g (gemv.rs:86,594) */
+    const float* k_norm;   /* [256] k_norm, same                                          */
+    const float* rope_cos; /* [max_pos, 32] (convert.rs:165-172)                          */
+    const float* rope_sin; /* [max_pos, 32]                                               */
+    int max_pos;
+} qm_gqa_params;
+
+/*
+ * GQA decode, one token per sequence.  Replaces the attention region
+ * src/gemv.rs:927-1011 of forward_attn_decode (907) and
+ * src/gpu_inference.rs:269-349 of forward_attn_decode_gpu (247):
+ * QK-RMSNorm (1+gamma), partial RoPE at position seq_len, KV append,
+ * softmax(q K^T / 16) V over seq_len+1 positions, sigmoid output gate.
+ *   q_gate [B,16,512] f32 q_proj output, per head Q then gate (gemv.rs:927)
+ *   k_new, v_new [B,4,256] f32 k_proj / v_proj outputs
+ *   out [B,16,256] f32 gated attention output (input of o_proj)
+ * QM_E_RANGE if seq_len >= capacity or seq_len >= max_pos.
+ * Uses the context workspace for split-KV partials (grown on first use).
+ */
+int qm_gqa_decode(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, const float* q_gate,
+                  const float* k_new, const float* v_new, float* out);
+int qm_gqa_decode_host(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, const float* q_gate,
+                       const float* k_new, const float* v_new, float* out);
+
+/*
+ * GQA causal prefill of T tokens per sequence.  Replaces the attention
+ * region src/gemv.rs:1364-1444 of prefill_attn_layer (1339) and
+ * src/gpu_inference.rs:690-766 (which materialises [16,S,S] scores).
+ * Like the reference (gemv.rs:1397-1400) it REPLACES the cache contents:
+ * positions 0..T-1 receive K after QK-norm + RoPE and raw V (bf16), and
+ * seq_len becomes T.
+ *   q_gate [B,T,16,512] bf16, k, v [B,T,4,256] bf16, out [B,T,16,256] f32.
+ */
+int qm_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, int T, const uint16_t* q_gate,
+                   const uint16_t* k, const uint16_t* v, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QORA_MIXER_H */

@@ -1,0 +1,466 @@
+// GQA decode: one new token for B sequences against a bf16 KV cache.
+//
+// Replaces src/gemv.rs:927-1011 (CPU, rayon over 16 heads) and
+// src/gpu_inference.rs:269-349 (wgpu: re-concatenates the cache and repeats
+// every KV head 4x each token).  Three launches:
+//
+//  1. prep     (B*4 CTAs)  QK-RMSNorm(1+g) + partial RoPE of the new q/k,
+//               bf16 append of k/v at position L, q split into bf16 hi+lo.
+//  2. attn     (nsplit x 4 x B CTAs)  split-KV attention over the L cached
+//               positions.  A producer warp streams 64-position K/V tiles
+//               with TMA (128-byte swizzle) into a 3-stage mbarrier ring;
+//               4 consumer warps run q.K^T and P.V on the tensor cores.
+//               The 4 query heads of a KV group share every K/V tile; q and
+//               P enter the MMA as bf16 hi+lo pairs so the products keep
+//               ~16 mantissa bits (the reference is f32 throughout).
+//  3. combine  (B*16 CTAs)  log-sum-exp merge of the split partials plus the
+//               new token itself in f32, then the sigmoid gate.
+//
+// The cache stays in place: the reference's per-token Tensor::cat (O(L) copy)
+// becomes one 1 KB write per (sequence, KV head).
+#include <cuda_bf16.h>
+
+#include <algorithm>
+
+#include "qm_internal.h"
+#include "qm_ptx.cuh"
+
+namespace qm {
+namespace {
+
+constexpr int kTile = 64;                       // positions per K/V tile
+constexpr int kStages = 3;
+constexpr int kSubBytes = 64 * 128;             // one 64x64 bf16 box (128 B rows)
+constexpr int kTileBytes = 4 * kSubBytes;       // 64 positions x 256 dims
+constexpr int kStageBytes = 2 * kTileBytes;     // K + V
+constexpr int kAttnSmem = kStages * kStageBytes + 1024 /*align*/ + 128 /*barriers*/;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Plan {
+    int ntiles = 0, nsplit = 0, tps = 0;
+};
+
+Plan plan_for(int B, int64_t L, int num_sms) {
+    Plan p;
+    p.ntiles = (int)((L + kTile - 1) / kTile);
+    if (p.ntiles == 0) return p;
+    const int64_t units = (int64_t)B * kNumKVH;
+    const int64_t total = (int64_t)p.ntiles * units;
+    const int64_t waves = std::max<int64_t>(1, total / ((int64_t)num_sms * 8));
+    const int64_t target = waves * num_sms;
+    int ns = (int)std::min<int64_t>(p.ntiles, std::max<int64_t>(1, (target + units - 1) / units));
+    p.tps = (p.ntiles + ns - 1) / ns;
+    p.nsplit = (p.ntiles + p.tps - 1) / p.tps;
+    return p;
+}
+
+struct WsLayout {
+    size_t q_bf, q_f32, kn, part_o, part_ml, total;
+};
+
+inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
+
+WsLayout ws_layout(int B, int nsplit) {
+    WsLayout w;
+    size_t off = 0;
+    w.q_bf = off;    off += al256((size_t)B * kNumH * 2 * kD * 2);
+    w.q_f32 = off;   off += al256((size_t)B * kNumH * kD * 4);
+    w.kn = off;      off += al256((size_t)B * kNumKVH * kD * 4);
+    w.part_o = off;  off += al256((size_t)B * kNumH * std::max(nsplit, 1) * kD * 4);
+    w.part_ml = off; off += al256((size_t)B * kNumH * std::max(nsplit, 1) * 2 * 4);
+    w.total = off;
+    return w;
+}
+
+// ---------------------------------------------------------------------------
+// 1. prep: gemv.rs:945-955 for the new token
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(160)
+gqa_prep_kernel(const float* __restrict__ q_gate, const float* __restrict__ k_new,
+                const float* __restrict__ v_new, const float* __restrict__ q_norm,
+                const float* __restrict__ k_norm, const float* __restrict__ rope_cos,
+                const float* __restrict__ rope_sin, int64_t pos, uint16_t* __restrict__ kcache,
+                uint16_t* __restrict__ vcache, int cap, uint16_t* __restrict__ q_bf,
+                float* __restrict__ q_f32, float* __restrict__ kn_out) {
+    const int b = blockIdx.x / kNumKVH, g = blockIdx.x % kNumKVH;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool is_q = warp < kGroup;
+    const int h = g * kGroup + warp;
+    const float* src = is_q ? q_gate + ((size_t)b * kNumH + h) * 2 * kD
+                            : k_new + ((size_t)b * kNumKVH + g) * kD;
+    const float* gamma = is_q ? q_norm : k_norm;
+    float x[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        x[i] = src[lane + 32 * i];
+        ss = fmaf(x[i], x[i], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.0f / sqrtf(ss * (1.0f / kD) + 1e-6f);  // gemv.rs:591
+#pragma unroll
+    for (int i = 0; i < 8; i++) x[i] = x[i] * inv * (1.0f + gamma[lane + 32 * i]);
+    // split-half partial RoPE (gemv.rs:604-627): pair (lane, lane + 32)
+    {
+        const float c = rope_cos[pos * kHalfRot + lane];
+        const float s = rope_sin[pos * kHalfRot + lane];
+        const float x1 = x[0], x2 = x[1];
+        x[0] = x1 * c - x2 * s;
+        x[1] = x2 * c + x1 * s;
+    }
+    if (is_q) {
+        uint16_t* qh = q_bf + ((size_t)b * kNumH + h) * 2 * kD;
+        float* qf = q_f32 + ((size_t)b * kNumH + h) * kD;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int e = lane + 32 * i;
+            const float qs = x[i] * 0.0625f;  // scale 1/sqrt(256) (gemv.rs:959), exact
+            const uint16_t hi = bf16_bits_rn(qs);
+            const uint16_t lo = bf16_bits_rn(qs - bf16_bits_to_f32(hi));
+            qf[e] = qs;
+            qh[e] = hi;
+            qh[kD + e] = lo;
+        }
+    } else {
+        const size_t row = (((size_t)b * kNumKVH + g) * cap + pos) * kD;
+        const float* vs = v_new + ((size_t)b * kNumKVH + g) * kD;
+        float* kn = kn_out + ((size_t)b * kNumKVH + g) * kD;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int e = lane + 32 * i;
+            kn[e] = x[i];
+            kcache[row + e] = bf16_bits_rn(x[i]);
+            vcache[row + e] = bf16_bits_rn(vs[e]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 2. split-KV attention over cached positions [0, L)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t swz_addr(uint32_t base, int pos, int dim) {
+    // 4 boxes of [64 positions x 64 dims]; within a box row = 128 B and the
+    // 16-byte chunk index is XOR-ed with (row % 8) (TMA SWIZZLE_128B).
+    return base + (uint32_t)((dim >> 6) * kSubBytes + pos * 128 +
+                             ((((dim & 63) >> 3) ^ (pos & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(160, 1)
+gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                const uint16_t* __restrict__ q_bf, float* __restrict__ part_o,
+                float* __restrict__ part_ml, int L, int tps, int nsplit, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
+
+    const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile0 = split * tps;
+    const int ntiles_all = (L + kTile - 1) / kTile;
+    const int ntiles = min(tps, ntiles_all - tile0);
+    const int pos_end = min(L, (tile0 + ntiles) * kTile);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), kGroup);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    const uint32_t sbase = smem_u32(smem);
+    if (warp == kGroup) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            prefetch_tmap(&tmk);
+            prefetch_tmap(&tmv);
+            const int zc = b * kNumKVH + g;
+            int it = 0;
+            for (; it < ntiles; it++) {
+                const int st = it % kStages, round = it / kStages;
+                if (round > 0 &&
+                    !mbar_wait_bounded(smem_u32(&empty[st]), (round - 1) & 1, abort_flag, err))
+                    break;
+                const uint32_t fb = smem_u32(&full[st]);
+                mbar_arrive_expect_tx(fb, kStageBytes);
+                const int p0 = (tile0 + it) * kTile;
+                const uint32_t kb = sbase + st * kStageBytes;
+#pragma unroll
+                for (int sub = 0; sub < 4; sub++) {
+                    tma_load_3d(kb + sub * kSubBytes, &tmk, sub * 64, p0, zc, fb);
+                    tma_load_3d(kb + kTileBytes + sub * kSubBytes, &tmv, sub * 64, p0, zc, fb);
+                }
+            }
+            // Do not leave while copies this CTA issued may still land.
+            for (int j = max(0, it - kStages); j < it; j++)
+                mbar_wait_bounded(smem_u32(&full[j % kStages]), (j / kStages) & 1, abort_flag, err);
+        }
+        return;
+    }
+
+    // ---------------- consumers: warp w owns positions [16w, 16w+16) of a tile ----
+    const int row = lane >> 2;          // A/C row: head (row & 3), hi/lo (row >> 2)
+    const int quad = lane & 3;
+    uint32_t qa[16][2];
+    {
+        const int head = row & 3, hl = row >> 2;
+        const uint16_t* qr = q_bf + (((size_t)b * kNumH + g * kGroup + head) * 2 + hl) * kD;
+#pragma unroll
+        for (int kk = 0; kk < 16; kk++) {
+            qa[kk][0] = *reinterpret_cast<const uint32_t*>(qr + kk * 16 + quad * 2);
+            qa[kk][1] = *reinterpret_cast<const uint32_t*>(qr + kk * 16 + 8 + quad * 2);
+        }
+    }
+    float o[32][2];
+#pragma unroll
+    for (int n = 0; n < 32; n++) o[n][0] = o[n][1] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+    for (int it = 0; it < ntiles; it++) {
+        const int st = it % kStages, round = it / kStages;
+        const bool ok = mbar_wait_bounded(smem_u32(&full[st]), round & 1, abort_flag, err);
+        if (ok) {
+            const uint32_t kb = sbase + st * kStageBytes;
+            const uint32_t vb = kb + kTileBytes;
+            // ---- S = q . K^T for 16 positions (2 n-tiles of 8) ----
+            float c[2][2];
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++) {
+                c[nt][0] = c[nt][1] = 0.f;
+                const int pos = warp * 16 + nt * 8 + (lane & 7);
+#pragma unroll
+                for (int k2 = 0; k2 < 8; k2++) {
+                    uint32_t r0, r1, r2, r3;
+                    ldsm_x4(swz_addr(kb, pos, k2 * 32 + (lane >> 3) * 8), r0, r1, r2, r3);
+                    mma_bf16_top(c[nt][0], c[nt][1], qa[2 * k2][0], qa[2 * k2][1], r0, r1);
+                    mma_bf16_top(c[nt][0], c[nt][1], qa[2 * k2 + 1][0], qa[2 * k2 + 1][1], r2, r3);
+                }
+            }
+            // ---- online softmax; hi and lo rows sit 16 lanes apart ----
+            const int pbase = (tile0 + it) * kTile + warp * 16 + quad * 2;
+            float s[2][2];
+            float tmax = -INFINITY;
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    float v = c[nt][j] + __shfl_xor_sync(0xffffffffu, c[nt][j], 16);
+                    if (pbase + nt * 8 + j >= pos_end) v = -INFINITY;
+                    s[nt][j] = v;
+                    tmax = fmaxf(tmax, v);
+                }
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+            const float m_new = fmaxf(m_run, tmax);
+            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+            const float corr = exp2f((m_run - m_use) * kLog2e);
+            float p[2][2], rs = 0.f;
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    p[nt][j] = exp2f((s[nt][j] - m_use) * kLog2e);
+                    rs += p[nt][j];
+                }
+            rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+            rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+            l_run = l_run * corr + rs;
+            m_run = m_new;
+            if (__any_sync(0xffffffffu, corr != 1.0f)) {
+#pragma unroll
+                for (int n = 0; n < 32; n++) {
+                    o[n][0] *= corr;
+                    o[n][1] *= corr;
+                }
+            }
+            // P as bf16 hi (rows 0-3, lanes 0-15) + lo (rows 4-7, lanes 16-31)
+            uint16_t pb[2][2];
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const uint16_t hi = bf16_bits_rn(p[nt][j]);
+                    pb[nt][j] = (lane < 16) ? hi : bf16_bits_rn(p[nt][j] - bf16_bits_to_f32(hi));
+                }
+            const uint32_t a0 = pack_bf16(pb[0][0], pb[0][1]);
+            const uint32_t a2 = pack_bf16(pb[1][0], pb[1][1]);
+            // ---- O += P . V over 256 dims ----
+            const int mi = lane >> 3;
+            const int vpos = warp * 16 + (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+            for (int dn = 0; dn < 16; dn++) {
+                uint32_t r0, r1, r2, r3;
+                ldsm_x4_t(swz_addr(vb, vpos, dn * 16 + (mi >> 1) * 8), r0, r1, r2, r3);
+                mma_bf16_top(o[2 * dn][0], o[2 * dn][1], a0, a2, r0, r1);
+                mma_bf16_top(o[2 * dn + 1][0], o[2 * dn + 1][1], a0, a2, r2, r3);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty[st]));
+    }
+
+    // ---- fold lo rows into hi rows, then merge the 4 warps through smem ----
+#pragma unroll
+    for (int n = 0; n < 32; n++) {
+        o[n][0] += __shfl_xor_sync(0xffffffffu, o[n][0], 16);
+        o[n][1] += __shfl_xor_sync(0xffffffffu, o[n][1], 16);
+    }
+    named_bar_sync(1, kGroup * 32);  // all consumers are done with the stage buffers
+    float* mo = reinterpret_cast<float*>(smem);           // [4 warps][4 heads][256]
+    float* mm = mo + kGroup * kGroup * kD;                // [4][4]
+    float* ml = mm + kGroup * kGroup;                     // [4][4]
+    if (lane < 16) {
+        const int head = lane >> 2;
+        float* dst = mo + (warp * kGroup + head) * kD + quad * 2;
+#pragma unroll
+        for (int n = 0; n < 32; n++) {
+            dst[n * 8] = o[n][0];
+            dst[n * 8 + 1] = o[n][1];
+        }
+        if (quad == 0) {
+            mm[warp * kGroup + head] = m_run;
+            ml[warp * kGroup + head] = l_run;
+        }
+    }
+    named_bar_sync(1, kGroup * 32);
+    const int t = threadIdx.x;  // 0..127
+#pragma unroll
+    for (int e = 0; e < (kGroup * kD) / 128; e++) {
+        const int idx = e * 128 + t;
+        const int head = idx / kD, d = idx % kD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kGroup; w++) M = fmaxf(M, mm[w * kGroup + head]);
+        float acc = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kGroup; w++) {
+                const float mw = mm[w * kGroup + head];
+                const float sc = (mw == -INFINITY) ? 0.f : exp2f((mw - M) * kLog2e);
+                acc += sc * mo[(w * kGroup + head) * kD + d];
+            }
+        }
+        const size_t hidx = (size_t)b * kNumH + g * kGroup + head;
+        part_o[(hidx * nsplit + split) * kD + d] = acc;
+        if (d == 0) {
+            float lsum = 0.f;
+            if (M != -INFINITY) {
+#pragma unroll
+                for (int w = 0; w < kGroup; w++) {
+                    const float mw = mm[w * kGroup + head];
+                    lsum += (mw == -INFINITY) ? 0.f : exp2f((mw - M) * kLog2e) * ml[w * kGroup + head];
+                }
+            }
+            part_ml[(hidx * nsplit + split) * 2 + 0] = M;
+            part_ml[(hidx * nsplit + split) * 2 + 1] = lsum;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 3. combine splits + the new token (f32) + sigmoid gate (gemv.rs:1008-1011)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+gqa_combine_kernel(const float* __restrict__ q_f32, const float* __restrict__ kn,
+                   const float* __restrict__ v_new, const float* __restrict__ q_gate,
+                   const float* __restrict__ part_o, const float* __restrict__ part_ml, int nsplit,
+                   float* __restrict__ out) {
+    const int bh = blockIdx.x;
+    const int b = bh / kNumH, h = bh % kNumH, g = h / kGroup;
+    const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
+    __shared__ float s_red[8];
+    __shared__ float s_ml[2 * 512];
+    float prod = q_f32[(size_t)bh * kD + d] * kn[((size_t)b * kNumKVH + g) * kD + d];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) prod += __shfl_xor_sync(0xffffffffu, prod, o);
+    if (lane == 0) s_red[warp] = prod;
+    for (int i = d; i < 2 * nsplit && i < 1024; i += 256) s_ml[i] = part_ml[(size_t)bh * nsplit * 2 + i];
+    __syncthreads();
+    float s_new = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) s_new += s_red[w];
+    float M = s_new;
+    for (int i = 0; i < nsplit; i++) {
+        const float mi = (i < 512) ? s_ml[2 * i] : part_ml[((size_t)bh * nsplit + i) * 2];
+        M = fmaxf(M, mi);
+    }
+    const float wn = exp2f((s_new - M) * kLog2e);
+    float acc = wn * v_new[((size_t)b * kNumKVH + g) * kD + d];
+    float lsum = wn;
+    for (int i = 0; i < nsplit; i++) {
+        const float mi = (i < 512) ? s_ml[2 * i] : part_ml[((size_t)bh * nsplit + i) * 2];
+        const float li = (i < 512) ? s_ml[2 * i + 1] : part_ml[((size_t)bh * nsplit + i) * 2 + 1];
+        if (mi == -INFINITY) continue;
+        const float w = exp2f((mi - M) * kLog2e);
+        acc += w * part_o[((size_t)bh * nsplit + i) * kD + d];
+        lsum += w * li;
+    }
+    const float gate = q_gate[(size_t)bh * 2 * kD + kD + d];
+    out[(size_t)bh * kD + d] = (acc / lsum) * (1.0f / (1.0f + __expf(-gate)));
+}
+
+}  // namespace
+
+size_t gqa_decode_ws_bytes(int batch, int64_t seq_len, int num_sms) {
+    Plan p = plan_for(batch, seq_len, num_sms);
+    return ws_layout(batch, p.nsplit).total;
+}
+
+cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
+                              const float* q_gate, const float* k_new, const float* v_new,
+                              float* out, void* ws, size_t ws_bytes) {
+    const int B = kv->batch;
+    const int64_t L = kv->seq_len;  // cached positions; the new token goes to index L
+    const Plan pl = plan_for(B, L, ctx->num_sms);
+    const WsLayout w = ws_layout(B, pl.nsplit);
+    if (w.total > ws_bytes) return cudaErrorInvalidValue;
+    char* base = static_cast<char*>(ws);
+    uint16_t* q_bf = reinterpret_cast<uint16_t*>(base + w.q_bf);
+    float* q_f32 = reinterpret_cast<float*>(base + w.q_f32);
+    float* kn = reinterpret_cast<float*>(base + w.kn);
+    float* part_o = reinterpret_cast<float*>(base + w.part_o);
+    float* part_ml = reinterpret_cast<float*>(base + w.part_ml);
+    cudaStream_t st = ctx->stream;
+
+    {
+        TimedLaunch tl(ctx, "gqa_prep");
+        gqa_prep_kernel<<<B * kNumKVH, 160, 0, st>>>(q_gate, k_new, v_new, prm->q_norm,
+                                                     prm->k_norm, prm->rope_cos, prm->rope_sin, L,
+                                                     kv->k, kv->v, kv->capacity, q_bf, q_f32, kn);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    ctx->launches += 1;
+    if (pl.nsplit > 0) {
+        static bool attr_set[64] = {};
+        if (ctx->device < 64 && !attr_set[ctx->device]) {
+            e = cudaFuncSetAttribute(gqa_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kAttnSmem);
+            if (e != cudaSuccess) return e;
+            attr_set[ctx->device] = true;
+        }
+        dim3 grid(pl.nsplit, kNumKVH, B);
+        TimedLaunch tl(ctx, "gqa_attn");
+        gqa_attn_kernel<<<grid, 160, kAttnSmem, st>>>(kv->tmap_k, kv->tmap_v, q_bf, part_o,
+                                                      part_ml, (int)L, pl.tps, pl.nsplit,
+                                                      ctx->d_err);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        ctx->launches += 1;
+    }
+    {
+        TimedLaunch tl(ctx, "gqa_combine");
+        gqa_combine_kernel<<<B * kNumH, 256, 0, st>>>(q_f32, kn, v_new, q_gate, part_o, part_ml,
+                                                      pl.nsplit, out);
+    }
+    e = cudaGetLastError();
+    if (e == cudaSuccess) ctx->launches += 1;
+    return e;
+}
+
+}  // namespace qm

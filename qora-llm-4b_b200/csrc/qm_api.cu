@@ -1,0 +1,700 @@
+// C-ABI front end: contexts, state/cache handles, argument checks, _host
+// variants.  Kernels live in dn_decode.cu, gqa_decode.cu, gqa_prefill.cu and
+// dn_prefill.cu.
+#include <cudaTypedefs.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "qm_internal.h"
+
+using namespace qm;
+
+namespace qm {
+
+int set_error(qm_ctx* ctx, int code, const std::string& msg) {
+    if (ctx) ctx->last_error = msg;
+    return code;
+}
+
+int cuda_error(qm_ctx* ctx, cudaError_t e, const char* what) {
+    std::string m = std::string(what) + ": " + cudaGetErrorString(e);
+    if (e == cudaErrorMemoryAllocation) return set_error(ctx, QM_E_OOM, m);
+    return set_error(ctx, QM_E_CUDA, m);
+}
+
+static bool stream_capturing(cudaStream_t s) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &st) != cudaSuccess) return false;
+    return st != cudaStreamCaptureStatusNone;
+}
+
+int ensure_workspace(qm_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->ws_bytes) return QM_OK;
+    if (stream_capturing(ctx->stream))
+        return set_error(ctx, QM_E_CAPTURE,
+                         "workspace must grow during stream capture; call qm_ctx_reserve first");
+    QM_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    if (ctx->ws) cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+    ctx->ws_bytes = 0;
+    size_t want = (bytes + 0xFFFFF) & ~size_t(0xFFFFF);
+    QM_CHECK_CUDA(ctx, cudaMalloc(&ctx->ws, want));
+    ctx->ws_bytes = want;
+    return QM_OK;
+}
+
+int ensure_stage(qm_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->stage_bytes) return QM_OK;
+    if (stream_capturing(ctx->stream))
+        return set_error(ctx, QM_E_CAPTURE, "staging buffer must grow during stream capture");
+    QM_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    if (ctx->stage) cudaFree(ctx->stage);
+    ctx->stage = nullptr;
+    ctx->stage_bytes = 0;
+    size_t want = (bytes + 0xFFFFF) & ~size_t(0xFFFFF);
+    QM_CHECK_CUDA(ctx, cudaMalloc(&ctx->stage, want));
+    ctx->stage_bytes = want;
+    return QM_OK;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_tiled() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 3-D bf16 view of a cache [B*4][cap][256]: box {64 dims, 64 positions, 1},
+// 128-byte swizzle, zero fill past the capacity.
+int encode_cache_tmap(CUtensorMap* m, void* base, int batch, int capacity, int box_rows) {
+    auto enc = get_encode_tiled();
+    if (!enc) return QM_E_CUDA;
+    cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)capacity, (cuuint64_t)batch * kNumKVH};
+    cuuint64_t strides[2] = {(cuuint64_t)kD * 2, (cuuint64_t)capacity * kD * 2};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? QM_OK : QM_E_CUDA;
+}
+
+int make_kv_tmaps(qm_kv* kv) {
+    kv->tmaps_ok = false;
+    if (encode_cache_tmap(&kv->tmap_k, kv->k, kv->batch, kv->capacity, 64) != QM_OK ||
+        encode_cache_tmap(&kv->tmap_v, kv->v, kv->batch, kv->capacity, 64) != QM_OK)
+        return set_error(kv->ctx, QM_E_CUDA, "cuTensorMapEncodeTiled failed for the KV cache");
+    kv->tmaps_ok = true;
+    return QM_OK;
+}
+
+}  // namespace qm
+
+// ---------------------------------------------------------------------------
+// status / shape
+// ---------------------------------------------------------------------------
+extern "C" int qm_shape_get(qm_shape* o) {
+    if (!o) return QM_E_ARG;
+    o->num_qk_heads = kNumQK;
+    o->num_v_heads = kNumV;
+    o->dn_head_dim = kHd;
+    o->conv_kernel = kConvK;
+    o->num_attn_heads = kNumH;
+    o->num_kv_heads = kNumKVH;
+    o->attn_head_dim = kD;
+    o->rope_dim = kRot;
+    o->rope_theta = 1.0e7f;
+    o->rms_eps = 1e-6f;
+    return QM_OK;
+}
+
+extern "C" const char* qm_status_string(int s) {
+    switch (s) {
+        case QM_OK: return "ok";
+        case QM_E_ARG: return "invalid argument";
+        case QM_E_SHAPE: return "shape or capacity mismatch";
+        case QM_E_OOM: return "out of device memory";
+        case QM_E_CUDA: return "CUDA error";
+        case QM_E_NCCL: return "NCCL error";
+        case QM_E_TIMEOUT: return "device-side wait timed out";
+        case QM_E_RANGE: return "position out of range";
+        case QM_E_MISMATCH: return "handle mismatch";
+        case QM_E_UNSUPPORTED: return "unsupported device";
+        case QM_E_CAPTURE: return "allocation needed during stream capture";
+        default: return "unknown status";
+    }
+}
+
+// ---------------------------------------------------------------------------
+// context
+// ---------------------------------------------------------------------------
+static void drop_events(qm_ctx* c);
+extern "C" int qm_ctx_create(int device, qm_ctx** out) {
+    if (!out) return QM_E_ARG;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return QM_E_ARG;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return QM_E_CUDA;
+    if (prop.major != 10) return QM_E_UNSUPPORTED;
+    qm_ctx* c = new (std::nothrow) qm_ctx();
+    if (!c) return QM_E_OOM;
+    c->device = device;
+    c->num_sms = prop.multiProcessorCount;
+    if (cudaSetDevice(device) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete c;
+        return QM_E_CUDA;
+    }
+    c->stream = c->own_stream;
+    if (cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess ||
+        cudaMemset(c->d_err, 0, sizeof(int)) != cudaSuccess) {
+        cudaStreamDestroy(c->own_stream);
+        delete c;
+        return QM_E_OOM;
+    }
+    *out = c;
+    return QM_OK;
+}
+
+extern "C" int qm_ctx_destroy(qm_ctx* c) {
+    if (!c) return QM_E_ARG;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    if (c->ws) cudaFree(c->ws);
+    if (c->stage) cudaFree(c->stage);
+    if (c->d_err) cudaFree(c->d_err);
+    drop_events(c);
+    for (cudaEvent_t e : c->event_pool) cudaEventDestroy(e);
+    if (c->own_stream) cudaStreamDestroy(c->own_stream);
+    delete c;
+    return QM_OK;
+}
+
+extern "C" int qm_ctx_set_stream(qm_ctx* c, void* stream) {
+    if (!c) return QM_E_ARG;
+    c->stream = stream ? (cudaStream_t)stream : c->own_stream;
+    return QM_OK;
+}
+
+extern "C" void* qm_ctx_get_stream(const qm_ctx* c) { return c ? (void*)c->stream : nullptr; }
+
+extern "C" int qm_sync(qm_ctx* c) {
+    if (!c) return QM_E_ARG;
+    cudaSetDevice(c->device);
+    QM_CHECK_CUDA(c, cudaStreamSynchronize(c->stream));
+    int err = 0;
+    QM_CHECK_CUDA(c, cudaMemcpy(&err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) {
+        cudaMemset(c->d_err, 0, sizeof(int));
+        return set_error(c, QM_E_TIMEOUT, "a device-side bounded wait gave up (error word set)");
+    }
+    return QM_OK;
+}
+
+extern "C" const char* qm_last_error(const qm_ctx* c) {
+    return c ? c->last_error.c_str() : "null context";
+}
+
+extern "C" int qm_ctx_reserve(qm_ctx* c, size_t bytes) {
+    if (!c) return QM_E_ARG;
+    cudaSetDevice(c->device);
+    return ensure_workspace(c, bytes);
+}
+
+extern "C" int64_t qm_ctx_launch_count(const qm_ctx* c) { return c ? c->launches : -1; }
+
+namespace qm {
+static cudaEvent_t pool_event(qm_ctx* c) {
+    if (!c->event_pool.empty()) {
+        cudaEvent_t e = c->event_pool.back();
+        c->event_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+TimedLaunch::TimedLaunch(qm_ctx* c, const char* name) : ctx(c) {
+    if (!c->timing) return;
+    cudaEvent_t start = pool_event(c);
+    stop = pool_event(c);
+    cudaEventRecord(start, c->stream);
+    c->events[name].push_back({start, stop});
+}
+
+TimedLaunch::~TimedLaunch() {
+    if (stop) cudaEventRecord(stop, ctx->stream);
+}
+}  // namespace qm
+
+static void drop_events(qm_ctx* c) {
+    for (auto& kv : c->events)
+        for (auto& pr : kv.second) {
+            c->event_pool.push_back(pr.first);
+            c->event_pool.push_back(pr.second);
+        }
+    c->events.clear();
+}
+
+extern "C" int qm_ctx_set_timing(qm_ctx* c, int on) {
+    if (!c) return QM_E_ARG;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    drop_events(c);
+    c->timing = on != 0;
+    return QM_OK;
+}
+
+extern "C" int qm_ctx_kernel_time(qm_ctx* c, const char* name, double* total_ms, int64_t* launches) {
+    if (!c || !name) return QM_E_ARG;
+    cudaSetDevice(c->device);
+    double t = 0.0;
+    int64_t n = 0;
+    auto it = c->events.find(name);
+    if (it != c->events.end()) {
+        for (auto& pr : it->second) {
+            QM_CHECK_CUDA(c, cudaEventSynchronize(pr.second));
+            float ms = 0.f;
+            QM_CHECK_CUDA(c, cudaEventElapsedTime(&ms, pr.first, pr.second));
+            t += ms;
+            n++;
+        }
+    }
+    if (total_ms) *total_ms = t;
+    if (launches) *launches = n;
+    return QM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// RoPE table: src/convert.rs:161-176, same f32 formula
+// ---------------------------------------------------------------------------
+extern "C" int qm_rope_table(float theta, int rope_dim, int max_pos, float* cos_h, float* sin_h) {
+    if (!cos_h || !sin_h || rope_dim <= 0 || (rope_dim & 1) || max_pos <= 0) return QM_E_ARG;
+    int half = rope_dim / 2;
+    std::vector<float> freq(half);
+    for (int i = 0; i < half; i++) {
+        volatile float e = 2.0f * (float)i;     // keep the f32 rounding steps of the reference
+        e = e / (float)rope_dim;
+        freq[i] = 1.0f / powf(theta, e);
+    }
+    for (int pos = 0; pos < max_pos; pos++) {
+        for (int i = 0; i < half; i++) {
+            volatile float angle = (float)pos * freq[i];
+            cos_h[(size_t)pos * half + i] = cosf(angle);
+            sin_h[(size_t)pos * half + i] = sinf(angle);
+        }
+    }
+    return QM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// DeltaNet state handles
+// ---------------------------------------------------------------------------
+static const size_t kSPerSeq = (size_t)kNumV * kHd * kHd;        // floats
+static const size_t kConvPerSeq = (size_t)kConvSlots * kQKVDim;  // floats
+
+extern "C" int qm_dn_state_create(qm_ctx* c, int batch, qm_dn_state** out) {
+    if (!c || !out || batch <= 0) return set_error(c, QM_E_ARG, "qm_dn_state_create: bad argument");
+    *out = nullptr;
+    cudaSetDevice(c->device);
+    qm_dn_state* st = new (std::nothrow) qm_dn_state();
+    if (!st) return QM_E_OOM;
+    st->ctx = c;
+    st->batch = batch;
+    st->owned = true;
+    if (cudaMalloc(&st->s, kSPerSeq * batch * 4) != cudaSuccess ||
+        cudaMalloc(&st->conv, kConvPerSeq * batch * 4) != cudaSuccess) {
+        if (st->s) cudaFree(st->s);
+        delete st;
+        return set_error(c, QM_E_OOM, "qm_dn_state_create: cudaMalloc failed");
+    }
+    int rc = qm_dn_state_reset(c, st);
+    if (rc != QM_OK) {
+        qm_dn_state_destroy(st);
+        return rc;
+    }
+    *out = st;
+    return QM_OK;
+}
+
+extern "C" int qm_dn_state_wrap(qm_ctx* c, int batch, float* s, float* conv, qm_dn_state** out) {
+    if (!c || !out || batch <= 0 || !s || !conv)
+        return set_error(c, QM_E_ARG, "qm_dn_state_wrap: bad argument");
+    if (((uintptr_t)s & 15) || ((uintptr_t)conv & 15))
+        return set_error(c, QM_E_ARG, "qm_dn_state_wrap: storage must be 16-byte aligned");
+    qm_dn_state* st = new (std::nothrow) qm_dn_state();
+    if (!st) return QM_E_OOM;
+    st->ctx = c;
+    st->batch = batch;
+    st->s = s;
+    st->conv = conv;
+    st->owned = false;
+    *out = st;
+    return QM_OK;
+}
+
+extern "C" int qm_dn_state_destroy(qm_dn_state* st) {
+    if (!st) return QM_E_ARG;
+    if (st->owned) {
+        cudaSetDevice(st->ctx->device);
+        cudaStreamSynchronize(st->ctx->stream);
+        cudaFree(st->s);
+        cudaFree(st->conv);
+    }
+    delete st;
+    return QM_OK;
+}
+
+extern "C" int qm_dn_state_reset(qm_ctx* c, qm_dn_state* st) {
+    if (!c || !st) return QM_E_ARG;
+    if (st->ctx != c) return set_error(c, QM_E_MISMATCH, "state belongs to another context");
+    cudaSetDevice(c->device);
+    QM_CHECK_CUDA(c, cudaMemsetAsync(st->s, 0, kSPerSeq * st->batch * 4, c->stream));
+    QM_CHECK_CUDA(c, cudaMemsetAsync(st->conv, 0, kConvPerSeq * st->batch * 4, c->stream));
+    st->conv_pos = 0;
+    return QM_OK;
+}
+
+extern "C" int qm_dn_state_snapshot(qm_ctx* c, const qm_dn_state* src, qm_dn_state** out) {
+    if (!c || !src || !out) return QM_E_ARG;
+    int rc = qm_dn_state_create(c, src->batch, out);
+    if (rc != QM_OK) return rc;
+    rc = qm_dn_state_restore(c, *out, src);
+    if (rc != QM_OK) {
+        qm_dn_state_destroy(*out);
+        *out = nullptr;
+    }
+    return rc;
+}
+
+extern "C" int qm_dn_state_restore(qm_ctx* c, qm_dn_state* dst, const qm_dn_state* src) {
+    if (!c || !dst || !src) return QM_E_ARG;
+    if (dst->batch != src->batch)
+        return set_error(c, QM_E_MISMATCH, "restore: batch sizes differ (reference: panic)");
+    cudaSetDevice(c->device);
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(dst->s, src->s, kSPerSeq * src->batch * 4,
+                                     cudaMemcpyDeviceToDevice, c->stream));
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(dst->conv, src->conv, kConvPerSeq * src->batch * 4,
+                                     cudaMemcpyDeviceToDevice, c->stream));
+    dst->conv_pos = src->conv_pos;
+    return QM_OK;
+}
+
+// Reference conv_buf[ch*3 + j] holds token conv_pos-3+j; the ring keeps
+// token t in slot t % 4.
+static inline int ring_slot(int64_t conv_pos, int j) {
+    int64_t t = conv_pos - 3 + j;
+    return (int)(((t % 4) + 4) % 4);
+}
+
+extern "C" int qm_dn_state_read(qm_ctx* c, const qm_dn_state* st, int b, float* s_h, float* conv_h) {
+    if (!c || !st || b < 0 || b >= st->batch) return set_error(c, QM_E_ARG, "qm_dn_state_read: bad argument");
+    cudaSetDevice(c->device);
+    QM_CHECK_CUDA(c, cudaStreamSynchronize(c->stream));
+    if (s_h)
+        QM_CHECK_CUDA(c, cudaMemcpy(s_h, st->s + kSPerSeq * b, kSPerSeq * 4, cudaMemcpyDeviceToHost));
+    if (conv_h) {
+        std::vector<float> ring(kConvPerSeq);
+        QM_CHECK_CUDA(c, cudaMemcpy(ring.data(), st->conv + kConvPerSeq * b, kConvPerSeq * 4,
+                                    cudaMemcpyDeviceToHost));
+        for (int j = 0; j < 3; j++) {
+            const float* slot = ring.data() + (size_t)ring_slot(st->conv_pos, j) * kQKVDim;
+            for (int ch = 0; ch < kQKVDim; ch++) conv_h[(size_t)ch * 3 + j] = slot[ch];
+        }
+    }
+    return QM_OK;
+}
+
+extern "C" int qm_dn_state_write(qm_ctx* c, qm_dn_state* st, int b, const float* s_h,
+                                 const float* conv_h) {
+    if (!c || !st || b < 0 || b >= st->batch) return set_error(c, QM_E_ARG, "qm_dn_state_write: bad argument");
+    cudaSetDevice(c->device);
+    QM_CHECK_CUDA(c, cudaStreamSynchronize(c->stream));
+    if (s_h)
+        QM_CHECK_CUDA(c, cudaMemcpy(st->s + kSPerSeq * b, s_h, kSPerSeq * 4, cudaMemcpyHostToDevice));
+    if (conv_h) {
+        std::vector<float> ring(kConvPerSeq, 0.0f);
+        for (int j = 0; j < 3; j++) {
+            float* slot = ring.data() + (size_t)ring_slot(st->conv_pos, j) * kQKVDim;
+            for (int ch = 0; ch < kQKVDim; ch++) slot[ch] = conv_h[(size_t)ch * 3 + j];
+        }
+        QM_CHECK_CUDA(c, cudaMemcpy(st->conv + kConvPerSeq * b, ring.data(), kConvPerSeq * 4,
+                                    cudaMemcpyHostToDevice));
+    }
+    return QM_OK;
+}
+
+extern "C" int64_t qm_dn_state_conv_pos(const qm_dn_state* st) { return st ? st->conv_pos : -1; }
+extern "C" int qm_dn_state_set_conv_pos(qm_dn_state* st, int64_t p) {
+    if (!st || p < 0) return QM_E_ARG;
+    st->conv_pos = p;
+    return QM_OK;
+}
+extern "C" int qm_dn_state_batch(const qm_dn_state* st) { return st ? st->batch : -1; }
+extern "C" int qm_dn_state_data(const qm_dn_state* st, float** s, float** conv) {
+    if (!st) return QM_E_ARG;
+    if (s) *s = st->s;
+    if (conv) *conv = st->conv;
+    return QM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// DeltaNet decode
+// ---------------------------------------------------------------------------
+static int check_dn_params(qm_ctx* c, const qm_dn_params* p, bool need_gamma) {
+    if (!p || !p->conv_w || !p->a_log || !p->dt_bias || (need_gamma && !p->norm_gamma))
+        return set_error(c, QM_E_ARG, "DeltaNet params: null pointer");
+    if ((uintptr_t)p->conv_w & 15) return set_error(c, QM_E_ARG, "conv_w must be 16-byte aligned");
+    return QM_OK;
+}
+
+extern "C" int qm_dn_decode(qm_ctx* c, const qm_dn_params* p, qm_dn_state* st, const float* qkv,
+                            const float* a, const float* b, float* y, const float* z, float* out) {
+    if (!c) return QM_E_ARG;
+    if (!st || !qkv || !a || !b || (!y && !out) || (out && !z) || (z && !out))
+        return set_error(c, QM_E_ARG, "qm_dn_decode: null pointer (y or z+out required)");
+    if (st->ctx != c) return set_error(c, QM_E_MISMATCH, "state belongs to another context");
+    int rc = check_dn_params(c, p, z != nullptr);
+    if (rc) return rc;
+    if (((uintptr_t)qkv & 15)) return set_error(c, QM_E_ARG, "qkv must be 16-byte aligned");
+    cudaSetDevice(c->device);
+    cudaError_t e = launch_dn_decode(c, p, st, qkv, a, b, y, z, out);
+    if (e != cudaSuccess) return cuda_error(c, e, "dn_decode launch");
+    st->conv_pos += 1;
+    return QM_OK;
+}
+
+extern "C" int qm_dn_decode_host(qm_ctx* c, const qm_dn_params* p, qm_dn_state* st,
+                                 const float* qkv, const float* a, const float* b, float* y,
+                                 const float* z, float* out) {
+    if (!c || !st) return QM_E_ARG;
+    const size_t B = st->batch;
+    const size_t n_qkv = B * kQKVDim, n_ab = B * kNumV, n_y = B * kVDim;
+    size_t bytes = 4 * (n_qkv + 2 * n_ab + (y ? n_y : 0) + (z ? 2 * n_y : 0)) + 256 * 6;
+    cudaSetDevice(c->device);
+    int rc = ensure_stage(c, bytes);
+    if (rc) return rc;
+    char* base = (char*)c->stage;
+    auto carve = [&](size_t n) {
+        float* r = (float*)base;
+        base += (n * 4 + 255) & ~size_t(255);
+        return r;
+    };
+    float* d_qkv = carve(n_qkv);
+    float* d_a = carve(n_ab);
+    float* d_b = carve(n_ab);
+    float* d_y = y ? carve(n_y) : nullptr;
+    float* d_z = z ? carve(n_y) : nullptr;
+    float* d_out = z ? carve(n_y) : nullptr;
+    cudaStream_t s = c->stream;
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(d_qkv, qkv, n_qkv * 4, cudaMemcpyHostToDevice, s));
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(d_a, a, n_ab * 4, cudaMemcpyHostToDevice, s));
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(d_b, b, n_ab * 4, cudaMemcpyHostToDevice, s));
+    if (z) QM_CHECK_CUDA(c, cudaMemcpyAsync(d_z, z, n_y * 4, cudaMemcpyHostToDevice, s));
+    rc = qm_dn_decode(c, p, st, d_qkv, d_a, d_b, d_y, d_z, d_out);
+    if (rc) return rc;
+    if (y) QM_CHECK_CUDA(c, cudaMemcpyAsync(y, d_y, n_y * 4, cudaMemcpyDeviceToHost, s));
+    if (out) QM_CHECK_CUDA(c, cudaMemcpyAsync(out, d_out, n_y * 4, cudaMemcpyDeviceToHost, s));
+    return qm_sync(c);
+}
+
+// ---------------------------------------------------------------------------
+// KV cache handles
+// ---------------------------------------------------------------------------
+static size_t kv_elems(int batch, int cap) { return (size_t)batch * kNumKVH * cap * kD; }
+
+extern "C" int qm_kv_create(qm_ctx* c, int batch, int capacity, qm_kv** out) {
+    if (!c || !out || batch <= 0 || capacity <= 0)
+        return set_error(c, QM_E_ARG, "qm_kv_create: bad argument");
+    *out = nullptr;
+    cudaSetDevice(c->device);
+    qm_kv* kv = new (std::nothrow) qm_kv();
+    if (!kv) return QM_E_OOM;
+    kv->ctx = c;
+    kv->batch = batch;
+    kv->capacity = capacity;
+    kv->owned = true;
+    size_t bytes = kv_elems(batch, capacity) * 2;
+    if (cudaMalloc(&kv->k, bytes) != cudaSuccess || cudaMalloc(&kv->v, bytes) != cudaSuccess) {
+        if (kv->k) cudaFree(kv->k);
+        delete kv;
+        return set_error(c, QM_E_OOM, "qm_kv_create: cudaMalloc failed");
+    }
+    cudaMemsetAsync(kv->k, 0, bytes, c->stream);
+    cudaMemsetAsync(kv->v, 0, bytes, c->stream);
+    int rc = make_kv_tmaps(kv);
+    if (rc) {
+        qm_kv_destroy(kv);
+        return rc;
+    }
+    *out = kv;
+    return QM_OK;
+}
+
+extern "C" int qm_kv_wrap(qm_ctx* c, int batch, int capacity, uint16_t* k, uint16_t* v, qm_kv** out) {
+    if (!c || !out || batch <= 0 || capacity <= 0 || !k || !v)
+        return set_error(c, QM_E_ARG, "qm_kv_wrap: bad argument");
+    if (((uintptr_t)k & 15) || ((uintptr_t)v & 15))
+        return set_error(c, QM_E_ARG, "qm_kv_wrap: cache must be 16-byte aligned");
+    qm_kv* kv = new (std::nothrow) qm_kv();
+    if (!kv) return QM_E_OOM;
+    kv->ctx = c;
+    kv->batch = batch;
+    kv->capacity = capacity;
+    kv->k = k;
+    kv->v = v;
+    kv->owned = false;
+    int rc = make_kv_tmaps(kv);
+    if (rc) {
+        delete kv;
+        return rc;
+    }
+    *out = kv;
+    return QM_OK;
+}
+
+extern "C" int qm_kv_destroy(qm_kv* kv) {
+    if (!kv) return QM_E_ARG;
+    if (kv->owned) {
+        cudaSetDevice(kv->ctx->device);
+        cudaStreamSynchronize(kv->ctx->stream);
+        cudaFree(kv->k);
+        cudaFree(kv->v);
+    }
+    delete kv;
+    return QM_OK;
+}
+
+extern "C" int qm_kv_snapshot(qm_ctx* c, const qm_kv* src, qm_kv** out) {
+    if (!c || !src || !out) return QM_E_ARG;
+    int rc = qm_kv_create(c, src->batch, src->capacity, out);
+    if (rc) return rc;
+    rc = qm_kv_restore(c, *out, src);
+    if (rc) {
+        qm_kv_destroy(*out);
+        *out = nullptr;
+    }
+    return rc;
+}
+
+extern "C" int qm_kv_restore(qm_ctx* c, qm_kv* dst, const qm_kv* src) {
+    if (!c || !dst || !src) return QM_E_ARG;
+    if (dst->batch != src->batch || dst->capacity < src->seq_len)
+        return set_error(c, QM_E_MISMATCH, "kv restore: batch or capacity mismatch");
+    cudaSetDevice(c->device);
+    // Copy the filled prefix of every (sequence, kv-head) row block.
+    size_t row = (size_t)kD * 2;
+    QM_CHECK_CUDA(c, cudaMemcpy2DAsync(dst->k, (size_t)dst->capacity * row, src->k,
+                                       (size_t)src->capacity * row, (size_t)src->seq_len * row,
+                                       (size_t)src->batch * kNumKVH, cudaMemcpyDeviceToDevice,
+                                       c->stream));
+    QM_CHECK_CUDA(c, cudaMemcpy2DAsync(dst->v, (size_t)dst->capacity * row, src->v,
+                                       (size_t)src->capacity * row, (size_t)src->seq_len * row,
+                                       (size_t)src->batch * kNumKVH, cudaMemcpyDeviceToDevice,
+                                       c->stream));
+    dst->seq_len = src->seq_len;
+    return QM_OK;
+}
+
+extern "C" int64_t qm_kv_seq_len(const qm_kv* kv) { return kv ? kv->seq_len : -1; }
+extern "C" int qm_kv_set_seq_len(qm_kv* kv, int64_t n) {
+    if (!kv || n < 0 || n > kv->capacity) return QM_E_ARG;
+    kv->seq_len = n;
+    return QM_OK;
+}
+extern "C" int qm_kv_capacity(const qm_kv* kv) { return kv ? kv->capacity : -1; }
+extern "C" int qm_kv_batch(const qm_kv* kv) { return kv ? kv->batch : -1; }
+extern "C" int qm_kv_data(const qm_kv* kv, uint16_t** k, uint16_t** v) {
+    if (!kv) return QM_E_ARG;
+    if (k) *k = kv->k;
+    if (v) *v = kv->v;
+    return QM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// GQA decode
+// ---------------------------------------------------------------------------
+static int check_gqa_params(qm_ctx* c, const qm_gqa_params* p) {
+    if (!p || !p->q_norm || !p->k_norm || !p->rope_cos || !p->rope_sin || p->max_pos <= 0)
+        return set_error(c, QM_E_ARG, "GQA params: null pointer or max_pos <= 0");
+    return QM_OK;
+}
+
+extern "C" int qm_gqa_decode(qm_ctx* c, const qm_gqa_params* p, qm_kv* kv, const float* q_gate,
+                             const float* k_new, const float* v_new, float* out) {
+    if (!c) return QM_E_ARG;
+    if (!kv || !q_gate || !k_new || !v_new || !out)
+        return set_error(c, QM_E_ARG, "qm_gqa_decode: null pointer");
+    if (kv->ctx != c) return set_error(c, QM_E_MISMATCH, "cache belongs to another context");
+    int rc = check_gqa_params(c, p);
+    if (rc) return rc;
+    if (kv->seq_len >= kv->capacity)
+        return set_error(c, QM_E_RANGE, "qm_gqa_decode: KV cache full");
+    if (kv->seq_len >= p->max_pos)
+        return set_error(c, QM_E_RANGE, "qm_gqa_decode: position beyond the RoPE table");
+    cudaSetDevice(c->device);
+    size_t ws = gqa_decode_ws_bytes(kv->batch, kv->seq_len, c->num_sms);
+    rc = ensure_workspace(c, ws);
+    if (rc) return rc;
+    cudaError_t e = launch_gqa_decode(c, p, kv, q_gate, k_new, v_new, out, c->ws, c->ws_bytes);
+    if (e != cudaSuccess) return cuda_error(c, e, "gqa_decode launch");
+    kv->seq_len += 1;
+    return QM_OK;
+}
+
+extern "C" int qm_gqa_decode_host(qm_ctx* c, const qm_gqa_params* p, qm_kv* kv,
+                                  const float* q_gate, const float* k_new, const float* v_new,
+                                  float* out) {
+    if (!c || !kv) return QM_E_ARG;
+    const size_t B = kv->batch;
+    const size_t n_q = B * kNumH * 2 * kD, n_kv = B * kNumKVH * kD, n_o = B * kNumH * kD;
+    cudaSetDevice(c->device);
+    int rc = ensure_stage(c, 4 * (n_q + 2 * n_kv + n_o) + 1024);
+    if (rc) return rc;
+    char* base = (char*)c->stage;
+    auto carve = [&](size_t n) {
+        float* r = (float*)base;
+        base += (n * 4 + 255) & ~size_t(255);
+        return r;
+    };
+    float* d_q = carve(n_q);
+    float* d_k = carve(n_kv);
+    float* d_v = carve(n_kv);
+    float* d_o = carve(n_o);
+    cudaStream_t s = c->stream;
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(d_q, q_gate, n_q * 4, cudaMemcpyHostToDevice, s));
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(d_k, k_new, n_kv * 4, cudaMemcpyHostToDevice, s));
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(d_v, v_new, n_kv * 4, cudaMemcpyHostToDevice, s));
+    rc = qm_gqa_decode(c, p, kv, d_q, d_k, d_v, d_o);
+    if (rc) return rc;
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(out, d_o, n_o * 4, cudaMemcpyDeviceToHost, s));
+    return qm_sync(c);
+}
+
+// ---------------------------------------------------------------------------
+// Prefill entry points (argument checks; kernels in gqa_prefill.cu / dn_prefill.cu)
+// ---------------------------------------------------------------------------
+#ifndef QM_HAVE_PREFILL
+extern "C" int qm_dn_prefill(qm_ctx* c, const qm_dn_params*, qm_dn_state*, int, const uint16_t*,
+                             const float*, const float*, float*, const float*, float*) {
+    return set_error(c, QM_E_UNSUPPORTED, "qm_dn_prefill: not built in this version");
+}
+extern "C" int qm_gqa_prefill(qm_ctx* c, const qm_gqa_params*, qm_kv*, int, const uint16_t*,
+                              const uint16_t*, const uint16_t*, float*) {
+    return set_error(c, QM_E_UNSUPPORTED, "qm_gqa_prefill: not built in this version");
+}
+#endif

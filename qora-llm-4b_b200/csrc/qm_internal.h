@@ -1,0 +1,109 @@
+// Internal definitions shared by the library's translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <map>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "qora_mixer.h"
+
+namespace qm {
+
+// Qor4bConfig::default_4b mixer fields (src/config.rs:52-78).
+constexpr int kNumQK = 16;
+constexpr int kNumV = 32;
+constexpr int kHd = 128;                            // DeltaNet head dim
+constexpr int kConvK = 4;
+constexpr int kQDim = kNumQK * kHd;                 // 2048
+constexpr int kVDim = kNumV * kHd;                  // 4096
+constexpr int kQKVDim = 2 * kQDim + kVDim;          // 8192
+constexpr int kConvSlots = 4;                       // ring of the last 4 inputs
+constexpr int kNumH = 16;                           // attention Q heads
+constexpr int kNumKVH = 4;
+constexpr int kD = 256;                             // attention head dim
+constexpr int kGroup = kNumH / kNumKVH;             // 4
+constexpr int kRot = 64;                            // rope_dim
+constexpr int kHalfRot = kRot / 2;                  // 32
+
+// Device-side error word bits (set by bounded waits that give up).
+constexpr int kErrTimeout = 1;
+
+}  // namespace qm
+
+struct qm_ctx {
+    int device = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    int* d_err = nullptr;           // device error word
+    void* ws = nullptr;             // workspace (split-KV partials, staging)
+    size_t ws_bytes = 0;
+    int num_sms = 0;
+    int64_t launches = 0;
+    std::string last_error;
+    // host-staging for the _host variants (device side)
+    void* stage = nullptr;
+    size_t stage_bytes = 0;
+    // optional per-kernel CUDA-event timing (qm_ctx_set_timing)
+    bool timing = false;
+    std::map<std::string, std::vector<std::pair<cudaEvent_t, cudaEvent_t>>> events;
+    std::vector<cudaEvent_t> event_pool;
+};
+
+struct qm_dn_state {
+    qm_ctx* ctx = nullptr;
+    int batch = 0;
+    float* s = nullptr;       // [B, 32, 128, 128]
+    float* conv = nullptr;    // [B, 4, 8192] ring, token t in slot t % 4
+    int64_t conv_pos = 0;
+    bool owned = false;
+};
+
+struct qm_kv {
+    qm_ctx* ctx = nullptr;
+    int batch = 0;
+    int capacity = 0;
+    uint16_t* k = nullptr;    // [B, 4, cap, 256] bf16
+    uint16_t* v = nullptr;
+    int64_t seq_len = 0;
+    bool owned = false;
+    CUtensorMap tmap_k;       // 3-D view {256, cap, B*4}, box {64, 64, 1}, 128B swizzle
+    CUtensorMap tmap_v;
+    bool tmaps_ok = false;
+};
+
+namespace qm {
+
+int set_error(qm_ctx* ctx, int code, const std::string& msg);
+int cuda_error(qm_ctx* ctx, cudaError_t e, const char* what);
+int ensure_workspace(qm_ctx* ctx, size_t bytes);
+int ensure_stage(qm_ctx* ctx, size_t bytes);
+int make_kv_tmaps(qm_kv* kv);
+
+// Records a start/stop event pair around a launch when ctx->timing is on.
+struct TimedLaunch {
+    qm_ctx* ctx;
+    cudaEvent_t stop = nullptr;
+    TimedLaunch(qm_ctx* c, const char* name);
+    ~TimedLaunch();
+};
+
+// Kernel launchers (return cudaError_t from the launch).
+cudaError_t launch_dn_decode(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, const float* qkv,
+                             const float* a, const float* b, float* y, const float* z, float* out);
+cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, const float* q_gate,
+                              const float* k_new, const float* v_new, float* out, void* ws,
+                              size_t ws_bytes);
+size_t gqa_decode_ws_bytes(int batch, int64_t seq_len, int num_sms);
+
+}  // namespace qm
+
+#define QM_CHECK_CUDA(ctx, expr)                                  \
+    do {                                                          \
+        cudaError_t _e = (expr);                                  \
+        if (_e != cudaSuccess) return qm::cuda_error(ctx, _e, #expr); \
+    } while (0)

@@ -1,0 +1,168 @@
+"""DeltaNet decode on the GPU vs the CPU restatement of src/gemv.rs:744-883.
+
+Tolerance (north_star, fp32-state decode): max|gpu - cpu| / RMS(cpu) <= 1e-3.
+The conv history holds raw inputs, so it must match bit for bit.
+"""
+import numpy as np
+import pytest
+
+import refmath
+from gpu_util import dev, host, make_ctx
+from qora_mixer import inputs as I
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = make_ctx()
+    yield c
+    c.close()
+
+
+def _run(ctx, orc, B, T, seed, fused, seed_state=False):
+    import torch
+
+    import qora_mixer as qm
+
+    g = I.rng(seed)
+    p = I.dn_layer_params(g)
+    toks = I.dn_token_inputs(g, T, B)
+    c = orc.cfg_4b()
+    avx = orc.has_avx512()
+    ost = [orc.DnState(c) for _ in range(B)]
+    st = qm.DnState(ctx, B)
+    if seed_state:
+        for bi in range(B):
+            ost[bi].s[:] = (g.standard_normal(ost[bi].s.shape) * 0.02).astype(np.float32)
+            ost[bi].conv_buf[:] = (g.standard_normal(ost[bi].conv_buf.shape) * 0.02).astype(np.float32)
+            st.write(bi, ost[bi].s, ost[bi].conv_buf)
+    keep = [dev(p["conv_w"]), dev(p["a_log"]), dev(p["dt_bias"]), dev(p["norm_gamma"])]
+    prm = qm.dn_params(*keep)
+    mx = qm.Mixer(ctx)
+    y = torch.empty(B, 32, 128, device="cuda")
+    out = torch.empty(B, 4096, device="cuda") if fused else None
+    worst_y = worst_o = 0.0
+    for t in range(T):
+        z = dev(toks["z"][:, t]) if fused else None
+        mx.dn_decode(prm, st, dev(toks["qkv"][:, t]), dev(toks["a"][:, t]), dev(toks["b"][:, t]),
+                     y, z, out)
+        ctx.sync()
+        yg = host(y)
+        og = host(out) if fused else None
+        for bi in range(B):
+            r = orc.dn_decode(c, ost[bi], toks["qkv"][bi, t], toks["a"][bi, t], toks["b"][bi, t],
+                              p["conv_w"], p["a_log"], p["dt_bias"], use_avx512=avx,
+                              z=toks["z"][bi, t] if fused else None,
+                              norm_gamma=p["norm_gamma"] if fused else None)
+            yo, go = (r if fused else (r, None))
+            worst_y = max(worst_y, refmath.rel_err(yg[bi], yo))
+            if fused:
+                worst_o = max(worst_o, refmath.rel_err(og[bi], go))
+    assert worst_y <= TOL, f"y rel err {worst_y:.3e}"
+    assert worst_o <= TOL, f"gated rel err {worst_o:.3e}"
+    assert st.conv_pos == T
+    for bi in range(B):
+        s_g, cb_g = st.read(bi)
+        assert refmath.rel_err(s_g, ost[bi].s) <= TOL
+        np.testing.assert_array_equal(cb_g, ost[bi].conv_buf)
+    return st
+
+
+def test_config0_decode_256_tokens(ctx, orc):
+    """Config 0: one DeltaNet layer, batch 1, 256 sequential tokens."""
+    _run(ctx, orc, B=1, T=256, seed=0x51A0 + 0, fused=False)
+
+
+@pytest.mark.parametrize("B,fused", [(1, True), (3, True), (3, False), (8, True), (8, False)])
+def test_decode_batch_and_split_variants(ctx, orc, B, fused):
+    """B=1 -> 4 CTAs per head (cluster epilogue), B=3 -> 2, B=8 -> 1."""
+    _run(ctx, orc, B=B, T=5, seed=200 + B, fused=fused)
+
+
+def test_decode_config4_batch_seeded_state(ctx, orc):
+    """Config-4 batch (64 sequences) from N(0, 0.02) states, two tokens."""
+    _run(ctx, orc, B=64, T=2, seed=0x51A0 + 4, fused=True, seed_state=True)
+
+
+def test_state_snapshot_restore_roundtrip(ctx, orc):
+    import torch
+
+    import qora_mixer as qm
+
+    g = I.rng(300)
+    p = I.dn_layer_params(g)
+    toks = I.dn_token_inputs(g, 4, 2)
+    keep = [dev(p["conv_w"]), dev(p["a_log"]), dev(p["dt_bias"])]
+    prm = qm.dn_params(*keep)
+    mx = qm.Mixer(ctx)
+    st = qm.DnState(ctx, 2)
+    y = torch.empty(2, 32, 128, device="cuda")
+    for t in range(2):
+        mx.dn_decode(prm, st, dev(toks["qkv"][:, t]), dev(toks["a"][:, t]), dev(toks["b"][:, t]), y)
+    snap = st.snapshot()
+    ys = []
+    for t in range(2, 4):
+        mx.dn_decode(prm, st, dev(toks["qkv"][:, t]), dev(toks["a"][:, t]), dev(toks["b"][:, t]), y)
+        ys.append(host(y).copy())
+    st.restore_from(snap)
+    assert st.conv_pos == 2
+    for i, t in enumerate(range(2, 4)):
+        mx.dn_decode(prm, st, dev(toks["qkv"][:, t]), dev(toks["a"][:, t]), dev(toks["b"][:, t]), y)
+        np.testing.assert_array_equal(host(y), ys[i])
+    st.reset()
+    s0, cb0 = st.read(1)
+    assert not s0.any() and not cb0.any() and st.conv_pos == 0
+    snap.close()
+
+
+def test_host_variant_matches_device_variant(ctx):
+    import torch
+
+    import qora_mixer as qm
+
+    g = I.rng(301)
+    p = I.dn_layer_params(g)
+    toks = I.dn_token_inputs(g, 1, 4)
+    keep = [dev(p["conv_w"]), dev(p["a_log"]), dev(p["dt_bias"]), dev(p["norm_gamma"])]
+    prm = qm.dn_params(*keep)
+    mx = qm.Mixer(ctx)
+    s1, s2 = qm.DnState(ctx, 4), qm.DnState(ctx, 4)
+    y = torch.empty(4, 32, 128, device="cuda")
+    out = torch.empty(4, 4096, device="cuda")
+    mx.dn_decode(prm, s1, dev(toks["qkv"][:, 0]), dev(toks["a"][:, 0]), dev(toks["b"][:, 0]), y,
+                 dev(toks["z"][:, 0]), out)
+    yh = np.empty((4, 32, 128), np.float32)
+    oh = np.empty((4, 4096), np.float32)
+    mx.dn_decode_host(prm, s2, np.ascontiguousarray(toks["qkv"][:, 0]),
+                      np.ascontiguousarray(toks["a"][:, 0]), np.ascontiguousarray(toks["b"][:, 0]),
+                      yh, np.ascontiguousarray(toks["z"][:, 0]), oh)
+    ctx.sync()
+    np.testing.assert_array_equal(yh, host(y))
+    np.testing.assert_array_equal(oh, host(out))
+
+
+def test_decode_argument_errors(ctx):
+    import torch
+
+    import qora_mixer as qm
+
+    g = I.rng(302)
+    p = I.dn_layer_params(g)
+    keep = [dev(p["conv_w"]), dev(p["a_log"]), dev(p["dt_bias"])]
+    prm = qm.dn_params(*keep)
+    mx = qm.Mixer(ctx)
+    st = qm.DnState(ctx, 1)
+    qkv = torch.zeros(1, 8192, device="cuda")
+    ab = torch.zeros(1, 32, device="cuda")
+    out = torch.empty(1, 4096, device="cuda")
+    with pytest.raises(qm.QmError) as e:
+        mx.dn_decode(prm, st, qkv, ab, ab, None, None, out)  # out without z
+    assert e.value.code == 1
+    other = qm.Ctx(0)
+    with pytest.raises(qm.QmError) as e:
+        qm.Mixer(other).dn_decode(prm, st, qkv, ab, ab, torch.empty(1, 32, 128, device="cuda"))
+    assert e.value.code == 8  # QM_E_MISMATCH
+    assert st.conv_pos == 0
+    other.close()

@@ -1,0 +1,147 @@
+"""GQA decode on the GPU vs the CPU restatement of src/gemv.rs:927-1011.
+
+The cache positions already present are bf16 (configs 1 and 4); the oracle
+attends over exactly those values widened to f32 plus the new token in f32,
+as the reference would after loading them.  After each step the oracle's
+copy of the appended row is replaced by the widened bf16 row the GPU stored,
+so multi-step runs compare like with like.
+Tolerance: max|gpu - cpu| / RMS(cpu) <= 1e-3.
+"""
+import numpy as np
+import pytest
+
+import refmath
+from gpu_util import dev, host, make_ctx
+from qora_mixer import inputs as I
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = make_ctx()
+    yield c
+    c.close()
+
+
+def _setup(ctx, orc, B, L, cap, seed, max_pos=None):
+    import torch
+
+    import qora_mixer as qm
+
+    g = I.rng(seed)
+    max_pos = max_pos or cap + 1
+    pr = I.gqa_layer_params(g, max_pos)
+    cos, sin = qm.rope_table(1.0e7, 64, max_pos)
+    K = torch.zeros(B, 4, cap, 256, dtype=torch.int16, device="cuda")
+    V = torch.zeros_like(K)
+    c = orc.cfg_4b()
+    okv = []
+    if L > 0:
+        kb, vb = I.gqa_cache_bf16(g, B, L)
+        K[:, :, :L] = dev(kb)
+        V[:, :, :L] = dev(vb)
+    for bi in range(B):
+        kv = orc.KvCache(c, cap + 1)
+        if L > 0:
+            kv.k[:L] = I.bf16_bits_to_f32(kb[bi]).transpose(1, 0, 2)
+            kv.v[:L] = I.bf16_bits_to_f32(vb[bi]).transpose(1, 0, 2)
+            kv.seq_len[0] = L
+        okv.append(kv)
+    kvh = qm.KvCache(ctx, B, cap, K, V)
+    kvh.seq_len = L
+    keep = [dev(pr["q_norm"]), dev(pr["k_norm"]), dev(cos), dev(sin)]
+    prm = qm.gqa_params(*keep)
+    return g, c, pr, cos, sin, K, V, okv, kvh, prm, keep
+
+
+def _steps(ctx, orc, B, L, cap, steps, seed):
+    import torch
+
+    import qora_mixer as qm
+
+    g, c, pr, cos, sin, K, V, okv, kvh, prm, keep = _setup(ctx, orc, B, L, cap, seed)
+    mx = qm.Mixer(ctx)
+    out = torch.empty(B, 16, 256, device="cuda")
+    worst = 0.0
+    for s in range(steps):
+        tok = I.gqa_token_inputs(g, B)
+        pos = L + s
+        mx.gqa_decode(prm, kvh, dev(tok["q_gate"]), dev(tok["k_new"]), dev(tok["v_new"]), out)
+        ctx.sync()
+        og = host(out)
+        kg = host(K[:, :, pos])  # [B,4,256] bf16 bits appended by the GPU
+        vg = host(V[:, :, pos])
+        for bi in range(B):
+            ref = orc.gqa_decode(c, okv[bi], tok["q_gate"][bi], tok["k_new"][bi], tok["v_new"][bi],
+                                 pr["q_norm"], pr["k_norm"], cos, sin)
+            worst = max(worst, refmath.rel_err(og[bi], ref))
+            # appended row = bf16(post-norm/RoPE k), bf16(raw v): within one bf16 ulp
+            ko = okv[bi].k[pos]
+            kgf = I.bf16_bits_to_f32(kg[bi])
+            assert np.all(np.abs(kgf - ko) <= np.abs(ko) * 2.0 ** -7 + 1e-30)
+            np.testing.assert_array_equal(vg[bi], I.f32_to_bf16_bits(tok["v_new"][bi]))
+            okv[bi].k[pos] = kgf
+            okv[bi].v[pos] = I.bf16_bits_to_f32(vg[bi])
+        assert kvh.seq_len == pos + 1
+    assert worst <= TOL, f"rel err {worst:.3e}"
+    return worst
+
+
+def test_config1_decode_L4096(ctx, orc):
+    """Config 1: batch 1, 4096 cached bf16 positions, new token at position 4096."""
+    _steps(ctx, orc, B=1, L=4096, cap=4100, steps=1, seed=0x51A0 + 1)
+
+
+@pytest.mark.parametrize("B,L", [(1, 0), (1, 1), (2, 63), (2, 64), (3, 65), (1, 200), (2, 1000)])
+def test_decode_edge_lengths(ctx, orc, B, L):
+    """Empty cache, partial tiles, tile boundaries, odd batch sizes; 3 steps each."""
+    _steps(ctx, orc, B=B, L=L, cap=L + 8, steps=3, seed=400 + L + B)
+
+
+def test_decode_long_context_batch(ctx, orc):
+    """Config-4 context length (32768 cached positions) at batch 2."""
+    _steps(ctx, orc, B=2, L=32768, cap=32770, steps=1, seed=0x51A0 + 4)
+
+
+def test_cache_full_and_rope_range_errors(ctx, orc):
+    import torch
+
+    import qora_mixer as qm
+
+    g, c, pr, cos, sin, K, V, okv, kvh, prm, keep = _setup(ctx, orc, 1, 8, 8, 500)
+    mx = qm.Mixer(ctx)
+    tok = I.gqa_token_inputs(g, 1)
+    out = torch.empty(1, 16, 256, device="cuda")
+    with pytest.raises(qm.QmError) as e:
+        mx.gqa_decode(prm, kvh, dev(tok["q_gate"]), dev(tok["k_new"]), dev(tok["v_new"]), out)
+    assert e.value.code == 7  # QM_E_RANGE: cache full
+    g, c, pr, cos, sin, K, V, okv, kvh, prm, keep = _setup(ctx, orc, 1, 8, 16, 501, max_pos=8)
+    with pytest.raises(qm.QmError) as e:
+        mx.gqa_decode(prm, kvh, dev(tok["q_gate"]), dev(tok["k_new"]), dev(tok["v_new"]), out)
+    assert e.value.code == 7  # QM_E_RANGE: past the RoPE table (reference indexes past it)
+    assert kvh.seq_len == 8
+
+
+def test_snapshot_restore_and_host_variant(ctx, orc):
+    import torch
+
+    import qora_mixer as qm
+
+    g, c, pr, cos, sin, K, V, okv, kvh, prm, keep = _setup(ctx, orc, 2, 100, 128, 502)
+    mx = qm.Mixer(ctx)
+    snap = kvh.snapshot()
+    tok = I.gqa_token_inputs(g, 2)
+    out = torch.empty(2, 16, 256, device="cuda")
+    mx.gqa_decode(prm, kvh, dev(tok["q_gate"]), dev(tok["k_new"]), dev(tok["v_new"]), out)
+    ctx.sync()
+    first = host(out).copy()
+    kvh.restore_from(snap)
+    assert kvh.seq_len == 100
+    oh = np.empty((2, 16, 256), np.float32)
+    mx.gqa_decode_host(prm, kvh, np.ascontiguousarray(tok["q_gate"]), np.ascontiguousarray(tok["k_new"]),
+                       np.ascontiguousarray(tok["v_new"]), oh)
+    np.testing.assert_array_equal(oh, first)
+    assert kvh.seq_len == 101
+    snap.close()
