@@ -86,7 +86,7 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(self.device)],
+                 "-lms", "20", "-i", str(self.device)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -271,6 +271,7 @@ def run_ours(args):
     barrier(ws)
     clocks = Clocks(local)
     clocks.start()
+    time.sleep(1.0)  # let nvidia-smi start sampling before the timed region
     ctx.set_timing(True)
     L0 = stack.seq_len()
     n0 = ctx.launch_count()

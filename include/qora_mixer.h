@@ -81,8 +81,9 @@ const char* qm_status_string(int status);
  * device is compute capability 10.x. */
 int qm_ctx_create(int device, qm_ctx** out);
 int qm_ctx_destroy(qm_ctx* ctx);
-/* Run subsequent calls on `stream` (a cudaStream_t); NULL restores the
- * context's own stream. */
+/* Run subsequent calls on `stream` (a cudaStream_t, taken verbatim: NULL is
+ * the legacy default stream).  A new context starts on a stream of its own,
+ * which qm_ctx_get_stream returns. */
 int qm_ctx_set_stream(qm_ctx* ctx, void* stream);
 void* qm_ctx_get_stream(const qm_ctx* ctx);
 /* Waits for the context's stream, then reports any device-side error word
@@ -119,6 +120,8 @@ int qm_rope_table(float theta, int rope_dim, int max_pos, float* cos_host, float
  * (row = v-dim, as the reference stores it), the causal-conv history and
  * conv_pos, all zero. */
 int qm_dn_state_create(qm_ctx* ctx, int batch, qm_dn_state** out);
+/* Handles may outlive their context only to be destroyed; destroy frees the
+ * storage on the handle's device without touching the context. */
 /* Same over caller-owned device memory (not freed by destroy):
  * s [B,32,128,128] f32 and conv [B,4,8192] f32 (see qm_dn_state_data). */
 int qm_dn_state_wrap(qm_ctx* ctx, int batch, float* s, float* conv, qm_dn_state** out);

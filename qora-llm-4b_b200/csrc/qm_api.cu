@@ -185,7 +185,7 @@ extern "C" int qm_ctx_destroy(qm_ctx* c) {
 
 extern "C" int qm_ctx_set_stream(qm_ctx* c, void* stream) {
     if (!c) return QM_E_ARG;
-    c->stream = stream ? (cudaStream_t)stream : c->own_stream;
+    c->stream = (cudaStream_t)stream;  // taken verbatim: NULL is the legacy default stream
     return QM_OK;
 }
 
@@ -314,6 +314,7 @@ extern "C" int qm_dn_state_create(qm_ctx* c, int batch, qm_dn_state** out) {
     qm_dn_state* st = new (std::nothrow) qm_dn_state();
     if (!st) return QM_E_OOM;
     st->ctx = c;
+    st->device = c->device;
     st->batch = batch;
     st->owned = true;
     if (cudaMalloc(&st->s, kSPerSeq * batch * 4) != cudaSuccess ||
@@ -339,6 +340,7 @@ extern "C" int qm_dn_state_wrap(qm_ctx* c, int batch, float* s, float* conv, qm_
     qm_dn_state* st = new (std::nothrow) qm_dn_state();
     if (!st) return QM_E_OOM;
     st->ctx = c;
+    st->device = c->device;
     st->batch = batch;
     st->s = s;
     st->conv = conv;
@@ -350,8 +352,7 @@ extern "C" int qm_dn_state_wrap(qm_ctx* c, int batch, float* s, float* conv, qm_
 extern "C" int qm_dn_state_destroy(qm_dn_state* st) {
     if (!st) return QM_E_ARG;
     if (st->owned) {
-        cudaSetDevice(st->ctx->device);
-        cudaStreamSynchronize(st->ctx->stream);
+        cudaSetDevice(st->device);  // cudaFree waits for work using the memory
         cudaFree(st->s);
         cudaFree(st->conv);
     }
@@ -525,6 +526,7 @@ extern "C" int qm_kv_create(qm_ctx* c, int batch, int capacity, qm_kv** out) {
     qm_kv* kv = new (std::nothrow) qm_kv();
     if (!kv) return QM_E_OOM;
     kv->ctx = c;
+    kv->device = c->device;
     kv->batch = batch;
     kv->capacity = capacity;
     kv->owned = true;
@@ -553,6 +555,7 @@ extern "C" int qm_kv_wrap(qm_ctx* c, int batch, int capacity, uint16_t* k, uint1
     qm_kv* kv = new (std::nothrow) qm_kv();
     if (!kv) return QM_E_OOM;
     kv->ctx = c;
+    kv->device = c->device;
     kv->batch = batch;
     kv->capacity = capacity;
     kv->k = k;
@@ -570,8 +573,7 @@ extern "C" int qm_kv_wrap(qm_ctx* c, int batch, int capacity, uint16_t* k, uint1
 extern "C" int qm_kv_destroy(qm_kv* kv) {
     if (!kv) return QM_E_ARG;
     if (kv->owned) {
-        cudaSetDevice(kv->ctx->device);
-        cudaStreamSynchronize(kv->ctx->stream);
+        cudaSetDevice(kv->device);  // cudaFree waits for work using the memory
         cudaFree(kv->k);
         cudaFree(kv->v);
     }

@@ -56,6 +56,7 @@ struct qm_ctx {
 
 struct qm_dn_state {
     qm_ctx* ctx = nullptr;
+    int device = 0;           // destroy uses this, never ctx (ctx may be gone)
     int batch = 0;
     float* s = nullptr;       // [B, 32, 128, 128]
     float* conv = nullptr;    // [B, 4, 8192] ring, token t in slot t % 4
@@ -65,6 +66,7 @@ struct qm_dn_state {
 
 struct qm_kv {
     qm_ctx* ctx = nullptr;
+    int device = 0;           // destroy uses this, never ctx (ctx may be gone)
     int batch = 0;
     int capacity = 0;
     uint16_t* k = nullptr;    // [B, 4, cap, 256] bf16

@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import weakref
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 PKG_DIR = os.path.dirname(_HERE)
@@ -172,6 +173,7 @@ class Ctx:
         if rc:
             raise QmError(rc, "qm_ctx_create")
         self.device = device
+        self._children = weakref.WeakSet()
         if stream is not None:
             self.set_stream(stream)
 
@@ -185,9 +187,12 @@ class Ctx:
             raise QmError(rc, f"{what}: {msg.decode() if msg else ''}")
 
     def set_stream(self, stream):
-        """stream: a torch.cuda.Stream, a raw cudaStream_t int, or None."""
+        """stream: a torch.cuda.Stream or a raw cudaStream_t int (0 = legacy default)."""
         raw = getattr(stream, "cuda_stream", stream)
-        self.check(lib().qm_ctx_set_stream(self._h, raw), "set_stream")
+        self.check(lib().qm_ctx_set_stream(self._h, raw or None), "set_stream")
+
+    def adopt(self, child):
+        self._children.add(child)
 
     def sync(self):
         self.check(lib().qm_sync(self._h), "qm_sync")
@@ -210,6 +215,8 @@ class Ctx:
 
     def close(self):
         if self._h:
+            for ch in list(self._children):
+                ch.close()
             lib().qm_ctx_destroy(self._h)
             self._h = C.c_void_p()
 
@@ -233,6 +240,7 @@ class DnState:
             rc = lib().qm_dn_state_wrap(ctx.handle, batch, _ptr(s), _ptr(conv), C.byref(self._h))
         ctx.check(rc, "dn_state create")
         self.batch = batch
+        ctx.adopt(self)
 
     @property
     def handle(self):
@@ -254,6 +262,7 @@ class DnState:
         o.ctx, o.batch, o._keep = self.ctx, self.batch, (None, None)
         o._h = C.c_void_p()
         self.ctx.check(lib().qm_dn_state_snapshot(self.ctx.handle, self._h, C.byref(o._h)), "snapshot")
+        self.ctx.adopt(o)
         return o
 
     def restore_from(self, src: "DnState"):
@@ -302,6 +311,7 @@ class KvCache:
             rc = lib().qm_kv_wrap(ctx.handle, batch, capacity, _ptr(k), _ptr(v), C.byref(self._h))
         ctx.check(rc, "kv create")
         self.batch, self.capacity = batch, capacity
+        ctx.adopt(self)
 
     @property
     def handle(self):
@@ -327,6 +337,7 @@ class KvCache:
         o.ctx, o.batch, o.capacity, o._keep = self.ctx, self.batch, self.capacity, (None, None)
         o._h = C.c_void_p()
         self.ctx.check(lib().qm_kv_snapshot(self.ctx.handle, self._h, C.byref(o._h)), "kv snapshot")
+        self.ctx.adopt(o)
         return o
 
     def restore_from(self, src: "KvCache"):

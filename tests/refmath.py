@@ -110,7 +110,7 @@ def gqa_prefill_rows_f64(q_gate, k, v, q_norm, k_norm, cos, sin, rows, H=16, KVH
 
 def rel_err(got, ref):
     """max |got - ref| / RMS(ref) — the north-star parity measure."""
-    got = np.asarray(got, np.float64)
-    ref = np.asarray(ref, np.float64)
+    got = np.asarray(got, np.float64).reshape(-1)
+    ref = np.asarray(ref, np.float64).reshape(-1)
     rms = np.sqrt(np.mean(ref * ref))
     return float(np.max(np.abs(got - ref)) / max(rms, 1e-30))
