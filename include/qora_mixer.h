@@ -244,6 +244,45 @@ int qm_gqa_decode_host(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, const flo
 int qm_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, int T, const uint16_t* q_gate,
                    const uint16_t* k, const uint16_t* v, float* out);
 
+/* ------------------------------------------------------------------ */
+/* GQA decode without any device allocation                             */
+/* ------------------------------------------------------------------ */
+/* Size of the library's fixed device scratch array for the entry point
+ * below: 16 MiB, held on every GPU that loads the library until exit. */
+#define QM_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/*
+ * qm_gqa_decode_noalloc — no counterpart in the reference (it adds a way to
+ * call the GQA decode kernels, not a reference function).
+ *
+ * Same computation as qm_gqa_decode, for callers that cannot call
+ * cudaMalloc: a serving engine whose memory manager reserves all device
+ * memory up front and forbids later allocations, or a plugin that only
+ * borrows its host's buffers and stream.  Such callers cannot create a
+ * qm_ctx, which allocates.  The caller passes everything by pointer:
+ *   k_cache, v_cache  bf16 [batch,4,capacity,256] (16-byte aligned)
+ *   seq_len           cached positions; the new token is written at index
+ *                     seq_len and the caller advances its own count
+ *   q_gate, k_new, v_new, out  as in qm_gqa_decode
+ *   stream            cudaStream_t on the current device (NULL = legacy)
+ * The split-KV partials go to a fixed device array inside the library
+ * (QM_NOALLOC_SCRATCH_BYTES per GPU).  Nothing is allocated: no cudaMalloc,
+ * cudaFree or allocating library call.  A request whose partials do not fit
+ * returns QM_E_SHAPE: they take about 36 KB per sequence plus 16.5 KB per
+ * (sequence, KV split); on a 148-SM B200, batch 16 fits at 32K context and
+ * batch 64 does not.
+ * The first call on each device does a one-time set-up with that device
+ * current (looks up the array's device address, reads the SM count); make
+ * that first call before any stream capture.  Every call on a device shares
+ * the one array and it keeps the last call's contents, so calls that
+ * overlap on the GPU (different streams, or other host threads) race:
+ * serialise them.  Returns after enqueueing the work; device-side wait
+ * timeouts are not reported by this entry point.
+ */
+int qm_gqa_decode_noalloc(const qm_gqa_params* p, uint16_t* k_cache, uint16_t* v_cache, int batch,
+                          int capacity, int64_t seq_len, const float* q_gate, const float* k_new,
+                          const float* v_new, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

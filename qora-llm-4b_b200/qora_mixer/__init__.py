@@ -42,6 +42,7 @@ EXPORTS = [
     "qm_dn_prefill", "qm_kv_create", "qm_kv_wrap", "qm_kv_destroy", "qm_kv_snapshot",
     "qm_kv_restore", "qm_kv_seq_len", "qm_kv_set_seq_len", "qm_kv_capacity", "qm_kv_batch",
     "qm_kv_data", "qm_gqa_decode", "qm_gqa_decode_host", "qm_gqa_prefill",
+    "qm_gqa_decode_noalloc",
 ]
 
 
@@ -124,6 +125,7 @@ def lib():
         "qm_gqa_decode": ([P, C.POINTER(QmGqaParams), P, P, P, P, P], I),
         "qm_gqa_decode_host": ([P, C.POINTER(QmGqaParams), P, P, P, P, P], I),
         "qm_gqa_prefill": ([P, C.POINTER(QmGqaParams), P, I, P, P, P, P], I),
+        "qm_gqa_decode_noalloc": ([C.POINTER(QmGqaParams), P, P, I, I, I64, P, P, P, P, P], I),
     }
     for name, (args, res) in sig.items():
         if hasattr(L, name):
@@ -400,3 +402,13 @@ class Mixer:
         rc = lib().qm_gqa_prefill(self.ctx.handle, C.byref(p), kv.handle, int(T),
                                   _ptr(q_gate_bf16), _ptr(k_bf16), _ptr(v_bf16), _ptr(out))
         self.ctx.check(rc, "qm_gqa_prefill")
+
+
+def gqa_decode_noalloc(p: QmGqaParams, k_cache, v_cache, batch, capacity, seq_len, q_gate, k_new,
+                       v_new, out, stream=None):
+    """qm_gqa_decode_noalloc: GQA decode for callers that cannot allocate device
+    memory.  The caller owns the cache and its seq_len count.  Returns the status."""
+    raw = getattr(stream, "cuda_stream", stream)
+    return lib().qm_gqa_decode_noalloc(C.byref(p), _ptr(k_cache), _ptr(v_cache), int(batch),
+                                       int(capacity), int(seq_len), _ptr(q_gate), _ptr(k_new),
+                                       _ptr(v_new), _ptr(out), raw or None)
