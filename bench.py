@@ -357,6 +357,8 @@ def run_ours(args):
         "kernel_ms_per_step": round(step_kernel_ms, 4),
         "clocks": clk,
     }
+    if not args.no_prefill:
+        line["prefill_gqa"] = bench_gqa_prefill(ctx, ws, args.prefill_reps)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(args.cpu_tokens)
     if rank == 0:
@@ -370,6 +372,63 @@ def run_ours(args):
         import torch.distributed as dist
 
         dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------
+# prefill (workload 3): GQA causal prefill, 4 x 32768 tokens
+# ----------------------------------------------------------------------------
+def bench_gqa_prefill(ctx, ws, reps, B=4, T=32768):
+    import numpy as np
+    import torch
+
+    import qora_mixer as qm
+    from qora_mixer import inputs as I
+
+    g = I.rng(3)
+    pr = I.gqa_layer_params(g, T + 1)
+    cos, sin = qm.rope_table(1.0e7, 64, T + 1)
+    keep = [torch.from_numpy(pr["q_norm"]).cuda(), torch.from_numpy(pr["k_norm"]).cuda(),
+            torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()]
+    prm = qm.gqa_params(*keep)
+    qg = I.device_normal_bf16((B, T, 16, 512), 0x51A3 * 10 + 1).view(torch.int16)
+    kk = I.device_normal_bf16((B, T, 4, 256), 0x51A3 * 10 + 2).view(torch.int16)
+    vv = I.device_normal_bf16((B, T, 4, 256), 0x51A3 * 10 + 3).view(torch.int16)
+    K = torch.zeros(B, 4, T, 256, dtype=torch.int16, device="cuda")
+    V = torch.zeros_like(K)
+    kv = qm.KvCache(ctx, B, T, K, V)
+    out = torch.empty(B, T, 16, 256, device="cuda")
+    mx = qm.Mixer(ctx)
+    stream = torch.cuda.current_stream()
+    for _ in range(2):
+        mx.gqa_prefill(prm, kv, T, qg, kk, vv, out)
+    ctx.sync()
+    barrier(ws)
+    ctx.set_timing(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        mx.gqa_prefill(prm, kv, T, qg, kk, vv, out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    call_ms = max_over_ranks(e0.elapsed_time(e1) / reps, ws)
+    att_ms, att_n = ctx.kernel_time("gqa_prefill_attn")
+    prep_ms, _ = ctx.kernel_time("gqa_prefill_prep")
+    ctx.set_timing(False)
+    kv.close()
+    flops = B * 16 * 4 * 256 * T * (T + 1) / 2  # QK^T + PV, causal
+    att = att_ms / att_n
+    peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"] if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
+    tflops = flops / (att / 1e3) / 1e12
+    del qg, kk, vv, out, K, V
+    torch.cuda.empty_cache()
+    return {"workload": f"GQA causal prefill, batch {B} x {T} tokens (workload 3)",
+            "value": round(B * T * ws / (call_ms / 1e3), 1), "unit": "tok/s",
+            "ms_per_call": round(call_ms, 3), "attn_ms": round(att, 3), "prep_ms": round(prep_ms / reps, 3),
+            "roofline": {"bound": "tensor", "kernel": "gqa_prefill_attn", "achieved": round(tflops, 1),
+                         "peak": peak, "unit": "TFLOP/s", "frac": round(tflops / peak, 4),
+                         "algorithmic_flops_per_launch": flops,
+                         "operands": "fp16 x fp16 -> f32 (tcgen05 kind::f16)"}}
 
 
 # ----------------------------------------------------------------------------
@@ -505,6 +564,8 @@ def main():
     ap.add_argument("--strong", action="store_true", help="64 sequences in total instead of per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer (e2e) pass")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill measurements")
+    ap.add_argument("--prefill-reps", type=int, default=3)
     ap.add_argument("--batch", type=int, default=B_PER_GPU, help="sequences per GPU")
     ap.add_argument("--context", type=int, default=CTX, help="cached positions per sequence")
     ap.add_argument("--cpu-tokens", type=int, default=4)

@@ -1,0 +1,586 @@
+// GQA causal prefill on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces src/gemv.rs:1364-1444 (CPU: rayon over 16 heads, O(S^2 D) scalar
+// loops) and src/gpu_inference.rs:690-766 (wgpu: materialises [16,S,S]
+// scores with a -1e9 mask, 64 GiB per sequence at S = 32768).
+//
+// 1. gqa_prefill_prep  (B*T*4 CTAs): per token, QK-RMSNorm(1+g) + partial
+//    RoPE at position t (gemv.rs:1388-1395).  The bf16 KV cache receives k
+//    and v (gemv.rs:1397-1400: the prefill replaces the cache).  The attention
+//    itself runs on fp16 operands — q*(1/16), the normed k and v converted
+//    exactly from bf16 — written to a workspace: with the (1+gamma) norms the
+//    scores have a std of ~4, and bf16's 8-bit mantissa on q and k alone
+//    costs ~7e-2 of output error; fp16 (10 bits, same tensor-core rate) keeps
+//    it near 1e-2.  fp16 holds these values with room to spare (|q/16| and
+//    |k| stay below ~40, v below 65504 — larger v saturates).
+// 2. gqa_prefill_attn  (one CTA per (sequence, head, 128-query tile)):
+//    flash attention, causal, online softmax in base 2.
+//      warp 0      TMA producer: the Q tile once, then K and V tiles of 64
+//                  positions (fp16 workspace copies) through separate 2-stage rings
+//      warp 1      TMEM owner + MMA issuer (one thread):
+//                  S_j = Q K_j^T  (M=128, N=64,  K=256: 16 x tcgen05.mma)
+//                  O  += P_j V_j  (M=128, N=256, K=64:   4 x tcgen05.mma,
+//                                  V read MN-major straight from its [pos][dim] tile)
+//      warps 2..5  softmax: each thread owns one query row = one TMEM lane;
+//                  S is read with tcgen05.ld, P is written to shared memory
+//                  in the swizzled K-major layout the next MMA reads; the O
+//                  accumulator is rescaled in TMEM only when the running
+//                  max grows by more than 2^8 (exact: the same stale max is
+//                  used for numerator and denominator).
+//    TMEM: S double buffer at columns [0,128), O at [256,512).
+//    S_{j+1} is issued while the softmax works on S_j.
+//    Epilogue: O / l * sigmoid(gate) (gemv.rs:1441-1444) written as f32.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+
+#include "qm_internal.h"
+#include "qm_ptx.cuh"
+
+namespace qm {
+
+int encode_cache_tmap(CUtensorMap* m, void* base, int batch, int capacity, int box_rows);
+int encode_rows_tmap(CUtensorMap* m, void* base, uint64_t inner, uint64_t rows, uint64_t planes,
+                     uint32_t box_inner, uint32_t box_rows, bool fp16);
+
+namespace {
+
+constexpr int kBM = 128;                   // query rows per CTA (UMMA M)
+constexpr int kBN = 64;                    // key positions per tile
+constexpr int kQBox = kBM * 128;           // [128 rows x 64 dims] bf16 = 16 KB
+constexpr int kKBox = kBN * 128;           // [64 rows x 64 dims] bf16 = 8 KB
+constexpr int kQBytes = 4 * kQBox;         // 64 KB
+constexpr int kKVTile = 4 * kKBox;         // 32 KB
+constexpr int kPBytes = kBM * 128;         // [128 x 64] bf16 = 16 KB
+constexpr int kNst = 2;
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kQBytes;
+constexpr int kOffV = kOffK + kNst * kKVTile;
+constexpr int kOffP = kOffV + kNst * kKVTile;
+constexpr int kOffBar = kOffP + 2 * kPBytes;  // 229376
+constexpr int kPrefillSmem = kOffBar + 256 + 1024;
+constexpr int kTmS = 0;
+constexpr int kTmO = 256;
+constexpr int kTmCols = 512;
+constexpr uint32_t kIdescS = umma_idesc_f16kind(kBM, kBN, false, false, false);  // fp16 x fp16
+constexpr uint32_t kIdescO = umma_idesc_f16kind(kBM, 256, false, true, false);
+constexpr uint32_t kIdescS_bf = umma_idesc_bf16(kBM, kBN, false, false);         // self-test
+constexpr uint32_t kIdescO_bf = umma_idesc_bf16(kBM, 256, false, true);
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct Bars {
+    uint64_t q_full;
+    uint64_t k_full[kNst], k_empty[kNst];
+    uint64_t v_full[kNst], v_empty[kNst];
+    uint64_t s_full[2], s_free[2];
+    uint64_t p_full[2], pv_done[2];
+    uint32_t tmem_base;
+    int abort_flag;
+};
+static_assert(sizeof(Bars) <= 256, "barrier block");
+
+// ---------------------------------------------------------------------------
+// 1. prep
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(160)
+gqa_prefill_prep(const uint16_t* __restrict__ q_gate, const uint16_t* __restrict__ k_in,
+                 const uint16_t* __restrict__ v_in, const float* __restrict__ q_norm,
+                 const float* __restrict__ k_norm, const float* __restrict__ rope_cos,
+                 const float* __restrict__ rope_sin, int T, uint16_t* __restrict__ qw,
+                 uint16_t* __restrict__ kw, uint16_t* __restrict__ vw,
+                 uint16_t* __restrict__ kcache, uint16_t* __restrict__ vcache, int cap) {
+    const int g = blockIdx.x % kNumKVH;
+    const int bt = blockIdx.x / kNumKVH;
+    const int t = bt % T, b = bt / T;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool is_q = warp < kGroup;
+    const int h = g * kGroup + warp;
+    const uint16_t* src = is_q ? q_gate + (((size_t)b * T + t) * kNumH + h) * 2 * kD
+                               : k_in + (((size_t)b * T + t) * kNumKVH + g) * kD;
+    const float* gamma = is_q ? q_norm : k_norm;
+    float x[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        x[i] = bf16_bits_to_f32(src[lane + 32 * i]);
+        ss = fmaf(x[i], x[i], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.0f / sqrtf(ss * (1.0f / kD) + 1e-6f);
+#pragma unroll
+    for (int i = 0; i < 8; i++) x[i] = x[i] * inv * (1.0f + gamma[lane + 32 * i]);
+    {
+        const float c = rope_cos[(size_t)t * kHalfRot + lane];
+        const float s = rope_sin[(size_t)t * kHalfRot + lane];
+        const float x1 = x[0], x2 = x[1];
+        x[0] = x1 * c - x2 * s;
+        x[1] = x2 * c + x1 * s;
+    }
+    if (is_q) {
+        uint16_t* dst = qw + (((size_t)b * kNumH + h) * T + t) * kD;
+#pragma unroll
+        for (int i = 0; i < 8; i++) dst[lane + 32 * i] = f16_bits_rn(x[i] * 0.0625f);
+    } else {
+        const size_t row = (((size_t)b * kNumKVH + g) * cap + t) * kD;
+        const size_t wrow = (((size_t)b * kNumKVH + g) * T + t) * kD;
+        const uint16_t* vs = v_in + (((size_t)b * T + t) * kNumKVH + g) * kD;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int e = lane + 32 * i;
+            const uint16_t vb = vs[e];
+            kcache[row + e] = bf16_bits_rn(x[i]);
+            vcache[row + e] = vb;
+            kw[wrow + e] = f16_bits_rn(x[i]);
+            vw[wrow + e] = __half_as_ushort(__float2half_rn(fminf(fmaxf(bf16_bits_to_f32(vb), -65504.f), 65504.f)));
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 2. flash attention
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(192, 1)
+gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                 const __grid_constant__ CUtensorMap tmv, const uint16_t* __restrict__ q_gate,
+                 float* __restrict__ out, int T, int nqt, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
+    volatile int* abort_flag = &bars->abort_flag;
+    const uint32_t sbase = smem_u32(smem);
+
+    // heaviest query tiles first; the 16 heads of one tile are adjacent so the
+    // 4 heads of a KV group read the same K/V tiles from L2
+    const int h = blockIdx.x % kNumH;
+    const int qt = nqt - 1 - (int)(blockIdx.x / kNumH);
+    const int b = blockIdx.y;
+    const int g = h / kGroup;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = qt * kBM;
+    const int n_tiles = min((q0 + kBM - 1) / kBN + 1, (T + kBN - 1) / kBN);
+
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bars->q_full), 1);
+        for (int i = 0; i < kNst; i++) {
+            mbar_init(smem_u32(&bars->k_full[i]), 1);
+            mbar_init(smem_u32(&bars->k_empty[i]), 1);
+            mbar_init(smem_u32(&bars->v_full[i]), 1);
+            mbar_init(smem_u32(&bars->v_empty[i]), 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(smem_u32(&bars->s_full[i]), 1);
+            mbar_init(smem_u32(&bars->s_free[i]), 4);
+            mbar_init(smem_u32(&bars->p_full[i]), 4);
+            mbar_init(smem_u32(&bars->pv_done[i]), 1);
+        }
+        bars->abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&bars->tmem_base), kTmCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = bars->tmem_base;
+
+    if (warp == 0) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            prefetch_tmap(&tmq);
+            prefetch_tmap(&tmk);
+            prefetch_tmap(&tmv);
+            const uint32_t qb = smem_u32(&bars->q_full);
+            mbar_arrive_expect_tx(qb, kQBytes);
+            for (int sub = 0; sub < 4; sub++)
+                tma_load_3d(sbase + kOffQ + sub * kQBox, &tmq, sub * 64, q0, b * kNumH + h, qb);
+            const int zc = b * kNumKVH + g;
+            int j = 0;
+            for (; j < n_tiles; j++) {
+                const int st = j % kNst, r = j / kNst;
+                if (r > 0 && !mbar_wait_bounded(smem_u32(&bars->k_empty[st]), (r - 1) & 1,
+                                                abort_flag, err))
+                    break;
+                const uint32_t kf = smem_u32(&bars->k_full[st]);
+                mbar_arrive_expect_tx(kf, kKVTile);
+                for (int sub = 0; sub < 4; sub++)
+                    tma_load_3d(sbase + kOffK + st * kKVTile + sub * kKBox, &tmk, sub * 64,
+                                j * kBN, zc, kf);
+                if (r > 0 && !mbar_wait_bounded(smem_u32(&bars->v_empty[st]), (r - 1) & 1,
+                                                abort_flag, err))
+                    break;
+                const uint32_t vf = smem_u32(&bars->v_full[st]);
+                mbar_arrive_expect_tx(vf, kKVTile);
+                for (int sub = 0; sub < 4; sub++)
+                    tma_load_3d(sbase + kOffV + st * kKVTile + sub * kKBox, &tmv, sub * 64,
+                                j * kBN, zc, vf);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer ----------------------------
+        if (lane == 0) {
+            bool ok = mbar_wait_bounded(smem_u32(&bars->q_full), 0, abort_flag, err);
+            auto issue_s = [&](int j) {
+                const int st = j % kNst, sb = j & 1;
+                const uint32_t kbase = sbase + kOffK + st * kKVTile;
+#pragma unroll
+                for (int kk = 0; kk < 16; kk++) {
+                    const uint64_t ad =
+                        umma_sdesc(sbase + kOffQ + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024);
+                    const uint64_t bd = umma_sdesc(kbase + (kk >> 2) * kKBox + (kk & 3) * 32, 16, 1024);
+                    umma_bf16_ss(tm + kTmS + sb * kBN, ad, bd, kIdescS, kk > 0 ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&bars->s_full[sb]));
+                umma_commit(smem_u32(&bars->k_empty[st]));
+            };
+            if (ok) ok = mbar_wait_bounded(smem_u32(&bars->k_full[0]), 0, abort_flag, err);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0);
+            }
+            for (int j = 0; ok && j < n_tiles; j++) {
+                if (j + 1 < n_tiles) {
+                    const int jn = j + 1;
+                    ok = mbar_wait_bounded(smem_u32(&bars->k_full[jn % kNst]), (jn / kNst) & 1,
+                                           abort_flag, err);
+                    if (ok && jn >= 2)
+                        ok = mbar_wait_bounded(smem_u32(&bars->s_free[jn & 1]), ((jn - 2) >> 1) & 1,
+                                               abort_flag, err);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_s(jn);
+                }
+                const int st = j % kNst, pb = j & 1;
+                ok = mbar_wait_bounded(smem_u32(&bars->p_full[pb]), (j >> 1) & 1, abort_flag, err);
+                if (ok) ok = mbar_wait_bounded(smem_u32(&bars->v_full[st]), (j / kNst) & 1, abort_flag, err);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t vbase = sbase + kOffV + st * kKVTile;
+                const uint32_t pbase = sbase + kOffP + pb * kPBytes;
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const uint64_t ad = umma_sdesc(pbase + kk * 32, 16, 1024);
+                    const uint64_t bd = umma_sdesc(vbase + kk * 2048, kKBox, 1024);
+                    umma_bf16_ss(tm + kTmO, ad, bd, kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&bars->pv_done[pb]));
+                umma_commit(smem_u32(&bars->v_empty[st]));
+            }
+        }
+    } else {
+        // ------------------------------ softmax (warps 2..5) -----------------
+        const int quarter = warp & 3;             // TMEM lanes 32*quarter .. +31
+        const int r = quarter * 32 + lane;        // query row within the tile
+        const int qp = q0 + r;                    // query position
+        const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+        float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_tiles; j++) {
+            const int sb = j & 1;
+            ok = ok && mbar_wait_bounded(smem_u32(&bars->s_full[sb]), (j >> 1) & 1, abort_flag, err);
+            float s[kBN];
+            if (ok) {
+                tc_fence_after();
+                tmem_ld32(tm + lane_addr + kTmS + sb * kBN, s);
+                tmem_ld32(tm + lane_addr + kTmS + sb * kBN + 32, s + 32);
+                tmem_ld_wait();
+            } else {
+#pragma unroll
+                for (int c = 0; c < kBN; c++) s[c] = 0.f;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&bars->s_free[sb]));
+            // scale to log2 units, causal + length mask
+            const int kp0 = j * kBN;
+            const bool diag = (kp0 + kBN - 1 > q0) || (kp0 + kBN > T);
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kBN; c++) {
+                float v = s[c] * kLog2e;
+                if (diag && (kp0 + c > qp || kp0 + c >= T)) v = -INFINITY;
+                s[c] = v;
+                mx = fmaxf(mx, v);
+            }
+            const float m_new = fmaxf(m_used, mx);
+            bool rescale = false;
+            float factor = 1.f;
+            if (m_used == -INFINITY) {
+                m_used = m_new;
+            } else if (m_new > m_used + kRescaleThreshold) {
+                factor = exp2f(m_used - m_new);
+                m_used = m_new;
+                rescale = true;
+            }
+            l *= factor;
+            uint32_t pk[kBN / 2];
+            float rs = 0.f;
+#pragma unroll
+            for (int c = 0; c < kBN; c += 2) {
+                const float p0 = exp2f(s[c] - m_used);
+                const float p1 = exp2f(s[c + 1] - m_used);
+                rs += p0 + p1;
+                pk[c / 2] = pack_bf16(f16_bits_rn(p0), f16_bits_rn(p1));
+            }
+            l += rs;
+            // PV_{j-1} must be complete: it read P buffer (j-1)&1, and PV_{j-2}
+            // (same buffer as j) completed before it; O is stable for rescaling.
+            if (j >= 1)
+                ok = ok && mbar_wait_bounded(smem_u32(&bars->pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1,
+                                             abort_flag, err);
+            if (ok) {
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, rescale) && j >= 1) {
+#pragma unroll 1
+                    for (int c = 0; c < 8; c++) {
+                        float o[32];
+                        tmem_ld32(tm + lane_addr + kTmO + c * 32, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) o[i] *= factor;
+                        tmem_st32(tm + lane_addr + kTmO + c * 32, o);
+                    }
+                    tmem_st_wait();
+                }
+                uint8_t* prow = smem + kOffP + sb * kPBytes;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+                    *reinterpret_cast<uint4*>(prow + sw128_off(r, c)) = v;
+                }
+                fence_proxy_async_shared();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[sb]));
+        }
+        // ------------------------------ epilogue ------------------------------
+        const int jl = n_tiles - 1;
+        ok = ok && mbar_wait_bounded(smem_u32(&bars->pv_done[jl & 1]), (jl >> 1) & 1, abort_flag, err);
+        if (ok) {
+            tc_fence_after();
+            const float inv_l = 1.0f / l;
+            const bool valid = qp < T;
+            const uint16_t* grow = q_gate + (((size_t)b * T + (valid ? qp : 0)) * kNumH + h) * 2 * kD + kD;
+            float* orow = out + (((size_t)b * T + (valid ? qp : 0)) * kNumH + h) * kD;
+#pragma unroll 1
+            for (int c = 0; c < 8; c++) {
+                float o[32];
+                tmem_ld32(tm + lane_addr + kTmO + c * 32, o);
+                tmem_ld_wait();
+                if (valid) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        float4 w;
+                        const float g0 = bf16_bits_to_f32(grow[c * 32 + i + 0]);
+                        const float g1 = bf16_bits_to_f32(grow[c * 32 + i + 1]);
+                        const float g2 = bf16_bits_to_f32(grow[c * 32 + i + 2]);
+                        const float g3 = bf16_bits_to_f32(grow[c * 32 + i + 3]);
+                        w.x = o[i + 0] * inv_l * (1.0f / (1.0f + __expf(-g0)));
+                        w.y = o[i + 1] * inv_l * (1.0f / (1.0f + __expf(-g1)));
+                        w.z = o[i + 2] * inv_l * (1.0f / (1.0f + __expf(-g2)));
+                        w.w = o[i + 3] * inv_l * (1.0f / (1.0f + __expf(-g3)));
+                        *reinterpret_cast<float4*>(orow + c * 32 + i) = w;
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tm, kTmCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Self-test of the tcgen05 building blocks (descriptors, TMEM mapping):
+//   D1[128x64]  = A[128x256] . B[64x256]^T   (K-major A and B, TMA SW128)
+//   D2[128x256] = P[128x64]  . V[64x256]      (P written by threads, V MN-major)
+// One CTA of 192 threads; same code paths as gqa_prefill_attn.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(192, 1)
+umma_selftest_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
+                     const __grid_constant__ CUtensorMap tmv, const uint16_t* __restrict__ P,
+                     float* __restrict__ d1, float* __restrict__ d2, int fp16, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
+    volatile int* abort_flag = &bars->abort_flag;
+    const uint32_t sbase = smem_u32(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bars->q_full), 1);
+        mbar_init(smem_u32(&bars->pv_done[0]), 1);
+        bars->abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&bars->tmem_base), kTmCols);
+        tmem_relinquish();
+    }
+    // P by plain stores into the swizzled K-major layout (rows of 64 bf16)
+    for (int i = threadIdx.x; i < kBM * 8; i += blockDim.x) {
+        const int row = i / 8, c = i % 8;
+        const uint4 v = *reinterpret_cast<const uint4*>(P + row * 64 + c * 8);
+        *reinterpret_cast<uint4*>(smem + kOffP + sw128_off(row, c)) = v;
+    }
+    fence_proxy_async_shared();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = bars->tmem_base;
+    if (threadIdx.x == 0) {
+        const uint32_t qb = smem_u32(&bars->q_full);
+        mbar_arrive_expect_tx(qb, kQBytes + 2 * kKVTile);
+        for (int sub = 0; sub < 4; sub++) {
+            tma_load_3d(sbase + kOffQ + sub * kQBox, &tma, sub * 64, 0, 0, qb);
+            tma_load_3d(sbase + kOffK + sub * kKBox, &tmb, sub * 64, 0, 0, qb);
+            tma_load_3d(sbase + kOffV + sub * kKBox, &tmv, sub * 64, 0, 0, qb);
+        }
+        if (mbar_wait_bounded(qb, 0, abort_flag, err)) {
+            tc_fence_after();
+            for (int kk = 0; kk < 16; kk++)
+                umma_bf16_ss(tm + kTmS,
+                             umma_sdesc(sbase + kOffQ + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024),
+                             umma_sdesc(sbase + kOffK + (kk >> 2) * kKBox + (kk & 3) * 32, 16, 1024),
+                             fp16 ? kIdescS : kIdescS_bf, kk > 0);
+            for (int kk = 0; kk < 4; kk++)
+                umma_bf16_ss(tm + kTmO, umma_sdesc(sbase + kOffP + kk * 32, 16, 1024),
+                             umma_sdesc(sbase + kOffV + kk * 2048, kKBox, 1024),
+                             fp16 ? kIdescO : kIdescO_bf, kk > 0);
+            umma_commit(smem_u32(&bars->pv_done[0]));
+        } else {
+            bars->abort_flag = 1;
+        }
+    }
+    if (warp >= 2) {
+        const int quarter = warp & 3, r = quarter * 32 + lane;
+        const uint32_t la = (uint32_t)(quarter * 32) << 16;
+        if (mbar_wait_bounded(smem_u32(&bars->pv_done[0]), 0, abort_flag, err)) {
+            tc_fence_after();
+            for (int c = 0; c < 2; c++) {
+                float v[32];
+                tmem_ld32(tm + la + kTmS + c * 32, v);
+                tmem_ld_wait();
+                for (int i = 0; i < 32; i++) d1[r * 64 + c * 32 + i] = v[i];
+            }
+            for (int c = 0; c < 8; c++) {
+                float v[32];
+                tmem_ld32(tm + la + kTmO + c * 32, v);
+                tmem_ld_wait();
+                for (int i = 0; i < 32; i++) d2[r * 256 + c * 32 + i] = v[i];
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tm, kTmCols);
+    }
+}
+
+}  // namespace
+
+// fp16 q [B,16,T,256], k and v [B,4,T,256]
+size_t gqa_prefill_ws_bytes(int batch, int T) {
+    return (size_t)batch * (kNumH + 2 * kNumKVH) * T * kD * 2;
+}
+
+cudaError_t launch_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv, int T,
+                               const uint16_t* q_gate, const uint16_t* k, const uint16_t* v,
+                               float* out) {
+    const int B = kv->batch;
+    cudaStream_t st = ctx->stream;
+    uint16_t* qw = static_cast<uint16_t*>(ctx->ws);
+    uint16_t* kw = qw + (size_t)B * kNumH * T * kD;
+    uint16_t* vw = kw + (size_t)B * kNumKVH * T * kD;
+    {
+        TimedLaunch tl(ctx, "gqa_prefill_prep");
+        gqa_prefill_prep<<<(unsigned)((size_t)B * T * kNumKVH), 160, 0, st>>>(
+            q_gate, k, v, prm->q_norm, prm->k_norm, prm->rope_cos, prm->rope_sin, T, qw, kw, vw,
+            kv->k, kv->v, kv->capacity);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    ctx->launches += 1;
+    CUtensorMap tmq, tmk, tmv;
+    if (encode_rows_tmap(&tmq, qw, kD, (uint64_t)T, (uint64_t)B * kNumH, 64, kBM, true) != QM_OK ||
+        encode_rows_tmap(&tmk, kw, kD, (uint64_t)T, (uint64_t)B * kNumKVH, 64, kBN, true) != QM_OK ||
+        encode_rows_tmap(&tmv, vw, kD, (uint64_t)T, (uint64_t)B * kNumKVH, 64, kBN, true) != QM_OK)
+        return cudaErrorInvalidValue;
+    static bool attr_set[64] = {};
+    if (ctx->device < 64 && !attr_set[ctx->device]) {
+        e = cudaFuncSetAttribute(gqa_prefill_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kPrefillSmem);
+        if (e != cudaSuccess) return e;
+        attr_set[ctx->device] = true;
+    }
+    const int nqt = (T + kBM - 1) / kBM;
+    dim3 grid(nqt * kNumH, B);
+    {
+        TimedLaunch tl(ctx, "gqa_prefill_attn");
+        gqa_prefill_attn<<<grid, 192, kPrefillSmem, st>>>(tmq, tmk, tmv, q_gate, out, T, nqt,
+                                                          ctx->d_err);
+    }
+    e = cudaGetLastError();
+    if (e == cudaSuccess) ctx->launches += 1;
+    return e;
+}
+
+}  // namespace qm
+
+using namespace qm;
+
+extern "C" int qm_gqa_prefill(qm_ctx* c, const qm_gqa_params* p, qm_kv* kv, int T,
+                              const uint16_t* q_gate, const uint16_t* k, const uint16_t* v,
+                              float* out) {
+    if (!c) return QM_E_ARG;
+    if (!p || !p->q_norm || !p->k_norm || !p->rope_cos || !p->rope_sin || p->max_pos <= 0)
+        return set_error(c, QM_E_ARG, "GQA params: null pointer or max_pos <= 0");
+    if (!kv || !q_gate || !k || !v || !out || T <= 0)
+        return set_error(c, QM_E_ARG, "qm_gqa_prefill: null pointer or T <= 0");
+    if (kv->ctx != c) return set_error(c, QM_E_MISMATCH, "cache belongs to another context");
+    if (T > kv->capacity) return set_error(c, QM_E_RANGE, "qm_gqa_prefill: T exceeds the cache capacity");
+    if (T > p->max_pos) return set_error(c, QM_E_RANGE, "qm_gqa_prefill: T exceeds the RoPE table");
+    if (((uintptr_t)out & 15) || ((uintptr_t)q_gate & 15))
+        return set_error(c, QM_E_ARG, "qm_gqa_prefill: out and q_gate must be 16-byte aligned");
+    cudaSetDevice(c->device);
+    int rc = ensure_workspace(c, gqa_prefill_ws_bytes(kv->batch, T));
+    if (rc) return rc;
+    cudaError_t e = launch_gqa_prefill(c, p, kv, T, q_gate, k, v, out);
+    if (e != cudaSuccess) return cuda_error(c, e, "gqa_prefill launch");
+    kv->seq_len = T;
+    return QM_OK;
+}
+
+// Self-test of the tcgen05 descriptor encodings (test hook, not part of the
+// mixer ABI).  a [128x256], b [64x256], v [64x256], p [128x64] (device; all
+// bf16, or all fp16 when fp16 != 0); d1 [128x64], d2 [128x256] f32.
+// Synchronous; returns a QM status.
+extern "C" int qm_selftest_umma(const uint16_t* a, const uint16_t* b, const uint16_t* v,
+                                const uint16_t* p, float* d1, float* d2, int fp16) {
+    CUtensorMap ta, tb, tv;
+    const bool h = fp16 != 0;
+    if (encode_rows_tmap(&ta, (void*)a, 256, 128, 1, 64, 128, h) != QM_OK ||
+        encode_rows_tmap(&tb, (void*)b, 256, 64, 1, 64, 64, h) != QM_OK ||
+        encode_rows_tmap(&tv, (void*)v, 256, 64, 1, 64, 64, h) != QM_OK)
+        return QM_E_CUDA;
+    int* err = nullptr;
+    if (cudaMalloc(&err, sizeof(int)) != cudaSuccess) return QM_E_OOM;
+    cudaMemset(err, 0, sizeof(int));
+    cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         kPrefillSmem);
+    umma_selftest_kernel<<<1, 192, kPrefillSmem>>>(ta, tb, tv, p, d1, d2, fp16, err);
+    cudaError_t e = cudaDeviceSynchronize();
+    int flag = 0;
+    cudaMemcpy(&flag, err, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(err);
+    if (e != cudaSuccess) return QM_E_CUDA;
+    return flag ? QM_E_TIMEOUT : QM_OK;
+}

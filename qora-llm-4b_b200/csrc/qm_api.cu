@@ -91,6 +91,22 @@ int encode_cache_tmap(CUtensorMap* m, void* base, int batch, int capacity, int b
     return r == CUDA_SUCCESS ? QM_OK : QM_E_CUDA;
 }
 
+// Generic 3-D bf16 view {inner, rows, planes} (row-major), 128-byte swizzle.
+int encode_rows_tmap(CUtensorMap* m, void* base, uint64_t inner, uint64_t rows, uint64_t planes,
+                     uint32_t box_inner, uint32_t box_rows, bool fp16) {
+    auto enc = get_encode_tiled();
+    if (!enc) return QM_E_CUDA;
+    cuuint64_t dims[3] = {inner, rows, planes};
+    cuuint64_t strides[2] = {inner * 2, rows * inner * 2};
+    cuuint32_t box[3] = {box_inner, box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                     base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? QM_OK : QM_E_CUDA;
+}
+
 int make_kv_tmaps(qm_kv* kv) {
     kv->tmaps_ok = false;
     if (encode_cache_tmap(&kv->tmap_k, kv->k, kv->batch, kv->capacity, 64) != QM_OK ||
@@ -694,9 +710,5 @@ extern "C" int qm_gqa_decode_host(qm_ctx* c, const qm_gqa_params* p, qm_kv* kv,
 extern "C" int qm_dn_prefill(qm_ctx* c, const qm_dn_params*, qm_dn_state*, int, const uint16_t*,
                              const float*, const float*, float*, const float*, float*) {
     return set_error(c, QM_E_UNSUPPORTED, "qm_dn_prefill: not built in this version");
-}
-extern "C" int qm_gqa_prefill(qm_ctx* c, const qm_gqa_params*, qm_kv*, int, const uint16_t*,
-                              const uint16_t*, const uint16_t*, float*) {
-    return set_error(c, QM_E_UNSUPPORTED, "qm_gqa_prefill: not built in this version");
 }
 #endif

@@ -101,6 +101,10 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, co
                               const float* k_new, const float* v_new, float* out, void* ws,
                               size_t ws_bytes);
 size_t gqa_decode_ws_bytes(int batch, int64_t seq_len, int num_sms);
+cudaError_t launch_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, int T,
+                               const uint16_t* q_gate, const uint16_t* k, const uint16_t* v,
+                               float* out);
+size_t gqa_prefill_ws_bytes(int batch, int T);
 
 }  // namespace qm
 
