@@ -359,6 +359,7 @@ def run_ours(args):
     }
     if not args.no_prefill:
         line["prefill_gqa"] = bench_gqa_prefill(ctx, ws, args.prefill_reps)
+        line["prefill_dn"] = bench_dn_prefill(ctx, ws, args.prefill_reps)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(args.cpu_tokens)
     if rank == 0:
@@ -429,6 +430,71 @@ def bench_gqa_prefill(ctx, ws, reps, B=4, T=32768):
                          "peak": peak, "unit": "TFLOP/s", "frac": round(tflops / peak, 4),
                          "algorithmic_flops_per_launch": flops,
                          "operands": "fp16 x fp16 -> f32 (tcgen05 kind::f16)"}}
+
+
+# ----------------------------------------------------------------------------
+# prefill (workload 2): DeltaNet chunked prefill, 8 x 8192 tokens, chunk 64
+# ----------------------------------------------------------------------------
+def bench_dn_prefill(ctx, ws, reps, B=8, T=8192):
+    import torch
+
+    import qora_mixer as qm
+    from qora_mixer import inputs as I
+
+    g = I.rng(2)
+    p = I.dn_layer_params(g)
+    keep = [torch.from_numpy(p[k]).cuda() for k in ("conv_w", "a_log", "dt_bias", "norm_gamma")]
+    prm = qm.dn_params(*keep)
+    qkv = I.device_normal_bf16((B, T, 8192), 0x51A2 * 10 + 1).view(torch.int16)
+    a = I.device_normal_f32((B, T, 32), 0x51A2 * 10 + 2)
+    bb = I.device_normal_f32((B, T, 32), 0x51A2 * 10 + 3)
+    st = qm.DnState(ctx, B)
+    y = torch.empty(B, T, 32, 128, device="cuda")
+    mx = qm.Mixer(ctx)
+    stream = torch.cuda.current_stream()
+    for _ in range(2):
+        st.reset()
+        mx.dn_prefill(prm, st, T, qkv, a, bb, y)
+    ctx.sync()
+    barrier(ws)
+    ctx.set_timing(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    tot = 0.0
+    for _ in range(reps):
+        st.reset()  # each call is a fresh 8192-token prompt
+        e0.record(stream)
+        mx.dn_prefill(prm, st, T, qkv, a, bb, y)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        tot += e0.elapsed_time(e1)
+    call_ms = max_over_ranks(tot / reps, ws)
+    k_ms, k_n = ctx.kernel_time("dn_prefill_chunk")
+    prep_ms, _ = ctx.kernel_time("dn_prefill_prep")
+    ctx.set_timing(False)
+    st.close()
+    flops = B * 32 * (T // 64) * (10 * 64 * 64 * 128 + 6 * 64 * 128 * 128 + 64 ** 3)
+    executed = B * 32 * (T // 64) * 2 * (3 * 128 * 64 * 128 + 3 * 128 * 64 * 64 * 2 + 2 * 128 * 64 * 128
+                                         + 3 * 128 * 64 * 64 + 3 * 128 * 128 * 64)
+    bytes_alg = B * T * (8192 * 2 + 64 * 4 + 32 * 128 * 4)
+    peak_t = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"] if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else 1590.0
+    peak_b, _ = load_peaks()
+    kk = k_ms / k_n
+    del qkv, a, bb, y
+    torch.cuda.empty_cache()
+    return {"workload": f"DeltaNet chunked prefill, batch {B} x {T} tokens, chunk 64 (workload 2)",
+            "value": round(B * T * ws / (call_ms / 1e3), 1), "unit": "tok/s",
+            "ms_per_call": round(call_ms, 3), "chunk_kernel_ms": round(kk, 3),
+            "prep_ms": round(prep_ms / reps, 3),
+            "roofline": {"bound": "tensor (north-star target) / hbm",
+                         "kernel": "dn_prefill_chunk",
+                         "achieved_tflops": round(flops / (kk / 1e3) / 1e12, 1), "peak_tflops": peak_t,
+                         "frac_tensor": round(flops / (kk / 1e3) / 1e12 / peak_t, 4),
+                         "executed_tflops": round(executed / (kk / 1e3) / 1e12, 1),
+                         "achieved_gbs_call": round(bytes_alg / (call_ms / 1e3) / 1e9, 1), "peak_gbs": peak_b,
+                         "frac_hbm_call": round(bytes_alg / (call_ms / 1e3) / 1e9 / peak_b, 4),
+                         "algorithmic_flops": flops, "algorithmic_bytes": bytes_alg,
+                         "operands": "fp16 hi/lo compensated (3 MMAs) intra-chunk, fp16 state products"}}
 
 
 # ----------------------------------------------------------------------------

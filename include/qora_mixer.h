@@ -179,9 +179,12 @@ int qm_dn_decode_host(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, const
  * prefill_deltanet_layer (1086) and the CPU recurrence that
  * prefill_deltanet_layer_gpu runs between device round trips
  * (src/gpu_inference.rs:464-604).
- *   qkv [B,T,8192] bf16, a,b [B,T,32] f32, y [B,T,32,128] f32,
- *   z [B,T,4096] f32 or NULL, out [B,T,4096] f32 or NULL.
+ *   qkv [B,T,8192] bf16, a,b [B,T,32] f32, y [B,T,32,128] f32 (required),
+ *   z [B,T,4096] f32 or NULL; when given, out [B,T,4096] f32 receives
+ *   RMSNorm(y)*gamma*SiLU(z) (gemv.rs:1205-1219).
  * The state continues from its current contents (conv history included).
+ * Chunks of 64 tokens; intra-chunk products are compensated fp16 tcgen05
+ * MMAs (hi.hi + hi.lo + lo.hi), the 64x64 triangular solve is f32.
  */
 int qm_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, int T, const uint16_t* qkv,
                   const float* a, const float* b, float* y, const float* z, float* out);

@@ -215,6 +215,8 @@ extern "C" int qm_sync(qm_ctx* c) {
     QM_CHECK_CUDA(c, cudaMemcpy(&err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (err) {
         cudaMemset(c->d_err, 0, sizeof(int));
+        if (err & kErrBounds)
+            return set_error(c, QM_E_RANGE, "a device-side index self-check failed (access skipped)");
         return set_error(c, QM_E_TIMEOUT, "a device-side bounded wait gave up (error word set)");
     }
     return QM_OK;
@@ -703,12 +705,3 @@ extern "C" int qm_gqa_decode_host(qm_ctx* c, const qm_gqa_params* p, qm_kv* kv,
     return qm_sync(c);
 }
 
-// ---------------------------------------------------------------------------
-// Prefill entry points (argument checks; kernels in gqa_prefill.cu / dn_prefill.cu)
-// ---------------------------------------------------------------------------
-#ifndef QM_HAVE_PREFILL
-extern "C" int qm_dn_prefill(qm_ctx* c, const qm_dn_params*, qm_dn_state*, int, const uint16_t*,
-                             const float*, const float*, float*, const float*, float*) {
-    return set_error(c, QM_E_UNSUPPORTED, "qm_dn_prefill: not built in this version");
-}
-#endif

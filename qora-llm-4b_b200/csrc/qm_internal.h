@@ -30,8 +30,9 @@ constexpr int kGroup = kNumH / kNumKVH;             // 4
 constexpr int kRot = 64;                            // rope_dim
 constexpr int kHalfRot = kRot / 2;                  // 32
 
-// Device-side error word bits (set by bounded waits that give up).
+// Device-side error word bits: a bounded wait gave up; an index self-check failed.
 constexpr int kErrTimeout = 1;
+constexpr int kErrBounds = 2;
 
 }  // namespace qm
 
@@ -105,6 +106,10 @@ cudaError_t launch_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, i
                                const uint16_t* q_gate, const uint16_t* k, const uint16_t* v,
                                float* out);
 size_t gqa_prefill_ws_bytes(int batch, int T);
+cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, int T,
+                              const uint16_t* qkv, const float* a, const float* b, float* y,
+                              const float* z, float* out);
+size_t dn_prefill_ws_bytes(int batch, int T);
 
 }  // namespace qm
 
