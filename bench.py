@@ -555,9 +555,18 @@ class CpuStack:
                 self.kv.seq_len[0] = L  # all 8 layers attend over the same 32768+1 positions
 
 
+def host_threads():
+    """Every core this process may run on (torchrun sets OMP_NUM_THREADS=1 per rank)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_sample(ntok):
     from oracle import oracle as orc
 
+    orc.set_num_threads(host_threads())
     cs = CpuStack(ntok)
     cs.token()  # warm
     t0 = time.perf_counter()
@@ -589,6 +598,7 @@ def run_reference(args):
     from oracle import oracle as orc
 
     per_step = args.cpu_tokens_per_step
+    orc.set_num_threads(host_threads())
     cs = CpuStack(per_step * (args.warmup + args.steps) + 1)
     for _ in range(args.warmup):
         for _ in range(per_step):
