@@ -646,9 +646,29 @@ def main():
     ap.add_argument("--context", type=int, default=CTX, help="cached positions per sequence")
     ap.add_argument("--cpu-tokens", type=int, default=4)
     ap.add_argument("--cpu-tokens-per-step", type=int, default=1)
+    ap.add_argument("--prefill-only", choices=["gqa", "dn"],
+                    help="time one prefill alone (profiling small cases); prints its record")
+    ap.add_argument("--prefill-batch", type=int, help="with --prefill-only: sequences")
+    ap.add_argument("--prefill-len", type=int, help="with --prefill-only: tokens per sequence")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.prefill_only:
+        import torch
+
+        import qora_mixer as qm
+
+        torch.cuda.set_device(0)
+        ctx = qm.Ctx(0, stream=torch.cuda.current_stream())
+        fn = bench_gqa_prefill if args.prefill_only == "gqa" else bench_dn_prefill
+        kw = {}
+        if args.prefill_batch:
+            kw["B"] = args.prefill_batch
+        if args.prefill_len:
+            kw["T"] = args.prefill_len
+        print(json.dumps(fn(ctx, 1, args.prefill_reps, **kw)), flush=True)
+        ctx.close()
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

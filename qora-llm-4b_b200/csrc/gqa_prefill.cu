@@ -57,8 +57,11 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kQBytes;
 constexpr int kOffV = kOffK + kNst * kKVTile;
 constexpr int kOffP = kOffV + kNst * kKVTile;
-constexpr int kOffBar = kOffP + 2 * kPBytes;  // 229376
+constexpr int kOffRed = kOffP + kPBytes;      // row-max / row-sum exchange [2][2][128] f32
+constexpr int kOffBar = kOffRed + 2 * 2 * kBM * 4;
 constexpr int kPrefillSmem = kOffBar + 256 + 1024;
+constexpr int kSoftmaxWarps = 8;              // two per TMEM lane quarter, 32 columns each
+constexpr int kAttnThreads = 64 + 32 * kSoftmaxWarps;
 constexpr int kTmS = 0;
 constexpr int kTmO = 256;
 constexpr int kTmCols = 512;
@@ -141,7 +144,7 @@ gqa_prefill_prep(const uint16_t* __restrict__ q_gate, const uint16_t* __restrict
 // ---------------------------------------------------------------------------
 // 2. flash attention
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kAttnThreads, 1)
 gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                  const __grid_constant__ CUtensorMap tmv, const uint16_t* __restrict__ q_gate,
                  float* __restrict__ out, int T, int nqt, int* err) {
@@ -171,8 +174,8 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(smem_u32(&bars->s_full[i]), 1);
-            mbar_init(smem_u32(&bars->s_free[i]), 4);
-            mbar_init(smem_u32(&bars->p_full[i]), 4);
+            mbar_init(smem_u32(&bars->s_free[i]), kSoftmaxWarps);
+            mbar_init(smem_u32(&bars->p_full[i]), kSoftmaxWarps);
             mbar_init(smem_u32(&bars->pv_done[i]), 1);
         }
         bars->abort_flag = 0;
@@ -259,7 +262,7 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t vbase = sbase + kOffV + st * kKVTile;
-                const uint32_t pbase = sbase + kOffP + pb * kPBytes;
+                const uint32_t pbase = sbase + kOffP;
 #pragma unroll
                 for (int kk = 0; kk < 4; kk++) {
                     const uint64_t ad = umma_sdesc(pbase + kk * 32, 16, 1024);
@@ -271,63 +274,81 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
             }
         }
     } else {
-        // ------------------------------ softmax (warps 2..5) -----------------
+        // ------------------------------ softmax (warps 2..9) -----------------
+        // Two warps per TMEM lane quarter: warp w reads lanes 32*(w%4).. and
+        // half (w-2)/4 of the 64 score columns.  The row max is exchanged
+        // through shared memory (parity double buffer, one named barrier of
+        // the quarter's 64 threads per tile); row sums stay per half until
+        // the epilogue.  Both halves see the same row max, so they take the
+        // same rescale decisions.
         const int quarter = warp & 3;             // TMEM lanes 32*quarter .. +31
+        const int half = (warp - 2) >> 2;         // score columns [32*half, 32*half+32)
         const int r = quarter * 32 + lane;        // query row within the tile
         const int qp = q0 + r;                    // query position
+        const int bar_id = 1 + quarter;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+        float* red = reinterpret_cast<float*>(smem + kOffRed);  // [parity][half][row]
         float m_used = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < n_tiles; j++) {
             const int sb = j & 1;
             ok = ok && mbar_wait_bounded(smem_u32(&bars->s_full[sb]), (j >> 1) & 1, abort_flag, err);
-            float s[kBN];
+            float s[32];
             if (ok) {
                 tc_fence_after();
-                tmem_ld32(tm + lane_addr + kTmS + sb * kBN, s);
-                tmem_ld32(tm + lane_addr + kTmS + sb * kBN + 32, s + 32);
+                tmem_ld32(tm + lane_addr + kTmS + sb * kBN + half * 32, s);
                 tmem_ld_wait();
             } else {
 #pragma unroll
-                for (int c = 0; c < kBN; c++) s[c] = 0.f;
+                for (int c = 0; c < 32; c++) s[c] = 0.f;
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&bars->s_free[sb]));
-            // scale to log2 units, causal + length mask
-            const int kp0 = j * kBN;
-            const bool diag = (kp0 + kBN - 1 > q0) || (kp0 + kBN > T);
-            float mx = -INFINITY;
+            // causal + length mask (only tiles that reach the diagonal or T)
+            const int kp0 = j * kBN + half * 32;
+            if (kp0 + 31 > q0 || kp0 + 32 > T) {
+                const int lim = min(qp, T - 1) - kp0;  // columns c <= lim are visible
 #pragma unroll
-            for (int c = 0; c < kBN; c++) {
-                float v = s[c] * kLog2e;
-                if (diag && (kp0 + c > qp || kp0 + c >= T)) v = -INFINITY;
-                s[c] = v;
-                mx = fmaxf(mx, v);
+                for (int c = 0; c < 32; c++)
+                    if (c > lim) s[c] = -INFINITY;
             }
-            const float m_new = fmaxf(m_used, mx);
+            float m4[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) m4[i] = fmaxf(s[i], s[i + 4]);
+#pragma unroll
+            for (int c = 8; c < 32; c += 4) {
+#pragma unroll
+                for (int i = 0; i < 4; i++) m4[i] = fmaxf(m4[i], s[c + i]);
+            }
+            float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+            red[(sb * 2 + half) * kBM + r] = mx;
+            named_bar_sync(bar_id, 64);
+            mx = fmaxf(mx, red[(sb * 2 + (half ^ 1)) * kBM + r]);
+            const float m_new = fmaxf(m_used, mx * kLog2e);
             bool rescale = false;
             float factor = 1.f;
             if (m_used == -INFINITY) {
                 m_used = m_new;
             } else if (m_new > m_used + kRescaleThreshold) {
-                factor = exp2f(m_used - m_new);
+                factor = ex2_approx(m_used - m_new);
                 m_used = m_new;
                 rescale = true;
             }
             l *= factor;
-            uint32_t pk[kBN / 2];
-            float rs = 0.f;
+            const float nm = -m_used;
+            uint32_t pk[16];
+            float r4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < kBN; c += 2) {
-                const float p0 = exp2f(s[c] - m_used);
-                const float p1 = exp2f(s[c + 1] - m_used);
-                rs += p0 + p1;
-                pk[c / 2] = pack_bf16(f16_bits_rn(p0), f16_bits_rn(p1));
+            for (int c = 0; c < 32; c += 2) {
+                const float p0 = ex2_approx(fmaf(s[c], kLog2e, nm));
+                const float p1 = ex2_approx(fmaf(s[c + 1], kLog2e, nm));
+                r4[(c >> 1) & 3] += p0 + p1;
+                pk[c / 2] = pack_f16x2_rn(p0, p1);
             }
-            l += rs;
-            // PV_{j-1} must be complete: it read P buffer (j-1)&1, and PV_{j-2}
-            // (same buffer as j) completed before it; O is stable for rescaling.
+            l += (r4[0] + r4[1]) + (r4[2] + r4[3]);
+            // PV_{j-1} must be complete: it read the P buffer, and O is
+            // stable for rescaling.
             if (j >= 1)
                 ok = ok && mbar_wait_bounded(smem_u32(&bars->pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1,
                                              abort_flag, err);
@@ -335,21 +356,22 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, rescale) && j >= 1) {
 #pragma unroll 1
-                    for (int c = 0; c < 8; c++) {
+                    for (int c = 0; c < 4; c++) {
                         float o[32];
-                        tmem_ld32(tm + lane_addr + kTmO + c * 32, o);
+                        const uint32_t oa = tm + lane_addr + kTmO + half * 128 + c * 32;
+                        tmem_ld32(oa, o);
                         tmem_ld_wait();
 #pragma unroll
                         for (int i = 0; i < 32; i++) o[i] *= factor;
-                        tmem_st32(tm + lane_addr + kTmO + c * 32, o);
+                        tmem_st32(oa, o);
                     }
                     tmem_st_wait();
                 }
-                uint8_t* prow = smem + kOffP + sb * kPBytes;
+                uint8_t* prow = smem + kOffP;
 #pragma unroll
-                for (int c = 0; c < 8; c++) {
+                for (int c = 0; c < 4; c++) {
                     uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-                    *reinterpret_cast<uint4*>(prow + sw128_off(r, c)) = v;
+                    *reinterpret_cast<uint4*>(prow + sw128_off(r, half * 4 + c)) = v;
                 }
                 fence_proxy_async_shared();
             }
@@ -358,31 +380,35 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
             if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[sb]));
         }
         // ------------------------------ epilogue ------------------------------
+        // the two halves' row sums (the exchange buffer of the next parity is
+        // free: its last readers passed this quarter's barrier of the last tile)
+        const int pe = n_tiles & 1;
+        red[(pe * 2 + half) * kBM + r] = l;
+        named_bar_sync(bar_id, 64);
+        l += red[(pe * 2 + (half ^ 1)) * kBM + r];
         const int jl = n_tiles - 1;
         ok = ok && mbar_wait_bounded(smem_u32(&bars->pv_done[jl & 1]), (jl >> 1) & 1, abort_flag, err);
         if (ok) {
             tc_fence_after();
             const float inv_l = 1.0f / l;
             const bool valid = qp < T;
-            const uint16_t* grow = q_gate + (((size_t)b * T + (valid ? qp : 0)) * kNumH + h) * 2 * kD + kD;
-            float* orow = out + (((size_t)b * T + (valid ? qp : 0)) * kNumH + h) * kD;
+            const uint16_t* grow = q_gate + (((size_t)b * T + (valid ? qp : 0)) * kNumH + h) * 2 * kD + kD
+                                   + half * 128;
+            float* orow = out + (((size_t)b * T + (valid ? qp : 0)) * kNumH + h) * kD + half * 128;
 #pragma unroll 1
-            for (int c = 0; c < 8; c++) {
+            for (int c = 0; c < 4; c++) {
                 float o[32];
-                tmem_ld32(tm + lane_addr + kTmO + c * 32, o);
+                tmem_ld32(tm + lane_addr + kTmO + half * 128 + c * 32, o);
                 tmem_ld_wait();
                 if (valid) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 4) {
+                        const uint2 gb = *reinterpret_cast<const uint2*>(grow + c * 32 + i);
                         float4 w;
-                        const float g0 = bf16_bits_to_f32(grow[c * 32 + i + 0]);
-                        const float g1 = bf16_bits_to_f32(grow[c * 32 + i + 1]);
-                        const float g2 = bf16_bits_to_f32(grow[c * 32 + i + 2]);
-                        const float g3 = bf16_bits_to_f32(grow[c * 32 + i + 3]);
-                        w.x = o[i + 0] * inv_l * (1.0f / (1.0f + __expf(-g0)));
-                        w.y = o[i + 1] * inv_l * (1.0f / (1.0f + __expf(-g1)));
-                        w.z = o[i + 2] * inv_l * (1.0f / (1.0f + __expf(-g2)));
-                        w.w = o[i + 3] * inv_l * (1.0f / (1.0f + __expf(-g3)));
+                        w.x = o[i + 0] * inv_l * (1.0f / (1.0f + __expf(-bf16_bits_to_f32(gb.x & 0xffffu))));
+                        w.y = o[i + 1] * inv_l * (1.0f / (1.0f + __expf(-bf16_bits_to_f32(gb.x >> 16))));
+                        w.z = o[i + 2] * inv_l * (1.0f / (1.0f + __expf(-bf16_bits_to_f32(gb.y & 0xffffu))));
+                        w.w = o[i + 3] * inv_l * (1.0f / (1.0f + __expf(-bf16_bits_to_f32(gb.y >> 16))));
                         *reinterpret_cast<float4*>(orow + c * 32 + i) = w;
                     }
                 }
@@ -525,7 +551,7 @@ cudaError_t launch_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
     dim3 grid(nqt * kNumH, B);
     {
         TimedLaunch tl(ctx, "gqa_prefill_attn");
-        gqa_prefill_attn<<<grid, 192, kPrefillSmem, st>>>(tmq, tmk, tmv, q_gate, out, T, nqt,
+        gqa_prefill_attn<<<grid, kAttnThreads, kPrefillSmem, st>>>(tmq, tmk, tmv, q_gate, out, T, nqt,
                                                           ctx->d_err);
     }
     e = cudaGetLastError();

@@ -102,11 +102,11 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
 // Only rows 0..7 of the result are kept (d0, d1); rows 8..15 are discarded.
 __device__ __forceinline__ void mma_bf16_top(float& d0, float& d1, uint32_t a0, uint32_t a2,
                                              uint32_t b0, uint32_t b1) {
-    float x2, x3;
     asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
-        "{%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
-        : "=f"(d0), "=f"(d1), "=f"(x2), "=f"(x3)
+        "{\n.reg .f32 x2, x3;\n"
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,x2,x3}, "
+        "{%2,%3,%4,%5}, {%6,%7}, {%8,%9,%10,%11};\n}"
+        : "=f"(d0), "=f"(d1)
         : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(d0), "f"(d1), "f"(0.f),
           "f"(0.f));
 }
@@ -118,6 +118,20 @@ __device__ __forceinline__ uint16_t bf16_bits_rn(float x) {
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
 
 __device__ __forceinline__ uint16_t f16_bits_rn(float x) { return __half_as_ushort(__float2half_rn(x)); }
+
+// Two f32 -> one f16x2 register (round to nearest even); lo in bits 0..15.
+__device__ __forceinline__ uint32_t pack_f16x2_rn(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
+}
+
+// 2^x on the special-function unit (ex2.approx, flush-to-zero); 2^-inf = 0.
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __device__ __forceinline__ uint32_t pack_bf16(uint16_t lo, uint16_t hi) {
     return (uint32_t)lo | ((uint32_t)hi << 16);
