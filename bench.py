@@ -249,6 +249,134 @@ class Stack:
     def seq_len(self):
         return self.layers[3]["kv"].seq_len
 
+    def close(self):
+        for L in self.layers:
+            for k in ("st", "kv"):
+                if k in L:
+                    L[k].close()
+        self.layers = []
+
+
+class ShardedStack:
+    """Workload 4's head-sharded variant (qm_shard_plan): B sequences in total
+    over all ranks.  This rank holds V heads [vh_lo, vh_lo+nvh) of the 24
+    DeltaNet layers for all B sequences, and KV heads [kv_lo, kv_lo+nkv) of
+    batch part seq_part for the 8 GQA layers.  Every layer's output slice is
+    all-gathered over NCCL (qm_comm_allgather) on the mixer's stream, as
+    out_proj / o_proj would need it."""
+
+    def __init__(self, ctx, comm, plan, B, cap, ctx_len=CTX):
+        import numpy as np
+        import torch
+
+        import qora_mixer as qm
+        from qora_mixer import inputs as I
+
+        self.ctx, self.comm, self.mx, self.plan, self.B = ctx, comm, qm.Mixer(ctx), plan, B
+        world = plan["world"]
+        nvh, nkv = plan["nvh"], plan["nkv"]
+        bp = B // plan["seq_parts"]
+        g = I.rng(4, stream=77)
+        cos, sin = qm.rope_table(1.0e7, 64, cap + 1)
+        self.rope = (torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda())
+        self.layers = []
+        dseed = 0x51A4 * 1000 + 7700 + plan["rank"] * 100
+        for li, kind in enumerate(LAYERS):
+            L = {"kind": kind}
+            if kind == "dn":
+                p = I.dn_layer_params(g)
+                L["keep"] = [torch.from_numpy(p[k]).cuda() for k in ("conv_w", "a_log", "dt_bias", "norm_gamma")]
+                L["prm"] = qm.dn_params(*L["keep"])
+                s = I.device_normal_f32((B, nvh, 128, 128), dseed + li, 0.02)
+                cv = torch.zeros(B, 4, 8192, device="cuda")
+                cv[:, 1:] = I.device_normal_f32((B, 3, 8192), dseed + 50 + li, 0.02)
+                L["store"] = (s, cv)
+                L["st"] = qm.DnState(ctx, B, s, cv, heads=(plan["vh_lo"], nvh))
+                L["st"].conv_pos = ctx_len
+                tok = I.dn_token_inputs(g, 1, B)
+                L["in"] = [torch.from_numpy(np.ascontiguousarray(tok[k][:, 0])).cuda()
+                           for k in ("qkv", "a", "b", "z")]
+                L["out"] = torch.empty(B, nvh * 128, device="cuda")
+            else:
+                p = I.gqa_layer_params(g, cap + 1)
+                L["keep"] = [torch.from_numpy(p["q_norm"]).cuda(), torch.from_numpy(p["k_norm"]).cuda(), *self.rope]
+                L["prm"] = qm.gqa_params(*L["keep"])
+                K = I.device_normal_bf16((bp, nkv, cap, 256), dseed + li, 0.02).view(torch.int16)
+                V = I.device_normal_bf16((bp, nkv, cap, 256), dseed + 70 + li, 0.02).view(torch.int16)
+                L["store"] = (K, V)
+                L["kv"] = qm.KvCache(ctx, bp, cap, K, V, heads=(plan["kv_lo"], nkv))
+                L["kv"].seq_len = ctx_len
+                tok = I.gqa_token_inputs(g, bp)
+                L["in"] = [torch.from_numpy(tok[k]).cuda() for k in ("q_gate", "k_new", "v_new")]
+                L["out"] = torch.empty(bp, nkv * 4 * 256, device="cuda")
+            L["gathered"] = torch.empty((world,) + tuple(L["out"].shape), device="cuda")
+            self.layers.append(L)
+        torch.cuda.synchronize()
+
+    def step(self):
+        mx, comm = self.mx, self.comm
+        for L in self.layers:
+            if L["kind"] == "dn":
+                qkv, a, b, z = L["in"]
+                mx.dn_decode(L["prm"], L["st"], qkv, a, b, None, z, L["out"])
+            else:
+                mx.gqa_decode(L["prm"], L["kv"], *L["in"], L["out"])
+            comm.allgather(L["out"], L["gathered"])
+
+    def close(self):
+        for L in self.layers:
+            for k in ("st", "kv"):
+                if k in L:
+                    L[k].close()
+        self.layers = []
+
+
+def bench_head_sharded(ctx, ws, rank, args):
+    """Time the head-sharded stack (B sequences in total across the ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    import qora_mixer as qm
+
+    plan = qm.shard_plan(ws, rank)
+    B = args.batch
+    cap = args.context + 2 * (args.warmup + args.steps) + 16
+    uid = [qm.comm_unique_id() if rank == 0 else None]
+    if ws > 1:
+        dist.broadcast_object_list(uid, src=0)
+    comm = qm.Comm(ctx, uid[0], ws, rank, timeout_ms=120000)
+    stack = ShardedStack(ctx, comm, plan, B, cap, ctx_len=args.context)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        stack.step()
+    ctx.sync()
+    barrier(ws)
+    ctx.set_timing(True)
+    n0 = ctx.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        stack.step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    launches = ctx.launch_count() - n0
+    ms = max_over_ranks(e0.elapsed_time(e1), ws)
+    kt = {k: ctx.kernel_time(k) for k in ("dn_decode", "gqa_prep", "gqa_attn", "gqa_combine", "allgather")}
+    ctx.set_timing(False)
+    stack.close()
+    comm.close()
+    torch.cuda.empty_cache()
+    gather_bytes = len(LAYERS) * B * 4096 * 4  # every layer's [B, 4096] f32 output, gathered
+    return {"workload": f"head-sharded mixer-stack decode, batch {B} in total, ctx {args.context}",
+            "value": round(B * args.steps / (ms / 1e3), 2), "unit": UNIT,
+            "ms_per_step": round(ms / args.steps, 4), "scaling": "strong",
+            "parallelism": (f"DeltaNet V heads /{ws}, GQA KV heads /{min(ws, 4)}"
+                            + (f" x batch /{ws // min(ws, 4)}" if ws > 4 else "")
+                            + ", NCCL all-gather of every layer's output"),
+            "allgather_bytes_per_step": gather_bytes, "gpu_launches": launches,
+            "kernels_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in kt.items()}}
+
 
 def run_ours(args):
     import torch
@@ -357,6 +485,10 @@ def run_ours(args):
         "kernel_ms_per_step": round(step_kernel_ms, 4),
         "clocks": clk,
     }
+    stack.close()
+    torch.cuda.empty_cache()
+    if (ws > 1 and not args.no_head_sharded) or args.head_sharded:
+        line["head_sharded"] = bench_head_sharded(ctx, ws, rank, args)
     if not args.no_prefill:
         line["prefill_gqa"] = bench_gqa_prefill(ctx, ws, args.prefill_reps)
         line["prefill_dn"] = bench_dn_prefill(ctx, ws, args.prefill_reps)
@@ -364,10 +496,6 @@ def run_ours(args):
         line["cpu_baseline"] = cpu_sample(args.cpu_tokens)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    for L in stack.layers:
-        for k in ("st", "kv"):
-            if k in L:
-                L[k].close()
     ctx.close()
     if ws > 1:
         import torch.distributed as dist
@@ -642,6 +770,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer (e2e) pass")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill measurements")
     ap.add_argument("--prefill-reps", type=int, default=3)
+    ap.add_argument("--head-sharded", action="store_true",
+                    help="also time the head-sharded variant at N=1 (always on for N>1)")
+    ap.add_argument("--no-head-sharded", action="store_true")
     ap.add_argument("--batch", type=int, default=B_PER_GPU, help="sequences per GPU")
     ap.add_argument("--context", type=int, default=CTX, help="cached positions per sequence")
     ap.add_argument("--cpu-tokens", type=int, default=4)

@@ -189,6 +189,17 @@ int qm_dn_decode_host(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, const
 int qm_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, int T, const uint16_t* qkv,
                   const float* a, const float* b, float* y, const float* z, float* out);
 
+/* Head-sharded state (multi-GPU, see qm_shard_plan): V heads
+ * [vh_lo, vh_lo + nvh) of every sequence, S [B,nvh,128,128]; vh_lo and nvh
+ * even (V heads 2j and 2j+1 share QK head j, gemv.rs:803-809, whose conv
+ * history the shard advances).  Decode on such a state reads the full-width
+ * inputs (qkv [B,8192], a/b [B,32], z [B,4096]) and writes y [B,nvh,128]
+ * and out [B,nvh*128] for its heads only.  Prefill takes full states only
+ * (QM_E_UNSUPPORTED).  qm_dn_state_create/wrap are the full range [0,32). */
+int qm_dn_state_create_heads(qm_ctx* ctx, int batch, int vh_lo, int nvh, qm_dn_state** out);
+int qm_dn_state_wrap_heads(qm_ctx* ctx, int batch, int vh_lo, int nvh, float* s, float* conv,
+                           qm_dn_state** out);
+int qm_dn_state_heads(const qm_dn_state* st, int* vh_lo, int* nvh);
 /* ------------------------------------------------------------------ */
 /* GQA KV cache                                                          */
 /* ------------------------------------------------------------------ */
@@ -209,6 +220,14 @@ int qm_kv_capacity(const qm_kv* kv);
 int qm_kv_batch(const qm_kv* kv);
 int qm_kv_data(const qm_kv* kv, uint16_t** k, uint16_t** v);
 
+/* Head-sharded cache: KV heads [kv_lo, kv_lo + nkv), K,V [B,nkv,capacity,256].
+ * Decode on it reads the full-width q_gate [B,16,512] and k_new/v_new
+ * [B,4,256] and writes out [B,nkv*4,256] (the query heads of its KV heads).
+ * Prefill takes full caches only (QM_E_UNSUPPORTED). */
+int qm_kv_create_heads(qm_ctx* ctx, int batch, int capacity, int kv_lo, int nkv, qm_kv** out);
+int qm_kv_wrap_heads(qm_ctx* ctx, int batch, int capacity, int kv_lo, int nkv, uint16_t* k,
+                     uint16_t* v, qm_kv** out);
+int qm_kv_heads(const qm_kv* kv, int* kv_lo, int* nkv);
 /* GQA layer parameters (device pointers). */
 typedef struct qm_gqa_params {
     const float* q_norm;   /* [256] q_norm widened from f16, applied as 1+g (gemv.rs:86,594) */
@@ -285,6 +304,41 @@ int qm_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, int T, const 
 int qm_gqa_decode_noalloc(const qm_gqa_params* p, uint16_t* k_cache, uint16_t* v_cache, int batch,
                           int capacity, int64_t seq_len, const float* q_gate, const float* k_new,
                           const float* v_new, float* out, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* Multi-GPU (one process per GPU).  The reference runs one device        */
+/* (src/gpu_inference.rs:981-1004); these calls spread a decode batch     */
+/* over the GPUs of one node.                                             */
+/* ------------------------------------------------------------------ */
+/* Head-sharded layout of rank `rank` of `world` (1, 2, 4, 8 or 16):
+ * DeltaNet V heads [vh_lo, vh_lo+nvh) = 32/world heads per rank; GQA KV
+ * heads [kv_lo, kv_lo+nkv) in min(world,4) groups, and, with more than 4
+ * ranks, part seq_part of seq_parts equal parts of the batch.  Sequence
+ * sharding (whole states per rank) needs no plan and no communication. */
+typedef struct qm_shard {
+    int world, rank;
+    int vh_lo, nvh;
+    int kv_lo, nkv;
+    int seq_part, seq_parts;
+} qm_shard;
+int qm_shard_plan(int world, int rank, qm_shard* out);
+
+/* NCCL communicator for the one collective of the head-sharded layout: the
+ * all-gather of the per-layer mixer outputs.  libnccl.so.2 is loaded at run
+ * time (QM_E_NCCL when absent).  One rank calls qm_comm_unique_id and
+ * passes the bytes to the others; every rank then calls qm_comm_create.
+ * Calls wait for NCCL at most timeout_ms on the host and then abort the
+ * communicator (QM_E_TIMEOUT), so a rank that never joins cannot hang the
+ * others. */
+#define QM_COMM_ID_BYTES 128
+typedef struct qm_comm qm_comm;
+int qm_comm_unique_id(unsigned char* id /* [QM_COMM_ID_BYTES] */);
+int qm_comm_create(qm_ctx* ctx, const unsigned char* id, int world, int rank, int timeout_ms,
+                   qm_comm** out);
+/* recv[world * bytes_per_rank] = every rank's send[bytes_per_rank], in rank
+ * order, on the context's stream. */
+int qm_comm_allgather(qm_comm* comm, const void* send, void* recv, size_t bytes_per_rank);
+int qm_comm_destroy(qm_comm* comm);
 
 #ifdef __cplusplus
 }

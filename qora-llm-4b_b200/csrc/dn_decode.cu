@@ -37,12 +37,13 @@ dn_decode_kernel(const float* __restrict__ qkv, const float* __restrict__ a_in,
                  const float* __restrict__ a_log, const float* __restrict__ dt_bias,
                  const float* __restrict__ norm_gamma, float* __restrict__ S,
                  float* __restrict__ conv, int slot_w, float* __restrict__ y,
-                 const float* __restrict__ z, float* __restrict__ out) {
+                 const float* __restrict__ z, float* __restrict__ out, int vh_lo, int nvh) {
     constexpr int ROWS = kHd / SPLIT;
     constexpr int PASSES = ROWS / 32;
     static_assert(PASSES >= 1, "ROWS must be a multiple of 32");
 
-    const int vh = blockIdx.x / SPLIT;
+    const int lh = blockIdx.x / SPLIT;  // head within the state's range
+    const int vh = vh_lo + lh;          // model V head (inputs, params, conv channels)
     const int part = blockIdx.x % SPLIT;
     const int b = blockIdx.y;
     const int tid = threadIdx.x;
@@ -60,7 +61,7 @@ dn_decode_kernel(const float* __restrict__ qkv, const float* __restrict__ a_in,
     __shared__ float s_sq;
 
     // ---- 1. issue the state loads first (they overlap the prologue) ----
-    float* Sh = S + ((size_t)(b * kNumV + vh) * kHd + part * ROWS) * kHd;
+    float* Sh = S + ((size_t)(b * nvh + lh) * kHd + part * ROWS) * kHd;
     float4 sr[PASSES][4];
 #pragma unroll
     for (int p = 0; p < PASSES; p++) {
@@ -148,7 +149,7 @@ dn_decode_kernel(const float* __restrict__ qkv, const float* __restrict__ a_in,
         kr[j] = reinterpret_cast<const float4*>(s_qk[1])[j * 8 + lane8];
         qr[j] = reinterpret_cast<const float4*>(s_qk[0])[j * 8 + lane8];
     }
-    float* yb = y ? y + ((size_t)b * kNumV + vh) * kHd + part * ROWS : nullptr;
+    float* yb = y ? y + ((size_t)b * nvh + lh) * kHd + part * ROWS : nullptr;
     float sq_part = 0.f;
 #pragma unroll
     for (int p = 0; p < PASSES; p++) {
@@ -225,9 +226,8 @@ dn_decode_kernel(const float* __restrict__ qkv, const float* __restrict__ a_in,
         const float inv_rms = 1.0f / sqrtf(total * (1.0f / kHd) + 1e-6f);
         if (tid < ROWS) {
             const int c = part * ROWS + tid;
-            const size_t o = (size_t)b * kVDim + (size_t)vh * kHd + c;
             const float yn = s_y[tid] * inv_rms * norm_gamma[c];
-            out[o] = yn * silu_f(z[o]);
+            out[((size_t)b * nvh + lh) * kHd + c] = yn * silu_f(z[(size_t)b * kVDim + (size_t)vh * kHd + c]);
         }
     }
 }
@@ -236,7 +236,7 @@ template <int SPLIT, bool FUSED>
 cudaError_t launch_t(cudaStream_t st, int B, const qm_dn_params* p, qm_dn_state* s,
                      const float* qkv, const float* a, const float* b, float* y, const float* z,
                      float* out, int slot_w) {
-    dim3 grid(kNumV * SPLIT, B);
+    dim3 grid(s->nvh * SPLIT, B);
     if (FUSED && SPLIT > 1) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = grid;
@@ -251,19 +251,19 @@ cudaError_t launch_t(cudaStream_t st, int B, const qm_dn_params* p, qm_dn_state*
         cfg.numAttrs = 1;
         return cudaLaunchKernelEx(&cfg, dn_decode_kernel<SPLIT, FUSED>, qkv, a, b, p->conv_w,
                                   p->a_log, p->dt_bias, p->norm_gamma, s->s, s->conv, slot_w, y,
-                                  z, out);
+                                  z, out, s->vh_lo, s->nvh);
     }
     dn_decode_kernel<SPLIT, FUSED><<<grid, 256, 0, st>>>(qkv, a, b, p->conv_w, p->a_log,
                                                          p->dt_bias, p->norm_gamma, s->s, s->conv,
-                                                         slot_w, y, z, out);
+                                                         slot_w, y, z, out, s->vh_lo, s->nvh);
     return cudaGetLastError();
 }
 
 }  // namespace
 
-int dn_decode_split_for(int batch, int num_sms) {
-    if (batch * kNumV >= num_sms) return 1;
-    if (batch * kNumV * 2 >= num_sms) return 2;
+int dn_decode_split_for(int units, int num_sms) {
+    if (units >= num_sms) return 1;
+    if (units * 2 >= num_sms) return 2;
     return 4;
 }
 
@@ -271,7 +271,7 @@ cudaError_t launch_dn_decode(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st
                              const float* a, const float* b, float* y, const float* z, float* out) {
     const int B = st->batch;
     const int slot_w = (int)(st->conv_pos & 3);
-    const int split = dn_decode_split_for(B, ctx->num_sms);
+    const int split = dn_decode_split_for(B * st->nvh, ctx->num_sms);
     const bool fused = (z != nullptr);
     cudaError_t e;
     TimedLaunch tl(ctx, "dn_decode");

@@ -663,6 +663,8 @@ extern "C" int qm_dn_prefill(qm_ctx* c, const qm_dn_params* p, qm_dn_state* st, 
     if (!st || !qkv || !a || !b || !y || T <= 0 || (out && !z) || (z && !out))
         return set_error(c, QM_E_ARG, "qm_dn_prefill: null pointer, T <= 0, or out without z");
     if (st->ctx != c) return set_error(c, QM_E_MISMATCH, "state belongs to another context");
+    if (st->nvh != kNumV)
+        return set_error(c, QM_E_UNSUPPORTED, "qm_dn_prefill: head-sharded states are decode-only");
     if ((uintptr_t)p->conv_w & 15) return set_error(c, QM_E_ARG, "conv_w must be 16-byte aligned");
     if ((y && ((uintptr_t)y & 15)) || (out && ((uintptr_t)out & 15)) || (z && ((uintptr_t)z & 15)))
         return set_error(c, QM_E_ARG, "qm_dn_prefill: y/z/out must be 16-byte aligned");

@@ -40,11 +40,12 @@ struct Plan {
     int ntiles = 0, nsplit = 0, tps = 0;
 };
 
-Plan plan_for(int B, int64_t L, int num_sms) {
+// B * nkv (sequence, KV head) pairs share the SMs.
+Plan plan_for(int B, int nkv, int64_t L, int num_sms) {
     Plan p;
     p.ntiles = (int)((L + kTile - 1) / kTile);
     if (p.ntiles == 0) return p;
-    const int64_t units = (int64_t)B * kNumKVH;
+    const int64_t units = (int64_t)B * nkv;
     const int64_t total = (int64_t)p.ntiles * units;
     const int64_t waves = std::max<int64_t>(1, total / ((int64_t)num_sms * 8));
     const int64_t target = waves * num_sms;
@@ -60,14 +61,16 @@ struct WsLayout {
 
 inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
-WsLayout ws_layout(int B, int nsplit) {
+// Workspace for B sequences x nkv KV heads (nkv * 4 query heads).
+WsLayout ws_layout(int B, int nkv, int nsplit) {
     WsLayout w;
+    const size_t nh = (size_t)nkv * kGroup;
     size_t off = 0;
-    w.q_bf = off;    off += al256((size_t)B * kNumH * 2 * kD * 2);
-    w.q_f32 = off;   off += al256((size_t)B * kNumH * kD * 4);
-    w.kn = off;      off += al256((size_t)B * kNumKVH * kD * 4);
-    w.part_o = off;  off += al256((size_t)B * kNumH * std::max(nsplit, 1) * kD * 4);
-    w.part_ml = off; off += al256((size_t)B * kNumH * std::max(nsplit, 1) * 2 * 4);
+    w.q_bf = off;    off += al256((size_t)B * nh * 2 * kD * 2);
+    w.q_f32 = off;   off += al256((size_t)B * nh * kD * 4);
+    w.kn = off;      off += al256((size_t)B * nkv * kD * 4);
+    w.part_o = off;  off += al256((size_t)B * nh * std::max(nsplit, 1) * kD * 4);
+    w.part_ml = off; off += al256((size_t)B * nh * std::max(nsplit, 1) * 2 * 4);
     w.total = off;
     return w;
 }
@@ -81,11 +84,13 @@ gqa_prep_kernel(const float* __restrict__ q_gate, const float* __restrict__ k_ne
                 const float* __restrict__ k_norm, const float* __restrict__ rope_cos,
                 const float* __restrict__ rope_sin, int64_t pos, uint16_t* __restrict__ kcache,
                 uint16_t* __restrict__ vcache, int cap, uint16_t* __restrict__ q_bf,
-                float* __restrict__ q_f32, float* __restrict__ kn_out) {
-    const int b = blockIdx.x / kNumKVH, g = blockIdx.x % kNumKVH;
+                float* __restrict__ q_f32, float* __restrict__ kn_out, int kv_lo, int nkv) {
+    // gl: KV head within the cache's range; g, h: model KV / query head (inputs)
+    const int b = blockIdx.x / nkv, gl = blockIdx.x % nkv, g = kv_lo + gl;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool is_q = warp < kGroup;
     const int h = g * kGroup + warp;
+    const size_t hl = ((size_t)b * nkv + gl) * kGroup + warp;  // local query-head row
     const float* src = is_q ? q_gate + ((size_t)b * kNumH + h) * 2 * kD
                             : k_new + ((size_t)b * kNumKVH + g) * kD;
     const float* gamma = is_q ? q_norm : k_norm;
@@ -110,8 +115,8 @@ gqa_prep_kernel(const float* __restrict__ q_gate, const float* __restrict__ k_ne
         x[1] = x2 * c + x1 * s;
     }
     if (is_q) {
-        uint16_t* qh = q_bf + ((size_t)b * kNumH + h) * 2 * kD;
-        float* qf = q_f32 + ((size_t)b * kNumH + h) * kD;
+        uint16_t* qh = q_bf + hl * 2 * kD;
+        float* qf = q_f32 + hl * kD;
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int e = lane + 32 * i;
@@ -123,9 +128,9 @@ gqa_prep_kernel(const float* __restrict__ q_gate, const float* __restrict__ k_ne
             qh[kD + e] = lo;
         }
     } else {
-        const size_t row = (((size_t)b * kNumKVH + g) * cap + pos) * kD;
+        const size_t row = (((size_t)b * nkv + gl) * cap + pos) * kD;
         const float* vs = v_new + ((size_t)b * kNumKVH + g) * kD;
-        float* kn = kn_out + ((size_t)b * kNumKVH + g) * kD;
+        float* kn = kn_out + ((size_t)b * nkv + gl) * kD;
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int e = lane + 32 * i;
@@ -149,7 +154,7 @@ __device__ __forceinline__ uint32_t swz_addr(uint32_t base, int pos, int dim) {
 __global__ void __launch_bounds__(160, 1)
 gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                 const uint16_t* __restrict__ q_bf, float* __restrict__ part_o,
-                float* __restrict__ part_ml, int L, int tps, int nsplit, int* err) {
+                float* __restrict__ part_ml, int L, int tps, int nsplit, int nkv, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -179,7 +184,7 @@ gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__
         if (lane == 0) {
             prefetch_tmap(&tmk);
             prefetch_tmap(&tmv);
-            const int zc = b * kNumKVH + g;
+            const int zc = b * nkv + g;
             int it = 0;
             for (; it < ntiles; it++) {
                 const int st = it % kStages, round = it / kStages;
@@ -209,7 +214,7 @@ gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__
     uint32_t qa[16][2];
     {
         const int head = row & 3, hl = row >> 2;
-        const uint16_t* qr = q_bf + (((size_t)b * kNumH + g * kGroup + head) * 2 + hl) * kD;
+        const uint16_t* qr = q_bf + ((((size_t)b * nkv + g) * kGroup + head) * 2 + hl) * kD;
 #pragma unroll
         for (int kk = 0; kk < 16; kk++) {
             qa[kk][0] = *reinterpret_cast<const uint32_t*>(qr + kk * 16 + quad * 2);
@@ -345,7 +350,7 @@ gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__
                 acc += sc * mo[(w * kGroup + head) * kD + d];
             }
         }
-        const size_t hidx = (size_t)b * kNumH + g * kGroup + head;
+        const size_t hidx = ((size_t)b * nkv + g) * kGroup + head;
         part_o[(hidx * nsplit + split) * kD + d] = acc;
         if (d == 0) {
             float lsum = 0.f;
@@ -369,13 +374,15 @@ __global__ void __launch_bounds__(256)
 gqa_combine_kernel(const float* __restrict__ q_f32, const float* __restrict__ kn,
                    const float* __restrict__ v_new, const float* __restrict__ q_gate,
                    const float* __restrict__ part_o, const float* __restrict__ part_ml, int nsplit,
-                   float* __restrict__ out) {
-    const int bh = blockIdx.x;
-    const int b = bh / kNumH, h = bh % kNumH, g = h / kGroup;
+                   float* __restrict__ out, int kv_lo, int nkv) {
+    const int bh = blockIdx.x;  // local (sequence, query head) row
+    const int nh = nkv * kGroup;
+    const int b = bh / nh, hl = bh % nh, gl = hl / kGroup;
+    const int h = kv_lo * kGroup + hl, g = kv_lo + gl;  // model heads (inputs)
     const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
     __shared__ float s_red[8];
     __shared__ float s_ml[2 * 512];
-    float prod = q_f32[(size_t)bh * kD + d] * kn[((size_t)b * kNumKVH + g) * kD + d];
+    float prod = q_f32[(size_t)bh * kD + d] * kn[((size_t)b * nkv + gl) * kD + d];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) prod += __shfl_xor_sync(0xffffffffu, prod, o);
     if (lane == 0) s_red[warp] = prod;
@@ -400,15 +407,15 @@ gqa_combine_kernel(const float* __restrict__ q_f32, const float* __restrict__ kn
         acc += w * part_o[((size_t)bh * nsplit + i) * kD + d];
         lsum += w * li;
     }
-    const float gate = q_gate[(size_t)bh * 2 * kD + kD + d];
+    const float gate = q_gate[((size_t)b * kNumH + h) * 2 * kD + kD + d];
     out[(size_t)bh * kD + d] = (acc / lsum) * (1.0f / (1.0f + __expf(-gate)));
 }
 
 }  // namespace
 
-size_t gqa_decode_ws_bytes(int batch, int64_t seq_len, int num_sms) {
-    Plan p = plan_for(batch, seq_len, num_sms);
-    return ws_layout(batch, p.nsplit).total;
+size_t gqa_decode_ws_bytes(int batch, int nkv, int64_t seq_len, int num_sms) {
+    Plan p = plan_for(batch, nkv, seq_len, num_sms);
+    return ws_layout(batch, nkv, p.nsplit).total;
 }
 
 cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
@@ -416,8 +423,9 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
                               float* out, void* ws, size_t ws_bytes) {
     const int B = kv->batch;
     const int64_t L = kv->seq_len;  // cached positions; the new token goes to index L
-    const Plan pl = plan_for(B, L, ctx->num_sms);
-    const WsLayout w = ws_layout(B, pl.nsplit);
+    const int nkv = kv->nkv;
+    const Plan pl = plan_for(B, nkv, L, ctx->num_sms);
+    const WsLayout w = ws_layout(B, nkv, pl.nsplit);
     if (w.total > ws_bytes) return cudaErrorInvalidValue;
     char* base = static_cast<char*>(ws);
     uint16_t* q_bf = reinterpret_cast<uint16_t*>(base + w.q_bf);
@@ -429,9 +437,9 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
 
     {
         TimedLaunch tl(ctx, "gqa_prep");
-        gqa_prep_kernel<<<B * kNumKVH, 160, 0, st>>>(q_gate, k_new, v_new, prm->q_norm,
-                                                     prm->k_norm, prm->rope_cos, prm->rope_sin, L,
-                                                     kv->k, kv->v, kv->capacity, q_bf, q_f32, kn);
+        gqa_prep_kernel<<<B * nkv, 160, 0, st>>>(q_gate, k_new, v_new, prm->q_norm, prm->k_norm,
+                                                 prm->rope_cos, prm->rope_sin, L, kv->k, kv->v,
+                                                 kv->capacity, q_bf, q_f32, kn, kv->kv_lo, nkv);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -444,10 +452,10 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
             if (e != cudaSuccess) return e;
             attr_set[ctx->device] = true;
         }
-        dim3 grid(pl.nsplit, kNumKVH, B);
+        dim3 grid(pl.nsplit, nkv, B);
         TimedLaunch tl(ctx, "gqa_attn");
         gqa_attn_kernel<<<grid, 160, kAttnSmem, st>>>(kv->tmap_k, kv->tmap_v, q_bf, part_o,
-                                                      part_ml, (int)L, pl.tps, pl.nsplit,
+                                                      part_ml, (int)L, pl.tps, pl.nsplit, nkv,
                                                       ctx->d_err);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
@@ -455,8 +463,8 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
     }
     {
         TimedLaunch tl(ctx, "gqa_combine");
-        gqa_combine_kernel<<<B * kNumH, 256, 0, st>>>(q_f32, kn, v_new, q_gate, part_o, part_ml,
-                                                      pl.nsplit, out);
+        gqa_combine_kernel<<<B * nkv * kGroup, 256, 0, st>>>(q_f32, kn, v_new, q_gate, part_o,
+                                                             part_ml, pl.nsplit, out, kv->kv_lo, nkv);
     }
     e = cudaGetLastError();
     if (e == cudaSuccess) ctx->launches += 1;

@@ -39,7 +39,6 @@
 
 namespace qm {
 
-int encode_cache_tmap(CUtensorMap* m, void* base, int batch, int capacity, int box_rows);
 int encode_rows_tmap(CUtensorMap* m, void* base, uint64_t inner, uint64_t rows, uint64_t planes,
                      uint32_t box_inner, uint32_t box_rows, bool fp16);
 
@@ -572,6 +571,8 @@ extern "C" int qm_gqa_prefill(qm_ctx* c, const qm_gqa_params* p, qm_kv* kv, int 
     if (!kv || !q_gate || !k || !v || !out || T <= 0)
         return set_error(c, QM_E_ARG, "qm_gqa_prefill: null pointer or T <= 0");
     if (kv->ctx != c) return set_error(c, QM_E_MISMATCH, "cache belongs to another context");
+    if (kv->nkv != kNumKVH)
+        return set_error(c, QM_E_UNSUPPORTED, "qm_gqa_prefill: head-sharded caches are decode-only");
     if (T > kv->capacity) return set_error(c, QM_E_RANGE, "qm_gqa_prefill: T exceeds the cache capacity");
     if (T > p->max_pos) return set_error(c, QM_E_RANGE, "qm_gqa_prefill: T exceeds the RoPE table");
     if (((uintptr_t)out & 15) || ((uintptr_t)q_gate & 15))

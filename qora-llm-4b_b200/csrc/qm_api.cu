@@ -76,12 +76,12 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_tiled() {
     return fn;
 }
 
-// 3-D bf16 view of a cache [B*4][cap][256]: box {64 dims, 64 positions, 1},
-// 128-byte swizzle, zero fill past the capacity.
-int encode_cache_tmap(CUtensorMap* m, void* base, int batch, int capacity, int box_rows) {
+// 3-D bf16 view of a cache [planes = B*nkv][cap][256]: box {64 dims, 64
+// positions, 1}, 128-byte swizzle, zero fill past the capacity.
+int encode_cache_tmap(CUtensorMap* m, void* base, int planes, int capacity, int box_rows) {
     auto enc = get_encode_tiled();
     if (!enc) return QM_E_CUDA;
-    cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)capacity, (cuuint64_t)batch * kNumKVH};
+    cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)capacity, (cuuint64_t)planes};
     cuuint64_t strides[2] = {(cuuint64_t)kD * 2, (cuuint64_t)capacity * kD * 2};
     cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
     cuuint32_t estr[3] = {1, 1, 1};
@@ -109,8 +109,9 @@ int encode_rows_tmap(CUtensorMap* m, void* base, uint64_t inner, uint64_t rows, 
 
 int make_kv_tmaps(qm_kv* kv) {
     kv->tmaps_ok = false;
-    if (encode_cache_tmap(&kv->tmap_k, kv->k, kv->batch, kv->capacity, 64) != QM_OK ||
-        encode_cache_tmap(&kv->tmap_v, kv->v, kv->batch, kv->capacity, 64) != QM_OK)
+    const int planes = kv->batch * kv->nkv;
+    if (encode_cache_tmap(&kv->tmap_k, kv->k, planes, kv->capacity, 64) != QM_OK ||
+        encode_cache_tmap(&kv->tmap_v, kv->v, planes, kv->capacity, 64) != QM_OK)
         return set_error(kv->ctx, QM_E_CUDA, "cuTensorMapEncodeTiled failed for the KV cache");
     kv->tmaps_ok = true;
     return QM_OK;
@@ -322,11 +323,19 @@ extern "C" int qm_rope_table(float theta, int rope_dim, int max_pos, float* cos_
 // ---------------------------------------------------------------------------
 // DeltaNet state handles
 // ---------------------------------------------------------------------------
-static const size_t kSPerSeq = (size_t)kNumV * kHd * kHd;        // floats
 static const size_t kConvPerSeq = (size_t)kConvSlots * kQKVDim;  // floats
+static size_t s_per_seq(const qm_dn_state* st) { return (size_t)st->nvh * kHd * kHd; }  // floats
 
-extern "C" int qm_dn_state_create(qm_ctx* c, int batch, qm_dn_state** out) {
+// V heads 2j and 2j+1 share QK head j, whose conv history the even head
+// advances: a head range must start and end on a QK-head boundary.
+static bool dn_heads_ok(int vh_lo, int nvh) {
+    return vh_lo >= 0 && nvh >= 2 && vh_lo + nvh <= kNumV && (vh_lo % 2) == 0 && (nvh % 2) == 0;
+}
+
+extern "C" int qm_dn_state_create_heads(qm_ctx* c, int batch, int vh_lo, int nvh, qm_dn_state** out) {
     if (!c || !out || batch <= 0) return set_error(c, QM_E_ARG, "qm_dn_state_create: bad argument");
+    if (!dn_heads_ok(vh_lo, nvh))
+        return set_error(c, QM_E_ARG, "V-head range must be even-aligned within [0, 32)");
     *out = nullptr;
     cudaSetDevice(c->device);
     qm_dn_state* st = new (std::nothrow) qm_dn_state();
@@ -334,8 +343,10 @@ extern "C" int qm_dn_state_create(qm_ctx* c, int batch, qm_dn_state** out) {
     st->ctx = c;
     st->device = c->device;
     st->batch = batch;
+    st->vh_lo = vh_lo;
+    st->nvh = nvh;
     st->owned = true;
-    if (cudaMalloc(&st->s, kSPerSeq * batch * 4) != cudaSuccess ||
+    if (cudaMalloc(&st->s, s_per_seq(st) * batch * 4) != cudaSuccess ||
         cudaMalloc(&st->conv, kConvPerSeq * batch * 4) != cudaSuccess) {
         if (st->s) cudaFree(st->s);
         delete st;
@@ -350,9 +361,16 @@ extern "C" int qm_dn_state_create(qm_ctx* c, int batch, qm_dn_state** out) {
     return QM_OK;
 }
 
-extern "C" int qm_dn_state_wrap(qm_ctx* c, int batch, float* s, float* conv, qm_dn_state** out) {
+extern "C" int qm_dn_state_create(qm_ctx* c, int batch, qm_dn_state** out) {
+    return qm_dn_state_create_heads(c, batch, 0, kNumV, out);
+}
+
+extern "C" int qm_dn_state_wrap_heads(qm_ctx* c, int batch, int vh_lo, int nvh, float* s, float* conv,
+                                      qm_dn_state** out) {
     if (!c || !out || batch <= 0 || !s || !conv)
         return set_error(c, QM_E_ARG, "qm_dn_state_wrap: bad argument");
+    if (!dn_heads_ok(vh_lo, nvh))
+        return set_error(c, QM_E_ARG, "V-head range must be even-aligned within [0, 32)");
     if (((uintptr_t)s & 15) || ((uintptr_t)conv & 15))
         return set_error(c, QM_E_ARG, "qm_dn_state_wrap: storage must be 16-byte aligned");
     qm_dn_state* st = new (std::nothrow) qm_dn_state();
@@ -360,10 +378,23 @@ extern "C" int qm_dn_state_wrap(qm_ctx* c, int batch, float* s, float* conv, qm_
     st->ctx = c;
     st->device = c->device;
     st->batch = batch;
+    st->vh_lo = vh_lo;
+    st->nvh = nvh;
     st->s = s;
     st->conv = conv;
     st->owned = false;
     *out = st;
+    return QM_OK;
+}
+
+extern "C" int qm_dn_state_wrap(qm_ctx* c, int batch, float* s, float* conv, qm_dn_state** out) {
+    return qm_dn_state_wrap_heads(c, batch, 0, kNumV, s, conv, out);
+}
+
+extern "C" int qm_dn_state_heads(const qm_dn_state* st, int* vh_lo, int* nvh) {
+    if (!st) return QM_E_ARG;
+    if (vh_lo) *vh_lo = st->vh_lo;
+    if (nvh) *nvh = st->nvh;
     return QM_OK;
 }
 
@@ -382,7 +413,7 @@ extern "C" int qm_dn_state_reset(qm_ctx* c, qm_dn_state* st) {
     if (!c || !st) return QM_E_ARG;
     if (st->ctx != c) return set_error(c, QM_E_MISMATCH, "state belongs to another context");
     cudaSetDevice(c->device);
-    QM_CHECK_CUDA(c, cudaMemsetAsync(st->s, 0, kSPerSeq * st->batch * 4, c->stream));
+    QM_CHECK_CUDA(c, cudaMemsetAsync(st->s, 0, s_per_seq(st) * st->batch * 4, c->stream));
     QM_CHECK_CUDA(c, cudaMemsetAsync(st->conv, 0, kConvPerSeq * st->batch * 4, c->stream));
     st->conv_pos = 0;
     return QM_OK;
@@ -390,7 +421,7 @@ extern "C" int qm_dn_state_reset(qm_ctx* c, qm_dn_state* st) {
 
 extern "C" int qm_dn_state_snapshot(qm_ctx* c, const qm_dn_state* src, qm_dn_state** out) {
     if (!c || !src || !out) return QM_E_ARG;
-    int rc = qm_dn_state_create(c, src->batch, out);
+    int rc = qm_dn_state_create_heads(c, src->batch, src->vh_lo, src->nvh, out);
     if (rc != QM_OK) return rc;
     rc = qm_dn_state_restore(c, *out, src);
     if (rc != QM_OK) {
@@ -402,10 +433,10 @@ extern "C" int qm_dn_state_snapshot(qm_ctx* c, const qm_dn_state* src, qm_dn_sta
 
 extern "C" int qm_dn_state_restore(qm_ctx* c, qm_dn_state* dst, const qm_dn_state* src) {
     if (!c || !dst || !src) return QM_E_ARG;
-    if (dst->batch != src->batch)
-        return set_error(c, QM_E_MISMATCH, "restore: batch sizes differ (reference: panic)");
+    if (dst->batch != src->batch || dst->vh_lo != src->vh_lo || dst->nvh != src->nvh)
+        return set_error(c, QM_E_MISMATCH, "restore: batch sizes or head ranges differ (reference: panic)");
     cudaSetDevice(c->device);
-    QM_CHECK_CUDA(c, cudaMemcpyAsync(dst->s, src->s, kSPerSeq * src->batch * 4,
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(dst->s, src->s, s_per_seq(src) * src->batch * 4,
                                      cudaMemcpyDeviceToDevice, c->stream));
     QM_CHECK_CUDA(c, cudaMemcpyAsync(dst->conv, src->conv, kConvPerSeq * src->batch * 4,
                                      cudaMemcpyDeviceToDevice, c->stream));
@@ -425,7 +456,8 @@ extern "C" int qm_dn_state_read(qm_ctx* c, const qm_dn_state* st, int b, float* 
     cudaSetDevice(c->device);
     QM_CHECK_CUDA(c, cudaStreamSynchronize(c->stream));
     if (s_h)
-        QM_CHECK_CUDA(c, cudaMemcpy(s_h, st->s + kSPerSeq * b, kSPerSeq * 4, cudaMemcpyDeviceToHost));
+        QM_CHECK_CUDA(c, cudaMemcpy(s_h, st->s + s_per_seq(st) * b, s_per_seq(st) * 4,
+                                    cudaMemcpyDeviceToHost));
     if (conv_h) {
         std::vector<float> ring(kConvPerSeq);
         QM_CHECK_CUDA(c, cudaMemcpy(ring.data(), st->conv + kConvPerSeq * b, kConvPerSeq * 4,
@@ -444,7 +476,8 @@ extern "C" int qm_dn_state_write(qm_ctx* c, qm_dn_state* st, int b, const float*
     cudaSetDevice(c->device);
     QM_CHECK_CUDA(c, cudaStreamSynchronize(c->stream));
     if (s_h)
-        QM_CHECK_CUDA(c, cudaMemcpy(st->s + kSPerSeq * b, s_h, kSPerSeq * 4, cudaMemcpyHostToDevice));
+        QM_CHECK_CUDA(c, cudaMemcpy(st->s + s_per_seq(st) * b, s_h, s_per_seq(st) * 4,
+                                    cudaMemcpyHostToDevice));
     if (conv_h) {
         std::vector<float> ring(kConvPerSeq, 0.0f);
         for (int j = 0; j < 3; j++) {
@@ -502,8 +535,9 @@ extern "C" int qm_dn_decode_host(qm_ctx* c, const qm_dn_params* p, qm_dn_state* 
                                  const float* z, float* out) {
     if (!c || !st) return QM_E_ARG;
     const size_t B = st->batch;
-    const size_t n_qkv = B * kQKVDim, n_ab = B * kNumV, n_y = B * kVDim;
-    size_t bytes = 4 * (n_qkv + 2 * n_ab + (y ? n_y : 0) + (z ? 2 * n_y : 0)) + 256 * 6;
+    // inputs are full width; y and out cover the state's V heads
+    const size_t n_qkv = B * kQKVDim, n_ab = B * kNumV, n_z = B * kVDim, n_y = B * st->nvh * kHd;
+    size_t bytes = 4 * (n_qkv + 2 * n_ab + (y ? n_y : 0) + (z ? n_z + n_y : 0)) + 256 * 6;
     cudaSetDevice(c->device);
     int rc = ensure_stage(c, bytes);
     if (rc) return rc;
@@ -517,13 +551,13 @@ extern "C" int qm_dn_decode_host(qm_ctx* c, const qm_dn_params* p, qm_dn_state* 
     float* d_a = carve(n_ab);
     float* d_b = carve(n_ab);
     float* d_y = y ? carve(n_y) : nullptr;
-    float* d_z = z ? carve(n_y) : nullptr;
+    float* d_z = z ? carve(n_z) : nullptr;
     float* d_out = z ? carve(n_y) : nullptr;
     cudaStream_t s = c->stream;
     QM_CHECK_CUDA(c, cudaMemcpyAsync(d_qkv, qkv, n_qkv * 4, cudaMemcpyHostToDevice, s));
     QM_CHECK_CUDA(c, cudaMemcpyAsync(d_a, a, n_ab * 4, cudaMemcpyHostToDevice, s));
     QM_CHECK_CUDA(c, cudaMemcpyAsync(d_b, b, n_ab * 4, cudaMemcpyHostToDevice, s));
-    if (z) QM_CHECK_CUDA(c, cudaMemcpyAsync(d_z, z, n_y * 4, cudaMemcpyHostToDevice, s));
+    if (z) QM_CHECK_CUDA(c, cudaMemcpyAsync(d_z, z, n_z * 4, cudaMemcpyHostToDevice, s));
     rc = qm_dn_decode(c, p, st, d_qkv, d_a, d_b, d_y, d_z, d_out);
     if (rc) return rc;
     if (y) QM_CHECK_CUDA(c, cudaMemcpyAsync(y, d_y, n_y * 4, cudaMemcpyDeviceToHost, s));
@@ -534,11 +568,13 @@ extern "C" int qm_dn_decode_host(qm_ctx* c, const qm_dn_params* p, qm_dn_state* 
 // ---------------------------------------------------------------------------
 // KV cache handles
 // ---------------------------------------------------------------------------
-static size_t kv_elems(int batch, int cap) { return (size_t)batch * kNumKVH * cap * kD; }
+static size_t kv_elems(int batch, int nkv, int cap) { return (size_t)batch * nkv * cap * kD; }
 
-extern "C" int qm_kv_create(qm_ctx* c, int batch, int capacity, qm_kv** out) {
+extern "C" int qm_kv_create_heads(qm_ctx* c, int batch, int capacity, int kv_lo, int nkv, qm_kv** out) {
     if (!c || !out || batch <= 0 || capacity <= 0)
         return set_error(c, QM_E_ARG, "qm_kv_create: bad argument");
+    if (kv_lo < 0 || nkv < 1 || kv_lo + nkv > kNumKVH)
+        return set_error(c, QM_E_ARG, "KV-head range outside [0, 4)");
     *out = nullptr;
     cudaSetDevice(c->device);
     qm_kv* kv = new (std::nothrow) qm_kv();
@@ -547,8 +583,10 @@ extern "C" int qm_kv_create(qm_ctx* c, int batch, int capacity, qm_kv** out) {
     kv->device = c->device;
     kv->batch = batch;
     kv->capacity = capacity;
+    kv->kv_lo = kv_lo;
+    kv->nkv = nkv;
     kv->owned = true;
-    size_t bytes = kv_elems(batch, capacity) * 2;
+    size_t bytes = kv_elems(batch, nkv, capacity) * 2;
     if (cudaMalloc(&kv->k, bytes) != cudaSuccess || cudaMalloc(&kv->v, bytes) != cudaSuccess) {
         if (kv->k) cudaFree(kv->k);
         delete kv;
@@ -565,9 +603,16 @@ extern "C" int qm_kv_create(qm_ctx* c, int batch, int capacity, qm_kv** out) {
     return QM_OK;
 }
 
-extern "C" int qm_kv_wrap(qm_ctx* c, int batch, int capacity, uint16_t* k, uint16_t* v, qm_kv** out) {
+extern "C" int qm_kv_create(qm_ctx* c, int batch, int capacity, qm_kv** out) {
+    return qm_kv_create_heads(c, batch, capacity, 0, kNumKVH, out);
+}
+
+extern "C" int qm_kv_wrap_heads(qm_ctx* c, int batch, int capacity, int kv_lo, int nkv, uint16_t* k,
+                                uint16_t* v, qm_kv** out) {
     if (!c || !out || batch <= 0 || capacity <= 0 || !k || !v)
         return set_error(c, QM_E_ARG, "qm_kv_wrap: bad argument");
+    if (kv_lo < 0 || nkv < 1 || kv_lo + nkv > kNumKVH)
+        return set_error(c, QM_E_ARG, "KV-head range outside [0, 4)");
     if (((uintptr_t)k & 15) || ((uintptr_t)v & 15))
         return set_error(c, QM_E_ARG, "qm_kv_wrap: cache must be 16-byte aligned");
     qm_kv* kv = new (std::nothrow) qm_kv();
@@ -576,6 +621,8 @@ extern "C" int qm_kv_wrap(qm_ctx* c, int batch, int capacity, uint16_t* k, uint1
     kv->device = c->device;
     kv->batch = batch;
     kv->capacity = capacity;
+    kv->kv_lo = kv_lo;
+    kv->nkv = nkv;
     kv->k = k;
     kv->v = v;
     kv->owned = false;
@@ -585,6 +632,17 @@ extern "C" int qm_kv_wrap(qm_ctx* c, int batch, int capacity, uint16_t* k, uint1
         return rc;
     }
     *out = kv;
+    return QM_OK;
+}
+
+extern "C" int qm_kv_wrap(qm_ctx* c, int batch, int capacity, uint16_t* k, uint16_t* v, qm_kv** out) {
+    return qm_kv_wrap_heads(c, batch, capacity, 0, kNumKVH, k, v, out);
+}
+
+extern "C" int qm_kv_heads(const qm_kv* kv, int* kv_lo, int* nkv) {
+    if (!kv) return QM_E_ARG;
+    if (kv_lo) *kv_lo = kv->kv_lo;
+    if (nkv) *nkv = kv->nkv;
     return QM_OK;
 }
 
@@ -601,7 +659,7 @@ extern "C" int qm_kv_destroy(qm_kv* kv) {
 
 extern "C" int qm_kv_snapshot(qm_ctx* c, const qm_kv* src, qm_kv** out) {
     if (!c || !src || !out) return QM_E_ARG;
-    int rc = qm_kv_create(c, src->batch, src->capacity, out);
+    int rc = qm_kv_create_heads(c, src->batch, src->capacity, src->kv_lo, src->nkv, out);
     if (rc) return rc;
     rc = qm_kv_restore(c, *out, src);
     if (rc) {
@@ -613,18 +671,19 @@ extern "C" int qm_kv_snapshot(qm_ctx* c, const qm_kv* src, qm_kv** out) {
 
 extern "C" int qm_kv_restore(qm_ctx* c, qm_kv* dst, const qm_kv* src) {
     if (!c || !dst || !src) return QM_E_ARG;
-    if (dst->batch != src->batch || dst->capacity < src->seq_len)
-        return set_error(c, QM_E_MISMATCH, "kv restore: batch or capacity mismatch");
+    if (dst->batch != src->batch || dst->capacity < src->seq_len || dst->kv_lo != src->kv_lo ||
+        dst->nkv != src->nkv)
+        return set_error(c, QM_E_MISMATCH, "kv restore: batch, capacity or head-range mismatch");
     cudaSetDevice(c->device);
     // Copy the filled prefix of every (sequence, kv-head) row block.
     size_t row = (size_t)kD * 2;
     QM_CHECK_CUDA(c, cudaMemcpy2DAsync(dst->k, (size_t)dst->capacity * row, src->k,
                                        (size_t)src->capacity * row, (size_t)src->seq_len * row,
-                                       (size_t)src->batch * kNumKVH, cudaMemcpyDeviceToDevice,
+                                       (size_t)src->batch * src->nkv, cudaMemcpyDeviceToDevice,
                                        c->stream));
     QM_CHECK_CUDA(c, cudaMemcpy2DAsync(dst->v, (size_t)dst->capacity * row, src->v,
                                        (size_t)src->capacity * row, (size_t)src->seq_len * row,
-                                       (size_t)src->batch * kNumKVH, cudaMemcpyDeviceToDevice,
+                                       (size_t)src->batch * src->nkv, cudaMemcpyDeviceToDevice,
                                        c->stream));
     dst->seq_len = src->seq_len;
     return QM_OK;
@@ -667,7 +726,7 @@ extern "C" int qm_gqa_decode(qm_ctx* c, const qm_gqa_params* p, qm_kv* kv, const
     if (kv->seq_len >= p->max_pos)
         return set_error(c, QM_E_RANGE, "qm_gqa_decode: position beyond the RoPE table");
     cudaSetDevice(c->device);
-    size_t ws = gqa_decode_ws_bytes(kv->batch, kv->seq_len, c->num_sms);
+    size_t ws = gqa_decode_ws_bytes(kv->batch, kv->nkv, kv->seq_len, c->num_sms);
     rc = ensure_workspace(c, ws);
     if (rc) return rc;
     cudaError_t e = launch_gqa_decode(c, p, kv, q_gate, k_new, v_new, out, c->ws, c->ws_bytes);
@@ -681,7 +740,8 @@ extern "C" int qm_gqa_decode_host(qm_ctx* c, const qm_gqa_params* p, qm_kv* kv,
                                   float* out) {
     if (!c || !kv) return QM_E_ARG;
     const size_t B = kv->batch;
-    const size_t n_q = B * kNumH * 2 * kD, n_kv = B * kNumKVH * kD, n_o = B * kNumH * kD;
+    // inputs are full width; out covers the cache's KV heads (4 query heads each)
+    const size_t n_q = B * kNumH * 2 * kD, n_kv = B * kNumKVH * kD, n_o = B * kv->nkv * kGroup * kD;
     cudaSetDevice(c->device);
     int rc = ensure_stage(c, 4 * (n_q + 2 * n_kv + n_o) + 1024);
     if (rc) return rc;

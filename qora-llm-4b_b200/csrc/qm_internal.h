@@ -59,7 +59,9 @@ struct qm_dn_state {
     qm_ctx* ctx = nullptr;
     int device = 0;           // destroy uses this, never ctx (ctx may be gone)
     int batch = 0;
-    float* s = nullptr;       // [B, 32, 128, 128]
+    int vh_lo = 0;            // V heads [vh_lo, vh_lo + nvh) of the model (head shard)
+    int nvh = qm::kNumV;
+    float* s = nullptr;       // [B, nvh, 128, 128]
     float* conv = nullptr;    // [B, 4, 8192] ring, token t in slot t % 4
     int64_t conv_pos = 0;
     bool owned = false;
@@ -70,11 +72,13 @@ struct qm_kv {
     int device = 0;           // destroy uses this, never ctx (ctx may be gone)
     int batch = 0;
     int capacity = 0;
-    uint16_t* k = nullptr;    // [B, 4, cap, 256] bf16
+    int kv_lo = 0;            // KV heads [kv_lo, kv_lo + nkv) of the model (head shard)
+    int nkv = qm::kNumKVH;
+    uint16_t* k = nullptr;    // [B, nkv, cap, 256] bf16
     uint16_t* v = nullptr;
     int64_t seq_len = 0;
     bool owned = false;
-    CUtensorMap tmap_k;       // 3-D view {256, cap, B*4}, box {64, 64, 1}, 128B swizzle
+    CUtensorMap tmap_k;       // 3-D view {256, cap, B*nkv}, box {64, 64, 1}, 128B swizzle
     CUtensorMap tmap_v;
     bool tmaps_ok = false;
 };
@@ -101,7 +105,7 @@ cudaError_t launch_dn_decode(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st
 cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, const float* q_gate,
                               const float* k_new, const float* v_new, float* out, void* ws,
                               size_t ws_bytes);
-size_t gqa_decode_ws_bytes(int batch, int64_t seq_len, int num_sms);
+size_t gqa_decode_ws_bytes(int batch, int nkv, int64_t seq_len, int num_sms);
 cudaError_t launch_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, int T,
                                const uint16_t* q_gate, const uint16_t* k, const uint16_t* v,
                                float* out);

@@ -77,7 +77,7 @@ extern "C" int qm_gqa_decode_noalloc(const qm_gqa_params* p, uint16_t* k_cache, 
     int rc = setup_device(dev, &s);
     if (rc != QM_OK) return rc;
     // Reject what does not fit the fixed scratch (never grow it).
-    if (qm::gqa_decode_ws_bytes(batch, seq_len, s->num_sms) > kWsBytes) return QM_E_SHAPE;
+    if (qm::gqa_decode_ws_bytes(batch, qm::kNumKVH, seq_len, s->num_sms) > kWsBytes) return QM_E_SHAPE;
 
     // Host-side bookkeeping only: these objects own no device memory.
     qm_ctx c;

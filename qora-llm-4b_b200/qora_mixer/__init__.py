@@ -7,6 +7,8 @@ Mirrors the reference's mixer call surface (qora-protocol/QORA-LLM-4B):
   Mixer.gqa_decode  <-> forward_attn_decode attention region (gemv.rs:927-1011)
   Mixer.dn_prefill  <-> prefill_deltanet_layer loop (gemv.rs:1119-1219)
   Mixer.gqa_prefill <-> prefill_attn_layer attention (gemv.rs:1364-1444)
+plus the multi-GPU pieces the reference does not have (shard_plan, Comm:
+head-sharded states/caches and the all-gather of their outputs),
 and raises QmError where the reference panics (layer/cache mismatch).
 
 Everything runs through the C ABI declared in include/qora_mixer.h.  torch is
@@ -43,7 +45,11 @@ EXPORTS = [
     "qm_kv_restore", "qm_kv_seq_len", "qm_kv_set_seq_len", "qm_kv_capacity", "qm_kv_batch",
     "qm_kv_data", "qm_gqa_decode", "qm_gqa_decode_host", "qm_gqa_prefill",
     "qm_gqa_decode_noalloc",
+    "qm_dn_state_create_heads", "qm_dn_state_wrap_heads", "qm_dn_state_heads",
+    "qm_kv_create_heads", "qm_kv_wrap_heads", "qm_kv_heads",
+    "qm_shard_plan", "qm_comm_unique_id", "qm_comm_create", "qm_comm_allgather", "qm_comm_destroy",
 ]
+COMM_ID_BYTES = 128
 
 
 class QmError(RuntimeError):
@@ -67,6 +73,12 @@ class QmDnParams(C.Structure):
 class QmGqaParams(C.Structure):
     _fields_ = [("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("rope_cos", C.c_void_p),
                 ("rope_sin", C.c_void_p), ("max_pos", C.c_int)]
+
+
+class QmShard(C.Structure):
+    _fields_ = [("world", C.c_int), ("rank", C.c_int), ("vh_lo", C.c_int), ("nvh", C.c_int),
+                ("kv_lo", C.c_int), ("nkv", C.c_int), ("seq_part", C.c_int),
+                ("seq_parts", C.c_int)]
 
 
 _lib = None
@@ -126,6 +138,17 @@ def lib():
         "qm_gqa_decode_host": ([P, C.POINTER(QmGqaParams), P, P, P, P, P], I),
         "qm_gqa_prefill": ([P, C.POINTER(QmGqaParams), P, I, P, P, P, P], I),
         "qm_gqa_decode_noalloc": ([C.POINTER(QmGqaParams), P, P, I, I, I64, P, P, P, P, P], I),
+        "qm_dn_state_create_heads": ([P, I, I, I, PP], I),
+        "qm_dn_state_wrap_heads": ([P, I, I, I, P, P, PP], I),
+        "qm_dn_state_heads": ([P, C.POINTER(I), C.POINTER(I)], I),
+        "qm_kv_create_heads": ([P, I, I, I, I, PP], I),
+        "qm_kv_wrap_heads": ([P, I, I, I, I, P, P, PP], I),
+        "qm_kv_heads": ([P, C.POINTER(I), C.POINTER(I)], I),
+        "qm_shard_plan": ([I, I, C.POINTER(QmShard)], I),
+        "qm_comm_unique_id": ([P], I),
+        "qm_comm_create": ([P, P, I, I, I, PP], I),
+        "qm_comm_allgather": ([P, P, P, C.c_size_t], I),
+        "qm_comm_destroy": ([P], I),
     }
     for name, (args, res) in sig.items():
         if hasattr(L, name):
@@ -230,18 +253,24 @@ class Ctx:
 
 
 class DnState:
-    """B DeltaNet recurrent states (DeltaNetState x B), owned or wrapping torch storage."""
+    """B DeltaNet recurrent states (DeltaNetState x B), owned or wrapping torch storage.
 
-    def __init__(self, ctx: Ctx, batch: int, s=None, conv=None):
+    heads=(vh_lo, nvh) makes a head-sharded state holding V heads
+    [vh_lo, vh_lo+nvh) only (decode only; see shard_plan)."""
+
+    def __init__(self, ctx: Ctx, batch: int, s=None, conv=None, heads=None):
         self.ctx = ctx
         self._h = C.c_void_p()
         self._keep = (s, conv)
+        lo, n = heads if heads is not None else (0, 32)
         if s is None:
-            rc = lib().qm_dn_state_create(ctx.handle, batch, C.byref(self._h))
+            rc = lib().qm_dn_state_create_heads(ctx.handle, batch, lo, n, C.byref(self._h))
         else:
-            rc = lib().qm_dn_state_wrap(ctx.handle, batch, _ptr(s), _ptr(conv), C.byref(self._h))
+            rc = lib().qm_dn_state_wrap_heads(ctx.handle, batch, lo, n, _ptr(s), _ptr(conv),
+                                              C.byref(self._h))
         ctx.check(rc, "dn_state create")
         self.batch = batch
+        self.heads = (lo, n)
         ctx.adopt(self)
 
     @property
@@ -261,7 +290,7 @@ class DnState:
 
     def snapshot(self) -> "DnState":
         o = DnState.__new__(DnState)
-        o.ctx, o.batch, o._keep = self.ctx, self.batch, (None, None)
+        o.ctx, o.batch, o.heads, o._keep = self.ctx, self.batch, self.heads, (None, None)
         o._h = C.c_void_p()
         self.ctx.check(lib().qm_dn_state_snapshot(self.ctx.handle, self._h, C.byref(o._h)), "snapshot")
         self.ctx.adopt(o)
@@ -271,10 +300,10 @@ class DnState:
         self.ctx.check(lib().qm_dn_state_restore(self.ctx.handle, self._h, src._h), "restore")
 
     def read(self, b: int):
-        """(S [32,128,128], conv_buf [8192,3]) of sequence b, reference layout."""
+        """(S [nvh,128,128], conv_buf [8192,3]) of sequence b, reference layout."""
         import numpy as np
 
-        s = np.empty((32, 128, 128), np.float32)
+        s = np.empty((self.heads[1], 128, 128), np.float32)
         cb = np.empty((8192, 3), np.float32)
         self.ctx.check(lib().qm_dn_state_read(self.ctx.handle, self._h, b, s.ctypes.data,
                                               cb.ctypes.data), "read")
@@ -301,18 +330,23 @@ class DnState:
 
 
 class KvCache:
-    """B bf16 KV caches [B,4,capacity,256] (KvCacheEntry x B)."""
+    """B bf16 KV caches [B,nkv,capacity,256] (KvCacheEntry x B).
 
-    def __init__(self, ctx: Ctx, batch: int, capacity: int, k=None, v=None):
+    heads=(kv_lo, nkv) makes a head-sharded cache of KV heads
+    [kv_lo, kv_lo+nkv) (decode only; see shard_plan)."""
+
+    def __init__(self, ctx: Ctx, batch: int, capacity: int, k=None, v=None, heads=None):
         self.ctx = ctx
         self._h = C.c_void_p()
         self._keep = (k, v)
+        lo, n = heads if heads is not None else (0, 4)
         if k is None:
-            rc = lib().qm_kv_create(ctx.handle, batch, capacity, C.byref(self._h))
+            rc = lib().qm_kv_create_heads(ctx.handle, batch, capacity, lo, n, C.byref(self._h))
         else:
-            rc = lib().qm_kv_wrap(ctx.handle, batch, capacity, _ptr(k), _ptr(v), C.byref(self._h))
+            rc = lib().qm_kv_wrap_heads(ctx.handle, batch, capacity, lo, n, _ptr(k), _ptr(v),
+                                        C.byref(self._h))
         ctx.check(rc, "kv create")
-        self.batch, self.capacity = batch, capacity
+        self.batch, self.capacity, self.heads = batch, capacity, (lo, n)
         ctx.adopt(self)
 
     @property
@@ -336,7 +370,8 @@ class KvCache:
 
     def snapshot(self) -> "KvCache":
         o = KvCache.__new__(KvCache)
-        o.ctx, o.batch, o.capacity, o._keep = self.ctx, self.batch, self.capacity, (None, None)
+        o.ctx, o.batch, o.capacity, o.heads = self.ctx, self.batch, self.capacity, self.heads
+        o._keep = (None, None)
         o._h = C.c_void_p()
         self.ctx.check(lib().qm_kv_snapshot(self.ctx.handle, self._h, C.byref(o._h)), "kv snapshot")
         self.ctx.adopt(o)
@@ -412,3 +447,52 @@ def gqa_decode_noalloc(p: QmGqaParams, k_cache, v_cache, batch, capacity, seq_le
     return lib().qm_gqa_decode_noalloc(C.byref(p), _ptr(k_cache), _ptr(v_cache), int(batch),
                                        int(capacity), int(seq_len), _ptr(q_gate), _ptr(k_new),
                                        _ptr(v_new), _ptr(out), raw or None)
+
+
+def shard_plan(world: int, rank: int) -> dict:
+    """qm_shard_plan: the head-sharded layout of rank `rank` of `world`."""
+    sh = QmShard()
+    rc = lib().qm_shard_plan(int(world), int(rank), C.byref(sh))
+    if rc:
+        raise QmError(rc, f"qm_shard_plan({world}, {rank})")
+    return {f: getattr(sh, f) for f, _ in QmShard._fields_}
+
+
+def comm_unique_id() -> bytes:
+    buf = (C.c_ubyte * COMM_ID_BYTES)()
+    rc = lib().qm_comm_unique_id(buf)
+    if rc:
+        raise QmError(rc, "qm_comm_unique_id")
+    return bytes(buf)
+
+
+class Comm:
+    """NCCL communicator of the head-sharded layout (qm_comm): all-gathers the
+    per-layer mixer outputs on the context's stream."""
+
+    def __init__(self, ctx: Ctx, uid: bytes, world: int, rank: int, timeout_ms: int = 60000):
+        assert len(uid) == COMM_ID_BYTES
+        self.ctx = ctx
+        self._h = C.c_void_p()
+        buf = (C.c_ubyte * COMM_ID_BYTES).from_buffer_copy(uid)
+        ctx.check(lib().qm_comm_create(ctx.handle, buf, int(world), int(rank), int(timeout_ms),
+                                       C.byref(self._h)), "qm_comm_create")
+        self.world, self.rank = world, rank
+        ctx.adopt(self)
+
+    def allgather(self, send, recv):
+        """recv (world x send.nbytes, contiguous) <- every rank's send, rank order."""
+        nbytes = send.numel() * send.element_size() if hasattr(send, "numel") else send.nbytes
+        self.ctx.check(lib().qm_comm_allgather(self._h, _ptr(send), _ptr(recv), nbytes),
+                       "qm_comm_allgather")
+
+    def close(self):
+        if self._h:
+            lib().qm_comm_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
