@@ -151,29 +151,8 @@ __global__ void dn_conv_ring(const uint16_t* __restrict__ qkv, float* __restrict
 }
 
 // ---------------------------------------------------------------------------
-// chunk kernel
+// chunk kernels
 // ---------------------------------------------------------------------------
-// shared memory map (offsets from a 1024-aligned base)
-constexpr int kOffKQh = 0;                 // [K;Q] hi: 2 boxes of [128 rows x 64] fp16 (16 KB each)
-constexpr int kOffKQl = 32768;             // [K;Q] lo
-constexpr int kOffVh = 65536;              // V hi: 2 boxes [64 x 64] (8 KB) ; later U^T hi [128x64]
-constexpr int kOffVl = 81920;              // V lo                            ; later U^T lo
-constexpr int kOffT1h = 98304;             // T' hi [64x64] 8 KB ; later W^T hi [128 x 64] 16 KB
-constexpr int kOffT1l = 106496;
-constexpr int kOffT2h = 114688;            // T'' hi
-constexpr int kOffT2l = 122880;
-constexpr int kOffPh = 131072;             // P' hi [64x64]
-constexpr int kOffPl = 139264;
-constexpr int kOffS = 147456;              // S0 fp16 [128 v x 128 k]: 2 boxes [128 x 64]
-constexpr int kOffUDh = 180224;            // (U^T diag D) hi [128 x 64]
-constexpr int kOffUDl = 196608;
-constexpr int kOffA = 212992;              // A f32 [64][64]
-constexpr int kOffMisc = 229376;           // G, beta, g: 3 x 64 f32; barriers
-constexpr int kChunkSmem = kOffMisc + 3 * 64 * 4 + 64 + 1024;
-
-// TMEM columns
-constexpr uint32_t kTmKQ = 0, kTmW = 64, kTmU = 128, kTmY1 = 192, kTmY2 = 256, kTmS = 384;
-
 constexpr uint32_t kNegA = 1u << 13;
 constexpr uint32_t kIdKK = umma_idesc_f16kind(128, 64, false, false, false);   // A K, B K
 constexpr uint32_t kIdW = umma_idesc_f16kind(128, 64, true, false, false);     // A MN, B K
@@ -186,36 +165,381 @@ __device__ __forceinline__ uint32_t swz(int row, int col) {  // fp16 [rows x 64]
     return (uint32_t)(row * 128 + ((((col >> 3) ^ (row & 7))) << 4) + (col & 7) * 2);
 }
 
+// 8 consecutive f32 -> fp16 hi (and lo = fp16 of the remainder) as two uint4
+__device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const __half a = __float2half_rn(v[2 * i]), b = __float2half_rn(v[2 * i + 1]);
+        h[i] = pack_bf16(__half_as_ushort(a), __half_as_ushort(b));
+        l[i] = pack_f16x2_rn(v[2 * i] - __half2float(a), v[2 * i + 1] - __half2float(b));
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+__device__ __forceinline__ uint4 round8(const float* v) {
+    return make_uint4(pack_f16x2_rn(v[0], v[1]), pack_f16x2_rn(v[2], v[3]),
+                      pack_f16x2_rn(v[4], v[5]), pack_f16x2_rn(v[6], v[7]));
+}
+
+// inclusive cumulative log-decay G_t of the 64 gates in sg[] (warp 0), plus
+// eG[t] = e^G_t and eD[s] = e^(G_63 - G_s)
+__device__ __forceinline__ void chunk_decays(const float* sg, float* sG, float* eG, float* eD,
+                                             int lane) {
+    float g0 = sg[lane], g1 = sg[lane + 32];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float u0 = __shfl_up_sync(0xffffffffu, g0, o);
+        const float u1 = __shfl_up_sync(0xffffffffu, g1, o);
+        if (lane >= o) {
+            g0 += u0;
+            g1 += u1;
+        }
+    }
+    g1 += __shfl_sync(0xffffffffu, g0, 31);
+    const float g63 = __shfl_sync(0xffffffffu, g1, 31);
+    sG[lane] = g0;
+    sG[lane + 32] = g1;
+    if (eG) {
+        eG[lane] = exp2f(g0 * kLog2e);
+        eG[lane + 32] = exp2f(g1 * kLog2e);
+        eD[lane] = exp2f((g63 - g0) * kLog2e);
+        eD[lane + 32] = exp2f((g63 - g1) * kLog2e);
+    }
+}
+
 struct ChunkBars {
     uint64_t load, mma;
     uint32_t tmem_base;
     int abort_flag;
 };
 
-__global__ void __launch_bounds__(128, 1)
-dn_prefill_chunk(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ CUtensorMap tql,
-                 const __grid_constant__ CUtensorMap tkh, const __grid_constant__ CUtensorMap tkl,
-                 const __grid_constant__ CUtensorMap tvh, const __grid_constant__ CUtensorMap tvl,
-                 const float* __restrict__ gin, const float* __restrict__ bin,
-                 float* __restrict__ S, float* __restrict__ y, int T, int* err) {
+// ---- 2a. chunk-local WY factors: one CTA per (V head, chunk, sequence) ----
+//
+// Everything in a chunk that does not depend on the state entering it:
+//   MMA1  [K;Q] K^T                       (compensated)  -> A (f32) and P'
+//   T = (I + A)^-1 by forward substitution, one column per thread (f32)
+//   MMA2  W^T  = K^T (T diag(b e^G))^T    (compensated)
+//   MMA3  U~^T = V^T (T diag(b))^T        (compensated)
+// written to the workspace for the state pass: W^T fp16 [128 k][64 t],
+// U~^T f32 as [16][128 v][4] (float4 of 4 tokens per v, so the state pass
+// reads it coalesced straight into registers) and P' fp16 hi/lo [64 t][64 s].
+// 100 KB of shared memory and 256 TMEM columns: two CTAs per SM.
+constexpr int kL_KQh = 0;              // [K;Q] hi: 2 boxes [128 rows x 64] fp16 (K rows 0-63,
+constexpr int kL_KQl = 32768;          //   Q rows 64-127); after MMA1 the four Q quarters
+constexpr int kL_T1h = kL_KQh + 8192;  //   hold T' and T'' (hi/lo), 8 KB each
+constexpr int kL_T1l = kL_KQh + 24576;
+constexpr int kL_T2h = kL_KQl + 8192;
+constexpr int kL_T2l = kL_KQl + 24576;
+constexpr int kL_A = 65536;            // A f32 [64][68] during the solve,
+constexpr int kL_Vh = 65536;           //   then V hi (2 boxes [64 x 64])
+constexpr int kL_Vl = 81920;           //   and V lo
+constexpr int kAStride = 68;           // floats per A row (float4-aligned, 4-way store conflicts)
+constexpr int kL_Misc = 98304;         // G, beta, g: 3 x 64 f32; barriers
+constexpr int kLocalSmem = kL_Misc + 3 * 64 * 4 + 64 + 1024;
+static_assert(kL_A + 64 * kAStride * 4 <= kL_Vl + 16384, "A fits the V region");
+constexpr uint32_t kTmKQ = 0, kTmW = 64, kTmU = 128;
+
+__global__ void __launch_bounds__(128, 2)
+dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ CUtensorMap tql,
+               const __grid_constant__ CUtensorMap tkh, const __grid_constant__ CUtensorMap tkl,
+               const __grid_constant__ CUtensorMap tvh, const __grid_constant__ CUtensorMap tvl,
+               const float* __restrict__ gin, const float* __restrict__ bin, int T, int nch,
+               uint16_t* __restrict__ wt_out, float* __restrict__ ut_out,
+               uint16_t* __restrict__ ph_out, uint16_t* __restrict__ pl_out, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    float* sG = reinterpret_cast<float*>(smem + kOffMisc);
+    float* sG = reinterpret_cast<float*>(smem + kL_Misc);
     float* sB = sG + 64;
     float* sg = sB + 64;
     ChunkBars* bars = reinterpret_cast<ChunkBars*>(sg + 64);
-    float* Amat = reinterpret_cast<float*>(smem + kOffA);
+    float* Amat = reinterpret_cast<float*>(smem + kL_A);
+    volatile int* abort_flag = &bars->abort_flag;
+    const uint32_t sb = smem_u32(smem);
+
+    const int vh = blockIdx.x, ci = blockIdx.y, b = blockIdx.z, qk = vh >> 1;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+    const int row = tid;
+    const int t0 = ci * kC, tc = min(kC, T - t0);
+    const size_t plane_qk = (size_t)b * kNumQK + qk, plane_v = (size_t)b * kNumV + vh;
+    const size_t item = ((size_t)b * kNumV + vh) * nch + ci;
+
+    if (tid == 0) {
+        mbar_init(smem_u32(&bars->load), 1);
+        mbar_init(smem_u32(&bars->mma), 1);
+        bars->abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(&bars->tmem_base), 256);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = bars->tmem_base;
+
+    // thread 0's record of the last phase it started on each barrier and not
+    // yet seen complete (drained on the way out of an aborted CTA)
+    bool ld_out = false, mm_out = false;
+    uint32_t ld_par = 0, mm_par = 0;
+    if (tid == 0) {
+        const uint32_t lb = smem_u32(&bars->load);
+        mbar_arrive_expect_tx(lb, 8 * 8192);
+        ld_out = true;
+        for (int hb = 0; hb < 2; hb++) {
+            tma_load_3d(sb + kL_KQh + hb * 16384, &tkh, hb * 64, t0, (int)plane_qk, lb);
+            tma_load_3d(sb + kL_KQl + hb * 16384, &tkl, hb * 64, t0, (int)plane_qk, lb);
+            tma_load_3d(sb + kL_KQh + hb * 16384 + 8192, &tqh, hb * 64, t0, (int)plane_qk, lb);
+            tma_load_3d(sb + kL_KQl + hb * 16384 + 8192, &tql, hb * 64, t0, (int)plane_qk, lb);
+        }
+    }
+    if (tid < kC) {
+        const bool valid = tid < tc;
+        sg[tid] = valid ? gin[plane_v * T + t0 + tid] : 0.f;
+        sB[tid] = valid ? bin[plane_v * T + t0 + tid] : 0.f;
+    }
+    __syncthreads();
+    if (warp == 0) chunk_decays(sg, sG, nullptr, nullptr, lane);
+    bool ok = mbar_wait_bounded(smem_u32(&bars->load), 0, abort_flag, err);
+    if (ok) ld_out = false;
+    ok = __syncthreads_and(ok) != 0;  // also publishes sG
+
+    // ---- MMA1: [K;Q] K^T (compensated) -> TMEM KQ ----
+    if (ok && tid == 0) {
+        tc_fence_after();
+        int n = 0;
+        for (int term = 0; term < 3; term++) {
+            const uint32_t abase = sb + (term == 2 ? kL_KQl : kL_KQh);
+            const uint32_t bbase = sb + (term == 1 ? kL_KQl : kL_KQh);
+            for (int kk = 0; kk < 8; kk++, n++) {
+                const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                umma_bf16_ss(tm + kTmKQ, umma_sdesc(abase + off, 16, 1024),
+                             umma_sdesc(bbase + off, 16, 1024), kIdKK, n > 0);
+            }
+        }
+        umma_commit(smem_u32(&bars->mma));
+        mm_out = true;
+    }
+    if (ok) {
+        ok = mbar_wait_bounded(smem_u32(&bars->mma), 0, abort_flag, err);
+        if (ok) mm_out = false;
+    }
+    ok = __syncthreads_and(ok) != 0;
+    tc_fence_after();
+
+    // ---- rows 0-63: A (f32, shared); rows 64-127: P' hi/lo (global) ----
+    if (ok) {
+        float kq[64];
+        tmem_ld32(tm + lane_addr + kTmKQ, kq);
+        tmem_ld32(tm + lane_addr + kTmKQ + 32, kq + 32);
+        tmem_ld_wait();
+        if (row < kC) {
+            const int t = row;
+            const float Gt = sG[t], bt = sB[t];
+            float* arow = Amat + t * kAStride;
+#pragma unroll
+            for (int s = 0; s < kC; s += 4) {
+                float4 v;
+                v.x = (s + 0 < t) ? bt * exp2f((Gt - sG[s + 0]) * kLog2e) * kq[s + 0] : 0.f;
+                v.y = (s + 1 < t) ? bt * exp2f((Gt - sG[s + 1]) * kLog2e) * kq[s + 1] : 0.f;
+                v.z = (s + 2 < t) ? bt * exp2f((Gt - sG[s + 2]) * kLog2e) * kq[s + 2] : 0.f;
+                v.w = (s + 3 < t) ? bt * exp2f((Gt - sG[s + 3]) * kLog2e) * kq[s + 3] : 0.f;
+                *reinterpret_cast<float4*>(arow + s) = v;
+            }
+        } else {
+            const int t = row - kC;
+            const float Gt = sG[t];
+            uint4* hrow = reinterpret_cast<uint4*>(ph_out + (item * kC + t) * kC);
+            uint4* lrow = reinterpret_cast<uint4*>(pl_out + (item * kC + t) * kC);
+#pragma unroll
+            for (int s = 0; s < kC; s += 8) {
+                float p[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+                    p[i] = (s + i <= t) ? exp2f((Gt - sG[s + i]) * kLog2e) * kq[s + i] : 0.f;
+                uint4 h, l;
+                split8(p, h, l);
+                hrow[s / 8] = h;
+                lrow[s / 8] = l;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- T = (I + A)^-1, column j per thread; T' = T diag(b e^G), T'' = T diag(b) ----
+    if (ok && tid < kC) {
+        const int j = tid;
+        float tcol[kC];
+#pragma unroll
+        for (int t = 0; t < kC; t++) {
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+            const float* arow = Amat + t * kAStride;
+#pragma unroll
+            for (int s = 0; s + 3 < t; s += 4) {
+                const float4 av = *reinterpret_cast<const float4*>(arow + s);
+                a0 = fmaf(av.x, tcol[s], a0);
+                a1 = fmaf(av.y, tcol[s + 1], a1);
+                a2 = fmaf(av.z, tcol[s + 2], a2);
+                a3 = fmaf(av.w, tcol[s + 3], a3);
+            }
+#pragma unroll
+            for (int s = (t / 4) * 4; s < t; s++) a0 = fmaf(arow[s], tcol[s], a0);
+            tcol[t] = (t == j) ? 1.f : -((a0 + a1) + (a2 + a3));
+        }
+        const float bj = sB[j];
+        const float c1 = bj * exp2f(sG[j] * kLog2e), c2 = bj;
+#pragma unroll
+        for (int t = 0; t < kC; t++) {
+            const float v1 = tcol[t] * c1, v2 = tcol[t] * c2;
+            const __half h1 = __float2half_rn(v1), h2 = __float2half_rn(v2);
+            const uint32_t o = swz(t, j);
+            *reinterpret_cast<uint16_t*>(smem + kL_T1h + o) = __half_as_ushort(h1);
+            *reinterpret_cast<uint16_t*>(smem + kL_T1l + o) = f16_bits_rn(v1 - __half2float(h1));
+            *reinterpret_cast<uint16_t*>(smem + kL_T2h + o) = __half_as_ushort(h2);
+            *reinterpret_cast<uint16_t*>(smem + kL_T2l + o) = f16_bits_rn(v2 - __half2float(h2));
+        }
+    }
+    fence_proxy_async_shared();
+    tc_fence_before();
+    __syncthreads();  // A is dead from here: V lands on it
+
+    // ---- MMA2 (W^T) now; V load; MMA3 (U~^T) once V has landed ----
+    if (ok && tid == 0) {
+        const uint32_t lb = smem_u32(&bars->load);
+        mbar_arrive_expect_tx(lb, 4 * 8192);
+        ld_out = true;
+        ld_par = 1;
+        for (int hb = 0; hb < 2; hb++) {
+            tma_load_3d(sb + kL_Vh + hb * 8192, &tvh, hb * 64, t0, (int)plane_v, lb);
+            tma_load_3d(sb + kL_Vl + hb * 8192, &tvl, hb * 64, t0, (int)plane_v, lb);
+        }
+        tc_fence_after();
+        int n = 0;
+        for (int term = 0; term < 3; term++) {
+            const uint32_t ka = sb + (term == 2 ? kL_KQl : kL_KQh);
+            const uint32_t tb = sb + (term == 1 ? kL_T1l : kL_T1h);
+            for (int kk = 0; kk < 4; kk++, n++)
+                umma_bf16_ss(tm + kTmW, umma_sdesc(ka + kk * 2048, 16384, 1024),
+                             umma_sdesc(tb + kk * 32, 16, 1024), kIdW, n > 0);
+        }
+        if (mbar_wait_bounded(lb, 1, abort_flag, err)) {
+            ld_out = false;
+            tc_fence_after();
+            n = 0;
+            for (int term = 0; term < 3; term++) {
+                const uint32_t va = sb + (term == 2 ? kL_Vl : kL_Vh);
+                const uint32_t tb = sb + (term == 1 ? kL_T2l : kL_T2h);
+                for (int kk = 0; kk < 4; kk++, n++)
+                    umma_bf16_ss(tm + kTmU, umma_sdesc(va + kk * 2048, 8192, 1024),
+                                 umma_sdesc(tb + kk * 32, 16, 1024), kIdW, n > 0);
+            }
+        }
+        umma_commit(smem_u32(&bars->mma));  // also covers MMA2 when the V wait gave up
+        mm_out = true;
+        mm_par = 1;
+    }
+    if (ok) {
+        ok = mbar_wait_bounded(smem_u32(&bars->mma), 1, abort_flag, err);
+        if (ok) mm_out = false;
+    }
+    ok = __syncthreads_and(ok && !*abort_flag) != 0;
+    tc_fence_after();
+
+    // ---- outputs: W^T row k (fp16), U~^T row v (f32, [t/4][v][4]) ----
+    if (ok) {
+        float wv[64];
+        tmem_ld32(tm + lane_addr + kTmW, wv);
+        tmem_ld32(tm + lane_addr + kTmW + 32, wv + 32);
+        tmem_ld_wait();
+        uint4* wrow = reinterpret_cast<uint4*>(wt_out + (item * kHd + row) * kC);
+#pragma unroll
+        for (int t = 0; t < kC; t += 8) wrow[t / 8] = round8(wv + t);
+        float uv[64];
+        tmem_ld32(tm + lane_addr + kTmU, uv);
+        tmem_ld32(tm + lane_addr + kTmU + 32, uv + 32);
+        tmem_ld_wait();
+        float4* ub = reinterpret_cast<float4*>(ut_out + item * kHd * kC);
+#pragma unroll
+        for (int t4 = 0; t4 < kC / 4; t4++)
+            ub[t4 * kHd + row] = make_float4(uv[4 * t4], uv[4 * t4 + 1], uv[4 * t4 + 2], uv[4 * t4 + 3]);
+    }
+    if (tid == 0) {
+        if (ld_out) mbar_drain(smem_u32(&bars->load), ld_par);
+        if (mm_out) mbar_drain(smem_u32(&bars->mma), mm_par);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tm, 256);
+    }
+}
+
+// ---- 2b. state pass: one CTA (128 threads, lane = v row) per (V head, sequence) ----
+//
+// Per chunk, with S0 the state entering it (f32 master in TMEM, fp16 copy in
+// shared memory as the A operand):
+//   MMA4  U_acc = -S0 W^T        MMA5  Y1 = S0 Q^T            (fp16 x fp16)
+//   U = U~ + U_acc (f32; U~ prefetched into registers), split into fp16 hi/lo,
+//   and (U diag(e^(G63-G)))^T hi/lo; S_master *= e^G63
+//   MMA6  Y2 = U^T P'^T          MMA7  S_master += (U D)^T K  (compensated)
+//   y_t = e^G_t Y1 + Y2;  S_master -> fp16 copy for the next chunk
+// W^T and Q are double-buffered and fetched a chunk ahead; P' and K are
+// fetched as soon as MMA6/MMA7 of the previous chunk have read them.
+constexpr int kS_S0 = 0;            // S0 fp16 [128 v x 128 k]: 2 boxes [128 x 64]
+constexpr int kS_W = 32768;         // W^T [128 k x 64 t] fp16, x2 (16 KB each)
+constexpr int kS_Q = 65536;         // Q [64 t x 128 k] fp16: 2 boxes [64 x 64], x2 (16 KB each)
+constexpr int kS_Ph = 98304;        // P' hi [64 t x 64 s]
+constexpr int kS_Pl = 106496;
+constexpr int kS_Kh = 114688;       // K hi [64 s x 128 k]: 2 boxes [64 x 64]
+constexpr int kS_Kl = 131072;
+constexpr int kS_Uh = 147456;       // U^T hi [128 v x 64 s]
+constexpr int kS_Ul = 163840;
+constexpr int kS_UDh = 180224;      // (U^T diag D) hi
+constexpr int kS_UDl = 196608;
+constexpr int kS_Misc = 212992;     // G, eG, eD, g: 4 x 64 f32; barriers
+constexpr int kStateSmem = kS_Misc + 4 * 64 * 4 + 128 + 1024;
+constexpr uint32_t kTmU2 = 0, kTmY1 = 64, kTmY2 = 128, kTmS = 256;
+
+struct StateBars {
+    uint64_t wq_full[2], pk_full, m45, m67;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+__global__ void __launch_bounds__(128, 1)
+dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ CUtensorMap tph,
+               const __grid_constant__ CUtensorMap tpl, const __grid_constant__ CUtensorMap tqh,
+               const __grid_constant__ CUtensorMap tkh, const __grid_constant__ CUtensorMap tkl,
+               const float* __restrict__ ut_in, const float* __restrict__ gin,
+               float* __restrict__ S, float* __restrict__ y, int T, int nch, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    float* sG = reinterpret_cast<float*>(smem + kS_Misc);
+    float* eG = sG + 64;
+    float* eD = eG + 64;
+    float* sg = eD + 64;
+    StateBars* bars = reinterpret_cast<StateBars*>(sg + 64);
     volatile int* abort_flag = &bars->abort_flag;
     const uint32_t sb = smem_u32(smem);
 
     const int vh = blockIdx.x, b = blockIdx.y, qk = vh >> 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
-    const int row = tid;  // TMEM lane == thread (warp w owns lanes 32w..32w+31)
+    const int row = tid;  // TMEM lane = v (or k for W) row
+    const int plane_qk = b * kNumQK + qk;
+    const size_t item0 = ((size_t)b * kNumV + vh) * nch;
 
     if (tid == 0) {
-        mbar_init(smem_u32(&bars->load), 1);
-        mbar_init(smem_u32(&bars->mma), 1);
+        mbar_init(smem_u32(&bars->wq_full[0]), 1);
+        mbar_init(smem_u32(&bars->wq_full[1]), 1);
+        mbar_init(smem_u32(&bars->pk_full), 1);
+        mbar_init(smem_u32(&bars->m45), 1);
+        mbar_init(smem_u32(&bars->m67), 1);
         bars->abort_flag = 0;
         fence_barrier_init();
     }
@@ -228,7 +552,38 @@ dn_prefill_chunk(const __grid_constant__ CUtensorMap tqh, const __grid_constant_
     tc_fence_after();
     const uint32_t tm = bars->tmem_base;
 
-    // ---- initial state: global f32 -> TMEM (master) and fp16 operand copy ----
+    // thread 0's record of the last phase it started on each barrier and not
+    // yet seen complete (drained on the way out of an aborted CTA)
+    bool wq_out[2] = {false, false}, pk_out = false, m45_out = false, m67_out = false;
+    uint32_t wq_par[2] = {0, 0}, pk_par = 0, m45_par = 0, m67_par = 0;
+    auto issue_wq = [&](int c) {  // W^T and Q of chunk c into buffer c & 1
+        const int buf = c & 1;
+        const uint32_t fb = smem_u32(&bars->wq_full[buf]);
+        wq_out[buf] = true;
+        wq_par[buf] = (uint32_t)(c >> 1) & 1;
+        mbar_arrive_expect_tx(fb, 16384 + 16384);
+        tma_load_3d(sb + kS_W + buf * 16384, &twt, 0, 0, (int)(item0 + c), fb);
+        for (int hb = 0; hb < 2; hb++)
+            tma_load_3d(sb + kS_Q + buf * 16384 + hb * 8192, &tqh, hb * 64, c * kC, plane_qk, fb);
+    };
+    auto issue_pk = [&](int c) {  // P' and K of chunk c
+        const uint32_t fb = smem_u32(&bars->pk_full);
+        pk_out = true;
+        pk_par = (uint32_t)c & 1;
+        mbar_arrive_expect_tx(fb, 8192 * 2 + 16384 * 2);
+        tma_load_3d(sb + kS_Ph, &tph, 0, 0, (int)(item0 + c), fb);
+        tma_load_3d(sb + kS_Pl, &tpl, 0, 0, (int)(item0 + c), fb);
+        for (int hb = 0; hb < 2; hb++) {
+            tma_load_3d(sb + kS_Kh + hb * 8192, &tkh, hb * 64, c * kC, plane_qk, fb);
+            tma_load_3d(sb + kS_Kl + hb * 8192, &tkl, hb * 64, c * kC, plane_qk, fb);
+        }
+    };
+    if (tid == 0) {
+        issue_wq(0);
+        issue_pk(0);
+    }
+
+    // ---- initial state: global f32 -> TMEM master and fp16 copy ----
     float* Sg = S + ((size_t)b * kNumV + vh) * kHd * kHd;
     {
         const float* srow = Sg + (size_t)row * kHd;
@@ -236,13 +591,16 @@ dn_prefill_chunk(const __grid_constant__ CUtensorMap tqh, const __grid_constant_
         for (int c = 0; c < 4; c++) {
             float v[32];
 #pragma unroll
-            for (int i = 0; i < 32; i++) v[i] = srow[c * 32 + i];
+            for (int i = 0; i < 32; i += 4) {
+                const float4 f = *reinterpret_cast<const float4*>(srow + c * 32 + i);
+                v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+            }
             tmem_st32(tm + lane_addr + kTmS + c * 32, v);
 #pragma unroll
-            for (int i = 0; i < 32; i += 2) {
+            for (int i = 0; i < 32; i += 8) {
                 const int k = c * 32 + i;
-                *reinterpret_cast<uint32_t*>(smem + kOffS + (k >> 6) * 16384 + swz(row, k & 63)) =
-                    pack_bf16(f16_bits_rn(v[i]), f16_bits_rn(v[i + 1]));
+                *reinterpret_cast<uint4*>(smem + kS_S0 + (k >> 6) * 16384 + sw128_off(row, (k & 63) >> 3)) =
+                    round8(v + i);
             }
         }
         tmem_st_wait();
@@ -251,229 +609,77 @@ dn_prefill_chunk(const __grid_constant__ CUtensorMap tqh, const __grid_constant_
     tc_fence_before();
     __syncthreads();
 
-    uint32_t load_phase = 0, mma_phase = 0;
     bool ok = true;
-    // every decision to stop is block-uniform, so no thread skips a barrier
-    auto wait_mma = [&]() {
-        const bool w = mbar_wait_bounded(smem_u32(&bars->mma), mma_phase, abort_flag, err);
-        ok = __syncthreads_and(ok && w) != 0;
-        mma_phase ^= 1;
+    for (int ci = 0; ci < nch && ok; ci++) {
+        const int t0 = ci * kC, tc = min(kC, T - t0);
+        const int buf = ci & 1;
+        if (tid == 0 && ci + 1 < nch) issue_wq(ci + 1);  // its buffer's MMAs (chunk ci-1) are done
+        // U~ of this chunk straight into registers (coalesced float4 per 4 tokens)
+        float ut[64];
+        {
+            const float4* ub = reinterpret_cast<const float4*>(ut_in + (item0 + ci) * kHd * kC);
+#pragma unroll
+            for (int t4 = 0; t4 < kC / 4; t4++) {
+                const float4 f = ub[t4 * kHd + row];
+                ut[4 * t4] = f.x; ut[4 * t4 + 1] = f.y; ut[4 * t4 + 2] = f.z; ut[4 * t4 + 3] = f.w;
+            }
+        }
+        if (tid < kC) sg[tid] = (tid < tc) ? gin[((size_t)b * kNumV + vh) * T + t0 + tid] : 0.f;
+        __syncthreads();
+        if (warp == 0) chunk_decays(sg, sG, eG, eD, lane);
+
+        // ---- MMA4 + MMA5 ----
+        if (tid == 0) {
+            if (mbar_wait_bounded(smem_u32(&bars->wq_full[buf]), (ci >> 1) & 1, abort_flag, err)) {
+                wq_out[buf] = false;
+                tc_fence_after();
+                const uint32_t wb = sb + kS_W + buf * 16384, qb = sb + kS_Q + buf * 16384;
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    umma_bf16_ss(tm + kTmU2, umma_sdesc(sb + kS_S0 + aoff, 16, 1024),
+                                 umma_sdesc(wb + kk * 2048, 8192, 1024), kIdSW, kk > 0);
+                }
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    umma_bf16_ss(tm + kTmY1, umma_sdesc(sb + kS_S0 + aoff, 16, 1024),
+                                 umma_sdesc(qb + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), kIdSQ,
+                                 kk > 0);
+                }
+            }
+            umma_commit(smem_u32(&bars->m45));
+            m45_out = true;
+            m45_par = (uint32_t)ci & 1;
+        }
+        {
+            const bool w = mbar_wait_bounded(smem_u32(&bars->m45), ci & 1, abort_flag, err);
+            if (w) m45_out = false;
+            ok = __syncthreads_and(ok && w && !*abort_flag) != 0;  // also publishes G, eG, eD
+        }
+        if (!ok) break;
         tc_fence_after();
-    };
-    auto commit_mma = [&]() {
-        if (tid == 0) umma_commit(smem_u32(&bars->mma));
-    };
-    const size_t plane_qk = (size_t)b * kNumQK + qk, plane_v = (size_t)b * kNumV + vh;
-    const int nchunks = (T + kC - 1) / kC;
 
-    for (int ci = 0; ci < nchunks && ok; ci++) {
-        const int t0 = ci * kC;
-        const int tc = min(kC, T - t0);
-        // ---- loads: K/Q/V hi+lo tiles via TMA, gates by threads ----
-        if (tid == 0) {
-            const uint32_t lb = smem_u32(&bars->load);
-            mbar_arrive_expect_tx(lb, 12 * 8192);
-            for (int hb = 0; hb < 2; hb++) {  // k halves
-                tma_load_3d(sb + kOffKQh + hb * 16384, &tkh, hb * 64, t0, (int)plane_qk, lb);
-                tma_load_3d(sb + kOffKQl + hb * 16384, &tkl, hb * 64, t0, (int)plane_qk, lb);
-                tma_load_3d(sb + kOffKQh + hb * 16384 + 8192, &tqh, hb * 64, t0, (int)plane_qk, lb);
-                tma_load_3d(sb + kOffKQl + hb * 16384 + 8192, &tql, hb * 64, t0, (int)plane_qk, lb);
-                tma_load_3d(sb + kOffVh + hb * 8192, &tvh, hb * 64, t0, (int)plane_v, lb);
-                tma_load_3d(sb + kOffVl + hb * 8192, &tvl, hb * 64, t0, (int)plane_v, lb);
-            }
-        }
-        if (tid < kC) {
-            const bool valid = tid < tc;
-            sg[tid] = valid ? gin[plane_v * T + t0 + tid] : 0.f;
-            sB[tid] = valid ? bin[plane_v * T + t0 + tid] : 0.f;
-        }
-        __syncthreads();
-        if (warp == 0) {  // inclusive cumulative log-decay G_t
-            float g0 = sg[lane], g1 = sg[lane + 32];
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const float u0 = __shfl_up_sync(0xffffffffu, g0, o);
-                const float u1 = __shfl_up_sync(0xffffffffu, g1, o);
-                if (lane >= o) {
-                    g0 += u0;
-                    g1 += u1;
-                }
-            }
-            const float tot0 = __shfl_sync(0xffffffffu, g0, 31);
-            sG[lane] = g0;
-            sG[lane + 32] = g1 + tot0;
-        }
+        // ---- U = U~ + U_acc -> hi/lo; U D -> hi/lo; S_master *= e^G63 ----
         {
-            const bool w = mbar_wait_bounded(smem_u32(&bars->load), load_phase, abort_flag, err);
-            ok = __syncthreads_and(ok && w) != 0;
-        }
-        load_phase ^= 1;
-        if (!ok) break;
-
-        // ---- MMA1: [K;Q] K^T  (compensated) -> TMEM KQ ----
-        if (tid == 0) {
-            tc_fence_after();
-            int n = 0;
-            for (int term = 0; term < 3; term++) {
-                const uint32_t abase = sb + (term == 2 ? kOffKQl : kOffKQh);
-                const uint32_t bbase = sb + (term == 1 ? kOffKQl : kOffKQh);
-                for (int kk = 0; kk < 8; kk++, n++) {
-                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16_ss(tm + kTmKQ, umma_sdesc(abase + off, 16, 1024),
-                                 umma_sdesc(bbase + off, 16, 1024), kIdKK, n > 0);
-                }
-            }
-        }
-        commit_mma();
-        wait_mma();
-        if (!ok) break;
-
-        // ---- A matrix (rows 0..63) and P' (rows 64..127) from TMEM ----
-        {
-            float kq[64];
-            tmem_ld32(tm + lane_addr + kTmKQ, kq);
-            tmem_ld32(tm + lane_addr + kTmKQ + 32, kq + 32);
-            tmem_ld_wait();
-            if (row < kC) {
-                const int t = row;
-                const float Gt = sG[t], bt = sB[t];
-#pragma unroll
-                for (int s = 0; s < kC; s++)
-                    Amat[t * kC + s] = (s < t) ? bt * exp2f((Gt - sG[s]) * kLog2e) * kq[s] : 0.f;
-            } else {
-                const int t = row - kC;
-                const float Gt = sG[t];
-#pragma unroll
-                for (int s = 0; s < kC; s += 2) {
-                    const float p0 = (s <= t) ? exp2f((Gt - sG[s]) * kLog2e) * kq[s] : 0.f;
-                    const float p1 = (s + 1 <= t) ? exp2f((Gt - sG[s + 1]) * kLog2e) * kq[s + 1] : 0.f;
-                    const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
-                    *reinterpret_cast<uint32_t*>(smem + kOffPh + swz(t, s)) =
-                        pack_bf16(__half_as_ushort(h0), __half_as_ushort(h1));
-                    *reinterpret_cast<uint32_t*>(smem + kOffPl + swz(t, s)) =
-                        pack_bf16(f16_bits_rn(p0 - __half2float(h0)), f16_bits_rn(p1 - __half2float(h1)));
-                }
-            }
-        }
-        tc_fence_before();
-        __syncthreads();
-
-        // ---- T = (I + A)^-1, one column per thread (f32); T' = T diag(b e^G), T'' = T diag(b) ----
-        if (tid < kC) {
-            const int j = tid;
-            float tcol[kC];
-#pragma unroll
-            for (int t = 0; t < kC; t++) {
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-                const float* arow = Amat + t * kC;
-#pragma unroll
-                for (int s = 0; s + 3 < t; s += 4) {
-                    const float4 av = *reinterpret_cast<const float4*>(arow + s);
-                    a0 = fmaf(av.x, tcol[s], a0);
-                    a1 = fmaf(av.y, tcol[s + 1], a1);
-                    a2 = fmaf(av.z, tcol[s + 2], a2);
-                    a3 = fmaf(av.w, tcol[s + 3], a3);
-                }
-#pragma unroll
-                for (int s = (t / 4) * 4; s < t; s++) a0 = fmaf(arow[s], tcol[s], a0);
-                tcol[t] = (t == j) ? 1.f : -((a0 + a1) + (a2 + a3));
-            }
-            const float bj = sB[j];
-            const float c1 = bj * exp2f(sG[j] * kLog2e), c2 = bj;
-#pragma unroll
-            for (int t = 0; t < kC; t++) {
-                const float v1 = tcol[t] * c1, v2 = tcol[t] * c2;
-                const __half h1 = __float2half_rn(v1), h2 = __float2half_rn(v2);
-                const uint32_t o = swz(t, j);
-                *reinterpret_cast<uint16_t*>(smem + kOffT1h + o) = __half_as_ushort(h1);
-                *reinterpret_cast<uint16_t*>(smem + kOffT1l + o) = f16_bits_rn(v1 - __half2float(h1));
-                *reinterpret_cast<uint16_t*>(smem + kOffT2h + o) = __half_as_ushort(h2);
-                *reinterpret_cast<uint16_t*>(smem + kOffT2l + o) = f16_bits_rn(v2 - __half2float(h2));
-            }
-        }
-        fence_proxy_async_shared();
-        tc_fence_before();
-        __syncthreads();
-
-        // ---- MMA2: W^T = K^T T'^T ; MMA3: U~^T = V^T T''^T (compensated) ; MMA5: Y1 = S0 Q^T ----
-        if (tid == 0) {
-            tc_fence_after();
-            int n = 0;
-            for (int term = 0; term < 3; term++) {
-                const uint32_t ka = sb + (term == 2 ? kOffKQl : kOffKQh);
-                const uint32_t tb = sb + (term == 1 ? kOffT1l : kOffT1h);
-                for (int kk = 0; kk < 4; kk++, n++)
-                    umma_bf16_ss(tm + kTmW, umma_sdesc(ka + kk * 2048, 16384, 1024),
-                                 umma_sdesc(tb + kk * 32, 16, 1024), kIdW, n > 0);
-            }
-            n = 0;
-            for (int term = 0; term < 3; term++) {
-                const uint32_t va = sb + (term == 2 ? kOffVl : kOffVh);
-                const uint32_t tb = sb + (term == 1 ? kOffT2l : kOffT2h);
-                for (int kk = 0; kk < 4; kk++, n++)
-                    umma_bf16_ss(tm + kTmU, umma_sdesc(va + kk * 2048, 8192, 1024),
-                                 umma_sdesc(tb + kk * 32, 16, 1024), kIdW, n > 0);
-            }
-            for (int kk = 0; kk < 8; kk++) {
-                const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                umma_bf16_ss(tm + kTmY1, umma_sdesc(sb + kOffS + off, 16, 1024),
-                             umma_sdesc(sb + kOffKQh + 8192 + off, 16, 1024), kIdSQ, kk > 0);
-            }
-        }
-        commit_mma();
-        wait_mma();
-        if (!ok) break;
-
-        // ---- W^T (TMEM, lane k) -> fp16 [k][t] for the state product ----
-        {
-            float wv[64];
-            tmem_ld32(tm + lane_addr + kTmW, wv);
-            tmem_ld32(tm + lane_addr + kTmW + 32, wv + 32);
+            float acc[64];
+            tmem_ld32(tm + lane_addr + kTmU2, acc);
+            tmem_ld32(tm + lane_addr + kTmU2 + 32, acc + 32);
             tmem_ld_wait();
 #pragma unroll
-            for (int t = 0; t < kC; t += 2)
-                *reinterpret_cast<uint32_t*>(smem + kOffT1h + swz(row, t)) =
-                    pack_bf16(f16_bits_rn(wv[t]), f16_bits_rn(wv[t + 1]));
-        }
-        fence_proxy_async_shared();
-        tc_fence_before();
-        __syncthreads();
-
-        // ---- MMA4: U^T -= S0 W^T ----
-        if (tid == 0) {
-            tc_fence_after();
-            for (int kk = 0; kk < 8; kk++) {
-                const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                umma_bf16_ss(tm + kTmU, umma_sdesc(sb + kOffS + off, 16, 1024),
-                             umma_sdesc(sb + kOffT1h + kk * 2048, 8192, 1024), kIdSW, 1u);
-            }
-        }
-        commit_mma();
-        wait_mma();
-        if (!ok) break;
-
-        // ---- U^T (lane v) -> hi/lo fp16 [v][s]; U^T diag(D) -> hi/lo; S *= e^G63 ----
-        {
-            const float G63 = sG[kC - 1];
-            float uv[64];
-            tmem_ld32(tm + lane_addr + kTmU, uv);
-            tmem_ld32(tm + lane_addr + kTmU + 32, uv + 32);
-            tmem_ld_wait();
+            for (int s = 0; s < kC; s++) acc[s] += ut[s];
 #pragma unroll
-            for (int s = 0; s < kC; s += 2) {
-                const uint32_t o = swz(row, s);
-                const __half h0 = __float2half_rn(uv[s]), h1 = __float2half_rn(uv[s + 1]);
-                *reinterpret_cast<uint32_t*>(smem + kOffVh + o) = pack_bf16(__half_as_ushort(h0), __half_as_ushort(h1));
-                *reinterpret_cast<uint32_t*>(smem + kOffVl + o) =
-                    pack_bf16(f16_bits_rn(uv[s] - __half2float(h0)), f16_bits_rn(uv[s + 1] - __half2float(h1)));
-                const float d0 = uv[s] * exp2f((G63 - sG[s]) * kLog2e);
-                const float d1 = uv[s + 1] * exp2f((G63 - sG[s + 1]) * kLog2e);
-                const __half e0 = __float2half_rn(d0), e1 = __float2half_rn(d1);
-                *reinterpret_cast<uint32_t*>(smem + kOffUDh + o) = pack_bf16(__half_as_ushort(e0), __half_as_ushort(e1));
-                *reinterpret_cast<uint32_t*>(smem + kOffUDl + o) =
-                    pack_bf16(f16_bits_rn(d0 - __half2float(e0)), f16_bits_rn(d1 - __half2float(e1)));
+            for (int s = 0; s < kC; s += 8) {
+                uint4 h, l;
+                split8(acc + s, h, l);
+                *reinterpret_cast<uint4*>(smem + kS_Uh + sw128_off(row, s >> 3)) = h;
+                *reinterpret_cast<uint4*>(smem + kS_Ul + sw128_off(row, s >> 3)) = l;
+                float d[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) d[i] = acc[s + i] * eD[s + i];
+                split8(d, h, l);
+                *reinterpret_cast<uint4*>(smem + kS_UDh + sw128_off(row, s >> 3)) = h;
+                *reinterpret_cast<uint4*>(smem + kS_UDl + sw128_off(row, s >> 3)) = l;
             }
-            const float decay = exp2f(G63 * kLog2e);
+            const float decay = eG[kC - 1];
 #pragma unroll 1
             for (int c = 0; c < 4; c++) {
                 float sv[32];
@@ -489,30 +695,41 @@ dn_prefill_chunk(const __grid_constant__ CUtensorMap tqh, const __grid_constant_
         tc_fence_before();
         __syncthreads();
 
-        // ---- MMA6: Y2 = U^T P'^T ; MMA7: S += (U^T D) K  (compensated) ----
+        // ---- MMA6 + MMA7 (compensated) ----
         if (tid == 0) {
-            tc_fence_after();
-            int n = 0;
-            for (int term = 0; term < 3; term++) {
-                const uint32_t ua = sb + (term == 2 ? kOffVl : kOffVh);
-                const uint32_t pb = sb + (term == 1 ? kOffPl : kOffPh);
-                for (int kk = 0; kk < 4; kk++, n++)
-                    umma_bf16_ss(tm + kTmY2, umma_sdesc(ua + kk * 32, 16, 1024),
-                                 umma_sdesc(pb + kk * 32, 16, 1024), kIdUP, n > 0);
+            if (mbar_wait_bounded(smem_u32(&bars->pk_full), ci & 1, abort_flag, err)) {
+                pk_out = false;
+                tc_fence_after();
+                int n = 0;
+                for (int term = 0; term < 3; term++) {
+                    const uint32_t ua = sb + (term == 2 ? kS_Ul : kS_Uh);
+                    const uint32_t pb = sb + (term == 1 ? kS_Pl : kS_Ph);
+                    for (int kk = 0; kk < 4; kk++, n++)
+                        umma_bf16_ss(tm + kTmY2, umma_sdesc(ua + kk * 32, 16, 1024),
+                                     umma_sdesc(pb + kk * 32, 16, 1024), kIdUP, n > 0);
+                }
+                for (int term = 0; term < 3; term++) {
+                    const uint32_t ua = sb + (term == 2 ? kS_UDl : kS_UDh);
+                    const uint32_t kb = sb + (term == 1 ? kS_Kl : kS_Kh);
+                    for (int kk = 0; kk < 4; kk++)
+                        umma_bf16_ss(tm + kTmS, umma_sdesc(ua + kk * 32, 16, 1024),
+                                     umma_sdesc(kb + kk * 2048, 8192, 1024), kIdUK, 1u);
+                }
             }
-            for (int term = 0; term < 3; term++) {
-                const uint32_t ua = sb + (term == 2 ? kOffUDl : kOffUDh);
-                const uint32_t kb = sb + (term == 1 ? kOffKQl : kOffKQh);
-                for (int kk = 0; kk < 4; kk++)
-                    umma_bf16_ss(tm + kTmS, umma_sdesc(ua + kk * 32, 16, 1024),
-                                 umma_sdesc(kb + kk * 2048, 16384, 1024), kIdUK, 1u);
-            }
+            umma_commit(smem_u32(&bars->m67));
+            m67_out = true;
+            m67_par = (uint32_t)ci & 1;
         }
-        commit_mma();
-        wait_mma();
+        {
+            const bool w = mbar_wait_bounded(smem_u32(&bars->m67), ci & 1, abort_flag, err);
+            if (w) m67_out = false;
+            ok = __syncthreads_and(ok && w && !*abort_flag) != 0;
+        }
         if (!ok) break;
+        tc_fence_after();
+        if (tid == 0 && ci + 1 < nch) issue_pk(ci + 1);  // P' and K buffers are free again
 
-        // ---- outputs y_t = e^G_t Y1 + Y2 (lane v); new S -> fp16 operand copy ----
+        // ---- y_t = e^G_t Y1 + Y2 (lane v); S_master -> fp16 copy ----
         {
             float y1[64], y2[64];
             tmem_ld32(tm + lane_addr + kTmY1, y1);
@@ -523,17 +740,17 @@ dn_prefill_chunk(const __grid_constant__ CUtensorMap tqh, const __grid_constant_
             float* yb = y + ((size_t)b * T + t0) * kVDim + (size_t)vh * kHd + row;
 #pragma unroll
             for (int t = 0; t < kC; t++)
-                if (t < tc) yb[(size_t)t * kVDim] = exp2f(sG[t] * kLog2e) * y1[t] + y2[t];
+                if (t < tc) yb[(size_t)t * kVDim] = eG[t] * y1[t] + y2[t];
 #pragma unroll 1
             for (int c = 0; c < 4; c++) {
                 float sv[32];
                 tmem_ld32(tm + lane_addr + kTmS + c * 32, sv);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
+                for (int i = 0; i < 32; i += 8) {
                     const int k = c * 32 + i;
-                    *reinterpret_cast<uint32_t*>(smem + kOffS + (k >> 6) * 16384 + swz(row, k & 63)) =
-                        pack_bf16(f16_bits_rn(sv[i]), f16_bits_rn(sv[i + 1]));
+                    *reinterpret_cast<uint4*>(smem + kS_S0 + (k >> 6) * 16384 + sw128_off(row, (k & 63) >> 3)) =
+                        round8(sv + i);
                 }
             }
         }
@@ -554,6 +771,14 @@ dn_prefill_chunk(const __grid_constant__ CUtensorMap tqh, const __grid_constant_
             for (int i = 0; i < 32; i += 4)
                 *reinterpret_cast<float4*>(srow + c * 32 + i) = make_float4(sv[i], sv[i + 1], sv[i + 2], sv[i + 3]);
         }
+    }
+    // do not leave while copies or MMAs this CTA issued may still land
+    if (tid == 0) {
+        for (int i = 0; i < 2; i++)
+            if (wq_out[i]) mbar_drain(smem_u32(&bars->wq_full[i]), wq_par[i]);
+        if (pk_out) mbar_drain(smem_u32(&bars->pk_full), pk_par);
+        if (m45_out) mbar_drain(smem_u32(&bars->m45), m45_par);
+        if (m67_out) mbar_drain(smem_u32(&bars->m67), m67_par);
     }
     tc_fence_before();
     __syncthreads();
@@ -587,25 +812,57 @@ __global__ void dn_prefill_gate(const float* __restrict__ y, const float* __rest
 
 }  // namespace
 
-size_t dn_prefill_ws_bytes(int batch, int T) {
-    // fp16 hi+lo planes: q,k (16 heads each) and v (32 heads); f32 g, beta
-    return (size_t)batch * T * (2 * kNumQK + kNumV) * kHd * 2 * 2 + (size_t)batch * kNumV * T * 8 + 1024;
+// Workspace: fp16 hi+lo planes of q, k (16 heads each) and v (32 heads); f32
+// g and beta [B*32][T]; per (sequence, V head, chunk) item the chunk-local
+// factors W^T fp16 [128][64], U~^T f32 [64][128] and P' fp16 hi/lo [64][64].
+struct DnWs {
+    size_t qh, ql, kh, kl, vh, vl, g, be, wt, ut, ph, pl, total;
+};
+
+static DnWs dn_ws_layout(int B, int T) {
+    auto al = [](size_t x) { return (x + 1023) & ~size_t(1023); };
+    const size_t nq = (size_t)B * kNumQK * T * kHd * 2, nv = (size_t)B * kNumV * T * kHd * 2;
+    const size_t items = (size_t)B * kNumV * ((T + kC - 1) / kC);
+    DnWs w;
+    size_t o = 0;
+    w.qh = o; o = al(o + nq);
+    w.ql = o; o = al(o + nq);
+    w.kh = o; o = al(o + nq);
+    w.kl = o; o = al(o + nq);
+    w.vh = o; o = al(o + nv);
+    w.vl = o; o = al(o + nv);
+    w.g = o;  o = al(o + (size_t)B * kNumV * T * 4);
+    w.be = o; o = al(o + (size_t)B * kNumV * T * 4);
+    w.wt = o; o = al(o + items * kHd * kC * 2);
+    w.ut = o; o = al(o + items * kHd * kC * 4);
+    w.ph = o; o = al(o + items * kC * kC * 2);
+    w.pl = o; o = al(o + items * kC * kC * 2);
+    w.total = o;
+    return w;
 }
+
+size_t dn_prefill_ws_bytes(int batch, int T) { return dn_ws_layout(batch, T).total; }
 
 cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, int T,
                               const uint16_t* qkv, const float* a, const float* bgate, float* y,
                               const float* z, float* out) {
     const int B = st->batch;
+    const int nch = (T + kC - 1) / kC;
     cudaStream_t s = ctx->stream;
-    const size_t nq = (size_t)B * kNumQK * T * kHd, nv = (size_t)B * kNumV * T * kHd;
-    uint16_t* qh = static_cast<uint16_t*>(ctx->ws);
-    uint16_t* ql = qh + nq;
-    uint16_t* kh = ql + nq;
-    uint16_t* kl = kh + nq;
-    uint16_t* vh = kl + nq;
-    uint16_t* vl = vh + nv;
-    float* g = reinterpret_cast<float*>(vl + nv);
-    float* be = g + (size_t)B * kNumV * T;
+    const DnWs w = dn_ws_layout(B, T);
+    char* base = static_cast<char*>(ctx->ws);
+    uint16_t* qh = reinterpret_cast<uint16_t*>(base + w.qh);
+    uint16_t* ql = reinterpret_cast<uint16_t*>(base + w.ql);
+    uint16_t* kh = reinterpret_cast<uint16_t*>(base + w.kh);
+    uint16_t* kl = reinterpret_cast<uint16_t*>(base + w.kl);
+    uint16_t* vh = reinterpret_cast<uint16_t*>(base + w.vh);
+    uint16_t* vl = reinterpret_cast<uint16_t*>(base + w.vl);
+    float* g = reinterpret_cast<float*>(base + w.g);
+    float* be = reinterpret_cast<float*>(base + w.be);
+    uint16_t* wt = reinterpret_cast<uint16_t*>(base + w.wt);
+    float* ut = reinterpret_cast<float*>(base + w.ut);
+    uint16_t* ph = reinterpret_cast<uint16_t*>(base + w.ph);
+    uint16_t* pl = reinterpret_cast<uint16_t*>(base + w.pl);
     {
         TimedLaunch tl(ctx, "dn_prefill_prep");
         dim3 grid((T + kPrepTok - 1) / kPrepTok, 2 * kNumQK + kNumV, B);
@@ -626,24 +883,39 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
         if (encode_rows_tmap(&m[i], planes[i], kHd, (uint64_t)T, np, 64, 64, true) != QM_OK)
             return cudaErrorInvalidValue;
     }
+    const uint64_t items = (uint64_t)B * kNumV * nch;
+    CUtensorMap mwt, mph, mpl;
+    if (encode_rows_tmap(&mwt, wt, kC, kHd, items, 64, kHd, true) != QM_OK ||
+        encode_rows_tmap(&mph, ph, kC, kC, items, 64, kC, true) != QM_OK ||
+        encode_rows_tmap(&mpl, pl, kC, kC, items, 64, kC, true) != QM_OK)
+        return cudaErrorInvalidValue;
     static bool attr_set[64] = {};
     if (ctx->device < 64 && !attr_set[ctx->device]) {
-        e = cudaFuncSetAttribute(dn_prefill_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize, kChunkSmem);
+        e = cudaFuncSetAttribute(dn_chunk_local, cudaFuncAttributeMaxDynamicSharedMemorySize, kLocalSmem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(dn_chunk_state, cudaFuncAttributeMaxDynamicSharedMemorySize, kStateSmem);
         if (e != cudaSuccess) return e;
         attr_set[ctx->device] = true;
     }
-    float* yy = y;  // the gate reads the raw y
     {
-        TimedLaunch tl(ctx, "dn_prefill_chunk");
-        dn_prefill_chunk<<<dim3(kNumV, B), 128, kChunkSmem, s>>>(m[0], m[1], m[2], m[3], m[4], m[5], g,
-                                                                  be, st->s, yy, T, ctx->d_err);
+        TimedLaunch tl(ctx, "dn_chunk_local");
+        dn_chunk_local<<<dim3(kNumV, nch, B), 128, kLocalSmem, s>>>(
+            m[0], m[1], m[2], m[3], m[4], m[5], g, be, T, nch, wt, ut, ph, pl, ctx->d_err);
+    }
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    ctx->launches += 1;
+    {
+        TimedLaunch tl(ctx, "dn_chunk_state");
+        dn_chunk_state<<<dim3(kNumV, B), 128, kStateSmem, s>>>(mwt, mph, mpl, m[0], m[2], m[3], ut, g,
+                                                               st->s, y, T, nch, ctx->d_err);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     ctx->launches += 1;
     if (z) {
         const size_t nh = (size_t)B * T * kNumV;
-        dn_prefill_gate<<<(unsigned)((nh + 7) / 8), 256, 0, s>>>(yy, z, p->norm_gamma, out, nh);
+        dn_prefill_gate<<<(unsigned)((nh + 7) / 8), 256, 0, s>>>(y, z, p->norm_gamma, out, nh);
         e = cudaGetLastError();
         if (e == cudaSuccess) ctx->launches += 1;
     }

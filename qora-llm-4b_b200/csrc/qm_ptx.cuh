@@ -70,6 +70,16 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     }
 }
 
+// On the way out of an aborted CTA: wait (with the same limit, ignoring the
+// abort flag) for a phase whose copies or MMAs this CTA issued, so nothing
+// lands in shared memory or TMEM after the CTA has released them.
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > kWaitCycles) return;
+    }
+}
+
 // 3-D tiled TMA load into shared memory, completion on `bar` (tx bytes).
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
                                             int c2, uint32_t bar) {
