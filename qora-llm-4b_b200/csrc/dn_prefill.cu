@@ -47,96 +47,115 @@ constexpr int kC = 64;  // chunk length (tokens)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // ---------------------------------------------------------------------------
-// prep: one CTA per (8-token tile, head-vector, sequence); 128 threads = channels
+// prep: one warp per (head-vector, run of 16 tokens, sequence); lane l owns
+// the 4 channels 4l..4l+3 of the 128-channel head-vector (8-byte bf16 loads,
+// the conv history of those channels kept in registers along the run).
 // head-vectors 0..15 = q heads, 16..31 = k heads, 32..63 = v heads
 // ---------------------------------------------------------------------------
-constexpr int kPrepTok = 8;
+constexpr int kPrepRun = 16;
+constexpr int kPrepWarps = 4;  // warps per CTA
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
-__global__ void __launch_bounds__(128)
+__device__ __forceinline__ float4 bf16x4_to_f32(uint2 u) {
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+}
+
+__global__ void __launch_bounds__(32 * kPrepWarps)
 dn_prefill_prep(const uint16_t* __restrict__ qkv, const float* __restrict__ a_in,
                 const float* __restrict__ b_in, const float* __restrict__ conv_w,
                 const float* __restrict__ a_log, const float* __restrict__ dt_bias,
-                const float* __restrict__ ring, int64_t conv_pos, int T,
+                const float* __restrict__ ring, int64_t conv_pos, int T, int nruns,
                 uint16_t* __restrict__ qh, uint16_t* __restrict__ ql, uint16_t* __restrict__ kh,
                 uint16_t* __restrict__ kl, uint16_t* __restrict__ vh, uint16_t* __restrict__ vl,
-                float* __restrict__ gout, float* __restrict__ bout) {
-    const int tile = blockIdx.x, hv = blockIdx.y, b = blockIdx.z;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int ch = hv * kHd + tid;  // channel within the 8192 mixed qkv
-    const float4 w = reinterpret_cast<const float4*>(conv_w)[ch];
+                float* __restrict__ gout, float* __restrict__ bout, int B) {
+    const int lane = threadIdx.x & 31;
+    const size_t gw = (size_t)blockIdx.x * kPrepWarps + (threadIdx.x >> 5);
+    const int hv = (int)(gw % 64);  // adjacent warps read adjacent 256-byte slices of a token row
+    const size_t rest = gw / 64;
+    const int run = (int)(rest % nruns);
+    const int b = (int)(rest / nruns);
+    if (b >= B) return;
+    const int t0 = run * kPrepRun;
+    const int ch = hv * kHd + lane * 4;  // first of this lane's 4 channels
+    float4 w[4];                          // w[c] = taps of channel ch + c
+#pragma unroll
+    for (int c = 0; c < 4; c++) w[c] = reinterpret_cast<const float4*>(conv_w)[ch + c];
     const uint16_t* xb = qkv + (size_t)b * T * kQKVDim + ch;
     const float* rb = ring + (size_t)b * kConvSlots * kQKVDim + ch;
-    const int t0 = tile * kPrepTok;
-    auto xval = [&](int t) -> float {  // raw input of token t (negative: history ring)
-        if (t >= 0) return bf16_bits_to_f32(xb[(size_t)t * kQKVDim]);
+    auto xval = [&](int t) -> float4 {  // raw inputs of token t (negative: the history ring)
+        if (t >= 0) return bf16x4_to_f32(*reinterpret_cast<const uint2*>(xb + (size_t)t * kQKVDim));
         const int64_t tok = conv_pos + t;
-        if (tok < 0) return 0.f;
-        return rb[(size_t)(tok & 3) * kQKVDim];
+        if (tok < 0) return make_float4(0.f, 0.f, 0.f, 0.f);
+        return *reinterpret_cast<const float4*>(rb + (size_t)(tok & 3) * kQKVDim);
     };
-    float x3 = xval(t0 - 3), x2 = xval(t0 - 2), x1 = xval(t0 - 1);
-    __shared__ float s_red[kPrepTok][4];
-    float act[kPrepTok];
-#pragma unroll
-    for (int i = 0; i < kPrepTok; i++) {
-        const int t = t0 + i;
-        const float x0 = (t < T) ? xval(t) : 0.f;
-        float cv = x3 * w.x;  // gemv.rs:1134-1139: history oldest first, then x
-        cv += x2 * w.y;
-        cv += x1 * w.z;
-        cv += x0 * w.w;
-        act[i] = silu_f(cv);
-        x3 = x2;
-        x2 = x1;
-        x1 = x0;
-    }
-    const bool is_qk = hv < 2 * kNumQK;
-    if (is_qk) {
-#pragma unroll
-        for (int i = 0; i < kPrepTok; i++) {
-            float ss = act[i] * act[i];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-            if (lane == 0) s_red[i][warp] = ss;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int i = 0; i < kPrepTok; i++) {
-            const float n = sqrtf(s_red[i][0] + s_red[i][1] + s_red[i][2] + s_red[i][3]);
-            if (n > 1e-12f) act[i] *= 1.0f / n;  // l2_normalize, gemv.rs:1153-1154
-            if (hv < kNumQK) act[i] *= 0.08838834764831845f;  // q * 1/sqrt(128)
-        }
-    }
+    float4 x3 = xval(t0 - 3), x2 = xval(t0 - 2), x1 = xval(t0 - 1);
+    const bool is_q = hv < kNumQK, is_qk = hv < 2 * kNumQK;
     uint16_t *ph, *pl;
     size_t plane;
-    if (hv < kNumQK) {
+    if (is_q) {
         ph = qh; pl = ql; plane = (size_t)b * kNumQK + hv;
-    } else if (hv < 2 * kNumQK) {
+    } else if (is_qk) {
         ph = kh; pl = kl; plane = (size_t)b * kNumQK + (hv - kNumQK);
     } else {
         ph = vh; pl = vl; plane = (size_t)b * kNumV + (hv - 2 * kNumQK);
     }
+    const int tend = min(kPrepRun, T - t0);
+    uint2 raw[kPrepRun];  // the run's raw inputs, all loads in flight at once
 #pragma unroll
-    for (int i = 0; i < kPrepTok; i++) {
-        const int t = t0 + i;
-        if (t < T) {
-            const size_t o = (plane * T + t) * kHd + tid;
-            const __half hi = __float2half_rn(act[i]);
-            ph[o] = __half_as_ushort(hi);
-            pl[o] = f16_bits_rn(act[i] - __half2float(hi));
+    for (int i = 0; i < kPrepRun; i++)
+        raw[i] = (i < tend) ? *reinterpret_cast<const uint2*>(xb + (size_t)(t0 + i) * kQKVDim)
+                            : make_uint2(0u, 0u);
+#pragma unroll
+    for (int i = 0; i < kPrepRun; i++) {
+        if (i >= tend) break;
+        const float4 x0 = bf16x4_to_f32(raw[i]);
+        // gemv.rs:1134-1139: history oldest first, then the token itself
+        float a[4];
+        const float* h3 = &x3.x;
+        const float* h2 = &x2.x;
+        const float* h1 = &x1.x;
+        const float* h0 = &x0.x;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            float cv = h3[c] * w[c].x;
+            cv += h2[c] * w[c].y;
+            cv += h1[c] * w[c].z;
+            cv += h0[c] * w[c].w;
+            a[c] = silu_f(cv);
         }
+        x3 = x2;
+        x2 = x1;
+        x1 = x0;
+        if (is_qk) {  // l2_normalize (gemv.rs:641-649, 1153-1155), q * 1/sqrt(128)
+            float ss = a[0] * a[0] + a[1] * a[1] + a[2] * a[2] + a[3] * a[3];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float n = sqrtf(ss);
+            const float inv = n > 1e-12f ? 1.0f / n : 1.0f;
+            const float sc = is_q ? 0.08838834764831845f : 1.0f;
+#pragma unroll
+            for (int c = 0; c < 4; c++) a[c] = (a[c] * inv) * sc;
+        }
+        const __half2 h01 = __floats2half2_rn(a[0], a[1]), h23 = __floats2half2_rn(a[2], a[3]);
+        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+        const __half2 l01 = __floats2half2_rn(a[0] - f01.x, a[1] - f01.y);
+        const __half2 l23 = __floats2half2_rn(a[2] - f23.x, a[3] - f23.y);
+        const size_t o = (plane * T + t0 + i) * kHd + lane * 4;
+        *reinterpret_cast<uint2*>(ph + o) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+        *reinterpret_cast<uint2*>(pl + o) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
     }
-    if (hv >= 2 * kNumQK && tid < kPrepTok) {
-        // gates of V head vh for this token (gemv.rs:1171-1172), as log-decay
-        const int vhh = hv - 2 * kNumQK, t = t0 + tid;
-        if (t < T) {
-            const float x = a_in[((size_t)b * T + t) * kNumV + vhh] + dt_bias[vhh];
-            const float sp = x > 20.0f ? x : log1pf(__expf(x));
-            gout[((size_t)b * kNumV + vhh) * T + t] = -__expf(a_log[vhh]) * sp;
-            bout[((size_t)b * kNumV + vhh) * T + t] =
-                1.0f / (1.0f + __expf(-b_in[((size_t)b * T + t) * kNumV + vhh]));
-        }
+    if (!is_qk && lane < tend) {
+        // gates of V head vhh for token t0 + lane (gemv.rs:1171-1172), as log-decay
+        const int vhh = hv - 2 * kNumQK, t = t0 + lane;
+        const float x = a_in[((size_t)b * T + t) * kNumV + vhh] + dt_bias[vhh];
+        const float sp = x > 20.0f ? x : log1pf(__expf(x));
+        gout[((size_t)b * kNumV + vhh) * T + t] = -__expf(a_log[vhh]) * sp;
+        bout[((size_t)b * kNumV + vhh) * T + t] =
+            1.0f / (1.0f + __expf(-b_in[((size_t)b * T + t) * kNumV + vhh]));
     }
 }
 
@@ -165,14 +184,24 @@ __device__ __forceinline__ uint32_t swz(int row, int col) {  // fp16 [rows x 64]
     return (uint32_t)(row * 128 + ((((col >> 3) ^ (row & 7))) << 4) + (col & 7) * 2);
 }
 
+__device__ __forceinline__ uint32_t h2bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// two f32 -> fp16 hi pair and the fp16 of the remainders (packed conversions)
+__device__ __forceinline__ void split2(float a, float b, __half2& hi, __half2& lo) {
+    hi = __floats2half2_rn(a, b);
+    const float2 f = __half22float2(hi);
+    lo = __floats2half2_rn(a - f.x, b - f.y);
+}
+
 // 8 consecutive f32 -> fp16 hi (and lo = fp16 of the remainder) as two uint4
 __device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
     uint32_t h[4], l[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const __half a = __float2half_rn(v[2 * i]), b = __float2half_rn(v[2 * i + 1]);
-        h[i] = pack_bf16(__half_as_ushort(a), __half_as_ushort(b));
-        l[i] = pack_f16x2_rn(v[2 * i] - __half2float(a), v[2 * i + 1] - __half2float(b));
+        __half2 a, b;
+        split2(v[2 * i], v[2 * i + 1], a, b);
+        h[i] = h2bits(a);
+        l[i] = h2bits(b);
     }
     hi = make_uint4(h[0], h[1], h[2], h[3]);
     lo = make_uint4(l[0], l[1], l[2], l[3]);
@@ -183,11 +212,11 @@ __device__ __forceinline__ uint4 round8(const float* v) {
                       pack_f16x2_rn(v[4], v[5]), pack_f16x2_rn(v[6], v[7]));
 }
 
-// inclusive cumulative log-decay G_t of the 64 gates in sg[] (warp 0), plus
-// eG[t] = e^G_t and eD[s] = e^(G_63 - G_s)
+// inclusive cumulative log-decay of the 64 gates in sg[] (warp 0), in log2
+// units: sG[t] = log2e * G_t; plus eG[t] = e^G_t and eD[s] = e^(G_63 - G_s)
 __device__ __forceinline__ void chunk_decays(const float* sg, float* sG, float* eG, float* eD,
                                              int lane) {
-    float g0 = sg[lane], g1 = sg[lane + 32];
+    float g0 = sg[lane] * kLog2e, g1 = sg[lane + 32] * kLog2e;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const float u0 = __shfl_up_sync(0xffffffffu, g0, o);
@@ -202,10 +231,10 @@ __device__ __forceinline__ void chunk_decays(const float* sg, float* sG, float* 
     sG[lane] = g0;
     sG[lane + 32] = g1;
     if (eG) {
-        eG[lane] = exp2f(g0 * kLog2e);
-        eG[lane + 32] = exp2f(g1 * kLog2e);
-        eD[lane] = exp2f((g63 - g0) * kLog2e);
-        eD[lane + 32] = exp2f((g63 - g1) * kLog2e);
+        eG[lane] = exp2f(g0);
+        eG[lane + 32] = exp2f(g1);
+        eD[lane] = exp2f(g63 - g0);
+        eD[lane + 32] = exp2f(g63 - g1);
     }
 }
 
@@ -343,10 +372,10 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
 #pragma unroll
             for (int s = 0; s < kC; s += 4) {
                 float4 v;
-                v.x = (s + 0 < t) ? bt * exp2f((Gt - sG[s + 0]) * kLog2e) * kq[s + 0] : 0.f;
-                v.y = (s + 1 < t) ? bt * exp2f((Gt - sG[s + 1]) * kLog2e) * kq[s + 1] : 0.f;
-                v.z = (s + 2 < t) ? bt * exp2f((Gt - sG[s + 2]) * kLog2e) * kq[s + 2] : 0.f;
-                v.w = (s + 3 < t) ? bt * exp2f((Gt - sG[s + 3]) * kLog2e) * kq[s + 3] : 0.f;
+                v.x = (s + 0 < t) ? bt * ex2_approx(Gt - sG[s + 0]) * kq[s + 0] : 0.f;
+                v.y = (s + 1 < t) ? bt * ex2_approx(Gt - sG[s + 1]) * kq[s + 1] : 0.f;
+                v.z = (s + 2 < t) ? bt * ex2_approx(Gt - sG[s + 2]) * kq[s + 2] : 0.f;
+                v.w = (s + 3 < t) ? bt * ex2_approx(Gt - sG[s + 3]) * kq[s + 3] : 0.f;
                 *reinterpret_cast<float4*>(arow + s) = v;
             }
         } else {
@@ -359,7 +388,7 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
                 float p[8];
 #pragma unroll
                 for (int i = 0; i < 8; i++)
-                    p[i] = (s + i <= t) ? exp2f((Gt - sG[s + i]) * kLog2e) * kq[s + i] : 0.f;
+                    p[i] = (s + i <= t) ? ex2_approx(Gt - sG[s + i]) * kq[s + i] : 0.f;
                 uint4 h, l;
                 split8(p, h, l);
                 hrow[s / 8] = h;
@@ -391,16 +420,16 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
             tcol[t] = (t == j) ? 1.f : -((a0 + a1) + (a2 + a3));
         }
         const float bj = sB[j];
-        const float c1 = bj * exp2f(sG[j] * kLog2e), c2 = bj;
+        const float c1 = bj * exp2f(sG[j]), c2 = bj;
 #pragma unroll
         for (int t = 0; t < kC; t++) {
-            const float v1 = tcol[t] * c1, v2 = tcol[t] * c2;
-            const __half h1 = __float2half_rn(v1), h2 = __float2half_rn(v2);
+            __half2 hi, lo;  // (T', T'') pairs
+            split2(tcol[t] * c1, tcol[t] * c2, hi, lo);
             const uint32_t o = swz(t, j);
-            *reinterpret_cast<uint16_t*>(smem + kL_T1h + o) = __half_as_ushort(h1);
-            *reinterpret_cast<uint16_t*>(smem + kL_T1l + o) = f16_bits_rn(v1 - __half2float(h1));
-            *reinterpret_cast<uint16_t*>(smem + kL_T2h + o) = __half_as_ushort(h2);
-            *reinterpret_cast<uint16_t*>(smem + kL_T2l + o) = f16_bits_rn(v2 - __half2float(h2));
+            *reinterpret_cast<__half*>(smem + kL_T1h + o) = __low2half(hi);
+            *reinterpret_cast<__half*>(smem + kL_T2h + o) = __high2half(hi);
+            *reinterpret_cast<__half*>(smem + kL_T1l + o) = __low2half(lo);
+            *reinterpret_cast<__half*>(smem + kL_T2l + o) = __high2half(lo);
         }
     }
     fence_proxy_async_shared();
@@ -481,18 +510,21 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
 
 // ---- 2b. state pass: one CTA (128 threads, lane = v row) per (V head, sequence) ----
 //
-// Per chunk, with S0 the state entering it (f32 master in TMEM, fp16 copy in
+// Per chunk c, with S0 the state entering it (f32 master in TMEM, fp16 copy in
 // shared memory as the A operand):
-//   MMA4  U_acc = -S0 W^T        MMA5  Y1 = S0 Q^T            (fp16 x fp16)
-//   U = U~ + U_acc (f32; U~ prefetched into registers), split into fp16 hi/lo,
-//   and (U diag(e^(G63-G)))^T hi/lo; S_master *= e^G63
-//   MMA6  Y2 = U^T P'^T          MMA7  S_master += (U D)^T K  (compensated)
-//   y_t = e^G_t Y1 + Y2;  S_master -> fp16 copy for the next chunk
-// W^T and Q are double-buffered and fetched a chunk ahead; P' and K are
-// fetched as soon as MMA6/MMA7 of the previous chunk have read them.
+//   MMA4  U_acc = -S0 W^T        MMA5  Y1[c&1] = S0 Q^T        (fp16 x fp16)
+//   (meanwhile: y of chunk c-1 = e^G Y1 + Y2 goes out)
+//   U = U~ + U_acc (f32), split into fp16 hi/lo, and (U diag(e^(G63-G)))^T hi/lo
+//   MMA6  Y2 = U^T P'^T          MMA7  dS = (U D)^T K          (compensated)
+//   S_master = e^G63 S_master + dS (f32), and its fp16 copy for chunk c+1
+// W^T, Q and U~ (one untiled bulk copy) are refetched for chunk c+1 as soon
+// as chunk c has consumed them, P' and K after MMA6/MMA7; the gates of chunk
+// c+1 are read into registers during chunk c.  Y1 is double-buffered in
+// TMEM so chunk c-1's outputs can be read while chunk c's MMA5 runs.
 constexpr int kS_S0 = 0;            // S0 fp16 [128 v x 128 k]: 2 boxes [128 x 64]
-constexpr int kS_W = 32768;         // W^T [128 k x 64 t] fp16, x2 (16 KB each)
-constexpr int kS_Q = 65536;         // Q [64 t x 128 k] fp16: 2 boxes [64 x 64], x2 (16 KB each)
+constexpr int kS_W = 32768;         // W^T [128 k x 64 t] fp16 (16 KB)
+constexpr int kS_Q = 49152;         // Q [64 t x 128 k] fp16: 2 boxes [64 x 64] (16 KB)
+constexpr int kS_Ut = 65536;        // U~^T f32 [16][128 v][4] (32 KB)
 constexpr int kS_Ph = 98304;        // P' hi [64 t x 64 s]
 constexpr int kS_Pl = 106496;
 constexpr int kS_Kh = 114688;       // K hi [64 s x 128 k]: 2 boxes [64 x 64]
@@ -501,12 +533,12 @@ constexpr int kS_Uh = 147456;       // U^T hi [128 v x 64 s]
 constexpr int kS_Ul = 163840;
 constexpr int kS_UDh = 180224;      // (U^T diag D) hi
 constexpr int kS_UDl = 196608;
-constexpr int kS_Misc = 212992;     // G, eG, eD, g: 4 x 64 f32; barriers
-constexpr int kStateSmem = kS_Misc + 4 * 64 * 4 + 128 + 1024;
-constexpr uint32_t kTmU2 = 0, kTmY1 = 64, kTmY2 = 128, kTmS = 256;
+constexpr int kS_Misc = 212992;     // [2] x (G, eG, eD, g): 8 x 64 f32; barriers
+constexpr int kStateSmem = kS_Misc + 8 * 64 * 4 + 128 + 1024;
+constexpr uint32_t kTmU2 = 0, kTmY1 = 64 /* x2 */, kTmY2 = 192, kTmS = 256, kTmDS = 384;
 
 struct StateBars {
-    uint64_t wq_full[2], pk_full, m45, m67;
+    uint64_t wqu_full, pk_full, m45, m67;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -519,24 +551,22 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
                float* __restrict__ S, float* __restrict__ y, int T, int nch, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    float* sG = reinterpret_cast<float*>(smem + kS_Misc);
-    float* eG = sG + 64;
-    float* eD = eG + 64;
-    float* sg = eD + 64;
-    StateBars* bars = reinterpret_cast<StateBars*>(sg + 64);
+    float* misc = reinterpret_cast<float*>(smem + kS_Misc);
+    // per chunk parity p: sG = misc + p*256, eG = +64, eD = +128, sg = +192
+    StateBars* bars = reinterpret_cast<StateBars*>(misc + 8 * 64);
     volatile int* abort_flag = &bars->abort_flag;
     const uint32_t sb = smem_u32(smem);
 
     const int vh = blockIdx.x, b = blockIdx.y, qk = vh >> 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
-    const int row = tid;  // TMEM lane = v (or k for W) row
+    const int row = tid;  // TMEM lane = v row
     const int plane_qk = b * kNumQK + qk;
-    const size_t item0 = ((size_t)b * kNumV + vh) * nch;
+    const size_t plane_v = (size_t)b * kNumV + vh;
+    const size_t item0 = plane_v * nch;
 
     if (tid == 0) {
-        mbar_init(smem_u32(&bars->wq_full[0]), 1);
-        mbar_init(smem_u32(&bars->wq_full[1]), 1);
+        mbar_init(smem_u32(&bars->wqu_full), 1);
         mbar_init(smem_u32(&bars->pk_full), 1);
         mbar_init(smem_u32(&bars->m45), 1);
         mbar_init(smem_u32(&bars->m67), 1);
@@ -554,17 +584,17 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
 
     // thread 0's record of the last phase it started on each barrier and not
     // yet seen complete (drained on the way out of an aborted CTA)
-    bool wq_out[2] = {false, false}, pk_out = false, m45_out = false, m67_out = false;
-    uint32_t wq_par[2] = {0, 0}, pk_par = 0, m45_par = 0, m67_par = 0;
-    auto issue_wq = [&](int c) {  // W^T and Q of chunk c into buffer c & 1
-        const int buf = c & 1;
-        const uint32_t fb = smem_u32(&bars->wq_full[buf]);
-        wq_out[buf] = true;
-        wq_par[buf] = (uint32_t)(c >> 1) & 1;
-        mbar_arrive_expect_tx(fb, 16384 + 16384);
-        tma_load_3d(sb + kS_W + buf * 16384, &twt, 0, 0, (int)(item0 + c), fb);
+    bool wqu_out = false, pk_out = false, m45_out = false, m67_out = false;
+    uint32_t wqu_par = 0, pk_par = 0, m45_par = 0, m67_par = 0;
+    auto issue_wqu = [&](int c) {  // W^T, Q and U~^T of chunk c
+        const uint32_t fb = smem_u32(&bars->wqu_full);
+        wqu_out = true;
+        wqu_par = (uint32_t)c & 1;
+        mbar_arrive_expect_tx(fb, 16384 + 16384 + 32768);
+        tma_load_3d(sb + kS_W, &twt, 0, 0, (int)(item0 + c), fb);
         for (int hb = 0; hb < 2; hb++)
-            tma_load_3d(sb + kS_Q + buf * 16384 + hb * 8192, &tqh, hb * 64, c * kC, plane_qk, fb);
+            tma_load_3d(sb + kS_Q + hb * 8192, &tqh, hb * 64, c * kC, plane_qk, fb);
+        bulk_load(sb + kS_Ut, ut_in + (item0 + c) * kHd * kC, 32768, fb);
     };
     auto issue_pk = [&](int c) {  // P' and K of chunk c
         const uint32_t fb = smem_u32(&bars->pk_full);
@@ -579,12 +609,13 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         }
     };
     if (tid == 0) {
-        issue_wq(0);
+        issue_wqu(0);
         issue_pk(0);
     }
+    float g_next = (tid < min(kC, T)) ? gin[plane_v * T + tid] : 0.f;  // gates of chunk 0
 
     // ---- initial state: global f32 -> TMEM master and fp16 copy ----
-    float* Sg = S + ((size_t)b * kNumV + vh) * kHd * kHd;
+    float* Sg = S + plane_v * kHd * kHd;
     {
         const float* srow = Sg + (size_t)row * kHd;
 #pragma unroll 1
@@ -609,60 +640,83 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
     tc_fence_before();
     __syncthreads();
 
-    bool ok = true;
-    for (int ci = 0; ci < nch && ok; ci++) {
-        const int t0 = ci * kC, tc = min(kC, T - t0);
-        const int buf = ci & 1;
-        if (tid == 0 && ci + 1 < nch) issue_wq(ci + 1);  // its buffer's MMAs (chunk ci-1) are done
-        // U~ of this chunk straight into registers (coalesced float4 per 4 tokens)
-        float ut[64];
-        {
-            const float4* ub = reinterpret_cast<const float4*>(ut_in + (item0 + ci) * kHd * kC);
+    // y of chunk c (parity p) from Y1[p], Y2 and e^G (lane v, coalesced per token)
+    auto write_y = [&](int c) {
+        const int p = c & 1, t0 = c * kC, tc = min(kC, T - t0);
+        const float* eGp = misc + p * 256 + 64;
+        float y1[64], y2[64];
+        tmem_ld32(tm + lane_addr + kTmY1 + p * 64, y1);
+        tmem_ld32(tm + lane_addr + kTmY1 + p * 64 + 32, y1 + 32);
+        tmem_ld32(tm + lane_addr + kTmY2, y2);
+        tmem_ld32(tm + lane_addr + kTmY2 + 32, y2 + 32);
+        tmem_ld_wait();
+        float* yb = y + ((size_t)b * T + t0) * kVDim + (size_t)vh * kHd + row;
 #pragma unroll
-            for (int t4 = 0; t4 < kC / 4; t4++) {
-                const float4 f = ub[t4 * kHd + row];
-                ut[4 * t4] = f.x; ut[4 * t4 + 1] = f.y; ut[4 * t4 + 2] = f.z; ut[4 * t4 + 3] = f.w;
-            }
+        for (int t = 0; t < kC; t++)
+            if (t < tc) yb[(size_t)t * kVDim] = eGp[t] * y1[t] + y2[t];
+    };
+
+    bool ok = true;
+    int ci = 0;
+    for (; ci < nch && ok; ci++) {
+        const int p = ci & 1;
+        float* sGp = misc + p * 256;
+        float* eGp = sGp + 64;
+        float* eDp = sGp + 128;
+        float* sgp = sGp + 192;
+        if (tid < kC) sgp[tid] = g_next;
+        {  // gates of chunk ci+1, consumed next iteration
+            const int tn = (ci + 1) * kC;
+            g_next = (ci + 1 < nch && tid < min(kC, T - tn)) ? gin[plane_v * T + tn + tid] : 0.f;
         }
-        if (tid < kC) sg[tid] = (tid < tc) ? gin[((size_t)b * kNumV + vh) * T + t0 + tid] : 0.f;
         __syncthreads();
-        if (warp == 0) chunk_decays(sg, sG, eG, eD, lane);
+        if (warp == 0) chunk_decays(sgp, sGp, eGp, eDp, lane);
 
         // ---- MMA4 + MMA5 ----
         if (tid == 0) {
-            if (mbar_wait_bounded(smem_u32(&bars->wq_full[buf]), (ci >> 1) & 1, abort_flag, err)) {
-                wq_out[buf] = false;
+            if (mbar_wait_bounded(smem_u32(&bars->wqu_full), p, abort_flag, err)) {
+                wqu_out = false;
                 tc_fence_after();
-                const uint32_t wb = sb + kS_W + buf * 16384, qb = sb + kS_Q + buf * 16384;
                 for (int kk = 0; kk < 8; kk++) {
                     const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
                     umma_bf16_ss(tm + kTmU2, umma_sdesc(sb + kS_S0 + aoff, 16, 1024),
-                                 umma_sdesc(wb + kk * 2048, 8192, 1024), kIdSW, kk > 0);
+                                 umma_sdesc(sb + kS_W + kk * 2048, 8192, 1024), kIdSW, kk > 0);
                 }
                 for (int kk = 0; kk < 8; kk++) {
                     const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16_ss(tm + kTmY1, umma_sdesc(sb + kS_S0 + aoff, 16, 1024),
-                                 umma_sdesc(qb + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), kIdSQ,
-                                 kk > 0);
+                    umma_bf16_ss(tm + kTmY1 + p * 64, umma_sdesc(sb + kS_S0 + aoff, 16, 1024),
+                                 umma_sdesc(sb + kS_Q + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
+                                 kIdSQ, kk > 0);
                 }
             }
             umma_commit(smem_u32(&bars->m45));
             m45_out = true;
-            m45_par = (uint32_t)ci & 1;
+            m45_par = (uint32_t)p;
         }
+        // outputs of the previous chunk while MMA4/MMA5 run (Y2 is rewritten only by MMA6)
+        if (ci > 0) write_y(ci - 1);
         {
-            const bool w = mbar_wait_bounded(smem_u32(&bars->m45), ci & 1, abort_flag, err);
+            // every thread waits on the load barrier too: it reads U~ from shared memory
+            const bool w = mbar_wait_bounded(smem_u32(&bars->m45), p, abort_flag, err) &&
+                           mbar_wait_bounded(smem_u32(&bars->wqu_full), p, abort_flag, err);
             if (w) m45_out = false;
             ok = __syncthreads_and(ok && w && !*abort_flag) != 0;  // also publishes G, eG, eD
         }
         if (!ok) break;
         tc_fence_after();
 
-        // ---- U = U~ + U_acc -> hi/lo; U D -> hi/lo; S_master *= e^G63 ----
+        // ---- U = U~ + U_acc -> hi/lo; U D -> hi/lo ----
         {
             float acc[64];
             tmem_ld32(tm + lane_addr + kTmU2, acc);
             tmem_ld32(tm + lane_addr + kTmU2 + 32, acc + 32);
+            const float4* ub = reinterpret_cast<const float4*>(smem + kS_Ut);
+            float ut[64];
+#pragma unroll
+            for (int t4 = 0; t4 < kC / 4; t4++) {
+                const float4 f = ub[t4 * kHd + row];
+                ut[4 * t4] = f.x; ut[4 * t4 + 1] = f.y; ut[4 * t4 + 2] = f.z; ut[4 * t4 + 3] = f.w;
+            }
             tmem_ld_wait();
 #pragma unroll
             for (int s = 0; s < kC; s++) acc[s] += ut[s];
@@ -674,30 +728,20 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
                 *reinterpret_cast<uint4*>(smem + kS_Ul + sw128_off(row, s >> 3)) = l;
                 float d[8];
 #pragma unroll
-                for (int i = 0; i < 8; i++) d[i] = acc[s + i] * eD[s + i];
+                for (int i = 0; i < 8; i++) d[i] = acc[s + i] * eDp[s + i];
                 split8(d, h, l);
                 *reinterpret_cast<uint4*>(smem + kS_UDh + sw128_off(row, s >> 3)) = h;
                 *reinterpret_cast<uint4*>(smem + kS_UDl + sw128_off(row, s >> 3)) = l;
             }
-            const float decay = eG[kC - 1];
-#pragma unroll 1
-            for (int c = 0; c < 4; c++) {
-                float sv[32];
-                tmem_ld32(tm + lane_addr + kTmS + c * 32, sv);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 32; i++) sv[i] *= decay;
-                tmem_st32(tm + lane_addr + kTmS + c * 32, sv);
-            }
-            tmem_st_wait();
         }
         fence_proxy_async_shared();
         tc_fence_before();
         __syncthreads();
 
-        // ---- MMA6 + MMA7 (compensated) ----
+        // ---- MMA6 + MMA7 (compensated); refetch W^T, Q, U~ for chunk ci+1 ----
         if (tid == 0) {
-            if (mbar_wait_bounded(smem_u32(&bars->pk_full), ci & 1, abort_flag, err)) {
+            if (ci + 1 < nch) issue_wqu(ci + 1);  // MMA4/5 read W/Q, every thread has read U~
+            if (mbar_wait_bounded(smem_u32(&bars->pk_full), p, abort_flag, err)) {
                 pk_out = false;
                 tc_fence_after();
                 int n = 0;
@@ -708,20 +752,21 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
                         umma_bf16_ss(tm + kTmY2, umma_sdesc(ua + kk * 32, 16, 1024),
                                      umma_sdesc(pb + kk * 32, 16, 1024), kIdUP, n > 0);
                 }
+                n = 0;
                 for (int term = 0; term < 3; term++) {
                     const uint32_t ua = sb + (term == 2 ? kS_UDl : kS_UDh);
                     const uint32_t kb = sb + (term == 1 ? kS_Kl : kS_Kh);
-                    for (int kk = 0; kk < 4; kk++)
-                        umma_bf16_ss(tm + kTmS, umma_sdesc(ua + kk * 32, 16, 1024),
-                                     umma_sdesc(kb + kk * 2048, 8192, 1024), kIdUK, 1u);
+                    for (int kk = 0; kk < 4; kk++, n++)
+                        umma_bf16_ss(tm + kTmDS, umma_sdesc(ua + kk * 32, 16, 1024),
+                                     umma_sdesc(kb + kk * 2048, 8192, 1024), kIdUK, n > 0);
                 }
             }
             umma_commit(smem_u32(&bars->m67));
             m67_out = true;
-            m67_par = (uint32_t)ci & 1;
+            m67_par = (uint32_t)p;
         }
         {
-            const bool w = mbar_wait_bounded(smem_u32(&bars->m67), ci & 1, abort_flag, err);
+            const bool w = mbar_wait_bounded(smem_u32(&bars->m67), p, abort_flag, err);
             if (w) m67_out = false;
             ok = __syncthreads_and(ok && w && !*abort_flag) != 0;
         }
@@ -729,38 +774,34 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         tc_fence_after();
         if (tid == 0 && ci + 1 < nch) issue_pk(ci + 1);  // P' and K buffers are free again
 
-        // ---- y_t = e^G_t Y1 + Y2 (lane v); S_master -> fp16 copy ----
-        {
-            float y1[64], y2[64];
-            tmem_ld32(tm + lane_addr + kTmY1, y1);
-            tmem_ld32(tm + lane_addr + kTmY1 + 32, y1 + 32);
-            tmem_ld32(tm + lane_addr + kTmY2, y2);
-            tmem_ld32(tm + lane_addr + kTmY2 + 32, y2 + 32);
-            tmem_ld_wait();
-            float* yb = y + ((size_t)b * T + t0) * kVDim + (size_t)vh * kHd + row;
-#pragma unroll
-            for (int t = 0; t < kC; t++)
-                if (t < tc) yb[(size_t)t * kVDim] = eG[t] * y1[t] + y2[t];
+        // ---- S_master = e^G63 S_master + dS, and its fp16 copy for the next chunk ----
+        const float decay = eGp[kC - 1];
 #pragma unroll 1
-            for (int c = 0; c < 4; c++) {
-                float sv[32];
-                tmem_ld32(tm + lane_addr + kTmS + c * 32, sv);
-                tmem_ld_wait();
+        for (int c = 0; c < 4; c++) {
+            float sv[32], dv[32];
+            tmem_ld32(tm + lane_addr + kTmS + c * 32, sv);
+            tmem_ld32(tm + lane_addr + kTmDS + c * 32, dv);
+            tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; i += 8) {
-                    const int k = c * 32 + i;
-                    *reinterpret_cast<uint4*>(smem + kS_S0 + (k >> 6) * 16384 + sw128_off(row, (k & 63) >> 3)) =
-                        round8(sv + i);
-                }
+            for (int i = 0; i < 32; i++) sv[i] = fmaf(sv[i], decay, dv[i]);
+            tmem_st32(tm + lane_addr + kTmS + c * 32, sv);
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+                const int k = c * 32 + i;
+                *reinterpret_cast<uint4*>(smem + kS_S0 + (k >> 6) * 16384 + sw128_off(row, (k & 63) >> 3)) =
+                    round8(sv + i);
             }
         }
+        tmem_st_wait();
         fence_proxy_async_shared();
         tc_fence_before();
         __syncthreads();
     }
 
-    // ---- final state back to global (f32) ----
+    // ---- outputs of the last chunk; final state back to global (f32) ----
     if (ok) {
+        tc_fence_after();
+        write_y(nch - 1);
         float* srow = Sg + (size_t)row * kHd;
 #pragma unroll 1
         for (int c = 0; c < 4; c++) {
@@ -774,8 +815,7 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
     }
     // do not leave while copies or MMAs this CTA issued may still land
     if (tid == 0) {
-        for (int i = 0; i < 2; i++)
-            if (wq_out[i]) mbar_drain(smem_u32(&bars->wq_full[i]), wq_par[i]);
+        if (wqu_out) mbar_drain(smem_u32(&bars->wqu_full), wqu_par);
         if (pk_out) mbar_drain(smem_u32(&bars->pk_full), pk_par);
         if (m45_out) mbar_drain(smem_u32(&bars->m45), m45_par);
         if (m67_out) mbar_drain(smem_u32(&bars->m67), m67_par);
@@ -865,9 +905,11 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
     uint16_t* pl = reinterpret_cast<uint16_t*>(base + w.pl);
     {
         TimedLaunch tl(ctx, "dn_prefill_prep");
-        dim3 grid((T + kPrepTok - 1) / kPrepTok, 2 * kNumQK + kNumV, B);
-        dn_prefill_prep<<<grid, 128, 0, s>>>(qkv, a, bgate, p->conv_w, p->a_log, p->dt_bias, st->conv,
-                                             st->conv_pos, T, qh, ql, kh, kl, vh, vl, g, be);
+        const int nruns = (T + kPrepRun - 1) / kPrepRun;
+        const size_t warps = (size_t)B * nruns * 64;
+        dn_prefill_prep<<<(unsigned)((warps + kPrepWarps - 1) / kPrepWarps), 32 * kPrepWarps, 0, s>>>(
+            qkv, a, bgate, p->conv_w, p->a_log, p->dt_bias, st->conv, st->conv_pos, T, nruns, qh, ql, kh,
+            kl, vh, vl, g, be, B);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -938,6 +980,7 @@ extern "C" int qm_dn_prefill(qm_ctx* c, const qm_dn_params* p, qm_dn_state* st, 
     if (st->nvh != kNumV)
         return set_error(c, QM_E_UNSUPPORTED, "qm_dn_prefill: head-sharded states are decode-only");
     if ((uintptr_t)p->conv_w & 15) return set_error(c, QM_E_ARG, "conv_w must be 16-byte aligned");
+    if ((uintptr_t)qkv & 15) return set_error(c, QM_E_ARG, "qm_dn_prefill: qkv must be 16-byte aligned");
     if ((y && ((uintptr_t)y & 15)) || (out && ((uintptr_t)out & 15)) || (z && ((uintptr_t)z & 15)))
         return set_error(c, QM_E_ARG, "qm_dn_prefill: y/z/out must be 16-byte aligned");
     cudaSetDevice(c->device);
