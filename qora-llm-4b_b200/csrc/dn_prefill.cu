@@ -180,10 +180,6 @@ constexpr uint32_t kIdSQ = umma_idesc_f16kind(128, 64, false, false, false);
 constexpr uint32_t kIdUP = umma_idesc_f16kind(128, 64, false, false, false);
 constexpr uint32_t kIdUK = umma_idesc_f16kind(128, 128, false, true, false);   // A K, B MN
 
-__device__ __forceinline__ uint32_t swz(int row, int col) {  // fp16 [rows x 64] tile element
-    return (uint32_t)(row * 128 + ((((col >> 3) ^ (row & 7))) << 4) + (col & 7) * 2);
-}
-
 __device__ __forceinline__ uint32_t h2bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 // two f32 -> fp16 hi pair and the fp16 of the remainders (packed conversions)
@@ -238,6 +234,55 @@ __device__ __forceinline__ void chunk_decays(const float* sg, float* sG, float* 
     }
 }
 
+// One block diagonal d (pairs (i, j) = (j + d, j), j = 0 .. 3-d) of the blocked
+// unit-lower-triangular inverse T of I + A (row stride kAStride floats):
+//   X_ij = sum_{k=j}^{i-1} A_ik T_kj   (kept in the unused upper block (j, i))
+//   T_ij = -T_ii X_ij                  (T_ii stored with zeros above its diagonal)
+// Each of the 128 threads owns 2 (4 - d) elements; all trip counts are
+// compile-time so the shared-memory loads issue ahead of the FMAs.
+template <int D>
+__device__ __forceinline__ void tri_inverse_diagonal(const float* __restrict__ A, float* __restrict__ Tm,
+                                                     int tid) {
+    constexpr int kStride = 68;
+    constexpr int NOUT = (4 - D) * 2;
+#pragma unroll
+    for (int m = 0; m < NOUT; m++) {
+        const int o = tid + 128 * m;
+        const int j = o >> 8, i = j + D, r = (o >> 4) & 15, c = o & 15;
+        const float* arow = A + (16 * i + r) * kStride + 16 * j;
+        const float* tcol = Tm + (16 * j) * kStride + 16 * j + c;
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int u = 0; u < 16 * D; u += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(arow + u);
+            x[0] = fmaf(a.x, tcol[(u + 0) * kStride], x[0]);
+            x[1] = fmaf(a.y, tcol[(u + 1) * kStride], x[1]);
+            x[2] = fmaf(a.z, tcol[(u + 2) * kStride], x[2]);
+            x[3] = fmaf(a.w, tcol[(u + 3) * kStride], x[3]);
+        }
+        Tm[(16 * j + r) * kStride + 16 * i + c] = (x[0] + x[1]) + (x[2] + x[3]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < NOUT; m++) {
+        const int o = tid + 128 * m;
+        const int j = o >> 8, i = j + D, r = (o >> 4) & 15, c = o & 15;
+        const float* trow = Tm + (16 * i + r) * kStride + 16 * i;
+        const float* xcol = Tm + (16 * j) * kStride + 16 * i + c;
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int u = 0; u < 16; u += 4) {
+            const float4 t = *reinterpret_cast<const float4*>(trow + u);
+            x[0] = fmaf(t.x, xcol[(u + 0) * kStride], x[0]);
+            x[1] = fmaf(t.y, xcol[(u + 1) * kStride], x[1]);
+            x[2] = fmaf(t.z, xcol[(u + 2) * kStride], x[2]);
+            x[3] = fmaf(t.w, xcol[(u + 3) * kStride], x[3]);
+        }
+        Tm[(16 * i + r) * kStride + 16 * j + c] = -((x[0] + x[1]) + (x[2] + x[3]));
+    }
+    __syncthreads();
+}
+
 struct ChunkBars {
     uint64_t load, mma;
     uint32_t tmem_base;
@@ -261,13 +306,14 @@ constexpr int kL_T1h = kL_KQh + 8192;  //   hold T' and T'' (hi/lo), 8 KB each
 constexpr int kL_T1l = kL_KQh + 24576;
 constexpr int kL_T2h = kL_KQl + 8192;
 constexpr int kL_T2l = kL_KQl + 24576;
-constexpr int kL_A = 65536;            // A f32 [64][68] during the solve,
-constexpr int kL_Vh = 65536;           //   then V hi (2 boxes [64 x 64])
-constexpr int kL_Vl = 81920;           //   and V lo
-constexpr int kAStride = 68;           // floats per A row (float4-aligned, 4-way store conflicts)
-constexpr int kL_Misc = 98304;         // G, beta, g: 3 x 64 f32; barriers
-constexpr int kLocalSmem = kL_Misc + 3 * 64 * 4 + 64 + 1024;
-static_assert(kL_A + 64 * kAStride * 4 <= kL_Vl + 16384, "A fits the V region");
+constexpr int kAStride = 68;           // floats per A / T row (float4-aligned)
+constexpr int kL_A = 65536;            // A f32 [64][68] and T f32 [64][68] during the
+constexpr int kL_Tm = kL_A + 64 * kAStride * 4;  // solve, then V hi (2 boxes [64 x 64])
+constexpr int kL_Vh = 65536;           //   and V lo on top of them
+constexpr int kL_Vl = 81920;
+constexpr int kL_Misc = kL_Tm + 64 * kAStride * 4;  // G, beta, g, b e^G: 4 x 64 f32; barriers
+constexpr int kLocalSmem = kL_Misc + 4 * 64 * 4 + 64 + 1024;
+static_assert(kL_Vl + 16384 <= kL_Misc, "V fits over A and T");
 constexpr uint32_t kTmKQ = 0, kTmW = 64, kTmU = 128;
 
 __global__ void __launch_bounds__(128, 2)
@@ -282,8 +328,10 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
     float* sG = reinterpret_cast<float*>(smem + kL_Misc);
     float* sB = sG + 64;
     float* sg = sB + 64;
-    ChunkBars* bars = reinterpret_cast<ChunkBars*>(sg + 64);
+    float* sC1 = sg + 64;  // b_j e^G_j
+    ChunkBars* bars = reinterpret_cast<ChunkBars*>(sC1 + 64);
     float* Amat = reinterpret_cast<float*>(smem + kL_A);
+    float* Tm = reinterpret_cast<float*>(smem + kL_Tm);
     volatile int* abort_flag = &bars->abort_flag;
     const uint32_t sb = smem_u32(smem);
 
@@ -399,37 +447,54 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
     tc_fence_before();
     __syncthreads();
 
-    // ---- T = (I + A)^-1, column j per thread; T' = T diag(b e^G), T'' = T diag(b) ----
-    if (ok && tid < kC) {
-        const int j = tid;
-        float tcol[kC];
+    // ---- T = (I + A)^-1, blocked by 16: diagonal blocks by forward substitution,
+    // then T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj by block diagonals i - j = 1, 2, 3
+    // (f32); the upper blocks of T's storage hold the partial sums X_ij ----
+    if (ok) {  // block-uniform
+        if (tid < kC) {
+            const int blk = tid >> 4, c = tid & 15, o = blk * 16;
+            float tc[16];
 #pragma unroll
-        for (int t = 0; t < kC; t++) {
-            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-            const float* arow = Amat + t * kAStride;
+            for (int r = 0; r < 16; r++) {
+                const float* arow = Amat + (o + r) * kAStride + o;
+                float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-            for (int s = 0; s + 3 < t; s += 4) {
-                const float4 av = *reinterpret_cast<const float4*>(arow + s);
-                a0 = fmaf(av.x, tcol[s], a0);
-                a1 = fmaf(av.y, tcol[s + 1], a1);
-                a2 = fmaf(av.z, tcol[s + 2], a2);
-                a3 = fmaf(av.w, tcol[s + 3], a3);
+                for (int u = 0; u + 1 < r; u += 2) {
+                    a0 = fmaf(arow[u], tc[u], a0);
+                    a1 = fmaf(arow[u + 1], tc[u + 1], a1);
+                }
+                if (r & 1) a0 = fmaf(arow[r - 1], tc[r - 1], a0);
+                tc[r] = (r == c) ? 1.f : (r < c ? 0.f : -(a0 + a1));
             }
 #pragma unroll
-            for (int s = (t / 4) * 4; s < t; s++) a0 = fmaf(arow[s], tcol[s], a0);
-            tcol[t] = (t == j) ? 1.f : -((a0 + a1) + (a2 + a3));
+            for (int r = 0; r < 16; r++) Tm[(o + r) * kAStride + o + c] = tc[r];
+        } else {
+            const int t = tid - kC;
+            sC1[t] = sB[t] * exp2f(sG[t]);
         }
-        const float bj = sB[j];
-        const float c1 = bj * exp2f(sG[j]), c2 = bj;
+        __syncthreads();
+        static_assert(kAStride == 68, "tri_inverse_diagonal assumes the A/T row stride");
+        tri_inverse_diagonal<1>(Amat, Tm, tid);
+        tri_inverse_diagonal<2>(Amat, Tm, tid);
+        tri_inverse_diagonal<3>(Amat, Tm, tid);
+        // T' = T diag(b e^G), T'' = T diag(b) as fp16 hi/lo [t][j] tiles (upper part zero)
+        for (int o = tid; o < kC * 8; o += 128) {
+            const int t = o >> 3, jc = o & 7, j0 = jc * 8;
+            float v1[8], v2[8];
 #pragma unroll
-        for (int t = 0; t < kC; t++) {
-            __half2 hi, lo;  // (T', T'') pairs
-            split2(tcol[t] * c1, tcol[t] * c2, hi, lo);
-            const uint32_t o = swz(t, j);
-            *reinterpret_cast<__half*>(smem + kL_T1h + o) = __low2half(hi);
-            *reinterpret_cast<__half*>(smem + kL_T2h + o) = __high2half(hi);
-            *reinterpret_cast<__half*>(smem + kL_T1l + o) = __low2half(lo);
-            *reinterpret_cast<__half*>(smem + kL_T2l + o) = __high2half(lo);
+            for (int q = 0; q < 8; q++) {
+                const int j = j0 + q;
+                const float tv = (j <= t) ? Tm[t * kAStride + j] : 0.f;
+                v1[q] = tv * sC1[j];
+                v2[q] = tv * sB[j];
+            }
+            uint4 h, l;
+            split8(v1, h, l);
+            *reinterpret_cast<uint4*>(smem + kL_T1h + sw128_off(t, jc)) = h;
+            *reinterpret_cast<uint4*>(smem + kL_T1l + sw128_off(t, jc)) = l;
+            split8(v2, h, l);
+            *reinterpret_cast<uint4*>(smem + kL_T2h + sw128_off(t, jc)) = h;
+            *reinterpret_cast<uint4*>(smem + kL_T2l + sw128_off(t, jc)) = l;
         }
     }
     fence_proxy_async_shared();
