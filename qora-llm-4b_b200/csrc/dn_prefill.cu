@@ -298,8 +298,10 @@ struct ChunkBars {
 //   MMA3  U~^T = V^T (T diag(b))^T        (compensated)
 // written to the workspace for the state pass: W^T fp16 [128 k][64 t],
 // U~^T f32 as [16][128 v][4] (float4 of 4 tokens per v, so the state pass
-// reads it coalesced straight into registers) and P' fp16 hi/lo [64 t][64 s].
-// 100 KB of shared memory and 256 TMEM columns: two CTAs per SM.
+// loads it with one bulk copy and reads it conflict-free), P' fp16 hi/lo
+// [64 t][64 s], and the decayed operands of the state products
+// Q~_t = e^G_t q_t (fp16) and K~_s = e^(G_63 - G_s) k_s (fp16 hi/lo), [64][128].
+// 102 KB of shared memory and 256 TMEM columns: two CTAs per SM.
 constexpr int kL_KQh = 0;              // [K;Q] hi: 2 boxes [128 rows x 64] fp16 (K rows 0-63,
 constexpr int kL_KQl = 32768;          //   Q rows 64-127); after MMA1 the four Q quarters
 constexpr int kL_T1h = kL_KQh + 8192;  //   hold T' and T'' (hi/lo), 8 KB each
@@ -311,8 +313,8 @@ constexpr int kL_A = 65536;            // A f32 [64][68] and T f32 [64][68] duri
 constexpr int kL_Tm = kL_A + 64 * kAStride * 4;  // solve, then V hi (2 boxes [64 x 64])
 constexpr int kL_Vh = 65536;           //   and V lo on top of them
 constexpr int kL_Vl = 81920;
-constexpr int kL_Misc = kL_Tm + 64 * kAStride * 4;  // G, beta, g, b e^G: 4 x 64 f32; barriers
-constexpr int kLocalSmem = kL_Misc + 4 * 64 * 4 + 64 + 1024;
+constexpr int kL_Misc = kL_Tm + 64 * kAStride * 4;  // G, beta, g, b e^G, e^G, e^(G63-G): 6 x 64 f32
+constexpr int kLocalSmem = kL_Misc + 6 * 64 * 4 + 64 + 1024;
 static_assert(kL_Vl + 16384 <= kL_Misc, "V fits over A and T");
 constexpr uint32_t kTmKQ = 0, kTmW = 64, kTmU = 128;
 
@@ -322,14 +324,18 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
                const __grid_constant__ CUtensorMap tvh, const __grid_constant__ CUtensorMap tvl,
                const float* __restrict__ gin, const float* __restrict__ bin, int T, int nch,
                uint16_t* __restrict__ wt_out, float* __restrict__ ut_out,
-               uint16_t* __restrict__ ph_out, uint16_t* __restrict__ pl_out, int* err) {
+               uint16_t* __restrict__ ph_out, uint16_t* __restrict__ pl_out,
+               uint16_t* __restrict__ qt_out, uint16_t* __restrict__ kth_out,
+               uint16_t* __restrict__ ktl_out, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     float* sG = reinterpret_cast<float*>(smem + kL_Misc);
     float* sB = sG + 64;
     float* sg = sB + 64;
     float* sC1 = sg + 64;  // b_j e^G_j
-    ChunkBars* bars = reinterpret_cast<ChunkBars*>(sC1 + 64);
+    float* eG = sC1 + 64;
+    float* eD = eG + 64;
+    ChunkBars* bars = reinterpret_cast<ChunkBars*>(eD + 64);
     float* Amat = reinterpret_cast<float*>(smem + kL_A);
     float* Tm = reinterpret_cast<float*>(smem + kL_Tm);
     volatile int* abort_flag = &bars->abort_flag;
@@ -379,7 +385,7 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
         sB[tid] = valid ? bin[plane_v * T + t0 + tid] : 0.f;
     }
     __syncthreads();
-    if (warp == 0) chunk_decays(sg, sG, nullptr, nullptr, lane);
+    if (warp == 0) chunk_decays(sg, sG, eG, eD, lane);
     bool ok = mbar_wait_bounded(smem_u32(&bars->load), 0, abort_flag, err);
     if (ok) ld_out = false;
     ok = __syncthreads_and(ok) != 0;  // also publishes sG
@@ -444,6 +450,42 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
             }
         }
     }
+    // ---- Q~ = e^G q (fp16) and K~ = e^(G63-G) k (fp16 hi/lo), from the hi/lo tiles ----
+    if (ok) {
+        const size_t rowbase = item * kC;
+#pragma unroll 2
+        for (int m = 0; m < 8; m++) {
+            const int o = tid + 128 * m, t = o >> 4, kc = o & 15;
+            const uint32_t off = (kc >> 3) * 16384 + sw128_off(t, kc & 7);
+            float v[8];
+            // Q rows sit 8 KB into each box
+            uint4 h = *reinterpret_cast<const uint4*>(smem + kL_KQh + 8192 + off);
+            uint4 l = *reinterpret_cast<const uint4*>(smem + kL_KQl + 8192 + off);
+            const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&hw[i]));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&lw[i]));
+                v[2 * i] = (a.x + b.x) * eG[t];
+                v[2 * i + 1] = (a.y + b.y) * eG[t];
+            }
+            reinterpret_cast<uint4*>(qt_out + (rowbase + t) * kHd)[kc] = round8(v);
+            h = *reinterpret_cast<const uint4*>(smem + kL_KQh + off);
+            l = *reinterpret_cast<const uint4*>(smem + kL_KQl + off);
+            const uint32_t hk[4] = {h.x, h.y, h.z, h.w}, lk[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&hk[i]));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&lk[i]));
+                v[2 * i] = (a.x + b.x) * eD[t];
+                v[2 * i + 1] = (a.y + b.y) * eD[t];
+            }
+            uint4 kh4, kl4;
+            split8(v, kh4, kl4);
+            reinterpret_cast<uint4*>(kth_out + (rowbase + t) * kHd)[kc] = kh4;
+            reinterpret_cast<uint4*>(ktl_out + (rowbase + t) * kHd)[kc] = kl4;
+        }
+    }
     tc_fence_before();
     __syncthreads();
 
@@ -470,7 +512,7 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
             for (int r = 0; r < 16; r++) Tm[(o + r) * kAStride + o + c] = tc[r];
         } else {
             const int t = tid - kC;
-            sC1[t] = sB[t] * exp2f(sG[t]);
+            sC1[t] = sB[t] * eG[t];
         }
         __syncthreads();
         static_assert(kAStride == 68, "tri_inverse_diagonal assumes the A/T row stride");
@@ -576,42 +618,40 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
 // ---- 2b. state pass: one CTA (128 threads, lane = v row) per (V head, sequence) ----
 //
 // Per chunk c, with S0 the state entering it (f32 master in TMEM, fp16 copy in
-// shared memory as the A operand):
-//   MMA4  U_acc = -S0 W^T        MMA5  Y1[c&1] = S0 Q^T        (fp16 x fp16)
-//   (meanwhile: y of chunk c-1 = e^G Y1 + Y2 goes out)
-//   U = U~ + U_acc (f32), split into fp16 hi/lo, and (U diag(e^(G63-G)))^T hi/lo
-//   MMA6  Y2 = U^T P'^T          MMA7  dS = (U D)^T K          (compensated)
+// shared memory as the A operand), Q~ = e^G Q and K~ = e^(G63-G) K:
+//   MMA4  U_acc = -S0 W^T                    MMA5  Y[c&1] = S0 Q~^T  (fp16)
+//   U = U~ + U_acc (f32) -> fp16 hi/lo
+//   MMA7  dS = U^T K~   (compensated)        MMA6  Y[c&1] += U^T P'^T (compensated)
 //   S_master = e^G63 S_master + dS (f32), and its fp16 copy for chunk c+1
-// W^T, Q and U~ (one untiled bulk copy) are refetched for chunk c+1 as soon
-// as chunk c has consumed them, P' and K after MMA6/MMA7; the gates of chunk
-// c+1 are read into registers during chunk c.  Y1 is double-buffered in
-// TMEM so chunk c-1's outputs can be read while chunk c's MMA5 runs.
+// The dependency chain per chunk is S copy -> MMA4 -> U -> MMA7 -> S copy;
+// MMA5, MMA6 and the output of chunk c-1 (y = Y[(c-1)&1], read while MMA7
+// runs) stay off it.  W^T, Q~ and U~ (one untiled bulk copy) are refetched
+// for chunk c+1 as soon as MMA4/MMA5 and the U step are done, K~ after MMA7,
+// and P' is double-buffered; the gates of chunk c+1 are read into registers
+// during chunk c.
 constexpr int kS_S0 = 0;            // S0 fp16 [128 v x 128 k]: 2 boxes [128 x 64]
 constexpr int kS_W = 32768;         // W^T [128 k x 64 t] fp16 (16 KB)
-constexpr int kS_Q = 49152;         // Q [64 t x 128 k] fp16: 2 boxes [64 x 64] (16 KB)
+constexpr int kS_Q = 49152;         // Q~ [64 t x 128 k] fp16: 2 boxes [64 x 64] (16 KB)
 constexpr int kS_Ut = 65536;        // U~^T f32 [16][128 v][4] (32 KB)
-constexpr int kS_Ph = 98304;        // P' hi [64 t x 64 s]
-constexpr int kS_Pl = 106496;
-constexpr int kS_Kh = 114688;       // K hi [64 s x 128 k]: 2 boxes [64 x 64]
-constexpr int kS_Kl = 131072;
-constexpr int kS_Uh = 147456;       // U^T hi [128 v x 64 s]
-constexpr int kS_Ul = 163840;
-constexpr int kS_UDh = 180224;      // (U^T diag D) hi
-constexpr int kS_UDl = 196608;
-constexpr int kS_Misc = 212992;     // [2] x (G, eG, eD, g): 8 x 64 f32; barriers
+constexpr int kS_P = 98304;         // P' hi, lo [64 t x 64 s] (8 KB each), x2 buffers (32 KB)
+constexpr int kS_Kh = 131072;       // K~ hi [64 s x 128 k]: 2 boxes [64 x 64]
+constexpr int kS_Kl = 147456;
+constexpr int kS_Uh = 163840;       // U^T hi [128 v x 64 s]
+constexpr int kS_Ul = 180224;
+constexpr int kS_Misc = 196608;     // [2] x (G, eG, eD, g): 8 x 64 f32; barriers
 constexpr int kStateSmem = kS_Misc + 8 * 64 * 4 + 128 + 1024;
-constexpr uint32_t kTmU2 = 0, kTmY1 = 64 /* x2 */, kTmY2 = 192, kTmS = 256, kTmDS = 384;
+constexpr uint32_t kTmU2 = 0, kTmY = 64 /* x2 */, kTmDS = 256, kTmS = 384;
 
 struct StateBars {
-    uint64_t wqu_full, pk_full, m45, m67;
+    uint64_t wqu_full, k_full, p_full[2], m4, m5, m7, mY;
     uint32_t tmem_base;
     int abort_flag;
 };
 
 __global__ void __launch_bounds__(128, 1)
 dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ CUtensorMap tph,
-               const __grid_constant__ CUtensorMap tpl, const __grid_constant__ CUtensorMap tqh,
-               const __grid_constant__ CUtensorMap tkh, const __grid_constant__ CUtensorMap tkl,
+               const __grid_constant__ CUtensorMap tpl, const __grid_constant__ CUtensorMap tqt,
+               const __grid_constant__ CUtensorMap tkth, const __grid_constant__ CUtensorMap tktl,
                const float* __restrict__ ut_in, const float* __restrict__ gin,
                float* __restrict__ S, float* __restrict__ y, int T, int nch, int* err) {
     extern __shared__ uint8_t smem_raw[];
@@ -622,19 +662,22 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
     volatile int* abort_flag = &bars->abort_flag;
     const uint32_t sb = smem_u32(smem);
 
-    const int vh = blockIdx.x, b = blockIdx.y, qk = vh >> 1;
+    const int vh = blockIdx.x, b = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
     const int row = tid;  // TMEM lane = v row
-    const int plane_qk = b * kNumQK + qk;
     const size_t plane_v = (size_t)b * kNumV + vh;
     const size_t item0 = plane_v * nch;
 
     if (tid == 0) {
         mbar_init(smem_u32(&bars->wqu_full), 1);
-        mbar_init(smem_u32(&bars->pk_full), 1);
-        mbar_init(smem_u32(&bars->m45), 1);
-        mbar_init(smem_u32(&bars->m67), 1);
+        mbar_init(smem_u32(&bars->k_full), 1);
+        mbar_init(smem_u32(&bars->p_full[0]), 1);
+        mbar_init(smem_u32(&bars->p_full[1]), 1);
+        mbar_init(smem_u32(&bars->m4), 1);
+        mbar_init(smem_u32(&bars->m5), 1);
+        mbar_init(smem_u32(&bars->m7), 1);
+        mbar_init(smem_u32(&bars->mY), 1);
         bars->abort_flag = 0;
         fence_barrier_init();
     }
@@ -649,33 +692,45 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
 
     // thread 0's record of the last phase it started on each barrier and not
     // yet seen complete (drained on the way out of an aborted CTA)
-    bool wqu_out = false, pk_out = false, m45_out = false, m67_out = false;
-    uint32_t wqu_par = 0, pk_par = 0, m45_par = 0, m67_par = 0;
-    auto issue_wqu = [&](int c) {  // W^T, Q and U~^T of chunk c
+    bool out_[8] = {false, false, false, false, false, false, false, false};
+    uint32_t par_[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    uint64_t* const bar_list[8] = {&bars->wqu_full, &bars->k_full, &bars->p_full[0], &bars->p_full[1],
+                                   &bars->m4, &bars->m5, &bars->m7, &bars->mY};
+    auto started = [&](int i, int c) { out_[i] = true; par_[i] = (uint32_t)c & 1; };
+    auto seen = [&](int i) { out_[i] = false; };
+    enum { kWqu = 0, kK = 1, kP0 = 2, kM4 = 4, kM5 = 5, kM7 = 6, kMY = 7 };
+
+    auto issue_wqu = [&](int c) {  // W^T, Q~ and U~^T of chunk c
         const uint32_t fb = smem_u32(&bars->wqu_full);
-        wqu_out = true;
-        wqu_par = (uint32_t)c & 1;
+        started(kWqu, c);
         mbar_arrive_expect_tx(fb, 16384 + 16384 + 32768);
         tma_load_3d(sb + kS_W, &twt, 0, 0, (int)(item0 + c), fb);
         for (int hb = 0; hb < 2; hb++)
-            tma_load_3d(sb + kS_Q + hb * 8192, &tqh, hb * 64, c * kC, plane_qk, fb);
+            tma_load_3d(sb + kS_Q + hb * 8192, &tqt, hb * 64, 0, (int)(item0 + c), fb);
         bulk_load(sb + kS_Ut, ut_in + (item0 + c) * kHd * kC, 32768, fb);
     };
-    auto issue_pk = [&](int c) {  // P' and K of chunk c
-        const uint32_t fb = smem_u32(&bars->pk_full);
-        pk_out = true;
-        pk_par = (uint32_t)c & 1;
-        mbar_arrive_expect_tx(fb, 8192 * 2 + 16384 * 2);
-        tma_load_3d(sb + kS_Ph, &tph, 0, 0, (int)(item0 + c), fb);
-        tma_load_3d(sb + kS_Pl, &tpl, 0, 0, (int)(item0 + c), fb);
+    auto issue_k = [&](int c) {  // K~ hi/lo of chunk c
+        const uint32_t fb = smem_u32(&bars->k_full);
+        started(kK, c);
+        mbar_arrive_expect_tx(fb, 16384 * 2);
         for (int hb = 0; hb < 2; hb++) {
-            tma_load_3d(sb + kS_Kh + hb * 8192, &tkh, hb * 64, c * kC, plane_qk, fb);
-            tma_load_3d(sb + kS_Kl + hb * 8192, &tkl, hb * 64, c * kC, plane_qk, fb);
+            tma_load_3d(sb + kS_Kh + hb * 8192, &tkth, hb * 64, 0, (int)(item0 + c), fb);
+            tma_load_3d(sb + kS_Kl + hb * 8192, &tktl, hb * 64, 0, (int)(item0 + c), fb);
         }
+    };
+    auto issue_p = [&](int c) {  // P' hi/lo of chunk c into buffer c & 1
+        const int buf = c & 1;
+        const uint32_t fb = smem_u32(&bars->p_full[buf]);
+        started(kP0 + buf, c >> 1);
+        mbar_arrive_expect_tx(fb, 8192 * 2);
+        tma_load_3d(sb + kS_P + buf * 16384, &tph, 0, 0, (int)(item0 + c), fb);
+        tma_load_3d(sb + kS_P + buf * 16384 + 8192, &tpl, 0, 0, (int)(item0 + c), fb);
     };
     if (tid == 0) {
         issue_wqu(0);
-        issue_pk(0);
+        issue_k(0);
+        issue_p(0);
+        if (nch > 1) issue_p(1);
     }
     float g_next = (tid < min(kC, T)) ? gin[plane_v * T + tid] : 0.f;  // gates of chunk 0
 
@@ -705,25 +760,22 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
     tc_fence_before();
     __syncthreads();
 
-    // y of chunk c (parity p) from Y1[p], Y2 and e^G (lane v, coalesced per token)
+    // y of chunk c from Y[c&1] (lane v, coalesced per token); the caller has
+    // seen MMA6 of chunk c complete
     auto write_y = [&](int c) {
-        const int p = c & 1, t0 = c * kC, tc = min(kC, T - t0);
-        const float* eGp = misc + p * 256 + 64;
-        float y1[64], y2[64];
-        tmem_ld32(tm + lane_addr + kTmY1 + p * 64, y1);
-        tmem_ld32(tm + lane_addr + kTmY1 + p * 64 + 32, y1 + 32);
-        tmem_ld32(tm + lane_addr + kTmY2, y2);
-        tmem_ld32(tm + lane_addr + kTmY2 + 32, y2 + 32);
+        const int t0 = c * kC, tc = min(kC, T - t0);
+        float yv[64];
+        tmem_ld32(tm + lane_addr + kTmY + (c & 1) * 64, yv);
+        tmem_ld32(tm + lane_addr + kTmY + (c & 1) * 64 + 32, yv + 32);
         tmem_ld_wait();
         float* yb = y + ((size_t)b * T + t0) * kVDim + (size_t)vh * kHd + row;
 #pragma unroll
         for (int t = 0; t < kC; t++)
-            if (t < tc) yb[(size_t)t * kVDim] = eGp[t] * y1[t] + y2[t];
+            if (t < tc) yb[(size_t)t * kVDim] = yv[t];
     };
 
     bool ok = true;
-    int ci = 0;
-    for (; ci < nch && ok; ci++) {
+    for (int ci = 0; ci < nch && ok; ci++) {
         const int p = ci & 1;
         float* sGp = misc + p * 256;
         float* eGp = sGp + 64;
@@ -737,40 +789,44 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         __syncthreads();
         if (warp == 0) chunk_decays(sgp, sGp, eGp, eDp, lane);
 
-        // ---- MMA4 + MMA5 ----
+        // ---- MMA4 (commit m4), MMA5 (commit m5) ----
         if (tid == 0) {
             if (mbar_wait_bounded(smem_u32(&bars->wqu_full), p, abort_flag, err)) {
-                wqu_out = false;
+                seen(kWqu);
                 tc_fence_after();
                 for (int kk = 0; kk < 8; kk++) {
                     const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
                     umma_bf16_ss(tm + kTmU2, umma_sdesc(sb + kS_S0 + aoff, 16, 1024),
                                  umma_sdesc(sb + kS_W + kk * 2048, 8192, 1024), kIdSW, kk > 0);
                 }
+                umma_commit(smem_u32(&bars->m4));
+                started(kM4, ci);
                 for (int kk = 0; kk < 8; kk++) {
                     const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16_ss(tm + kTmY1 + p * 64, umma_sdesc(sb + kS_S0 + aoff, 16, 1024),
+                    umma_bf16_ss(tm + kTmY + p * 64, umma_sdesc(sb + kS_S0 + aoff, 16, 1024),
                                  umma_sdesc(sb + kS_Q + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
                                  kIdSQ, kk > 0);
                 }
+            } else {
+                umma_commit(smem_u32(&bars->m4));
+                started(kM4, ci);
             }
-            umma_commit(smem_u32(&bars->m45));
-            m45_out = true;
-            m45_par = (uint32_t)p;
+            umma_commit(smem_u32(&bars->m5));
+            started(kM5, ci);
         }
-        // outputs of the previous chunk while MMA4/MMA5 run (Y2 is rewritten only by MMA6)
-        if (ci > 0) write_y(ci - 1);
         {
             // every thread waits on the load barrier too: it reads U~ from shared memory
-            const bool w = mbar_wait_bounded(smem_u32(&bars->m45), p, abort_flag, err) &&
+            const bool w = mbar_wait_bounded(smem_u32(&bars->m4), p, abort_flag, err) &&
                            mbar_wait_bounded(smem_u32(&bars->wqu_full), p, abort_flag, err);
-            if (w) m45_out = false;
+            if (w) seen(kM4);
             ok = __syncthreads_and(ok && w && !*abort_flag) != 0;  // also publishes G, eG, eD
         }
         if (!ok) break;
         tc_fence_after();
+        // MMA6 of chunk ci-1 read P' buffer (ci+1)&1 and finished before MMA4 of ci
+        if (tid == 0 && ci + 1 < nch && ci >= 1) issue_p(ci + 1);
 
-        // ---- U = U~ + U_acc -> hi/lo; U D -> hi/lo ----
+        // ---- U = U~ + U_acc -> fp16 hi/lo ----
         {
             float acc[64];
             tmem_ld32(tm + lane_addr + kTmU2, acc);
@@ -784,60 +840,66 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
             }
             tmem_ld_wait();
 #pragma unroll
-            for (int s = 0; s < kC; s++) acc[s] += ut[s];
-#pragma unroll
             for (int s = 0; s < kC; s += 8) {
+                float u8[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++) u8[i] = acc[s + i] + ut[s + i];
                 uint4 h, l;
-                split8(acc + s, h, l);
+                split8(u8, h, l);
                 *reinterpret_cast<uint4*>(smem + kS_Uh + sw128_off(row, s >> 3)) = h;
                 *reinterpret_cast<uint4*>(smem + kS_Ul + sw128_off(row, s >> 3)) = l;
-                float d[8];
-#pragma unroll
-                for (int i = 0; i < 8; i++) d[i] = acc[s + i] * eDp[s + i];
-                split8(d, h, l);
-                *reinterpret_cast<uint4*>(smem + kS_UDh + sw128_off(row, s >> 3)) = h;
-                *reinterpret_cast<uint4*>(smem + kS_UDl + sw128_off(row, s >> 3)) = l;
             }
+        }
+        if (tid == 0) {  // MMA5 must be done before W/Q~ are refilled and S0 is rewritten
+            if (mbar_wait_bounded(smem_u32(&bars->m5), p, abort_flag, err)) seen(kM5);
         }
         fence_proxy_async_shared();
         tc_fence_before();
         __syncthreads();
 
-        // ---- MMA6 + MMA7 (compensated); refetch W^T, Q, U~ for chunk ci+1 ----
+        // ---- MMA7 (commit m7), MMA6 (commit mY); refetch W^T, Q~, U~ for chunk ci+1 ----
         if (tid == 0) {
-            if (ci + 1 < nch) issue_wqu(ci + 1);  // MMA4/5 read W/Q, every thread has read U~
-            if (mbar_wait_bounded(smem_u32(&bars->pk_full), p, abort_flag, err)) {
-                pk_out = false;
-                tc_fence_after();
+            if (ci + 1 < nch && !*abort_flag) issue_wqu(ci + 1);
+            const bool kok = mbar_wait_bounded(smem_u32(&bars->k_full), p, abort_flag, err);
+            const bool pok = kok && mbar_wait_bounded(smem_u32(&bars->p_full[p]), (ci >> 1) & 1, abort_flag, err);
+            if (kok) seen(kK);
+            if (pok) seen(kP0 + p);
+            tc_fence_after();
+            if (kok) {
                 int n = 0;
                 for (int term = 0; term < 3; term++) {
                     const uint32_t ua = sb + (term == 2 ? kS_Ul : kS_Uh);
-                    const uint32_t pb = sb + (term == 1 ? kS_Pl : kS_Ph);
-                    for (int kk = 0; kk < 4; kk++, n++)
-                        umma_bf16_ss(tm + kTmY2, umma_sdesc(ua + kk * 32, 16, 1024),
-                                     umma_sdesc(pb + kk * 32, 16, 1024), kIdUP, n > 0);
-                }
-                n = 0;
-                for (int term = 0; term < 3; term++) {
-                    const uint32_t ua = sb + (term == 2 ? kS_UDl : kS_UDh);
                     const uint32_t kb = sb + (term == 1 ? kS_Kl : kS_Kh);
                     for (int kk = 0; kk < 4; kk++, n++)
                         umma_bf16_ss(tm + kTmDS, umma_sdesc(ua + kk * 32, 16, 1024),
                                      umma_sdesc(kb + kk * 2048, 8192, 1024), kIdUK, n > 0);
                 }
             }
-            umma_commit(smem_u32(&bars->m67));
-            m67_out = true;
-            m67_par = (uint32_t)p;
+            umma_commit(smem_u32(&bars->m7));
+            started(kM7, ci);
+            if (pok) {
+                const uint32_t pb = sb + kS_P + p * 16384;
+                for (int term = 0; term < 3; term++) {
+                    const uint32_t ua = sb + (term == 2 ? kS_Ul : kS_Uh);
+                    const uint32_t pbt = pb + (term == 1 ? 8192 : 0);
+                    for (int kk = 0; kk < 4; kk++)
+                        umma_bf16_ss(tm + kTmY + p * 64, umma_sdesc(ua + kk * 32, 16, 1024),
+                                     umma_sdesc(pbt + kk * 32, 16, 1024), kIdUP, 1u);
+                }
+            }
+            umma_commit(smem_u32(&bars->mY));
+            started(kMY, ci);
         }
+        // outputs of chunk ci-1 while MMA7 runs (its MMA6 finished before MMA4 of ci)
+        if (ci > 0) write_y(ci - 1);
         {
-            const bool w = mbar_wait_bounded(smem_u32(&bars->m67), p, abort_flag, err);
-            if (w) m67_out = false;
+            const bool w = mbar_wait_bounded(smem_u32(&bars->m7), p, abort_flag, err);
+            if (w) seen(kM7);
             ok = __syncthreads_and(ok && w && !*abort_flag) != 0;
         }
         if (!ok) break;
         tc_fence_after();
-        if (tid == 0 && ci + 1 < nch) issue_pk(ci + 1);  // P' and K buffers are free again
+        if (tid == 0 && ci + 1 < nch) issue_k(ci + 1);  // MMA7 has read K~
 
         // ---- S_master = e^G63 S_master + dS, and its fp16 copy for the next chunk ----
         const float decay = eGp[kC - 1];
@@ -865,25 +927,28 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
 
     // ---- outputs of the last chunk; final state back to global (f32) ----
     if (ok) {
+        const bool w = mbar_wait_bounded(smem_u32(&bars->mY), (nch - 1) & 1, abort_flag, err);
+        if (w) seen(kMY);
         tc_fence_after();
-        write_y(nch - 1);
-        float* srow = Sg + (size_t)row * kHd;
+        if (w) {
+            write_y(nch - 1);
+            float* srow = Sg + (size_t)row * kHd;
 #pragma unroll 1
-        for (int c = 0; c < 4; c++) {
-            float sv[32];
-            tmem_ld32(tm + lane_addr + kTmS + c * 32, sv);
-            tmem_ld_wait();
+            for (int c = 0; c < 4; c++) {
+                float sv[32];
+                tmem_ld32(tm + lane_addr + kTmS + c * 32, sv);
+                tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; i += 4)
-                *reinterpret_cast<float4*>(srow + c * 32 + i) = make_float4(sv[i], sv[i + 1], sv[i + 2], sv[i + 3]);
+                for (int i = 0; i < 32; i += 4)
+                    *reinterpret_cast<float4*>(srow + c * 32 + i) =
+                        make_float4(sv[i], sv[i + 1], sv[i + 2], sv[i + 3]);
+            }
         }
     }
     // do not leave while copies or MMAs this CTA issued may still land
     if (tid == 0) {
-        if (wqu_out) mbar_drain(smem_u32(&bars->wqu_full), wqu_par);
-        if (pk_out) mbar_drain(smem_u32(&bars->pk_full), pk_par);
-        if (m45_out) mbar_drain(smem_u32(&bars->m45), m45_par);
-        if (m67_out) mbar_drain(smem_u32(&bars->m67), m67_par);
+        for (int i = 0; i < 8; i++)
+            if (out_[i]) mbar_drain(smem_u32(bar_list[i]), par_[i]);
     }
     tc_fence_before();
     __syncthreads();
@@ -919,9 +984,10 @@ __global__ void dn_prefill_gate(const float* __restrict__ y, const float* __rest
 
 // Workspace: fp16 hi+lo planes of q, k (16 heads each) and v (32 heads); f32
 // g and beta [B*32][T]; per (sequence, V head, chunk) item the chunk-local
-// factors W^T fp16 [128][64], U~^T f32 [64][128] and P' fp16 hi/lo [64][64].
+// factors W^T fp16 [128][64], U~^T f32 [64][128], P' fp16 hi/lo [64][64],
+// Q~ fp16 [64][128] and K~ fp16 hi/lo [64][128].
 struct DnWs {
-    size_t qh, ql, kh, kl, vh, vl, g, be, wt, ut, ph, pl, total;
+    size_t qh, ql, kh, kl, vh, vl, g, be, wt, ut, ph, pl, qt, kth, ktl, total;
 };
 
 static DnWs dn_ws_layout(int B, int T) {
@@ -942,6 +1008,9 @@ static DnWs dn_ws_layout(int B, int T) {
     w.ut = o; o = al(o + items * kHd * kC * 4);
     w.ph = o; o = al(o + items * kC * kC * 2);
     w.pl = o; o = al(o + items * kC * kC * 2);
+    w.qt = o; o = al(o + items * kC * kHd * 2);
+    w.kth = o; o = al(o + items * kC * kHd * 2);
+    w.ktl = o; o = al(o + items * kC * kHd * 2);
     w.total = o;
     return w;
 }
@@ -968,6 +1037,9 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
     float* ut = reinterpret_cast<float*>(base + w.ut);
     uint16_t* ph = reinterpret_cast<uint16_t*>(base + w.ph);
     uint16_t* pl = reinterpret_cast<uint16_t*>(base + w.pl);
+    uint16_t* qt = reinterpret_cast<uint16_t*>(base + w.qt);
+    uint16_t* kth = reinterpret_cast<uint16_t*>(base + w.kth);
+    uint16_t* ktl = reinterpret_cast<uint16_t*>(base + w.ktl);
     {
         TimedLaunch tl(ctx, "dn_prefill_prep");
         const int nruns = (T + kPrepRun - 1) / kPrepRun;
@@ -991,10 +1063,13 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
             return cudaErrorInvalidValue;
     }
     const uint64_t items = (uint64_t)B * kNumV * nch;
-    CUtensorMap mwt, mph, mpl;
+    CUtensorMap mwt, mph, mpl, mqt, mkth, mktl;
     if (encode_rows_tmap(&mwt, wt, kC, kHd, items, 64, kHd, true) != QM_OK ||
         encode_rows_tmap(&mph, ph, kC, kC, items, 64, kC, true) != QM_OK ||
-        encode_rows_tmap(&mpl, pl, kC, kC, items, 64, kC, true) != QM_OK)
+        encode_rows_tmap(&mpl, pl, kC, kC, items, 64, kC, true) != QM_OK ||
+        encode_rows_tmap(&mqt, qt, kHd, kC, items, 64, kC, true) != QM_OK ||
+        encode_rows_tmap(&mkth, kth, kHd, kC, items, 64, kC, true) != QM_OK ||
+        encode_rows_tmap(&mktl, ktl, kHd, kC, items, 64, kC, true) != QM_OK)
         return cudaErrorInvalidValue;
     static bool attr_set[64] = {};
     if (ctx->device < 64 && !attr_set[ctx->device]) {
@@ -1007,14 +1082,14 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
     {
         TimedLaunch tl(ctx, "dn_chunk_local");
         dn_chunk_local<<<dim3(kNumV, nch, B), 128, kLocalSmem, s>>>(
-            m[0], m[1], m[2], m[3], m[4], m[5], g, be, T, nch, wt, ut, ph, pl, ctx->d_err);
+            m[0], m[1], m[2], m[3], m[4], m[5], g, be, T, nch, wt, ut, ph, pl, qt, kth, ktl, ctx->d_err);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     ctx->launches += 1;
     {
         TimedLaunch tl(ctx, "dn_chunk_state");
-        dn_chunk_state<<<dim3(kNumV, B), 128, kStateSmem, s>>>(mwt, mph, mpl, m[0], m[2], m[3], ut, g,
+        dn_chunk_state<<<dim3(kNumV, B), 128, kStateSmem, s>>>(mwt, mph, mpl, mqt, mkth, mktl, ut, g,
                                                                st->s, y, T, nch, ctx->d_err);
     }
     e = cudaGetLastError();
