@@ -37,7 +37,7 @@ dn_decode_kernel(const float* __restrict__ qkv, const float* __restrict__ a_in,
                  const float* __restrict__ a_log, const float* __restrict__ dt_bias,
                  const float* __restrict__ norm_gamma, float* __restrict__ S,
                  float* __restrict__ conv, int slot_w, float* __restrict__ y,
-                 const float* __restrict__ z, float* __restrict__ out, int vh_lo, int nvh) {
+                 const float* __restrict__ z, float* __restrict__ out, int vh_lo, int nvh, int b0) {
     constexpr int ROWS = kHd / SPLIT;
     constexpr int PASSES = ROWS / 32;
     static_assert(PASSES >= 1, "ROWS must be a multiple of 32");
@@ -45,7 +45,7 @@ dn_decode_kernel(const float* __restrict__ qkv, const float* __restrict__ a_in,
     const int lh = blockIdx.x / SPLIT;  // head within the state's range
     const int vh = vh_lo + lh;          // model V head (inputs, params, conv channels)
     const int part = blockIdx.x % SPLIT;
-    const int b = blockIdx.y;
+    const int b = b0 + blockIdx.y;  // sequences [b0, b0 + gridDim.y) of the batch
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
@@ -233,10 +233,10 @@ dn_decode_kernel(const float* __restrict__ qkv, const float* __restrict__ a_in,
 }
 
 template <int SPLIT, bool FUSED>
-cudaError_t launch_t(cudaStream_t st, int B, const qm_dn_params* p, qm_dn_state* s,
+cudaError_t launch_t(cudaStream_t st, int b0, int nb, const qm_dn_params* p, qm_dn_state* s,
                      const float* qkv, const float* a, const float* b, float* y, const float* z,
                      float* out, int slot_w) {
-    dim3 grid(s->nvh * SPLIT, B);
+    dim3 grid(s->nvh * SPLIT, nb);
     if (FUSED && SPLIT > 1) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = grid;
@@ -251,11 +251,11 @@ cudaError_t launch_t(cudaStream_t st, int B, const qm_dn_params* p, qm_dn_state*
         cfg.numAttrs = 1;
         return cudaLaunchKernelEx(&cfg, dn_decode_kernel<SPLIT, FUSED>, qkv, a, b, p->conv_w,
                                   p->a_log, p->dt_bias, p->norm_gamma, s->s, s->conv, slot_w, y,
-                                  z, out, s->vh_lo, s->nvh);
+                                  z, out, s->vh_lo, s->nvh, b0);
     }
     dn_decode_kernel<SPLIT, FUSED><<<grid, 256, 0, st>>>(qkv, a, b, p->conv_w, p->a_log,
                                                          p->dt_bias, p->norm_gamma, s->s, s->conv,
-                                                         slot_w, y, z, out, s->vh_lo, s->nvh);
+                                                         slot_w, y, z, out, s->vh_lo, s->nvh, b0);
     return cudaGetLastError();
 }
 
@@ -268,22 +268,23 @@ int dn_decode_split_for(int units, int num_sms) {
 }
 
 cudaError_t launch_dn_decode(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, const float* qkv,
-                             const float* a, const float* b, float* y, const float* z, float* out) {
-    const int B = st->batch;
+                             const float* a, const float* b, float* y, const float* z, float* out,
+                             int b0, int nb) {
+    const int B = nb < 0 ? st->batch : nb;
     const int slot_w = (int)(st->conv_pos & 3);
     const int split = dn_decode_split_for(B * st->nvh, ctx->num_sms);
     const bool fused = (z != nullptr);
     cudaError_t e;
     TimedLaunch tl(ctx, "dn_decode");
     if (split == 1)
-        e = fused ? launch_t<1, true>(ctx->stream, B, p, st, qkv, a, b, y, z, out, slot_w)
-                  : launch_t<1, false>(ctx->stream, B, p, st, qkv, a, b, y, z, out, slot_w);
+        e = fused ? launch_t<1, true>(ctx->stream, b0, B, p, st, qkv, a, b, y, z, out, slot_w)
+                  : launch_t<1, false>(ctx->stream, b0, B, p, st, qkv, a, b, y, z, out, slot_w);
     else if (split == 2)
-        e = fused ? launch_t<2, true>(ctx->stream, B, p, st, qkv, a, b, y, z, out, slot_w)
-                  : launch_t<2, false>(ctx->stream, B, p, st, qkv, a, b, y, z, out, slot_w);
+        e = fused ? launch_t<2, true>(ctx->stream, b0, B, p, st, qkv, a, b, y, z, out, slot_w)
+                  : launch_t<2, false>(ctx->stream, b0, B, p, st, qkv, a, b, y, z, out, slot_w);
     else
-        e = fused ? launch_t<4, true>(ctx->stream, B, p, st, qkv, a, b, y, z, out, slot_w)
-                  : launch_t<4, false>(ctx->stream, B, p, st, qkv, a, b, y, z, out, slot_w);
+        e = fused ? launch_t<4, true>(ctx->stream, b0, B, p, st, qkv, a, b, y, z, out, slot_w)
+                  : launch_t<4, false>(ctx->stream, b0, B, p, st, qkv, a, b, y, z, out, slot_w);
     if (e == cudaSuccess) ctx->launches += 1;
     return e;
 }

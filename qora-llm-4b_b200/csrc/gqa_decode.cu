@@ -84,9 +84,9 @@ gqa_prep_kernel(const float* __restrict__ q_gate, const float* __restrict__ k_ne
                 const float* __restrict__ k_norm, const float* __restrict__ rope_cos,
                 const float* __restrict__ rope_sin, int64_t pos, uint16_t* __restrict__ kcache,
                 uint16_t* __restrict__ vcache, int cap, uint16_t* __restrict__ q_bf,
-                float* __restrict__ q_f32, float* __restrict__ kn_out, int kv_lo, int nkv) {
+                float* __restrict__ q_f32, float* __restrict__ kn_out, int kv_lo, int nkv, int b0) {
     // gl: KV head within the cache's range; g, h: model KV / query head (inputs)
-    const int b = blockIdx.x / nkv, gl = blockIdx.x % nkv, g = kv_lo + gl;
+    const int b = b0 + blockIdx.x / nkv, gl = blockIdx.x % nkv, g = kv_lo + gl;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool is_q = warp < kGroup;
     const int h = g * kGroup + warp;
@@ -154,14 +154,14 @@ __device__ __forceinline__ uint32_t swz_addr(uint32_t base, int pos, int dim) {
 __global__ void __launch_bounds__(160, 1)
 gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                 const uint16_t* __restrict__ q_bf, float* __restrict__ part_o,
-                float* __restrict__ part_ml, int L, int tps, int nsplit, int nkv, int* err) {
+                float* __restrict__ part_ml, int L, int tps, int nsplit, int nkv, int b0, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
     uint64_t* empty = full + kStages;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
 
-    const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int split = blockIdx.x, g = blockIdx.y, b = b0 + blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tile0 = split * tps;
     const int ntiles_all = (L + kTile - 1) / kTile;
@@ -374,8 +374,8 @@ __global__ void __launch_bounds__(256)
 gqa_combine_kernel(const float* __restrict__ q_f32, const float* __restrict__ kn,
                    const float* __restrict__ v_new, const float* __restrict__ q_gate,
                    const float* __restrict__ part_o, const float* __restrict__ part_ml, int nsplit,
-                   float* __restrict__ out, int kv_lo, int nkv) {
-    const int bh = blockIdx.x;  // local (sequence, query head) row
+                   float* __restrict__ out, int kv_lo, int nkv, int b0) {
+    const int bh = b0 * nkv * kGroup + blockIdx.x;  // (sequence, query head) row of the cache's heads
     const int nh = nkv * kGroup;
     const int b = bh / nh, hl = bh % nh, gl = hl / kGroup;
     const int h = kv_lo * kGroup + hl, g = kv_lo + gl;  // model heads (inputs)
@@ -413,19 +413,21 @@ gqa_combine_kernel(const float* __restrict__ q_f32, const float* __restrict__ kn
 
 }  // namespace
 
-size_t gqa_decode_ws_bytes(int batch, int nkv, int64_t seq_len, int num_sms) {
-    Plan p = plan_for(batch, nkv, seq_len, num_sms);
+// Workspace of a call on sequences [b0, b0 + nb) of a batch-`batch` cache
+// (nb = batch: the whole batch).
+size_t gqa_decode_ws_bytes(int batch, int nkv, int64_t seq_len, int num_sms, int nb) {
+    Plan p = plan_for(nb < 0 ? batch : nb, nkv, seq_len, num_sms);
     return ws_layout(batch, nkv, p.nsplit).total;
 }
 
 cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
                               const float* q_gate, const float* k_new, const float* v_new,
-                              float* out, void* ws, size_t ws_bytes) {
-    const int B = kv->batch;
+                              float* out, void* ws, size_t ws_bytes, int b0, int nb) {
+    const int B = nb < 0 ? kv->batch : nb;  // sequences [b0, b0 + B) of the cache
     const int64_t L = kv->seq_len;  // cached positions; the new token goes to index L
     const int nkv = kv->nkv;
     const Plan pl = plan_for(B, nkv, L, ctx->num_sms);
-    const WsLayout w = ws_layout(B, nkv, pl.nsplit);
+    const WsLayout w = ws_layout(kv->batch, nkv, pl.nsplit);  // indexed by absolute sequence
     if (w.total > ws_bytes) return cudaErrorInvalidValue;
     char* base = static_cast<char*>(ws);
     uint16_t* q_bf = reinterpret_cast<uint16_t*>(base + w.q_bf);
@@ -439,7 +441,7 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
         TimedLaunch tl(ctx, "gqa_prep");
         gqa_prep_kernel<<<B * nkv, 160, 0, st>>>(q_gate, k_new, v_new, prm->q_norm, prm->k_norm,
                                                  prm->rope_cos, prm->rope_sin, L, kv->k, kv->v,
-                                                 kv->capacity, q_bf, q_f32, kn, kv->kv_lo, nkv);
+                                                 kv->capacity, q_bf, q_f32, kn, kv->kv_lo, nkv, b0);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -455,7 +457,7 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
         dim3 grid(pl.nsplit, nkv, B);
         TimedLaunch tl(ctx, "gqa_attn");
         gqa_attn_kernel<<<grid, 160, kAttnSmem, st>>>(kv->tmap_k, kv->tmap_v, q_bf, part_o,
-                                                      part_ml, (int)L, pl.tps, pl.nsplit, nkv,
+                                                      part_ml, (int)L, pl.tps, pl.nsplit, nkv, b0,
                                                       ctx->d_err);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
@@ -464,7 +466,7 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
     {
         TimedLaunch tl(ctx, "gqa_combine");
         gqa_combine_kernel<<<B * nkv * kGroup, 256, 0, st>>>(q_f32, kn, v_new, q_gate, part_o,
-                                                             part_ml, pl.nsplit, out, kv->kv_lo, nkv);
+                                                             part_ml, pl.nsplit, out, kv->kv_lo, nkv, b0);
     }
     e = cudaGetLastError();
     if (e == cudaSuccess) ctx->launches += 1;

@@ -53,6 +53,10 @@ struct qm_ctx {
     bool timing = false;
     std::map<std::string, std::vector<std::pair<cudaEvent_t, cudaEvent_t>>> events;
     std::vector<cudaEvent_t> event_pool;
+    // copy streams and events of the pipelined _host variants (created on first use)
+    cudaStream_t copy_in = nullptr, copy_out = nullptr;
+    cudaEvent_t pipe_in[8] = {}, pipe_done[8] = {};
+    bool pipe_ready = false;
 };
 
 struct qm_dn_state {
@@ -100,12 +104,14 @@ struct TimedLaunch {
 };
 
 // Kernel launchers (return cudaError_t from the launch).
+// b0, nb: run sequences [b0, b0 + nb) of the handle's batch (nb < 0: all)
 cudaError_t launch_dn_decode(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, const float* qkv,
-                             const float* a, const float* b, float* y, const float* z, float* out);
+                             const float* a, const float* b, float* y, const float* z, float* out,
+                             int b0 = 0, int nb = -1);
 cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, const float* q_gate,
                               const float* k_new, const float* v_new, float* out, void* ws,
-                              size_t ws_bytes);
-size_t gqa_decode_ws_bytes(int batch, int nkv, int64_t seq_len, int num_sms);
+                              size_t ws_bytes, int b0 = 0, int nb = -1);
+size_t gqa_decode_ws_bytes(int batch, int nkv, int64_t seq_len, int num_sms, int nb = -1);
 cudaError_t launch_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, int T,
                                const uint16_t* q_gate, const uint16_t* k, const uint16_t* v,
                                float* out);

@@ -139,8 +139,11 @@ def test_host_variant_matches_device_variant(ctx):
                       np.ascontiguousarray(toks["a"][:, 0]), np.ascontiguousarray(toks["b"][:, 0]),
                       yh, np.ascontiguousarray(toks["z"][:, 0]), oh)
     ctx.sync()
+    # when the host variant runs the batch in overlapped parts, a head may
+    # span more CTAs, so the gated output's sum of squares can be added in
+    # another order
     np.testing.assert_array_equal(yh, host(y))
-    np.testing.assert_array_equal(oh, host(out))
+    assert refmath.rel_err(oh, host(out)) <= 1e-5
 
 
 def test_decode_argument_errors(ctx):
@@ -166,3 +169,35 @@ def test_decode_argument_errors(ctx):
     assert e.value.code == 8  # QM_E_MISMATCH
     assert st.conv_pos == 0
     other.close()
+
+
+def test_host_variant_pipelined_matches_device(ctx, orc):
+    """qm_dn_decode_host cuts a batch of 16 into parts whose copies overlap
+    the kernels; its y equals the device-buffer call's bit for bit (same
+    per-row arithmetic) and the gated output agrees to a few f32 roundings (1e-5)."""
+    import torch
+
+    import qora_mixer as qm
+
+    B = 16
+    g = I.rng(830)
+    p = I.dn_layer_params(g)
+    toks = I.dn_token_inputs(g, 2, B)
+    keep = [dev(p["conv_w"]), dev(p["a_log"]), dev(p["dt_bias"]), dev(p["norm_gamma"])]
+    prm = qm.dn_params(*keep)
+    mx = qm.Mixer(ctx)
+    st_d, st_h = qm.DnState(ctx, B), qm.DnState(ctx, B)
+    for t in range(2):
+        qkv, a, b, z = (np.ascontiguousarray(toks[k][:, t]) for k in ("qkv", "a", "b", "z"))
+        y = torch.empty(B, 32, 128, device="cuda")
+        out = torch.empty(B, 4096, device="cuda")
+        mx.dn_decode(prm, st_d, dev(qkv), dev(a), dev(b), y, dev(z), out)
+        ctx.sync()
+        yh = np.empty((B, 32, 128), np.float32)
+        oh = np.empty((B, 4096), np.float32)
+        mx.dn_decode_host(prm, st_h, qkv, a, b, yh, z, oh)
+        np.testing.assert_array_equal(yh, host(y))
+        assert refmath.rel_err(oh, host(out)) <= 1e-5
+    assert st_h.conv_pos == 2
+    for bi in (0, 7, 15):
+        np.testing.assert_array_equal(st_h.read(bi)[0], st_d.read(bi)[0])

@@ -145,3 +145,28 @@ def test_snapshot_restore_and_host_variant(ctx, orc):
     np.testing.assert_array_equal(oh, first)
     assert kvh.seq_len == 101
     snap.close()
+
+
+def test_host_variant_pipelined_batch(ctx, orc):
+    """qm_gqa_decode_host on a batch of 16 runs overlapped parts; every
+    sequence still matches the oracle and the appended rows are in place."""
+    import torch
+
+    import qora_mixer as qm
+
+    B, L = 16, 300
+    g, c, pr, cos, sin, K, V, okv, kvh, prm, keep = _setup(ctx, orc, B, L, L + 8, 840)
+    mx = qm.Mixer(ctx)
+    tok = I.gqa_token_inputs(g, B)
+    oh = np.empty((B, 16, 256), np.float32)
+    mx.gqa_decode_host(prm, kvh, np.ascontiguousarray(tok["q_gate"]), np.ascontiguousarray(tok["k_new"]),
+                       np.ascontiguousarray(tok["v_new"]), oh)
+    assert kvh.seq_len == L + 1
+    vg = host(V[:, :, L])
+    worst = 0.0
+    for bi in range(B):
+        ref = orc.gqa_decode(c, okv[bi], tok["q_gate"][bi], tok["k_new"][bi], tok["v_new"][bi],
+                             pr["q_norm"], pr["k_norm"], cos, sin)
+        worst = max(worst, refmath.rel_err(oh[bi], ref))
+        np.testing.assert_array_equal(vg[bi], I.f32_to_bf16_bits(tok["v_new"][bi]))
+    assert worst <= TOL, worst
