@@ -238,16 +238,16 @@ __device__ __forceinline__ void chunk_decays(const float* sg, float* sG, float* 
 // unit-lower-triangular inverse T of I + A (row stride kAStride floats):
 //   X_ij = sum_{k=j}^{i-1} A_ik T_kj   (kept in the unused upper block (j, i))
 //   T_ij = -T_ii X_ij                  (T_ii stored with zeros above its diagonal)
-// Each of the 128 threads owns 2 (4 - d) elements; all trip counts are
-// compile-time so the shared-memory loads issue ahead of the FMAs.
-template <int D>
+// Each of the NT threads owns (4 - d) * 256 / NT elements; all trip counts
+// are compile-time so the shared-memory loads issue ahead of the FMAs.
+template <int D, int NT>
 __device__ __forceinline__ void tri_inverse_diagonal(const float* __restrict__ A, float* __restrict__ Tm,
                                                      int tid) {
     constexpr int kStride = 68;
-    constexpr int NOUT = (4 - D) * 2;
+    constexpr int NOUT = (4 - D) * 256 / NT;
 #pragma unroll
     for (int m = 0; m < NOUT; m++) {
-        const int o = tid + 128 * m;
+        const int o = tid + NT * m;
         const int j = o >> 8, i = j + D, r = (o >> 4) & 15, c = o & 15;
         const float* arow = A + (16 * i + r) * kStride + 16 * j;
         const float* tcol = Tm + (16 * j) * kStride + 16 * j + c;
@@ -265,7 +265,7 @@ __device__ __forceinline__ void tri_inverse_diagonal(const float* __restrict__ A
     __syncthreads();
 #pragma unroll
     for (int m = 0; m < NOUT; m++) {
-        const int o = tid + 128 * m;
+        const int o = tid + NT * m;
         const int j = o >> 8, i = j + D, r = (o >> 4) & 15, c = o & 15;
         const float* trow = Tm + (16 * i + r) * kStride + 16 * i;
         const float* xcol = Tm + (16 * j) * kStride + 16 * i + c;
@@ -289,7 +289,7 @@ struct ChunkBars {
     int abort_flag;
 };
 
-// ---- 2a. chunk-local WY factors: one CTA per (V head, chunk, sequence) ----
+// ---- 2a. chunk-local WY factors: one CTA (8 warps) per (V head, chunk, sequence) ----
 //
 // Everything in a chunk that does not depend on the state entering it:
 //   MMA1  [K;Q] K^T                       (compensated)  -> A (f32) and P'
@@ -301,7 +301,8 @@ struct ChunkBars {
 // loads it with one bulk copy and reads it conflict-free), P' fp16 hi/lo
 // [64 t][64 s], and the decayed operands of the state products
 // Q~_t = e^G_t q_t (fp16) and K~_s = e^(G_63 - G_s) k_s (fp16 hi/lo), [64][128].
-// 102 KB of shared memory and 256 TMEM columns: two CTAs per SM.
+// 102 KB of shared memory and 256 TMEM columns: two CTAs per SM.  Warps w and
+// w+4 share TMEM lane quarter w%4 and split the 64 columns of every TMEM tile.
 constexpr int kL_KQh = 0;              // [K;Q] hi: 2 boxes [128 rows x 64] fp16 (K rows 0-63,
 constexpr int kL_KQl = 32768;          //   Q rows 64-127); after MMA1 the four Q quarters
 constexpr int kL_T1h = kL_KQh + 8192;  //   hold T' and T'' (hi/lo), 8 KB each
@@ -317,8 +318,9 @@ constexpr int kL_Misc = kL_Tm + 64 * kAStride * 4;  // G, beta, g, b e^G, e^G, e
 constexpr int kLocalSmem = kL_Misc + 6 * 64 * 4 + 64 + 1024;
 static_assert(kL_Vl + 16384 <= kL_Misc, "V fits over A and T");
 constexpr uint32_t kTmKQ = 0, kTmW = 64, kTmU = 128;
+constexpr int kLocalThreads = 256;
 
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(kLocalThreads, 2)
 dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ CUtensorMap tql,
                const __grid_constant__ CUtensorMap tkh, const __grid_constant__ CUtensorMap tkl,
                const __grid_constant__ CUtensorMap tvh, const __grid_constant__ CUtensorMap tvl,
@@ -343,8 +345,9 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
 
     const int vh = blockIdx.x, ci = blockIdx.y, b = blockIdx.z, qk = vh >> 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
-    const int row = tid;
+    const int quarter = warp & 3, half = warp >> 2;  // TMEM lanes 32*quarter.., columns 32*half..
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const int row = quarter * 32 + lane;              // TMEM lane = tile row
     const int t0 = ci * kC, tc = min(kC, T - t0);
     const size_t plane_qk = (size_t)b * kNumQK + qk, plane_v = (size_t)b * kNumV + vh;
     const size_t item = ((size_t)b * kNumV + vh) * nch + ci;
@@ -413,40 +416,44 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
     ok = __syncthreads_and(ok) != 0;
     tc_fence_after();
 
-    // ---- rows 0-63: A (f32, shared); rows 64-127: P' hi/lo (global) ----
+    // ---- rows 0-63: A (f32, shared); rows 64-127: P' hi/lo (global); this
+    // thread's 32 columns [s0, s0 + 32) ----
     if (ok) {
-        float kq[64];
-        tmem_ld32(tm + lane_addr + kTmKQ, kq);
-        tmem_ld32(tm + lane_addr + kTmKQ + 32, kq + 32);
+        float kq[32];
+        const int s0 = half * 32;
+        tmem_ld32(tm + lane_addr + kTmKQ + s0, kq);
         tmem_ld_wait();
         if (row < kC) {
             const int t = row;
             const float Gt = sG[t], bt = sB[t];
-            float* arow = Amat + t * kAStride;
+            float* arow = Amat + t * kAStride + s0;
 #pragma unroll
-            for (int s = 0; s < kC; s += 4) {
+            for (int i = 0; i < 32; i += 4) {
+                const int s = s0 + i;
                 float4 v;
-                v.x = (s + 0 < t) ? bt * ex2_approx(Gt - sG[s + 0]) * kq[s + 0] : 0.f;
-                v.y = (s + 1 < t) ? bt * ex2_approx(Gt - sG[s + 1]) * kq[s + 1] : 0.f;
-                v.z = (s + 2 < t) ? bt * ex2_approx(Gt - sG[s + 2]) * kq[s + 2] : 0.f;
-                v.w = (s + 3 < t) ? bt * ex2_approx(Gt - sG[s + 3]) * kq[s + 3] : 0.f;
-                *reinterpret_cast<float4*>(arow + s) = v;
+                v.x = (s + 0 < t) ? bt * ex2_approx(Gt - sG[s + 0]) * kq[i + 0] : 0.f;
+                v.y = (s + 1 < t) ? bt * ex2_approx(Gt - sG[s + 1]) * kq[i + 1] : 0.f;
+                v.z = (s + 2 < t) ? bt * ex2_approx(Gt - sG[s + 2]) * kq[i + 2] : 0.f;
+                v.w = (s + 3 < t) ? bt * ex2_approx(Gt - sG[s + 3]) * kq[i + 3] : 0.f;
+                *reinterpret_cast<float4*>(arow + i) = v;
             }
         } else {
             const int t = row - kC;
             const float Gt = sG[t];
-            uint4* hrow = reinterpret_cast<uint4*>(ph_out + (item * kC + t) * kC);
-            uint4* lrow = reinterpret_cast<uint4*>(pl_out + (item * kC + t) * kC);
+            uint4* hrow = reinterpret_cast<uint4*>(ph_out + (item * kC + t) * kC + s0);
+            uint4* lrow = reinterpret_cast<uint4*>(pl_out + (item * kC + t) * kC + s0);
 #pragma unroll
-            for (int s = 0; s < kC; s += 8) {
+            for (int i = 0; i < 32; i += 8) {
                 float p[8];
 #pragma unroll
-                for (int i = 0; i < 8; i++)
-                    p[i] = (s + i <= t) ? ex2_approx(Gt - sG[s + i]) * kq[s + i] : 0.f;
+                for (int q = 0; q < 8; q++) {
+                    const int s = s0 + i + q;
+                    p[q] = (s <= t) ? ex2_approx(Gt - sG[s]) * kq[i + q] : 0.f;
+                }
                 uint4 h, l;
                 split8(p, h, l);
-                hrow[s / 8] = h;
-                lrow[s / 8] = l;
+                hrow[i / 8] = h;
+                lrow[i / 8] = l;
             }
         }
     }
@@ -454,8 +461,8 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
     if (ok) {
         const size_t rowbase = item * kC;
 #pragma unroll 2
-        for (int m = 0; m < 8; m++) {
-            const int o = tid + 128 * m, t = o >> 4, kc = o & 15;
+        for (int m = 0; m < 1024 / kLocalThreads; m++) {
+            const int o = tid + kLocalThreads * m, t = o >> 4, kc = o & 15;
             const uint32_t off = (kc >> 3) * 16384 + sw128_off(t, kc & 7);
             float v[8];
             // Q rows sit 8 KB into each box
@@ -510,17 +517,17 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
             }
 #pragma unroll
             for (int r = 0; r < 16; r++) Tm[(o + r) * kAStride + o + c] = tc[r];
-        } else {
+        } else if (tid < 2 * kC) {
             const int t = tid - kC;
             sC1[t] = sB[t] * eG[t];
         }
         __syncthreads();
         static_assert(kAStride == 68, "tri_inverse_diagonal assumes the A/T row stride");
-        tri_inverse_diagonal<1>(Amat, Tm, tid);
-        tri_inverse_diagonal<2>(Amat, Tm, tid);
-        tri_inverse_diagonal<3>(Amat, Tm, tid);
+        tri_inverse_diagonal<1, kLocalThreads>(Amat, Tm, tid);
+        tri_inverse_diagonal<2, kLocalThreads>(Amat, Tm, tid);
+        tri_inverse_diagonal<3, kLocalThreads>(Amat, Tm, tid);
         // T' = T diag(b e^G), T'' = T diag(b) as fp16 hi/lo [t][j] tiles (upper part zero)
-        for (int o = tid; o < kC * 8; o += 128) {
+        for (int o = tid; o < kC * 8; o += kLocalThreads) {
             const int t = o >> 3, jc = o & 7, j0 = jc * 8;
             float v1[8], v2[8];
 #pragma unroll
@@ -585,23 +592,22 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
     ok = __syncthreads_and(ok && !*abort_flag) != 0;
     tc_fence_after();
 
-    // ---- outputs: W^T row k (fp16), U~^T row v (f32, [t/4][v][4]) ----
+    // ---- outputs: W^T row k (fp16), U~^T row v (f32, [t/4][v][4]); this
+    // thread's 32 tokens [32 half, 32 half + 32) ----
     if (ok) {
-        float wv[64];
-        tmem_ld32(tm + lane_addr + kTmW, wv);
-        tmem_ld32(tm + lane_addr + kTmW + 32, wv + 32);
+        float wv[32];
+        tmem_ld32(tm + lane_addr + kTmW + half * 32, wv);
         tmem_ld_wait();
-        uint4* wrow = reinterpret_cast<uint4*>(wt_out + (item * kHd + row) * kC);
+        uint4* wrow = reinterpret_cast<uint4*>(wt_out + (item * kHd + row) * kC) + half * 4;
 #pragma unroll
-        for (int t = 0; t < kC; t += 8) wrow[t / 8] = round8(wv + t);
-        float uv[64];
-        tmem_ld32(tm + lane_addr + kTmU, uv);
-        tmem_ld32(tm + lane_addr + kTmU + 32, uv + 32);
+        for (int t = 0; t < 32; t += 8) wrow[t / 8] = round8(wv + t);
+        float uv[32];
+        tmem_ld32(tm + lane_addr + kTmU + half * 32, uv);
         tmem_ld_wait();
         float4* ub = reinterpret_cast<float4*>(ut_out + item * kHd * kC);
 #pragma unroll
-        for (int t4 = 0; t4 < kC / 4; t4++)
-            ub[t4 * kHd + row] = make_float4(uv[4 * t4], uv[4 * t4 + 1], uv[4 * t4 + 2], uv[4 * t4 + 3]);
+        for (int i = 0; i < 8; i++)
+            ub[(half * 8 + i) * kHd + row] = make_float4(uv[4 * i], uv[4 * i + 1], uv[4 * i + 2], uv[4 * i + 3]);
     }
     if (tid == 0) {
         if (ld_out) mbar_drain(smem_u32(&bars->load), ld_par);
@@ -1081,7 +1087,7 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
     }
     {
         TimedLaunch tl(ctx, "dn_chunk_local");
-        dn_chunk_local<<<dim3(kNumV, nch, B), 128, kLocalSmem, s>>>(
+        dn_chunk_local<<<dim3(kNumV, nch, B), kLocalThreads, kLocalSmem, s>>>(
             m[0], m[1], m[2], m[3], m[4], m[5], g, be, T, nch, wt, ut, ph, pl, qt, kth, ktl, ctx->d_err);
     }
     e = cudaGetLastError();
