@@ -61,8 +61,9 @@ constexpr int kOffBar = kOffRed + 2 * 2 * kBM * 4;
 constexpr int kPrefillSmem = kOffBar + 256 + 1024;
 constexpr int kSoftmaxWarps = 8;              // two per TMEM lane quarter, 32 columns each
 constexpr int kAttnThreads = 64 + 32 * kSoftmaxWarps;
-constexpr int kTmS = 0;
-constexpr int kTmO = 256;
+constexpr int kTmQ = 0;    // Q as the A operand of S = Q K^T: 128 lanes x 128 columns (fp16 pairs)
+constexpr int kTmS = 128;  // S double buffer, 2 x 64 columns
+constexpr int kTmO = 256;  // O accumulator, 256 columns
 constexpr int kTmCols = 512;
 constexpr uint32_t kIdescS = umma_idesc_f16kind(kBM, kBN, false, false, false);  // fp16 x fp16
 constexpr uint32_t kIdescO = umma_idesc_f16kind(kBM, 256, false, true, false);
@@ -72,7 +73,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct Bars {
-    uint64_t q_full;
+    uint64_t q_full, q_tmem;
     uint64_t k_full[kNst], k_empty[kNst];
     uint64_t v_full[kNst], v_empty[kNst];
     uint64_t s_full[2], s_free[2];
@@ -81,6 +82,27 @@ struct Bars {
     int abort_flag;
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
+
+// Rows of a [128 x 256] fp16 tile held as 4 TMA boxes of [128 rows x 64]
+// (128-byte swizzle) -> TMEM, column col0 + d/2 of lane `row` holding dims d
+// and d+1 (the A-operand layout of tcgen05.mma); boxes [box0, box0 + nbox).
+// `taddr` is the warp's lane base plus col0.
+__device__ __forceinline__ void tile_rows_to_tmem(const uint8_t* tile, uint32_t taddr, int row, int box0,
+                                                  int nbox) {
+    for (int bi = 0; bi < nbox; bi++) {
+        const int bx = box0 + bi;
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            const uint4 w = *reinterpret_cast<const uint4*>(tile + bx * kQBox + sw128_off(row, c));
+            v[4 * c] = __uint_as_float(w.x);
+            v[4 * c + 1] = __uint_as_float(w.y);
+            v[4 * c + 2] = __uint_as_float(w.z);
+            v[4 * c + 3] = __uint_as_float(w.w);
+        }
+        tmem_st32(taddr + bx * 32, v);
+    }
+}
 
 // ---------------------------------------------------------------------------
 // 1. prep
@@ -165,6 +187,7 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
 
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(&bars->q_full), 1);
+        mbar_init(smem_u32(&bars->q_tmem), kSoftmaxWarps);
         for (int i = 0; i < kNst; i++) {
             mbar_init(smem_u32(&bars->k_full[i]), 1);
             mbar_init(smem_u32(&bars->k_empty[i]), 1);
@@ -224,16 +247,15 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
     } else if (warp == 1) {
         // ------------------------------ MMA issuer ----------------------------
         if (lane == 0) {
-            bool ok = mbar_wait_bounded(smem_u32(&bars->q_full), 0, abort_flag, err);
+            // Q reaches TMEM through the softmax warps (q_tmem)
+            bool ok = mbar_wait_bounded(smem_u32(&bars->q_tmem), 0, abort_flag, err);
             auto issue_s = [&](int j) {
                 const int st = j % kNst, sb = j & 1;
                 const uint32_t kbase = sbase + kOffK + st * kKVTile;
 #pragma unroll
-                for (int kk = 0; kk < 16; kk++) {
-                    const uint64_t ad =
-                        umma_sdesc(sbase + kOffQ + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024);
+                for (int kk = 0; kk < 16; kk++) {  // A = Q from TMEM, 16 dims = 8 columns per step
                     const uint64_t bd = umma_sdesc(kbase + (kk >> 2) * kKBox + (kk & 3) * 32, 16, 1024);
-                    umma_bf16_ss(tm + kTmS + sb * kBN, ad, bd, kIdescS, kk > 0 ? 1u : 0u);
+                    umma_f16_ts(tm + kTmS + sb * kBN, tm + kTmQ + kk * 8, bd, kIdescS, kk > 0 ? 1u : 0u);
                 }
                 umma_commit(smem_u32(&bars->s_full[sb]));
                 umma_commit(smem_u32(&bars->k_empty[st]));
@@ -288,7 +310,16 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
         float* red = reinterpret_cast<float*>(smem + kOffRed);  // [parity][half][row]
         float m_used = -INFINITY, l = 0.f;
-        bool ok = true;
+        // Q tile -> TMEM (this warp's rows, dims [128 half, 128 half + 128)), once:
+        // the S MMAs then read it from there instead of 64 KB of shared memory per key tile
+        bool ok = mbar_wait_bounded(smem_u32(&bars->q_full), 0, abort_flag, err);
+        if (ok) {
+            tile_rows_to_tmem(smem + kOffQ, tm + lane_addr + kTmQ, r, 2 * half, 2);
+            tmem_st_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bars->q_tmem));
         for (int j = 0; j < n_tiles; j++) {
             const int sb = j & 1;
             ok = ok && mbar_wait_bounded(smem_u32(&bars->s_full[sb]), (j >> 1) & 1, abort_flag, err);
@@ -424,14 +455,16 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
 
 // ---------------------------------------------------------------------------
 // Self-test of the tcgen05 building blocks (descriptors, TMEM mapping):
-//   D1[128x64]  = A[128x256] . B[64x256]^T   (K-major A and B, TMA SW128)
+//   D1[128x64]  = A[128x256] . B[64x256]^T   (K-major A and B, TMA SW128; with
+//                 mode bit 1 A is first copied to TMEM and read from there)
 //   D2[128x256] = P[128x64]  . V[64x256]      (P written by threads, V MN-major)
 // One CTA of 192 threads; same code paths as gqa_prefill_attn.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(192, 1)
 umma_selftest_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
                      const __grid_constant__ CUtensorMap tmv, const uint16_t* __restrict__ P,
-                     float* __restrict__ d1, float* __restrict__ d2, int fp16, int* err) {
+                     float* __restrict__ d1, float* __restrict__ d2, int mode, int* err) {
+    const bool fp16 = (mode & 1) != 0, a_tmem = (mode & 2) != 0;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
@@ -459,31 +492,41 @@ umma_selftest_kernel(const __grid_constant__ CUtensorMap tma, const __grid_const
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = bars->tmem_base;
+    const uint32_t qb = smem_u32(&bars->q_full);
     if (threadIdx.x == 0) {
-        const uint32_t qb = smem_u32(&bars->q_full);
         mbar_arrive_expect_tx(qb, kQBytes + 2 * kKVTile);
         for (int sub = 0; sub < 4; sub++) {
             tma_load_3d(sbase + kOffQ + sub * kQBox, &tma, sub * 64, 0, 0, qb);
             tma_load_3d(sbase + kOffK + sub * kKBox, &tmb, sub * 64, 0, 0, qb);
             tma_load_3d(sbase + kOffV + sub * kKBox, &tmv, sub * 64, 0, 0, qb);
         }
-        if (mbar_wait_bounded(qb, 0, abort_flag, err)) {
-            tc_fence_after();
-            for (int kk = 0; kk < 16; kk++)
-                umma_bf16_ss(tm + kTmS,
-                             umma_sdesc(sbase + kOffQ + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024),
-                             umma_sdesc(sbase + kOffK + (kk >> 2) * kKBox + (kk & 3) * 32, 16, 1024),
-                             fp16 ? kIdescS : kIdescS_bf, kk > 0);
-            for (int kk = 0; kk < 4; kk++)
-                umma_bf16_ss(tm + kTmO, umma_sdesc(sbase + kOffP + kk * 32, 16, 1024),
-                             umma_sdesc(sbase + kOffV + kk * 2048, kKBox, 1024),
-                             fp16 ? kIdescO : kIdescO_bf, kk > 0);
-            umma_commit(smem_u32(&bars->pv_done[0]));
-        } else {
-            bars->abort_flag = 1;
-        }
     }
-    if (warp >= 2) {
+    bool ok = mbar_wait_bounded(qb, 0, abort_flag, err);
+    if (ok && a_tmem && warp >= 2) {  // warps 2..5 own lane quarters 2, 3, 0, 1
+        const int quarter = warp & 3;
+        tile_rows_to_tmem(smem + kOffQ, tm + ((uint32_t)(quarter * 32) << 16) + kTmQ, quarter * 32 + lane, 0, 4);
+        tmem_st_wait();
+    }
+    tc_fence_before();
+    ok = __syncthreads_and(ok) != 0;
+    if (threadIdx.x == 0 && ok) {
+        tc_fence_after();
+        for (int kk = 0; kk < 16; kk++) {
+            const uint64_t bd = umma_sdesc(sbase + kOffK + (kk >> 2) * kKBox + (kk & 3) * 32, 16, 1024);
+            if (a_tmem)
+                umma_f16_ts(tm + kTmS, tm + kTmQ + kk * 8, bd, fp16 ? kIdescS : kIdescS_bf, kk > 0);
+            else
+                umma_bf16_ss(tm + kTmS,
+                             umma_sdesc(sbase + kOffQ + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024), bd,
+                             fp16 ? kIdescS : kIdescS_bf, kk > 0);
+        }
+        for (int kk = 0; kk < 4; kk++)
+            umma_bf16_ss(tm + kTmO, umma_sdesc(sbase + kOffP + kk * 32, 16, 1024),
+                         umma_sdesc(sbase + kOffV + kk * 2048, kKBox, 1024),
+                         fp16 ? kIdescO : kIdescO_bf, kk > 0);
+        umma_commit(smem_u32(&bars->pv_done[0]));
+    }
+    if (warp >= 2 && ok) {
         const int quarter = warp & 3, r = quarter * 32 + lane;
         const uint32_t la = (uint32_t)(quarter * 32) << 16;
         if (mbar_wait_bounded(smem_u32(&bars->pv_done[0]), 0, abort_flag, err)) {
@@ -588,12 +631,13 @@ extern "C" int qm_gqa_prefill(qm_ctx* c, const qm_gqa_params* p, qm_kv* kv, int 
 
 // Self-test of the tcgen05 descriptor encodings (test hook, not part of the
 // mixer ABI).  a [128x256], b [64x256], v [64x256], p [128x64] (device; all
-// bf16, or all fp16 when fp16 != 0); d1 [128x64], d2 [128x256] f32.
-// Synchronous; returns a QM status.
+// bf16, or all fp16 when mode bit 0 is set; mode bit 1: the first product
+// reads a from TMEM); d1 [128x64], d2 [128x256] f32.  Synchronous; returns a
+// QM status.
 extern "C" int qm_selftest_umma(const uint16_t* a, const uint16_t* b, const uint16_t* v,
-                                const uint16_t* p, float* d1, float* d2, int fp16) {
+                                const uint16_t* p, float* d1, float* d2, int mode) {
     CUtensorMap ta, tb, tv;
-    const bool h = fp16 != 0;
+    const bool h = (mode & 1) != 0;
     if (encode_rows_tmap(&ta, (void*)a, 256, 128, 1, 64, 128, h) != QM_OK ||
         encode_rows_tmap(&tb, (void*)b, 256, 64, 1, 64, 64, h) != QM_OK ||
         encode_rows_tmap(&tv, (void*)v, 256, 64, 1, 64, 64, h) != QM_OK)
@@ -603,7 +647,7 @@ extern "C" int qm_selftest_umma(const uint16_t* a, const uint16_t* b, const uint
     cudaMemset(err, 0, sizeof(int));
     cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kPrefillSmem);
-    umma_selftest_kernel<<<1, 192, kPrefillSmem>>>(ta, tb, tv, p, d1, d2, fp16, err);
+    umma_selftest_kernel<<<1, 192, kPrefillSmem>>>(ta, tb, tv, p, d1, d2, mode, err);
     cudaError_t e = cudaDeviceSynchronize();
     int flag = 0;
     cudaMemcpy(&flag, err, sizeof(int), cudaMemcpyDeviceToHost);

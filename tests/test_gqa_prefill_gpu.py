@@ -25,9 +25,10 @@ def ctx():
     c.close()
 
 
-@pytest.mark.parametrize("fp16", [0, 1])
-def test_tcgen05_descriptor_selftest(fp16):
-    """Q.K^T (K-major operands via TMA, 128B swizzle) and P.V (P written by
+@pytest.mark.parametrize("fp16,a_tmem", [(0, 0), (1, 0), (1, 1), (0, 1)])
+def test_tcgen05_descriptor_selftest(fp16, a_tmem):
+    """Q.K^T (K-major operands via TMA, 128B swizzle; or Q copied to TMEM and
+    read from there, as the prefill kernel does) and P.V (P written by
     threads, V MN-major) on one tile, against float64 products of the same
     bf16 (or fp16) values."""
     import torch
@@ -48,7 +49,7 @@ def test_tcgen05_descriptor_selftest(fp16):
     d2 = torch.zeros(128, 256, device="cuda")
     torch.cuda.synchronize()
     rc = fn(a.data_ptr(), b.data_ptr(), v.data_ptr(), p.data_ptr(), d1.data_ptr(), d2.data_ptr(),
-            fp16)
+            fp16 | (a_tmem << 1))
     assert rc == 0
     r1 = a.double() @ b.double().T
     r2 = p.double() @ v.double()
