@@ -18,18 +18,31 @@
 //      warp 0      TMA producer: the Q tile once, then K and V tiles of 64
 //                  positions (fp16 workspace copies) through separate 2-stage rings
 //      warp 1      TMEM owner + MMA issuer (one thread):
-//                  S_j = Q K_j^T  (M=128, N=64,  K=256: 16 x tcgen05.mma)
+//                  S_j = Q K_j^T  (M=128, N=64,  K=256: 16 x tcgen05.mma,
+//                                  A = Q read from TMEM)
 //                  O  += P_j V_j  (M=128, N=256, K=64:   4 x tcgen05.mma,
 //                                  V read MN-major straight from its [pos][dim] tile)
-//      warps 2..5  softmax: each thread owns one query row = one TMEM lane;
-//                  S is read with tcgen05.ld, P is written to shared memory
-//                  in the swizzled K-major layout the next MMA reads; the O
-//                  accumulator is rescaled in TMEM only when the running
+//      warps 2..9  softmax, two warps per TMEM lane quarter (32 score
+//                  columns each): they first copy the Q tile from shared
+//                  memory into TMEM (so the S MMAs do not re-read 64 KB of
+//                  shared memory per key tile), then per tile read S with
+//                  tcgen05.ld, exchange the row max, write P to shared memory
+//                  in the swizzled K-major layout the next MMA reads, and
+//                  rescale the O accumulator in TMEM only when the running
 //                  max grows by more than 2^8 (exact: the same stale max is
 //                  used for numerator and denominator).
-//    TMEM: S double buffer at columns [0,128), O at [256,512).
-//    S_{j+1} is issued while the softmax works on S_j.
+//    TMEM: Q at columns [0,128) (fp16 pairs), S double buffer [128,256),
+//    O [256,512).  S_{j+1} is issued while the softmax works on S_j.
 //    Epilogue: O / l * sigmoid(gate) (gemv.rs:1441-1444) written as f32.
+//
+//    Measured limit (clock64 per phase of the issuing thread, workload-3
+//    shapes): the 16 narrow S MMAs (N = 64) take ~79 cycles each against
+//    ~32 of tensor math, the 4 P.V MMAs (N = 256) ~136 against 128; a second
+//    P buffer, two interleaved S accumulators and a warp-converged issue
+//    loop each changed nothing.  Wider key tiles (N = 128) do not fit TMEM
+//    (Q 128 + S 2x128 + O 256 columns) and shared memory at head dim 256 on
+//    one SM; the two-SM form (cta_group::2, M = 256 split across a CTA
+//    pair) is the next step.
 #include <cuda_bf16.h>
 
 #include <algorithm>
