@@ -57,6 +57,12 @@ constexpr int kPrepWarps = 4;  // warps per CTA
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
+// SiLU with an approximate division (2 ulp): the prep kernel writes its
+// activations as fp16 hi + lo (22 significant bits), well above that error,
+// and the IEEE division's multi-instruction sequence was a third of its
+// special-function-unit work.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 __device__ __forceinline__ float4 bf16x4_to_f32(uint2 u) {
     return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
                        __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
@@ -123,7 +129,7 @@ dn_prefill_prep(const uint16_t* __restrict__ qkv, const float* __restrict__ a_in
             cv += h2[c] * w[c].y;
             cv += h1[c] * w[c].z;
             cv += h0[c] * w[c].w;
-            a[c] = silu_f(cv);
+            a[c] = silu_fast(cv);
         }
         x3 = x2;
         x2 = x1;
