@@ -270,7 +270,8 @@ class ShardedStack:
     over all ranks.  This rank holds V heads [vh_lo, vh_lo+nvh) of the 24
     DeltaNet layers for all B sequences, and KV heads [kv_lo, kv_lo+nkv) of
     batch part seq_part for the 8 GQA layers.  Every layer's output slice is
-    all-gathered over NCCL (qm_comm_allgather) on the mixer's stream, as
+    all-gathered (qm_comm_allgather: the peer-memory kernel once
+    qm_comm_enable_peer is on, else NCCL) on the mixer's stream, as
     out_proj / o_proj would need it."""
 
     def __init__(self, ctx, comm, plan, B, cap, ctx_len=CTX):
@@ -354,6 +355,9 @@ def bench_head_sharded(ctx, ws, rank, args):
         dist.broadcast_object_list(uid, src=0)
     comm = qm.Comm(ctx, uid[0], ws, rank, timeout_ms=120000)
     stack = ShardedStack(ctx, comm, plan, B, cap, ctx_len=args.context)
+    peer = False
+    if args.gather == "peer":
+        peer = comm.enable_peer(max(L["out"].numel() * 4 for L in stack.layers), wait_ms=10000)
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
         stack.step()
@@ -381,7 +385,8 @@ def bench_head_sharded(ctx, ws, rank, args):
             "ms_per_step": round(ms / args.steps, 4), "scaling": "strong",
             "parallelism": (f"DeltaNet V heads /{ws}, GQA KV heads /{min(ws, 4)}"
                             + (f" x batch /{ws // min(ws, 4)}" if ws > 4 else "")
-                            + ", NCCL all-gather of every layer's output"),
+                            + (", peer-memory all-gather (NVLink stores, one kernel)" if peer
+                               else ", NCCL all-gather") + " of every layer's output"),
             "allgather_bytes_per_step": gather_bytes, "gpu_launches": launches,
             "kernels_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in kt.items()}}
 
@@ -783,6 +788,8 @@ def main():
     ap.add_argument("--head-sharded", action="store_true",
                     help="also time the head-sharded variant at N=1 (always on for N>1)")
     ap.add_argument("--no-head-sharded", action="store_true")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="head-sharded all-gather: peer-memory kernel (qm_comm_enable_peer) or NCCL")
     ap.add_argument("--batch", type=int, default=B_PER_GPU, help="sequences per GPU")
     ap.add_argument("--context", type=int, default=CTX, help="cached positions per sequence")
     ap.add_argument("--cpu-tokens", type=int, default=4)

@@ -338,6 +338,19 @@ int qm_comm_create(qm_ctx* ctx, const unsigned char* id, int world, int rank, in
 /* recv[world * bytes_per_rank] = every rank's send[bytes_per_rank], in rank
  * order, on the context's stream. */
 int qm_comm_allgather(qm_comm* comm, const void* send, void* recv, size_t bytes_per_rank);
+/* Switches qm_comm_allgather to a peer-memory path for calls of at most
+ * max_bytes_per_rank bytes per rank: one kernel stores this rank's bytes
+ * straight into every other rank's gather area over NVLink (the areas are
+ * mapped once, here, through CUDA IPC) and copies the rows that arrived
+ * into recv, with no NCCL kernel and no host wait per call.  Collective:
+ * every rank calls it at the same point.  Returns QM_E_UNSUPPORTED on every
+ * rank when some rank cannot map another's memory or two ranks share a
+ * GPU; NCCL then stays in use.  A device-side wait for a peer gives up
+ * after wait_ms and sets the context's error word (qm_sync: QM_E_TIMEOUT);
+ * later calls then fail with QM_E_TIMEOUT, as the ranks are out of step.
+ * With the peer path on, qm_comm_destroy is collective too: a rank frees
+ * its area only after every rank has unmapped it. */
+int qm_comm_enable_peer(qm_comm* comm, size_t max_bytes_per_rank, int wait_ms);
 int qm_comm_destroy(qm_comm* comm);
 
 #ifdef __cplusplus

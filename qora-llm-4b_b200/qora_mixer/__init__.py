@@ -47,7 +47,8 @@ EXPORTS = [
     "qm_gqa_decode_noalloc",
     "qm_dn_state_create_heads", "qm_dn_state_wrap_heads", "qm_dn_state_heads",
     "qm_kv_create_heads", "qm_kv_wrap_heads", "qm_kv_heads",
-    "qm_shard_plan", "qm_comm_unique_id", "qm_comm_create", "qm_comm_allgather", "qm_comm_destroy",
+    "qm_shard_plan", "qm_comm_unique_id", "qm_comm_create", "qm_comm_allgather", "qm_comm_enable_peer",
+    "qm_comm_destroy",
 ]
 COMM_ID_BYTES = 128
 
@@ -148,6 +149,7 @@ def lib():
         "qm_comm_unique_id": ([P], I),
         "qm_comm_create": ([P, P, I, I, I, PP], I),
         "qm_comm_allgather": ([P, P, P, C.c_size_t], I),
+        "qm_comm_enable_peer": ([P, C.c_size_t, I], I),
         "qm_comm_destroy": ([P], I),
     }
     for name, (args, res) in sig.items():
@@ -478,6 +480,7 @@ class Comm:
         ctx.check(lib().qm_comm_create(ctx.handle, buf, int(world), int(rank), int(timeout_ms),
                                        C.byref(self._h)), "qm_comm_create")
         self.world, self.rank = world, rank
+        self.peer = False
         ctx.adopt(self)
 
     def allgather(self, send, recv):
@@ -485,6 +488,17 @@ class Comm:
         nbytes = send.numel() * send.element_size() if hasattr(send, "numel") else send.nbytes
         self.ctx.check(lib().qm_comm_allgather(self._h, _ptr(send), _ptr(recv), nbytes),
                        "qm_comm_allgather")
+
+    def enable_peer(self, max_bytes: int, wait_ms: int = 2000) -> bool:
+        """Collective: gathers of at most max_bytes per rank go through the
+        peer-memory kernel (qm_comm_enable_peer).  False when some rank cannot
+        map the others' memory (NCCL stays in use)."""
+        rc = lib().qm_comm_enable_peer(self._h, int(max_bytes), int(wait_ms))
+        if rc == 9:  # QM_E_UNSUPPORTED
+            return False
+        self.ctx.check(rc, "qm_comm_enable_peer")
+        self.peer = True
+        return True
 
     def close(self):
         if self._h:

@@ -259,3 +259,141 @@ def test_two_gpus_nccl_allgather_of_head_shards():
     for pr in procs:
         assert pr.exitcode == 0
     assert all(e <= TOL for e in res.values()), res
+
+
+# ---------------------------------------------------------------------------
+# peer-memory all-gather (qm_comm_enable_peer)
+# ---------------------------------------------------------------------------
+def _gather_cases(world, rank, torch, off_send=0, off_recv=0):
+    """(send, recv) pairs of assorted sizes; offsets make unaligned views."""
+    out = []
+    for n in (16, 4112, 131072, 300003, 2 << 20):
+        g = torch.Generator().manual_seed(n * 31 + rank)
+        sb = torch.randint(0, 256, (n + off_send,), dtype=torch.uint8, generator=g).cuda()
+        rb = torch.zeros(world * n + off_recv, dtype=torch.uint8, device="cuda")
+        out.append((sb[off_send:off_send + n], rb[off_recv:off_recv + world * n]))
+    return out
+
+
+def test_peer_allgather_single_rank(ctx):
+    """World of one: the gather kernel's own-row copy (16-byte and byte paths,
+    one to sixteen chunks) and the NCCL path above the peer size limit."""
+    import torch
+
+    import qora_mixer as qm
+
+    comm = qm.Comm(ctx, qm.comm_unique_id(), 1, 0, timeout_ms=30000)
+    try:
+        assert comm.enable_peer(1 << 20, wait_ms=1000)
+        with pytest.raises(qm.QmError):
+            comm.enable_peer(1 << 20)  # already on
+        n0 = ctx.launch_count()
+        for osend, orecv in ((0, 0), (1, 3)):
+            for send, recv in _gather_cases(1, 0, torch, osend, orecv):
+                comm.allgather(send, recv)
+                ctx.sync()
+                assert torch.equal(recv, send)
+        assert ctx.launch_count() - n0 == 8  # the two 2 MiB gathers went to NCCL
+    finally:
+        comm.close()
+
+
+def _two_gpu_peer_rank(rank, world, port, q):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (root, os.path.join(root, "qora-llm-4b_b200"), os.path.join(root, "tests")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    import qora_mixer as qm
+
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    ctx = qm.Ctx(rank, stream=torch.cuda.current_stream())
+    comm = None
+    res = {"rank": rank}
+    try:
+        uid = [qm.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = qm.Comm(ctx, uid[0], world, rank, timeout_ms=30000)
+        # NCCL results first, then the same gathers through the peer kernel
+        cases = {}
+        for osend, orecv in ((0, 0), (1, 3)):
+            for send, recv in _gather_cases(world, rank, torch, osend, orecv):
+                comm.allgather(send, recv)
+                ctx.sync()
+                cases[(osend, orecv, send.numel())] = recv.clone()
+        res["peer"] = comm.enable_peer(1 << 20, wait_ms=2000)
+        same = True
+        for rep in range(3):  # both slots, several epochs
+            for osend, orecv in ((0, 0), (1, 3)):
+                for send, recv in _gather_cases(world, rank, torch, osend, orecv):
+                    recv.zero_()
+                    comm.allgather(send, recv)
+                    ctx.sync()
+                    same &= bool(torch.equal(recv, cases[(osend, orecv, send.numel())]))
+        res["same"] = same
+        # a rank that skips one call: the other's bounded wait gives up
+        send, recv = _gather_cases(world, rank, torch)[2]
+        if rank == 0:
+            t0 = time.time()
+            comm.allgather(send, recv)
+            try:
+                ctx.sync()
+                res["timeout_code"] = 0
+            except qm.QmError as e:
+                res["timeout_code"] = e.code
+            res["waited_s"] = time.time() - t0
+            try:
+                comm.allgather(send, recv)
+                res["after_code"] = 0
+            except qm.QmError as e:
+                res["after_code"] = e.code
+        dist.barrier()
+        comm.close()  # collective with the peer path on
+        comm = None
+        q.put(res)
+    finally:
+        if comm is not None:
+            comm.close()
+        ctx.close()
+        dist.destroy_process_group()
+
+
+def test_two_gpus_peer_allgather_matches_nccl():
+    """Two GPUs: the peer-memory gather reproduces NCCL's bytes (aligned and
+    unaligned buffers, sizes 16 B .. 300 KB, both slots), sizes above the
+    limit still go to NCCL, and a rank that skips a call makes the other's
+    device-side wait give up after its limit (QM_E_TIMEOUT from qm_sync and
+    from every later call), with no GPU fault."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    mctx = mp.get_context("spawn")
+    q = mctx.Queue()
+    port = _free_port()
+    procs = [mctx.Process(target=_two_gpu_peer_rank, args=(r, world, port, q)) for r in range(world)]
+    for pr in procs:
+        pr.start()
+    for pr in procs:
+        pr.join(timeout=300)
+    res = {r["rank"]: r for r in (q.get(timeout=5) for _ in range(world))}
+    for pr in procs:
+        assert pr.exitcode == 0
+    for r in range(world):
+        assert res[r]["peer"] and res[r]["same"], res
+    assert res[0]["timeout_code"] == 6 and res[0]["after_code"] == 6, res
+    assert 1.5 < res[0]["waited_s"] < 30, res
