@@ -93,6 +93,22 @@ const char* qm_last_error(const qm_ctx* ctx);
 /* Grows the context workspace to `bytes` now, so later calls never
  * allocate (needed before capturing calls into a CUDA graph). */
 int qm_ctx_reserve(qm_ctx* ctx, size_t bytes);
+/* Number of overlapped parts the _host variants cut a batch into (part i's
+ * input copy, kernels and output copy run on three streams, so neighbouring
+ * parts overlap): dn_parts for qm_dn_decode_host, gqa_parts for
+ * qm_gqa_decode_host, 1..8, or 0 for the default (2 from batch 8 up). */
+int qm_ctx_set_host_parts(qm_ctx* ctx, int dn_parts, int gqa_parts);
+/* on != 0 (the default): when a _host call's buffers are page-locked host
+ * memory mapped into the device's address space (cudaHostAlloc,
+ * cudaHostRegister, a pinned torch tensor), each range inside its
+ * allocation, the kernels use them in place, reading inputs and writing
+ * outputs over PCIe, no staging copies and one synchronisation at the end
+ * (every buffer of the call must be mapped).  Otherwise (pageable memory)
+ * a call is staged through overlapped copies.
+ * on == 0 stages every call.  qm_ctx_host_calls counts the calls that took
+ * each path. */
+int qm_ctx_set_host_direct(qm_ctx* ctx, int on);
+int qm_ctx_host_calls(const qm_ctx* ctx, int64_t* in_place, int64_t* staged);
 /* Kernels this context launched since creation (for launch accounting). */
 int64_t qm_ctx_launch_count(const qm_ctx* ctx);
 /* Per-kernel timing: when on, every launch is bracketed by CUDA events on the

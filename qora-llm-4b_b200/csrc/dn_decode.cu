@@ -258,6 +258,7 @@ struct DnHeadIn {
     float r[6];              // history slots s0, s1, s2 of the same channels
     float4 w0, w1;           // conv taps
     float a, bb, alog, dtb;  // gate inputs (thread 255)
+    float zv;                // z of the gated epilogue (threads < 128)
 };
 
 __device__ __forceinline__ void dn_fetch_head(DnHeadIn& in, const float* __restrict__ qkv,
@@ -266,7 +267,8 @@ __device__ __forceinline__ void dn_fetch_head(DnHeadIn& in, const float* __restr
                                               const float* __restrict__ conv_w,
                                               const float* __restrict__ a_log,
                                               const float* __restrict__ dt_bias,
-                                              const float* __restrict__ conv, int b, int vh,
+                                              const float* __restrict__ conv,
+                                              const float* __restrict__ z, int b, int vh,
                                               int s0, int s1, int s2, int tid) {
     const float* x = qkv + (size_t)b * kQKVDim;
     const float* ring = conv + (size_t)b * kConvSlots * kQKVDim;
@@ -282,6 +284,8 @@ __device__ __forceinline__ void dn_fetch_head(DnHeadIn& in, const float* __restr
         in.r[3] = ring[s0 * kQKVDim + chk];
         in.r[4] = ring[s1 * kQKVDim + chk];
         in.r[5] = ring[s2 * kQKVDim + chk];
+        // fetched with the other inputs so its latency hides behind this head's work
+        in.zv = z ? z[(size_t)b * kVDim + (size_t)vh * kHd + tid] : 0.f;
     } else {
         const int chv = 2 * kQDim + vh * kHd + (tid - kHd);
         in.w0 = reinterpret_cast<const float4*>(conv_w)[chv];
@@ -356,7 +360,7 @@ dn_decode_stream(const float* __restrict__ qkv, const float* __restrict__ a_in,
     DnHeadIn cur, nxt;
     if (nk > 0) {
         const int item = blockIdx.x, b = b0 + item / nvh, vh = vh_lo + item % nvh;
-        dn_fetch_head(nxt, qkv, a_in, b_in, conv_w, a_log, dt_bias, conv, b, vh, s0, s1, s2, tid);
+        dn_fetch_head(nxt, qkv, a_in, b_in, conv_w, a_log, dt_bias, conv, z, b, vh, s0, s1, s2, tid);
     }
     bool ok = true;
     for (int k = 0; k < nk && ok; k++) {
@@ -366,7 +370,7 @@ dn_decode_stream(const float* __restrict__ qkv, const float* __restrict__ a_in,
         cur = nxt;
         if (k + 1 < nk) {  // the next head's inputs, in flight during this one
             const int it2 = item + G, b2 = b0 + it2 / nvh, vh2 = vh_lo + it2 % nvh;
-            dn_fetch_head(nxt, qkv, a_in, b_in, conv_w, a_log, dt_bias, conv, b2, vh2, s0, s1, s2, tid);
+            dn_fetch_head(nxt, qkv, a_in, b_in, conv_w, a_log, dt_bias, conv, z, b2, vh2, s0, s1, s2, tid);
         }
 
         // ---- prologue: conv1d(k=4) + SiLU + L2 norm (gemv.rs:744-785) ----
@@ -502,8 +506,7 @@ dn_decode_stream(const float* __restrict__ qkv, const float* __restrict__ a_in,
             const float inv_rms = 1.0f / sqrtf(total * (1.0f / kHd) + 1e-6f);
             if (tid < kHd) {
                 const float yn = s_y[tid] * inv_rms * norm_gamma[tid];
-                out[((size_t)b * nvh + lh) * kHd + tid] =
-                    yn * silu_f(z[(size_t)b * kVDim + (size_t)vh * kHd + tid]);
+                out[((size_t)b * nvh + lh) * kHd + tid] = yn * silu_f(cur.zv);
             }
         }
         __syncthreads();  // the buffer, s_qk, s_v, s_y are free again

@@ -422,7 +422,8 @@ size_t gqa_decode_ws_bytes(int batch, int nkv, int64_t seq_len, int num_sms, int
 
 cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
                               const float* q_gate, const float* k_new, const float* v_new,
-                              float* out, void* ws, size_t ws_bytes, int b0, int nb) {
+                              float* out, void* ws, size_t ws_bytes, int b0, int nb,
+                              const GqaCombineSrc* comb) {
     const int B = nb < 0 ? kv->batch : nb;  // sequences [b0, b0 + B) of the cache
     const int64_t L = kv->seq_len;  // cached positions; the new token goes to index L
     const int nkv = kv->nkv;
@@ -463,9 +464,19 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
         if (e != cudaSuccess) return e;
         ctx->launches += 1;
     }
+    const float* c_gate = q_gate;
+    const float* c_v = v_new;
+    if (comb) {
+        if (comb->ready) {
+            e = cudaStreamWaitEvent(st, comb->ready, 0);
+            if (e != cudaSuccess) return e;
+        }
+        c_gate = comb->q_gate ? comb->q_gate : q_gate;
+        c_v = comb->v_new ? comb->v_new : v_new;
+    }
     {
         TimedLaunch tl(ctx, "gqa_combine");
-        gqa_combine_kernel<<<B * nkv * kGroup, 256, 0, st>>>(q_f32, kn, v_new, q_gate, part_o,
+        gqa_combine_kernel<<<B * nkv * kGroup, 256, 0, st>>>(q_f32, kn, c_v, c_gate, part_o,
                                                              part_ml, pl.nsplit, out, kv->kv_lo, nkv, b0);
     }
     e = cudaGetLastError();

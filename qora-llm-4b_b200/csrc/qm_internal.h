@@ -57,6 +57,10 @@ struct qm_ctx {
     cudaStream_t copy_in = nullptr, copy_out = nullptr;
     cudaEvent_t pipe_in[8] = {}, pipe_done[8] = {};
     bool pipe_ready = false;
+    int* h_err = nullptr;           // pinned copy of the error word (pipelined calls)
+    int host_parts[2] = {0, 0};     // parts of a DeltaNet / GQA _host call (0: default)
+    bool host_direct = true;        // _host calls use page-locked buffers in place
+    int64_t host_in_place = 0, host_staged = 0;  // _host calls by path
 };
 
 struct qm_dn_state {
@@ -108,9 +112,18 @@ struct TimedLaunch {
 cudaError_t launch_dn_decode(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, const float* qkv,
                              const float* a, const float* b, float* y, const float* z, float* out,
                              int b0 = 0, int nb = -1);
+// GqaCombineSrc: where the combine kernel reads the gate half of q_gate and
+// v_new (default: the call's own q_gate / v_new), after waiting for `ready`
+// on the launch stream when it is set.
+struct GqaCombineSrc {
+    const float* q_gate = nullptr;
+    const float* v_new = nullptr;
+    cudaEvent_t ready = nullptr;
+};
 cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, const float* q_gate,
                               const float* k_new, const float* v_new, float* out, void* ws,
-                              size_t ws_bytes, int b0 = 0, int nb = -1);
+                              size_t ws_bytes, int b0 = 0, int nb = -1,
+                              const GqaCombineSrc* comb = nullptr);
 size_t gqa_decode_ws_bytes(int batch, int nkv, int64_t seq_len, int num_sms, int nb = -1);
 cudaError_t launch_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, int T,
                                const uint16_t* q_gate, const uint16_t* k, const uint16_t* v,

@@ -35,7 +35,8 @@ STATUS = {
 # Every symbol include/qora_mixer.h declares (checked by the CPU test suite).
 EXPORTS = [
     "qm_shape_get", "qm_status_string", "qm_ctx_create", "qm_ctx_destroy", "qm_ctx_set_stream",
-    "qm_ctx_get_stream", "qm_sync", "qm_last_error", "qm_ctx_reserve", "qm_ctx_launch_count",
+    "qm_ctx_get_stream", "qm_sync", "qm_last_error", "qm_ctx_reserve", "qm_ctx_set_host_parts",
+    "qm_ctx_set_host_direct", "qm_ctx_host_calls", "qm_ctx_launch_count",
     "qm_ctx_set_timing", "qm_ctx_kernel_time",
     "qm_rope_table", "qm_dn_state_create", "qm_dn_state_wrap", "qm_dn_state_destroy",
     "qm_dn_state_reset", "qm_dn_state_snapshot", "qm_dn_state_restore", "qm_dn_state_read",
@@ -106,6 +107,9 @@ def lib():
         "qm_sync": ([P], I),
         "qm_last_error": ([P], C.c_char_p),
         "qm_ctx_reserve": ([P, C.c_size_t], I),
+        "qm_ctx_set_host_parts": ([P, I, I], I),
+        "qm_ctx_set_host_direct": ([P, I], I),
+        "qm_ctx_host_calls": ([P, C.POINTER(I64), C.POINTER(I64)], I),
         "qm_ctx_launch_count": ([P], I64),
         "qm_ctx_set_timing": ([P, I], I),
         "qm_ctx_kernel_time": ([P, C.c_char_p, C.POINTER(C.c_double), C.POINTER(C.c_int64)], I),
@@ -226,6 +230,21 @@ class Ctx:
 
     def reserve(self, nbytes):
         self.check(lib().qm_ctx_reserve(self._h, int(nbytes)), "reserve")
+
+    def set_host_parts(self, dn_parts=0, gqa_parts=0):
+        """Overlapped parts of the _host variants (0: default)."""
+        self.check(lib().qm_ctx_set_host_parts(self._h, int(dn_parts), int(gqa_parts)),
+                   "set_host_parts")
+
+    def set_host_direct(self, on=True):
+        """_host calls on page-locked buffers run the kernels on them in place."""
+        self.check(lib().qm_ctx_set_host_direct(self._h, int(bool(on))), "set_host_direct")
+
+    def host_calls(self):
+        """(in-place, staged) counts of the _host calls made on this context."""
+        a, b = C.c_int64(), C.c_int64()
+        self.check(lib().qm_ctx_host_calls(self._h, C.byref(a), C.byref(b)), "host_calls")
+        return a.value, b.value
 
     def launch_count(self) -> int:
         return int(lib().qm_ctx_launch_count(self._h))

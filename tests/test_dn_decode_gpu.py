@@ -201,3 +201,68 @@ def test_host_variant_pipelined_matches_device(ctx, orc):
     assert st_h.conv_pos == 2
     for bi in (0, 7, 15):
         np.testing.assert_array_equal(st_h.read(bi)[0], st_d.read(bi)[0])
+
+
+def _pinned(a):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+
+
+def test_host_variant_in_place_on_pinned_buffers(ctx, orc):
+    """Page-locked host buffers: qm_dn_decode_host runs one kernel launch on
+    them in place (inputs read and outputs written over PCIe) and matches the
+    device-buffer call bit for bit and the oracle within 1e-3; with the
+    in-place path switched off, or with one pageable buffer among pinned
+    ones, the same call is staged through copies in two parts."""
+    import torch
+
+    import qora_mixer as qm
+
+    B, T = 16, 3
+    g = I.rng(850)
+    p = I.dn_layer_params(g)
+    toks = I.dn_token_inputs(g, T, B)
+    keep = [dev(p["conv_w"]), dev(p["a_log"]), dev(p["dt_bias"]), dev(p["norm_gamma"])]
+    prm = qm.dn_params(*keep)
+    mx = qm.Mixer(ctx)
+    st_d, st_h = qm.DnState(ctx, B), qm.DnState(ctx, B)
+    c = orc.cfg_4b()
+    ost = [orc.DnState(c) for _ in range(B)]
+    try:
+        for t in range(T):
+            qkv, a, b, z = (np.ascontiguousarray(toks[k][:, t]) for k in ("qkv", "a", "b", "z"))
+            y = torch.empty(B, 32, 128, device="cuda")
+            out = torch.empty(B, 4096, device="cuda")
+            mx.dn_decode(prm, st_d, dev(qkv), dev(a), dev(b), y, dev(z), out)
+            ctx.sync()
+            yh = torch.empty(B, 32, 128).pin_memory()
+            oh = torch.empty(B, 4096).pin_memory()
+            ins = [_pinned(x) for x in (qkv, a, b, z)]
+            if t == 1:
+                ctx.set_host_direct(False)
+            if t == 2:
+                ins[3] = z  # one pageable buffer: staged
+            n0, c0 = ctx.launch_count(), ctx.host_calls()
+            mx.dn_decode_host(prm, st_h, ins[0], ins[1], ins[2], yh, ins[3], oh)
+            c1 = ctx.host_calls()
+            assert ctx.launch_count() - n0 == (1 if t == 0 else 2)
+            assert (c1[0] - c0[0], c1[1] - c0[1]) == ((1, 0) if t == 0 else (0, 1))
+            ctx.set_host_direct(True)
+            np.testing.assert_array_equal(yh.numpy(), host(y))
+            if t == 0:
+                np.testing.assert_array_equal(oh.numpy(), host(out))
+            else:
+                assert refmath.rel_err(oh.numpy(), host(out)) <= 1e-5
+            for bi in range(B):
+                yo, go = orc.dn_decode(c, ost[bi], qkv[bi], a[bi], b[bi], p["conv_w"], p["a_log"],
+                                       p["dt_bias"], use_avx512=False, z=z[bi],
+                                       norm_gamma=p["norm_gamma"])
+                assert refmath.rel_err(yh.numpy()[bi], yo) <= TOL
+                assert refmath.rel_err(oh.numpy()[bi], go) <= TOL
+        assert st_h.conv_pos == T
+        for bi in (0, 15):
+            np.testing.assert_array_equal(st_h.read(bi)[0], st_d.read(bi)[0])
+            np.testing.assert_array_equal(st_h.read(bi)[1], st_d.read(bi)[1])
+    finally:
+        ctx.set_host_direct(True)

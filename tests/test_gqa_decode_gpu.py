@@ -170,3 +170,46 @@ def test_host_variant_pipelined_batch(ctx, orc):
         worst = max(worst, refmath.rel_err(oh[bi], ref))
         np.testing.assert_array_equal(vg[bi], I.f32_to_bf16_bits(tok["v_new"][bi]))
     assert worst <= TOL, worst
+
+
+def test_host_variant_in_place_on_pinned_buffers(ctx, orc):
+    """Page-locked host buffers: qm_gqa_decode_host runs the prep / attention
+    / combine launches on them in place and matches the device-buffer call
+    bit for bit; switched off, the same call is staged in two parts."""
+    import torch
+
+    import qora_mixer as qm
+
+    B, L = 16, 200
+    g, c, pr, cos, sin, K, V, okv, kvh, prm, keep = _setup(ctx, orc, B, L, L + 8, 860)
+    K2, V2 = K.clone(), V.clone()
+    kvd = qm.KvCache(ctx, B, L + 8, K2, V2)
+    kvd.seq_len = L
+    mx = qm.Mixer(ctx)
+    try:
+        for t, direct in enumerate((True, False)):
+            tok = I.gqa_token_inputs(g, B)
+            out = torch.empty(B, 16, 256, device="cuda")
+            mx.gqa_decode(prm, kvd, dev(tok["q_gate"]), dev(tok["k_new"]), dev(tok["v_new"]), out)
+            ctx.sync()
+            ins = [torch.from_numpy(np.ascontiguousarray(tok[k])).pin_memory()
+                   for k in ("q_gate", "k_new", "v_new")]
+            oh = torch.empty(B, 16, 256).pin_memory()
+            ctx.set_host_direct(direct)
+            n0, c0 = ctx.launch_count(), ctx.host_calls()
+            mx.gqa_decode_host(prm, kvh, *ins, oh)
+            n, c1 = ctx.launch_count() - n0, ctx.host_calls()
+            ctx.set_host_direct(True)
+            assert (c1[0] - c0[0], c1[1] - c0[1]) == ((1, 0) if direct else (0, 1))
+            n_dev = 3  # prep, attention, combine
+            assert n == (n_dev if direct else 2 * n_dev), n
+            if direct:
+                np.testing.assert_array_equal(oh.numpy(), host(out))
+            else:
+                assert refmath.rel_err(oh.numpy(), host(out)) <= TOL
+            assert kvh.seq_len == L + 1 + t
+            np.testing.assert_array_equal(host(V[:, :, L + t]), host(V2[:, :, L + t]))
+            np.testing.assert_array_equal(host(K[:, :, L + t]), host(K2[:, :, L + t]))
+    finally:
+        ctx.set_host_direct(True)
+        kvd.close()
