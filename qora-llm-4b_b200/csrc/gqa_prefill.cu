@@ -14,35 +14,41 @@
 //    it near 1e-2.  fp16 holds these values with room to spare (|q/16| and
 //    |k| stay below ~40, v below 65504 — larger v saturates).
 // 2. gqa_prefill_attn  (one CTA per (sequence, head, 128-query tile)):
-//    flash attention, causal, online softmax in base 2.
-//      warp 0      TMA producer: the Q tile once, then K and V tiles of 64
-//                  positions (fp16 workspace copies) through separate 2-stage rings
+//    flash attention, causal, online softmax in base 2, 128-key tiles.
+//      warp 0      TMA producer: one ring of 11 x 16 KB slots, filled in the
+//                  order the consumers take them: the Q tile (4 slots), then
+//                  K_0, and per tile j K_{j+1} ([128 keys x 64 dims] per slot)
+//                  and V_j ([32 keys x 256 dims] per slot)
 //      warp 1      TMEM owner + MMA issuer (one thread):
-//                  S_j = Q K_j^T  (M=128, N=64,  K=256: 16 x tcgen05.mma,
+//                  S_j = Q K_j^T  (M=128, N=128, K=256: 16 x tcgen05.mma,
 //                                  A = Q read from TMEM)
-//                  O  += P_j V_j  (M=128, N=256, K=64:   4 x tcgen05.mma,
-//                                  V read MN-major straight from its [pos][dim] tile)
-//      warps 2..9  softmax, two warps per TMEM lane quarter (32 score
-//                  columns each): they first copy the Q tile from shared
-//                  memory into TMEM (so the S MMAs do not re-read 64 KB of
+//                  O  += P_j V_j  (M=128, N=256, K=128:  8 x tcgen05.mma,
+//                                  V read MN-major straight from its [pos][dim] boxes)
+//                  in the order S_0, S_1, PV_0, S_2, PV_1, ...: while the
+//                  softmax works on S_j, the tensor pipe runs S_{j+1} and PV_{j-1}
+//      warps 2..9  softmax, two warps per TMEM lane quarter (64 score
+//                  columns each): they first copy the Q tile from its ring
+//                  slots into TMEM (so the S MMAs do not re-read 64 KB of
 //                  shared memory per key tile), then per tile read S with
 //                  tcgen05.ld, exchange the row max, write P to shared memory
 //                  in the swizzled K-major layout the next MMA reads, and
 //                  rescale the O accumulator in TMEM only when the running
 //                  max grows by more than 2^8 (exact: the same stale max is
 //                  used for numerator and denominator).
-//    TMEM: Q at columns [0,128) (fp16 pairs), S double buffer [128,256),
-//    O [256,512).  S_{j+1} is issued while the softmax works on S_j.
+//    TMEM: Q at columns [0,128) (fp16 pairs), S [128,256) (one buffer: S_{j+1}
+//    is issued once the softmax warps hold S_j in registers), O [256,512).
 //    Epilogue: O / l * sigmoid(gate) (gemv.rs:1441-1444) written as f32.
 //
-//    Measured limit (clock64 per phase of the issuing thread, workload-3
-//    shapes): the 16 narrow S MMAs (N = 64) take ~79 cycles each against
-//    ~32 of tensor math, the 4 P.V MMAs (N = 256) ~136 against 128; a second
-//    P buffer, two interleaved S accumulators and a warp-converged issue
-//    loop each changed nothing.  Wider key tiles (N = 128) do not fit TMEM
-//    (Q 128 + S 2x128 + O 256 columns) and shared memory at head dim 256 on
-//    one SM; the two-SM form (cta_group::2, M = 256 split across a CTA
-//    pair) is the next step.
+//    Why 128-key tiles: a tcgen05.mma of M = 128, K = 16 costs ~68 cycles at
+//    N = 64 and at N = 128 alike (N = 256: 128, the math rate), so the
+//    earlier 64-key tiles ran S = Q K^T at half rate (871 -> 1,001 TFLOP/s on
+//    workload 3).  Measured limit now (clock64 per phase of the issuing
+//    thread): the S MMAs take ~90 cycles and the P.V MMAs ~158 in the kernel
+//    (68 and 128 alone), and ~20 % of the time the issuer waits for K/V
+//    chunks — shared memory (ring 176 KB + P 32 KB) and TMEM (all 512
+//    columns) are both full at head dim 256 on one SM.  The two-SM form
+//    (cta_group::2, each CTA of a pair holding half of every K/V tile) is
+//    the next step.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -58,43 +64,57 @@ int encode_rows_tmap(CUtensorMap* m, void* base, uint64_t inner, uint64_t rows, 
 namespace {
 
 constexpr int kBM = 128;                   // query rows per CTA (UMMA M)
-constexpr int kBN = 64;                    // key positions per tile
-constexpr int kQBox = kBM * 128;           // [128 rows x 64 dims] bf16 = 16 KB
-constexpr int kKBox = kBN * 128;           // [64 rows x 64 dims] bf16 = 8 KB
-constexpr int kQBytes = 4 * kQBox;         // 64 KB
-constexpr int kKVTile = 4 * kKBox;         // 32 KB
-constexpr int kPBytes = kBM * 128;         // [128 x 64] bf16 = 16 KB
-constexpr int kNst = 2;
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kQBytes;
-constexpr int kOffV = kOffK + kNst * kKVTile;
-constexpr int kOffP = kOffV + kNst * kKVTile;
+constexpr int kBN = 128;                   // key positions per tile (UMMA N of S = Q K^T)
+constexpr int kQBox = kBM * 128;           // [128 rows x 64 dims] fp16 = 16 KB
+constexpr int kSlot = 16384;               // one ring slot
+constexpr int kRing = 11;                  // ring slots (176 KB)
+constexpr int kVBox = 32 * 128;            // [32 keys x 64 dims] fp16 = 4 KB
+constexpr int kPBox = kBM * 128;           // [128 rows x 64 keys] fp16 = 16 KB
+constexpr int kPBytes = 2 * kPBox;         // P tile [128 x 128]
+constexpr int kOffRing = 0;
+constexpr int kOffP = kOffRing + kRing * kSlot;
 constexpr int kOffRed = kOffP + kPBytes;      // row-max / row-sum exchange [2][2][128] f32
 constexpr int kOffBar = kOffRed + 2 * 2 * kBM * 4;
 constexpr int kPrefillSmem = kOffBar + 256 + 1024;
-constexpr int kSoftmaxWarps = 8;              // two per TMEM lane quarter, 32 columns each
+static_assert(kPrefillSmem <= 232448, "shared memory per CTA");
+constexpr int kSoftmaxWarps = 8;              // two per TMEM lane quarter, 64 columns each
 constexpr int kAttnThreads = 64 + 32 * kSoftmaxWarps;
 constexpr int kTmQ = 0;    // Q as the A operand of S = Q K^T: 128 lanes x 128 columns (fp16 pairs)
-constexpr int kTmS = 128;  // S double buffer, 2 x 64 columns
+constexpr int kTmS = 128;  // S, 128 columns (one buffer: S_{j+1} is issued once S_j is in registers)
 constexpr int kTmO = 256;  // O accumulator, 256 columns
 constexpr int kTmCols = 512;
 constexpr uint32_t kIdescS = umma_idesc_f16kind(kBM, kBN, false, false, false);  // fp16 x fp16
 constexpr uint32_t kIdescO = umma_idesc_f16kind(kBM, 256, false, true, false);
-constexpr uint32_t kIdescS_bf = umma_idesc_bf16(kBM, kBN, false, false);         // self-test
-constexpr uint32_t kIdescO_bf = umma_idesc_bf16(kBM, 256, false, true);
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct Bars {
-    uint64_t q_full, q_tmem;
-    uint64_t k_full[kNst], k_empty[kNst];
-    uint64_t v_full[kNst], v_empty[kNst];
-    uint64_t s_full[2], s_free[2];
-    uint64_t p_full[2], pv_done[2];
+    uint64_t full[kRing], empty[kRing];  // ring slots: TMA landed / MMAs done reading
+    uint64_t q_tmem;                     // Q copied into TMEM (softmax warps)
+    uint64_t s_full, s_free;             // S_j in TMEM / S_j read into registers
+    uint64_t p_full, pv_done;            // P_j in shared memory / O += P_j V_j done
     uint32_t tmem_base;
     int abort_flag;
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
+
+// Self-test layout (umma_selftest_kernel): one 64-key tile of each operand.
+constexpr int kStKBox = 64 * 128;                 // [64 rows x 64 dims] = 8 KB
+constexpr int kStOffQ = 0;
+constexpr int kStOffK = kStOffQ + 4 * kQBox;
+constexpr int kStOffV = kStOffK + 4 * kStKBox;
+constexpr int kStOffP = kStOffV + 4 * kStKBox;
+constexpr int kStOffBar = kStOffP + kBM * 128;
+constexpr int kStSmem = kStOffBar + 256 + 1024;
+constexpr int kStTmS = 128;
+constexpr uint32_t kStIdescS = umma_idesc_f16kind(kBM, 64, false, false, false);
+constexpr uint32_t kStIdescS_bf = umma_idesc_bf16(kBM, 64, false, false);
+constexpr uint32_t kStIdescO_bf = umma_idesc_bf16(kBM, 256, false, true);
+struct StBars {
+    uint64_t ld_full, mma_done;
+    uint32_t tmem_base;
+    int abort_flag;
+};
 
 // Rows of a [128 x 256] fp16 tile held as 4 TMA boxes of [128 rows x 64]
 // (128-byte swizzle) -> TMEM, column col0 + d/2 of lane `row` holding dims d
@@ -178,6 +198,12 @@ gqa_prefill_prep(const uint16_t* __restrict__ q_gate, const uint16_t* __restrict
 // ---------------------------------------------------------------------------
 // 2. flash attention
 // ---------------------------------------------------------------------------
+// Shared memory holds a ring of 16 KB slots that the TMA producer fills in
+// the order the consumers take them: the Q tile (4 slots, copied into TMEM by
+// the softmax warps and released), then K_0, and for each tile j: K_{j+1}
+// (4 slots of [128 keys x 64 dims]) and V_j (4 slots of [32 keys x 256 dims],
+// each as 4 boxes of [32 x 64]) — the issue order S_0, S_1, PV_0, S_2, PV_1,
+// ...  Slot n of the sequence is slot n % kRing, phase (n / kRing) & 1.
 __global__ void __launch_bounds__(kAttnThreads, 1)
 gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                  const __grid_constant__ CUtensorMap tmv, const uint16_t* __restrict__ q_gate,
@@ -187,6 +213,7 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
     Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
     volatile int* abort_flag = &bars->abort_flag;
     const uint32_t sbase = smem_u32(smem);
+    const uint32_t ring = sbase + kOffRing;
 
     // heaviest query tiles first; the 16 heads of one tile are adjacent so the
     // 4 heads of a KV group read the same K/V tiles from L2
@@ -196,23 +223,18 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
     const int g = h / kGroup;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q0 = qt * kBM;
-    const int n_tiles = min((q0 + kBM - 1) / kBN + 1, (T + kBN - 1) / kBN);
+    const int n_tiles = min(qt + 1, (T + kBN - 1) / kBN);  // kBM == kBN: tile qt holds the diagonal
 
     if (threadIdx.x == 0) {
-        mbar_init(smem_u32(&bars->q_full), 1);
+        for (int i = 0; i < kRing; i++) {
+            mbar_init(smem_u32(&bars->full[i]), 1);
+            mbar_init(smem_u32(&bars->empty[i]), 1);
+        }
         mbar_init(smem_u32(&bars->q_tmem), kSoftmaxWarps);
-        for (int i = 0; i < kNst; i++) {
-            mbar_init(smem_u32(&bars->k_full[i]), 1);
-            mbar_init(smem_u32(&bars->k_empty[i]), 1);
-            mbar_init(smem_u32(&bars->v_full[i]), 1);
-            mbar_init(smem_u32(&bars->v_empty[i]), 1);
-        }
-        for (int i = 0; i < 2; i++) {
-            mbar_init(smem_u32(&bars->s_full[i]), 1);
-            mbar_init(smem_u32(&bars->s_free[i]), kSoftmaxWarps);
-            mbar_init(smem_u32(&bars->p_full[i]), kSoftmaxWarps);
-            mbar_init(smem_u32(&bars->pv_done[i]), 1);
-        }
+        mbar_init(smem_u32(&bars->s_full), 1);
+        mbar_init(smem_u32(&bars->s_free), kSoftmaxWarps);
+        mbar_init(smem_u32(&bars->p_full), kSoftmaxWarps);
+        mbar_init(smem_u32(&bars->pv_done), 1);
         bars->abort_flag = 0;
         fence_barrier_init();
     }
@@ -231,143 +253,176 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
             prefetch_tmap(&tmq);
             prefetch_tmap(&tmk);
             prefetch_tmap(&tmv);
-            const uint32_t qb = smem_u32(&bars->q_full);
-            mbar_arrive_expect_tx(qb, kQBytes);
-            for (int sub = 0; sub < 4; sub++)
-                tma_load_3d(sbase + kOffQ + sub * kQBox, &tmq, sub * 64, q0, b * kNumH + h, qb);
             const int zc = b * kNumKVH + g;
-            int j = 0;
-            for (; j < n_tiles; j++) {
-                const int st = j % kNst, r = j / kNst;
-                if (r > 0 && !mbar_wait_bounded(smem_u32(&bars->k_empty[st]), (r - 1) & 1,
-                                                abort_flag, err))
-                    break;
-                const uint32_t kf = smem_u32(&bars->k_full[st]);
-                mbar_arrive_expect_tx(kf, kKVTile);
-                for (int sub = 0; sub < 4; sub++)
-                    tma_load_3d(sbase + kOffK + st * kKVTile + sub * kKBox, &tmk, sub * 64,
-                                j * kBN, zc, kf);
-                if (r > 0 && !mbar_wait_bounded(smem_u32(&bars->v_empty[st]), (r - 1) & 1,
-                                                abort_flag, err))
-                    break;
-                const uint32_t vf = smem_u32(&bars->v_full[st]);
-                mbar_arrive_expect_tx(vf, kKVTile);
-                for (int sub = 0; sub < 4; sub++)
-                    tma_load_3d(sbase + kOffV + st * kKVTile + sub * kKBox, &tmv, sub * 64,
-                                j * kBN, zc, vf);
+            int n = 0;
+            bool ok = true;
+            // slot of chunk n, once the chunk kRing places earlier has been released
+            auto claim = [&](int& slot) -> bool {
+                slot = n % kRing;
+                if (n >= kRing && !mbar_wait_bounded(smem_u32(&bars->empty[slot]), ((n / kRing) - 1) & 1,
+                                                     abort_flag, err))
+                    return false;
+                mbar_arrive_expect_tx(smem_u32(&bars->full[slot]), kSlot);
+                return true;
+            };
+            for (int sub = 0; sub < 4; sub++) {  // Q: chunks 0..3 (slots 0..3, contiguous)
+                int slot;
+                claim(slot);
+                tma_load_3d(ring + slot * kSlot, &tmq, sub * 64, q0, b * kNumH + h,
+                            smem_u32(&bars->full[slot]));
+                n++;
+            }
+            auto load_k = [&](int j) {
+                for (int c = 0; c < 4 && ok; c++) {
+                    int slot;
+                    if (!(ok = claim(slot))) break;
+                    tma_load_3d(ring + slot * kSlot, &tmk, c * 64, j * kBN, zc, smem_u32(&bars->full[slot]));
+                    n++;
+                }
+            };
+            auto load_v = [&](int j) {
+                for (int c = 0; c < 4 && ok; c++) {
+                    int slot;
+                    if (!(ok = claim(slot))) break;
+                    for (int d = 0; d < 4; d++)
+                        tma_load_3d(ring + slot * kSlot + d * kVBox, &tmv, d * 64, j * kBN + c * 32, zc,
+                                    smem_u32(&bars->full[slot]));
+                    n++;
+                }
+            };
+            load_k(0);
+            for (int j = 0; j < n_tiles && ok; j++) {
+                if (j + 1 < n_tiles) load_k(j + 1);
+                load_v(j);
             }
         }
     } else if (warp == 1) {
         // ------------------------------ MMA issuer ----------------------------
         if (lane == 0) {
-            // Q reaches TMEM through the softmax warps (q_tmem)
+            int n = 4;  // chunks 0..3 held Q
+            // Q reaches TMEM through the softmax warps (q_tmem); its slots are then free
             bool ok = mbar_wait_bounded(smem_u32(&bars->q_tmem), 0, abort_flag, err);
-            auto issue_s = [&](int j) {
-                const int st = j % kNst, sb = j & 1;
-                const uint32_t kbase = sbase + kOffK + st * kKVTile;
-#pragma unroll
-                for (int kk = 0; kk < 16; kk++) {  // A = Q from TMEM, 16 dims = 8 columns per step
-                    const uint64_t bd = umma_sdesc(kbase + (kk >> 2) * kKBox + (kk & 3) * 32, 16, 1024);
-                    umma_f16_ts(tm + kTmS + sb * kBN, tm + kTmQ + kk * 8, bd, kIdescS, kk > 0 ? 1u : 0u);
-                }
-                umma_commit(smem_u32(&bars->s_full[sb]));
-                umma_commit(smem_u32(&bars->k_empty[st]));
-            };
-            if (ok) ok = mbar_wait_bounded(smem_u32(&bars->k_full[0]), 0, abort_flag, err);
-            if (ok) {
+            if (ok)
+                for (int i = 0; i < 4; i++) mbar_arrive(smem_u32(&bars->empty[i]));
+            auto take = [&](int& slot) -> bool {
+                slot = n % kRing;
+                if (!mbar_wait_bounded(smem_u32(&bars->full[slot]), (n / kRing) & 1, abort_flag, err))
+                    return false;
                 tc_fence_after();
-                issue_s(0);
-            }
+                return true;
+            };
+            // S_j = Q K_j^T: 16 MMAs (K = 16 dims each), A = Q from TMEM
+            auto issue_s = [&]() -> bool {
+                for (int c = 0; c < 4; c++) {
+                    int slot;
+                    if (!take(slot)) return false;
+#pragma unroll
+                    for (int k4 = 0; k4 < 4; k4++) {
+                        const int kk = c * 4 + k4;
+                        const uint64_t bd = umma_sdesc(ring + slot * kSlot + k4 * 32, 16, 1024);
+                        umma_f16_ts(tm + kTmS, tm + kTmQ + kk * 8, bd, kIdescS, kk > 0 ? 1u : 0u);
+                    }
+                    umma_commit(smem_u32(&bars->empty[slot]));
+                    n++;
+                }
+                umma_commit(smem_u32(&bars->s_full));
+                return true;
+            };
+            // O += P_j V_j: 8 MMAs (K = 16 keys each), P from shared memory,
+            // V read MN-major from its [key][dim] boxes
+            auto issue_pv = [&](int j) -> bool {
+                if (!mbar_wait_bounded(smem_u32(&bars->p_full), j & 1, abort_flag, err)) return false;
+                tc_fence_after();
+                const uint32_t pbase = sbase + kOffP;
+                for (int c = 0; c < 4; c++) {
+                    int slot;
+                    if (!take(slot)) return false;
+#pragma unroll
+                    for (int k2 = 0; k2 < 2; k2++) {
+                        const int kk = c * 2 + k2;
+                        const uint64_t ad = umma_sdesc(pbase + (kk >> 2) * kPBox + (kk & 3) * 32, 16, 1024);
+                        const uint64_t bd = umma_sdesc(ring + slot * kSlot + k2 * 2048, kVBox, 1024);
+                        umma_bf16_ss(tm + kTmO, ad, bd, kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(smem_u32(&bars->empty[slot]));
+                    n++;
+                }
+                umma_commit(smem_u32(&bars->pv_done));
+                return true;
+            };
+            if (ok) ok = issue_s();
             for (int j = 0; ok && j < n_tiles; j++) {
                 if (j + 1 < n_tiles) {
-                    const int jn = j + 1;
-                    ok = mbar_wait_bounded(smem_u32(&bars->k_full[jn % kNst]), (jn / kNst) & 1,
-                                           abort_flag, err);
-                    if (ok && jn >= 2)
-                        ok = mbar_wait_bounded(smem_u32(&bars->s_free[jn & 1]), ((jn - 2) >> 1) & 1,
-                                               abort_flag, err);
-                    if (!ok) break;
-                    tc_fence_after();
-                    issue_s(jn);
+                    // S_{j+1} overwrites S_j: wait until the softmax warps hold S_j in registers
+                    ok = mbar_wait_bounded(smem_u32(&bars->s_free), j & 1, abort_flag, err);
+                    if (ok) ok = issue_s();
                 }
-                const int st = j % kNst, pb = j & 1;
-                ok = mbar_wait_bounded(smem_u32(&bars->p_full[pb]), (j >> 1) & 1, abort_flag, err);
-                if (ok) ok = mbar_wait_bounded(smem_u32(&bars->v_full[st]), (j / kNst) & 1, abort_flag, err);
-                if (!ok) break;
-                tc_fence_after();
-                const uint32_t vbase = sbase + kOffV + st * kKVTile;
-                const uint32_t pbase = sbase + kOffP;
-#pragma unroll
-                for (int kk = 0; kk < 4; kk++) {
-                    const uint64_t ad = umma_sdesc(pbase + kk * 32, 16, 1024);
-                    const uint64_t bd = umma_sdesc(vbase + kk * 2048, kKBox, 1024);
-                    umma_bf16_ss(tm + kTmO, ad, bd, kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
-                }
-                umma_commit(smem_u32(&bars->pv_done[pb]));
-                umma_commit(smem_u32(&bars->v_empty[st]));
+                if (ok) ok = issue_pv(j);
             }
         }
     } else {
         // ------------------------------ softmax (warps 2..9) -----------------
         // Two warps per TMEM lane quarter: warp w reads lanes 32*(w%4).. and
-        // half (w-2)/4 of the 64 score columns.  The row max is exchanged
+        // half (w-2)/4 of the 128 score columns.  The row max is exchanged
         // through shared memory (parity double buffer, one named barrier of
         // the quarter's 64 threads per tile); row sums stay per half until
         // the epilogue.  Both halves see the same row max, so they take the
         // same rescale decisions.
         const int quarter = warp & 3;             // TMEM lanes 32*quarter .. +31
-        const int half = (warp - 2) >> 2;         // score columns [32*half, 32*half+32)
+        const int half = (warp - 2) >> 2;         // score columns [64*half, 64*half+64)
         const int r = quarter * 32 + lane;        // query row within the tile
         const int qp = q0 + r;                    // query position
         const int bar_id = 1 + quarter;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
         float* red = reinterpret_cast<float*>(smem + kOffRed);  // [parity][half][row]
         float m_used = -INFINITY, l = 0.f;
-        // Q tile -> TMEM (this warp's rows, dims [128 half, 128 half + 128)), once:
-        // the S MMAs then read it from there instead of 64 KB of shared memory per key tile
-        bool ok = mbar_wait_bounded(smem_u32(&bars->q_full), 0, abort_flag, err);
+        // Q tile (ring slots 0..3) -> TMEM, this warp's rows and dims
+        // [128 half, 128 half + 128), once: the S MMAs read it from there
+        bool ok = mbar_wait_bounded(smem_u32(&bars->full[2 * half]), 0, abort_flag, err);
+        ok = ok && mbar_wait_bounded(smem_u32(&bars->full[2 * half + 1]), 0, abort_flag, err);
         if (ok) {
-            tile_rows_to_tmem(smem + kOffQ, tm + lane_addr + kTmQ, r, 2 * half, 2);
+            tile_rows_to_tmem(smem + kOffRing, tm + lane_addr + kTmQ, r, 2 * half, 2);
             tmem_st_wait();
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&bars->q_tmem));
         for (int j = 0; j < n_tiles; j++) {
-            const int sb = j & 1;
-            ok = ok && mbar_wait_bounded(smem_u32(&bars->s_full[sb]), (j >> 1) & 1, abort_flag, err);
-            float s[32];
+            ok = ok && mbar_wait_bounded(smem_u32(&bars->s_full), j & 1, abort_flag, err);
+            float s[64];
             if (ok) {
                 tc_fence_after();
-                tmem_ld32(tm + lane_addr + kTmS + sb * kBN + half * 32, s);
+                tmem_ld32(tm + lane_addr + kTmS + half * 64, s);
+                tmem_ld32(tm + lane_addr + kTmS + half * 64 + 32, s + 32);
                 tmem_ld_wait();
             } else {
 #pragma unroll
-                for (int c = 0; c < 32; c++) s[c] = 0.f;
+                for (int c = 0; c < 64; c++) s[c] = 0.f;
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&bars->s_free[sb]));
+            if (lane == 0) mbar_arrive(smem_u32(&bars->s_free));
             // causal + length mask (only tiles that reach the diagonal or T)
-            const int kp0 = j * kBN + half * 32;
-            if (kp0 + 31 > q0 || kp0 + 32 > T) {
+            const int kp0 = j * kBN + half * 64;
+            if (kp0 + 63 > q0 || kp0 + 64 > T) {
                 const int lim = min(qp, T - 1) - kp0;  // columns c <= lim are visible
 #pragma unroll
-                for (int c = 0; c < 32; c++)
+                for (int c = 0; c < 64; c++)
                     if (c > lim) s[c] = -INFINITY;
             }
             float m4[4];
 #pragma unroll
             for (int i = 0; i < 4; i++) m4[i] = fmaxf(s[i], s[i + 4]);
 #pragma unroll
-            for (int c = 8; c < 32; c += 4) {
+            for (int c = 8; c < 64; c += 4) {
 #pragma unroll
                 for (int i = 0; i < 4; i++) m4[i] = fmaxf(m4[i], s[c + i]);
             }
             float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-            red[(sb * 2 + half) * kBM + r] = mx;
+            const int par = j & 1;
+            red[(par * 2 + half) * kBM + r] = mx;
             named_bar_sync(bar_id, 64);
-            mx = fmaxf(mx, red[(sb * 2 + (half ^ 1)) * kBM + r]);
+            mx = fmaxf(mx, red[(par * 2 + (half ^ 1)) * kBM + r]);
             const float m_new = fmaxf(m_used, mx * kLog2e);
             bool rescale = false;
             float factor = 1.f;
@@ -380,10 +435,10 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
             }
             l *= factor;
             const float nm = -m_used;
-            uint32_t pk[16];
+            uint32_t pk[32];
             float r4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < 32; c += 2) {
+            for (int c = 0; c < 64; c += 2) {
                 const float p0 = ex2_approx(fmaf(s[c], kLog2e, nm));
                 const float p1 = ex2_approx(fmaf(s[c + 1], kLog2e, nm));
                 r4[(c >> 1) & 3] += p0 + p1;
@@ -393,8 +448,7 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
             // PV_{j-1} must be complete: it read the P buffer, and O is
             // stable for rescaling.
             if (j >= 1)
-                ok = ok && mbar_wait_bounded(smem_u32(&bars->pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1,
-                                             abort_flag, err);
+                ok = ok && mbar_wait_bounded(smem_u32(&bars->pv_done), (j - 1) & 1, abort_flag, err);
             if (ok) {
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, rescale) && j >= 1) {
@@ -410,17 +464,18 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
                     }
                     tmem_st_wait();
                 }
-                uint8_t* prow = smem + kOffP;
+                // this half's 64 keys = one 128-byte row of P box `half`
+                uint8_t* pbox = smem + kOffP + half * kPBox;
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
+                for (int c = 0; c < 8; c++) {
                     uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-                    *reinterpret_cast<uint4*>(prow + sw128_off(r, half * 4 + c)) = v;
+                    *reinterpret_cast<uint4*>(pbox + sw128_off(r, c)) = v;
                 }
                 fence_proxy_async_shared();
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[sb]));
+            if (lane == 0) mbar_arrive(smem_u32(&bars->p_full));
         }
         // ------------------------------ epilogue ------------------------------
         // the two halves' row sums (the exchange buffer of the next parity is
@@ -430,7 +485,7 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
         named_bar_sync(bar_id, 64);
         l += red[(pe * 2 + (half ^ 1)) * kBM + r];
         const int jl = n_tiles - 1;
-        ok = ok && mbar_wait_bounded(smem_u32(&bars->pv_done[jl & 1]), (jl >> 1) & 1, abort_flag, err);
+        ok = ok && mbar_wait_bounded(smem_u32(&bars->pv_done), jl & 1, abort_flag, err);
         if (ok) {
             tc_fence_after();
             const float inv_l = 1.0f / l;
@@ -480,13 +535,13 @@ umma_selftest_kernel(const __grid_constant__ CUtensorMap tma, const __grid_const
     const bool fp16 = (mode & 1) != 0, a_tmem = (mode & 2) != 0;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
+    StBars* bars = reinterpret_cast<StBars*>(smem + kStOffBar);
     volatile int* abort_flag = &bars->abort_flag;
     const uint32_t sbase = smem_u32(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        mbar_init(smem_u32(&bars->q_full), 1);
-        mbar_init(smem_u32(&bars->pv_done[0]), 1);
+        mbar_init(smem_u32(&bars->ld_full), 1);
+        mbar_init(smem_u32(&bars->mma_done), 1);
         bars->abort_flag = 0;
         fence_barrier_init();
     }
@@ -498,26 +553,26 @@ umma_selftest_kernel(const __grid_constant__ CUtensorMap tma, const __grid_const
     for (int i = threadIdx.x; i < kBM * 8; i += blockDim.x) {
         const int row = i / 8, c = i % 8;
         const uint4 v = *reinterpret_cast<const uint4*>(P + row * 64 + c * 8);
-        *reinterpret_cast<uint4*>(smem + kOffP + sw128_off(row, c)) = v;
+        *reinterpret_cast<uint4*>(smem + kStOffP + sw128_off(row, c)) = v;
     }
     fence_proxy_async_shared();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = bars->tmem_base;
-    const uint32_t qb = smem_u32(&bars->q_full);
+    const uint32_t qb = smem_u32(&bars->ld_full);
     if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(qb, kQBytes + 2 * kKVTile);
+        mbar_arrive_expect_tx(qb, 4 * kQBox + 8 * kStKBox);
         for (int sub = 0; sub < 4; sub++) {
-            tma_load_3d(sbase + kOffQ + sub * kQBox, &tma, sub * 64, 0, 0, qb);
-            tma_load_3d(sbase + kOffK + sub * kKBox, &tmb, sub * 64, 0, 0, qb);
-            tma_load_3d(sbase + kOffV + sub * kKBox, &tmv, sub * 64, 0, 0, qb);
+            tma_load_3d(sbase + kStOffQ + sub * kQBox, &tma, sub * 64, 0, 0, qb);
+            tma_load_3d(sbase + kStOffK + sub * kStKBox, &tmb, sub * 64, 0, 0, qb);
+            tma_load_3d(sbase + kStOffV + sub * kStKBox, &tmv, sub * 64, 0, 0, qb);
         }
     }
     bool ok = mbar_wait_bounded(qb, 0, abort_flag, err);
     if (ok && a_tmem && warp >= 2) {  // warps 2..5 own lane quarters 2, 3, 0, 1
         const int quarter = warp & 3;
-        tile_rows_to_tmem(smem + kOffQ, tm + ((uint32_t)(quarter * 32) << 16) + kTmQ, quarter * 32 + lane, 0, 4);
+        tile_rows_to_tmem(smem + kStOffQ, tm + ((uint32_t)(quarter * 32) << 16) + kTmQ, quarter * 32 + lane, 0, 4);
         tmem_st_wait();
     }
     tc_fence_before();
@@ -525,28 +580,28 @@ umma_selftest_kernel(const __grid_constant__ CUtensorMap tma, const __grid_const
     if (threadIdx.x == 0 && ok) {
         tc_fence_after();
         for (int kk = 0; kk < 16; kk++) {
-            const uint64_t bd = umma_sdesc(sbase + kOffK + (kk >> 2) * kKBox + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = umma_sdesc(sbase + kStOffK + (kk >> 2) * kStKBox + (kk & 3) * 32, 16, 1024);
             if (a_tmem)
-                umma_f16_ts(tm + kTmS, tm + kTmQ + kk * 8, bd, fp16 ? kIdescS : kIdescS_bf, kk > 0);
+                umma_f16_ts(tm + kStTmS, tm + kTmQ + kk * 8, bd, fp16 ? kStIdescS : kStIdescS_bf, kk > 0);
             else
-                umma_bf16_ss(tm + kTmS,
-                             umma_sdesc(sbase + kOffQ + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024), bd,
-                             fp16 ? kIdescS : kIdescS_bf, kk > 0);
+                umma_bf16_ss(tm + kStTmS,
+                             umma_sdesc(sbase + kStOffQ + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024), bd,
+                             fp16 ? kStIdescS : kStIdescS_bf, kk > 0);
         }
         for (int kk = 0; kk < 4; kk++)
-            umma_bf16_ss(tm + kTmO, umma_sdesc(sbase + kOffP + kk * 32, 16, 1024),
-                         umma_sdesc(sbase + kOffV + kk * 2048, kKBox, 1024),
-                         fp16 ? kIdescO : kIdescO_bf, kk > 0);
-        umma_commit(smem_u32(&bars->pv_done[0]));
+            umma_bf16_ss(tm + kTmO, umma_sdesc(sbase + kStOffP + kk * 32, 16, 1024),
+                         umma_sdesc(sbase + kStOffV + kk * 2048, kStKBox, 1024),
+                         fp16 ? kIdescO : kStIdescO_bf, kk > 0);
+        umma_commit(smem_u32(&bars->mma_done));
     }
     if (warp >= 2 && ok) {
         const int quarter = warp & 3, r = quarter * 32 + lane;
         const uint32_t la = (uint32_t)(quarter * 32) << 16;
-        if (mbar_wait_bounded(smem_u32(&bars->pv_done[0]), 0, abort_flag, err)) {
+        if (mbar_wait_bounded(smem_u32(&bars->mma_done), 0, abort_flag, err)) {
             tc_fence_after();
             for (int c = 0; c < 2; c++) {
                 float v[32];
-                tmem_ld32(tm + la + kTmS + c * 32, v);
+                tmem_ld32(tm + la + kStTmS + c * 32, v);
                 tmem_ld_wait();
                 for (int i = 0; i < 32; i++) d1[r * 64 + c * 32 + i] = v[i];
             }
@@ -593,7 +648,7 @@ cudaError_t launch_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
     CUtensorMap tmq, tmk, tmv;
     if (encode_rows_tmap(&tmq, qw, kD, (uint64_t)T, (uint64_t)B * kNumH, 64, kBM, true) != QM_OK ||
         encode_rows_tmap(&tmk, kw, kD, (uint64_t)T, (uint64_t)B * kNumKVH, 64, kBN, true) != QM_OK ||
-        encode_rows_tmap(&tmv, vw, kD, (uint64_t)T, (uint64_t)B * kNumKVH, 64, kBN, true) != QM_OK)
+        encode_rows_tmap(&tmv, vw, kD, (uint64_t)T, (uint64_t)B * kNumKVH, 64, 32, true) != QM_OK)
         return cudaErrorInvalidValue;
     static bool attr_set[64] = {};
     if (ctx->device < 64 && !attr_set[ctx->device]) {
@@ -658,9 +713,8 @@ extern "C" int qm_selftest_umma(const uint16_t* a, const uint16_t* b, const uint
     int* err = nullptr;
     if (cudaMalloc(&err, sizeof(int)) != cudaSuccess) return QM_E_OOM;
     cudaMemset(err, 0, sizeof(int));
-    cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         kPrefillSmem);
-    umma_selftest_kernel<<<1, 192, kPrefillSmem>>>(ta, tb, tv, p, d1, d2, mode, err);
+    cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStSmem);
+    umma_selftest_kernel<<<1, 192, kStSmem>>>(ta, tb, tv, p, d1, d2, mode, err);
     cudaError_t e = cudaDeviceSynchronize();
     int flag = 0;
     cudaMemcpy(&flag, err, sizeof(int), cudaMemcpyDeviceToHost);
