@@ -46,9 +46,10 @@
 //    thread): the S MMAs take ~90 cycles and the P.V MMAs ~158 in the kernel
 //    (68 and 128 alone), and ~20 % of the time the issuer waits for K/V
 //    chunks — shared memory (ring 176 KB + P 32 KB) and TMEM (all 512
-//    columns) are both full at head dim 256 on one SM.  The two-SM form
-//    (cta_group::2, each CTA of a pair holding half of every K/V tile) is
-//    the next step.
+//    columns) are both full at head dim 256 on one SM.  A CTA-pair form
+//    (cta_group::2, M = 256, each CTA staging half of every K/V tile) gave
+//    the same per-SM MMA times and K/V waits and was not kept; its building
+//    blocks are in qm_ptx.cuh, checked by qm_selftest_umma_pair.
 #include <cuda_bf16.h>
 
 #include <algorithm>
