@@ -75,7 +75,7 @@ def _case(ctx, orc, B, T, seed, decode_first=0, gate=False):
     return st
 
 
-@pytest.mark.parametrize("B,T", [(1, 64), (1, 100), (2, 200), (1, 3)])
+@pytest.mark.parametrize("B,T", [(1, 64), (1, 100), (2, 200), (1, 3), (1, 1), (1, 65), (3, 128)])
 def test_prefill_small_every_token(ctx, orc, B, T):
     """Full chunk, partial chunks, several chunks, a prompt shorter than the conv."""
     _case(ctx, orc, B, T, 900 + T + B)

@@ -113,7 +113,7 @@ def _run_prefill(ctx, B, T, seed, cap=None):
     return g, pr, cos, sin, qg, kk, vv, kv, out
 
 
-@pytest.mark.parametrize("B,T", [(1, 64), (1, 128), (2, 200), (1, 391)])
+@pytest.mark.parametrize("B,T", [(1, 1), (1, 64), (1, 128), (1, 129), (2, 200), (1, 391)])
 def test_prefill_small_all_rows(ctx, orc, B, T):
     """Every row of short prompts: single tile, partial tiles, several query tiles."""
     c = orc.cfg_4b()
