@@ -399,14 +399,26 @@ gqa_combine_kernel(const float* __restrict__ q_f32, const float* __restrict__ kn
     const float wn = exp2f((s_new - M) * kLog2e);
     float acc = wn * v_new[((size_t)b * kNumKVH + g) * kD + d];
     float lsum = wn;
-    for (int i = 0; i < nsplit; i++) {
+    auto add_split = [&](int i, float o) {
         const float mi = (i < 512) ? s_ml[2 * i] : part_ml[((size_t)bh * nsplit + i) * 2];
         const float li = (i < 512) ? s_ml[2 * i + 1] : part_ml[((size_t)bh * nsplit + i) * 2 + 1];
-        if (mi == -INFINITY) continue;
+        if (mi == -INFINITY) return;
         const float w = exp2f((mi - M) * kLog2e);
-        acc += w * part_o[((size_t)bh * nsplit + i) * kD + d];
+        acc += w * o;
         lsum += w * li;
+    };
+    // the partials' loads, 8 splits at a time, are all in flight before the
+    // first is used (one split per iteration left each load's latency exposed)
+    const float* po = part_o + (size_t)bh * nsplit * kD + d;
+    int i = 0;
+    for (; i + 8 <= nsplit; i += 8) {
+        float pv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) pv[u] = po[(size_t)(i + u) * kD];
+#pragma unroll
+        for (int u = 0; u < 8; u++) add_split(i + u, pv[u]);
     }
+    for (; i < nsplit; i++) add_split(i, po[(size_t)i * kD]);
     const float gate = q_gate[((size_t)b * kNumH + h) * 2 * kD + kD + d];
     out[(size_t)bh * kD + d] = (acc / lsum) * (1.0f / (1.0f + __expf(-gate)));
 }
