@@ -302,8 +302,42 @@ __device__ __forceinline__ void dn_fetch_head(DnHeadIn& in, const float* __restr
     }
 }
 
-// NB shared buffers per CTA; MINB CTAs per SM.
-template <bool FUSED, int NB, int MINB>
+// The inputs that differ between the two V heads of one QK head (v, its
+// history and taps, z, the gates); q and k stay as fetched for the partner.
+__device__ __forceinline__ void dn_fetch_vhead(DnHeadIn& in, const float* __restrict__ qkv,
+                                               const float* __restrict__ a_in,
+                                               const float* __restrict__ b_in,
+                                               const float* __restrict__ conv_w,
+                                               const float* __restrict__ a_log,
+                                               const float* __restrict__ dt_bias,
+                                               const float* __restrict__ conv,
+                                               const float* __restrict__ z, int b, int vh, int s0,
+                                               int s1, int s2, int tid) {
+    const float* x = qkv + (size_t)b * kQKVDim;
+    const float* ring = conv + (size_t)b * kConvSlots * kQKVDim;
+    if (tid < kHd) {
+        in.zv = z ? z[(size_t)b * kVDim + (size_t)vh * kHd + tid] : 0.f;
+    } else {
+        const int chv = 2 * kQDim + vh * kHd + (tid - kHd);
+        in.w0 = reinterpret_cast<const float4*>(conv_w)[chv];
+        in.x0 = x[chv];
+        in.r[0] = ring[s0 * kQKVDim + chv];
+        in.r[1] = ring[s1 * kQKVDim + chv];
+        in.r[2] = ring[s2 * kQKVDim + chv];
+    }
+    if (tid == 255) {
+        in.a = a_in[b * kNumV + vh];
+        in.bb = b_in[b * kNumV + vh];
+        in.alog = a_log[vh];
+        in.dtb = dt_bias[vh];
+    }
+}
+
+// NB shared buffers per CTA; MINB CTAs per SM.  PAIR: CTA c takes the two V
+// heads 2c, 2c+1 of the item list (the two V heads of one QK head of one
+// sequence) one after the other and fetches q and k once for both — used when
+// the inputs are read from host memory over PCIe, where each byte counts.
+template <bool FUSED, int NB, int MINB, bool PAIR = false>
 __global__ void __launch_bounds__(256, MINB)
 dn_decode_stream(const float* __restrict__ qkv, const float* __restrict__ a_in,
                  const float* __restrict__ b_in, const float* __restrict__ conv_w,
@@ -328,7 +362,9 @@ dn_decode_stream(const float* __restrict__ qkv, const float* __restrict__ a_in,
     const int lane8 = lane & 7, rsub = lane >> 3;
     const int G = gridDim.x;
     const int s0 = (slot_w + 1) & 3, s1 = (slot_w + 2) & 3, s2 = (slot_w + 3) & 3;
-    const int nk = (n_items - (int)blockIdx.x + G - 1) / G;  // heads of this CTA
+    // heads of this CTA and the item of its k-th head
+    const int nk = PAIR ? 2 : (n_items - (int)blockIdx.x + G - 1) / G;
+    auto item_of = [&](int k) { return PAIR ? 2 * (int)blockIdx.x + k : (int)blockIdx.x + k * G; };
 
     if (tid == 0) {
         for (int i = 0; i < NB; i++) mbar_init(smem_u32(&full[i]), 1);
@@ -343,7 +379,7 @@ dn_decode_stream(const float* __restrict__ qkv, const float* __restrict__ a_in,
 #pragma unroll
     for (int i = 0; i < NB; i++) pending[i] = -1;
     auto issue = [&](int k) {  // state of this CTA's k-th head into buffer k % NB
-        const int item = (int)blockIdx.x + k * G;
+        const int item = item_of(k);
         const int buf = k % NB;
         const int b = b0 + item / nvh, lh = item % nvh;
         const uint8_t* src = reinterpret_cast<const uint8_t*>(S + ((size_t)b * nvh + lh) * kHd * kHd);
@@ -359,18 +395,21 @@ dn_decode_stream(const float* __restrict__ qkv, const float* __restrict__ a_in,
 
     DnHeadIn cur, nxt;
     if (nk > 0) {
-        const int item = blockIdx.x, b = b0 + item / nvh, vh = vh_lo + item % nvh;
+        const int item = item_of(0), b = b0 + item / nvh, vh = vh_lo + item % nvh;
         dn_fetch_head(nxt, qkv, a_in, b_in, conv_w, a_log, dt_bias, conv, z, b, vh, s0, s1, s2, tid);
     }
     bool ok = true;
     for (int k = 0; k < nk && ok; k++) {
-        const int item = (int)blockIdx.x + k * G;
+        const int item = item_of(k);
         const int b = b0 + item / nvh, lh = item % nvh, vh = vh_lo + lh;
         const int buf = k % NB;
         cur = nxt;
         if (k + 1 < nk) {  // the next head's inputs, in flight during this one
-            const int it2 = item + G, b2 = b0 + it2 / nvh, vh2 = vh_lo + it2 % nvh;
-            dn_fetch_head(nxt, qkv, a_in, b_in, conv_w, a_log, dt_bias, conv, z, b2, vh2, s0, s1, s2, tid);
+            const int it2 = item_of(k + 1), b2 = b0 + it2 / nvh, vh2 = vh_lo + it2 % nvh;
+            if (PAIR)  // the partner V head: same q and k
+                dn_fetch_vhead(nxt, qkv, a_in, b_in, conv_w, a_log, dt_bias, conv, z, b2, vh2, s0, s1, s2, tid);
+            else
+                dn_fetch_head(nxt, qkv, a_in, b_in, conv_w, a_log, dt_bias, conv, z, b2, vh2, s0, s1, s2, tid);
         }
 
         // ---- prologue: conv1d(k=4) + SiLU + L2 norm (gemv.rs:744-785) ----
@@ -550,19 +589,19 @@ cudaError_t launch_t(cudaStream_t st, int b0, int nb, const qm_dn_params* p, qm_
 constexpr int kStreamNB = 1, kStreamMinB = 3;  // one buffer per CTA, three CTAs per SM
 constexpr int kStreamSmem = kStreamNB * kHeadBytes + 1024;
 
-template <bool FUSED>
+template <bool FUSED, bool PAIR>
 cudaError_t launch_stream(qm_ctx* ctx, int b0, int nb, const qm_dn_params* p, qm_dn_state* s,
                           const float* qkv, const float* a, const float* b, float* y,
                           const float* z, float* out, int slot_w) {
-    auto kern = dn_decode_stream<FUSED, kStreamNB, kStreamMinB>;
-    static bool attr_set[2][64] = {};
-    if (ctx->device < 64 && !attr_set[FUSED][ctx->device]) {
+    auto kern = dn_decode_stream<FUSED, kStreamNB, kStreamMinB, PAIR>;
+    static bool attr_set[2][2][64] = {};
+    if (ctx->device < 64 && !attr_set[FUSED][PAIR][ctx->device]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem);
         if (e != cudaSuccess) return e;
-        attr_set[FUSED][ctx->device] = true;
+        attr_set[FUSED][PAIR][ctx->device] = true;
     }
     const int n_items = nb * s->nvh;
-    const int grid = n_items;  // one CTA per head
+    const int grid = PAIR ? n_items / 2 : n_items;  // one CTA per head (per V-head pair)
     kern<<<grid, 256, kStreamSmem, ctx->stream>>>(
         qkv, a, b, p->conv_w, p->a_log, p->dt_bias, p->norm_gamma, s->s, s->conv, slot_w, y, z, out,
         s->vh_lo, s->nvh, b0, n_items, ctx->d_err);
@@ -577,16 +616,19 @@ int dn_decode_split_for(int units, int num_sms) {
 
 cudaError_t launch_dn_decode(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, const float* qkv,
                              const float* a, const float* b, float* y, const float* z, float* out,
-                             int b0, int nb) {
+                             int b0, int nb, bool pair) {
     const int B = nb < 0 ? st->batch : nb;
     const int slot_w = (int)(st->conv_pos & 3);
     const int split = dn_decode_split_for(B * st->nvh, ctx->num_sms);
     const bool fused = (z != nullptr);
     cudaError_t e;
     TimedLaunch tl(ctx, "dn_decode");
-    if (split == 1)  // the batch covers the GPU: staged CTAs, three per SM
-        e = fused ? launch_stream<true>(ctx, b0, B, p, st, qkv, a, b, y, z, out, slot_w)
-                  : launch_stream<false>(ctx, b0, B, p, st, qkv, a, b, y, z, out, slot_w);
+    if (split == 1 && pair)  // inputs in host memory: q and k fetched once per V-head pair
+        e = fused ? launch_stream<true, true>(ctx, b0, B, p, st, qkv, a, b, y, z, out, slot_w)
+                  : launch_stream<false, true>(ctx, b0, B, p, st, qkv, a, b, y, z, out, slot_w);
+    else if (split == 1)  // the batch covers the GPU: staged CTAs, three per SM
+        e = fused ? launch_stream<true, false>(ctx, b0, B, p, st, qkv, a, b, y, z, out, slot_w)
+                  : launch_stream<false, false>(ctx, b0, B, p, st, qkv, a, b, y, z, out, slot_w);
     else if (split == 2)
         e = fused ? launch_t<2, true>(ctx->stream, b0, B, p, st, qkv, a, b, y, z, out, slot_w)
                   : launch_t<2, false>(ctx->stream, b0, B, p, st, qkv, a, b, y, z, out, slot_w);

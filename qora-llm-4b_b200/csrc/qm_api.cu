@@ -705,7 +705,7 @@ extern "C" int qm_dn_decode_host(qm_ctx* c, const qm_dn_params* p, qm_dn_state* 
             ((uintptr_t)m_qkv & 15) == 0) {
             cudaError_t e = launch_dn_decode(c, p, st, (const float*)m_qkv, (const float*)m_a,
                                              (const float*)m_b, (float*)m_y, (const float*)m_z,
-                                             (float*)m_out);
+                                             (float*)m_out, 0, -1, true);
             if (e != cudaSuccess) return cuda_error(c, e, "dn_decode launch");
             st->conv_pos += 1;
             c->host_in_place += 1;

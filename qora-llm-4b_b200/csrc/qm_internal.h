@@ -109,9 +109,10 @@ struct TimedLaunch {
 
 // Kernel launchers (return cudaError_t from the launch).
 // b0, nb: run sequences [b0, b0 + nb) of the handle's batch (nb < 0: all)
+// pair: fetch q and k once per V-head pair (inputs in host memory, read over PCIe)
 cudaError_t launch_dn_decode(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, const float* qkv,
                              const float* a, const float* b, float* y, const float* z, float* out,
-                             int b0 = 0, int nb = -1);
+                             int b0 = 0, int nb = -1, bool pair = false);
 // GqaCombineSrc: where the combine kernel reads the gate half of q_gate and
 // v_new (default: the call's own q_gate / v_new), after waiting for `ready`
 // on the launch stream when it is set.
