@@ -264,6 +264,7 @@ typedef struct qm_gqa_params {
  *   out [B,16,256] f32 gated attention output (input of o_proj)
  * QM_E_RANGE if seq_len >= capacity or seq_len >= max_pos.
  * Uses the context workspace for split-KV partials (grown on first use).
+ * Cache rows at and past seq_len are never used, whatever they hold.
  */
 int qm_gqa_decode(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, const float* q_gate,
                   const float* k_new, const float* v_new, float* out);

@@ -294,6 +294,22 @@ gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__
                 }
             const uint32_t a0 = pack_bf16(pb[0][0], pb[0][1]);
             const uint32_t a2 = pack_bf16(pb[1][0], pb[1][1]);
+            // ---- rows at or past the end of the range: P is 0 there, but cache
+            // memory beyond seq_len may hold anything (a caller's buffer) and
+            // 0 * NaN would poison O, so this warp's V rows there become zeros ----
+            const int wpos0 = (tile0 + it) * kTile + warp * 16;
+            if (wpos0 + 16 > pos_end) {
+                for (int e = lane; e < 16 * 32; e += 32) {
+                    const int i = e >> 5, c = e & 31;
+                    if (wpos0 + i >= pos_end)
+                        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(
+                                         swz_addr(vb, warp * 16 + i, c * 8)),
+                                     "r"(0u)
+                                     : "memory");
+                }
+                __syncwarp();
+                fence_proxy_async_shared();  // before TMA refills this stage
+            }
             // ---- O += P . V over 256 dims ----
             const int mi = lane >> 3;
             const int vpos = warp * 16 + (mi & 1) * 8 + (lane & 7);

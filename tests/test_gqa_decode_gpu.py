@@ -213,3 +213,27 @@ def test_host_variant_in_place_on_pinned_buffers(ctx, orc):
     finally:
         ctx.set_host_direct(True)
         kvd.close()
+
+
+def test_cache_rows_past_seq_len_may_hold_nan(ctx, orc):
+    """A caller's cache may hold anything at and past seq_len (the attention
+    loads whole 64-position tiles): NaN bit patterns there must not reach the
+    output.  L = 100 ends inside a tile."""
+    import torch
+
+    import qora_mixer as qm
+
+    B, L, cap = 2, 100, 200
+    g, c, pr, cos, sin, K, V, okv, kvh, prm, keep = _setup(ctx, orc, B, L, cap, 870)
+    K[:, :, L:] = 0x7FC0  # bf16 quiet NaN
+    V[:, :, L:] = 0x7FC0
+    tok = I.gqa_token_inputs(g, B)
+    out = torch.empty(B, 16, 256, device="cuda")
+    qm.Mixer(ctx).gqa_decode(prm, kvh, dev(tok["q_gate"]), dev(tok["k_new"]), dev(tok["v_new"]), out)
+    ctx.sync()
+    o = host(out)
+    assert np.isfinite(o).all()
+    for bi in range(B):
+        ref = orc.gqa_decode(c, okv[bi], tok["q_gate"][bi], tok["k_new"][bi], tok["v_new"][bi],
+                             pr["q_norm"], pr["k_norm"], cos, sin)
+        assert refmath.rel_err(o[bi], ref) <= TOL
