@@ -574,6 +574,122 @@ def bench_gqa_prefill(ctx, ws, reps, B=4, T=32768):
 
 
 # ----------------------------------------------------------------------------
+# projections around the mixers (the next row after the mixers): all 32 layers'
+# in_proj_qkv/a/b/z + out_proj (DeltaNet) and q/k/v/o_proj (GQA) for one decode
+# token at batch B, Q4 or F16 weights, each layer's weights distinct (734 MB in
+# Q4: larger than L2, so every step streams them from HBM)
+# ----------------------------------------------------------------------------
+PROJ_DN = [(2560, 8192), (2560, 32), (2560, 32), (2560, 4096), (4096, 2560)]
+PROJ_GQA = [(2560, 8192), (2560, 1024), (2560, 1024), (4096, 2560)]
+
+
+def bench_gemv(ctx, reps, batch=1, kind="q4"):
+    """Each form of the step is captured once in a CUDA graph and replayed
+    `reps` times between two events: fused (qm_gemv_multi over the weights
+    that share x, 2 launches per layer), one launch per weight (152), and the
+    32 in_proj_qkv / q_proj launches alone (the per-kernel roofline)."""
+    import torch
+
+    import qora_mixer as qm
+
+    gen = torch.Generator(device="cuda").manual_seed(0x51A5)
+    layers = [PROJ_GQA if layer % 4 == 3 else PROJ_DN for layer in range(32)]
+    weights, keep, nbytes = [], [], 0
+    for shapes in layers:
+        lw = []
+        for k, n in shapes:
+            if kind == "q4":
+                pk = torch.randint(0, 256, (k, n // 2), dtype=torch.uint8, device="cuda", generator=gen)
+                sc = (torch.rand(k, n // 32, device="cuda", generator=gen) * 0.01).half().view(torch.int16)
+                lw.append(qm.weight_q4(pk, sc))
+                nbytes += pk.numel() + sc.numel() * 2
+            else:
+                w16 = (torch.randn(k, n, device="cuda", generator=gen) * 0.02).half().view(torch.int16)
+                lw.append(qm.weight_f16(w16))
+                nbytes += w16.numel() * 2
+        weights.append(lw)
+    xs = {k: torch.randn(batch, k, device="cuda", generator=gen) for k in (2560, 4096)}
+    ys = {n: torch.empty(batch, n, device="cuda") for n in (8192, 32, 4096, 2560, 1024)}
+    ys_b = torch.empty(batch, 32, device="cuda")  # in_proj_b beside in_proj_a
+    mx = qm.Mixer(ctx)
+
+    def fused():
+        for lw, shapes in zip(weights, layers):
+            outs = [ys[n] for _, n in shapes[:-1]]
+            if len(outs) == 4:
+                outs[2] = ys_b
+            mx.gemv_multi(lw[:-1], xs[2560], outs)
+            mx.gemv(lw[-1], xs[4096], ys[2560])
+
+    def unfused():
+        for lw, shapes in zip(weights, layers):
+            for w, (k, n) in zip(lw, shapes):
+                mx.gemv(w, xs[k], ys[n])
+
+    def big_only():
+        for lw in weights:
+            mx.gemv(lw[0], xs[2560], ys[8192])
+
+    side = torch.cuda.Stream()
+
+    def timed(fn):
+        n0 = ctx.launch_count()
+        fn()  # warm-up and the launch count
+        launches = ctx.launch_count() - n0
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        ctx.set_stream(side)
+        try:
+            with torch.cuda.graph(g, stream=side):
+                fn()
+        finally:
+            ctx.set_stream(torch.cuda.current_stream())
+        for _ in range(3):
+            g.replay()
+        stream = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del g
+        return e0.elapsed_time(e1) / reps, launches
+
+    f_ms, f_n = timed(fused)
+    u_ms, u_n = timed(unfused)
+    b_ms, b_n = timed(big_only)
+    n0 = ctx.launch_count()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fused()
+    e1.record()
+    torch.cuda.synchronize()
+    d_ms = e0.elapsed_time(e1) / reps
+    peak, peak_kind = load_peaks()
+    per_w = 0.5625 if kind == "q4" else 2.0
+    big_gbs = 2560 * 8192 * per_w / (b_ms / b_n / 1e3) / 1e9
+    ach = nbytes / (f_ms / 1e3) / 1e9
+    del keep, weights
+    torch.cuda.empty_cache()
+    return {"metric": "mixer projections, 32 layers, one decode token", "workload":
+            f"in_proj_qkv/a/b/z + out_proj x 24 DeltaNet layers, q/k/v/o_proj x 8 GQA layers, batch {batch}, "
+            f"{kind.upper()} weights ({nbytes / 1e6:.0f} MB, larger than L2)",
+            "value": round(batch / (f_ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(f_ms, 4),
+            "launches_per_step": f_n, "timing": "CUDA graph of the step, replayed; CUDA events",
+            "one_launch_per_weight": {"ms_per_step": round(u_ms, 4), "launches_per_step": u_n},
+            "fused_without_graph_ms_per_step": round(d_ms, 4),
+            "roofline": {"bound": "hbm", "kernel": "qm_gemv_kernel", "achieved": round(ach, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / peak, 4),
+                         "algorithmic_bytes_per_step": nbytes,
+                         "in_proj_qkv_alone_gbs": round(big_gbs, 1),
+                         "in_proj_qkv_alone_frac": round(big_gbs / peak, 4)}}
+
+
+# ----------------------------------------------------------------------------
 # prefill (workload 2): DeltaNet chunked prefill, 8 x 8192 tokens, chunk 64
 # ----------------------------------------------------------------------------
 def bench_dn_prefill(ctx, ws, reps, B=8, T=8192):
@@ -798,9 +914,22 @@ def main():
                     help="time one prefill alone (profiling small cases); prints its record")
     ap.add_argument("--prefill-batch", type=int, help="with --prefill-only: sequences")
     ap.add_argument("--prefill-len", type=int, help="with --prefill-only: tokens per sequence")
+    ap.add_argument("--gemv-only", choices=["q4", "f16"],
+                    help="time the 32 layers' mixer projections (Q4 / F16 weight GEMV) alone")
+    ap.add_argument("--gemv-batch", type=int, default=1, help="with --gemv-only: sequences per step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.gemv_only:
+        import torch
+
+        import qora_mixer as qm
+
+        torch.cuda.set_device(0)
+        ctx = qm.Ctx(0, stream=torch.cuda.current_stream())
+        print(json.dumps(bench_gemv(ctx, args.steps, args.gemv_batch, args.gemv_only)), flush=True)
+        ctx.close()
+        return
     if args.prefill_only:
         import torch
 

@@ -323,6 +323,39 @@ int qm_gqa_decode_noalloc(const qm_gqa_params* p, uint16_t* k_cache, uint16_t* v
                           const float* v_new, float* out, void* stream);
 
 /* ------------------------------------------------------------------ */
+/* Projections around the mixers (the next component beside the path):  */
+/* y[b] = x[b] . W for the reference's weight formats                    */
+/* (src/gemv.rs:21-40, gemv 286-300): W [k rows (input) x n (output)].   */
+/* ------------------------------------------------------------------ */
+#define QM_W_F16 0  /* data: f16 [k][n] (gemv_f16, src/gemv.rs:338-368)           */
+#define QM_W_Q4 1   /* data: uint8 [k][n/2], even column in the low nibble, value */
+                    /* q - 8; scales: f16 [k][n/32] (gemv_q4, src/gemv.rs:411-450; */
+                    /* format src/convert.rs:437-467)                             */
+typedef struct qm_weight {
+    int kind;            /* QM_W_F16 or QM_W_Q4 */
+    int k, n;
+    const void* data;    /* device */
+    const void* scales;  /* device, Q4 only */
+} qm_weight;
+/* y[batch][n] = x[batch][k] . W on the context's stream (device pointers);
+ * replaces gemv(input, weight) (src/gemv.rs:286-291) at decode batch sizes.
+ * Q4 needs n % 32 == 0, F16 n % 8 == 0.  Sums are f32 and added in a fixed
+ * order (the result does not depend on timing).  The kernel issues its
+ * weight loads before it waits for the preceding kernel of the stream
+ * (programmatic dependent launch): it reads x only after that kernel is done.
+ * Calls on one context share a scratch area (partial sums, allocated by the
+ * first call that needs it; QM_E_CAPTURE if that call is inside a stream
+ * capture): issue them in order on the context's stream. */
+int qm_gemv(qm_ctx* ctx, const qm_weight* w, int batch, const float* x, float* y);
+/* ys[i][batch][ws[i].n] = x[batch][k] . W_i for count <= 4 weights of one
+ * kind and one k that share the input, in one launch: the reference's
+ * in_proj_qkv / a / b / z of one x_norm (src/gemv.rs:742,788-789,865) or
+ * q / k / v_proj (src/gemv.rs:928,941-942).  QM_E_MISMATCH when the weights
+ * differ in k or kind.  ys is a host array of device pointers. */
+int qm_gemv_multi(qm_ctx* ctx, const qm_weight* ws, int count, int batch, const float* x,
+                  float* const* ys);
+
+/* ------------------------------------------------------------------ */
 /* Multi-GPU (one process per GPU).  The reference runs one device        */
 /* (src/gpu_inference.rs:981-1004); these calls spread a decode batch     */
 /* over the GPUs of one node.                                             */

@@ -65,6 +65,9 @@ def lib():
             [C.POINTER(OrCfg), C.c_int] + [P] * 10 + [C.c_int, P, C.c_int, P, P, P]
         )
         L.or_gqa_prefill_rows.restype = C.c_int
+        L.or_quantize_q4.argtypes = [P, C.c_int, C.c_int, P, P]
+        L.or_gemv_q4.argtypes = [P, P, P, C.c_int, C.c_int, P]
+        L.or_gemv_f16.argtypes = [P, P, C.c_int, C.c_int, P]
         _lib = L
     return _lib
 
@@ -222,3 +225,41 @@ def gqa_prefill_rows(c, q_gate, k, v, q_norm, k_norm, cos, sin, rows, want_cache
     if rc != 0:
         raise ValueError(f"or_gqa_prefill_rows failed ({rc})")
     return (out, kc, vc) if want_cache else out
+
+
+def quantize_q4(w):
+    """src/convert.rs:437-467: f32 [k, n] -> (packed uint8 [k, n/2], f16 scale bits uint16 [k, n/32])."""
+    w = _f32(w)
+    k, n = w.shape
+    packed = np.empty((k, n // 2), np.uint8)
+    scales = np.empty((k, n // 32), np.uint16)
+    lib().or_quantize_q4(_p(w), k, n, _p(packed), _p(scales))
+    return packed, scales
+
+
+def dequantize_q4(packed, scales):
+    """The weights a Q4 matrix stands for, f32 [k, n]: (q - 8) * f16 scale."""
+    k = packed.shape[0]
+    q = np.empty((k, packed.shape[1] * 2), np.float32)
+    q[:, 0::2] = (packed & 0x0F).astype(np.float32) - 8.0
+    q[:, 1::2] = (packed >> 4).astype(np.float32) - 8.0
+    s = scales.view(np.float16).astype(np.float32)
+    return q * np.repeat(s, 32, axis=1)
+
+
+def gemv_q4(x, packed, scales):
+    """src/gemv.rs:411-450 (scalar path): y[n] = x[k] . W_q4[k, n]."""
+    x = _f32(x)
+    k, n = packed.shape[0], packed.shape[1] * 2
+    y = np.empty(n, np.float32)
+    lib().or_gemv_q4(_p(x), _p(np.ascontiguousarray(packed)), _p(np.ascontiguousarray(scales)), k, n, _p(y))
+    return y
+
+
+def gemv_f16(x, w16):
+    """src/gemv.rs:361-368 (scalar path): y[n] = x[k] . W_f16[k, n]; w16 = f16 bits uint16 [k, n]."""
+    x = _f32(x)
+    k, n = w16.shape
+    y = np.empty(n, np.float32)
+    lib().or_gemv_f16(_p(x), _p(np.ascontiguousarray(w16)), k, n, _p(y))
+    return y

@@ -550,3 +550,72 @@ int or_gqa_prefill_rows(const or_cfg* c, int S, const float* q_gate_f32,
     free(v_all);
     return 0;
 }
+
+/* ------------------------------------------------------------------ */
+/* Projections around the mixers: Q4 and F16 weight GEMV               */
+/* ------------------------------------------------------------------ */
+
+/* Q4 symmetric quantization of a [k][n] f32 matrix, groups of 32 along n
+ * (src/convert.rs:437-467): scale = absmax / 7 stored as f16, values
+ * round(x / scale) (half away from zero, with the f32 scale) clamped to
+ * [-8, 7] and offset by 8, two per byte, the even column in the low nibble. */
+void or_quantize_q4(const float* w, int k, int n, uint8_t* packed, uint16_t* scales) {
+    const int gs = 32, groups = n / gs;
+    for (int ki = 0; ki < k; ki++)
+        for (int g = 0; g < groups; g++) {
+            const float* grp = w + (size_t)ki * n + (size_t)g * gs;
+            float absmax = 0.0f;
+            for (int j = 0; j < gs; j++) absmax = fmaxf(absmax, fabsf(grp[j]));
+            const float scale = absmax > 0.0f ? absmax / 7.0f : 0.0f;
+            _Float16 sh = (_Float16)scale;
+            memcpy(&scales[(size_t)ki * groups + g], &sh, 2);
+            const float inv = scale > 0.0f ? 1.0f / scale : 0.0f;
+            uint8_t* dst = packed + (size_t)ki * (n / 2) + (size_t)g * (gs / 2);
+            for (int j = 0; j < gs; j += 2) {
+                int q0 = (int)roundf(grp[j] * inv), q1 = (int)roundf(grp[j + 1] * inv);
+                q0 = (q0 < -8 ? -8 : q0 > 7 ? 7 : q0) + 8;
+                q1 = (q1 < -8 ? -8 : q1 > 7 ? 7 : q1) + 8;
+                dst[j / 2] = (uint8_t)(q0 | (q1 << 4));
+            }
+        }
+}
+
+static inline float f16_bits_to_f32(uint16_t b) {
+    _Float16 h;
+    memcpy(&h, &b, 2);
+    return (float)h;
+}
+
+/* y[n] = x[k] . W[k][n] for Q4 W (src/gemv.rs:411-450, the scalar path):
+ * rows with x == 0 and groups with scale * x == 0 are skipped; per group a
+ * 16-entry table s * (q - 8) with s = scale * x; f32 sums in row order. */
+void or_gemv_q4(const float* x, const uint8_t* packed, const uint16_t* scales, int k, int n, float* y) {
+    const int gs = 32, groups = n / gs;
+    for (int j = 0; j < n; j++) y[j] = 0.0f;
+    for (int ki = 0; ki < k; ki++) {
+        const float val = x[ki];
+        if (val == 0.0f) continue;
+        for (int g = 0; g < groups; g++) {
+            const float s = f16_bits_to_f32(scales[(size_t)ki * groups + g]) * val;
+            if (s == 0.0f) continue;
+            float lut[16];
+            for (int i = 0; i < 16; i++) lut[i] = s * (float)(i - 8);
+            const uint8_t* src = packed + (size_t)ki * (n / 2) + (size_t)g * (gs / 2);
+            float* o = y + (size_t)g * gs;
+            for (int jj = 0; jj < gs / 2; jj++) {
+                o[2 * jj] += lut[src[jj] & 0x0F];
+                o[2 * jj + 1] += lut[src[jj] >> 4];
+            }
+        }
+    }
+}
+
+/* y[n] = x[k] . W[k][n] for F16 W (src/gemv.rs:361-368, the scalar path). */
+void or_gemv_f16(const float* x, const uint16_t* w, int k, int n, float* y) {
+    for (int j = 0; j < n; j++) y[j] = 0.0f;
+    for (int ki = 0; ki < k; ki++) {
+        const float val = x[ki];
+        const uint16_t* row = w + (size_t)ki * n;
+        for (int j = 0; j < n; j++) y[j] += val * f16_bits_to_f32(row[j]);
+    }
+}

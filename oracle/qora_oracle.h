@@ -115,6 +115,12 @@ int or_gqa_prefill_rows(const or_cfg* c, int S,
 int or_num_threads(void);
 void or_set_num_threads(int n);
 
+/* Q4 / F16 weight GEMV of the projections around the mixers (src/gemv.rs:286-300,
+ * 338-368, 411-450; format src/convert.rs:437-467). */
+void or_quantize_q4(const float* w, int k, int n, uint8_t* packed, uint16_t* scales);
+void or_gemv_q4(const float* x, const uint8_t* packed, const uint16_t* scales, int k, int n, float* y);
+void or_gemv_f16(const float* x, const uint16_t* w, int k, int n, float* y);
+
 #ifdef __cplusplus
 }
 #endif

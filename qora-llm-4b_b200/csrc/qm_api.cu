@@ -260,6 +260,8 @@ extern "C" int qm_ctx_destroy(qm_ctx* c) {
     if (c->ws) cudaFree(c->ws);
     if (c->stage) cudaFree(c->stage);
     if (c->d_err) cudaFree(c->d_err);
+    if (c->gemv_partial) cudaFree(c->gemv_partial);
+    if (c->gemv_count) cudaFree(c->gemv_count);
     drop_events(c);
     for (cudaEvent_t e : c->event_pool) cudaEventDestroy(e);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);

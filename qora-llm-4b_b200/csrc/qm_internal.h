@@ -61,6 +61,10 @@ struct qm_ctx {
     int host_parts[2] = {0, 0};     // parts of a DeltaNet / GQA _host call (0: default)
     bool host_direct = true;        // _host calls use page-locked buffers in place
     int64_t host_in_place = 0, host_staged = 0;  // _host calls by path
+    // qm_gemv: per-CTA partial sums of a column tile and the per-tile counters
+    void* gemv_partial = nullptr;
+    size_t gemv_partial_bytes = 0;
+    int* gemv_count = nullptr;
 };
 
 struct qm_dn_state {

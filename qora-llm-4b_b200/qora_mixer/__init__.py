@@ -48,7 +48,8 @@ EXPORTS = [
     "qm_gqa_decode_noalloc",
     "qm_dn_state_create_heads", "qm_dn_state_wrap_heads", "qm_dn_state_heads",
     "qm_kv_create_heads", "qm_kv_wrap_heads", "qm_kv_heads",
-    "qm_shard_plan", "qm_comm_unique_id", "qm_comm_create", "qm_comm_allgather", "qm_comm_enable_peer",
+    "qm_gemv", "qm_gemv_multi", "qm_shard_plan", "qm_comm_unique_id", "qm_comm_create", "qm_comm_allgather",
+    "qm_comm_enable_peer",
     "qm_comm_destroy",
 ]
 COMM_ID_BYTES = 128
@@ -75,6 +76,14 @@ class QmDnParams(C.Structure):
 class QmGqaParams(C.Structure):
     _fields_ = [("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("rope_cos", C.c_void_p),
                 ("rope_sin", C.c_void_p), ("max_pos", C.c_int)]
+
+
+class QmWeight(C.Structure):
+    _fields_ = [("kind", C.c_int), ("k", C.c_int), ("n", C.c_int), ("data", C.c_void_p),
+                ("scales", C.c_void_p)]
+
+
+W_F16, W_Q4 = 0, 1
 
 
 class QmShard(C.Structure):
@@ -150,6 +159,8 @@ def lib():
         "qm_kv_wrap_heads": ([P, I, I, I, I, P, P, PP], I),
         "qm_kv_heads": ([P, C.POINTER(I), C.POINTER(I)], I),
         "qm_shard_plan": ([I, I, C.POINTER(QmShard)], I),
+        "qm_gemv": ([P, C.POINTER(QmWeight), I, P, P], I),
+        "qm_gemv_multi": ([P, C.POINTER(QmWeight), I, I, P, C.POINTER(C.c_void_p)], I),
         "qm_comm_unique_id": ([P], I),
         "qm_comm_create": ([P, P, I, I, I, PP], I),
         "qm_comm_allgather": ([P, P, P, C.c_size_t], I),
@@ -418,6 +429,21 @@ def dn_params(conv_w, a_log, dt_bias, norm_gamma=None) -> QmDnParams:
     return QmDnParams(_ptr(conv_w), _ptr(a_log), _ptr(dt_bias), _ptr(norm_gamma))
 
 
+def weight_q4(packed, scales) -> QmWeight:
+    """Device Q4 weight (packed uint8 [k, n/2], f16 scale bits [k, n/32]) -> qm_weight."""
+    k, n = int(packed.shape[0]), int(packed.shape[1]) * 2
+    w = QmWeight(W_Q4, k, n, _ptr(packed), _ptr(scales))
+    w._keep = (packed, scales)  # the descriptor holds raw pointers: keep the buffers alive with it
+    return w
+
+
+def weight_f16(w16) -> QmWeight:
+    """Device f16 weight [k, n] (f16 or its bits) -> qm_weight."""
+    w = QmWeight(W_F16, int(w16.shape[0]), int(w16.shape[1]), _ptr(w16), None)
+    w._keep = (w16,)
+    return w
+
+
 def gqa_params(q_norm, k_norm, rope_cos, rope_sin) -> QmGqaParams:
     return QmGqaParams(_ptr(q_norm), _ptr(k_norm), _ptr(rope_cos), _ptr(rope_sin),
                        int(rope_cos.shape[0]))
@@ -428,6 +454,19 @@ class Mixer:
 
     def __init__(self, ctx: Ctx):
         self.ctx = ctx
+
+    def gemv(self, w: QmWeight, x, y):
+        """y[batch, n] = x[batch, k] . W (qm_gemv); x, y device f32."""
+        batch = int(x.shape[0]) if len(x.shape) == 2 else 1
+        self.ctx.check(lib().qm_gemv(self.ctx.handle, C.byref(w), batch, _ptr(x), _ptr(y)), "qm_gemv")
+
+    def gemv_multi(self, ws, x, ys):
+        """ys[i][batch, n_i] = x[batch, k] . W_i for up to 4 weights sharing x (qm_gemv_multi)."""
+        batch = int(x.shape[0]) if len(x.shape) == 2 else 1
+        arr = (QmWeight * len(ws))(*ws)
+        yp = (C.c_void_p * len(ys))(*[_ptr(y) for y in ys])
+        self.ctx.check(lib().qm_gemv_multi(self.ctx.handle, arr, len(ws), batch, _ptr(x), yp),
+                       "qm_gemv_multi")
 
     def dn_decode(self, p: QmDnParams, st: DnState, qkv, a, b, y=None, z=None, out=None):
         rc = lib().qm_dn_decode(self.ctx.handle, C.byref(p), st.handle, _ptr(qkv), _ptr(a),

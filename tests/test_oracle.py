@@ -268,3 +268,27 @@ def test_gqa_prefill_rows_equal_decode_loop_and_float64(orc):
     np.testing.assert_array_equal(vc, kv.v)
     ref, _ = refmath.gqa_prefill_rows_f64(qg, kk, vv, pr["q_norm"], pr["k_norm"], cos, sin, rows)
     assert refmath.rel_err(out, ref) < 2e-5
+
+
+def test_q4_restatement_quantizes_and_multiplies(orc):
+    """The Q4 restatement (src/convert.rs:437-467, src/gemv.rs:411-450): every
+    weight is within half a quantisation step of its f32 value (steps of
+    absmax/7 per group of 32), all-zero groups get scale 0, and the GEMV equals
+    x . dequantised W up to f32 rounding; the F16 GEMV likewise."""
+    g = np.random.default_rng(5)
+    w = (g.standard_normal((48, 96)) * 0.03).astype(np.float32)
+    w[3, 32:64] = 0.0
+    packed, scales = orc.quantize_q4(w)
+    sc = scales.view(np.float16).astype(np.float32)
+    assert sc[3, 1] == 0.0
+    step = np.repeat(np.abs(w).reshape(48, 3, 32).max(axis=2) / 7.0, 32, axis=1)
+    wd = orc.dequantize_q4(packed, scales)
+    # f16 rounding of the stored scale adds at most 2^-11 relative per step
+    assert (np.abs(wd - w) <= 0.5 * step * (1 + 8 * 2.0 ** -11) + 1e-12).all()
+    x = g.standard_normal(48).astype(np.float32)
+    ref = x.astype(np.float64) @ wd.astype(np.float64)
+    y = orc.gemv_q4(x, packed, scales)
+    assert np.abs(y - ref).max() <= 1e-5 * np.sqrt((ref ** 2).mean())
+    w16 = w.astype(np.float16).view(np.uint16)
+    ref16 = x.astype(np.float64) @ w.astype(np.float16).astype(np.float64)
+    assert np.abs(orc.gemv_f16(x, w16) - ref16).max() <= 1e-5 * np.sqrt((ref16 ** 2).mean())
