@@ -690,6 +690,81 @@ def bench_gemv(ctx, reps, batch=1, kind="q4"):
 
 
 # ----------------------------------------------------------------------------
+# the decode loop's tail: lm_head over the tied embedding (248,320 x 2,560),
+# penalties over a 512-token history, top-k / top-p sampling
+# ----------------------------------------------------------------------------
+VOCAB, HIDDEN = 248320, 2560
+
+
+def bench_head(ctx, reps, batch=1, kind="q4"):
+    import torch
+
+    import qora_mixer as qm
+
+    gen = torch.Generator(device="cuda").manual_seed(0x51A6)
+    if kind == "q4":
+        pk = torch.randint(0, 256, (VOCAB, HIDDEN // 2), dtype=torch.uint8, device="cuda", generator=gen)
+        sc = (torch.rand(VOCAB, HIDDEN // 32, device="cuda", generator=gen) * 0.01).half().view(torch.int16)
+        w = qm.weight_q4_rows(pk, sc)
+        nbytes = pk.numel() + sc.numel() * 2
+    else:
+        e16 = (torch.randn(VOCAB, HIDDEN, device="cuda", generator=gen) * 0.02).half().view(torch.int16)
+        w = qm.weight_f16_rows(e16)
+        nbytes = e16.numel() * 2
+    x = torch.randn(batch, HIDDEN, device="cuda", generator=gen)
+    logits = torch.empty(batch, VOCAB, device="cuda")
+    hist = 512
+    toks = torch.randint(0, VOCAB, (batch, hist), dtype=torch.int32, device="cuda", generator=gen)
+    lens = torch.full((batch,), hist, dtype=torch.int32, device="cuda")
+    r = torch.rand(batch, device="cuda", generator=gen)
+    ids = torch.empty(batch, dtype=torch.int32, device="cuda")
+    mx = qm.Mixer(ctx)
+    stream = torch.cuda.current_stream()
+
+    def head():
+        mx.gemv(w, x, logits)
+
+    def tail():
+        mx.penalize(logits, toks, lens, 1.1, 1.5, -1)
+        mx.sample(logits, 0.7, 0.95, 20, r, ids)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    h_ms = timed(head)
+    t_ms = timed(tail)
+    ctx.set_timing(True)
+    timed(tail)
+    pen_ms, pen_n = ctx.kernel_time("penalize")
+    smp_ms, smp_n = ctx.kernel_time("sample")
+    ctx.set_timing(False)
+    s_ms = timed(lambda: (head(), tail()))
+    peak, peak_kind = load_peaks()
+    launches_lm = (batch + (0 if kind == "q4" else 1)) // (1 if kind == "q4" else 2)
+    ach = nbytes * launches_lm / (h_ms / 1e3) / 1e9
+    del w, logits
+    torch.cuda.empty_cache()
+    return {"metric": "decode tail: lm_head + penalties + sampling", "workload":
+            f"lm_head over the tied embedding {VOCAB} x {HIDDEN} ({kind.upper()}, {nbytes / 1e6:.0f} MB), "
+            f"batch {batch}; repetition + presence penalties over {hist} tokens; top_k 20, top_p 0.95, T 0.7",
+            "value": round(batch / (s_ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(s_ms, 4),
+            "lm_head_ms": round(h_ms, 4), "penalize_ms": round(pen_ms / pen_n, 4),
+            "sample_ms": round(smp_ms / smp_n, 4), "tail_ms": round(t_ms, 4),
+            "roofline": {"bound": "hbm", "kernel": "qm_rows_kernel", "achieved": round(ach, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / peak, 4),
+                         "algorithmic_bytes_per_step": nbytes * launches_lm}}
+
+
+# ----------------------------------------------------------------------------
 # prefill (workload 2): DeltaNet chunked prefill, 8 x 8192 tokens, chunk 64
 # ----------------------------------------------------------------------------
 def bench_dn_prefill(ctx, ws, reps, B=8, T=8192):
@@ -916,10 +991,22 @@ def main():
     ap.add_argument("--prefill-len", type=int, help="with --prefill-only: tokens per sequence")
     ap.add_argument("--gemv-only", choices=["q4", "f16"],
                     help="time the 32 layers' mixer projections (Q4 / F16 weight GEMV) alone")
-    ap.add_argument("--gemv-batch", type=int, default=1, help="with --gemv-only: sequences per step")
+    ap.add_argument("--gemv-batch", type=int, default=1, help="with --gemv-only / --head-only: sequences per step")
+    ap.add_argument("--head-only", choices=["q4", "f16"],
+                    help="time the decode tail alone: lm_head, penalties and sampling")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.head_only:
+        import torch
+
+        import qora_mixer as qm
+
+        torch.cuda.set_device(0)
+        ctx = qm.Ctx(0, stream=torch.cuda.current_stream())
+        print(json.dumps(bench_head(ctx, args.steps, args.gemv_batch, args.head_only)), flush=True)
+        ctx.close()
+        return
     if args.gemv_only:
         import torch
 

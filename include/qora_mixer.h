@@ -331,6 +331,10 @@ int qm_gqa_decode_noalloc(const qm_gqa_params* p, uint16_t* k_cache, uint16_t* v
 #define QM_W_Q4 1   /* data: uint8 [k][n/2], even column in the low nibble, value */
                     /* q - 8; scales: f16 [k][n/32] (gemv_q4, src/gemv.rs:411-450; */
                     /* format src/convert.rs:437-467)                             */
+#define QM_W_F16_ROWS 2  /* one row per output, f16 [n][k]: the tied embedding as */
+                         /* lm_head (src/gemv.rs:664-676)                         */
+#define QM_W_Q4_ROWS 3   /* one row per output, packed [n][k/2] and f16 scales    */
+                         /* [n][k/32], groups of 32 along k (src/gemv.rs:677-707) */
 typedef struct qm_weight {
     int kind;            /* QM_W_F16 or QM_W_Q4 */
     int k, n;
@@ -354,6 +358,34 @@ int qm_gemv(qm_ctx* ctx, const qm_weight* w, int batch, const float* x, float* y
  * differ in k or kind.  ys is a host array of device pointers. */
 int qm_gemv_multi(qm_ctx* ctx, const qm_weight* ws, int count, int batch, const float* x,
                   float* const* ys);
+/* (Row-layout weights, QM_W_F16_ROWS / QM_W_Q4_ROWS, go through qm_gemv with
+ * one weight per call: logits[b][v] = x[b] . E[v], the reference's
+ * lm_head_parallel, src/gemv.rs:662-711.  Q4 rows need k % 32 == 0.) */
+
+/* ------------------------------------------------------------------ */
+/* The decode loop's tail (src/generate.rs:185-198), device pointers.  */
+/* ------------------------------------------------------------------ */
+/* Penalties on logits[batch][vocab] in the reference's order: repetition
+ * (src/generate.rs:58-69: over the last min(len, 64) tokens of each
+ * history, every occurrence divides a positive logit by the penalty or
+ * multiplies a non-positive one; off when <= 1), presence (72-83: every
+ * token of the history loses the penalty once; off when <= 0), then
+ * ban_token (>= 0) set to -inf (the EOS ban inside a think block, 191).
+ * Sequence b's history is tokens[b * stride + i], i < lens[b]. */
+int qm_logits_penalize(qm_ctx* ctx, float* logits, int batch, int vocab, const int* tokens,
+                       const int* lens, int stride, float repetition_penalty,
+                       float presence_penalty, int ban_token);
+/* sample_token_top_k (src/generate.rs:334-384) for each sequence:
+ * temperature <= 0 gives the first index of the largest logit; otherwise
+ * the top_k largest (value descending, index ascending), softmax at the
+ * temperature against the largest logit, the top-p nucleus, and the draw
+ * r[b] in [0, 1) (the reference's rng.next_f32(); the caller keeps the
+ * generator).  ids[b] receives the token.  top_k must resolve to at most
+ * 4096 candidates (QM_E_UNSUPPORTED otherwise; top_k 0 means the whole
+ * vocabulary).  Logits must not be NaN (the reference's order is then
+ * unspecified). */
+int qm_sample(qm_ctx* ctx, const float* logits, int batch, int vocab, float temperature,
+              float top_p, int top_k, const float* r, int* ids);
 
 /* ------------------------------------------------------------------ */
 /* Multi-GPU (one process per GPU).  The reference runs one device        */

@@ -68,6 +68,15 @@ def lib():
         L.or_quantize_q4.argtypes = [P, C.c_int, C.c_int, P, P]
         L.or_gemv_q4.argtypes = [P, P, P, C.c_int, C.c_int, P]
         L.or_gemv_f16.argtypes = [P, P, C.c_int, C.c_int, P]
+        L.or_lm_head_f16.argtypes = [P, P, C.c_int, C.c_int, P]
+        L.or_lm_head_q4.argtypes = [P, P, P, C.c_int, C.c_int, P]
+        L.or_repetition_penalty.argtypes = [P, C.c_int, P, C.c_int, C.c_float]
+        L.or_presence_penalty.argtypes = [P, C.c_int, P, C.c_int, C.c_float]
+        L.or_sample_top_k.argtypes = [P, C.c_int, C.c_float, C.c_float, C.c_int, C.c_float,
+                                      C.POINTER(C.c_double)]
+        L.or_sample_top_k.restype = C.c_int
+        L.or_rng_next_f32.argtypes = [C.POINTER(C.c_uint64)]
+        L.or_rng_next_f32.restype = C.c_float
         _lib = L
     return _lib
 
@@ -263,3 +272,52 @@ def gemv_f16(x, w16):
     y = np.empty(n, np.float32)
     lib().or_gemv_f16(_p(x), _p(np.ascontiguousarray(w16)), k, n, _p(y))
     return y
+
+
+def lm_head_f16(x, e16):
+    """src/gemv.rs:664-676: logits[v] = x . E[v] over f16 embedding rows (uint16 bits [vocab, hidden])."""
+    x = _f32(x)
+    vocab, hidden = e16.shape
+    y = np.empty(vocab, np.float32)
+    lib().or_lm_head_f16(_p(x), _p(np.ascontiguousarray(e16)), vocab, hidden, _p(y))
+    return y
+
+
+def lm_head_q4(x, packed, scales):
+    """src/gemv.rs:677-707: the same over Q4 rows (packed uint8 [vocab, hidden/2], f16 bits [vocab, hidden/32])."""
+    x = _f32(x)
+    vocab, hidden = packed.shape[0], packed.shape[1] * 2
+    y = np.empty(vocab, np.float32)
+    lib().or_lm_head_q4(_p(x), _p(np.ascontiguousarray(packed)), _p(np.ascontiguousarray(scales)), vocab,
+                        hidden, _p(y))
+    return y
+
+
+def penalize(logits, generated, repetition=1.0, presence=0.0, ban=-1):
+    """src/generate.rs:58-83 in the order of the decode loop (185-196): repetition,
+    then presence, then the banned token (-inf).  Returns a new array."""
+    out = _f32(logits).copy()
+    gen = np.ascontiguousarray(np.asarray(generated, np.int32))
+    lib().or_repetition_penalty(_p(out), out.size, _p(gen), gen.size, repetition)
+    lib().or_presence_penalty(_p(out), out.size, _p(gen), gen.size, presence)
+    if ban >= 0:
+        out[ban] = -np.inf
+    return out
+
+
+def sample_top_k(logits, temperature, top_p, top_k, r):
+    """src/generate.rs:334-384 with the draw r given: (token, margin)."""
+    lg = _f32(logits)
+    m = C.c_double()
+    tok = lib().or_sample_top_k(_p(lg), lg.size, temperature, top_p, top_k, r, C.byref(m))
+    return int(tok), float(m.value)
+
+
+class Rng:
+    """The reference's xorshift64 (src/generate.rs:41-55) with a fixed seed."""
+
+    def __init__(self, seed):
+        self.state = C.c_uint64(seed | 1)
+
+    def next_f32(self):
+        return float(lib().or_rng_next_f32(C.byref(self.state)))

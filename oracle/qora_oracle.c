@@ -619,3 +619,177 @@ void or_gemv_f16(const float* x, const uint16_t* w, int k, int n, float* y) {
         for (int j = 0; j < n; j++) y[j] += val * f16_bits_to_f32(row[j]);
     }
 }
+
+/* ------------------------------------------------------------------ */
+/* lm_head, logit penalties and sampling (the decode loop's tail)      */
+/* ------------------------------------------------------------------ */
+
+/* y[v] = x[hidden] . E[v][hidden] over the tied embedding rows, F16
+ * (src/gemv.rs:664-676): f32 products added in column order per row. */
+void or_lm_head_f16(const float* x, const uint16_t* e, int vocab, int hidden, float* y) {
+    for (int v = 0; v < vocab; v++) {
+        const uint16_t* row = e + (size_t)v * hidden;
+        float sum = 0.0f;
+        for (int j = 0; j < hidden; j++) sum += x[j] * f16_bits_to_f32(row[j]);
+        y[v] = sum;
+    }
+}
+
+/* The same for Q4 rows (src/gemv.rs:677-707): packed [vocab][hidden/2],
+ * scales [vocab][hidden/32]; groups with scale 0 are skipped, per group a
+ * table scale * (q - 8), dot += x[j] * table[q] in column order. */
+void or_lm_head_q4(const float* x, const uint8_t* packed, const uint16_t* scales, int vocab, int hidden,
+                   float* y) {
+    const int gs = 32, groups = hidden / gs;
+    for (int v = 0; v < vocab; v++) {
+        float dot = 0.0f;
+        for (int g = 0; g < groups; g++) {
+            const float scale = f16_bits_to_f32(scales[(size_t)v * groups + g]);
+            if (scale == 0.0f) continue;
+            float lut[16];
+            for (int i = 0; i < 16; i++) lut[i] = scale * (float)(i - 8);
+            const uint8_t* src = packed + (size_t)v * (hidden / 2) + (size_t)g * (gs / 2);
+            const float* xi = x + (size_t)g * gs;
+            for (int jj = 0; jj < gs / 2; jj++) {
+                dot += xi[2 * jj] * lut[src[jj] & 0x0F];
+                dot += xi[2 * jj + 1] * lut[src[jj] >> 4];
+            }
+        }
+        y[v] = dot;
+    }
+}
+
+/* Repetition penalty (src/generate.rs:58-69): over the last min(len, 64)
+ * generated tokens, each occurrence divides a positive logit by the penalty
+ * or multiplies a non-positive one; nothing when penalty <= 1. */
+void or_repetition_penalty(float* logits, int vocab, const int32_t* gen, int len, float penalty) {
+    if (penalty <= 1.0f) return;
+    const int window = len < 64 ? len : 64;
+    for (int i = len - window; i < len; i++) {
+        const int idx = gen[i];
+        if (idx >= 0 && idx < vocab) {
+            if (logits[idx] > 0.0f) logits[idx] /= penalty;
+            else logits[idx] *= penalty;
+        }
+    }
+}
+
+/* Presence penalty (src/generate.rs:72-83): every token seen at least once
+ * in the whole history loses `penalty` once; nothing when penalty <= 0 or the
+ * history is empty. */
+void or_presence_penalty(float* logits, int vocab, const int32_t* gen, int len, float penalty) {
+    if (penalty <= 0.0f || len == 0) return;
+    unsigned char* seen = (unsigned char*)calloc((size_t)vocab, 1);
+    for (int i = 0; i < len; i++)
+        if (gen[i] >= 0 && gen[i] < vocab) seen[gen[i]] = 1;
+    for (int v = 0; v < vocab; v++)
+        if (seen[v]) logits[v] -= penalty;
+    free(seen);
+}
+
+typedef struct {
+    int id;
+    float val;
+} or_cand;
+
+static int cand_desc(const void* a, const void* b) {
+    const or_cand* x = (const or_cand*)a;
+    const or_cand* y = (const or_cand*)b;
+    if (x->val > y->val) return -1;
+    if (x->val < y->val) return 1;
+    return x->id < y->id ? -1 : (x->id > y->id);  /* a stable sort keeps index order on ties */
+}
+
+/* sample_token_top_k (src/generate.rs:334-384) with the random draw r
+ * (rng.next_f32()) given.  Returns the token; *margin (when not NULL) is
+ * the smallest relative distance between a decision and its threshold
+ * (the top-p cutoff, where moving it would change the candidates' mass by
+ * more than 1e-5, and the draw against the running sums), so a test can
+ * tell a boundary case from a mismatch.  Logits must not be NaN (the
+ * reference's sort order is unspecified then). */
+int or_sample_top_k(const float* logits, int vocab, float temperature, float top_p, int top_k, float r,
+                    double* margin) {
+    if (margin) *margin = 1.0;
+    if (temperature <= 0.0f) {
+        int best = 0;
+        float bv = -INFINITY;
+        for (int i = 0; i < vocab; i++)
+            if (logits[i] > bv) {
+                bv = logits[i];
+                best = i;
+            }
+        return best;
+    }
+    const float inv_temp = 1.0f / temperature;
+    float max_logit = -INFINITY;
+    for (int i = 0; i < vocab; i++) max_logit = fmaxf(max_logit, logits[i]);
+    or_cand* c = (or_cand*)malloc(sizeof(or_cand) * (size_t)vocab);
+    for (int i = 0; i < vocab; i++) {
+        c[i].id = i;
+        c[i].val = logits[i];
+    }
+    qsort(c, (size_t)vocab, sizeof(or_cand), cand_desc);
+    const int k = top_k > 0 ? (top_k < vocab ? top_k : vocab) : vocab;
+    float* p = (float*)malloc(sizeof(float) * (size_t)k);
+    float sum = 0.0f;
+    for (int i = 0; i < k; i++) {
+        p[i] = expf((c[i].val - max_logit) * inv_temp);
+        sum += p[i];
+    }
+    int out;
+    if (sum <= 0.0f) {
+        out = c[0].id;
+    } else {
+        const float inv = 1.0f / sum;
+        for (int i = 0; i < k; i++) p[i] *= inv;
+        float cum = 0.0f;
+        int cutoff = k;
+        for (int i = 0; i < k; i++) {
+            cum += p[i];
+            /* a cut that flips here moves the candidate mass by ~(1 - cum):
+             * a boundary only when that is more than rounding */
+            if (margin && top_p != 0.0f && 1.0 - (double)cum > 1e-5) {
+                const double d = fabs((double)cum - (double)top_p) / fabs((double)top_p);
+                if (d < *margin) *margin = d;
+            }
+            if (cum >= top_p) {
+                cutoff = i + 1;
+                break;
+            }
+        }
+        float total = 0.0f;
+        for (int i = 0; i < cutoff; i++) total += p[i];
+        if (total <= 0.0f) {
+            out = c[0].id;
+        } else {
+            const float rv = r * total;
+            float acc = 0.0f;
+            out = c[0].id;
+            for (int i = 0; i < cutoff; i++) {
+                acc += p[i];
+                if (margin && rv != 0.0f) {
+                    const double d = fabs((double)acc - (double)rv) / (double)total;
+                    if (d < *margin) *margin = d;
+                }
+                if (acc >= rv) {
+                    out = c[i].id;
+                    break;
+                }
+            }
+        }
+    }
+    free(p);
+    free(c);
+    return out;
+}
+
+/* The reference's xorshift64 generator (src/generate.rs:41-55), for tests
+ * that draw r the way the reference's decode loop does. */
+float or_rng_next_f32(uint64_t* state) {
+    uint64_t s = *state;
+    s ^= s << 13;
+    s ^= s >> 7;
+    s ^= s << 17;
+    *state = s;
+    return (float)(s >> 40) / 16777216.0f;
+}

@@ -121,6 +121,16 @@ void or_quantize_q4(const float* w, int k, int n, uint8_t* packed, uint16_t* sca
 void or_gemv_q4(const float* x, const uint8_t* packed, const uint16_t* scales, int k, int n, float* y);
 void or_gemv_f16(const float* x, const uint16_t* w, int k, int n, float* y);
 
+/* lm_head over tied embedding rows, penalties, sampling */
+void or_lm_head_f16(const float* x, const uint16_t* e, int vocab, int hidden, float* y);
+void or_lm_head_q4(const float* x, const uint8_t* packed, const uint16_t* scales, int vocab, int hidden,
+                   float* y);
+void or_repetition_penalty(float* logits, int vocab, const int32_t* gen, int len, float penalty);
+void or_presence_penalty(float* logits, int vocab, const int32_t* gen, int len, float penalty);
+int or_sample_top_k(const float* logits, int vocab, float temperature, float top_p, int top_k, float r,
+                    double* margin);
+float or_rng_next_f32(uint64_t* state);
+
 #ifdef __cplusplus
 }
 #endif

@@ -385,6 +385,12 @@ extern "C" int qm_gemv_multi(qm_ctx* c, const qm_weight* ws, int count, int batc
     if (!ws || !x || !ys || count < 1 || batch < 1) return set_error(c, QM_E_ARG, "null pointer or empty batch");
     if (count > kGvJobs) return set_error(c, QM_E_SHAPE, "at most 4 weights per call");
     const int k = ws[0].k, kind = ws[0].kind;
+    if (kind == QM_W_F16_ROWS || kind == QM_W_Q4_ROWS) {  // one row per output: the lm_head kernel
+        if (count != 1) return set_error(c, QM_E_SHAPE, "row-layout weights take one weight per call");
+        if (!ws[0].data || !ys[0] || ws[0].k < 1 || ws[0].n < 1)
+            return set_error(c, QM_E_ARG, "null pointer or empty shape");
+        return gemv_rows(c, &ws[0], batch, x, ys[0]);
+    }
     const bool q4 = kind == QM_W_Q4;
     int tiles = 0;
     for (int i = 0; i < count; i++) {

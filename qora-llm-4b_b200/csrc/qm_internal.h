@@ -98,6 +98,8 @@ struct qm_kv {
 namespace qm {
 
 int set_error(qm_ctx* ctx, int code, const std::string& msg);
+// y[b][v] = x[b] . W[v] for QM_W_F16_ROWS / QM_W_Q4_ROWS weights (qm_head.cu)
+int gemv_rows(qm_ctx* c, const qm_weight* w, int batch, const float* x, float* y);
 int cuda_error(qm_ctx* ctx, cudaError_t e, const char* what);
 int ensure_workspace(qm_ctx* ctx, size_t bytes);
 int ensure_stage(qm_ctx* ctx, size_t bytes);

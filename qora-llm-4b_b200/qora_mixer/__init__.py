@@ -48,7 +48,7 @@ EXPORTS = [
     "qm_gqa_decode_noalloc",
     "qm_dn_state_create_heads", "qm_dn_state_wrap_heads", "qm_dn_state_heads",
     "qm_kv_create_heads", "qm_kv_wrap_heads", "qm_kv_heads",
-    "qm_gemv", "qm_gemv_multi", "qm_shard_plan", "qm_comm_unique_id", "qm_comm_create", "qm_comm_allgather",
+    "qm_gemv", "qm_gemv_multi", "qm_logits_penalize", "qm_sample", "qm_shard_plan", "qm_comm_unique_id", "qm_comm_create", "qm_comm_allgather",
     "qm_comm_enable_peer",
     "qm_comm_destroy",
 ]
@@ -83,7 +83,7 @@ class QmWeight(C.Structure):
                 ("scales", C.c_void_p)]
 
 
-W_F16, W_Q4 = 0, 1
+W_F16, W_Q4, W_F16_ROWS, W_Q4_ROWS = 0, 1, 2, 3
 
 
 class QmShard(C.Structure):
@@ -161,6 +161,8 @@ def lib():
         "qm_shard_plan": ([I, I, C.POINTER(QmShard)], I),
         "qm_gemv": ([P, C.POINTER(QmWeight), I, P, P], I),
         "qm_gemv_multi": ([P, C.POINTER(QmWeight), I, I, P, C.POINTER(C.c_void_p)], I),
+        "qm_logits_penalize": ([P, P, I, I, P, P, I, C.c_float, C.c_float, I], I),
+        "qm_sample": ([P, P, I, I, C.c_float, C.c_float, I, P, P], I),
         "qm_comm_unique_id": ([P], I),
         "qm_comm_create": ([P, P, I, I, I, PP], I),
         "qm_comm_allgather": ([P, P, P, C.c_size_t], I),
@@ -444,6 +446,21 @@ def weight_f16(w16) -> QmWeight:
     return w
 
 
+def weight_q4_rows(packed, scales) -> QmWeight:
+    """Device Q4 rows (packed uint8 [n, k/2], f16 scale bits [n, k/32]): the tied embedding as lm_head."""
+    n, k = int(packed.shape[0]), int(packed.shape[1]) * 2
+    w = QmWeight(W_Q4_ROWS, k, n, _ptr(packed), _ptr(scales))
+    w._keep = (packed, scales)
+    return w
+
+
+def weight_f16_rows(e16) -> QmWeight:
+    """Device f16 rows [n, k] (f16 or its bits)."""
+    w = QmWeight(W_F16_ROWS, int(e16.shape[1]), int(e16.shape[0]), _ptr(e16), None)
+    w._keep = (e16,)
+    return w
+
+
 def gqa_params(q_norm, k_norm, rope_cos, rope_sin) -> QmGqaParams:
     return QmGqaParams(_ptr(q_norm), _ptr(k_norm), _ptr(rope_cos), _ptr(rope_sin),
                        int(rope_cos.shape[0]))
@@ -459,6 +476,21 @@ class Mixer:
         """y[batch, n] = x[batch, k] . W (qm_gemv); x, y device f32."""
         batch = int(x.shape[0]) if len(x.shape) == 2 else 1
         self.ctx.check(lib().qm_gemv(self.ctx.handle, C.byref(w), batch, _ptr(x), _ptr(y)), "qm_gemv")
+
+    def penalize(self, logits, tokens=None, lens=None, repetition=1.0, presence=0.0, ban=-1):
+        """qm_logits_penalize on device logits [batch, vocab]; tokens int32 [batch, stride], lens int32 [batch]."""
+        batch, vocab = int(logits.shape[0]), int(logits.shape[1])
+        stride = int(tokens.shape[1]) if tokens is not None else 0
+        self.ctx.check(lib().qm_logits_penalize(self.ctx.handle, _ptr(logits), batch, vocab,
+                                                _ptr(tokens) if tokens is not None else None,
+                                                _ptr(lens) if lens is not None else None, stride,
+                                                repetition, presence, ban), "qm_logits_penalize")
+
+    def sample(self, logits, temperature, top_p, top_k, r, ids):
+        """qm_sample: ids[b] from device logits [batch, vocab] and draws r [batch] (device f32)."""
+        batch, vocab = int(logits.shape[0]), int(logits.shape[1])
+        self.ctx.check(lib().qm_sample(self.ctx.handle, _ptr(logits), batch, vocab, temperature, top_p,
+                                       top_k, _ptr(r) if r is not None else None, _ptr(ids)), "qm_sample")
 
     def gemv_multi(self, ws, x, ys):
         """ys[i][batch, n_i] = x[batch, k] . W_i for up to 4 weights sharing x (qm_gemv_multi)."""

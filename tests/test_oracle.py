@@ -292,3 +292,76 @@ def test_q4_restatement_quantizes_and_multiplies(orc):
     w16 = w.astype(np.float16).view(np.uint16)
     ref16 = x.astype(np.float64) @ w.astype(np.float16).astype(np.float64)
     assert np.abs(orc.gemv_f16(x, w16) - ref16).max() <= 1e-5 * np.sqrt((ref16 ** 2).mean())
+
+
+def _py_sample(l, temp, top_p, top_k, r):
+    """An independent pure-Python restatement of src/generate.rs:334-384 (f32 steps)."""
+    f = np.float32
+    l = l.astype(np.float32)
+    if temp <= 0:
+        best, bv = 0, -np.inf
+        for i, v in enumerate(l):
+            if v > bv:
+                best, bv = i, v
+        return best
+    inv, mx = f(1) / f(temp), f(l.max())
+    order = sorted(range(len(l)), key=lambda i: (-l[i], i))
+    k = min(top_k, len(l)) if top_k > 0 else len(l)
+    import math
+    p = [f(math.exp(float(f(f(l[i] - mx) * inv)))) for i in order[:k]]
+    s = f(0)
+    for v in p:
+        s = f(s + v)
+    p = [f(v * (f(1) / s)) for v in p]
+    cum, cut = f(0), k
+    for i, v in enumerate(p):
+        cum = f(cum + v)
+        if cum >= f(top_p):
+            cut = i + 1
+            break
+    tot = f(0)
+    for v in p[:cut]:
+        tot = f(tot + v)
+    rv, acc = f(f(r) * tot), f(0)
+    for i in range(cut):
+        acc = f(acc + p[i])
+        if acc >= rv:
+            return order[i]
+    return order[0]
+
+
+def test_sampling_and_penalty_restatement(orc):
+    """or_sample_top_k against a pure-Python restatement (the same token unless
+    the oracle's decision margin is below 1e-5: Python's exp is a double exp),
+    the reference's xorshift draws, and the penalties against their rules."""
+    g = np.random.default_rng(3)
+    rng = orc.Rng(4242)
+    checked = 0
+    for t in range(200):
+        l = (g.standard_normal(700) * 3).astype(np.float32)
+        if t % 5 == 0:
+            l = (np.round(l * 2) / 2).astype(np.float32)  # ties
+        temp, top_p, top_k = [(0.7, 0.95, 20), (1.0, 0.8, 0), (0.0, 0.9, 5), (1.2, 1.0, 700)][t % 4]
+        r = rng.next_f32()
+        tok, margin = orc.sample_top_k(l, temp, top_p, top_k, r)
+        if margin > 1e-5:
+            assert tok == _py_sample(l, temp, top_p, top_k, r), t
+            checked += 1
+    assert checked >= 190
+    s = orc.Rng(1)
+    st = 1
+    for _ in range(5):  # xorshift64 with shifts 13, 7, 17; the top 24 bits / 2^24
+        st ^= (st << 13) & 0xFFFFFFFFFFFFFFFF
+        st ^= st >> 7
+        st ^= (st << 17) & 0xFFFFFFFFFFFFFFFF
+        assert s.next_f32() == np.float32((st >> 40) / 16777216.0)
+    lg = g.standard_normal(40).astype(np.float32)
+    gen = [3, 3, 7, 10, 3] + [20] * 70  # 20 repeats past the 64-token window
+    out = orc.penalize(lg, gen, repetition=1.3, presence=1.5, ban=5)
+    exp = lg.copy()
+    for t in gen[-64:]:
+        exp[t] = exp[t] / np.float32(1.3) if exp[t] > 0 else exp[t] * np.float32(1.3)
+    for t in set(gen):
+        exp[t] -= np.float32(1.5)
+    exp[5] = -np.inf
+    np.testing.assert_array_equal(out, exp)
