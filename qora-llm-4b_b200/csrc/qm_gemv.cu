@@ -33,11 +33,13 @@
 // writes y.  Every sum is in a fixed order: the result does not depend on
 // timing.  BT <= 4 sequences per launch; larger batches run in groups of 4.
 //
-// Q4 nibble -> f32 without a shift: for the nibble q at bit 4j of a 16-bit
-// half of the word, (bits & (0xF << 4j)) | 0x4B000000 is the float
-// 2^23 + q 2^(4j) exactly, and subtracting 2^23 + 8 2^(4j) leaves
-// (q - 8) 2^(4j), exact; the column's sum is scaled by 2^(-4j) at the end
-// (exact).  One LOP3, one FADD and one FFMA per weight at batch 1.
+// Q4 nibble without a shift or a conversion: the nibble q at bit 4j of a
+// 16-bit half of the word, masked in place and read as a float, is the
+// denormal q 2^(4j - 149); times s x 2^(100 - 4j) (4 products a row) it is
+// q s x 2^-49 exactly, whatever j.  The column's sum is scaled back by 2^49
+// and the -8 of every nibble enters once as -8 sum(s x) over the lane's rows
+// (the same for its 32 columns).  One AND and one FFMA per weight at batch 1.
+// (Valid while |s x| < 2^27; denormals are not flushed: no fast math.)
 #include <cuda_fp16.h>
 
 #include <atomic>
@@ -148,10 +150,13 @@ qm_gemv_kernel(const __grid_constant__ GvArgs a) {
     __syncthreads();
 
     float acc[BT][CPL];
+    float sxsum[BT];  // Q4: the lane's sum of s x over its rows (the -8 of every nibble)
 #pragma unroll
-    for (int b = 0; b < BT; b++)
+    for (int b = 0; b < BT; b++) {
+        sxsum[b] = 0.f;
 #pragma unroll
         for (int i = 0; i < CPL; i++) acc[b][i] = 0.f;
+    }
 
     for (int base = 0; base < nrs; base += R) {
 #pragma unroll
@@ -161,9 +166,14 @@ qm_gemv_kernel(const __grid_constant__ GvArgs a) {
             const int r = stream + 16 * i;
             if (Q4) {
                 const float s = __half2float(__ushort_as_half((uint16_t)sv[u]));
-                float sx[BT];
+                float sxj[BT][4];  // s x 2^(100 - 4 jn): times the denormal nibble, q s x 2^-49
 #pragma unroll
-                for (int b = 0; b < BT; b++) sx[b] = s * xs[b * rps + r];
+                for (int b = 0; b < BT; b++) {
+                    const float sx = s * xs[b * rps + r];
+                    sxsum[b] += sx;
+#pragma unroll
+                    for (int jn = 0; jn < 4; jn++) sxj[b][jn] = sx * (1.2676506e30f / (float)(1u << (4 * jn)));
+                }
                 const uint32_t ww[4] = {wv[u][0].x, wv[u][0].y, wv[u][0].z, wv[u][0].w};
                 if (i + R < nrs) load_row(u, i + R);  // the slot's registers are copied: refill it
 #pragma unroll
@@ -173,12 +183,12 @@ qm_gemv_kernel(const __grid_constant__ GvArgs a) {
                     for (int hh = 0; hh < 2; hh++)
 #pragma unroll
                         for (int jn = 0; jn < 4; jn++) {
-                            // nibble 4 hh + jn of word wd: column 8 wd + 4 hh + jn of the lane's 32
-                            const float v = __uint_as_float((halves[hh] & (0xFu << (4 * jn))) | 0x4B000000u) -
-                                            (8388608.0f + (float)(8u << (4 * jn)));
+                            // nibble 4 hh + jn of word wd (column 8 wd + 4 hh + jn of the lane's
+                            // 32) masked in place: the denormal q 2^(4 jn - 149)
+                            const float v = __uint_as_float(halves[hh] & (0xFu << (4 * jn)));
 #pragma unroll
                             for (int b = 0; b < BT; b++)
-                                acc[b][8 * wd + 4 * hh + jn] = fmaf(v, sx[b], acc[b][8 * wd + 4 * hh + jn]);
+                                acc[b][8 * wd + 4 * hh + jn] = fmaf(v, sxj[b][jn], acc[b][8 * wd + 4 * hh + jn]);
                         }
                 }
             } else {
@@ -206,7 +216,7 @@ qm_gemv_kernel(const __grid_constant__ GvArgs a) {
     for (int b = 0; b < BT; b++)
 #pragma unroll
         for (int i = 0; i < CPL; i++) {
-            if (Q4) acc[b][i] *= 1.0f / (float)(1u << (4 * (i & 3)));  // undo the nibble's 2^(4j)
+            if (Q4) acc[b][i] = fmaf(acc[b][i], 562949953421312.0f, -8.0f * sxsum[b]);  // 2^49 sum q s x - 8 sum s x
             acc[b][i] += __shfl_xor_sync(0xffffffffu, acc[b][i], 16);
         }
     if (lane < 16) {

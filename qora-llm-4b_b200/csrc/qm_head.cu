@@ -13,9 +13,13 @@
 // 2^(-4 (j mod 4)) so the nibble trick of qm_gemv needs no shift (one LOP3,
 // one FADD and one FFMA per weight); a lane's 4 rows reuse the x chunk it
 // loaded.  Row sums are reduced across the warp in a fixed butterfly order.
-// Q4 is issue-bound here, not HBM-bound: the dequantisation costs three
-// instructions a weight on the CUDA cores (an L2 prefetch of the next rows
-// changed nothing); a tensor-core (mma) dequantising variant is the way on.
+// Q4 per weight is one AND and one FFMA: the nibble masked in place (no
+// shift) read as a float is the denormal q 2^(4j - 149), x is staged
+// prescaled by 2^(100 - 4j) (j = position mod 4), so their product is
+// q x 2^-49 exactly; the group's sum is scaled back by 2^49 and the -8 of
+// every nibble enters once a group as -8 sum(x), kept in the chunk's
+// padding slot.  (Valid for |x| < 2^27; denormals are not flushed: no fast
+// math.)
 //
 // qm_penalize_kernel: one CTA per sequence.  Repetition: the last
 // min(len, 64) tokens; the first occurrence of each token id applies all of
@@ -65,8 +69,16 @@ qm_rows_kernel(const void* __restrict__ data, const uint16_t* __restrict__ scale
     for (int i = tid; i < BT * k; i += kRwThreads) {
         const int b = i / k, j = i % k;
         float v = x[i];
-        if (Q4) v *= 1.0f / (float)(1u << (4 * (j & 3)));  // exact: a power of two
+        if (Q4) v *= 1.2676506e30f / (float)(1u << (4 * (j & 3)));  // x 2^(100 - 4 (j mod 4)): exact
         xs[(b * C + j / CW) * XS + j % CW] = v;
+    }
+    if (Q4) {  // each chunk's plain sum of x in its padding slot (for the -8 of every nibble)
+        for (int i = tid; i < BT * C; i += kRwThreads) {
+            const float* xc = x + (size_t)(i / C) * k + (size_t)(i % C) * CW;
+            float t = 0.f;
+            for (int j = 0; j < CW; j++) t += xc[j];
+            xs[i * XS + CW] = t;
+        }
     }
     __syncthreads();
     const int groups = (n + kRwRows - 1) / kRwRows;
@@ -117,6 +129,8 @@ qm_rows_kernel(const void* __restrict__ data, const uint16_t* __restrict__ scale
                     for (int rr = 0; rr < kRwRows; rr++) {
                         const uint32_t ww[4] = {w[rr][i].x, w[rr][i].y, w[rr][i].z, w[rr][i].w};
                         if (Q4) {
+                            // the nibble masked in place is the denormal q 2^(4j-149); times the
+                            // prescaled x it is q x 2^-49 exactly, whatever j
                             float part[4] = {0.f, 0.f, 0.f, 0.f};  // one chain per word: 4 independent FMA chains
 #pragma unroll
                             for (int wd = 0; wd < 4; wd++) {
@@ -124,16 +138,14 @@ qm_rows_kernel(const void* __restrict__ data, const uint16_t* __restrict__ scale
 #pragma unroll
                                 for (int hh = 0; hh < 2; hh++)
 #pragma unroll
-                                    for (int jn = 0; jn < 4; jn++) {
-                                        const float v =
-                                            __uint_as_float((halves[hh] & (0xFu << (4 * jn))) | 0x4B000000u) -
-                                            (8388608.0f + (float)(8u << (4 * jn)));
-                                        part[wd] = fmaf(v, xv[8 * wd + 4 * hh + jn], part[wd]);
-                                    }
+                                    for (int jn = 0; jn < 4; jn++)
+                                        part[wd] = fmaf(__uint_as_float(halves[hh] & (0xFu << (4 * jn))),
+                                                        xv[8 * wd + 4 * hh + jn], part[wd]);
                             }
-                            const float inner = (part[0] + part[1]) + (part[2] + part[3]);
+                            const float qx = ((part[0] + part[1]) + (part[2] + part[3])) * 562949953421312.0f;  // 2^49
+                            const float xsum = xs[(b * C + c) * XS + CW];
                             const float sc = __half2float(__ushort_as_half((uint16_t)s[rr][Q4 ? i : 0]));
-                            acc[b][rr] = fmaf(sc, inner, acc[b][rr]);
+                            acc[b][rr] = fmaf(sc, fmaf(-8.0f, xsum, qx), acc[b][rr]);
                         } else {
 #pragma unroll
                             for (int q = 0; q < 4; q++) {
