@@ -28,14 +28,15 @@
 // atomic clear finds the bit set subtracts the penalty, so each seen token
 // loses it exactly once.  Then the banned token (if any) becomes -inf.
 //
-// qm_sample_kernel: a cluster of 8 CTAs of 1024 threads per sequence, each
-// over 1/8 of the vocabulary (the histograms and candidate lists meet in
+// qm_sample_kernel: a cluster of 16 CTAs of 1024 threads per sequence, each
+// over 1/16 of the vocabulary, each thread's 16 logits read once and kept
+// as keys in registers (the histograms and candidate lists meet in
 // distributed shared memory; rank 0 sorts and draws).  Greedy
 // (temperature <= 0): the first index of the largest logit.  Otherwise the
 // k largest logits in the reference's order (value descending, index
 // ascending: its stable sort) are found with a radix select on the
 // order-preserving 32-bit key (4 passes of 8 bits with one histogram per
-// warp, the first also taking the maximum), collected (ties at the
+// warp), collected (ties at the
 // threshold: lowest indices first) and bitonic-sorted in shared memory; one
 // thread then runs the reference's softmax / top-p / draw with its f32
 // operations in its order.
@@ -248,7 +249,8 @@ qm_penalize_kernel(float* logits, int vocab, const int* __restrict__ tokens, con
 // ---------------------------------------------------------------------------
 constexpr int kSmThreads = 1024;
 constexpr int kSmWarps = kSmThreads / 32;
-constexpr int kSmCluster = 8;  // CTAs per sequence, each over 1/8 of the vocabulary
+constexpr int kSmCluster = 16;  // CTAs per sequence, each over 1/16 of the vocabulary
+constexpr int kSmPer = 16;      // keys a thread holds in registers: vocab <= 16 x 1024 x 16
 constexpr int kSmMaxK = 4096;
 constexpr int kSmBins = 256;  // 8-bit digits, one histogram per warp
 
@@ -350,32 +352,35 @@ qm_sample_kernel(const float* __restrict__ logits, int vocab, float temperature,
     }
     const int k = top_k > 0 ? (top_k < vocab ? top_k : vocab) : vocab;
 
+    // this thread's logits lo + tid + 1024 e, read once (all in flight) and
+    // kept as order-preserving keys for every pass; the maximum on the way
+    float mx = -INFINITY;
+    uint32_t keys[kSmPer];
+    const int nmine = hi - lo - tid > 0 ? (hi - lo - tid + kSmThreads - 1) / kSmThreads : 0;
+    {
+        float v[kSmPer];
+#pragma unroll
+        for (int e = 0; e < kSmPer; e++) v[e] = e < nmine ? lg[lo + tid + e * kSmThreads] : -INFINITY;
+#pragma unroll
+        for (int e = 0; e < kSmPer; e++) {
+            mx = fmaxf(mx, v[e]);
+            keys[e] = order_key(v[e]);
+        }
+    }
+
     // radix select of the k-th largest key, 8 bits a pass from the top.  Each
     // warp counts its elements into its own histogram; the CTA adds its 32,
-    // the cluster adds its 8 CTAs' (every CTA the same sums, so every CTA
-    // picks the same digit).  The first pass also takes the maximum.
+    // the cluster adds its 16 CTAs' (every CTA the same sums, so every CTA
+    // picks the same digit).
     uint32_t prefix = 0u, pmask = 0u, kleft = (uint32_t)k;
-    float mx = -INFINITY;
     uint32_t* myhist = whist + warp * kSmBins;
     for (int pass = 0; pass < 4; pass++) {
         const int sh = 24 - 8 * pass;
         for (int i = tid; i < kSmWarps * kSmBins; i += kSmThreads) whist[i] = 0u;
         __syncthreads();
-        for (int i0 = lo; i0 < hi; i0 += 4 * kSmThreads) {
-            float v[4];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int i = i0 + u * kSmThreads + tid;
-                v[u] = i < hi ? lg[i] : 0.f;
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                if (i0 + u * kSmThreads + tid >= hi) continue;
-                if (pass == 0) mx = fmaxf(mx, v[u]);
-                const uint32_t key = order_key(v[u]);
-                if ((key & pmask) == prefix) atomicAdd(&myhist[(key >> sh) & 255u], 1u);
-            }
-        }
+        for (int e = 0; e < kSmPer; e++)
+            if (e < nmine && (keys[e] & pmask) == prefix) atomicAdd(&myhist[(keys[e] >> sh) & 255u], 1u);
         if (pass == 0) {
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -393,27 +398,59 @@ qm_sample_kernel(const float* __restrict__ logits, int vocab, float temperature,
             sh_cmax = m;
         }
         cluster_sync_all();  // every CTA's histogram (and maximum) is complete
-        if (tid < kSmBins) {
+        if (tid < kSmBins) {  // all 16 remote loads in flight, then the adds in rank order
+            uint32_t h8[kSmCluster];
+#pragma unroll
+            for (int q = 0; q < kSmCluster; q++) h8[q] = dsmem_u32(&chist[tid], (uint32_t)q);
             uint32_t tot = 0u;
-            for (uint32_t q = 0; q < kSmCluster; q++) tot += dsmem_u32(&chist[tid], q);
+#pragma unroll
+            for (int q = 0; q < kSmCluster; q++) tot += h8[q];
             ghist[tid] = tot;
         }
-        if (pass == 0 && tid == 0) {
+        if (pass == 0 && tid == kSmBins) {
+            float m8[kSmCluster];
+#pragma unroll
+            for (int q = 0; q < kSmCluster; q++) m8[q] = __uint_as_float(dsmem_u32(&sh_cmax, (uint32_t)q));
             float m = -INFINITY;
-            for (uint32_t q = 0; q < kSmCluster; q++) m = fmaxf(m, __uint_as_float(dsmem_u32(&sh_cmax, q)));
+#pragma unroll
+            for (int q = 0; q < kSmCluster; q++) m = fmaxf(m, m8[q]);
             red_f[0] = m;
         }
         __syncthreads();
-        if (tid == 0) {
-            uint32_t cum = 0u;
-            int d = kSmBins - 1;
-            for (; d > 0; d--) {
-                if (cum + ghist[d] >= kleft) break;
-                cum += ghist[d];
+        if (warp == 0) {  // the digit: the highest d with (count above d) < kleft <= (count from d up)
+            // lane l owns bins [8 (31 - l), 8 (31 - l) + 8): lane 0 the top 8
+            uint32_t c8[8], own = 0u;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                c8[e] = ghist[8 * (31 - lane) + 7 - e];  // e = 0: this lane's highest bin
+                own += c8[e];
             }
-            sh_digit = (uint32_t)d;
-            sh_kleft = kleft - cum;
-            if (pass == 3) sh_eq_total = ghist[d];
+            uint32_t above = own;  // inclusive prefix over lanes 0..lane (bins from the top)
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const uint32_t o = __shfl_up_sync(0xffffffffu, above, off);
+                if (lane >= off) above += o;
+            }
+            above -= own;  // count in the bins above this lane's
+            const bool mine = above < kleft && above + own >= kleft;
+            const uint32_t who = __ballot_sync(0xffffffffu, mine);
+            if (who == 0u) {  // cannot happen while kleft <= the matching count; take bin 0
+                if (lane == 31) {
+                    sh_digit = 0u;
+                    sh_kleft = kleft - (above + own - c8[7]);
+                    if (pass == 3) sh_eq_total = c8[7];
+                }
+            } else if (lane == __ffs(who) - 1) {
+                uint32_t cum = above;
+                int e = 0;
+                for (; e < 7; e++) {
+                    if (cum + c8[e] >= kleft) break;
+                    cum += c8[e];
+                }
+                sh_digit = (uint32_t)(8 * (31 - lane) + 7 - e);
+                sh_kleft = kleft - cum;
+                if (pass == 3) sh_eq_total = c8[e];
+            }
         }
         __syncthreads();
         if (pass == 0) mx = red_f[0];
@@ -428,9 +465,10 @@ qm_sample_kernel(const float* __restrict__ logits, int vocab, float temperature,
     if (tid == 0) sh_count = 0;
     __syncthreads();
     if (all_eq) {  // no tie straddles the cut: every key >= T is a candidate
-        for (int i = lo + tid; i < hi; i += kSmThreads) {
-            const uint32_t key = order_key(lg[i]);
-            if (key >= T) lcand[atomicAdd(&sh_count, 1)] = ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)i);
+#pragma unroll
+        for (int e = 0; e < kSmPer; e++) {
+            const uint32_t i = (uint32_t)(lo + tid + e * kSmThreads);
+            if (e < nmine && keys[e] >= T) lcand[atomicAdd(&sh_count, 1)] = ((unsigned long long)keys[e] << 32) | (0xFFFFFFFFu - i);
         }
     } else {  // keys > T, then the k_eq lowest-index keys == T: warp ranges, then CTAs, in index order
         const int span = hi > lo ? hi - lo : 0;
@@ -606,6 +644,8 @@ extern "C" int qm_sample(qm_ctx* c, const float* logits, int batch, int vocab, f
     if (!logits || !ids || batch < 1 || vocab < 1) return set_error(c, QM_E_ARG, "null pointer or empty shape");
     if (!(temperature <= 0.0f)) {  // not greedy (as the reference tests it)
         if (!r) return set_error(c, QM_E_ARG, "sampling needs the draws r");
+        if (vocab > kSmCluster * kSmThreads * kSmPer)
+            return set_error(c, QM_E_UNSUPPORTED, "sampling holds at most 262,144 logits a sequence");
         const int k = top_k > 0 ? (top_k < vocab ? top_k : vocab) : vocab;
         if (k > kSmMaxK)
             return set_error(c, QM_E_UNSUPPORTED, "top_k must be in [1, 4096] (or the vocabulary at most 4096)");
@@ -615,8 +655,8 @@ extern "C" int qm_sample(qm_ctx* c, const float* logits, int batch, int vocab, f
     static std::atomic<uint64_t> attr_set{0};
     const uint64_t bit = 1ull << (c->device & 63);
     if (!(attr_set.load() & bit)) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(qm_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(qm_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(qm_sample_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return cuda_error(c, e, "qm_sample setup");
         attr_set.fetch_or(bit);
     }
