@@ -690,6 +690,54 @@ def bench_gemv(ctx, reps, batch=1, kind="q4"):
 
 
 # ----------------------------------------------------------------------------
+# prefill projections: the Q4 GEMM over a whole prompt (tensor cores)
+# ----------------------------------------------------------------------------
+GEMM_SHAPES = [("in_proj_qkv / q_proj", 2560, 8192), ("in_proj_z", 2560, 4096), ("out_proj / o_proj", 4096, 2560),
+               ("k_proj / v_proj", 2560, 1024)]
+
+
+def bench_gemm(ctx, reps, T=8192):
+    import torch
+
+    import qora_mixer as qm
+
+    gen = torch.Generator(device="cuda").manual_seed(0x51A7)
+    mx = qm.Mixer(ctx)
+    stream = torch.cuda.current_stream()
+    peak, peak_kind = load_tensor_peak()
+    rows, tot_flops, tot_ms = [], 0.0, 0.0
+    for name, k, n in GEMM_SHAPES:
+        pk = torch.randint(0, 256, (k, n // 2), dtype=torch.uint8, device="cuda", generator=gen)
+        sc = (torch.rand(k, n // 32, device="cuda", generator=gen) * 0.01).half().view(torch.int16)
+        w = qm.weight_q4(pk, sc)
+        x = torch.randn(T, k, device="cuda", generator=gen).bfloat16().view(torch.int16)
+        y = torch.empty(T, n, device="cuda")
+        for _ in range(3):
+            mx.gemm(w, x, y)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            mx.gemm(w, x, y)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        flops = 2.0 * T * k * n
+        rows.append({"weight": name, "k": k, "n": n, "ms": round(ms, 4),
+                     "tflops": round(flops / (ms / 1e3) / 1e12, 1)})
+        tot_flops += flops
+        tot_ms += ms
+        del pk, sc, w, x, y
+    torch.cuda.empty_cache()
+    ach = tot_flops / (tot_ms / 1e3) / 1e12
+    return {"metric": "prefill projections (Q4 GEMM)", "workload": f"{T} tokens x the 4B's projection shapes, "
+            "bf16 x, Q4 weights dequantised to bf16 in the kernel, f32 y", "per_shape": rows,
+            "value": round(T / (tot_ms / 1e3), 1), "unit": "tok/s (the 4 shapes once each)",
+            "roofline": {"bound": "tensor", "kernel": "qm_gemm_q4_kernel", "achieved": round(ach, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": round(ach / peak, 4)}}
+
+
+# ----------------------------------------------------------------------------
 # the decode loop's tail: lm_head over the tied embedding (248,320 x 2,560),
 # penalties over a 512-token history, top-k / top-p sampling
 # ----------------------------------------------------------------------------
@@ -992,11 +1040,22 @@ def main():
     ap.add_argument("--gemv-only", choices=["q4", "f16"],
                     help="time the 32 layers' mixer projections (Q4 / F16 weight GEMV) alone")
     ap.add_argument("--gemv-batch", type=int, default=1, help="with --gemv-only / --head-only: sequences per step")
+    ap.add_argument("--gemm-only", action="store_true", help="time the Q4 prefill projection GEMM alone")
     ap.add_argument("--head-only", choices=["q4", "f16"],
                     help="time the decode tail alone: lm_head, penalties and sampling")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.gemm_only:
+        import torch
+
+        import qora_mixer as qm
+
+        torch.cuda.set_device(0)
+        ctx = qm.Ctx(0, stream=torch.cuda.current_stream())
+        print(json.dumps(bench_gemm(ctx, args.steps, args.prefill_len or 8192)), flush=True)
+        ctx.close()
+        return
     if args.head_only:
         import torch
 

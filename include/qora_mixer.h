@@ -358,6 +358,13 @@ int qm_gemv(qm_ctx* ctx, const qm_weight* w, int batch, const float* x, float* y
  * differ in k or kind.  ys is a host array of device pointers. */
 int qm_gemv_multi(qm_ctx* ctx, const qm_weight* ws, int count, int batch, const float* x,
                   float* const* ys);
+/* y[T][n] = x[T][k] . W for a whole prompt on the tensor cores: the
+ * reference's gemm over seq_len tokens (src/gemv.rs:294-300, its prefill at
+ * 1114-1117, 1222, 1366-1385).  Q4 weights only, k % 64 == 0, n % 32 == 0;
+ * x bf16 [T][k] (16-byte aligned, as the prefill mixers take their inputs),
+ * y f32 [T][n].  The weights are dequantised to bf16 on the way in:
+ * max|y - exact| / RMS(y) is a few 1e-3. */
+int qm_gemm(qm_ctx* ctx, const qm_weight* w, int T, const uint16_t* x, float* y);
 /* (Row-layout weights, QM_W_F16_ROWS / QM_W_Q4_ROWS, go through qm_gemv with
  * one weight per call: logits[b][v] = x[b] . E[v], the reference's
  * lm_head_parallel, src/gemv.rs:662-711.  Q4 rows need k % 32 == 0.) */

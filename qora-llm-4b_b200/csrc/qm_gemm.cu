@@ -1,0 +1,259 @@
+// Prefill projections: Y[T][n] = X[T][k] . W for Q4 weights over a whole
+// prompt (the reference's gemm / gemm_q4, src/gemv.rs:294-300, used by its
+// prefill at src/gemv.rs:1114-1117, 1222 and 1366-1385).  At T tokens each
+// weight is reused T times, so this is a tensor-core GEMM, not a stream.
+//
+// qm_gemm_q4_kernel: one CTA per 128 x 256 tile of Y, K in steps of 64.
+//  * warp 0 (one thread) loads X tiles [128 tokens x 64 k] bf16 with TMA
+//    (128-byte swizzle: the K-major A operand);
+//  * warps 2-7 dequantise the matching W tile [64 k x 256 n] from the
+//    reference's Q4 layout (packed nibbles [k][n/2], f16 scales [k][n/32])
+//    to bf16 s (q - 8) (the next stage's words in flight while this one is
+//    converted), written into shared memory in the layout a
+//    128-byte-swizzled TMA box of [64 k rows x 64 n] would have (the
+//    MN-major B operand: 4 boxes for 256 columns);
+//  * warp 1 allocates 256 TMEM columns (D: 128 lanes x 256 f32) and one
+//    thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32, M 128,
+//    N 256, K 16) four times per stage, each stage released to the producers
+//    by tcgen05.commit;
+//  * warps 4-7 read D out of TMEM (their lane quarters) and store Y (f32).
+// A ring of 4 stages (48 KB each) keeps loads, dequantisation and MMAs
+// overlapped.  Every wait is bounded: on a timeout the kernel sets the
+// context's error word and an abort flag, the TMA thread waits (bounded) for
+// its copies in flight, and TMEM is freed before the CTA leaves.
+// W in bf16 carries 8 bits of mantissa: max|y - y_exact| / RMS(y) stays
+// within a few 1e-3 (the prefill tolerance is 2e-2).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <atomic>
+
+#include "qm_internal.h"
+#include "qm_ptx.cuh"
+
+namespace qm {
+int encode_rows_tmap(CUtensorMap* m, void* base, uint64_t inner, uint64_t rows, uint64_t planes,
+                     uint32_t box_inner, uint32_t box_rows, bool fp16);
+namespace {
+
+constexpr int kGmBM = 128, kGmBN = 256, kGmBK = 64, kGmStages = 4;
+constexpr int kGmXBox = kGmBM * 128;             // [128 rows x 64 bf16] = 16 KB
+constexpr int kGmWBox = kGmBK * 128;             // [64 k rows x 64 n bf16] = 8 KB
+constexpr int kGmStage = kGmXBox + 4 * kGmWBox;  // 48 KB
+constexpr int kGmOffBar = kGmStages * kGmStage;  // 192 KB
+constexpr int kGmSmem = kGmOffBar + 256 + 1024;  // + barriers + alignment slack
+constexpr int kGmThreads = 256;
+constexpr int kGmProdWarps = 6;  // warps 2..7
+constexpr int kGmChunks = (kGmBK * (kGmBN / 8) + kGmProdWarps * 32 - 1) / (kGmProdWarps * 32);  // 11 a thread
+constexpr int kGmTmCols = 256;
+constexpr uint32_t kGmIdesc = umma_idesc_bf16(kGmBM, kGmBN, false, true);  // A K-major, B MN-major
+
+struct GmBars {
+    uint64_t x_full[kGmStages], w_full[kGmStages], free_[kGmStages], done;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+static_assert(sizeof(GmBars) <= 256, "barrier block");
+
+__global__ void __launch_bounds__(kGmThreads, 1)
+qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restrict__ packed,
+                  const uint16_t* __restrict__ scales, int T, int K, int N, float* __restrict__ y, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    GmBars* bars = reinterpret_cast<GmBars*>(smem + kGmOffBar);
+    volatile int* abort_flag = &bars->abort_flag;
+    const uint32_t sbase = smem_u32(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_n = (N + kGmBN - 1) / kGmBN;
+    const int tm = blockIdx.x / tiles_n, tn = blockIdx.x % tiles_n;
+    const int nk = K / kGmBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kGmStages; s++) {
+            mbar_init(smem_u32(&bars->x_full[s]), 1);
+            mbar_init(smem_u32(&bars->w_full[s]), kGmProdWarps);
+            mbar_init(smem_u32(&bars->free_[s]), 1);
+        }
+        mbar_init(smem_u32(&bars->done), 1);
+        bars->abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(&bars->tmem_base), kGmTmCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {  // X tiles by TMA
+            prefetch_tmap(&tmx);
+            int issued = 0;
+            for (int i = 0; i < nk; i++) {
+                const int s = i % kGmStages;
+                if (i >= kGmStages &&
+                    !mbar_wait_bounded(smem_u32(&bars->free_[s]), ((i / kGmStages) - 1) & 1, abort_flag, err)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                const uint32_t xb = smem_u32(&bars->x_full[s]);
+                mbar_arrive_expect_tx(xb, kGmXBox);
+                tma_load_3d(sbase + s * kGmStage, &tmx, i * kGmBK, tm * kGmBM, 0, xb);
+                issued = i + 1;
+            }
+            // every copy this thread issued has landed before the CTA can leave
+            for (int i = issued - kGmStages > 0 ? issued - kGmStages : 0; i < issued; i++)
+                mbar_drain(smem_u32(&bars->x_full[i % kGmStages]), (i / kGmStages) & 1);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issue
+            bool ok = true;
+            for (int i = 0; i < nk && ok; i++) {
+                const int s = i % kGmStages;
+                const uint32_t par = (i / kGmStages) & 1;
+                ok = mbar_wait_bounded(smem_u32(&bars->x_full[s]), par, abort_flag, err) &&
+                     mbar_wait_bounded(smem_u32(&bars->w_full[s]), par, abort_flag, err);
+                if (!ok) {
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t xs = sbase + s * kGmStage, ws = xs + kGmXBox;
+#pragma unroll
+                for (int kk = 0; kk < kGmBK / 16; kk++) {
+                    const uint64_t ad = umma_sdesc(xs + kk * 32, 16, 1024);
+                    const uint64_t bd = umma_sdesc(ws + kk * 2048, kGmWBox, 1024);
+                    umma_bf16_ss(tmem, ad, bd, kGmIdesc, (i > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&bars->free_[s]));
+            }
+            umma_commit(smem_u32(&bars->done));  // every MMA issued above has completed
+        }
+    } else {  // warps 2..7: dequantise W tiles
+        // thread pt takes chunks q = pt + 192 m (row q / 32, 8 columns at (q % 32) * 8) of every
+        // stage; the next stage's words are loaded while this stage's are converted
+        const int pt = threadIdx.x - 64;  // 0..191
+        const int n0_tile = tn * kGmBN;
+        uint32_t wA[kGmChunks], wB[kGmChunks];
+        uint16_t sA[kGmChunks], sB[kGmChunks];
+        auto load_stage = [&](int i, uint32_t(&wv)[kGmChunks], uint16_t(&sv)[kGmChunks]) {
+#pragma unroll
+            for (int m = 0; m < kGmChunks; m++) {
+                const int q = pt + m * kGmProdWarps * 32;
+                const int r = q >> 5, n0 = n0_tile + (q & 31) * 8;
+                const bool ok = q < kGmBK * (kGmBN / 8) && n0 < N && i < nk;
+                const size_t kr = (size_t)i * kGmBK + r;
+                wv[m] = ok ? __ldg(reinterpret_cast<const unsigned int*>(packed + kr * (N / 2) + n0 / 2)) : 0x88888888u;
+                sv[m] = ok ? __ldg(reinterpret_cast<const unsigned short*>(scales + kr * (N / 32) + n0 / 32)) : (uint16_t)0;
+            }
+        };
+        // stage i into its ring slot (after the MMAs that read the slot last are done)
+        auto convert_stage = [&](int i, const uint32_t(&wv)[kGmChunks], const uint16_t(&sv)[kGmChunks]) -> bool {
+            const int s = i % kGmStages;
+            if (i >= kGmStages &&
+                !mbar_wait_bounded(smem_u32(&bars->free_[s]), ((i / kGmStages) - 1) & 1, abort_flag, err)) {
+                *abort_flag = 1;
+                return false;
+            }
+            uint8_t* wt = smem + s * kGmStage + kGmXBox;
+#pragma unroll
+            for (int m = 0; m < kGmChunks; m++) {
+                const int q = pt + m * kGmProdWarps * 32;
+                if (q >= kGmBK * (kGmBN / 8)) break;
+                const int r = q >> 5, ch = q & 31;
+                const float sc = __half2float(__ushort_as_half(sv[m]));
+                const uint32_t w = wv[m];
+                uint32_t pk[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    // (q - 8) exactly: 2^23 + q read as a float, minus 2^23 + 8
+                    const float lo = (__uint_as_float(0x4B000000u | ((w >> (8 * j)) & 0xFu)) - 8388616.0f) * sc;
+                    const float hi = (__uint_as_float(0x4B000000u | ((w >> (8 * j + 4)) & 0xFu)) - 8388616.0f) * sc;
+                    const __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
+                    pk[j] = *reinterpret_cast<const uint32_t*>(&b2);
+                }
+                *reinterpret_cast<uint4*>(wt + (ch >> 3) * kGmWBox + sw128_off(r, ch & 7)) =
+                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&bars->w_full[s]));
+            return true;
+        };
+        load_stage(0, wA, sA);
+        for (int i = 0; i < nk; i += 2) {  // two stages a turn: each buffer a fixed register set
+            load_stage(i + 1, wB, sB);
+            if (!convert_stage(i, wA, sA) || i + 1 >= nk) break;
+            load_stage(i + 2, wA, sA);
+            if (!convert_stage(i + 1, wB, sB)) break;
+        }
+        if (warp >= 4) {  // epilogue: TMEM lane quarter warp & 3
+            if (mbar_wait_bounded(smem_u32(&bars->done), 0, abort_flag, err) && !*abort_flag) {
+                tc_fence_after();
+                const int quarter = warp & 3;
+                const int row = tm * kGmBM + quarter * 32 + lane;
+                const uint32_t la = (uint32_t)(quarter * 32) << 16;
+                for (int c = 0; c < kGmBN / 32; c++) {
+                    float v[32];
+                    tmem_ld32(tmem + la + c * 32, v);
+                    tmem_ld_wait();
+                    const int col = n0_tile + c * 32;
+                    if (row < T && col < N) {
+                        float* dst = y + (size_t)row * N + col;
+#pragma unroll
+                        for (int q = 0; q < 8; q++)
+                            *reinterpret_cast<float4*>(dst + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    }
+                }
+            }
+        }
+    }
+    // the MMA thread committed `done` on every path: once it completes, no
+    // MMA still writes TMEM
+    if (warp == 1 && lane == 0) mbar_drain(smem_u32(&bars->done), 0);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kGmTmCols);
+    }
+}
+
+}  // namespace
+}  // namespace qm
+
+using namespace qm;
+
+extern "C" int qm_gemm(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, float* y) {
+    if (!c) return QM_E_ARG;
+    if (!w || !x || !y || !w->data || T < 1 || w->k < 1 || w->n < 1)
+        return set_error(c, QM_E_ARG, "null pointer or empty shape");
+    if (w->kind != QM_W_Q4) return set_error(c, QM_E_UNSUPPORTED, "qm_gemm takes Q4 weights ([k][n/2] + scales)");
+    if (!w->scales) return set_error(c, QM_E_ARG, "Q4 weights need scales");
+    if (w->k % kGmBK || w->n % 32) return set_error(c, QM_E_SHAPE, "qm_gemm needs k % 64 == 0 and n % 32 == 0");
+    if (((uintptr_t)x & 15) || ((uintptr_t)y & 15) || ((uintptr_t)w->data & 3) || ((uintptr_t)w->scales & 1))
+        return set_error(c, QM_E_ARG, "x and y must be 16-byte, data 4-byte and scales 2-byte aligned");
+    cudaSetDevice(c->device);
+    CUtensorMap tmx;
+    if (encode_rows_tmap(&tmx, const_cast<uint16_t*>(x), (uint64_t)w->k, (uint64_t)T, 1, 64, kGmBM, false) != QM_OK)
+        return set_error(c, QM_E_CUDA, "cuTensorMapEncodeTiled failed for x");
+    static std::atomic<uint64_t> attr_set{0};
+    const uint64_t bit = 1ull << (c->device & 63);
+    if (!(attr_set.load() & bit)) {
+        const cudaError_t e = cudaFuncSetAttribute(qm_gemm_q4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
+        if (e != cudaSuccess) return cuda_error(c, e, "qm_gemm setup");
+        attr_set.fetch_or(bit);
+    }
+    const int tiles = ((T + kGmBM - 1) / kGmBM) * ((w->n + kGmBN - 1) / kGmBN);
+    TimedLaunch tl(c, "gemm");
+    qm_gemm_q4_kernel<<<tiles, kGmThreads, kGmSmem, c->stream>>>(
+        tmx, static_cast<const uint8_t*>(w->data), static_cast<const uint16_t*>(w->scales), T, w->k, w->n, y,
+        c->d_err);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(c, e, "qm_gemm launch");
+    c->launches += 1;
+    return QM_OK;
+}

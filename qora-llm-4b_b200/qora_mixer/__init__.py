@@ -48,7 +48,7 @@ EXPORTS = [
     "qm_gqa_decode_noalloc",
     "qm_dn_state_create_heads", "qm_dn_state_wrap_heads", "qm_dn_state_heads",
     "qm_kv_create_heads", "qm_kv_wrap_heads", "qm_kv_heads",
-    "qm_gemv", "qm_gemv_multi", "qm_logits_penalize", "qm_sample", "qm_shard_plan", "qm_comm_unique_id", "qm_comm_create", "qm_comm_allgather",
+    "qm_gemv", "qm_gemv_multi", "qm_gemm", "qm_logits_penalize", "qm_sample", "qm_shard_plan", "qm_comm_unique_id", "qm_comm_create", "qm_comm_allgather",
     "qm_comm_enable_peer",
     "qm_comm_destroy",
 ]
@@ -161,6 +161,7 @@ def lib():
         "qm_shard_plan": ([I, I, C.POINTER(QmShard)], I),
         "qm_gemv": ([P, C.POINTER(QmWeight), I, P, P], I),
         "qm_gemv_multi": ([P, C.POINTER(QmWeight), I, I, P, C.POINTER(C.c_void_p)], I),
+        "qm_gemm": ([P, C.POINTER(QmWeight), I, P, P], I),
         "qm_logits_penalize": ([P, P, I, I, P, P, I, C.c_float, C.c_float, I], I),
         "qm_sample": ([P, P, I, I, C.c_float, C.c_float, I, P, P], I),
         "qm_comm_unique_id": ([P], I),
@@ -491,6 +492,10 @@ class Mixer:
         batch, vocab = int(logits.shape[0]), int(logits.shape[1])
         self.ctx.check(lib().qm_sample(self.ctx.handle, _ptr(logits), batch, vocab, temperature, top_p,
                                        top_k, _ptr(r) if r is not None else None, _ptr(ids)), "qm_sample")
+
+    def gemm(self, w: QmWeight, x, y):
+        """qm_gemm: y [T, n] f32 = x [T, k] bf16 (bits as int16) . W (Q4) on the tensor cores."""
+        self.ctx.check(lib().qm_gemm(self.ctx.handle, C.byref(w), int(x.shape[0]), _ptr(x), _ptr(y)), "qm_gemm")
 
     def gemv_multi(self, ws, x, ys):
         """ys[i][batch, n_i] = x[batch, k] . W_i for up to 4 weights sharing x (qm_gemv_multi)."""

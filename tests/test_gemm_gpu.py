@@ -1,0 +1,68 @@
+"""The prefill projection GEMM (qm_gemm) on the tensor cores against the
+reference's gemm over a prompt (src/gemv.rs:294-300): every row of y is the
+reference's gemv_q4 of that row of x (the restatement, src/gemv.rs:411-450),
+here checked against a float64 product with the same dequantised weights
+(and, for a few rows, against the restatement itself).  x arrives as bf16;
+W is dequantised to bf16 on the way to the tensor cores (8 bits of
+mantissa), so max|gpu - ref| / RMS(ref) <= 2e-2, the prefill tolerance."""
+import numpy as np
+import pytest
+
+import refmath
+from gpu_util import dev, host, make_ctx
+from qora_mixer import inputs as I
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = make_ctx()
+    yield c
+    c.close()
+
+
+@pytest.mark.parametrize("T,k,n", [(1, 64, 32), (200, 256, 288), (129, 2560, 8192), (300, 4096, 2560),
+                                   (1000, 2560, 1024), (37, 2560, 32)])
+def test_q4_gemm_matches_reference_rows(ctx, orc, T, k, n):
+    import torch
+
+    import qora_mixer as qm
+
+    g = np.random.default_rng(T + k + n)
+    w = (g.standard_normal((k, n)) * 0.02).astype(np.float32)
+    w[0] = 0.0
+    packed, scales = orc.quantize_q4(w)
+    xb = I.f32_to_bf16_bits(g.standard_normal((T, k)).astype(np.float32))
+    x = I.bf16_bits_to_f32(xb)
+    y = torch.full((T, n), float("nan"), device="cuda")
+    qm.Mixer(ctx).gemm(qm.weight_q4(dev(packed), dev(scales)), dev(xb), y)
+    ctx.sync()
+    yg = host(y)
+    wd = orc.dequantize_q4(packed, scales).astype(np.float64)
+    ref = x.astype(np.float64) @ wd
+    assert np.isfinite(yg).all()
+    err = refmath.rel_err(yg, ref)
+    assert err <= TOL, err
+    for t in sorted({0, T // 2, T - 1}):
+        assert refmath.rel_err(yg[t], orc.gemv_q4(x[t], packed, scales)) <= TOL
+
+
+def test_gemm_argument_errors(ctx):
+    import torch
+
+    import qora_mixer as qm
+
+    mx = qm.Mixer(ctx)
+    x = torch.zeros(4, 96, dtype=torch.int16, device="cuda")
+    y = torch.zeros(4, 64, device="cuda")
+    pk = torch.zeros(96, 32, dtype=torch.uint8, device="cuda")
+    sc = torch.zeros(96, 2, dtype=torch.int16, device="cuda")
+    with pytest.raises(qm.QmError) as e:
+        mx.gemm(qm.weight_q4(pk, sc), x, y)  # k = 96: not a multiple of 64
+    assert e.value.code == 2
+    with pytest.raises(qm.QmError) as e:
+        mx.gemm(qm.weight_f16(torch.zeros(64, 64, dtype=torch.int16, device="cuda")),
+                torch.zeros(4, 64, dtype=torch.int16, device="cuda"), y)
+    assert e.value.code == 9
