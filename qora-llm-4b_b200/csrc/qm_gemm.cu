@@ -6,10 +6,12 @@
 // qm_gemm_q4_kernel: one CTA per 128 x 256 tile of Y, K in steps of 64.
 //  * warp 0 (one thread) loads X tiles [128 tokens x 64 k] bf16 with TMA
 //    (128-byte swizzle: the K-major A operand);
-//  * warps 2-7 dequantise the matching W tile [64 k x 256 n] from the
+//  * warps 2-11 dequantise the matching W tile [64 k x 256 n] from the
 //    reference's Q4 layout (packed nibbles [k][n/2], f16 scales [k][n/32])
 //    to bf16 s (q - 8) (the next stage's words in flight while this one is
-//    converted), written into shared memory in the layout a
+//    converted; two nibbles a LOP3 as bf16x2 128 + q, minus 136, times the
+//    scale in bf16, the columns of each 8 stored in the order 0 4 1 5 2 6 3 7
+//    and put back by the epilogue), written into shared memory in the layout a
 //    128-byte-swizzled TMA box of [64 k rows x 64 n] would have (the
 //    MN-major B operand: 4 boxes for 256 columns);
 //  * warp 1 allocates 256 TMEM columns (D: 128 lanes x 256 f32) and one
@@ -21,8 +23,9 @@
 // overlapped.  Every wait is bounded: on a timeout the kernel sets the
 // context's error word and an abort flag, the TMA thread waits (bounded) for
 // its copies in flight, and TMEM is freed before the CTA leaves.
-// W in bf16 carries 8 bits of mantissa: max|y - y_exact| / RMS(y) stays
-// within a few 1e-3 (the prefill tolerance is 2e-2).
+// W in bf16 (the scale rounded to bf16, then the product) carries 8 bits of
+// mantissa: max|y - y_exact| / RMS(y) stays within a few 1e-3 (the prefill
+// tolerance is 2e-2).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -43,9 +46,9 @@ constexpr int kGmWBox = kGmBK * 128;             // [64 k rows x 64 n bf16] = 8 
 constexpr int kGmStage = kGmXBox + 4 * kGmWBox;  // 48 KB
 constexpr int kGmOffBar = kGmStages * kGmStage;  // 192 KB
 constexpr int kGmSmem = kGmOffBar + 256 + 1024;  // + barriers + alignment slack
-constexpr int kGmThreads = 256;
-constexpr int kGmProdWarps = 6;  // warps 2..7
-constexpr int kGmChunks = (kGmBK * (kGmBN / 8) + kGmProdWarps * 32 - 1) / (kGmProdWarps * 32);  // 11 a thread
+constexpr int kGmThreads = 384;
+constexpr int kGmProdWarps = 10;  // warps 2..11
+constexpr int kGmChunks = (kGmBK * (kGmBN / 8) + kGmProdWarps * 32 - 1) / (kGmProdWarps * 32);  // 7 a thread
 constexpr int kGmTmCols = 256;
 constexpr uint32_t kGmIdesc = umma_idesc_bf16(kGmBM, kGmBN, false, true);  // A K-major, B MN-major
 
@@ -132,10 +135,10 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
             }
             umma_commit(smem_u32(&bars->done));  // every MMA issued above has completed
         }
-    } else {  // warps 2..7: dequantise W tiles
-        // thread pt takes chunks q = pt + 192 m (row q / 32, 8 columns at (q % 32) * 8) of every
+    } else {  // warps 2..11: dequantise W tiles
+        // thread pt takes chunks q = pt + 320 m (row q / 32, 8 columns at (q % 32) * 8) of every
         // stage; the next stage's words are loaded while this stage's are converted
-        const int pt = threadIdx.x - 64;  // 0..191
+        const int pt = threadIdx.x - 64;  // 0..319
         const int n0_tile = tn * kGmBN;
         uint32_t wA[kGmChunks], wB[kGmChunks];
         uint16_t sA[kGmChunks], sB[kGmChunks];
@@ -164,16 +167,18 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
                 const int q = pt + m * kGmProdWarps * 32;
                 if (q >= kGmBK * (kGmBN / 8)) break;
                 const int r = q >> 5, ch = q & 31;
-                const float sc = __half2float(__ushort_as_half(sv[m]));
+                // two nibbles per LOP3 as bf16x2 (128 + q, exact), minus 136 (exact), times the
+                // scale in bf16: columns (c, c + 4) of the chunk land side by side, so the chunk's
+                // 8 columns sit in the order 0 4 1 5 2 6 3 7 (the epilogue puts them back)
+                const __nv_bfloat162 s2 = __float2bfloat162_rn(__half2float(__ushort_as_half(sv[m])));
+                const __nv_bfloat162 c136 = __float2bfloat162_rn(136.0f);
                 const uint32_t w = wv[m];
                 uint32_t pk[4];
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    // (q - 8) exactly: 2^23 + q read as a float, minus 2^23 + 8
-                    const float lo = (__uint_as_float(0x4B000000u | ((w >> (8 * j)) & 0xFu)) - 8388616.0f) * sc;
-                    const float hi = (__uint_as_float(0x4B000000u | ((w >> (8 * j + 4)) & 0xFu)) - 8388616.0f) * sc;
-                    const __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
-                    pk[j] = *reinterpret_cast<const uint32_t*>(&b2);
+                    const uint32_t t = ((w >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
+                    const __nv_bfloat162 h = __hmul2(__hsub2(*reinterpret_cast<const __nv_bfloat162*>(&t), c136), s2);
+                    pk[j] = *reinterpret_cast<const uint32_t*>(&h);
                 }
                 *reinterpret_cast<uint4*>(wt + (ch >> 3) * kGmWBox + sw128_off(r, ch & 7)) =
                     make_uint4(pk[0], pk[1], pk[2], pk[3]);
@@ -190,22 +195,24 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
             load_stage(i + 2, wA, sA);
             if (!convert_stage(i + 1, wB, sB)) break;
         }
-        if (warp >= 4) {  // epilogue: TMEM lane quarter warp & 3
+        if (warp >= 4 && warp < 8) {  // epilogue: TMEM lane quarter warp & 3
             if (mbar_wait_bounded(smem_u32(&bars->done), 0, abort_flag, err) && !*abort_flag) {
                 tc_fence_after();
                 const int quarter = warp & 3;
                 const int row = tm * kGmBM + quarter * 32 + lane;
                 const uint32_t la = (uint32_t)(quarter * 32) << 16;
                 for (int c = 0; c < kGmBN / 32; c++) {
-                    float v[32];
+                    float v[32], o[32];
                     tmem_ld32(tmem + la + c * 32, v);
                     tmem_ld_wait();
+#pragma unroll
+                    for (int p = 0; p < 32; p++) o[(p & ~7) + ((p & 1) ? 4 : 0) + ((p & 7) >> 1)] = v[p];  // 0 4 1 5 2 6 3 7
                     const int col = n0_tile + c * 32;
                     if (row < T && col < N) {
                         float* dst = y + (size_t)row * N + col;
 #pragma unroll
                         for (int q = 0; q < 8; q++)
-                            *reinterpret_cast<float4*>(dst + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                            *reinterpret_cast<float4*>(dst + 4 * q) = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
                     }
                 }
             }
