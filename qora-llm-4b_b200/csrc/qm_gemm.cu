@@ -3,8 +3,8 @@
 // prefill at src/gemv.rs:1114-1117, 1222 and 1366-1385).  At T tokens each
 // weight is reused T times, so this is a tensor-core GEMM, not a stream.
 //
-// qm_gemm_q4_kernel: one CTA per 128 x 256 tile of Y, K in steps of 64.
-//  * warp 0 (one thread) loads X tiles [128 tokens x 64 k] bf16 with TMA
+// qm_gemm_q4_kernel: one CTA per 256 x 256 tile of Y, K in steps of 64.
+//  * warp 0 (one thread) loads X tiles [2 x 128 tokens x 64 k] bf16 with TMA
 //    (128-byte swizzle: the K-major A operand);
 //  * warps 2-11 dequantise the matching W tile [64 k x 256 n] from the
 //    reference's Q4 layout (packed nibbles [k][n/2], f16 scales [k][n/32])
@@ -14,12 +14,14 @@
 //    and put back by the epilogue), written into shared memory in the layout a
 //    128-byte-swizzled TMA box of [64 k rows x 64 n] would have (the
 //    MN-major B operand: 4 boxes for 256 columns);
-//  * warp 1 allocates 256 TMEM columns (D: 128 lanes x 256 f32) and one
-//    thread issues tcgen05.mma (kind::f16, bf16 x bf16 -> f32, M 128,
-//    N 256, K 16) four times per stage, each stage released to the producers
-//    by tcgen05.commit;
+//  * warp 1 allocates all 512 TMEM columns (two accumulators of 128 lanes x
+//    256 f32, one per half of the 256 rows) and one thread issues
+//    tcgen05.mma (kind::f16, bf16 x bf16 -> f32, M 128, N 256, K 16) twice
+//    per k-step, both halves reading the same dequantised B, so each W tile
+//    is dequantised once for 256 rows; each stage is released to the
+//    producers by tcgen05.commit;
 //  * warps 4-7 read D out of TMEM (their lane quarters) and store Y (f32).
-// A ring of 4 stages (48 KB each) keeps loads, dequantisation and MMAs
+// A ring of 3 stages (64 KB each) keeps loads, dequantisation and MMAs
 // overlapped.  Every wait is bounded: on a timeout the kernel sets the
 // context's error word and an abort flag, the TMA thread waits (bounded) for
 // its copies in flight, and TMEM is freed before the CTA leaves.
@@ -40,17 +42,17 @@ int encode_rows_tmap(CUtensorMap* m, void* base, uint64_t inner, uint64_t rows, 
                      uint32_t box_inner, uint32_t box_rows, bool fp16);
 namespace {
 
-constexpr int kGmBM = 128, kGmBN = 256, kGmBK = 64, kGmStages = 4;
-constexpr int kGmXBox = kGmBM * 128;             // [128 rows x 64 bf16] = 16 KB
+constexpr int kGmBM = 256, kGmBN = 256, kGmBK = 64, kGmStages = 3;
+constexpr int kGmXBox = 128 * 128;               // [128 rows x 64 bf16] = 16 KB (two a stage)
 constexpr int kGmWBox = kGmBK * 128;             // [64 k rows x 64 n bf16] = 8 KB
-constexpr int kGmStage = kGmXBox + 4 * kGmWBox;  // 48 KB
+constexpr int kGmStage = 2 * kGmXBox + 4 * kGmWBox;  // 64 KB
 constexpr int kGmOffBar = kGmStages * kGmStage;  // 192 KB
 constexpr int kGmSmem = kGmOffBar + 256 + 1024;  // + barriers + alignment slack
 constexpr int kGmThreads = 384;
 constexpr int kGmProdWarps = 10;  // warps 2..11
 constexpr int kGmChunks = (kGmBK * (kGmBN / 8) + kGmProdWarps * 32 - 1) / (kGmProdWarps * 32);  // 7 a thread
-constexpr int kGmTmCols = 256;
-constexpr uint32_t kGmIdesc = umma_idesc_bf16(kGmBM, kGmBN, false, true);  // A K-major, B MN-major
+constexpr int kGmTmCols = 512;  // two accumulators of 128 lanes x 256 f32
+constexpr uint32_t kGmIdesc = umma_idesc_bf16(128, kGmBN, false, true);  // A K-major, B MN-major
 
 struct GmBars {
     uint64_t x_full[kGmStages], w_full[kGmStages], free_[kGmStages], done;
@@ -103,8 +105,9 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
                     break;
                 }
                 const uint32_t xb = smem_u32(&bars->x_full[s]);
-                mbar_arrive_expect_tx(xb, kGmXBox);
+                mbar_arrive_expect_tx(xb, 2 * kGmXBox);
                 tma_load_3d(sbase + s * kGmStage, &tmx, i * kGmBK, tm * kGmBM, 0, xb);
+                tma_load_3d(sbase + s * kGmStage + kGmXBox, &tmx, i * kGmBK, tm * kGmBM + 128, 0, xb);
                 issued = i + 1;
             }
             // every copy this thread issued has landed before the CTA can leave
@@ -124,12 +127,13 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
                     break;
                 }
                 tc_fence_after();
-                const uint32_t xs = sbase + s * kGmStage, ws = xs + kGmXBox;
+                const uint32_t xs = sbase + s * kGmStage, ws = xs + 2 * kGmXBox;
 #pragma unroll
-                for (int kk = 0; kk < kGmBK / 16; kk++) {
-                    const uint64_t ad = umma_sdesc(xs + kk * 32, 16, 1024);
+                for (int kk = 0; kk < kGmBK / 16; kk++) {  // one B, two A halves: rows 0-127, 128-255
                     const uint64_t bd = umma_sdesc(ws + kk * 2048, kGmWBox, 1024);
-                    umma_bf16_ss(tmem, ad, bd, kGmIdesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    umma_bf16_ss(tmem, umma_sdesc(xs + kk * 32, 16, 1024), bd, kGmIdesc, (i > 0 || kk > 0) ? 1u : 0u);
+                    umma_bf16_ss(tmem + kGmBN, umma_sdesc(xs + kGmXBox + kk * 32, 16, 1024), bd, kGmIdesc,
+                                 (i > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(smem_u32(&bars->free_[s]));
             }
@@ -161,7 +165,7 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
                 *abort_flag = 1;
                 return false;
             }
-            uint8_t* wt = smem + s * kGmStage + kGmXBox;
+            uint8_t* wt = smem + s * kGmStage + 2 * kGmXBox;
 #pragma unroll
             for (int m = 0; m < kGmChunks; m++) {
                 const int q = pt + m * kGmProdWarps * 32;
@@ -199,20 +203,23 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
             if (mbar_wait_bounded(smem_u32(&bars->done), 0, abort_flag, err) && !*abort_flag) {
                 tc_fence_after();
                 const int quarter = warp & 3;
-                const int row = tm * kGmBM + quarter * 32 + lane;
                 const uint32_t la = (uint32_t)(quarter * 32) << 16;
-                for (int c = 0; c < kGmBN / 32; c++) {
-                    float v[32], o[32];
-                    tmem_ld32(tmem + la + c * 32, v);
-                    tmem_ld_wait();
+                for (int hf = 0; hf < 2; hf++) {  // accumulator hf: rows hf * 128 + lane quarter
+                    const int row = tm * kGmBM + hf * 128 + quarter * 32 + lane;
+                    for (int c = 0; c < kGmBN / 32; c++) {
+                        float v[32], o[32];
+                        tmem_ld32(tmem + la + hf * kGmBN + c * 32, v);
+                        tmem_ld_wait();
 #pragma unroll
-                    for (int p = 0; p < 32; p++) o[(p & ~7) + ((p & 1) ? 4 : 0) + ((p & 7) >> 1)] = v[p];  // 0 4 1 5 2 6 3 7
-                    const int col = n0_tile + c * 32;
-                    if (row < T && col < N) {
-                        float* dst = y + (size_t)row * N + col;
+                        for (int p = 0; p < 32; p++) o[(p & ~7) + ((p & 1) ? 4 : 0) + ((p & 7) >> 1)] = v[p];  // 0 4 1 5 2 6 3 7
+                        const int col = n0_tile + c * 32;
+                        if (row < T && col < N) {
+                            float* dst = y + (size_t)row * N + col;
 #pragma unroll
-                        for (int q = 0; q < 8; q++)
-                            *reinterpret_cast<float4*>(dst + 4 * q) = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                            for (int q = 0; q < 8; q++)
+                                *reinterpret_cast<float4*>(dst + 4 * q) =
+                                    make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                        }
                     }
                 }
             }
@@ -245,7 +252,7 @@ extern "C" int qm_gemm(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, 
         return set_error(c, QM_E_ARG, "x and y must be 16-byte, data 4-byte and scales 2-byte aligned");
     cudaSetDevice(c->device);
     CUtensorMap tmx;
-    if (encode_rows_tmap(&tmx, const_cast<uint16_t*>(x), (uint64_t)w->k, (uint64_t)T, 1, 64, kGmBM, false) != QM_OK)
+    if (encode_rows_tmap(&tmx, const_cast<uint16_t*>(x), (uint64_t)w->k, (uint64_t)T, 1, 64, 128, false) != QM_OK)
         return set_error(c, QM_E_CUDA, "cuTensorMapEncodeTiled failed for x");
     static std::atomic<uint64_t> attr_set{0};
     const uint64_t bit = 1ull << (c->device & 63);
