@@ -796,6 +796,10 @@ def bench_head(ctx, reps, batch=1, kind="q4"):
     smp_ms, smp_n = ctx.kernel_time("sample")
     ctx.set_timing(False)
     s_ms = timed(lambda: (head(), tail()))
+    gemm_ms = None
+    if kind == "q4" and batch > 1:  # the same logits for all sequences at once on the tensor cores (bf16 x)
+        xb = x.bfloat16().view(torch.int16)
+        gemm_ms = timed(lambda: mx.gemm(w, xb, logits))
     peak, peak_kind = load_peaks()
     launches_lm = (batch + (0 if kind == "q4" else 1)) // (1 if kind == "q4" else 2)
     ach = nbytes * launches_lm / (h_ms / 1e3) / 1e9
@@ -807,6 +811,7 @@ def bench_head(ctx, reps, batch=1, kind="q4"):
             "value": round(batch / (s_ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(s_ms, 4),
             "lm_head_ms": round(h_ms, 4), "penalize_ms": round(pen_ms / pen_n, 4),
             "sample_ms": round(smp_ms / smp_n, 4), "tail_ms": round(t_ms, 4),
+            "lm_head_gemm_ms": round(gemm_ms, 4) if gemm_ms is not None else None,
             "roofline": {"bound": "hbm", "kernel": "qm_rows_kernel", "achieved": round(ach, 1), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(ach / peak, 4),
                          "algorithmic_bytes_per_step": nbytes * launches_lm}}

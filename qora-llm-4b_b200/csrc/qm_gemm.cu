@@ -52,7 +52,8 @@ constexpr int kGmThreads = 384;
 constexpr int kGmProdWarps = 10;  // warps 2..11
 constexpr int kGmChunks = (kGmBK * (kGmBN / 8) + kGmProdWarps * 32 - 1) / (kGmProdWarps * 32);  // 7 a thread
 constexpr int kGmTmCols = 512;  // two accumulators of 128 lanes x 256 f32
-constexpr uint32_t kGmIdesc = umma_idesc_bf16(128, kGmBN, false, true);  // A K-major, B MN-major
+constexpr uint32_t kGmIdesc = umma_idesc_bf16(128, kGmBN, false, true);      // A K-major, B MN-major
+constexpr uint32_t kGmIdescRows = umma_idesc_bf16(128, kGmBN, false, false); // A and B K-major
 
 struct GmBars {
     uint64_t x_full[kGmStages], w_full[kGmStages], free_[kGmStages], done;
@@ -61,6 +62,10 @@ struct GmBars {
 };
 static_assert(sizeof(GmBars) <= 256, "barrier block");
 
+// ROWS: W stored one row per output (QM_W_Q4_ROWS, the tied embedding as
+// lm_head: packed [n][k/2], scales [n][k/32]) -> B is K-major, one 256-row
+// swizzled box, k kept in order; otherwise W [k][n] -> B MN-major.
+template <bool ROWS>
 __global__ void __launch_bounds__(kGmThreads, 1)
 qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restrict__ packed,
                   const uint16_t* __restrict__ scales, int T, int K, int N, float* __restrict__ y, int* err) {
@@ -130,9 +135,10 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
                 const uint32_t xs = sbase + s * kGmStage, ws = xs + 2 * kGmXBox;
 #pragma unroll
                 for (int kk = 0; kk < kGmBK / 16; kk++) {  // one B, two A halves: rows 0-127, 128-255
-                    const uint64_t bd = umma_sdesc(ws + kk * 2048, kGmWBox, 1024);
-                    umma_bf16_ss(tmem, umma_sdesc(xs + kk * 32, 16, 1024), bd, kGmIdesc, (i > 0 || kk > 0) ? 1u : 0u);
-                    umma_bf16_ss(tmem + kGmBN, umma_sdesc(xs + kGmXBox + kk * 32, 16, 1024), bd, kGmIdesc,
+                    const uint64_t bd = ROWS ? umma_sdesc(ws + kk * 32, 16, 1024) : umma_sdesc(ws + kk * 2048, kGmWBox, 1024);
+                    const uint32_t id = ROWS ? kGmIdescRows : kGmIdesc;
+                    umma_bf16_ss(tmem, umma_sdesc(xs + kk * 32, 16, 1024), bd, id, (i > 0 || kk > 0) ? 1u : 0u);
+                    umma_bf16_ss(tmem + kGmBN, umma_sdesc(xs + kGmXBox + kk * 32, 16, 1024), bd, id,
                                  (i > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(smem_u32(&bars->free_[s]));
@@ -150,11 +156,19 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
 #pragma unroll
             for (int m = 0; m < kGmChunks; m++) {
                 const int q = pt + m * kGmProdWarps * 32;
-                const int r = q >> 5, n0 = n0_tile + (q & 31) * 8;
-                const bool ok = q < kGmBK * (kGmBN / 8) && n0 < N && i < nk;
-                const size_t kr = (size_t)i * kGmBK + r;
-                wv[m] = ok ? __ldg(reinterpret_cast<const unsigned int*>(packed + kr * (N / 2) + n0 / 2)) : 0x88888888u;
-                sv[m] = ok ? __ldg(reinterpret_cast<const unsigned short*>(scales + kr * (N / 32) + n0 / 32)) : (uint16_t)0;
+                if (ROWS) {  // row n = q / 8 of the tile, k chunk q % 8 (8 values: 4 bytes, one scale)
+                    const int n = n0_tile + (q >> 3);
+                    const bool ok = q < kGmBK * (kGmBN / 8) && n < N && i < nk;
+                    const size_t k0 = (size_t)i * kGmBK + (q & 7) * 8;
+                    wv[m] = ok ? __ldg(reinterpret_cast<const unsigned int*>(packed + (size_t)n * (K / 2) + k0 / 2)) : 0x88888888u;
+                    sv[m] = ok ? __ldg(reinterpret_cast<const unsigned short*>(scales + (size_t)n * (K / 32) + k0 / 32)) : (uint16_t)0;
+                } else {  // k row q / 32 of the stage, 8 columns at (q % 32) * 8
+                    const int r = q >> 5, n0 = n0_tile + (q & 31) * 8;
+                    const bool ok = q < kGmBK * (kGmBN / 8) && n0 < N && i < nk;
+                    const size_t kr = (size_t)i * kGmBK + r;
+                    wv[m] = ok ? __ldg(reinterpret_cast<const unsigned int*>(packed + kr * (N / 2) + n0 / 2)) : 0x88888888u;
+                    sv[m] = ok ? __ldg(reinterpret_cast<const unsigned short*>(scales + kr * (N / 32) + n0 / 32)) : (uint16_t)0;
+                }
             }
         };
         // stage i into its ring slot (after the MMAs that read the slot last are done)
@@ -170,7 +184,6 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
             for (int m = 0; m < kGmChunks; m++) {
                 const int q = pt + m * kGmProdWarps * 32;
                 if (q >= kGmBK * (kGmBN / 8)) break;
-                const int r = q >> 5, ch = q & 31;
                 // two nibbles per LOP3 as bf16x2 (128 + q, exact), minus 136 (exact), times the
                 // scale in bf16: columns (c, c + 4) of the chunk land side by side, so the chunk's
                 // 8 columns sit in the order 0 4 1 5 2 6 3 7 (the epilogue puts them back)
@@ -184,8 +197,13 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
                     const __nv_bfloat162 h = __hmul2(__hsub2(*reinterpret_cast<const __nv_bfloat162*>(&t), c136), s2);
                     pk[j] = *reinterpret_cast<const uint32_t*>(&h);
                 }
-                *reinterpret_cast<uint4*>(wt + (ch >> 3) * kGmWBox + sw128_off(r, ch & 7)) =
-                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                if (ROWS)  // k must stay in order (it meets x's k): pairs (c, c+4) -> (c, c+1)
+                    *reinterpret_cast<uint4*>(wt + sw128_off(q >> 3, q & 7)) =
+                        make_uint4(__byte_perm(pk[0], pk[1], 0x5410), __byte_perm(pk[2], pk[3], 0x5410),
+                                   __byte_perm(pk[0], pk[1], 0x7632), __byte_perm(pk[2], pk[3], 0x7632));
+                else
+                    *reinterpret_cast<uint4*>(wt + ((q & 31) >> 3) * kGmWBox + sw128_off(q >> 5, q & 7)) =
+                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
             fence_proxy_async_shared();
             __syncwarp();
@@ -211,7 +229,8 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
                         tmem_ld32(tmem + la + hf * kGmBN + c * 32, v);
                         tmem_ld_wait();
 #pragma unroll
-                        for (int p = 0; p < 32; p++) o[(p & ~7) + ((p & 1) ? 4 : 0) + ((p & 7) >> 1)] = v[p];  // 0 4 1 5 2 6 3 7
+                        for (int p = 0; p < 32; p++)  // MN-major B: columns of each 8 in the order 0 4 1 5 2 6 3 7
+                            o[ROWS ? p : (p & ~7) + ((p & 1) ? 4 : 0) + ((p & 7) >> 1)] = v[p];
                         const int col = n0_tile + c * 32;
                         if (row < T && col < N) {
                             float* dst = y + (size_t)row * N + col;
@@ -245,7 +264,9 @@ extern "C" int qm_gemm(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, 
     if (!c) return QM_E_ARG;
     if (!w || !x || !y || !w->data || T < 1 || w->k < 1 || w->n < 1)
         return set_error(c, QM_E_ARG, "null pointer or empty shape");
-    if (w->kind != QM_W_Q4) return set_error(c, QM_E_UNSUPPORTED, "qm_gemm takes Q4 weights ([k][n/2] + scales)");
+    const bool rows = w->kind == QM_W_Q4_ROWS;
+    if (w->kind != QM_W_Q4 && !rows)
+        return set_error(c, QM_E_UNSUPPORTED, "qm_gemm takes Q4 weights ([k][n/2] or row layout [n][k/2], with scales)");
     if (!w->scales) return set_error(c, QM_E_ARG, "Q4 weights need scales");
     if (w->k % kGmBK || w->n % 32) return set_error(c, QM_E_SHAPE, "qm_gemm needs k % 64 == 0 and n % 32 == 0");
     if (((uintptr_t)x & 15) || ((uintptr_t)y & 15) || ((uintptr_t)w->data & 3) || ((uintptr_t)w->scales & 1))
@@ -254,18 +275,19 @@ extern "C" int qm_gemm(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, 
     CUtensorMap tmx;
     if (encode_rows_tmap(&tmx, const_cast<uint16_t*>(x), (uint64_t)w->k, (uint64_t)T, 1, 64, 128, false) != QM_OK)
         return set_error(c, QM_E_CUDA, "cuTensorMapEncodeTiled failed for x");
-    static std::atomic<uint64_t> attr_set{0};
+    auto kern = rows ? qm_gemm_q4_kernel<true> : qm_gemm_q4_kernel<false>;
+    static std::atomic<uint64_t> attr_set[2];
     const uint64_t bit = 1ull << (c->device & 63);
-    if (!(attr_set.load() & bit)) {
-        const cudaError_t e = cudaFuncSetAttribute(qm_gemm_q4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
+    if (!(attr_set[rows].load() & bit)) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
         if (e != cudaSuccess) return cuda_error(c, e, "qm_gemm setup");
-        attr_set.fetch_or(bit);
+        attr_set[rows].fetch_or(bit);
     }
     const int tiles = ((T + kGmBM - 1) / kGmBM) * ((w->n + kGmBN - 1) / kGmBN);
     TimedLaunch tl(c, "gemm");
-    qm_gemm_q4_kernel<<<tiles, kGmThreads, kGmSmem, c->stream>>>(
-        tmx, static_cast<const uint8_t*>(w->data), static_cast<const uint16_t*>(w->scales), T, w->k, w->n, y,
-        c->d_err);
+    kern<<<tiles, kGmThreads, kGmSmem, c->stream>>>(tmx, static_cast<const uint8_t*>(w->data),
+                                                    static_cast<const uint16_t*>(w->scales), T, w->k, w->n, y,
+                                                    c->d_err);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(c, e, "qm_gemm launch");
     c->launches += 1;

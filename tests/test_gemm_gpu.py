@@ -66,3 +66,28 @@ def test_gemm_argument_errors(ctx):
         mx.gemm(qm.weight_f16(torch.zeros(64, 64, dtype=torch.int16, device="cuda")),
                 torch.zeros(4, 64, dtype=torch.int16, device="cuda"), y)
     assert e.value.code == 9
+
+
+@pytest.mark.parametrize("T,vocab,hidden", [(1, 1024, 2560), (8, 4128, 2560), (64, 20032, 2560), (300, 96, 64)])
+def test_q4_rows_gemm_is_batched_lm_head(ctx, orc, T, vocab, hidden):
+    """The tied embedding (row layout, groups along hidden) through the same
+    GEMM: logits for T sequences at once against the reference's
+    lm_head_parallel (src/gemv.rs:677-707) on the bf16-rounded x."""
+    import torch
+
+    import qora_mixer as qm
+
+    g = np.random.default_rng(T + vocab)
+    e = (g.standard_normal((vocab, hidden)) * 0.02).astype(np.float32)
+    e[3] = 0.0
+    packed, scales = orc.quantize_q4(e)
+    xb = I.f32_to_bf16_bits(g.standard_normal((T, hidden)).astype(np.float32))
+    x = I.bf16_bits_to_f32(xb)
+    y = torch.full((T, vocab), float("nan"), device="cuda")
+    qm.Mixer(ctx).gemm(qm.weight_q4_rows(dev(packed), dev(scales)), dev(xb), y)
+    ctx.sync()
+    yg = host(y)
+    assert np.isfinite(yg).all()
+    for t in sorted({0, T // 2, T - 1}):
+        assert refmath.rel_err(yg[t], orc.lm_head_q4(x[t], packed, scales)) <= TOL, t
+    assert np.all(yg[:, 3] == 0.0)
