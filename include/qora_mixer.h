@@ -367,6 +367,9 @@ int qm_gemv_multi(qm_ctx* ctx, const qm_weight* ws, int count, int batch, const 
  * y f32 [T][n].  The weights are dequantised to bf16 on the way in:
  * max|y - exact| / RMS(y) is a few 1e-3. */
 int qm_gemm(qm_ctx* ctx, const qm_weight* w, int T, const uint16_t* x, float* y);
+/* The same with y bf16 [T][n] (the f32 sum rounded to nearest): the form the
+ * prefill mixers take their q / k / v in (qm_dn_prefill, qm_gqa_prefill). */
+int qm_gemm_bf16(qm_ctx* ctx, const qm_weight* w, int T, const uint16_t* x, uint16_t* y);
 /* (Row-layout weights, QM_W_F16_ROWS / QM_W_Q4_ROWS, go through qm_gemv with
  * one weight per call: logits[b][v] = x[b] . E[v], the reference's
  * lm_head_parallel, src/gemv.rs:662-711.  Q4 rows need k % 32 == 0.) */

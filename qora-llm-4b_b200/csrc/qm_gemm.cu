@@ -65,10 +65,11 @@ static_assert(sizeof(GmBars) <= 256, "barrier block");
 // ROWS: W stored one row per output (QM_W_Q4_ROWS, the tied embedding as
 // lm_head: packed [n][k/2], scales [n][k/32]) -> B is K-major, one 256-row
 // swizzled box, k kept in order; otherwise W [k][n] -> B MN-major.
-template <bool ROWS>
+// OBF16: y is bf16 (round to nearest from the f32 accumulator) instead of f32.
+template <bool ROWS, bool OBF16>
 __global__ void __launch_bounds__(kGmThreads, 1)
 qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restrict__ packed,
-                  const uint16_t* __restrict__ scales, int T, int K, int N, float* __restrict__ y, int* err) {
+                  const uint16_t* __restrict__ scales, int T, int K, int N, void* __restrict__ y, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     GmBars* bars = reinterpret_cast<GmBars*>(smem + kGmOffBar);
@@ -233,11 +234,25 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
                             o[ROWS ? p : (p & ~7) + ((p & 1) ? 4 : 0) + ((p & 7) >> 1)] = v[p];
                         const int col = n0_tile + c * 32;
                         if (row < T && col < N) {
-                            float* dst = y + (size_t)row * N + col;
+                            if (OBF16) {
+                                uint16_t* dst = static_cast<uint16_t*>(y) + (size_t)row * N + col;
 #pragma unroll
-                            for (int q = 0; q < 8; q++)
-                                *reinterpret_cast<float4*>(dst + 4 * q) =
-                                    make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                                for (int q = 0; q < 4; q++) {
+                                    uint32_t h[4];
+#pragma unroll
+                                    for (int e = 0; e < 4; e++) {
+                                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * q + 2 * e], o[8 * q + 2 * e + 1]);
+                                        h[e] = *reinterpret_cast<const uint32_t*>(&b2);
+                                    }
+                                    *reinterpret_cast<uint4*>(dst + 8 * q) = make_uint4(h[0], h[1], h[2], h[3]);
+                                }
+                            } else {
+                                float* dst = static_cast<float*>(y) + (size_t)row * N + col;
+#pragma unroll
+                                for (int q = 0; q < 8; q++)
+                                    *reinterpret_cast<float4*>(dst + 4 * q) =
+                                        make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                            }
                         }
                     }
                 }
@@ -260,7 +275,7 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
 
 using namespace qm;
 
-extern "C" int qm_gemm(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, float* y) {
+static int gemm_call(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, void* y, bool obf16) {
     if (!c) return QM_E_ARG;
     if (!w || !x || !y || !w->data || T < 1 || w->k < 1 || w->n < 1)
         return set_error(c, QM_E_ARG, "null pointer or empty shape");
@@ -275,13 +290,15 @@ extern "C" int qm_gemm(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, 
     CUtensorMap tmx;
     if (encode_rows_tmap(&tmx, const_cast<uint16_t*>(x), (uint64_t)w->k, (uint64_t)T, 1, 64, 128, false) != QM_OK)
         return set_error(c, QM_E_CUDA, "cuTensorMapEncodeTiled failed for x");
-    auto kern = rows ? qm_gemm_q4_kernel<true> : qm_gemm_q4_kernel<false>;
-    static std::atomic<uint64_t> attr_set[2];
+    auto kern = rows ? (obf16 ? qm_gemm_q4_kernel<true, true> : qm_gemm_q4_kernel<true, false>)
+                     : (obf16 ? qm_gemm_q4_kernel<false, true> : qm_gemm_q4_kernel<false, false>);
+    static std::atomic<uint64_t> attr_set[4];
+    const int which = (rows ? 2 : 0) + (obf16 ? 1 : 0);
     const uint64_t bit = 1ull << (c->device & 63);
-    if (!(attr_set[rows].load() & bit)) {
+    if (!(attr_set[which].load() & bit)) {
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
         if (e != cudaSuccess) return cuda_error(c, e, "qm_gemm setup");
-        attr_set[rows].fetch_or(bit);
+        attr_set[which].fetch_or(bit);
     }
     const int tiles = ((T + kGmBM - 1) / kGmBM) * ((w->n + kGmBN - 1) / kGmBN);
     TimedLaunch tl(c, "gemm");
@@ -292,4 +309,12 @@ extern "C" int qm_gemm(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, 
     if (e != cudaSuccess) return cuda_error(c, e, "qm_gemm launch");
     c->launches += 1;
     return QM_OK;
+}
+
+extern "C" int qm_gemm(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, float* y) {
+    return gemm_call(c, w, T, x, y, false);
+}
+
+extern "C" int qm_gemm_bf16(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, uint16_t* y) {
+    return gemm_call(c, w, T, x, y, true);
 }

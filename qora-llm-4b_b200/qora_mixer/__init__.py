@@ -48,7 +48,7 @@ EXPORTS = [
     "qm_gqa_decode_noalloc",
     "qm_dn_state_create_heads", "qm_dn_state_wrap_heads", "qm_dn_state_heads",
     "qm_kv_create_heads", "qm_kv_wrap_heads", "qm_kv_heads",
-    "qm_gemv", "qm_gemv_multi", "qm_gemm", "qm_logits_penalize", "qm_sample", "qm_shard_plan", "qm_comm_unique_id", "qm_comm_create", "qm_comm_allgather",
+    "qm_gemv", "qm_gemv_multi", "qm_gemm", "qm_gemm_bf16", "qm_logits_penalize", "qm_sample", "qm_shard_plan", "qm_comm_unique_id", "qm_comm_create", "qm_comm_allgather",
     "qm_comm_enable_peer",
     "qm_comm_destroy",
 ]
@@ -162,6 +162,7 @@ def lib():
         "qm_gemv": ([P, C.POINTER(QmWeight), I, P, P], I),
         "qm_gemv_multi": ([P, C.POINTER(QmWeight), I, I, P, C.POINTER(C.c_void_p)], I),
         "qm_gemm": ([P, C.POINTER(QmWeight), I, P, P], I),
+        "qm_gemm_bf16": ([P, C.POINTER(QmWeight), I, P, P], I),
         "qm_logits_penalize": ([P, P, I, I, P, P, I, C.c_float, C.c_float, I], I),
         "qm_sample": ([P, P, I, I, C.c_float, C.c_float, I, P, P], I),
         "qm_comm_unique_id": ([P], I),
@@ -496,6 +497,11 @@ class Mixer:
     def gemm(self, w: QmWeight, x, y):
         """qm_gemm: y [T, n] f32 = x [T, k] bf16 (bits as int16) . W (Q4) on the tensor cores."""
         self.ctx.check(lib().qm_gemm(self.ctx.handle, C.byref(w), int(x.shape[0]), _ptr(x), _ptr(y)), "qm_gemm")
+
+    def gemm_bf16(self, w: QmWeight, x, y):
+        """qm_gemm_bf16: y [T, n] bf16 (bits as int16), the f32 sum rounded to nearest."""
+        self.ctx.check(lib().qm_gemm_bf16(self.ctx.handle, C.byref(w), int(x.shape[0]), _ptr(x), _ptr(y)),
+                       "qm_gemm_bf16")
 
     def gemv_multi(self, ws, x, ys):
         """ys[i][batch, n_i] = x[batch, k] . W_i for up to 4 weights sharing x (qm_gemv_multi)."""

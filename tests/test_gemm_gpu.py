@@ -91,3 +91,26 @@ def test_q4_rows_gemm_is_batched_lm_head(ctx, orc, T, vocab, hidden):
     for t in sorted({0, T // 2, T - 1}):
         assert refmath.rel_err(yg[t], orc.lm_head_q4(x[t], packed, scales)) <= TOL, t
     assert np.all(yg[:, 3] == 0.0)
+
+
+@pytest.mark.parametrize("rows", [False, True])
+def test_bf16_output_is_the_f32_sum_rounded(ctx, orc, rows):
+    """qm_gemm_bf16 rounds the same accumulator qm_gemm stores: bit for bit
+    the f32 result rounded to nearest bf16."""
+    import torch
+
+    import qora_mixer as qm
+
+    g = np.random.default_rng(11 + rows)
+    T, k, n = 300, 2560, 1056
+    w = (g.standard_normal((n, k) if rows else (k, n)) * 0.02).astype(np.float32)
+    packed, scales = orc.quantize_q4(w)
+    wt = qm.weight_q4_rows(dev(packed), dev(scales)) if rows else qm.weight_q4(dev(packed), dev(scales))
+    xb = dev(I.f32_to_bf16_bits(g.standard_normal((T, k)).astype(np.float32)))
+    y32 = torch.empty(T, n, device="cuda")
+    y16 = torch.empty(T, n, dtype=torch.int16, device="cuda")
+    mx = qm.Mixer(ctx)
+    mx.gemm(wt, xb, y32)
+    mx.gemm_bf16(wt, xb, y16)
+    ctx.sync()
+    np.testing.assert_array_equal(host(y16), I.f32_to_bf16_bits(host(y32)))
