@@ -8,7 +8,7 @@
 //    (128-byte swizzle: the K-major A operand);
 //  * warps 2-11 dequantise the matching W tile [64 k x 256 n] from the
 //    reference's Q4 layout (packed nibbles [k][n/2], f16 scales [k][n/32])
-//    to bf16 s (q - 8) (the next stage's words in flight while this one is
+//    to bf16 s (q - 8) (the next two stages' words in flight while one is
 //    converted; two nibbles a LOP3 as bf16x2 128 + q, minus 136, times the
 //    scale in bf16, the columns of each 8 stored in the order 0 4 1 5 2 6 3 7
 //    and put back by the epilogue), written into shared memory in the layout a
@@ -147,12 +147,12 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
             umma_commit(smem_u32(&bars->done));  // every MMA issued above has completed
         }
     } else {  // warps 2..11: dequantise W tiles
-        // thread pt takes chunks q = pt + 320 m (row q / 32, 8 columns at (q % 32) * 8) of every
-        // stage; the next stage's words are loaded while this stage's are converted
+        // thread pt takes chunks q = pt + 320 m of every stage; the words of the next two stages
+        // are in flight while this stage's are converted
         const int pt = threadIdx.x - 64;  // 0..319
         const int n0_tile = tn * kGmBN;
-        uint32_t wA[kGmChunks], wB[kGmChunks];
-        uint16_t sA[kGmChunks], sB[kGmChunks];
+        uint32_t wA[kGmChunks], wB[kGmChunks], wC[kGmChunks];
+        uint16_t sA[kGmChunks], sB[kGmChunks], sC[kGmChunks];
         auto load_stage = [&](int i, uint32_t(&wv)[kGmChunks], uint16_t(&sv)[kGmChunks]) {
 #pragma unroll
             for (int m = 0; m < kGmChunks; m++) {
@@ -212,11 +212,14 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
             return true;
         };
         load_stage(0, wA, sA);
-        for (int i = 0; i < nk; i += 2) {  // two stages a turn: each buffer a fixed register set
-            load_stage(i + 1, wB, sB);
+        load_stage(1, wB, sB);
+        for (int i = 0; i < nk; i += 3) {  // three stages a turn: each buffer a fixed register set,
+            load_stage(i + 2, wC, sC);     // loads two stages ahead of the conversion
             if (!convert_stage(i, wA, sA) || i + 1 >= nk) break;
-            load_stage(i + 2, wA, sA);
-            if (!convert_stage(i + 1, wB, sB)) break;
+            load_stage(i + 3, wA, sA);
+            if (!convert_stage(i + 1, wB, sB) || i + 2 >= nk) break;
+            load_stage(i + 4, wB, sB);
+            if (!convert_stage(i + 2, wC, sC)) break;
         }
         if (warp >= 4 && warp < 8) {  // epilogue: TMEM lane quarter warp & 3
             if (mbar_wait_bounded(smem_u32(&bars->done), 0, abort_flag, err) && !*abort_flag) {
