@@ -153,23 +153,39 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
         const int n0_tile = tn * kGmBN;
         uint32_t wA[kGmChunks], wB[kGmChunks], wC[kGmChunks];
         uint16_t sA[kGmChunks], sB[kGmChunks], sC[kGmChunks];
+        // per chunk m, fixed over the stages: the byte offset of its 4 nibble bytes in stage 0 (a
+        // stage adds `stride`), the scale at that offset >> 4 (the chunk's place in its 32-group
+        // adds at most 12 bytes), its swizzled place in the stage's B tile, and whether it is
+        // inside the tile (qmask) and inside W (okmask; outside, it dequantises to zeros)
+        uint32_t woff[kGmChunks], soff[kGmChunks], okmask = 0u, qmask = 0u;
+#pragma unroll
+        for (int m = 0; m < kGmChunks; m++) {
+            const int q = pt + m * kGmProdWarps * 32;
+            const bool inq = q < kGmBK * (kGmBN / 8);
+            bool ok;
+            if (ROWS) {  // row n = q / 8 of the tile, k chunk q % 8 (8 values: 4 bytes, one scale)
+                const int n = n0_tile + (q >> 3);
+                ok = inq && n < N;
+                woff[m] = ok ? (uint32_t)n * (uint32_t)(K / 2) + (uint32_t)(q & 7) * 4u : 0u;
+                soff[m] = sw128_off(q >> 3, q & 7);
+            } else {  // k row q / 32 of the stage, 8 columns at (q % 32) * 8
+                const int n0 = n0_tile + (q & 31) * 8;
+                ok = inq && n0 < N;
+                woff[m] = ok ? (uint32_t)(q >> 5) * (uint32_t)(N / 2) + (uint32_t)(n0 / 2) : 0u;
+                soff[m] = ((q & 31) >> 3) * kGmWBox + sw128_off(q >> 5, q & 7);
+            }
+            okmask |= (ok ? 1u : 0u) << m;
+            qmask |= (inq ? 1u : 0u) << m;
+        }
+        const uint32_t stride = ROWS ? (uint32_t)(kGmBK / 2) : (uint32_t)kGmBK * (uint32_t)(N / 2);
         auto load_stage = [&](int i, uint32_t(&wv)[kGmChunks], uint16_t(&sv)[kGmChunks]) {
+            const uint32_t base = (uint32_t)i * stride;
 #pragma unroll
             for (int m = 0; m < kGmChunks; m++) {
-                const int q = pt + m * kGmProdWarps * 32;
-                if (ROWS) {  // row n = q / 8 of the tile, k chunk q % 8 (8 values: 4 bytes, one scale)
-                    const int n = n0_tile + (q >> 3);
-                    const bool ok = q < kGmBK * (kGmBN / 8) && n < N && i < nk;
-                    const size_t k0 = (size_t)i * kGmBK + (q & 7) * 8;
-                    wv[m] = ok ? __ldg(reinterpret_cast<const unsigned int*>(packed + (size_t)n * (K / 2) + k0 / 2)) : 0x88888888u;
-                    sv[m] = ok ? __ldg(reinterpret_cast<const unsigned short*>(scales + (size_t)n * (K / 32) + k0 / 32)) : (uint16_t)0;
-                } else {  // k row q / 32 of the stage, 8 columns at (q % 32) * 8
-                    const int r = q >> 5, n0 = n0_tile + (q & 31) * 8;
-                    const bool ok = q < kGmBK * (kGmBN / 8) && n0 < N && i < nk;
-                    const size_t kr = (size_t)i * kGmBK + r;
-                    wv[m] = ok ? __ldg(reinterpret_cast<const unsigned int*>(packed + kr * (N / 2) + n0 / 2)) : 0x88888888u;
-                    sv[m] = ok ? __ldg(reinterpret_cast<const unsigned short*>(scales + kr * (N / 32) + n0 / 32)) : (uint16_t)0;
-                }
+                const bool ok = ((okmask >> m) & 1u) && i < nk;
+                const uint32_t off = woff[m] + base;
+                wv[m] = ok ? __ldg(reinterpret_cast<const unsigned int*>(packed + off)) : 0x88888888u;
+                sv[m] = ok ? __ldg(reinterpret_cast<const unsigned short*>(scales + (off >> 4))) : (uint16_t)0;
             }
         };
         // stage i into its ring slot (after the MMAs that read the slot last are done)
@@ -183,8 +199,7 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
             uint8_t* wt = smem + s * kGmStage + 2 * kGmXBox;
 #pragma unroll
             for (int m = 0; m < kGmChunks; m++) {
-                const int q = pt + m * kGmProdWarps * 32;
-                if (q >= kGmBK * (kGmBN / 8)) break;
+                if (!((qmask >> m) & 1u)) break;
                 // two nibbles per LOP3 as bf16x2 (128 + q, exact), minus 136 (exact), times the
                 // scale in bf16: columns (c, c + 4) of the chunk land side by side, so the chunk's
                 // 8 columns sit in the order 0 4 1 5 2 6 3 7 (the epilogue puts them back)
@@ -199,12 +214,11 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
                     pk[j] = *reinterpret_cast<const uint32_t*>(&h);
                 }
                 if (ROWS)  // k must stay in order (it meets x's k): pairs (c, c+4) -> (c, c+1)
-                    *reinterpret_cast<uint4*>(wt + sw128_off(q >> 3, q & 7)) =
+                    *reinterpret_cast<uint4*>(wt + soff[m]) =
                         make_uint4(__byte_perm(pk[0], pk[1], 0x5410), __byte_perm(pk[2], pk[3], 0x5410),
                                    __byte_perm(pk[0], pk[1], 0x7632), __byte_perm(pk[2], pk[3], 0x7632));
                 else
-                    *reinterpret_cast<uint4*>(wt + ((q & 31) >> 3) * kGmWBox + sw128_off(q >> 5, q & 7)) =
-                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    *reinterpret_cast<uint4*>(wt + soff[m]) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
             fence_proxy_async_shared();
             __syncwarp();
@@ -287,6 +301,8 @@ static int gemm_call(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, vo
         return set_error(c, QM_E_UNSUPPORTED, "qm_gemm takes Q4 weights ([k][n/2] or row layout [n][k/2], with scales)");
     if (!w->scales) return set_error(c, QM_E_ARG, "Q4 weights need scales");
     if (w->k % kGmBK || w->n % 32) return set_error(c, QM_E_SHAPE, "qm_gemm needs k % 64 == 0 and n % 32 == 0");
+    if ((uint64_t)w->k * (uint64_t)w->n / 2 >= (1ull << 32))
+        return set_error(c, QM_E_SHAPE, "qm_gemm weights must be under 4 GB of nibbles");
     if (((uintptr_t)x & 15) || ((uintptr_t)y & 15) || ((uintptr_t)w->data & 3) || ((uintptr_t)w->scales & 1))
         return set_error(c, QM_E_ARG, "x and y must be 16-byte, data 4-byte and scales 2-byte aligned");
     cudaSetDevice(c->device);
