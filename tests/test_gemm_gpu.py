@@ -114,3 +114,45 @@ def test_bf16_output_is_the_f32_sum_rounded(ctx, orc, rows):
     mx.gemm_bf16(wt, xb, y16)
     ctx.sync()
     np.testing.assert_array_equal(host(y16), I.f32_to_bf16_bits(host(y32)))
+
+
+def test_prefill_projections_feed_the_prefill_mixer(ctx, orc):
+    """A DeltaNet layer's prefill on the device end to end: x_norm (bf16) ->
+    qm_gemm_bf16 (in_proj_qkv, src/gemv.rs:1114) and qm_gemm (in_proj_a / b,
+    1115-1116) -> qm_dn_prefill, the mixer's output against the sequential
+    restatement (src/gemv.rs:1119-1219) run on the projections the device
+    produced, and those projections against the reference's gemv."""
+    import torch
+
+    import qora_mixer as qm
+
+    T = 512
+    g = np.random.default_rng(21)
+    p = I.dn_layer_params(I.rng(22))
+    keep = [dev(p["conv_w"]), dev(p["a_log"]), dev(p["dt_bias"]), dev(p["norm_gamma"])]
+    prm = qm.dn_params(*keep)
+    ws = {name: orc.quantize_q4((g.standard_normal((2560, n)) * 0.02).astype(np.float32))
+          for name, n in (("qkv", 8192), ("a", 32), ("b", 32))}
+    dws = {name: qm.weight_q4(dev(pk), dev(sc)) for name, (pk, sc) in ws.items()}
+    xb = I.f32_to_bf16_bits(g.standard_normal((T, 2560)).astype(np.float32))
+    xd = dev(xb)
+    mx = qm.Mixer(ctx)
+    qkv = torch.empty(1, T, 8192, dtype=torch.int16, device="cuda")
+    a = torch.empty(1, T, 32, device="cuda")
+    b = torch.empty(1, T, 32, device="cuda")
+    mx.gemm_bf16(dws["qkv"], xd, qkv.view(T, 8192))
+    mx.gemm(dws["a"], xd, a.view(T, 32))
+    mx.gemm(dws["b"], xd, b.view(T, 32))
+    st = qm.DnState(ctx, 1)
+    y = torch.full((1, T, 32, 128), float("nan"), device="cuda")
+    mx.dn_prefill(prm, st, T, qkv, a, b, y)
+    ctx.sync()
+    qkv_h, a_h, b_h = host(qkv)[0], host(a)[0], host(b)[0]
+    x = I.bf16_bits_to_f32(xb)
+    for t in (0, T - 1):
+        assert refmath.rel_err(I.bf16_bits_to_f32(qkv_h[t]), orc.gemv_q4(x[t], *ws["qkv"])) <= TOL
+        assert refmath.rel_err(a_h[t], orc.gemv_q4(x[t], *ws["a"])) <= TOL
+    c = orc.cfg_4b()
+    yo = orc.dn_prefill(c, orc.DnState(c), qkv_h, a_h, b_h, p["conv_w"], p["a_log"], p["dt_bias"])
+    assert refmath.rel_err(host(y)[0], yo) <= TOL
+    st.close()
