@@ -156,3 +156,44 @@ def test_prefill_projections_feed_the_prefill_mixer(ctx, orc):
     yo = orc.dn_prefill(c, orc.DnState(c), qkv_h, a_h, b_h, p["conv_w"], p["a_log"], p["dt_bias"])
     assert refmath.rel_err(host(y)[0], yo) <= TOL
     st.close()
+
+
+def test_prefill_projections_feed_the_attention_prefill(ctx, orc):
+    """An attention layer's prefill end to end on the device: x_norm (bf16) ->
+    qm_gemm_bf16 for q_proj / k_proj / v_proj (src/gemv.rs:1366, 1384-1385;
+    q_proj's [T, 16 x 512] is the per-head [Q, gate] layout the mixer takes) ->
+    qm_gqa_prefill, against the restatement (src/gemv.rs:1364-1444) on the
+    projections the device produced (sampled rows)."""
+    import torch
+
+    import qora_mixer as qm
+
+    T = 400
+    g = np.random.default_rng(31)
+    pr = I.gqa_layer_params(I.rng(32), T + 1)
+    cos, sin = qm.rope_table(1.0e7, 64, T + 1)
+    keep = [dev(pr["q_norm"]), dev(pr["k_norm"]), dev(cos), dev(sin)]
+    prm = qm.gqa_params(*keep)
+    ws = {name: orc.quantize_q4((g.standard_normal((2560, n)) * 0.02).astype(np.float32))
+          for name, n in (("q", 8192), ("k", 1024), ("v", 1024))}
+    dws = {name: qm.weight_q4(dev(pk), dev(sc)) for name, (pk, sc) in ws.items()}
+    xd = dev(I.f32_to_bf16_bits(g.standard_normal((T, 2560)).astype(np.float32)))
+    mx = qm.Mixer(ctx)
+    qg = torch.empty(1, T, 16, 512, dtype=torch.int16, device="cuda")
+    kk = torch.empty(1, T, 4, 256, dtype=torch.int16, device="cuda")
+    vv = torch.empty(1, T, 4, 256, dtype=torch.int16, device="cuda")
+    mx.gemm_bf16(dws["q"], xd, qg.view(T, 8192))
+    mx.gemm_bf16(dws["k"], xd, kk.view(T, 1024))
+    mx.gemm_bf16(dws["v"], xd, vv.view(T, 1024))
+    K = torch.zeros(1, 4, T, 256, dtype=torch.int16, device="cuda")
+    V = torch.zeros_like(K)
+    kv = qm.KvCache(ctx, 1, T, K, V)
+    out = torch.full((1, T, 16, 256), float("nan"), device="cuda")
+    mx.gqa_prefill(prm, kv, T, qg, kk, vv, out)
+    ctx.sync()
+    c = orc.cfg_4b()
+    rows = np.array([0, 1, 127, 128, 255, 399])
+    ref = orc.gqa_prefill_rows(c, host(qg)[0].reshape(T, -1), host(kk)[0].reshape(T, -1),
+                               host(vv)[0].reshape(T, -1), pr["q_norm"], pr["k_norm"], cos, sin, rows)
+    assert refmath.rel_err(host(out)[0][rows], ref) <= TOL
+    kv.close()
