@@ -696,7 +696,7 @@ GEMM_SHAPES = [("in_proj_qkv / q_proj", 2560, 8192), ("in_proj_z", 2560, 4096), 
                ("k_proj / v_proj", 2560, 1024)]
 
 
-def bench_gemm(ctx, reps, T=8192):
+def bench_gemm(ctx, reps, T=8192, kind="q4"):
     import torch
 
     import qora_mixer as qm
@@ -707,9 +707,14 @@ def bench_gemm(ctx, reps, T=8192):
     peak, peak_kind = load_tensor_peak()
     rows, tot_flops, tot_ms = [], 0.0, 0.0
     for name, k, n in GEMM_SHAPES:
-        pk = torch.randint(0, 256, (k, n // 2), dtype=torch.uint8, device="cuda", generator=gen)
-        sc = (torch.rand(k, n // 32, device="cuda", generator=gen) * 0.01).half().view(torch.int16)
-        w = qm.weight_q4(pk, sc)
+        if kind == "q4":
+            pk = torch.randint(0, 256, (k, n // 2), dtype=torch.uint8, device="cuda", generator=gen)
+            sc = (torch.rand(k, n // 32, device="cuda", generator=gen) * 0.01).half().view(torch.int16)
+            w = qm.weight_q4(pk, sc)
+        else:
+            pk = (torch.randn(k, n, device="cuda", generator=gen) * 0.02).half().view(torch.int16)
+            sc = None
+            w = qm.weight_f16(pk)
         x = torch.randn(T, k, device="cuda", generator=gen).bfloat16().view(torch.int16)
         y = torch.empty(T, n, device="cuda")
         for _ in range(3):
@@ -730,8 +735,9 @@ def bench_gemm(ctx, reps, T=8192):
         del pk, sc, w, x, y
     torch.cuda.empty_cache()
     ach = tot_flops / (tot_ms / 1e3) / 1e12
-    return {"metric": "prefill projections (Q4 GEMM)", "workload": f"{T} tokens x the 4B's projection shapes, "
-            "bf16 x, Q4 weights dequantised to bf16 in the kernel, f32 y", "per_shape": rows,
+    wdesc = "Q4 weights dequantised" if kind == "q4" else "F16 weights rounded"
+    return {"metric": f"prefill projections ({kind.upper()} GEMM)", "workload": f"{T} tokens x the 4B's "
+            f"projection shapes, bf16 x, {wdesc} to bf16 in the kernel, f32 y", "per_shape": rows,
             "value": round(T / (tot_ms / 1e3), 1), "unit": "tok/s (the 4 shapes once each)",
             "roofline": {"bound": "tensor", "kernel": "qm_gemm_q4_kernel", "achieved": round(ach, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": round(ach / peak, 4)}}
@@ -1045,7 +1051,8 @@ def main():
     ap.add_argument("--gemv-only", choices=["q4", "f16"],
                     help="time the 32 layers' mixer projections (Q4 / F16 weight GEMV) alone")
     ap.add_argument("--gemv-batch", type=int, default=1, help="with --gemv-only / --head-only: sequences per step")
-    ap.add_argument("--gemm-only", action="store_true", help="time the Q4 prefill projection GEMM alone")
+    ap.add_argument("--gemm-only", nargs="?", const="q4", choices=["q4", "f16"],
+                    help="time the prefill projection GEMM alone (Q4 weights unless f16 is given)")
     ap.add_argument("--head-only", choices=["q4", "f16"],
                     help="time the decode tail alone: lm_head, penalties and sampling")
     args = ap.parse_args()
@@ -1058,7 +1065,7 @@ def main():
 
         torch.cuda.set_device(0)
         ctx = qm.Ctx(0, stream=torch.cuda.current_stream())
-        print(json.dumps(bench_gemm(ctx, args.steps, args.prefill_len or 8192)), flush=True)
+        print(json.dumps(bench_gemm(ctx, args.steps, args.prefill_len or 8192, args.gemm_only)), flush=True)
         ctx.close()
         return
     if args.head_only:

@@ -360,11 +360,14 @@ int qm_gemv_multi(qm_ctx* ctx, const qm_weight* ws, int count, int batch, const 
                   float* const* ys);
 /* y[T][n] = x[T][k] . W for a whole prompt on the tensor cores: the
  * reference's gemm over seq_len tokens (src/gemv.rs:294-300, its prefill at
- * 1114-1117, 1222, 1366-1385).  Q4 weights ([k][n/2], or QM_W_Q4_ROWS:
- * the tied embedding as a batched lm_head, src/gemv.rs:677-707), k % 64 == 0,
- * n % 32 == 0;
+ * 1114-1117, 1222, 1366-1385), for both weight formats it dispatches on
+ * (gemm_q4 / gemm_f16, src/gemv.rs:390, 529): QM_W_Q4 [k][n/2] or QM_W_F16
+ * [k][n] (data 16-byte aligned), or their row layouts QM_W_Q4_ROWS /
+ * QM_W_F16_ROWS (the tied embedding as a batched lm_head, src/gemv.rs:677-707);
+ * k % 64 == 0, n % 32 == 0;
  * x bf16 [T][k] (16-byte aligned, as the prefill mixers take their inputs),
- * y f32 [T][n].  The weights are dequantised to bf16 on the way in:
+ * y f32 [T][n].  The weights are rounded to bf16 on the way in (Q4: the
+ * scale, then the product):
  * max|y - exact| / RMS(y) is a few 1e-3. */
 int qm_gemm(qm_ctx* ctx, const qm_weight* w, int T, const uint16_t* x, float* y);
 /* The same with y bf16 [T][n] (the f32 sum rounded to nearest): the form the

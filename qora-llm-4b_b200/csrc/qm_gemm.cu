@@ -1,7 +1,8 @@
-// Prefill projections: Y[T][n] = X[T][k] . W for Q4 weights over a whole
-// prompt (the reference's gemm / gemm_q4, src/gemv.rs:294-300, used by its
-// prefill at src/gemv.rs:1114-1117, 1222 and 1366-1385).  At T tokens each
-// weight is reused T times, so this is a tensor-core GEMM, not a stream.
+// Prefill projections: Y[T][n] = X[T][k] . W for Q4 or F16 weights over a
+// whole prompt (the reference's gemm -> gemm_q4 / gemm_f16, src/gemv.rs:294-300,
+// 390, 529, used by its prefill at src/gemv.rs:1114-1117, 1222 and 1366-1385).
+// At T tokens each weight is reused T times, so this is a tensor-core GEMM,
+// not a stream.
 //
 // qm_gemm_q4_kernel: one CTA per 256 x 256 tile of Y, K in steps of 64.
 //  * warp 0 (one thread) loads X tiles [2 x 128 tokens x 64 k] bf16 with TMA
@@ -11,7 +12,9 @@
 //    to bf16 s (q - 8) (the next two stages' words in flight while one is
 //    converted; two nibbles a LOP3 as bf16x2 128 + q, minus 136, times the
 //    scale in bf16, the columns of each 8 stored in the order 0 4 1 5 2 6 3 7
-//    and put back by the epilogue), written into shared memory in the layout a
+//    and put back by the epilogue; F16 weights: 8 f16 a 16-byte load, each
+//    rounded to the nearest bf16, in column order), written into shared
+//    memory in the layout a
 //    128-byte-swizzled TMA box of [64 k rows x 64 n] would have (the
 //    MN-major B operand: 4 boxes for 256 columns);
 //  * warp 1 allocates all 512 TMEM columns (two accumulators of 128 lanes x
@@ -33,6 +36,7 @@
 #include <cuda_fp16.h>
 
 #include <atomic>
+#include <type_traits>
 
 #include "qm_internal.h"
 #include "qm_ptx.cuh"
@@ -66,7 +70,8 @@ static_assert(sizeof(GmBars) <= 256, "barrier block");
 // lm_head: packed [n][k/2], scales [n][k/32]) -> B is K-major, one 256-row
 // swizzled box, k kept in order; otherwise W [k][n] -> B MN-major.
 // OBF16: y is bf16 (round to nearest from the f32 accumulator) instead of f32.
-template <bool ROWS, bool OBF16>
+// F16W: W is f16 ([k][n] or, with ROWS, [n][k]) instead of Q4; `scales` unused.
+template <bool ROWS, bool OBF16, bool F16W>
 __global__ void __launch_bounds__(kGmThreads, 1)
 qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restrict__ packed,
                   const uint16_t* __restrict__ scales, int T, int K, int N, void* __restrict__ y, int* err) {
@@ -151,12 +156,14 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
         // are in flight while this stage's are converted
         const int pt = threadIdx.x - 64;  // 0..319
         const int n0_tile = tn * kGmBN;
-        uint32_t wA[kGmChunks], wB[kGmChunks], wC[kGmChunks];
+        using WT = typename std::conditional<F16W, uint4, uint32_t>::type;  // one chunk's 8 weights
+        WT wA[kGmChunks], wB[kGmChunks], wC[kGmChunks];
         uint16_t sA[kGmChunks], sB[kGmChunks], sC[kGmChunks];
-        // per chunk m, fixed over the stages: the byte offset of its 4 nibble bytes in stage 0 (a
-        // stage adds `stride`), the scale at that offset >> 4 (the chunk's place in its 32-group
-        // adds at most 12 bytes), its swizzled place in the stage's B tile, and whether it is
-        // inside the tile (qmask) and inside W (okmask; outside, it dequantises to zeros)
+        // per chunk m, fixed over the stages: the byte offset of its 4 nibble bytes (F16: 16
+        // bytes) in stage 0 (a stage adds `stride`), for Q4 the scale at that offset >> 4 (the
+        // chunk's place in its 32-group adds at most 12 bytes), its swizzled place in the stage's
+        // B tile, and whether it is inside the tile (qmask) and inside W (okmask; outside, it
+        // dequantises to zeros)
         uint32_t woff[kGmChunks], soff[kGmChunks], okmask = 0u, qmask = 0u;
 #pragma unroll
         for (int m = 0; m < kGmChunks; m++) {
@@ -166,30 +173,39 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
             if (ROWS) {  // row n = q / 8 of the tile, k chunk q % 8 (8 values: 4 bytes, one scale)
                 const int n = n0_tile + (q >> 3);
                 ok = inq && n < N;
-                woff[m] = ok ? (uint32_t)n * (uint32_t)(K / 2) + (uint32_t)(q & 7) * 4u : 0u;
+                woff[m] = !ok ? 0u
+                          : F16W ? (uint32_t)n * (uint32_t)(K * 2) + (uint32_t)(q & 7) * 16u
+                                 : (uint32_t)n * (uint32_t)(K / 2) + (uint32_t)(q & 7) * 4u;
                 soff[m] = sw128_off(q >> 3, q & 7);
             } else {  // k row q / 32 of the stage, 8 columns at (q % 32) * 8
                 const int n0 = n0_tile + (q & 31) * 8;
                 ok = inq && n0 < N;
-                woff[m] = ok ? (uint32_t)(q >> 5) * (uint32_t)(N / 2) + (uint32_t)(n0 / 2) : 0u;
+                woff[m] = !ok ? 0u
+                          : F16W ? (uint32_t)(q >> 5) * (uint32_t)(N * 2) + (uint32_t)(n0 * 2)
+                                 : (uint32_t)(q >> 5) * (uint32_t)(N / 2) + (uint32_t)(n0 / 2);
                 soff[m] = ((q & 31) >> 3) * kGmWBox + sw128_off(q >> 5, q & 7);
             }
             okmask |= (ok ? 1u : 0u) << m;
             qmask |= (inq ? 1u : 0u) << m;
         }
-        const uint32_t stride = ROWS ? (uint32_t)(kGmBK / 2) : (uint32_t)kGmBK * (uint32_t)(N / 2);
-        auto load_stage = [&](int i, uint32_t(&wv)[kGmChunks], uint16_t(&sv)[kGmChunks]) {
+        const uint32_t stride = F16W ? (ROWS ? (uint32_t)(kGmBK * 2) : (uint32_t)kGmBK * (uint32_t)(N * 2))
+                                     : (ROWS ? (uint32_t)(kGmBK / 2) : (uint32_t)kGmBK * (uint32_t)(N / 2));
+        auto load_stage = [&](int i, WT(&wv)[kGmChunks], uint16_t(&sv)[kGmChunks]) {
             const uint32_t base = (uint32_t)i * stride;
 #pragma unroll
             for (int m = 0; m < kGmChunks; m++) {
                 const bool ok = ((okmask >> m) & 1u) && i < nk;
                 const uint32_t off = woff[m] + base;
-                wv[m] = ok ? __ldg(reinterpret_cast<const unsigned int*>(packed + off)) : 0x88888888u;
-                sv[m] = ok ? __ldg(reinterpret_cast<const unsigned short*>(scales + (off >> 4))) : (uint16_t)0;
+                if constexpr (F16W) {
+                    wv[m] = ok ? __ldg(reinterpret_cast<const uint4*>(packed + off)) : make_uint4(0u, 0u, 0u, 0u);
+                } else {
+                    wv[m] = ok ? __ldg(reinterpret_cast<const unsigned int*>(packed + off)) : 0x88888888u;
+                    sv[m] = ok ? __ldg(reinterpret_cast<const unsigned short*>(scales + (off >> 4))) : (uint16_t)0;
+                }
             }
         };
         // stage i into its ring slot (after the MMAs that read the slot last are done)
-        auto convert_stage = [&](int i, const uint32_t(&wv)[kGmChunks], const uint16_t(&sv)[kGmChunks]) -> bool {
+        auto convert_stage = [&](int i, const WT(&wv)[kGmChunks], const uint16_t(&sv)[kGmChunks]) -> bool {
             const int s = i % kGmStages;
             if (i >= kGmStages &&
                 !mbar_wait_bounded(smem_u32(&bars->free_[s]), ((i / kGmStages) - 1) & 1, abort_flag, err)) {
@@ -200,12 +216,24 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
 #pragma unroll
             for (int m = 0; m < kGmChunks; m++) {
                 if (!((qmask >> m) & 1u)) break;
+                if constexpr (F16W) {  // f16 pairs -> bf16 pairs (round to nearest), order kept
+                    const uint32_t src[4] = {wv[m].x, wv[m].y, wv[m].z, wv[m].w};
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const __nv_bfloat162 h =
+                            __float22bfloat162_rn(__half22float2(*reinterpret_cast<const __half2*>(&src[j])));
+                        pk[j] = *reinterpret_cast<const uint32_t*>(&h);
+                    }
+                    *reinterpret_cast<uint4*>(wt + soff[m]) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    continue;
+                }
                 // two nibbles per LOP3 as bf16x2 (128 + q, exact), minus 136 (exact), times the
                 // scale in bf16: columns (c, c + 4) of the chunk land side by side, so the chunk's
                 // 8 columns sit in the order 0 4 1 5 2 6 3 7 (the epilogue puts them back)
                 const __nv_bfloat162 s2 = __float2bfloat162_rn(__half2float(__ushort_as_half(sv[m])));
                 const __nv_bfloat162 c136 = __float2bfloat162_rn(136.0f);
-                const uint32_t w = wv[m];
+                const uint32_t w = *reinterpret_cast<const uint32_t*>(&wv[m]);
                 uint32_t pk[4];
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
@@ -247,8 +275,8 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
                         tmem_ld32(tmem + la + hf * kGmBN + c * 32, v);
                         tmem_ld_wait();
 #pragma unroll
-                        for (int p = 0; p < 32; p++)  // MN-major B: columns of each 8 in the order 0 4 1 5 2 6 3 7
-                            o[ROWS ? p : (p & ~7) + ((p & 1) ? 4 : 0) + ((p & 7) >> 1)] = v[p];
+                        for (int p = 0; p < 32; p++)  // MN-major Q4 B: columns of each 8 in the order 0 4 1 5 2 6 3 7
+                            o[(ROWS || F16W) ? p : (p & ~7) + ((p & 1) ? 4 : 0) + ((p & 7) >> 1)] = v[p];
                         const int col = n0_tile + c * 32;
                         if (row < T && col < N) {
                             if (OBF16) {
@@ -296,23 +324,30 @@ static int gemm_call(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, vo
     if (!c) return QM_E_ARG;
     if (!w || !x || !y || !w->data || T < 1 || w->k < 1 || w->n < 1)
         return set_error(c, QM_E_ARG, "null pointer or empty shape");
-    const bool rows = w->kind == QM_W_Q4_ROWS;
-    if (w->kind != QM_W_Q4 && !rows)
-        return set_error(c, QM_E_UNSUPPORTED, "qm_gemm takes Q4 weights ([k][n/2] or row layout [n][k/2], with scales)");
-    if (!w->scales) return set_error(c, QM_E_ARG, "Q4 weights need scales");
+    const bool rows = w->kind == QM_W_Q4_ROWS || w->kind == QM_W_F16_ROWS;
+    const bool f16w = w->kind == QM_W_F16 || w->kind == QM_W_F16_ROWS;
+    if (w->kind != QM_W_Q4 && w->kind != QM_W_Q4_ROWS && !f16w)
+        return set_error(c, QM_E_UNSUPPORTED, "qm_gemm takes QM_W_F16, QM_W_Q4, QM_W_F16_ROWS or QM_W_Q4_ROWS weights");
+    if (!f16w && !w->scales) return set_error(c, QM_E_ARG, "Q4 weights need scales");
     if (w->k % kGmBK || w->n % 32) return set_error(c, QM_E_SHAPE, "qm_gemm needs k % 64 == 0 and n % 32 == 0");
-    if ((uint64_t)w->k * (uint64_t)w->n / 2 >= (1ull << 32))
-        return set_error(c, QM_E_SHAPE, "qm_gemm weights must be under 4 GB of nibbles");
-    if (((uintptr_t)x & 15) || ((uintptr_t)y & 15) || ((uintptr_t)w->data & 3) || ((uintptr_t)w->scales & 1))
-        return set_error(c, QM_E_ARG, "x and y must be 16-byte, data 4-byte and scales 2-byte aligned");
+    if ((uint64_t)w->k * (uint64_t)w->n * (f16w ? 2u : 1u) / (f16w ? 1u : 2u) >= (1ull << 32))
+        return set_error(c, QM_E_SHAPE, "qm_gemm weights must be under 4 GB");
+    if (((uintptr_t)x & 15) || ((uintptr_t)y & 15) || ((uintptr_t)w->data & (f16w ? 15 : 3)) ||
+        (!f16w && ((uintptr_t)w->scales & 1)))
+        return set_error(c, QM_E_ARG, "x, y and F16 data must be 16-byte, Q4 data 4-byte and scales 2-byte aligned");
     cudaSetDevice(c->device);
     CUtensorMap tmx;
     if (encode_rows_tmap(&tmx, const_cast<uint16_t*>(x), (uint64_t)w->k, (uint64_t)T, 1, 64, 128, false) != QM_OK)
         return set_error(c, QM_E_CUDA, "cuTensorMapEncodeTiled failed for x");
-    auto kern = rows ? (obf16 ? qm_gemm_q4_kernel<true, true> : qm_gemm_q4_kernel<true, false>)
-                     : (obf16 ? qm_gemm_q4_kernel<false, true> : qm_gemm_q4_kernel<false, false>);
-    static std::atomic<uint64_t> attr_set[4];
-    const int which = (rows ? 2 : 0) + (obf16 ? 1 : 0);
+    using Kern = void (*)(CUtensorMap, const uint8_t*, const uint16_t*, int, int, int, void*, int*);
+    static const Kern kerns[8] = {
+        qm_gemm_q4_kernel<false, false, false>, qm_gemm_q4_kernel<false, true, false>,
+        qm_gemm_q4_kernel<true, false, false>,  qm_gemm_q4_kernel<true, true, false>,
+        qm_gemm_q4_kernel<false, false, true>,  qm_gemm_q4_kernel<false, true, true>,
+        qm_gemm_q4_kernel<true, false, true>,   qm_gemm_q4_kernel<true, true, true>};
+    static std::atomic<uint64_t> attr_set[8];
+    const int which = (f16w ? 4 : 0) + (rows ? 2 : 0) + (obf16 ? 1 : 0);
+    const Kern kern = kerns[which];
     const uint64_t bit = 1ull << (c->device & 63);
     if (!(attr_set[which].load() & bit)) {
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);

@@ -495,7 +495,7 @@ class Mixer:
                                        top_k, _ptr(r) if r is not None else None, _ptr(ids)), "qm_sample")
 
     def gemm(self, w: QmWeight, x, y):
-        """qm_gemm: y [T, n] f32 = x [T, k] bf16 (bits as int16) . W (Q4) on the tensor cores."""
+        """qm_gemm: y [T, n] f32 = x [T, k] bf16 (bits as int16) . W (Q4 or F16, either layout) on the tensor cores."""
         self.ctx.check(lib().qm_gemm(self.ctx.handle, C.byref(w), int(x.shape[0]), _ptr(x), _ptr(y)), "qm_gemm")
 
     def gemm_bf16(self, w: QmWeight, x, y):

@@ -2,9 +2,11 @@
 reference's gemm over a prompt (src/gemv.rs:294-300): every row of y is the
 reference's gemv_q4 of that row of x (the restatement, src/gemv.rs:411-450),
 here checked against a float64 product with the same dequantised weights
-(and, for a few rows, against the restatement itself).  x arrives as bf16;
-W is dequantised to bf16 on the way to the tensor cores (8 bits of
-mantissa), so max|gpu - ref| / RMS(ref) <= 2e-2, the prefill tolerance."""
+(and, for a few rows, against the restatement itself).  F16 weights follow
+gemm_f16 (src/gemv.rs:390) and are checked the same way against gemv_f16
+(src/gemv.rs:361-368) and lm_head_f16 (664-676).  x arrives as bf16; W is
+rounded to bf16 on the way to the tensor cores (8 bits of mantissa), so
+max|gpu - ref| / RMS(ref) <= 2e-2, the prefill tolerance."""
 import numpy as np
 import pytest
 
@@ -62,10 +64,15 @@ def test_gemm_argument_errors(ctx):
     with pytest.raises(qm.QmError) as e:
         mx.gemm(qm.weight_q4(pk, sc), x, y)  # k = 96: not a multiple of 64
     assert e.value.code == 2
+    w16 = torch.zeros(64 * 64 + 1, dtype=torch.int16, device="cuda")
+    bad = qm.QmWeight(7, 64, 64, w16.data_ptr(), None)  # no such weight kind
     with pytest.raises(qm.QmError) as e:
-        mx.gemm(qm.weight_f16(torch.zeros(64, 64, dtype=torch.int16, device="cuda")),
-                torch.zeros(4, 64, dtype=torch.int16, device="cuda"), y)
+        mx.gemm(bad, torch.zeros(4, 64, dtype=torch.int16, device="cuda"), y)
     assert e.value.code == 9
+    odd = qm.QmWeight(qm.W_F16, 64, 64, w16.data_ptr() + 2, None)  # F16 data 2 bytes off 16
+    with pytest.raises(qm.QmError) as e:
+        mx.gemm(odd, torch.zeros(4, 64, dtype=torch.int16, device="cuda"), y)
+    assert e.value.code == 1
 
 
 @pytest.mark.parametrize("T,vocab,hidden", [(1, 1024, 2560), (8, 4128, 2560), (64, 20032, 2560), (300, 96, 64)])
@@ -197,3 +204,58 @@ def test_prefill_projections_feed_the_attention_prefill(ctx, orc):
                                host(vv)[0].reshape(T, -1), pr["q_norm"], pr["k_norm"], cos, sin, rows)
     assert refmath.rel_err(host(out)[0][rows], ref) <= TOL
     kv.close()
+
+
+@pytest.mark.parametrize("T,k,n", [(1, 64, 32), (200, 256, 288), (129, 2560, 8192), (300, 4096, 2560),
+                                   (37, 2560, 32)])
+def test_f16_gemm_matches_reference_rows(ctx, orc, T, k, n):
+    """F16 weights [k][n] (gemm_f16, src/gemv.rs:390) against a float64
+    product of the same f16 values and, for a few rows, gemv_f16."""
+    import torch
+
+    import qora_mixer as qm
+
+    g = np.random.default_rng(T + k + n + 5)
+    w16 = (g.standard_normal((k, n)) * 0.02).astype(np.float16)
+    w16[0] = 0.0
+    wb = w16.view(np.uint16)
+    xb = I.f32_to_bf16_bits(g.standard_normal((T, k)).astype(np.float32))
+    x = I.bf16_bits_to_f32(xb)
+    y = torch.full((T, n), float("nan"), device="cuda")
+    qm.Mixer(ctx).gemm(qm.weight_f16(dev(wb)), dev(xb), y)
+    ctx.sync()
+    yg = host(y)
+    assert np.isfinite(yg).all()
+    ref = x.astype(np.float64) @ w16.astype(np.float64)
+    assert refmath.rel_err(yg, ref) <= TOL
+    for t in sorted({0, T // 2, T - 1}):
+        assert refmath.rel_err(yg[t], orc.gemv_f16(x[t], wb)) <= TOL
+
+
+@pytest.mark.parametrize("T,vocab,hidden", [(1, 1024, 2560), (64, 20032, 2560), (300, 96, 64)])
+def test_f16_rows_gemm_is_batched_lm_head(ctx, orc, T, vocab, hidden):
+    """An f16 tied embedding (row layout) as a batched lm_head against
+    lm_head_f16 (src/gemv.rs:664-676), bf16 output rounded from the same sum."""
+    import torch
+
+    import qora_mixer as qm
+
+    g = np.random.default_rng(T + vocab + 9)
+    e16 = (g.standard_normal((vocab, hidden)) * 0.02).astype(np.float16)
+    e16[3] = 0.0
+    eb = e16.view(np.uint16)
+    xb = I.f32_to_bf16_bits(g.standard_normal((T, hidden)).astype(np.float32))
+    x = I.bf16_bits_to_f32(xb)
+    wt = qm.weight_f16_rows(dev(eb))
+    y = torch.full((T, vocab), float("nan"), device="cuda")
+    y16 = torch.empty(T, vocab, dtype=torch.int16, device="cuda")
+    mx = qm.Mixer(ctx)
+    mx.gemm(wt, dev(xb), y)
+    mx.gemm_bf16(wt, dev(xb), y16)
+    ctx.sync()
+    yg = host(y)
+    assert np.isfinite(yg).all()
+    for t in sorted({0, T // 2, T - 1}):
+        assert refmath.rel_err(yg[t], orc.lm_head_f16(x[t], eb)) <= TOL, t
+    assert np.all(yg[:, 3] == 0.0)
+    np.testing.assert_array_equal(host(y16), I.f32_to_bf16_bits(yg))
