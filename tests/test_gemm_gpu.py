@@ -100,19 +100,22 @@ def test_q4_rows_gemm_is_batched_lm_head(ctx, orc, T, vocab, hidden):
     assert np.all(yg[:, 3] == 0.0)
 
 
-@pytest.mark.parametrize("rows", [False, True])
-def test_bf16_output_is_the_f32_sum_rounded(ctx, orc, rows):
+@pytest.mark.parametrize("rows,f16", [(False, False), (True, False), (False, True)])
+def test_bf16_output_is_the_f32_sum_rounded(ctx, orc, rows, f16):
     """qm_gemm_bf16 rounds the same accumulator qm_gemm stores: bit for bit
-    the f32 result rounded to nearest bf16."""
+    the f32 result rounded to nearest bf16 (Q4 in both layouts, F16 [k][n])."""
     import torch
 
     import qora_mixer as qm
 
-    g = np.random.default_rng(11 + rows)
+    g = np.random.default_rng(11 + rows + 2 * f16)
     T, k, n = 300, 2560, 1056
     w = (g.standard_normal((n, k) if rows else (k, n)) * 0.02).astype(np.float32)
-    packed, scales = orc.quantize_q4(w)
-    wt = qm.weight_q4_rows(dev(packed), dev(scales)) if rows else qm.weight_q4(dev(packed), dev(scales))
+    if f16:
+        wt = qm.weight_f16(dev(w.astype(np.float16).view(np.uint16)))
+    else:
+        packed, scales = orc.quantize_q4(w)
+        wt = qm.weight_q4_rows(dev(packed), dev(scales)) if rows else qm.weight_q4(dev(packed), dev(scales))
     xb = dev(I.f32_to_bf16_bits(g.standard_normal((T, k)).astype(np.float32)))
     y32 = torch.empty(T, n, device="cuda")
     y16 = torch.empty(T, n, dtype=torch.int16, device="cuda")

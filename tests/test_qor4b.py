@@ -114,10 +114,13 @@ def test_rejections(orc, tmp_path):
 
 
 @pytest.mark.gpu
-def test_file_to_device_mixer_path(orc, tmp_path):
-    """A one-DeltaNet + one-attention model at the 4B's dimensions: every
-    projection, both mixers and lm_head from the uploaded file against the
-    restatement on the file's own records."""
+@pytest.mark.parametrize("kind", ["q4", "f16"])
+def test_file_to_device_mixer_path(orc, tmp_path, kind):
+    """A one-DeltaNet + one-attention model at the 4B's dimensions, Q4 or F16
+    weights: every projection, both mixers and lm_head from the uploaded file
+    against the restatement on the file's own records (gemv_q4 / gemv_f16 and
+    lm_head_q4 / lm_head_f16 as the record's format says, src/gemv.rs:286-291,
+    662-711)."""
     import torch
 
     import qora_mixer as qm
@@ -126,7 +129,7 @@ def test_file_to_device_mixer_path(orc, tmp_path):
 
     g = np.random.default_rng(3)
     m = _model(orc, g, [0, 1], hidden=2560, qkv=8192, vdim=4096, nv=32, q_out=8192, kv_out=1024, head_dim=256,
-               vocab=1000, max_pos=64)
+               vocab=1000, max_pos=64, kind=kind)
     p = tmp_path / "m.qor4b"
     Q.write_qor4b(p, m)
     r = Q.read_qor4b(p)
@@ -135,6 +138,10 @@ def test_file_to_device_mixer_path(orc, tmp_path):
         up = Q.upload_mixers(r)
         mx = qm.Mixer(ctx)
         c = orc.cfg_4b()
+
+        def ref_gemv(v, w):
+            return orc.gemv_q4(v, w.data, w.scales) if w.kind == "q4" else orc.gemv_f16(v, w.data)
+
         x = g.standard_normal((1, 2560)).astype(np.float32)
         xd = dev(x)
         # DeltaNet layer: fused in_proj, the mixer with its fused gate, out_proj
@@ -144,7 +151,8 @@ def test_file_to_device_mixer_path(orc, tmp_path):
         ctx.sync()
         got = [host(o)[0] for o in outs]
         for name, o in zip(("in_proj_qkv", "in_proj_a", "in_proj_b", "in_proj_z"), got):
-            assert refmath.rel_err(o, orc.gemv_q4(x[0], L0[name].data, L0[name].scales)) <= 5e-5, name
+            assert L0[name].kind == kind
+            assert refmath.rel_err(o, ref_gemv(x[0], L0[name])) <= 5e-5, name
         st = qm.DnState(ctx, 1)
         y = torch.empty(1, 32, 128, device="cuda")
         gated = torch.empty(1, 4096, device="cuda")
@@ -159,8 +167,7 @@ def test_file_to_device_mixer_path(orc, tmp_path):
         h = torch.empty(1, 2560, device="cuda")
         mx.gemv(up[0]["out_proj"], gated, h)
         ctx.sync()
-        assert refmath.rel_err(host(h)[0], orc.gemv_q4(host(gated)[0], L0["out_proj"].data,
-                                                        L0["out_proj"].scales)) <= 5e-5
+        assert refmath.rel_err(host(h)[0], ref_gemv(host(gated)[0], L0["out_proj"])) <= 5e-5
         st.close()
         # attention layer at position 0 (empty cache)
         L1 = r.layers[1]
@@ -187,6 +194,7 @@ def test_file_to_device_mixer_path(orc, tmp_path):
         mx.gemv(up[-1]["lm_head"], xd, logits)
         ctx.sync()
         E = r.globals["embed"]
-        assert refmath.rel_err(host(logits)[0], orc.lm_head_q4(x[0], E.data, E.scales)) <= 5e-5
+        ref_logits = orc.lm_head_q4(x[0], E.data, E.scales) if kind == "q4" else orc.lm_head_f16(x[0], E.data)
+        assert refmath.rel_err(host(logits)[0], ref_logits) <= 5e-5
     finally:
         ctx.close()
