@@ -368,7 +368,10 @@ int qm_gemv_multi(qm_ctx* ctx, const qm_weight* ws, int count, int batch, const 
  * x bf16 [T][k] (16-byte aligned, as the prefill mixers take their inputs),
  * y f32 [T][n].  The weights are rounded to bf16 on the way in (Q4: the
  * scale, then the product):
- * max|y - exact| / RMS(y) is a few 1e-3. */
+ * max|y - exact| / RMS(y) is a few 1e-3.  When T and n give fewer 256 x 256
+ * tiles than half the SMs, K is split over up to 4 CTAs a tile whose partial
+ * sums meet in the scratch area qm_gemv uses (same rules: a fixed order of
+ * addition, QM_E_CAPTURE if it must grow inside a stream capture). */
 int qm_gemm(qm_ctx* ctx, const qm_weight* w, int T, const uint16_t* x, float* y);
 /* The same with y bf16 [T][n] (the f32 sum rounded to nearest): the form the
  * prefill mixers take their q / k / v in (qm_dn_prefill, qm_gqa_prefill). */

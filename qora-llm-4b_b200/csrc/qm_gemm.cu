@@ -23,7 +23,13 @@
 //    per k-step, both halves reading the same dequantised B, so each W tile
 //    is dequantised once for 256 rows; each stage is released to the
 //    producers by tcgen05.commit;
-//  * warps 4-7 read D out of TMEM (their lane quarters) and store Y (f32).
+//  * warps 4-7 read D out of TMEM (their lane quarters) and store Y (f32 or bf16).
+// When the tiles would fill less than half the SMs (a short prompt, a narrow
+// weight), K is split over up to 4 CTAs a tile: each stores its f32 partial
+// tile to a scratch area and the last to finish (an acquire-release counter)
+// adds the partials in split order and stores Y, so the result does not
+// depend on timing.  A tile whose second 128 rows all lie past T loads and
+// multiplies only its first half.
 // A ring of 3 stages (64 KB each) keeps loads, dequantisation and MMAs
 // overlapped.  Every wait is bounded: on a timeout the kernel sets the
 // context's error word and an abort flag, the TMA thread waits (bounded) for
@@ -55,7 +61,8 @@ constexpr int kGmSmem = kGmOffBar + 256 + 1024;  // + barriers + alignment slack
 constexpr int kGmThreads = 384;
 constexpr int kGmProdWarps = 10;  // warps 2..11
 constexpr int kGmChunks = (kGmBK * (kGmBN / 8) + kGmProdWarps * 32 - 1) / (kGmProdWarps * 32);  // 7 a thread
-constexpr int kGmTmCols = 512;  // two accumulators of 128 lanes x 256 f32
+constexpr int kGmTmCols = 512;
+constexpr int kGmMaxSplits = 4;  // split-K: CTAs a tile at most  // two accumulators of 128 lanes x 256 f32
 constexpr uint32_t kGmIdesc = umma_idesc_bf16(128, kGmBN, false, true);      // A K-major, B MN-major
 constexpr uint32_t kGmIdescRows = umma_idesc_bf16(128, kGmBN, false, false); // A and B K-major
 
@@ -63,6 +70,7 @@ struct GmBars {
     uint64_t x_full[kGmStages], w_full[kGmStages], free_[kGmStages], done;
     uint32_t tmem_base;
     int abort_flag;
+    int last;  // split-K: this CTA is the tile's last to finish and adds the partials
 };
 static_assert(sizeof(GmBars) <= 256, "barrier block");
 
@@ -74,7 +82,8 @@ static_assert(sizeof(GmBars) <= 256, "barrier block");
 template <bool ROWS, bool OBF16, bool F16W>
 __global__ void __launch_bounds__(kGmThreads, 1)
 qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restrict__ packed,
-                  const uint16_t* __restrict__ scales, int T, int K, int N, void* __restrict__ y, int* err) {
+                  const uint16_t* __restrict__ scales, int T, int K, int N, void* __restrict__ y, int splits,
+                  float* __restrict__ partial, int* __restrict__ count, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     GmBars* bars = reinterpret_cast<GmBars*>(smem + kGmOffBar);
@@ -82,8 +91,15 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
     const uint32_t sbase = smem_u32(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_n = (N + kGmBN - 1) / kGmBN;
-    const int tm = blockIdx.x / tiles_n, tn = blockIdx.x % tiles_n;
-    const int nk = K / kGmBK;
+    // split-K: CTA (tile, split) takes k steps [kbeg, kbeg + nk) of the tile's K / 64
+    const int tile = blockIdx.x / splits, split = blockIdx.x % splits;
+    const int tm = tile / tiles_n, tn = tile % tiles_n;
+    const int nk_all = K / kGmBK;
+    const int kbeg = (int)((long long)split * nk_all / splits);
+    const int nk = (int)((long long)(split + 1) * nk_all / splits) - kbeg;
+    // a tile whose second 128 rows are all past T (a short prompt, or the last tile of one) loads,
+    // multiplies and stores only its first half
+    const bool two = tm * kGmBM + 128 < T;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kGmStages; s++) {
@@ -116,9 +132,10 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
                     break;
                 }
                 const uint32_t xb = smem_u32(&bars->x_full[s]);
-                mbar_arrive_expect_tx(xb, 2 * kGmXBox);
-                tma_load_3d(sbase + s * kGmStage, &tmx, i * kGmBK, tm * kGmBM, 0, xb);
-                tma_load_3d(sbase + s * kGmStage + kGmXBox, &tmx, i * kGmBK, tm * kGmBM + 128, 0, xb);
+                mbar_arrive_expect_tx(xb, two ? 2 * kGmXBox : kGmXBox);
+                const int kx = (kbeg + i) * kGmBK;
+                tma_load_3d(sbase + s * kGmStage, &tmx, kx, tm * kGmBM, 0, xb);
+                if (two) tma_load_3d(sbase + s * kGmStage + kGmXBox, &tmx, kx, tm * kGmBM + 128, 0, xb);
                 issued = i + 1;
             }
             // every copy this thread issued has landed before the CTA can leave
@@ -144,8 +161,9 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
                     const uint64_t bd = ROWS ? umma_sdesc(ws + kk * 32, 16, 1024) : umma_sdesc(ws + kk * 2048, kGmWBox, 1024);
                     const uint32_t id = ROWS ? kGmIdescRows : kGmIdesc;
                     umma_bf16_ss(tmem, umma_sdesc(xs + kk * 32, 16, 1024), bd, id, (i > 0 || kk > 0) ? 1u : 0u);
-                    umma_bf16_ss(tmem + kGmBN, umma_sdesc(xs + kGmXBox + kk * 32, 16, 1024), bd, id,
-                                 (i > 0 || kk > 0) ? 1u : 0u);
+                    if (two)
+                        umma_bf16_ss(tmem + kGmBN, umma_sdesc(xs + kGmXBox + kk * 32, 16, 1024), bd, id,
+                                     (i > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(smem_u32(&bars->free_[s]));
             }
@@ -191,7 +209,7 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
         const uint32_t stride = F16W ? (ROWS ? (uint32_t)(kGmBK * 2) : (uint32_t)kGmBK * (uint32_t)(N * 2))
                                      : (ROWS ? (uint32_t)(kGmBK / 2) : (uint32_t)kGmBK * (uint32_t)(N / 2));
         auto load_stage = [&](int i, WT(&wv)[kGmChunks], uint16_t(&sv)[kGmChunks]) {
-            const uint32_t base = (uint32_t)i * stride;
+            const uint32_t base = (uint32_t)(kbeg + i) * stride;
 #pragma unroll
             for (int m = 0; m < kGmChunks; m++) {
                 const bool ok = ((okmask >> m) & 1u) && i < nk;
@@ -264,12 +282,38 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
             if (!convert_stage(i + 2, wC, sC)) break;
         }
         if (warp >= 4 && warp < 8) {  // epilogue: TMEM lane quarter warp & 3
+            const int quarter = warp & 3;
+            const uint32_t la = (uint32_t)(quarter * 32) << 16;
+            // 32 sums of row `row`, columns [col, col + 32), into y (rows past T and columns past N skipped)
+            auto store32 = [&](int row, int col, const float* o) {
+                if (row >= T || col >= N) return;
+                if (OBF16) {
+                    uint16_t* dst = static_cast<uint16_t*>(y) + (size_t)row * N + col;
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        uint32_t h[4];
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * q + 2 * e], o[8 * q + 2 * e + 1]);
+                            h[e] = *reinterpret_cast<const uint32_t*>(&b2);
+                        }
+                        *reinterpret_cast<uint4*>(dst + 8 * q) = make_uint4(h[0], h[1], h[2], h[3]);
+                    }
+                } else {
+                    float* dst = static_cast<float*>(y) + (size_t)row * N + col;
+#pragma unroll
+                    for (int q = 0; q < 8; q++)
+                        *reinterpret_cast<float4*>(dst + 4 * q) = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                }
+            };
             if (mbar_wait_bounded(smem_u32(&bars->done), 0, abort_flag, err) && !*abort_flag) {
                 tc_fence_after();
-                const int quarter = warp & 3;
-                const uint32_t la = (uint32_t)(quarter * 32) << 16;
-                for (int hf = 0; hf < 2; hf++) {  // accumulator hf: rows hf * 128 + lane quarter
-                    const int row = tm * kGmBM + hf * 128 + quarter * 32 + lane;
+                // split-K: this CTA's partial tile as float4 [64 column quads][256 rows], so that the
+                // lanes of a warp (consecutive rows) store and later load 512 contiguous bytes
+                float4* mine = splits > 1 ? reinterpret_cast<float4*>(partial) + (size_t)blockIdx.x * (kGmBM * kGmBN / 4)
+                                          : nullptr;
+                for (int hf = 0; hf < (two ? 2 : 1); hf++) {  // accumulator hf: rows hf * 128 + lane quarter
+                    const int r = hf * 128 + quarter * 32 + lane;
                     for (int c = 0; c < kGmBN / 32; c++) {
                         float v[32], o[32];
                         tmem_ld32(tmem + la + hf * kGmBN + c * 32, v);
@@ -277,29 +321,55 @@ qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __rest
 #pragma unroll
                         for (int p = 0; p < 32; p++)  // MN-major Q4 B: columns of each 8 in the order 0 4 1 5 2 6 3 7
                             o[(ROWS || F16W) ? p : (p & ~7) + ((p & 1) ? 4 : 0) + ((p & 7) >> 1)] = v[p];
-                        const int col = n0_tile + c * 32;
-                        if (row < T && col < N) {
-                            if (OBF16) {
-                                uint16_t* dst = static_cast<uint16_t*>(y) + (size_t)row * N + col;
+                        if (splits == 1) {
+                            store32(tm * kGmBM + r, n0_tile + c * 32, o);
+                        } else {
 #pragma unroll
-                                for (int q = 0; q < 4; q++) {
-                                    uint32_t h[4];
+                            for (int q = 0; q < 8; q++)
+                                __stcg(mine + (c * 8 + q) * kGmBM + r, make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]));
+                        }
+                    }
+                }
+            }
+            if (splits > 1) {
+                // every epilogue warp reaches both barriers on every path (an aborted CTA still counts
+                // itself, so the tile's counter always returns to zero).  The counter update is a
+                // release at GPU scope for the partial stores ordered before it by the barrier, and an
+                // acquire: the last CTA then sees every split's partial.
+                named_bar_sync(1, 128);
+                if (warp == 4 && lane == 0) {
+                    int prev;
+                    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(count + tile) : "memory");
+                    bars->last = prev == splits - 1;
+                }
+                named_bar_sync(1, 128);
+                if (bars->last) {
+                    if (!*abort_flag) {
+                        const float4* tp = reinterpret_cast<const float4*>(partial) +
+                                           (size_t)tile * splits * (kGmBM * kGmBN / 4);
+                        for (int hf = 0; hf < (two ? 2 : 1); hf++) {
+                            const int r = hf * 128 + quarter * 32 + lane;
+                            for (int c = 0; c < kGmBN / 32; c++) {
+                                float o[32];
 #pragma unroll
-                                    for (int e = 0; e < 4; e++) {
-                                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[8 * q + 2 * e], o[8 * q + 2 * e + 1]);
-                                        h[e] = *reinterpret_cast<const uint32_t*>(&b2);
+                                for (int p = 0; p < 32; p++) o[p] = 0.f;
+#pragma unroll
+                                for (int sp = 0; sp < kGmMaxSplits; sp++) {  // in split order: the sum does not
+                                    if (sp >= splits) break;                  // depend on timing
+#pragma unroll
+                                    for (int q = 0; q < 8; q++) {
+                                        const float4 f = __ldcg(tp + ((sp * 64 + c * 8 + q) * kGmBM + r));
+                                        o[4 * q] += f.x;
+                                        o[4 * q + 1] += f.y;
+                                        o[4 * q + 2] += f.z;
+                                        o[4 * q + 3] += f.w;
                                     }
-                                    *reinterpret_cast<uint4*>(dst + 8 * q) = make_uint4(h[0], h[1], h[2], h[3]);
                                 }
-                            } else {
-                                float* dst = static_cast<float*>(y) + (size_t)row * N + col;
-#pragma unroll
-                                for (int q = 0; q < 8; q++)
-                                    *reinterpret_cast<float4*>(dst + 4 * q) =
-                                        make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                                store32(tm * kGmBM + r, n0_tile + c * 32, o);
                             }
                         }
                     }
+                    if (warp == 4 && lane == 0) count[tile] = 0;  // ready for the next launch
                 }
             }
         }
@@ -339,7 +409,7 @@ static int gemm_call(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, vo
     CUtensorMap tmx;
     if (encode_rows_tmap(&tmx, const_cast<uint16_t*>(x), (uint64_t)w->k, (uint64_t)T, 1, 64, 128, false) != QM_OK)
         return set_error(c, QM_E_CUDA, "cuTensorMapEncodeTiled failed for x");
-    using Kern = void (*)(CUtensorMap, const uint8_t*, const uint16_t*, int, int, int, void*, int*);
+    using Kern = void (*)(CUtensorMap, const uint8_t*, const uint16_t*, int, int, int, void*, int, float*, int*, int*);
     static const Kern kerns[8] = {
         qm_gemm_q4_kernel<false, false, false>, qm_gemm_q4_kernel<false, true, false>,
         qm_gemm_q4_kernel<true, false, false>,  qm_gemm_q4_kernel<true, true, false>,
@@ -355,10 +425,23 @@ static int gemm_call(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, vo
         attr_set[which].fetch_or(bit);
     }
     const int tiles = ((T + kGmBM - 1) / kGmBM) * ((w->n + kGmBN - 1) / kGmBN);
+    // split K while the tiles would leave more than half the SMs idle: at most 4 splits, at least
+    // 4 k-steps (256 of K) each, and no more CTAs than SMs (one CTA fills an SM)
+    int splits = 1;
+    if (2 * tiles <= c->num_sms) {
+        splits = c->num_sms / tiles;
+        splits = splits < kGmMaxSplits ? splits : kGmMaxSplits;
+        splits = splits < w->k / (4 * kGmBK) ? splits : w->k / (4 * kGmBK);
+        splits = splits > 1 ? splits : 1;
+    }
+    if (splits > 1) {
+        const int rc = ensure_gemv_scratch(c, (size_t)tiles * splits * kGmBM * kGmBN * sizeof(float));
+        if (rc != QM_OK) return rc;
+    }
     TimedLaunch tl(c, "gemm");
-    kern<<<tiles, kGmThreads, kGmSmem, c->stream>>>(tmx, static_cast<const uint8_t*>(w->data),
-                                                    static_cast<const uint16_t*>(w->scales), T, w->k, w->n, y,
-                                                    c->d_err);
+    kern<<<tiles * splits, kGmThreads, kGmSmem, c->stream>>>(
+        tmx, static_cast<const uint8_t*>(w->data), static_cast<const uint16_t*>(w->scales), T, w->k, w->n, y, splits,
+        splits > 1 ? static_cast<float*>(c->gemv_partial) : nullptr, splits > 1 ? c->gemv_count : nullptr, c->d_err);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(c, e, "qm_gemm launch");
     c->launches += 1;

@@ -55,7 +55,7 @@ constexpr int kGvThreads = kGvWarps * 32;
 constexpr int kGvMaxParts = 64;
 constexpr int kGvMaxB = 4;
 constexpr int kGvJobs = 4;         // weights per launch
-constexpr int kGvMaxTiles = 4096;  // counters in the scratch area
+constexpr int kGvMaxTiles = kSplitCounters;  // counters in the scratch area
 
 template <bool Q4>
 struct GvShape {
@@ -359,6 +359,8 @@ int pick_parts(const qm_ctx* c, const GvOccupancy& o, int tiles, int k) {
     return p > 1 ? p : 1;
 }
 
+}  // namespace
+
 int ensure_gemv_scratch(qm_ctx* c, size_t partial_bytes) {
     cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
     const bool capturing = cudaStreamIsCapturing(c->stream, &st) == cudaSuccess && st != cudaStreamCaptureStatusNone;
@@ -384,7 +386,6 @@ int ensure_gemv_scratch(qm_ctx* c, size_t partial_bytes) {
     return QM_OK;
 }
 
-}  // namespace
 }  // namespace qm
 
 using namespace qm;

@@ -100,6 +100,10 @@ namespace qm {
 int set_error(qm_ctx* ctx, int code, const std::string& msg);
 // y[b][v] = x[b] . W[v] for QM_W_F16_ROWS / QM_W_Q4_ROWS weights (qm_head.cu)
 int gemv_rows(qm_ctx* c, const qm_weight* w, int batch, const float* x, float* y);
+// the split-K scratch the GEMV and the GEMM share (calls on one context are stream-ordered): at least
+// partial_bytes of f32 partials and kSplitCounters zeroed tile counters, which every launch leaves zeroed
+constexpr int kSplitCounters = 4096;
+int ensure_gemv_scratch(qm_ctx* c, size_t partial_bytes);
 int cuda_error(qm_ctx* ctx, cudaError_t e, const char* what);
 int ensure_workspace(qm_ctx* ctx, size_t bytes);
 int ensure_stage(qm_ctx* ctx, size_t bytes);

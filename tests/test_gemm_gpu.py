@@ -262,3 +262,33 @@ def test_f16_rows_gemm_is_batched_lm_head(ctx, orc, T, vocab, hidden):
         assert refmath.rel_err(yg[t], orc.lm_head_f16(x[t], eb)) <= TOL, t
     assert np.all(yg[:, 3] == 0.0)
     np.testing.assert_array_equal(host(y16), I.f32_to_bf16_bits(yg))
+
+
+def test_split_k_repeats_and_shares_scratch_with_gemv(ctx, orc):
+    """A short prompt splits K (32 tiles of 256 x 256 on 148 SMs): the same
+    call repeated, with a split-K qm_gemv between them on the same scratch
+    area and counters, gives the same bits, and both match the reference."""
+    import torch
+
+    import qora_mixer as qm
+
+    g = np.random.default_rng(29)
+    T, k, n = 100, 2560, 8192
+    w = (g.standard_normal((k, n)) * 0.02).astype(np.float32)
+    packed, scales = orc.quantize_q4(w)
+    wt = qm.weight_q4(dev(packed), dev(scales))
+    xb = I.f32_to_bf16_bits(g.standard_normal((T, k)).astype(np.float32))
+    x = I.bf16_bits_to_f32(xb)
+    mx = qm.Mixer(ctx)
+    y1 = torch.empty(T, n, device="cuda")
+    y2 = torch.empty(T, n, device="cuda")
+    yv = torch.empty(2, n, device="cuda")
+    mx.gemm(wt, dev(xb), y1)
+    mx.gemv(wt, dev(x[:2]), yv)
+    mx.gemm(wt, dev(xb), y2)
+    ctx.sync()
+    np.testing.assert_array_equal(host(y1), host(y2))
+    ref = x.astype(np.float64) @ orc.dequantize_q4(packed, scales).astype(np.float64)
+    assert refmath.rel_err(host(y1), ref) <= TOL
+    for b in range(2):
+        assert refmath.rel_err(host(yv)[b], orc.gemv_q4(x[b], packed, scales)) <= 5e-5
