@@ -690,7 +690,7 @@ def bench_gemv(ctx, reps, batch=1, kind="q4"):
 
 
 # ----------------------------------------------------------------------------
-# prefill projections: the Q4 GEMM over a whole prompt (tensor cores)
+# prefill projections: the Q4 / F16 GEMM over a whole prompt (tensor cores)
 # ----------------------------------------------------------------------------
 GEMM_SHAPES = [("in_proj_qkv / q_proj", 2560, 8192), ("in_proj_z", 2560, 4096), ("out_proj / o_proj", 4096, 2560),
                ("k_proj / v_proj", 2560, 1024)]
