@@ -739,7 +739,7 @@ def bench_gemm(ctx, reps, T=8192, kind="q4"):
     return {"metric": f"prefill projections ({kind.upper()} GEMM)", "workload": f"{T} tokens x the 4B's "
             f"projection shapes, bf16 x, {wdesc} to bf16 in the kernel, f32 y", "per_shape": rows,
             "value": round(T / (tot_ms / 1e3), 1), "unit": "tok/s (the 4 shapes once each)",
-            "roofline": {"bound": "tensor", "kernel": "qm_gemm_q4_kernel", "achieved": round(ach, 1),
+            "roofline": {"bound": "tensor", "kernel": "qm_gemm_kernel", "achieved": round(ach, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": round(ach / peak, 4)}}
 
 

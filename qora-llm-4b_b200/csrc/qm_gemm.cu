@@ -4,7 +4,7 @@
 // At T tokens each weight is reused T times, so this is a tensor-core GEMM,
 // not a stream.
 //
-// qm_gemm_q4_kernel: one CTA per 256 x 256 tile of Y, K in steps of 64.
+// qm_gemm_kernel: one CTA per 256 x 256 tile of Y, K in steps of 64.
 //  * warp 0 (one thread) loads X tiles [2 x 128 tokens x 64 k] bf16 with TMA
 //    (128-byte swizzle: the K-major A operand);
 //  * warps 2-11 dequantise the matching W tile [64 k x 256 n] from the
@@ -81,7 +81,7 @@ static_assert(sizeof(GmBars) <= 256, "barrier block");
 // F16W: W is f16 ([k][n] or, with ROWS, [n][k]) instead of Q4; `scales` unused.
 template <bool ROWS, bool OBF16, bool F16W>
 __global__ void __launch_bounds__(kGmThreads, 1)
-qm_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restrict__ packed,
+qm_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restrict__ packed,
                   const uint16_t* __restrict__ scales, int T, int K, int N, void* __restrict__ y, int splits,
                   float* __restrict__ partial, int* __restrict__ count, int* err) {
     extern __shared__ uint8_t smem_raw[];
@@ -411,10 +411,10 @@ static int gemm_call(qm_ctx* c, const qm_weight* w, int T, const uint16_t* x, vo
         return set_error(c, QM_E_CUDA, "cuTensorMapEncodeTiled failed for x");
     using Kern = void (*)(CUtensorMap, const uint8_t*, const uint16_t*, int, int, int, void*, int, float*, int*, int*);
     static const Kern kerns[8] = {
-        qm_gemm_q4_kernel<false, false, false>, qm_gemm_q4_kernel<false, true, false>,
-        qm_gemm_q4_kernel<true, false, false>,  qm_gemm_q4_kernel<true, true, false>,
-        qm_gemm_q4_kernel<false, false, true>,  qm_gemm_q4_kernel<false, true, true>,
-        qm_gemm_q4_kernel<true, false, true>,   qm_gemm_q4_kernel<true, true, true>};
+        qm_gemm_kernel<false, false, false>, qm_gemm_kernel<false, true, false>,
+        qm_gemm_kernel<true, false, false>,  qm_gemm_kernel<true, true, false>,
+        qm_gemm_kernel<false, false, true>,  qm_gemm_kernel<false, true, true>,
+        qm_gemm_kernel<true, false, true>,   qm_gemm_kernel<true, true, true>};
     static std::atomic<uint64_t> attr_set[8];
     const int which = (f16w ? 4 : 0) + (rows ? 2 : 0) + (obf16 ? 1 : 0);
     const Kern kern = kerns[which];
