@@ -61,8 +61,8 @@ constexpr int kGmSmem = kGmOffBar + 256 + 1024;  // + barriers + alignment slack
 constexpr int kGmThreads = 384;
 constexpr int kGmProdWarps = 10;  // warps 2..11
 constexpr int kGmChunks = (kGmBK * (kGmBN / 8) + kGmProdWarps * 32 - 1) / (kGmProdWarps * 32);  // 7 a thread
-constexpr int kGmTmCols = 512;
-constexpr int kGmMaxSplits = 4;  // split-K: CTAs a tile at most  // two accumulators of 128 lanes x 256 f32
+constexpr int kGmTmCols = 512;    // two accumulators of 128 lanes x 256 f32
+constexpr int kGmMaxSplits = 4;  // split-K: CTAs a tile at most
 constexpr uint32_t kGmIdesc = umma_idesc_bf16(128, kGmBN, false, true);      // A K-major, B MN-major
 constexpr uint32_t kGmIdescRows = umma_idesc_bf16(128, kGmBN, false, false); // A and B K-major
 
@@ -82,8 +82,8 @@ static_assert(sizeof(GmBars) <= 256, "barrier block");
 template <bool ROWS, bool OBF16, bool F16W>
 __global__ void __launch_bounds__(kGmThreads, 1)
 qm_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restrict__ packed,
-                  const uint16_t* __restrict__ scales, int T, int K, int N, void* __restrict__ y, int splits,
-                  float* __restrict__ partial, int* __restrict__ count, int* err) {
+               const uint16_t* __restrict__ scales, int T, int K, int N, void* __restrict__ y, int splits,
+               float* __restrict__ partial, int* __restrict__ count, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     GmBars* bars = reinterpret_cast<GmBars*>(smem + kGmOffBar);
