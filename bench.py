@@ -113,9 +113,15 @@ class Clocks:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
+        return self.summarize(self.lines)
+
+    @staticmethod
+    def summarize(lines):
+        """Median SM clock, the max clock and the throttle reasons seen Active, from nvidia-smi CSV lines
+        (malformed or not-available samples are skipped)."""
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue

@@ -39,3 +39,25 @@ def test_reference_arm_other_ranks_exit_quietly():
     p = _run({"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"}, "--steps", "1", "--warmup", "3")
     assert p.returncode == 0, p.stderr[-2000:]
     assert not [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
+
+
+def test_clock_samples_summary():
+    """The clocks record of the JSON line, from nvidia-smi CSV samples: median SM clock under load, the
+    max clock, and every throttle reason seen Active (sw_power_cap is kept and noted; the hw/thermal ones
+    make a run invalid)."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    lines = [
+        "0, 1965, 1965, 700.1, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active",
+        "0, 1890, 1965, 990.5, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        "0, 1950, 1965, 995.0, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        "0, [N/A], 1965, 0, 0x0, Not Active, Not Active, Not Active, Not Active",
+        "garbage",
+    ]
+    d = bench.Clocks.summarize(lines)
+    assert d == {"sm_mhz": 1950.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 3}
+    hot = bench.Clocks.summarize([lines[0].replace("Not Active, Not Active, Not Active, Not Active",
+                                                   "Active, Not Active, Active, Not Active")])
+    assert hot["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"]
+    assert bench.Clocks.summarize([])["sm_mhz"] is None
