@@ -19,7 +19,7 @@ cpu_baseline = the CPU restatement of the reference mixer path on a bounded
          sample (rank 0, N=1 only).
 
 --impl reference times that CPU restatement as the reference arm (the
-reference is Rust and cannot be built here).
+reference is a Rust crate and no Rust toolchain exists on these machines).
 """
 from __future__ import annotations
 
@@ -113,7 +113,8 @@ class Clocks:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        return self.summarize(self.lines)
+        self.t.join(timeout=5)  # the reader has seen every line before the summary
+        return self.summarize(list(self.lines))
 
     @staticmethod
     def summarize(lines):
@@ -493,6 +494,9 @@ def run_ours(args):
                      "achieved": round(att_achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(att_achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": att_traffic,
+                     "traffic_source": ("not measured in this run: the DRAM bytes per (sequence, cached position) "
+                                        "of an ncu capture of a smaller case (profiles/traffic.json) x batch x "
+                                        "positions") if att_traffic else None,
                      "algorithmic_bytes_per_launch": att_bytes,
                      "avg_launch_us": round(att_ms / att_n * 1e3, 2)},
         "kernels": {

@@ -594,12 +594,9 @@ cudaError_t launch_stream(qm_ctx* ctx, int b0, int nb, const qm_dn_params* p, qm
                           const float* qkv, const float* a, const float* b, float* y,
                           const float* z, float* out, int slot_w) {
     auto kern = dn_decode_stream<FUSED, kStreamNB, kStreamMinB, PAIR>;
-    static bool attr_set[2][2][64] = {};
-    if (ctx->device < 64 && !attr_set[FUSED][PAIR][ctx->device]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kStreamSmem);
-        if (e != cudaSuccess) return e;
-        attr_set[FUSED][PAIR][ctx->device] = true;
-    }
+    static std::atomic<uint64_t> attr_set{0};  // one per template instance
+    const cudaError_t ea = set_smem_once(attr_set, ctx->device, kern, kStreamSmem);
+    if (ea != cudaSuccess) return ea;
     const int n_items = nb * s->nvh;
     const int grid = PAIR ? n_items / 2 : n_items;  // one CTA per head (per V-head pair)
     kern<<<grid, 256, kStreamSmem, ctx->stream>>>(

@@ -1083,14 +1083,10 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
         encode_rows_tmap(&mkth, kth, kHd, kC, items, 64, kC, true) != QM_OK ||
         encode_rows_tmap(&mktl, ktl, kHd, kC, items, 64, kC, true) != QM_OK)
         return cudaErrorInvalidValue;
-    static bool attr_set[64] = {};
-    if (ctx->device < 64 && !attr_set[ctx->device]) {
-        e = cudaFuncSetAttribute(dn_chunk_local, cudaFuncAttributeMaxDynamicSharedMemorySize, kLocalSmem);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(dn_chunk_state, cudaFuncAttributeMaxDynamicSharedMemorySize, kStateSmem);
-        if (e != cudaSuccess) return e;
-        attr_set[ctx->device] = true;
-    }
+    static std::atomic<uint64_t> attr_local{0}, attr_state{0};
+    e = set_smem_once(attr_local, ctx->device, dn_chunk_local, kLocalSmem);
+    if (e == cudaSuccess) e = set_smem_once(attr_state, ctx->device, dn_chunk_state, kStateSmem);
+    if (e != cudaSuccess) return e;
     {
         TimedLaunch tl(ctx, "dn_chunk_local");
         dn_chunk_local<<<dim3(kNumV, nch, B), kLocalThreads, kLocalSmem, s>>>(

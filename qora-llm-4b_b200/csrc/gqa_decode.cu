@@ -476,13 +476,9 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
     if (e != cudaSuccess) return e;
     ctx->launches += 1;
     if (pl.nsplit > 0) {
-        static bool attr_set[64] = {};
-        if (ctx->device < 64 && !attr_set[ctx->device]) {
-            e = cudaFuncSetAttribute(gqa_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kAttnSmem);
-            if (e != cudaSuccess) return e;
-            attr_set[ctx->device] = true;
-        }
+        static std::atomic<uint64_t> attr_set{0};
+        e = set_smem_once(attr_set, ctx->device, gqa_attn_kernel, kAttnSmem);
+        if (e != cudaSuccess) return e;
         dim3 grid(pl.nsplit, nkv, B);
         TimedLaunch tl(ctx, "gqa_attn");
         gqa_attn_kernel<<<grid, 160, kAttnSmem, st>>>(kv->tmap_k, kv->tmap_v, q_bf, part_o,

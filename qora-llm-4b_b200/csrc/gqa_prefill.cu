@@ -48,8 +48,7 @@
 //    chunks — shared memory (ring 176 KB + P 32 KB) and TMEM (all 512
 //    columns) are both full at head dim 256 on one SM.  A CTA-pair form
 //    (cta_group::2, M = 256, each CTA staging half of every K/V tile) gave
-//    the same per-SM MMA times and K/V waits and was not kept; its building
-//    blocks are in qm_ptx.cuh, checked by qm_selftest_umma_pair.
+//    the same per-SM MMA times and K/V waits and was not kept.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -98,24 +97,6 @@ struct Bars {
     int abort_flag;
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
-
-// Self-test layout (umma_selftest_kernel): one 64-key tile of each operand.
-constexpr int kStKBox = 64 * 128;                 // [64 rows x 64 dims] = 8 KB
-constexpr int kStOffQ = 0;
-constexpr int kStOffK = kStOffQ + 4 * kQBox;
-constexpr int kStOffV = kStOffK + 4 * kStKBox;
-constexpr int kStOffP = kStOffV + 4 * kStKBox;
-constexpr int kStOffBar = kStOffP + kBM * 128;
-constexpr int kStSmem = kStOffBar + 256 + 1024;
-constexpr int kStTmS = 128;
-constexpr uint32_t kStIdescS = umma_idesc_f16kind(kBM, 64, false, false, false);
-constexpr uint32_t kStIdescS_bf = umma_idesc_bf16(kBM, 64, false, false);
-constexpr uint32_t kStIdescO_bf = umma_idesc_bf16(kBM, 256, false, true);
-struct StBars {
-    uint64_t ld_full, mma_done;
-    uint32_t tmem_base;
-    int abort_flag;
-};
 
 // Rows of a [128 x 256] fp16 tile held as 4 TMA boxes of [128 rows x 64]
 // (128-byte swizzle) -> TMEM, column col0 + d/2 of lane `row` holding dims d
@@ -522,230 +503,6 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
     }
 }
 
-// ---------------------------------------------------------------------------
-// Self-test of the tcgen05 building blocks (descriptors, TMEM mapping):
-//   D1[128x64]  = A[128x256] . B[64x256]^T   (K-major A and B, TMA SW128; with
-//                 mode bit 1 A is first copied to TMEM and read from there)
-//   D2[128x256] = P[128x64]  . V[64x256]      (P written by threads, V MN-major)
-// One CTA of 192 threads; same code paths as gqa_prefill_attn.
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(192, 1)
-umma_selftest_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
-                     const __grid_constant__ CUtensorMap tmv, const uint16_t* __restrict__ P,
-                     float* __restrict__ d1, float* __restrict__ d2, int mode, int* err) {
-    const bool fp16 = (mode & 1) != 0, a_tmem = (mode & 2) != 0;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    StBars* bars = reinterpret_cast<StBars*>(smem + kStOffBar);
-    volatile int* abort_flag = &bars->abort_flag;
-    const uint32_t sbase = smem_u32(smem);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        mbar_init(smem_u32(&bars->ld_full), 1);
-        mbar_init(smem_u32(&bars->mma_done), 1);
-        bars->abort_flag = 0;
-        fence_barrier_init();
-    }
-    if (warp == 1) {
-        tmem_alloc(smem_u32(&bars->tmem_base), kTmCols);
-        tmem_relinquish();
-    }
-    // P by plain stores into the swizzled K-major layout (rows of 64 bf16)
-    for (int i = threadIdx.x; i < kBM * 8; i += blockDim.x) {
-        const int row = i / 8, c = i % 8;
-        const uint4 v = *reinterpret_cast<const uint4*>(P + row * 64 + c * 8);
-        *reinterpret_cast<uint4*>(smem + kStOffP + sw128_off(row, c)) = v;
-    }
-    fence_proxy_async_shared();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tm = bars->tmem_base;
-    const uint32_t qb = smem_u32(&bars->ld_full);
-    if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(qb, 4 * kQBox + 8 * kStKBox);
-        for (int sub = 0; sub < 4; sub++) {
-            tma_load_3d(sbase + kStOffQ + sub * kQBox, &tma, sub * 64, 0, 0, qb);
-            tma_load_3d(sbase + kStOffK + sub * kStKBox, &tmb, sub * 64, 0, 0, qb);
-            tma_load_3d(sbase + kStOffV + sub * kStKBox, &tmv, sub * 64, 0, 0, qb);
-        }
-    }
-    bool ok = mbar_wait_bounded(qb, 0, abort_flag, err);
-    if (ok && a_tmem && warp >= 2) {  // warps 2..5 own lane quarters 2, 3, 0, 1
-        const int quarter = warp & 3;
-        tile_rows_to_tmem(smem + kStOffQ, tm + ((uint32_t)(quarter * 32) << 16) + kTmQ, quarter * 32 + lane, 0, 4);
-        tmem_st_wait();
-    }
-    tc_fence_before();
-    ok = __syncthreads_and(ok) != 0;
-    if (threadIdx.x == 0 && ok) {
-        tc_fence_after();
-        for (int kk = 0; kk < 16; kk++) {
-            const uint64_t bd = umma_sdesc(sbase + kStOffK + (kk >> 2) * kStKBox + (kk & 3) * 32, 16, 1024);
-            if (a_tmem)
-                umma_f16_ts(tm + kStTmS, tm + kTmQ + kk * 8, bd, fp16 ? kStIdescS : kStIdescS_bf, kk > 0);
-            else
-                umma_bf16_ss(tm + kStTmS,
-                             umma_sdesc(sbase + kStOffQ + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024), bd,
-                             fp16 ? kStIdescS : kStIdescS_bf, kk > 0);
-        }
-        for (int kk = 0; kk < 4; kk++)
-            umma_bf16_ss(tm + kTmO, umma_sdesc(sbase + kStOffP + kk * 32, 16, 1024),
-                         umma_sdesc(sbase + kStOffV + kk * 2048, kStKBox, 1024),
-                         fp16 ? kIdescO : kStIdescO_bf, kk > 0);
-        umma_commit(smem_u32(&bars->mma_done));
-    }
-    if (warp >= 2 && ok) {
-        const int quarter = warp & 3, r = quarter * 32 + lane;
-        const uint32_t la = (uint32_t)(quarter * 32) << 16;
-        if (mbar_wait_bounded(smem_u32(&bars->mma_done), 0, abort_flag, err)) {
-            tc_fence_after();
-            for (int c = 0; c < 2; c++) {
-                float v[32];
-                tmem_ld32(tm + la + kStTmS + c * 32, v);
-                tmem_ld_wait();
-                for (int i = 0; i < 32; i++) d1[r * 64 + c * 32 + i] = v[i];
-            }
-            for (int c = 0; c < 8; c++) {
-                float v[32];
-                tmem_ld32(tm + la + kTmO + c * 32, v);
-                tmem_ld_wait();
-                for (int i = 0; i < 32; i++) d2[r * 256 + c * 32 + i] = v[i];
-            }
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tm, kTmCols);
-    }
-}
-
-
-// ---------------------------------------------------------------------------
-// Self-test of the CTA-pair (cta_group::2) building blocks, one cluster of 2:
-//   D1[256x128] = A[256x256] . B[128x256]^T  rank r holds A rows [128r, +128)
-//                 and B rows (the N of this product) [64r, +64); mode bit 1:
-//                 A is first copied to TMEM and read from there
-//   D2[256x256] = P[256x64] . V[64x256]      rank r holds P rows [128r, +128)
-//                 and V dims (N) [128r, +128), V MN-major
-// A completes on a barrier of its own CTA; B and V on rank 0's barrier.
-// ---------------------------------------------------------------------------
-constexpr int kPtOffA = 0;                         // 4 boxes [128 x 64]
-constexpr int kPtOffB = kPtOffA + 4 * kQBox;       // 4 boxes [64 x 64]
-constexpr int kPtOffV = kPtOffB + 4 * kStKBox;     // 2 boxes [64 keys x 64 dims]
-constexpr int kPtOffP = kPtOffV + 2 * kStKBox;     // [128 x 64]
-constexpr int kPtOffBar = kPtOffP + kBM * 128;
-constexpr int kPtSmem = kPtOffBar + 256 + 1024;
-struct PtBars {
-    uint64_t a_full, ld_full, mma_done;
-    uint32_t tmem_base;
-    int abort_flag;
-};
-
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
-umma_pair_selftest_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb,
-                          const __grid_constant__ CUtensorMap tmv, const uint16_t* __restrict__ P,
-                          float* __restrict__ d1, float* __restrict__ d2, int mode, int* err) {
-    const bool fp16 = (mode & 1) != 0, a_tmem = (mode & 2) != 0;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    PtBars* bars = reinterpret_cast<PtBars*>(smem + kPtOffBar);
-    volatile int* abort_flag = &bars->abort_flag;
-    const uint32_t sbase = smem_u32(smem);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t rank = cluster_ctarank();
-    if (threadIdx.x == 0) {
-        mbar_init(smem_u32(&bars->a_full), 1);
-        mbar_init(smem_u32(&bars->ld_full), 1);
-        mbar_init(smem_u32(&bars->mma_done), 1);
-        bars->abort_flag = 0;
-        fence_barrier_init();
-    }
-    if (warp == 1) {
-        tmem_alloc_pair(smem_u32(&bars->tmem_base), kTmCols);
-        tmem_relinquish_pair();
-    }
-    for (int i = threadIdx.x; i < kBM * 8; i += blockDim.x) {
-        const int row = i / 8, c = i % 8;
-        const uint4 v = *reinterpret_cast<const uint4*>(P + ((size_t)rank * kBM + row) * 64 + c * 8);
-        *reinterpret_cast<uint4*>(smem + kPtOffP + sw128_off(row, c)) = v;
-    }
-    fence_proxy_async_shared();
-    tc_fence_before();
-    cluster_sync_all();  // both CTAs' barriers initialised, TMEM allocated
-    tc_fence_after();
-    const uint32_t tm = bars->tmem_base;
-    if (threadIdx.x == 0) {
-        const uint32_t af = smem_u32(&bars->a_full);
-        mbar_arrive_expect_tx(af, 4 * kQBox);
-        for (int sub = 0; sub < 4; sub++)
-            tma_load_3d(sbase + kPtOffA + sub * kQBox, &tma, sub * 64, kBM * (int)rank, 0, af);
-        const uint32_t lf0 = mapa_shared(smem_u32(&bars->ld_full), 0);
-        if (rank == 0) mbar_arrive_expect_tx(smem_u32(&bars->ld_full), 2 * (4 + 2) * kStKBox);
-        for (int sub = 0; sub < 4; sub++)
-            tma_load_3d_pair(sbase + kPtOffB + sub * kStKBox, &tmb, sub * 64, 64 * (int)rank, 0, lf0);
-        for (int d = 0; d < 2; d++)
-            tma_load_3d_pair(sbase + kPtOffV + d * kStKBox, &tmv, 128 * (int)rank + 64 * d, 0, 0, lf0);
-    }
-    bool ok = mbar_wait_bounded(smem_u32(&bars->a_full), 0, abort_flag, err);
-    if (ok && a_tmem && warp >= 2) {  // warps 2..5 own lane quarters 2, 3, 0, 1
-        const int quarter = warp & 3;
-        tile_rows_to_tmem(smem + kPtOffA, tm + ((uint32_t)(quarter * 32) << 16) + kTmQ, quarter * 32 + lane, 0, 4);
-        tmem_st_wait();
-    }
-    tc_fence_before();
-    cluster_sync_all();  // both CTAs' A in TMEM (or shared memory) and P written
-    tc_fence_after();
-    if (rank == 0 && threadIdx.x == 0 && ok) {
-        ok = mbar_wait_cluster_bounded(smem_u32(&bars->ld_full), 0, abort_flag, err);
-        if (ok) {
-            tc_fence_after();
-            const uint32_t id1 = umma_idesc_f16kind(2 * kBM, 128, false, false, !fp16);
-            const uint32_t id2 = umma_idesc_f16kind(2 * kBM, 256, false, true, !fp16);
-            for (int kk = 0; kk < 16; kk++) {
-                const uint64_t bd = umma_sdesc(sbase + kPtOffB + (kk >> 2) * kStKBox + (kk & 3) * 32, 16, 1024);
-                if (a_tmem)
-                    umma_pair_ts(tm + kStTmS, tm + kTmQ + kk * 8, bd, id1, kk > 0);
-                else
-                    umma_pair_ss(tm + kStTmS, umma_sdesc(sbase + kPtOffA + (kk >> 2) * kQBox + (kk & 3) * 32, 16, 1024),
-                                 bd, id1, kk > 0);
-            }
-            for (int kk = 0; kk < 4; kk++)
-                umma_pair_ss(tm + kTmO, umma_sdesc(sbase + kPtOffP + kk * 32, 16, 1024),
-                             umma_sdesc(sbase + kPtOffV + kk * 2048, kStKBox, 1024), id2, kk > 0);
-            umma_commit_pair(smem_u32(&bars->mma_done), 0x3);
-        }
-    }
-    if (warp >= 2 && ok) {
-        const int quarter = warp & 3, r = quarter * 32 + lane;
-        const size_t row = (size_t)rank * kBM + r;
-        const uint32_t la = (uint32_t)(quarter * 32) << 16;
-        if (mbar_wait_cluster_bounded(smem_u32(&bars->mma_done), 0, abort_flag, err)) {
-            tc_fence_after();
-            for (int c = 0; c < 4; c++) {
-                float v[32];
-                tmem_ld32(tm + la + kStTmS + c * 32, v);
-                tmem_ld_wait();
-                for (int i = 0; i < 32; i++) d1[row * 128 + c * 32 + i] = v[i];
-            }
-            for (int c = 0; c < 8; c++) {
-                float v[32];
-                tmem_ld32(tm + la + kTmO + c * 32, v);
-                tmem_ld_wait();
-                for (int i = 0; i < 32; i++) d2[row * 256 + c * 32 + i] = v[i];
-            }
-        }
-    }
-    tc_fence_before();
-    cluster_sync_all();  // no CTA leaves (or frees TMEM) while the pair's MMAs may still read it
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc_pair(tm, kTmCols);
-    }
-}
-
 }  // namespace
 
 // fp16 q [B,16,T,256], k and v [B,4,T,256]
@@ -775,13 +532,9 @@ cudaError_t launch_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
         encode_rows_tmap(&tmk, kw, kD, (uint64_t)T, (uint64_t)B * kNumKVH, 64, kBN, true) != QM_OK ||
         encode_rows_tmap(&tmv, vw, kD, (uint64_t)T, (uint64_t)B * kNumKVH, 64, 32, true) != QM_OK)
         return cudaErrorInvalidValue;
-    static bool attr_set[64] = {};
-    if (ctx->device < 64 && !attr_set[ctx->device]) {
-        e = cudaFuncSetAttribute(gqa_prefill_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kPrefillSmem);
-        if (e != cudaSuccess) return e;
-        attr_set[ctx->device] = true;
-    }
+    static std::atomic<uint64_t> attr_set{0};
+    e = set_smem_once(attr_set, ctx->device, gqa_prefill_attn, kPrefillSmem);
+    if (e != cudaSuccess) return e;
     const int nqt = (T + kBM - 1) / kBM;
     dim3 grid(nqt * kNumH, B);
     {
@@ -820,55 +573,4 @@ extern "C" int qm_gqa_prefill(qm_ctx* c, const qm_gqa_params* p, qm_kv* kv, int 
     if (e != cudaSuccess) return cuda_error(c, e, "gqa_prefill launch");
     kv->seq_len = T;
     return QM_OK;
-}
-
-// Self-test of the tcgen05 descriptor encodings (test hook, not part of the
-// mixer ABI).  a [128x256], b [64x256], v [64x256], p [128x64] (device; all
-// bf16, or all fp16 when mode bit 0 is set; mode bit 1: the first product
-// reads a from TMEM); d1 [128x64], d2 [128x256] f32.  Synchronous; returns a
-// QM status.
-extern "C" int qm_selftest_umma(const uint16_t* a, const uint16_t* b, const uint16_t* v,
-                                const uint16_t* p, float* d1, float* d2, int mode) {
-    CUtensorMap ta, tb, tv;
-    const bool h = (mode & 1) != 0;
-    if (encode_rows_tmap(&ta, (void*)a, 256, 128, 1, 64, 128, h) != QM_OK ||
-        encode_rows_tmap(&tb, (void*)b, 256, 64, 1, 64, 64, h) != QM_OK ||
-        encode_rows_tmap(&tv, (void*)v, 256, 64, 1, 64, 64, h) != QM_OK)
-        return QM_E_CUDA;
-    int* err = nullptr;
-    if (cudaMalloc(&err, sizeof(int)) != cudaSuccess) return QM_E_OOM;
-    cudaMemset(err, 0, sizeof(int));
-    cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStSmem);
-    umma_selftest_kernel<<<1, 192, kStSmem>>>(ta, tb, tv, p, d1, d2, mode, err);
-    cudaError_t e = cudaDeviceSynchronize();
-    int flag = 0;
-    cudaMemcpy(&flag, err, sizeof(int), cudaMemcpyDeviceToHost);
-    cudaFree(err);
-    if (e != cudaSuccess) return QM_E_CUDA;
-    return flag ? QM_E_TIMEOUT : QM_OK;
-}
-
-// Self-test of the CTA-pair building blocks (test hook, not part of the mixer
-// ABI): a [256x256], b [128x256], v [64x256], p [256x64] (device; all bf16, or
-// all fp16 when mode bit 0 is set; mode bit 1: the first product reads a from
-// TMEM); d1 [256x128], d2 [256x256] f32.  Synchronous; returns a QM status.
-extern "C" int qm_selftest_umma_pair(const uint16_t* a, const uint16_t* b, const uint16_t* v,
-                                     const uint16_t* p, float* d1, float* d2, int mode) {
-    CUtensorMap ta, tb, tv;
-    const bool h = (mode & 1) != 0;
-    if (encode_rows_tmap(&ta, (void*)a, 256, 256, 1, 64, 128, h) != QM_OK ||
-        encode_rows_tmap(&tb, (void*)b, 256, 128, 1, 64, 64, h) != QM_OK ||
-        encode_rows_tmap(&tv, (void*)v, 256, 64, 1, 64, 64, h) != QM_OK)
-        return QM_E_CUDA;
-    int* err = nullptr;
-    if (cudaMalloc(&err, sizeof(int)) != cudaSuccess) return QM_E_OOM;
-    cudaMemset(err, 0, sizeof(int));
-    cudaFuncSetAttribute(umma_pair_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPtSmem);
-    umma_pair_selftest_kernel<<<2, 192, kPtSmem>>>(ta, tb, tv, p, d1, d2, mode, err);
-    cudaError_t e = cudaDeviceSynchronize();
-    int flag = 0;
-    cudaMemcpy(&flag, err, sizeof(int), cudaMemcpyDeviceToHost);
-    cudaFree(err);
-    if (e != cudaSuccess) return QM_E_CUDA;
-    return flag ? QM_E_TIMEOUT : QM_OK;
 }

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <map>
 #include <string>
 #include <utility>
@@ -144,6 +145,19 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
                               const uint16_t* qkv, const float* a, const float* b, float* y,
                               const float* z, float* out);
 size_t dn_prefill_ws_bytes(int batch, int T);
+
+// Raises a kernel's dynamic shared memory limit once per device.  `done` holds
+// one bit per device and is atomic: contexts on different devices (and the
+// allocation-free entry point) may be driven from different host threads.
+// Setting the attribute twice is harmless, so a lost race only repeats it.
+template <typename Kernel>
+cudaError_t set_smem_once(std::atomic<uint64_t>& done, int device, Kernel kern, int bytes) {
+    const uint64_t bit = (device >= 0 && device < 64) ? (1ull << device) : 0;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
 
 }  // namespace qm
 

@@ -288,20 +288,11 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int chunk) {
 }
 
 // ---------------------------------------------------------------------------
-// CTA pairs (cluster of 2) for tcgen05 with cta_group::2: one MMA of M = 256
-// spans both SMs; A's rows and B's N columns are split between the two CTAs
-// (rank r holds rows / columns [r*M/2, (r+1)*M/2) and [r*N/2, (r+1)*N/2) at
-// the same shared-memory offsets) and each CTA's TMEM holds its M/2 rows of
-// D over all N columns.  Rank 0 issues the MMAs.
+// Thread-block clusters: rank, cluster-wide barrier, distributed shared memory.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t cluster_nctarank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
     return r;
 }
 __device__ __forceinline__ void cluster_sync_all() {
@@ -312,91 +303,6 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
     uint32_t r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
     return r;
-}
-// Arrive on an mbarrier of another CTA of the cluster (address from mapa_shared).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait (cluster-scope acquire) for barriers that other CTAs arrive on.
-__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint32_t bar, uint32_t parity,
-                                                          volatile int* abort_flag, int* err) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    const long long t0 = clock64();
-    while (true) {
-        if (*abort_flag) return false;
-        if (mbar_try_wait_cluster(bar, parity)) return true;
-        if (clock64() - t0 > kWaitCycles) {
-            *abort_flag = 1;
-            atomicOr(err, kErrTimeout);
-            return false;
-        }
-    }
-}
-// 3-D tiled TMA load into this CTA's shared memory whose completion (tx
-// bytes) is counted on `bar_cluster`, an mbarrier of rank 0 (mapa_shared):
-// the pair's loads of one stage complete on the issuing CTA's barrier.  No
-// multicast.
-__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, int c0, int c1,
-                                                 int c2, uint32_t bar_cluster) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar_cluster)
-        : "memory");
-}
-// TMEM allocation for a CTA pair: the same warp of both CTAs executes it,
-// with the same shared-memory destination offset.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t smem_dst, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_dst),
-                 "r"(ncols)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-                 : "memory");
-}
-// D(tmem, both CTAs) (+)= A(smem desc, both CTAs) * B(smem desc, both CTAs)
-__device__ __forceinline__ void umma_pair_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
-        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
-        : "memory");
-}
-// D(tmem) (+)= A(tmem, both CTAs) * B(smem desc, both CTAs)
-__device__ __forceinline__ void umma_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                             uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
-        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
-        : "memory");
-}
-// One arrival on the mbarrier at offset `bar` of every CTA in `mask` once all
-// prior pair MMAs of this thread complete.
-__device__ __forceinline__ void umma_commit_pair(uint32_t bar, uint16_t mask) {
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-            bar),
-        "h"(mask)
-        : "memory");
 }
 
 }  // namespace qm

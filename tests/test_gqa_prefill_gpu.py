@@ -6,6 +6,7 @@ K (after QK-norm and RoPE) within one bf16 rounding of the oracle's f32 K,
 V bit-exact (a copy of the bf16 input).
 """
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -35,7 +36,8 @@ def test_tcgen05_descriptor_selftest(fp16, a_tmem):
 
     import qora_mixer as qm
 
-    L = qm.lib()
+    qm.lib()  # the self-test library links against the product library
+    L = C.CDLL(os.path.join(qm.PKG_DIR, "libqora_selftest.so"))
     fn = L.qm_selftest_umma
     fn.argtypes = [C.c_void_p] * 6 + [C.c_int]
     fn.restype = C.c_int
@@ -47,38 +49,6 @@ def test_tcgen05_descriptor_selftest(fp16, a_tmem):
     p = torch.rand(128, 64, device="cuda", generator=g).to(dt)
     d1 = torch.zeros(128, 64, device="cuda")
     d2 = torch.zeros(128, 256, device="cuda")
-    torch.cuda.synchronize()
-    rc = fn(a.data_ptr(), b.data_ptr(), v.data_ptr(), p.data_ptr(), d1.data_ptr(), d2.data_ptr(),
-            fp16 | (a_tmem << 1))
-    assert rc == 0
-    r1 = a.double() @ b.double().T
-    r2 = p.double() @ v.double()
-    assert refmath.rel_err(d1.cpu().numpy(), r1.cpu().numpy()) < 1e-5
-    assert refmath.rel_err(d2.cpu().numpy(), r2.cpu().numpy()) < 1e-5
-
-
-@pytest.mark.parametrize("fp16,a_tmem", [(1, 0), (1, 1), (0, 0)])
-def test_tcgen05_pair_selftest(fp16, a_tmem):
-    """The CTA-pair (cta_group::2) forms on one M = 256 product: A rows and B
-    columns split between the two CTAs of a cluster, B and V loads completing
-    on rank 0's barrier, MMAs issued by rank 0, completion multicast to both
-    CTAs; each CTA reads its 128 rows of D from its own TMEM."""
-    import torch
-
-    import qora_mixer as qm
-
-    L = qm.lib()
-    fn = L.qm_selftest_umma_pair
-    fn.argtypes = [C.c_void_p] * 6 + [C.c_int]
-    fn.restype = C.c_int
-    dt = torch.float16 if fp16 else torch.bfloat16
-    g = torch.Generator(device="cuda").manual_seed(11)
-    a = torch.randn(256, 256, device="cuda", generator=g).to(dt)
-    b = torch.randn(128, 256, device="cuda", generator=g).to(dt)
-    v = torch.randn(64, 256, device="cuda", generator=g).to(dt)
-    p = torch.rand(256, 64, device="cuda", generator=g).to(dt)
-    d1 = torch.zeros(256, 128, device="cuda")
-    d2 = torch.zeros(256, 256, device="cuda")
     torch.cuda.synchronize()
     rc = fn(a.data_ptr(), b.data_ptr(), v.data_ptr(), p.data_ptr(), d1.data_ptr(), d2.data_ptr(),
             fp16 | (a_tmem << 1))
