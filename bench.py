@@ -515,6 +515,10 @@ def run_ours(args):
     if not args.no_prefill:
         line["prefill_gqa"] = bench_gqa_prefill(ctx, ws, args.prefill_reps)
         line["prefill_dn"] = bench_dn_prefill(ctx, ws, args.prefill_reps)
+    if not args.no_small:
+        cpu = rank == 0 and ws == 1 and not args.no_cpu_baseline
+        line["decode_config0"] = bench_config0(ctx, args.prefill_reps * 3, cpu=cpu)
+        line["decode_config1"] = bench_config1(ctx, args.prefill_reps * 3, cpu=cpu)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(args.cpu_tokens)
     if rank == 0:
@@ -901,6 +905,205 @@ def bench_dn_prefill(ctx, ws, reps, B=8, T=8192):
 
 
 # ----------------------------------------------------------------------------
+# workloads 0 and 1: single-layer decode at batch 1
+# ----------------------------------------------------------------------------
+CFG0_BYTES_TOKEN = 2 * 32 * 128 * 128 * 4 + 2 * 8192 * 3 * 4 + 8192 * 4 + 2 * 32 * 4 + 32 * 128 * 4
+CFG1_L = 4096
+
+
+def cfg1_bytes(L=CFG1_L):
+    """K/V of L cached positions plus the new one read, the new row appended, q/gate, k, v in, out."""
+    return 2 * 4 * (L + 1) * 256 * 2 + 2 * 4 * 256 * 2 + (16 * 512 + 2 * 4 * 256) * 4 + 16 * 256 * 4
+
+
+def _graph_time(ctx, fn, reps):
+    """fn captured once in a CUDA graph on a side stream, replayed reps times between two events."""
+    import torch
+
+    side = torch.cuda.Stream()
+    fn()  # warm-up (grows any workspace outside the capture)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    ctx.set_stream(side)
+    try:
+        with torch.cuda.graph(g, stream=side):
+            fn()
+    finally:
+        ctx.set_stream(torch.cuda.current_stream())
+    for _ in range(3):
+        g.replay()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / reps
+
+
+def bench_config0(ctx, reps, cpu=True):
+    """Workload 0: one DeltaNet layer, batch 1, 256 sequential tokens from a
+    zero state.  Timed two ways: qm_dn_decode_seq (the 256 tokens in one
+    launch, the 2 MiB state in registers throughout) and 256 qm_dn_decode
+    calls (one per token, as a decode loop issues them) captured in a CUDA
+    graph.  The algorithmic bytes are the per-token traffic of the reference
+    algorithm with the state in memory (state read + write, conv history,
+    inputs, output): with the state on chip, the GB/s figure is effective."""
+    import numpy as np
+    import torch
+
+    import qora_mixer as qm
+    from qora_mixer import inputs as I
+
+    T = 256
+    g = I.rng(0)
+    p = I.dn_layer_params(g)
+    toks = I.dn_token_inputs(g, T, 1)
+    keep = [torch.from_numpy(p[k]).cuda() for k in ("conv_w", "a_log", "dt_bias", "norm_gamma")]
+    prm = qm.dn_params(*keep)
+    qkv, a, b = (torch.from_numpy(np.ascontiguousarray(toks[k])).cuda() for k in ("qkv", "a", "b"))
+    st = qm.DnState(ctx, 1)
+    y = torch.empty(1, T, 32, 128, device="cuda")
+    yd = torch.empty(1, 32, 128, device="cuda")
+    mx = qm.Mixer(ctx)
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        st.reset()
+        mx.dn_decode_seq(prm, st, T, qkv, a, b, y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    tot = 0.0
+    for _ in range(reps):
+        st.reset()
+        e0.record(stream)
+        mx.dn_decode_seq(prm, st, T, qkv, a, b, y)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        tot += e0.elapsed_time(e1)
+    seq_ms = tot / reps
+    tok_views = [(qkv[:, t], a[:, t], b[:, t]) for t in range(T)]
+
+    def per_token():
+        for q_t, a_t, b_t in tok_views:
+            mx.dn_decode(prm, st, q_t, a_t, b_t, yd)
+
+    st.reset()
+    loop_ms = _graph_time(ctx, per_token, max(2, reps // 2))
+    st.close()
+    peak, peak_kind = load_peaks()
+    alg = CFG0_BYTES_TOKEN * T
+    ach = alg / (seq_ms / 1e3) / 1e9
+    ach_loop = alg / (loop_ms / 1e3) / 1e9
+    rec = {"workload": "DeltaNet layer decode, batch 1, 256 sequential tokens (workload 0)",
+           "value": round(T / (seq_ms / 1e3), 1), "unit": "tok/s", "ms_per_256_tokens": round(seq_ms, 4),
+           "path": "qm_dn_decode_seq: one launch, state on chip",
+           "per_token_calls": {"path": "256 qm_dn_decode launches in a CUDA graph",
+                               "value": round(T / (loop_ms / 1e3), 1), "unit": "tok/s",
+                               "ms_per_256_tokens": round(loop_ms, 4),
+                               "effective_gbs": round(ach_loop, 1), "frac": round(ach_loop / peak, 4)},
+           "roofline": {"bound": "hbm (effective: the state stays on chip)", "kernel": "dn_decode_seq_kernel",
+                        "achieved": round(ach, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                        "frac": round(ach / peak, 4), "algorithmic_bytes_per_token": CFG0_BYTES_TOKEN}}
+    if cpu:
+        from oracle import oracle as orc
+
+        c = orc.cfg_4b()
+        ost = orc.DnState(c)
+        avx = orc.has_avx512()
+        t0 = time.perf_counter()
+        for t in range(T):
+            orc.dn_decode(c, ost, toks["qkv"][0, t], toks["a"][0, t], toks["b"][0, t], p["conv_w"],
+                          p["a_log"], p["dt_bias"], use_avx512=avx)
+        dt = time.perf_counter() - t0
+        rec["cpu_baseline"] = {"value": round(T / dt, 2), "unit": "tok/s", "cores": 1, "kind": "port",
+                               "sample": "the same 256 tokens through the CPU restatement, heads serial "
+                                         "(gemv.rs:817) with the AVX-512 head update (simd.rs:292-362)"
+                                         if avx else "the same 256 tokens, scalar head update (gemv.rs:836-861)"}
+    return rec
+
+
+def bench_config1(ctx, reps, cpu=True, ncache=24):
+    """Workload 1: one GQA layer decode, batch 1, 4096 cached bf16 positions,
+    new token at 4096.  One 16.8 MB cache fits in L2, so the timed calls
+    rotate over `ncache` distinct caches (403 MB at 24): each call reads its
+    K/V from HBM.  The calls, one per cache, are captured in a CUDA graph and
+    replayed; every call appends at position 4096 of its cache."""
+    import torch
+
+    import qora_mixer as qm
+    from qora_mixer import inputs as I
+
+    L, cap = CFG1_L, CFG1_L + 8
+    g = I.rng(1)
+    pr = I.gqa_layer_params(g, cap + 1)
+    cos, sin = qm.rope_table(1.0e7, 64, cap + 1)
+    keep = [torch.from_numpy(pr["q_norm"]).cuda(), torch.from_numpy(pr["k_norm"]).cuda(),
+            torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()]
+    prm = qm.gqa_params(*keep)
+    caches = []
+    for i in range(ncache):
+        K = I.device_normal_bf16((1, 4, cap, 256), 0x51A1 * 100 + 2 * i).view(torch.int16)
+        V = I.device_normal_bf16((1, 4, cap, 256), 0x51A1 * 100 + 2 * i + 1).view(torch.int16)
+        kv = qm.KvCache(ctx, 1, cap, K, V)
+        kv.seq_len = L
+        caches.append((kv, K, V))
+    tok = I.gqa_token_inputs(g, 1)
+    ins = [torch.from_numpy(tok[k]).cuda() for k in ("q_gate", "k_new", "v_new")]
+    out = torch.empty(1, 16, 256, device="cuda")
+    mx = qm.Mixer(ctx)
+
+    def calls():
+        for kv, _, _ in caches:
+            kv.seq_len = L
+            mx.gqa_decode(prm, kv, *ins, out)
+
+    n0 = ctx.launch_count()
+    calls()
+    launches = (ctx.launch_count() - n0) // ncache
+    ms = _graph_time(ctx, calls, max(10, reps * 5)) / ncache
+    for kv, _, _ in caches:
+        kv.close()
+    del caches
+    torch.cuda.empty_cache()
+    peak, peak_kind = load_peaks()
+    alg = cfg1_bytes(L)
+    ach = alg / (ms / 1e3) / 1e9
+    rec = {"workload": "GQA layer decode, batch 1, 4096 cached positions (workload 1)",
+           "value": round(1 / (ms / 1e3), 1), "unit": "tok/s", "us_per_call": round(ms * 1e3, 3),
+           "launches_per_call": launches,
+           "l2": f"{ncache} distinct caches rotated ({ncache * alg / 1e6:.0f} MB > L2)",
+           "timing": "one call per cache captured in a CUDA graph, replayed; CUDA events",
+           "roofline": {"bound": "hbm", "kernel": "gqa_prep + gqa_attn + gqa_combine (whole call)",
+                        "achieved": round(ach, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                        "frac": round(ach / peak, 4), "algorithmic_bytes_per_call": alg}}
+    if cpu:
+        import numpy as np
+
+        from oracle import oracle as orc
+
+        c = orc.cfg_4b()
+        kb = I.f32_to_bf16_bits(g.standard_normal((L, 4 * 256), dtype=np.float32))
+        vb = I.f32_to_bf16_bits(g.standard_normal((L, 4 * 256), dtype=np.float32))
+        okv = orc.KvCache(c, cap + 1, I.bf16_bits_to_f32(kb), I.bf16_bits_to_f32(vb))
+        orc.set_num_threads(host_threads())
+        n = 20
+        t0 = time.perf_counter()
+        for _ in range(n):
+            okv.seq_len[0] = L
+            orc.gqa_decode(c, okv, tok["q_gate"][0], tok["k_new"][0], tok["v_new"][0], pr["q_norm"],
+                           pr["k_norm"], cos, sin)
+        dt = (time.perf_counter() - t0) / n
+        rec["cpu_baseline"] = {"value": round(1 / dt, 2), "unit": "tok/s",
+                               "cores": min(16, orc.num_threads()), "kind": "port",
+                               "sample": f"{n} calls of the CPU restatement at L=4096, the 16 heads on an "
+                                         "OpenMP pool as rayon runs them (gemv.rs:963)"}
+    return rec
+
+
+# ----------------------------------------------------------------------------
 # CPU restatement on a bounded sample (reference arm and cpu_baseline)
 # ----------------------------------------------------------------------------
 class CpuStack:
@@ -1045,6 +1248,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer (e2e) pass")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill measurements")
     ap.add_argument("--prefill-reps", type=int, default=3)
+    ap.add_argument("--no-small", action="store_true", help="skip the workload 0 / 1 records")
+    ap.add_argument("--small-only", action="store_true",
+                    help="time workloads 0 and 1 alone (batch-1 single-layer decode); prints their records")
     ap.add_argument("--head-sharded", action="store_true",
                     help="also time the head-sharded variant at N=1 (always on for N>1)")
     ap.add_argument("--no-head-sharded", action="store_true")
@@ -1096,6 +1302,18 @@ def main():
         torch.cuda.set_device(0)
         ctx = qm.Ctx(0, stream=torch.cuda.current_stream())
         print(json.dumps(bench_gemv(ctx, args.steps, args.gemv_batch, args.gemv_only)), flush=True)
+        ctx.close()
+        return
+    if args.small_only:
+        import torch
+
+        import qora_mixer as qm
+
+        torch.cuda.set_device(0)
+        ctx = qm.Ctx(0, stream=torch.cuda.current_stream())
+        rec = {"decode_config0": bench_config0(ctx, args.steps, cpu=not args.no_cpu_baseline),
+               "decode_config1": bench_config1(ctx, args.steps, cpu=not args.no_cpu_baseline)}
+        print(json.dumps(rec), flush=True)
         ctx.close()
         return
     if args.prefill_only:

@@ -190,6 +190,24 @@ int qm_dn_decode_host(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, const
                       const float* a, const float* b, float* y, const float* z, float* out);
 
 /*
+ * T sequential DeltaNet decode steps per sequence in one launch: the same
+ * result as T qm_dn_decode calls, with the f32 state kept on chip for the
+ * whole call (one read and one write of S instead of one per token).
+ * Replaces the per-token loop of prefill_deltanet_layer
+ * (src/gemv.rs:1129-1203) and T successive mixer regions of
+ * forward_deltanet_decode (src/gemv.rs:744-883) when the inputs are known
+ * ahead (a prompt, a draft to verify).  f32 arithmetic throughout, so the
+ * decode tolerance applies, unlike the tensor-core qm_dn_prefill.
+ *   qkv [B,T,8192] f32 (16-byte aligned), a,b [B,T,32] f32,
+ *   y [B,T,nvh,128] f32 or NULL when out is given,
+ *   z [B,T,4096] f32 or NULL; when given, out [B,T,nvh,128] receives
+ *   RMSNorm(y)*gamma*SiLU(z) per token.
+ * Works on head-sharded states like qm_dn_decode.
+ */
+int qm_dn_decode_seq(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, int T, const float* qkv,
+                     const float* a, const float* b, float* y, const float* z, float* out);
+
+/*
  * DeltaNet prefill of T tokens per sequence (chunked WY form on the tensor
  * cores).  Replaces the sequential loop src/gemv.rs:1119-1219 of
  * prefill_deltanet_layer (1086) and the CPU recurrence that

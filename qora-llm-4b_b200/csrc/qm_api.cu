@@ -673,6 +673,22 @@ extern "C" int qm_dn_decode(qm_ctx* c, const qm_dn_params* p, qm_dn_state* st, c
     return QM_OK;
 }
 
+// T sequential decode steps in one launch, the state kept on chip (dn_decode_seq.cu).
+extern "C" int qm_dn_decode_seq(qm_ctx* c, const qm_dn_params* p, qm_dn_state* st, int T,
+                                const float* qkv, const float* a, const float* b, float* y,
+                                const float* z, float* out) {
+    int rc = check_dn_decode(c, p, st, qkv, a, b, y, z, out);
+    if (rc) return rc;
+    if (T <= 0) return set_error(c, QM_E_ARG, "qm_dn_decode_seq: T <= 0");
+    if (((uintptr_t)qkv & 15) || (z && ((uintptr_t)z & 15)))
+        return set_error(c, QM_E_ARG, "qm_dn_decode_seq: qkv and z must be 16-byte aligned");
+    cudaSetDevice(c->device);
+    cudaError_t e = launch_dn_decode_seq(c, p, st, T, qkv, a, b, y, z, out);
+    if (e != cudaSuccess) return cuda_error(c, e, "dn_decode_seq launch");
+    st->conv_pos += T;
+    return QM_OK;
+}
+
 extern "C" int qm_dn_decode_host(qm_ctx* c, const qm_dn_params* p, qm_dn_state* st,
                                  const float* qkv, const float* a, const float* b, float* y,
                                  const float* z, float* out) {

@@ -124,6 +124,10 @@ struct TimedLaunch {
 cudaError_t launch_dn_decode(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, const float* qkv,
                              const float* a, const float* b, float* y, const float* z, float* out,
                              int b0 = 0, int nb = -1, bool pair = false);
+// T tokens per sequence in order, the state in registers for the whole call
+cudaError_t launch_dn_decode_seq(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, int T,
+                                 const float* qkv, const float* a, const float* b, float* y,
+                                 const float* z, float* out);
 // GqaCombineSrc: where the combine kernel reads the gate half of q_gate and
 // v_new (default: the call's own q_gate / v_new), after waiting for `ready`
 // on the launch stream when it is set.

@@ -41,7 +41,7 @@ EXPORTS = [
     "qm_rope_table", "qm_dn_state_create", "qm_dn_state_wrap", "qm_dn_state_destroy",
     "qm_dn_state_reset", "qm_dn_state_snapshot", "qm_dn_state_restore", "qm_dn_state_read",
     "qm_dn_state_write", "qm_dn_state_conv_pos", "qm_dn_state_set_conv_pos",
-    "qm_dn_state_batch", "qm_dn_state_data", "qm_dn_decode", "qm_dn_decode_host",
+    "qm_dn_state_batch", "qm_dn_state_data", "qm_dn_decode", "qm_dn_decode_host", "qm_dn_decode_seq",
     "qm_dn_prefill", "qm_kv_create", "qm_kv_wrap", "qm_kv_destroy", "qm_kv_snapshot",
     "qm_kv_restore", "qm_kv_seq_len", "qm_kv_set_seq_len", "qm_kv_capacity", "qm_kv_batch",
     "qm_kv_data", "qm_gqa_decode", "qm_gqa_decode_host", "qm_gqa_prefill",
@@ -138,6 +138,7 @@ def lib():
         "qm_dn_decode": ([P, C.POINTER(QmDnParams), P, P, P, P, P, P, P], I),
         "qm_dn_decode_host": ([P, C.POINTER(QmDnParams), P, P, P, P, P, P, P], I),
         "qm_dn_prefill": ([P, C.POINTER(QmDnParams), P, I, P, P, P, P, P, P], I),
+        "qm_dn_decode_seq": ([P, C.POINTER(QmDnParams), P, I, P, P, P, P, P, P], I),
         "qm_kv_create": ([P, I, I, PP], I),
         "qm_kv_wrap": ([P, I, I, P, P, PP], I),
         "qm_kv_destroy": ([P], I),
@@ -520,6 +521,12 @@ class Mixer:
         rc = lib().qm_dn_decode_host(self.ctx.handle, C.byref(p), st.handle, _ptr(qkv), _ptr(a),
                                      _ptr(b), _ptr(y), _ptr(z), _ptr(out))
         self.ctx.check(rc, "qm_dn_decode_host")
+
+    def dn_decode_seq(self, p: QmDnParams, st: DnState, T, qkv, a, b, y=None, z=None, out=None):
+        """T decode steps per sequence in one launch (qkv [B,T,8192] f32)."""
+        rc = lib().qm_dn_decode_seq(self.ctx.handle, C.byref(p), st.handle, int(T), _ptr(qkv),
+                                    _ptr(a), _ptr(b), _ptr(y), _ptr(z), _ptr(out))
+        self.ctx.check(rc, "qm_dn_decode_seq")
 
     def dn_prefill(self, p: QmDnParams, st: DnState, T, qkv_bf16, a, b, y=None, z=None, out=None):
         rc = lib().qm_dn_prefill(self.ctx.handle, C.byref(p), st.handle, int(T), _ptr(qkv_bf16),

@@ -221,6 +221,19 @@ extern "C" {
         z: *const f32,
         out: *mut f32,
     ) -> c_int;
+    /// T sequential decode steps in one launch (src/gemv.rs:1129-1203), f32, state on chip.
+    pub fn qm_dn_decode_seq(
+        ctx: *mut qm_ctx,
+        p: *const qm_dn_params,
+        st: *mut qm_dn_state,
+        t: c_int,
+        qkv: *const f32,
+        a: *const f32,
+        b: *const f32,
+        y: *mut f32,
+        z: *const f32,
+        out: *mut f32,
+    ) -> c_int;
     /// src/gemv.rs:1119-1219 (prefill, chunked on the tensor cores).
     pub fn qm_dn_prefill(
         ctx: *mut qm_ctx,
