@@ -85,6 +85,10 @@ gqa_prep_kernel(const float* __restrict__ q_gate, const float* __restrict__ k_ne
                 const float* __restrict__ rope_sin, int64_t pos, uint16_t* __restrict__ kcache,
                 uint16_t* __restrict__ vcache, int cap, uint16_t* __restrict__ q_bf,
                 float* __restrict__ q_f32, float* __restrict__ kn_out, int kv_lo, int nkv, int b0) {
+    // the attention kernel may start now: its K/V loads read only positions the
+    // preceding calls have finished writing, and it waits before reading q
+    pdl_launch_dependents();
+    pdl_wait();  // the inputs may come from the preceding kernel
     // gl: KV head within the cache's range; g, h: model KV / query head (inputs)
     const int b = b0 + blockIdx.x / nkv, gl = blockIdx.x % nkv, g = kv_lo + gl;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -168,6 +172,7 @@ gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__
     const int ntiles = min(tps, ntiles_all - tile0);
     const int pos_end = min(L, (tile0 + ntiles) * kTile);
 
+    pdl_launch_dependents();  // the combine kernel waits for this grid's completion
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
             mbar_init(smem_u32(&full[s]), 1);
@@ -181,6 +186,11 @@ gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__
     const uint32_t sbase = smem_u32(smem);
     if (warp == kGroup) {
         // ---------------- producer ----------------
+        // Positions [0, L) of the cache are not written by the prep kernel of
+        // this call (it appends at L), and the preceding call's kernels have
+        // completed: the combine kernel never lets its successor start early,
+        // and it waited for everything before it.  So the loads start at once,
+        // before the prep kernel is done.
         if (lane == 0) {
             prefetch_tmap(&tmk);
             prefetch_tmap(&tmv);
@@ -212,6 +222,7 @@ gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__
     const int row = lane >> 2;          // A/C row: head (row & 3), hi/lo (row >> 2)
     const int quad = lane & 3;
     uint32_t qa[16][2];
+    pdl_wait();  // q comes from the prep kernel (the producer's K/V loads did not wait)
     {
         const int head = row & 3, hl = row >> 2;
         const uint16_t* qr = q_bf + ((((size_t)b * nkv + g) * kGroup + head) * 2 + hl) * kD;
@@ -385,58 +396,104 @@ gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__
 
 // ---------------------------------------------------------------------------
 // 3. combine splits + the new token (f32) + sigmoid gate (gemv.rs:1008-1011)
+// One CTA per (sequence, query head): warp w merges splits w, w + 8, ... with
+// lane l holding dims [8l, 8l + 8), all of a warp's loads in flight at once;
+// then thread d merges the 8 warps' partials and the new token for dim d.
 // ---------------------------------------------------------------------------
+constexpr int kCombWarps = 8;
+constexpr int kCombUnroll = 4;  // splits a warp loads at once
+
 __global__ void __launch_bounds__(256)
 gqa_combine_kernel(const float* __restrict__ q_f32, const float* __restrict__ kn,
                    const float* __restrict__ v_new, const float* __restrict__ q_gate,
                    const float* __restrict__ part_o, const float* __restrict__ part_ml, int nsplit,
                    float* __restrict__ out, int kv_lo, int nkv, int b0) {
+    // Waits for the attention grid (and, through it, the prep grid).  It never
+    // lets its successor start early: the next call's attention kernel loads
+    // the cache without waiting, which is safe only once this call is done.
+    pdl_wait();
     const int bh = b0 * nkv * kGroup + blockIdx.x;  // (sequence, query head) row of the cache's heads
     const int nh = nkv * kGroup;
     const int b = bh / nh, hl = bh % nh, gl = hl / kGroup;
     const int h = kv_lo * kGroup + hl, g = kv_lo + gl;  // model heads (inputs)
     const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
-    __shared__ float s_red[8];
-    __shared__ float s_ml[2 * 512];
+    __shared__ float s_red[kCombWarps];
+    __shared__ __align__(16) float s_o[kCombWarps][kD];
+    __shared__ float s_m[kCombWarps], s_l[kCombWarps];
+
+    // the new token's score q . k_new (f32, never rounded for this step)
     float prod = q_f32[(size_t)bh * kD + d] * kn[((size_t)b * nkv + gl) * kD + d];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) prod += __shfl_xor_sync(0xffffffffu, prod, o);
     if (lane == 0) s_red[warp] = prod;
-    for (int i = d; i < 2 * nsplit && i < 1024; i += 256) s_ml[i] = part_ml[(size_t)bh * nsplit * 2 + i];
+
+    // this warp's splits, online over groups of kCombUnroll
+    const float* ml = part_ml + (size_t)bh * nsplit * 2;
+    const float* po = part_o + (size_t)bh * nsplit * kD + 8 * lane;
+    float M = -INFINITY, lw = 0.f;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] = 0.f;
+    for (int i0 = warp; i0 < nsplit; i0 += kCombWarps * kCombUnroll) {
+        float mi[kCombUnroll], li[kCombUnroll];
+        float4 oa[kCombUnroll], ob[kCombUnroll];
+#pragma unroll
+        for (int u = 0; u < kCombUnroll; u++) {
+            const int i = i0 + u * kCombWarps;
+            if (i < nsplit) {
+                mi[u] = ml[2 * i];
+                li[u] = ml[2 * i + 1];
+                oa[u] = reinterpret_cast<const float4*>(po + (size_t)i * kD)[0];
+                ob[u] = reinterpret_cast<const float4*>(po + (size_t)i * kD)[1];
+            } else {
+                mi[u] = -INFINITY;
+                li[u] = 0.f;
+                oa[u] = ob[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        float Mn = M;
+#pragma unroll
+        for (int u = 0; u < kCombUnroll; u++) Mn = fmaxf(Mn, mi[u]);
+        if (Mn == -INFINITY) continue;  // nothing attended yet (empty splits)
+        const float c = exp2f((M - Mn) * kLog2e);  // 0 while M is -inf
+        lw *= c;
+#pragma unroll
+        for (int i = 0; i < 8; i++) acc[i] *= c;
+#pragma unroll
+        for (int u = 0; u < kCombUnroll; u++) {
+            if (mi[u] == -INFINITY) continue;
+            const float w = exp2f((mi[u] - Mn) * kLog2e);
+            lw += w * li[u];
+            acc[0] += w * oa[u].x; acc[1] += w * oa[u].y; acc[2] += w * oa[u].z; acc[3] += w * oa[u].w;
+            acc[4] += w * ob[u].x; acc[5] += w * ob[u].y; acc[6] += w * ob[u].z; acc[7] += w * ob[u].w;
+        }
+        M = Mn;
+    }
+    reinterpret_cast<float4*>(&s_o[warp][8 * lane])[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    reinterpret_cast<float4*>(&s_o[warp][8 * lane])[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    if (lane == 0) {
+        s_m[warp] = M;
+        s_l[warp] = lw;
+    }
     __syncthreads();
     float s_new = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; w++) s_new += s_red[w];
-    float M = s_new;
-    for (int i = 0; i < nsplit; i++) {
-        const float mi = (i < 512) ? s_ml[2 * i] : part_ml[((size_t)bh * nsplit + i) * 2];
-        M = fmaxf(M, mi);
-    }
-    const float wn = exp2f((s_new - M) * kLog2e);
-    float acc = wn * v_new[((size_t)b * kNumKVH + g) * kD + d];
+    for (int w = 0; w < kCombWarps; w++) s_new += s_red[w];
+    float Mall = s_new;
+#pragma unroll
+    for (int w = 0; w < kCombWarps; w++) Mall = fmaxf(Mall, s_m[w]);
+    const float wn = exp2f((s_new - Mall) * kLog2e);
+    float o = wn * v_new[((size_t)b * kNumKVH + g) * kD + d];
     float lsum = wn;
-    auto add_split = [&](int i, float o) {
-        const float mi = (i < 512) ? s_ml[2 * i] : part_ml[((size_t)bh * nsplit + i) * 2];
-        const float li = (i < 512) ? s_ml[2 * i + 1] : part_ml[((size_t)bh * nsplit + i) * 2 + 1];
-        if (mi == -INFINITY) return;
-        const float w = exp2f((mi - M) * kLog2e);
-        acc += w * o;
-        lsum += w * li;
-    };
-    // the partials' loads, 8 splits at a time, are all in flight before the
-    // first is used (one split per iteration left each load's latency exposed)
-    const float* po = part_o + (size_t)bh * nsplit * kD + d;
-    int i = 0;
-    for (; i + 8 <= nsplit; i += 8) {
-        float pv[8];
 #pragma unroll
-        for (int u = 0; u < 8; u++) pv[u] = po[(size_t)(i + u) * kD];
-#pragma unroll
-        for (int u = 0; u < 8; u++) add_split(i + u, pv[u]);
+    for (int w = 0; w < kCombWarps; w++) {
+        if (s_m[w] == -INFINITY) continue;
+        const float f = exp2f((s_m[w] - Mall) * kLog2e);
+        o += f * s_o[w][d];
+        lsum += f * s_l[w];
     }
-    for (; i < nsplit; i++) add_split(i, po[(size_t)i * kD]);
     const float gate = q_gate[((size_t)b * kNumH + h) * 2 * kD + kD + d];
-    out[(size_t)bh * kD + d] = (acc / lsum) * (1.0f / (1.0f + __expf(-gate)));
+    out[(size_t)bh * kD + d] = (o / lsum) * (1.0f / (1.0f + __expf(-gate)));
 }
 
 }  // namespace
@@ -466,25 +523,41 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
     float* part_ml = reinterpret_cast<float*>(base + w.part_ml);
     cudaStream_t st = ctx->stream;
 
+    // All three kernels are launched with programmatic stream serialization
+    // (each may start while its predecessor runs; see the kernels' waits).
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    auto cfg_for = [&](dim3 grid, int threads, size_t smem) {
+        cudaLaunchConfig_t c = {};
+        c.gridDim = grid;
+        c.blockDim = dim3(threads);
+        c.dynamicSmemBytes = smem;
+        c.stream = st;
+        c.attrs = pdl;
+        c.numAttrs = 1;
+        return c;
+    };
+    cudaError_t e;
     {
         TimedLaunch tl(ctx, "gqa_prep");
-        gqa_prep_kernel<<<B * nkv, 160, 0, st>>>(q_gate, k_new, v_new, prm->q_norm, prm->k_norm,
-                                                 prm->rope_cos, prm->rope_sin, L, kv->k, kv->v,
-                                                 kv->capacity, q_bf, q_f32, kn, kv->kv_lo, nkv, b0);
+        const cudaLaunchConfig_t c = cfg_for(dim3(B * nkv), 160, 0);
+        e = cudaLaunchKernelEx(&c, gqa_prep_kernel, q_gate, k_new, v_new, prm->q_norm, prm->k_norm,
+                               prm->rope_cos, prm->rope_sin, L, kv->k, kv->v, kv->capacity, q_bf, q_f32,
+                               kn, kv->kv_lo, nkv, b0);
     }
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     ctx->launches += 1;
     if (pl.nsplit > 0) {
         static std::atomic<uint64_t> attr_set{0};
         e = set_smem_once(attr_set, ctx->device, gqa_attn_kernel, kAttnSmem);
         if (e != cudaSuccess) return e;
-        dim3 grid(pl.nsplit, nkv, B);
         TimedLaunch tl(ctx, "gqa_attn");
-        gqa_attn_kernel<<<grid, 160, kAttnSmem, st>>>(kv->tmap_k, kv->tmap_v, q_bf, part_o,
-                                                      part_ml, (int)L, pl.tps, pl.nsplit, nkv, b0,
-                                                      ctx->d_err);
-        e = cudaGetLastError();
+        const cudaLaunchConfig_t c = cfg_for(dim3(pl.nsplit, nkv, B), 160, kAttnSmem);
+        e = cudaLaunchKernelEx(&c, gqa_attn_kernel, kv->tmap_k, kv->tmap_v, (const uint16_t*)q_bf, part_o,
+                               part_ml, (int)L, pl.tps, pl.nsplit, nkv, b0, ctx->d_err);
+        if (e == cudaSuccess) e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         ctx->launches += 1;
     }
@@ -500,10 +573,12 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
     }
     {
         TimedLaunch tl(ctx, "gqa_combine");
-        gqa_combine_kernel<<<B * nkv * kGroup, 256, 0, st>>>(q_f32, kn, c_v, c_gate, part_o,
-                                                             part_ml, pl.nsplit, out, kv->kv_lo, nkv, b0);
+        const cudaLaunchConfig_t c = cfg_for(dim3(B * nkv * kGroup), 256, 0);
+        e = cudaLaunchKernelEx(&c, gqa_combine_kernel, (const float*)q_f32, (const float*)kn, c_v, c_gate,
+                               (const float*)part_o, (const float*)part_ml, pl.nsplit, out, kv->kv_lo,
+                               nkv, b0);
     }
-    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e == cudaSuccess) ctx->launches += 1;
     return e;
 }

@@ -90,9 +90,6 @@ struct GvArgs {
     int* count;      // [tiles], zero between launches
 };
 
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
 template <bool Q4, int BT>
 __global__ void __launch_bounds__(kGvThreads, BT <= 2 ? 2 : 1)
 qm_gemv_kernel(const __grid_constant__ GvArgs a) {

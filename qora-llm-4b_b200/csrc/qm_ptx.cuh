@@ -99,6 +99,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with the
+// programmatic-stream-serialization attribute may start while the preceding
+// kernel of the stream runs.  launch_dependents lets the next such kernel
+// start (once every CTA of this grid has issued it or exited); wait blocks
+// the calling thread until the preceding grid has completed and its memory
+// is visible.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
