@@ -521,6 +521,7 @@ def run_ours(args):
         line["decode_config1"] = bench_config1(ctx, args.prefill_reps * 3, cpu=cpu)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(args.cpu_tokens)
+        line["cpu_baseline"]["batch_parallel"] = cpu_sample_batch(args.cpu_tokens)
     if rank == 0:
         print(json.dumps(line), flush=True)
     ctx.close()
@@ -1141,6 +1142,17 @@ class CpuStack:
             self.att.append((pr, tok))
         self.avx = orc.has_avx512()
 
+    def clone(self):
+        """An independent copy (own states and cache) for another sequence."""
+        import copy
+
+        o = copy.copy(self)
+        o.dn = [(p, st.copy(), tok) for (p, st, tok) in self.dn]
+        kv = self.orc.KvCache.__new__(self.orc.KvCache)
+        kv.k, kv.v, kv.seq_len = self.kv.k.copy(), self.kv.v.copy(), self.kv.seq_len.copy()
+        o.kv = kv
+        return o
+
     def token(self):
         """One decode token through all 32 layers (3 DeltaNet + 1 GQA, x8)."""
         orc = self.orc
@@ -1184,6 +1196,37 @@ def cpu_sample(ntok):
             "sample": (f"{ntok} decode tokens of one sequence through all 32 mixer layers at context "
                        f"{CTX}; GQA heads on an OpenMP pool (rayon over 16 heads, gemv.rs:963), "
                        "DeltaNet heads serial with the AVX-512 update (gemv.rs:817, simd.rs:292)"),
+            "cpu": cpu_model()}
+
+
+def cpu_sample_batch(ntok, nseq=None):
+    """Independent sequences across the host cores, one per core, each run as
+    the reference runs a sequence but with its own OpenMP team of one: the
+    throughput a CPU host gets by batching sequences the way the GPU does."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as orc
+
+    cores = host_threads()
+    nseq = nseq or min(16, cores)
+    orc.set_num_threads(1)
+    base = CpuStack(ntok + 1)
+    stacks = [base] + [base.clone() for _ in range(nseq - 1)]
+
+    def run(cs, n=ntok):
+        for _ in range(n):
+            cs.token()
+
+    with ThreadPoolExecutor(max_workers=nseq) as ex:
+        list(ex.map(lambda cs: run(cs, 1), stacks))  # warm
+        t0 = time.perf_counter()
+        list(ex.map(run, stacks))
+        dt = time.perf_counter() - t0
+    orc.set_num_threads(cores)
+    return {"value": round(nseq * ntok / dt, 4), "unit": UNIT, "cores": nseq, "kind": "port",
+            "sample": (f"{nseq} independent sequences in parallel, one per core, {ntok} decode tokens each "
+                       f"through all 32 mixer layers at context {CTX}; per sequence the reference's "
+                       "arithmetic (DeltaNet heads serial with the AVX-512 update, GQA heads serial)"),
             "cpu": cpu_model()}
 
 

@@ -69,6 +69,15 @@ typedef struct qm_shape {
     float rms_eps;       /* 1e-6 */
 } qm_shape;
 
+/* How the library was built (no reference counterpart): a bit set of
+ * QM_BUILD_* flags.  QM_BUILD_BOUNDS_CHECKS: the checked build
+ * (libqora_mixer_checked.so, -DQM_CHECK_BOUNDS), whose prefill and GEMM
+ * kernels compare their computed buffer offsets with the buffers' extents
+ * and, instead of an out-of-range access, skip it and set the error word
+ * (qm_sync then returns QM_E_RANGE). */
+#define QM_BUILD_BOUNDS_CHECKS 1
+int qm_build_flags(void);
+
 /* Replaces Qor4bConfig::default_4b (src/config.rs:42-79) for the mixer fields. */
 int qm_shape_get(qm_shape* out);
 const char* qm_status_string(int status);
@@ -223,6 +232,16 @@ int qm_dn_decode_seq(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, int T,
 int qm_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, int T, const uint16_t* qkv,
                   const float* a, const float* b, float* y, const float* z, float* out);
 
+/* Host-buffer variant of qm_dn_prefill (params stay device pointers):
+ * qkv, a, b, y, z, out are host memory (pinned or pageable).  The inputs
+ * are copied into the context's staging buffer, the prefill runs, and y
+ * (and out) are copied back before the call returns — the reference's GPU
+ * prefill flow, which moves each layer's activations down and up around its
+ * recurrence (src/gpu_inference.rs:464-476, 591-604). */
+int qm_dn_prefill_host(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* st, int T,
+                       const uint16_t* qkv, const float* a, const float* b, float* y, const float* z,
+                       float* out);
+
 /* Head-sharded state (multi-GPU, see qm_shard_plan): V heads
  * [vh_lo, vh_lo + nvh) of every sequence, S [B,nvh,128,128]; vh_lo and nvh
  * even (V heads 2j and 2j+1 share QK head j, gemv.rs:803-809, whose conv
@@ -300,6 +319,13 @@ int qm_gqa_decode_host(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, const flo
  */
 int qm_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, int T, const uint16_t* q_gate,
                    const uint16_t* k, const uint16_t* v, float* out);
+
+/* Host-buffer variant of qm_gqa_prefill: q_gate, k, v, out in host memory
+ * (the reference's prefill_attn_layer_gpu uploads its activations and reads
+ * the output back, src/gpu_inference.rs:690-766); returns after out is in
+ * host memory. */
+int qm_gqa_prefill_host(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, int T, const uint16_t* q_gate,
+                        const uint16_t* k, const uint16_t* v, float* out);
 
 /* ------------------------------------------------------------------ */
 /* GQA decode without any device allocation                             */

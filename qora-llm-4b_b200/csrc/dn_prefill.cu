@@ -75,7 +75,7 @@ dn_prefill_prep(const uint16_t* __restrict__ qkv, const float* __restrict__ a_in
                 const float* __restrict__ ring, int64_t conv_pos, int T, int nruns,
                 uint16_t* __restrict__ qh, uint16_t* __restrict__ ql, uint16_t* __restrict__ kh,
                 uint16_t* __restrict__ kl, uint16_t* __restrict__ vh, uint16_t* __restrict__ vl,
-                float* __restrict__ gout, float* __restrict__ bout, int B) {
+                float* __restrict__ gout, float* __restrict__ bout, int B, int* err) {
     const int lane = threadIdx.x & 31;
     const size_t gw = (size_t)blockIdx.x * kPrepWarps + (threadIdx.x >> 5);
     const int hv = (int)(gw % 64);  // adjacent warps read adjacent 256-byte slices of a token row
@@ -149,6 +149,7 @@ dn_prefill_prep(const uint16_t* __restrict__ qkv, const float* __restrict__ a_in
         const __half2 l01 = __floats2half2_rn(a[0] - f01.x, a[1] - f01.y);
         const __half2 l23 = __floats2half2_rn(a[2] - f23.x, a[3] - f23.y);
         const size_t o = (plane * T + t0 + i) * kHd + lane * 4;
+        if (!QM_IN(o, 4, (size_t)B * (is_qk ? kNumQK : kNumV) * T * kHd, err)) continue;
         *reinterpret_cast<uint2*>(ph + o) =
             make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
         *reinterpret_cast<uint2*>(pl + o) =
@@ -157,6 +158,7 @@ dn_prefill_prep(const uint16_t* __restrict__ qkv, const float* __restrict__ a_in
     if (!is_qk && lane < tend) {
         // gates of V head vhh for token t0 + lane (gemv.rs:1171-1172), as log-decay
         const int vhh = hv - 2 * kNumQK, t = t0 + lane;
+        if (!QM_IN(((size_t)b * kNumV + vhh) * T + t, 1, (size_t)B * kNumV * T, err)) return;
         const float x = a_in[((size_t)b * T + t) * kNumV + vhh] + dt_bias[vhh];
         const float sp = x > 20.0f ? x : log1pf(__expf(x));
         gout[((size_t)b * kNumV + vhh) * T + t] = -__expf(a_log[vhh]) * sp;
@@ -433,6 +435,7 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
             const int t = row;
             const float Gt = sG[t], bt = sB[t];
             float* arow = Amat + t * kAStride + s0;
+            if (QM_IN(t * kAStride + s0, 32, kC * kAStride, err))
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
                 const int s = s0 + i;
@@ -446,25 +449,28 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
         } else {
             const int t = row - kC;
             const float Gt = sG[t];
-            uint4* hrow = reinterpret_cast<uint4*>(ph_out + (item * kC + t) * kC + s0);
-            uint4* lrow = reinterpret_cast<uint4*>(pl_out + (item * kC + t) * kC + s0);
+            const size_t items = (size_t)gridDim.x * gridDim.y * gridDim.z;
+            if (QM_IN((item * kC + t) * kC + s0, 32, items * kC * kC, err)) {
+                uint4* hrow = reinterpret_cast<uint4*>(ph_out + (item * kC + t) * kC + s0);
+                uint4* lrow = reinterpret_cast<uint4*>(pl_out + (item * kC + t) * kC + s0);
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-                float p[8];
+                for (int i = 0; i < 32; i += 8) {
+                    float p[8];
 #pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    const int s = s0 + i + q;
-                    p[q] = (s <= t) ? ex2_approx(Gt - sG[s]) * kq[i + q] : 0.f;
+                    for (int q = 0; q < 8; q++) {
+                        const int s = s0 + i + q;
+                        p[q] = (s <= t) ? ex2_approx(Gt - sG[s]) * kq[i + q] : 0.f;
+                    }
+                    uint4 h, l;
+                    split8(p, h, l);
+                    hrow[i / 8] = h;
+                    lrow[i / 8] = l;
                 }
-                uint4 h, l;
-                split8(p, h, l);
-                hrow[i / 8] = h;
-                lrow[i / 8] = l;
             }
         }
     }
     // ---- Q~ = e^G q (fp16) and K~ = e^(G63-G) k (fp16 hi/lo), from the hi/lo tiles ----
-    if (ok) {
+    if (ok && QM_IN(item * kC * kHd, kC * kHd, (size_t)gridDim.x * gridDim.y * gridDim.z * kC * kHd, err)) {
         const size_t rowbase = item * kC;
 #pragma unroll 2
         for (int m = 0; m < 1024 / kLocalThreads; m++) {
@@ -600,7 +606,7 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
 
     // ---- outputs: W^T row k (fp16), U~^T row v (f32, [t/4][v][4]); this
     // thread's 32 tokens [32 half, 32 half + 32) ----
-    if (ok) {
+    if (ok && QM_IN(item * kHd * kC, kHd * kC, (size_t)gridDim.x * gridDim.y * gridDim.z * kHd * kC, err)) {
         float wv[32];
         tmem_ld32(tm + lane_addr + kTmW + half * 32, wv);
         tmem_ld_wait();
@@ -719,7 +725,8 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         tma_load_3d(sb + kS_W, &twt, 0, 0, (int)(item0 + c), fb);
         for (int hb = 0; hb < 2; hb++)
             tma_load_3d(sb + kS_Q + hb * 8192, &tqt, hb * 64, 0, (int)(item0 + c), fb);
-        bulk_load(sb + kS_Ut, ut_in + (item0 + c) * kHd * kC, 32768, fb);
+        if (QM_IN((item0 + c) * kHd * kC, kHd * kC, (size_t)gridDim.x * gridDim.y * nch * kHd * kC, err))
+            bulk_load(sb + kS_Ut, ut_in + (item0 + c) * kHd * kC, 32768, fb);
     };
     auto issue_k = [&](int c) {  // K~ hi/lo of chunk c
         const uint32_t fb = smem_u32(&bars->k_full);
@@ -747,7 +754,8 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
     float g_next = (tid < min(kC, T)) ? gin[plane_v * T + tid] : 0.f;  // gates of chunk 0
 
     // ---- initial state: global f32 -> TMEM master and fp16 copy ----
-    float* Sg = S + plane_v * kHd * kHd;
+    float* Sg = S + (QM_IN(plane_v * kHd * kHd, kHd * kHd, (size_t)gridDim.x * gridDim.y * kHd * kHd, err)
+                         ? plane_v * kHd * kHd : 0);
     {
         const float* srow = Sg + (size_t)row * kHd;
 #pragma unroll 1
@@ -781,6 +789,9 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         tmem_ld32(tm + lane_addr + kTmY + (c & 1) * 64 + 32, yv + 32);
         tmem_ld_wait();
         float* yb = y + ((size_t)b * T + t0) * kVDim + (size_t)vh * kHd + row;
+        if (!QM_IN(((size_t)b * T + t0 + tc - 1) * kVDim + (size_t)vh * kHd + row, 1,
+                   (size_t)gridDim.y * T * kVDim, err))
+            return;
 #pragma unroll
         for (int t = 0; t < kC; t++)
             if (t < tc) yb[(size_t)t * kVDim] = yv[t];
@@ -1058,7 +1069,7 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
         const size_t warps = (size_t)B * nruns * 64;
         dn_prefill_prep<<<(unsigned)((warps + kPrepWarps - 1) / kPrepWarps), 32 * kPrepWarps, 0, s>>>(
             qkv, a, bgate, p->conv_w, p->a_log, p->dt_bias, st->conv, st->conv_pos, T, nruns, qh, ql, kh,
-            kl, vh, vl, g, be, B);
+            kl, vh, vl, g, be, B, ctx->d_err);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;

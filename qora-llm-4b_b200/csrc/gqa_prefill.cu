@@ -128,7 +128,8 @@ gqa_prefill_prep(const uint16_t* __restrict__ q_gate, const uint16_t* __restrict
                  const float* __restrict__ k_norm, const float* __restrict__ rope_cos,
                  const float* __restrict__ rope_sin, int T, uint16_t* __restrict__ qw,
                  uint16_t* __restrict__ kw, uint16_t* __restrict__ vw,
-                 uint16_t* __restrict__ kcache, uint16_t* __restrict__ vcache, int cap) {
+                 uint16_t* __restrict__ kcache, uint16_t* __restrict__ vcache, int cap, int B,
+                 int* err) {
     const int g = blockIdx.x % kNumKVH;
     const int bt = blockIdx.x / kNumKVH;
     const int t = bt % T, b = bt / T;
@@ -158,12 +159,17 @@ gqa_prefill_prep(const uint16_t* __restrict__ q_gate, const uint16_t* __restrict
         x[1] = x2 * c + x1 * s;
     }
     if (is_q) {
-        uint16_t* dst = qw + (((size_t)b * kNumH + h) * T + t) * kD;
+        const size_t qrow = (((size_t)b * kNumH + h) * T + t) * kD;
+        if (!QM_IN(qrow, kD, (size_t)B * kNumH * T * kD, err)) return;
+        uint16_t* dst = qw + qrow;
 #pragma unroll
         for (int i = 0; i < 8; i++) dst[lane + 32 * i] = f16_bits_rn(x[i] * 0.0625f);
     } else {
         const size_t row = (((size_t)b * kNumKVH + g) * cap + t) * kD;
         const size_t wrow = (((size_t)b * kNumKVH + g) * T + t) * kD;
+        if (!QM_IN(row, kD, (size_t)B * kNumKVH * cap * kD, err) ||
+            !QM_IN(wrow, kD, (size_t)B * kNumKVH * T * kD, err))
+            return;
         const uint16_t* vs = v_in + (((size_t)b * T + t) * kNumKVH + g) * kD;
 #pragma unroll
         for (int i = 0; i < 8; i++) {
@@ -250,15 +256,17 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
             for (int sub = 0; sub < 4; sub++) {  // Q: chunks 0..3 (slots 0..3, contiguous)
                 int slot;
                 claim(slot);
-                tma_load_3d(ring + slot * kSlot, &tmq, sub * 64, q0, b * kNumH + h,
-                            smem_u32(&bars->full[slot]));
+                if (QM_IN(slot * kSlot, kSlot, kRing * kSlot, err))
+                    tma_load_3d(ring + slot * kSlot, &tmq, sub * 64, q0, b * kNumH + h,
+                                smem_u32(&bars->full[slot]));
                 n++;
             }
             auto load_k = [&](int j) {
                 for (int c = 0; c < 4 && ok; c++) {
                     int slot;
                     if (!(ok = claim(slot))) break;
-                    tma_load_3d(ring + slot * kSlot, &tmk, c * 64, j * kBN, zc, smem_u32(&bars->full[slot]));
+                    if (QM_IN(slot * kSlot, kSlot, kRing * kSlot, err))
+                        tma_load_3d(ring + slot * kSlot, &tmk, c * 64, j * kBN, zc, smem_u32(&bars->full[slot]));
                     n++;
                 }
             };
@@ -267,8 +275,9 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
                     int slot;
                     if (!(ok = claim(slot))) break;
                     for (int d = 0; d < 4; d++)
-                        tma_load_3d(ring + slot * kSlot + d * kVBox, &tmv, d * 64, j * kBN + c * 32, zc,
-                                    smem_u32(&bars->full[slot]));
+                        if (QM_IN(slot * kSlot + d * kVBox, kVBox, kRing * kSlot, err))
+                            tma_load_3d(ring + slot * kSlot + d * kVBox, &tmv, d * 64, j * kBN + c * 32, zc,
+                                        smem_u32(&bars->full[slot]));
                     n++;
                 }
             };
@@ -402,7 +411,7 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
             }
             float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
             const int par = j & 1;
-            red[(par * 2 + half) * kBM + r] = mx;
+            if (QM_IN((par * 2 + half) * kBM + r, 1, 2 * 2 * kBM, err)) red[(par * 2 + half) * kBM + r] = mx;
             named_bar_sync(bar_id, 64);
             mx = fmaxf(mx, red[(par * 2 + (half ^ 1)) * kBM + r]);
             const float m_new = fmaxf(m_used, mx * kLog2e);
@@ -451,7 +460,8 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
 #pragma unroll
                 for (int c = 0; c < 8; c++) {
                     uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-                    *reinterpret_cast<uint4*>(pbox + sw128_off(r, c)) = v;
+                    if (QM_IN(half * kPBox + sw128_off(r, c), 16, kPBytes, err))
+                        *reinterpret_cast<uint4*>(pbox + sw128_off(r, c)) = v;
                 }
                 fence_proxy_async_shared();
             }
@@ -463,7 +473,7 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
         // the two halves' row sums (the exchange buffer of the next parity is
         // free: its last readers passed this quarter's barrier of the last tile)
         const int pe = n_tiles & 1;
-        red[(pe * 2 + half) * kBM + r] = l;
+        if (QM_IN((pe * 2 + half) * kBM + r, 1, 2 * 2 * kBM, err)) red[(pe * 2 + half) * kBM + r] = l;
         named_bar_sync(bar_id, 64);
         l += red[(pe * 2 + (half ^ 1)) * kBM + r];
         const int jl = n_tiles - 1;
@@ -471,7 +481,8 @@ gqa_prefill_attn(const __grid_constant__ CUtensorMap tmq, const __grid_constant_
         if (ok) {
             tc_fence_after();
             const float inv_l = 1.0f / l;
-            const bool valid = qp < T;
+            const size_t orow_off = (((size_t)b * T + (qp < T ? qp : 0)) * kNumH + h) * kD + half * 128;
+            const bool valid = qp < T && QM_IN(orow_off, 128, (size_t)gridDim.y * T * kNumH * kD, err);
             const uint16_t* grow = q_gate + (((size_t)b * T + (valid ? qp : 0)) * kNumH + h) * 2 * kD + kD
                                    + half * 128;
             float* orow = out + (((size_t)b * T + (valid ? qp : 0)) * kNumH + h) * kD + half * 128;
@@ -522,7 +533,7 @@ cudaError_t launch_gqa_prefill(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
         TimedLaunch tl(ctx, "gqa_prefill_prep");
         gqa_prefill_prep<<<(unsigned)((size_t)B * T * kNumKVH), 160, 0, st>>>(
             q_gate, k, v, prm->q_norm, prm->k_norm, prm->rope_cos, prm->rope_sin, T, qw, kw, vw,
-            kv->k, kv->v, kv->capacity);
+            kv->k, kv->v, kv->capacity, B, ctx->d_err);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;

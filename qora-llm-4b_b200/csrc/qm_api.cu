@@ -189,6 +189,14 @@ int make_kv_tmaps(qm_kv* kv) {
 // ---------------------------------------------------------------------------
 // status / shape
 // ---------------------------------------------------------------------------
+extern "C" int qm_build_flags(void) {
+#ifdef QM_CHECK_BOUNDS
+    return QM_BUILD_BOUNDS_CHECKS;
+#else
+    return 0;
+#endif
+}
+
 extern "C" int qm_shape_get(qm_shape* o) {
     if (!o) return QM_E_ARG;
     o->num_qk_heads = kNumQK;
@@ -1040,3 +1048,81 @@ extern "C" int qm_gqa_decode_host(qm_ctx* c, const qm_gqa_params* p, qm_kv* kv,
     return pipe_finish(c);
 }
 
+
+// ---------------------------------------------------------------------------
+// Prefill on host buffers.  The reference's GPU prefill moves every layer's
+// activations between host and device around its recurrence
+// (src/gpu_inference.rs:464-476 down, 591-604 up); these calls take the host
+// buffers, copy them in on the context stream, run the device prefill and
+// copy the outputs back before returning.  Prefill kernels read their
+// inputs many times, so the inputs are always staged (never read over PCIe
+// in place).
+// ---------------------------------------------------------------------------
+static size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
+
+extern "C" int qm_dn_prefill_host(qm_ctx* c, const qm_dn_params* p, qm_dn_state* st, int T,
+                                  const uint16_t* qkv, const float* a, const float* b, float* y,
+                                  const float* z, float* out) {
+    if (!c) return QM_E_ARG;
+    if (!st || !qkv || !a || !b || !y || T <= 0 || (out && !z) || (z && !out))
+        return set_error(c, QM_E_ARG, "qm_dn_prefill_host: null pointer, T <= 0, or out without z");
+    if (st->ctx != c) return set_error(c, QM_E_MISMATCH, "state belongs to another context");
+    const size_t n = (size_t)st->batch * (size_t)T;
+    const size_t b_qkv = n * kQKVDim * 2, b_ab = n * kNumV * 4, b_y = n * kVDim * 4;
+    const size_t bytes = al256(b_qkv) + 2 * al256(b_ab) + al256(b_y) + (z ? 2 * al256(b_y) : 0);
+    cudaSetDevice(c->device);
+    int rc = ensure_stage(c, bytes);
+    if (!rc) rc = ensure_pipe(c);
+    if (rc) return rc;
+    char* base = static_cast<char*>(c->stage);
+    auto carve = [&](size_t nb) {
+        char* r = base;
+        base += al256(nb);
+        return r;
+    };
+    uint16_t* d_qkv = reinterpret_cast<uint16_t*>(carve(b_qkv));
+    float* d_a = reinterpret_cast<float*>(carve(b_ab));
+    float* d_b = reinterpret_cast<float*>(carve(b_ab));
+    float* d_y = reinterpret_cast<float*>(carve(b_y));
+    float* d_z = z ? reinterpret_cast<float*>(carve(b_y)) : nullptr;
+    float* d_out = z ? reinterpret_cast<float*>(carve(b_y)) : nullptr;
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(d_qkv, qkv, b_qkv, cudaMemcpyHostToDevice, c->stream));
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(d_a, a, b_ab, cudaMemcpyHostToDevice, c->stream));
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(d_b, b, b_ab, cudaMemcpyHostToDevice, c->stream));
+    if (z) QM_CHECK_CUDA(c, cudaMemcpyAsync(d_z, z, b_y, cudaMemcpyHostToDevice, c->stream));
+    rc = qm_dn_prefill(c, p, st, T, d_qkv, d_a, d_b, d_y, d_z, d_out);
+    if (rc) return rc;
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(y, d_y, b_y, cudaMemcpyDeviceToHost, c->stream));
+    if (out) QM_CHECK_CUDA(c, cudaMemcpyAsync(out, d_out, b_y, cudaMemcpyDeviceToHost, c->stream));
+    c->host_staged += 1;
+    return direct_finish(c);
+}
+
+extern "C" int qm_gqa_prefill_host(qm_ctx* c, const qm_gqa_params* p, qm_kv* kv, int T,
+                                   const uint16_t* q_gate, const uint16_t* k, const uint16_t* v,
+                                   float* out) {
+    if (!c) return QM_E_ARG;
+    if (!kv || !q_gate || !k || !v || !out || T <= 0)
+        return set_error(c, QM_E_ARG, "qm_gqa_prefill_host: null pointer or T <= 0");
+    if (kv->ctx != c) return set_error(c, QM_E_MISMATCH, "cache belongs to another context");
+    const size_t n = (size_t)kv->batch * (size_t)T;
+    const size_t b_q = n * kNumH * 2 * kD * 2, b_kv = n * kNumKVH * kD * 2, b_o = n * kNumH * kD * 4;
+    const size_t bytes = al256(b_q) + 2 * al256(b_kv) + al256(b_o);
+    cudaSetDevice(c->device);
+    int rc = ensure_stage(c, bytes);
+    if (!rc) rc = ensure_pipe(c);
+    if (rc) return rc;
+    char* base = static_cast<char*>(c->stage);
+    uint16_t* d_q = reinterpret_cast<uint16_t*>(base);
+    uint16_t* d_k = reinterpret_cast<uint16_t*>(base + al256(b_q));
+    uint16_t* d_v = reinterpret_cast<uint16_t*>(base + al256(b_q) + al256(b_kv));
+    float* d_o = reinterpret_cast<float*>(base + al256(b_q) + 2 * al256(b_kv));
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(d_q, q_gate, b_q, cudaMemcpyHostToDevice, c->stream));
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(d_k, k, b_kv, cudaMemcpyHostToDevice, c->stream));
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(d_v, v, b_kv, cudaMemcpyHostToDevice, c->stream));
+    rc = qm_gqa_prefill(c, p, kv, T, d_q, d_k, d_v, d_o);
+    if (rc) return rc;
+    QM_CHECK_CUDA(c, cudaMemcpyAsync(out, d_o, b_o, cudaMemcpyDeviceToHost, c->stream));
+    c->host_staged += 1;
+    return direct_finish(c);
+}

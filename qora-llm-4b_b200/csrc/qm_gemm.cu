@@ -287,6 +287,7 @@ qm_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restric
             // 32 sums of row `row`, columns [col, col + 32), into y (rows past T and columns past N skipped)
             auto store32 = [&](int row, int col, const float* o) {
                 if (row >= T || col >= N) return;
+                if (!QM_IN((size_t)row * N + col, 32, (size_t)T * N, err)) return;
                 if (OBF16) {
                     uint16_t* dst = static_cast<uint16_t*>(y) + (size_t)row * N + col;
 #pragma unroll
@@ -323,7 +324,8 @@ qm_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restric
                             o[(ROWS || F16W) ? p : (p & ~7) + ((p & 1) ? 4 : 0) + ((p & 7) >> 1)] = v[p];
                         if (splits == 1) {
                             store32(tm * kGmBM + r, n0_tile + c * 32, o);
-                        } else {
+                        } else if (QM_IN((size_t)blockIdx.x * (kGmBM * kGmBN / 4) + (c * 8 + 7) * kGmBM + r, 1,
+                                         (size_t)gridDim.x * (kGmBM * kGmBN / 4), err)) {
 #pragma unroll
                             for (int q = 0; q < 8; q++)
                                 __stcg(mine + (c * 8 + q) * kGmBM + r, make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]));
@@ -338,8 +340,10 @@ qm_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restric
                 // acquire: the last CTA then sees every split's partial.
                 named_bar_sync(1, 128);
                 if (warp == 4 && lane == 0) {
-                    int prev;
-                    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(count + tile) : "memory");
+                    int prev = 0;
+                    if (QM_IN(tile, 1, kSplitCounters, err))
+                        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(count + tile)
+                                     : "memory");
                     bars->last = prev == splits - 1;
                 }
                 named_bar_sync(1, 128);
@@ -358,7 +362,11 @@ qm_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restric
                                     if (sp >= splits) break;                  // depend on timing
 #pragma unroll
                                     for (int q = 0; q < 8; q++) {
-                                        const float4 f = __ldcg(tp + ((sp * 64 + c * 8 + q) * kGmBM + r));
+                                        const size_t pi = (size_t)tile * splits * (kGmBM * kGmBN / 4) +
+                                                          (sp * 64 + c * 8 + q) * kGmBM + r;
+                                        const float4 f = QM_IN(pi, 1, (size_t)gridDim.x * (kGmBM * kGmBN / 4), err)
+                                                             ? __ldcg(tp + ((sp * 64 + c * 8 + q) * kGmBM + r))
+                                                             : make_float4(0.f, 0.f, 0.f, 0.f);
                                         o[4 * q] += f.x;
                                         o[4 * q + 1] += f.y;
                                         o[4 * q + 2] += f.z;
@@ -369,7 +377,8 @@ qm_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restric
                             }
                         }
                     }
-                    if (warp == 4 && lane == 0) count[tile] = 0;  // ready for the next launch
+                    if (warp == 4 && lane == 0 && QM_IN(tile, 1, kSplitCounters, err))
+                        count[tile] = 0;  // ready for the next launch
                 }
             }
         }

@@ -99,6 +99,24 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Device-side index self-checks, compiled into the checked library
+// (-DQM_CHECK_BOUNDS, libqora_mixer_checked.so) in place of the sanitizer:
+// QM_IN(off, n, size, err) is true when elements [off, off + n) lie inside a
+// buffer of `size` elements; otherwise it sets kErrBounds in the error word
+// (qm_sync then returns QM_E_RANGE) and is false, and the caller skips the
+// access — nothing traps.  In the normal build it is the constant true (its
+// arguments have no side effects, so the compiler drops them).
+#ifdef QM_CHECK_BOUNDS
+#define QM_IN(off, n, size, err) ::qm::in_bounds_rec((size_t)(off), (size_t)(n), (size_t)(size), (err))
+#else
+#define QM_IN(off, n, size, err) ((void)(off), (void)(n), (void)(size), (void)(err), true)
+#endif
+__device__ __forceinline__ bool in_bounds_rec(size_t off, size_t n, size_t size, int* err) {
+    if (off <= size && n <= size - off) return true;
+    atomicOr(err, kErrBounds);
+    return false;
+}
+
 // Programmatic dependent launch: a kernel launched with the
 // programmatic-stream-serialization attribute may start while the preceding
 // kernel of the stream runs.  launch_dependents lets the next such kernel

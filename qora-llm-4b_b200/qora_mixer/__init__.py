@@ -23,7 +23,9 @@ import weakref
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 PKG_DIR = os.path.dirname(_HERE)
-LIB_PATH = os.path.join(PKG_DIR, "libqora_mixer.so")
+# QORA_MIXER_LIB selects another build of the same ABI (the checked build,
+# libqora_mixer_checked.so, for the device-side bounds self-check tests)
+LIB_PATH = os.environ.get("QORA_MIXER_LIB") or os.path.join(PKG_DIR, "libqora_mixer.so")
 
 QM_OK = 0
 STATUS = {
@@ -34,7 +36,7 @@ STATUS = {
 
 # Every symbol include/qora_mixer.h declares (checked by the CPU test suite).
 EXPORTS = [
-    "qm_shape_get", "qm_status_string", "qm_ctx_create", "qm_ctx_destroy", "qm_ctx_set_stream",
+    "qm_build_flags", "qm_shape_get", "qm_status_string", "qm_ctx_create", "qm_ctx_destroy", "qm_ctx_set_stream",
     "qm_ctx_get_stream", "qm_sync", "qm_last_error", "qm_ctx_reserve", "qm_ctx_set_host_parts",
     "qm_ctx_set_host_direct", "qm_ctx_host_calls", "qm_ctx_launch_count",
     "qm_ctx_set_timing", "qm_ctx_kernel_time",
@@ -42,9 +44,9 @@ EXPORTS = [
     "qm_dn_state_reset", "qm_dn_state_snapshot", "qm_dn_state_restore", "qm_dn_state_read",
     "qm_dn_state_write", "qm_dn_state_conv_pos", "qm_dn_state_set_conv_pos",
     "qm_dn_state_batch", "qm_dn_state_data", "qm_dn_decode", "qm_dn_decode_host", "qm_dn_decode_seq",
-    "qm_dn_prefill", "qm_kv_create", "qm_kv_wrap", "qm_kv_destroy", "qm_kv_snapshot",
+    "qm_dn_prefill", "qm_dn_prefill_host", "qm_kv_create", "qm_kv_wrap", "qm_kv_destroy", "qm_kv_snapshot",
     "qm_kv_restore", "qm_kv_seq_len", "qm_kv_set_seq_len", "qm_kv_capacity", "qm_kv_batch",
-    "qm_kv_data", "qm_gqa_decode", "qm_gqa_decode_host", "qm_gqa_prefill",
+    "qm_kv_data", "qm_gqa_decode", "qm_gqa_decode_host", "qm_gqa_prefill", "qm_gqa_prefill_host",
     "qm_gqa_decode_noalloc",
     "qm_dn_state_create_heads", "qm_dn_state_wrap_heads", "qm_dn_state_heads",
     "qm_kv_create_heads", "qm_kv_wrap_heads", "qm_kv_heads",
@@ -139,6 +141,9 @@ def lib():
         "qm_dn_decode_host": ([P, C.POINTER(QmDnParams), P, P, P, P, P, P, P], I),
         "qm_dn_prefill": ([P, C.POINTER(QmDnParams), P, I, P, P, P, P, P, P], I),
         "qm_dn_decode_seq": ([P, C.POINTER(QmDnParams), P, I, P, P, P, P, P, P], I),
+        "qm_build_flags": ([], I),
+        "qm_dn_prefill_host": ([P, C.POINTER(QmDnParams), P, I, P, P, P, P, P, P], I),
+        "qm_gqa_prefill_host": ([P, C.POINTER(QmGqaParams), P, I, P, P, P, P], I),
         "qm_kv_create": ([P, I, I, PP], I),
         "qm_kv_wrap": ([P, I, I, P, P, PP], I),
         "qm_kv_destroy": ([P], I),
@@ -542,6 +547,18 @@ class Mixer:
         rc = lib().qm_gqa_decode_host(self.ctx.handle, C.byref(p), kv.handle, _ptr(q_gate),
                                       _ptr(k_new), _ptr(v_new), _ptr(out))
         self.ctx.check(rc, "qm_gqa_decode_host")
+
+    def dn_prefill_host(self, p: QmDnParams, st: DnState, T, qkv_bf16, a, b, y, z=None, out=None):
+        """qm_dn_prefill on host arrays (numpy / CPU tensors); returns after y (and out) are filled."""
+        rc = lib().qm_dn_prefill_host(self.ctx.handle, C.byref(p), st.handle, int(T), _ptr(qkv_bf16),
+                                      _ptr(a), _ptr(b), _ptr(y), _ptr(z), _ptr(out))
+        self.ctx.check(rc, "qm_dn_prefill_host")
+
+    def gqa_prefill_host(self, p: QmGqaParams, kv: KvCache, T, q_gate_bf16, k_bf16, v_bf16, out):
+        """qm_gqa_prefill on host arrays; returns after out is filled."""
+        rc = lib().qm_gqa_prefill_host(self.ctx.handle, C.byref(p), kv.handle, int(T), _ptr(q_gate_bf16),
+                                       _ptr(k_bf16), _ptr(v_bf16), _ptr(out))
+        self.ctx.check(rc, "qm_gqa_prefill_host")
 
     def gqa_prefill(self, p: QmGqaParams, kv: KvCache, T, q_gate_bf16, k_bf16, v_bf16, out):
         rc = lib().qm_gqa_prefill(self.ctx.handle, C.byref(p), kv.handle, int(T),

@@ -41,6 +41,9 @@ pub const QM_W_Q4_ROWS: c_int = 3; // one row per output, [n][k/2] + scales [n][
 
 pub const QM_COMM_ID_BYTES: usize = 128;
 
+/// `qm_build_flags` bit: device-side bounds self-checks compiled in.
+pub const QM_BUILD_BOUNDS_CHECKS: c_int = 1;
+
 // ---- opaque handles -------------------------------------------------------
 #[repr(C)]
 pub struct qm_ctx {
@@ -128,7 +131,8 @@ pub struct qm_shard {
 }
 
 extern "C" {
-    // ---- shape, status ----------------------------------------------------
+    // ---- build, shape, status ------------------------------------------------
+    pub fn qm_build_flags() -> c_int;
     pub fn qm_shape_get(out: *mut qm_shape) -> c_int;
     pub fn qm_status_string(status: c_int) -> *const c_char;
 
@@ -247,6 +251,18 @@ extern "C" {
         z: *const f32,
         out: *mut f32,
     ) -> c_int;
+    pub fn qm_dn_prefill_host(
+        ctx: *mut qm_ctx,
+        p: *const qm_dn_params,
+        st: *mut qm_dn_state,
+        t: c_int,
+        qkv: *const u16,
+        a: *const f32,
+        b: *const f32,
+        y: *mut f32,
+        z: *const f32,
+        out: *mut f32,
+    ) -> c_int;
     pub fn qm_dn_state_create_heads(
         ctx: *mut qm_ctx,
         batch: c_int,
@@ -325,6 +341,16 @@ extern "C" {
     ) -> c_int;
     /// src/gemv.rs:1364-1444 (causal prefill; replaces the cache contents).
     pub fn qm_gqa_prefill(
+        ctx: *mut qm_ctx,
+        p: *const qm_gqa_params,
+        kv: *mut qm_kv,
+        t: c_int,
+        q_gate: *const u16,
+        k: *const u16,
+        v: *const u16,
+        out: *mut f32,
+    ) -> c_int;
+    pub fn qm_gqa_prefill_host(
         ctx: *mut qm_ctx,
         p: *const qm_gqa_params,
         kv: *mut qm_kv,

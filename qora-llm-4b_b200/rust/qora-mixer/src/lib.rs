@@ -559,6 +559,50 @@ impl<'c> Mixer<'c> {
         self.ctx.check(sys::qm_dn_prefill(self.ctx.raw, &p.raw, st.raw, t, qkv_bf16, a, b, y, z, out))
     }
 
+    /// `prefill_deltanet_layer`'s loop on host buffers (the reference's GPU
+    /// prefill flow, src/gpu_inference.rs:464-604): qkv bf16 bits
+    /// [B*t*8192], a, b [B*t*32], y [B*t*4096]; with `z_out`, the gated
+    /// output (z [B*t*4096] in, out [B*t*4096]).
+    pub fn dn_prefill_host(
+        &self,
+        p: &DnParams<'_>,
+        st: &mut DnStateHandle<'_>,
+        t: i32,
+        qkv_bf16: &[u16],
+        a: &[f32],
+        b: &[f32],
+        y: &mut [f32],
+        z_out: Option<(&[f32], &mut [f32])>,
+    ) -> Result<()> {
+        let n = st.batch() as usize * t.max(0) as usize;
+        need(qkv_bf16.len(), n * 8192, "qkv")?;
+        need(a.len(), n * 32, "a")?;
+        need(b.len(), n * 32, "b")?;
+        need(y.len(), n * 4096, "y")?;
+        let (zp, op) = match z_out {
+            Some((z, out)) => {
+                need(z.len(), n * 4096, "z")?;
+                need(out.len(), n * 4096, "out")?;
+                (z.as_ptr(), out.as_mut_ptr())
+            }
+            None => (null(), null_mut()),
+        };
+        self.ctx.check(unsafe {
+            sys::qm_dn_prefill_host(
+                self.ctx.raw,
+                &p.raw,
+                st.raw,
+                t,
+                qkv_bf16.as_ptr(),
+                a.as_ptr(),
+                b.as_ptr(),
+                y.as_mut_ptr(),
+                zp,
+                op,
+            )
+        })
+    }
+
     /// `forward_attn_decode`'s attention region (src/gemv.rs:927-1011) on
     /// host buffers: q_gate [B*16*512], k_new, v_new [B*4*256], out [B*16*256].
     pub fn gqa_decode_host(
@@ -600,6 +644,57 @@ impl<'c> Mixer<'c> {
         out: *mut f32,
     ) -> Result<()> {
         self.ctx.check(sys::qm_gqa_decode(self.ctx.raw, &p.raw, kv.raw, q_gate, k_new, v_new, out))
+    }
+
+    /// `prefill_attn_layer`'s attention region on host buffers (bf16 bits):
+    /// q_gate [B*t*16*512], k, v [B*t*4*256]; out [B*t*16*256] f32.
+    pub fn gqa_prefill_host(
+        &self,
+        p: &GqaParams<'_>,
+        kv: &mut KvHandle<'_>,
+        t: i32,
+        q_gate_bf16: &[u16],
+        k_bf16: &[u16],
+        v_bf16: &[u16],
+        out: &mut [f32],
+    ) -> Result<()> {
+        let n = kv.batch() as usize * t.max(0) as usize;
+        need(q_gate_bf16.len(), n * 16 * 512, "q_gate")?;
+        need(k_bf16.len(), n * 4 * 256, "k")?;
+        need(v_bf16.len(), n * 4 * 256, "v")?;
+        need(out.len(), n * 16 * 256, "out")?;
+        self.ctx.check(unsafe {
+            sys::qm_gqa_prefill_host(
+                self.ctx.raw,
+                &p.raw,
+                kv.raw,
+                t,
+                q_gate_bf16.as_ptr(),
+                k_bf16.as_ptr(),
+                v_bf16.as_ptr(),
+                out.as_mut_ptr(),
+            )
+        })
+    }
+
+    /// T sequential decode steps in one launch (device pointers; see `qm_dn_decode_seq`).
+    ///
+    /// # Safety
+    /// Device pointers: qkv [B*t*8192] (16-byte aligned), a, b [B*t*32],
+    /// y [B*t*nvh*128] or null when out is given; z [B*t*4096] and out, or both null.
+    pub unsafe fn dn_decode_seq_device(
+        &self,
+        p: &DnParams<'_>,
+        st: &mut DnStateHandle<'_>,
+        t: i32,
+        qkv: *const f32,
+        a: *const f32,
+        b: *const f32,
+        y: *mut f32,
+        z: *const f32,
+        out: *mut f32,
+    ) -> Result<()> {
+        self.ctx.check(sys::qm_dn_decode_seq(self.ctx.raw, &p.raw, st.raw, t, qkv, a, b, y, z, out))
     }
 
     /// `prefill_attn_layer`'s attention region (src/gemv.rs:1364-1444); it
