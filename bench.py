@@ -1077,7 +1077,10 @@ def bench_config1(ctx, reps, cpu=True, ncache=24):
            "launches_per_call": launches,
            "l2": f"{ncache} distinct caches rotated ({ncache * alg / 1e6:.0f} MB > L2)",
            "timing": "one call per cache captured in a CUDA graph, replayed; CUDA events",
-           "roofline": {"bound": "hbm", "kernel": "gqa_prep + gqa_attn + gqa_combine (whole call)",
+           "roofline": {"bound": "hbm",
+                        "kernel": ("gqa_fused (q norm + RoPE, split-KV attention, cluster merge, gate: "
+                                   "one launch)" if launches == 1 else
+                                   "gqa_prep + gqa_attn + gqa_combine (whole call)"),
                         "achieved": round(ach, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                         "frac": round(ach / peak, 4), "algorithmic_bytes_per_call": alg}}
     if cpu:

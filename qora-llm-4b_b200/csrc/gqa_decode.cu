@@ -21,6 +21,8 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
 
 #include "qm_internal.h"
 #include "qm_ptx.cuh"
@@ -155,88 +157,16 @@ __device__ __forceinline__ uint32_t swz_addr(uint32_t base, int pos, int dim) {
                              ((((dim & 63) >> 3) ^ (pos & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(160, 1)
-gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                const uint16_t* __restrict__ q_bf, float* __restrict__ part_o,
-                float* __restrict__ part_ml, int L, int tps, int nsplit, int nkv, int b0, int* err) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-    uint64_t* empty = full + kStages;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
-
-    const int split = blockIdx.x, g = blockIdx.y, b = b0 + blockIdx.z;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile0 = split * tps;
-    const int ntiles_all = (L + kTile - 1) / kTile;
-    const int ntiles = min(tps, ntiles_all - tile0);
-    const int pos_end = min(L, (tile0 + ntiles) * kTile);
-
-    pdl_launch_dependents();  // the combine kernel waits for this grid's completion
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; s++) {
-            mbar_init(smem_u32(&full[s]), 1);
-            mbar_init(smem_u32(&empty[s]), kGroup);
-        }
-        *abort_flag = 0;
-        fence_barrier_init();
-    }
-    __syncthreads();
-
-    const uint32_t sbase = smem_u32(smem);
-    if (warp == kGroup) {
-        // ---------------- producer ----------------
-        // Positions [0, L) of the cache are not written by the prep kernel of
-        // this call (it appends at L), and the preceding call's kernels have
-        // completed: the combine kernel never lets its successor start early,
-        // and it waited for everything before it.  So the loads start at once,
-        // before the prep kernel is done.
-        if (lane == 0) {
-            prefetch_tmap(&tmk);
-            prefetch_tmap(&tmv);
-            const int zc = b * nkv + g;
-            int it = 0;
-            for (; it < ntiles; it++) {
-                const int st = it % kStages, round = it / kStages;
-                if (round > 0 &&
-                    !mbar_wait_bounded(smem_u32(&empty[st]), (round - 1) & 1, abort_flag, err))
-                    break;
-                const uint32_t fb = smem_u32(&full[st]);
-                mbar_arrive_expect_tx(fb, kStageBytes);
-                const int p0 = (tile0 + it) * kTile;
-                const uint32_t kb = sbase + st * kStageBytes;
-#pragma unroll
-                for (int sub = 0; sub < 4; sub++) {
-                    tma_load_3d(kb + sub * kSubBytes, &tmk, sub * 64, p0, zc, fb);
-                    tma_load_3d(kb + kTileBytes + sub * kSubBytes, &tmv, sub * 64, p0, zc, fb);
-                }
-            }
-            // Do not leave while copies this CTA issued may still land.
-            for (int j = max(0, it - kStages); j < it; j++)
-                mbar_wait_bounded(smem_u32(&full[j % kStages]), (j / kStages) & 1, abort_flag, err);
-        }
-        return;
-    }
-
-    // ---------------- consumers: warp w owns positions [16w, 16w+16) of a tile ----
-    const int row = lane >> 2;          // A/C row: head (row & 3), hi/lo (row >> 2)
+// Consumer side of the split-KV attention over tiles [tile0, tile0 + ntiles)
+// (positions below pos_end count): warp w (0..3) owns positions [16w, 16w+16)
+// of each 64-position tile of the stage ring; qa holds the 4 query heads' q
+// as bf16 A fragments, hi parts in rows 0-3 and lo parts in rows 4-7.  o, m_run
+// and l_run are the warp's running (unnormalised) output, maximum and sum.
+__device__ __forceinline__ void attend_tiles(uint32_t sbase, uint64_t* full, uint64_t* empty,
+                                             volatile int* abort_flag, int* err, const uint32_t (&qa)[16][2],
+                                             int tile0, int ntiles, int pos_end, int warp, int lane,
+                                             float (&o)[32][2], float& m_run, float& l_run) {
     const int quad = lane & 3;
-    uint32_t qa[16][2];
-    pdl_wait();  // q comes from the prep kernel (the producer's K/V loads did not wait)
-    {
-        const int head = row & 3, hl = row >> 2;
-        const uint16_t* qr = q_bf + ((((size_t)b * nkv + g) * kGroup + head) * 2 + hl) * kD;
-#pragma unroll
-        for (int kk = 0; kk < 16; kk++) {
-            qa[kk][0] = *reinterpret_cast<const uint32_t*>(qr + kk * 16 + quad * 2);
-            qa[kk][1] = *reinterpret_cast<const uint32_t*>(qr + kk * 16 + 8 + quad * 2);
-        }
-    }
-    float o[32][2];
-#pragma unroll
-    for (int n = 0; n < 32; n++) o[n][0] = o[n][1] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
-
     for (int it = 0; it < ntiles; it++) {
         const int st = it % kStages, round = it / kStages;
         const bool ok = mbar_wait_bounded(smem_u32(&full[st]), round & 1, abort_flag, err);
@@ -335,6 +265,100 @@ gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&empty[st]));
     }
+
+}
+
+__global__ void __launch_bounds__(160, 1)
+gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                const uint16_t* __restrict__ q_bf, float* __restrict__ part_o,
+                float* __restrict__ part_ml, int L, int tps, int nsplit, int nkv, int b0, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
+
+    const int split = blockIdx.x, g = blockIdx.y, b = b0 + blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile0 = split * tps;
+    const int ntiles_all = (L + kTile - 1) / kTile;
+    const int ntiles = min(tps, ntiles_all - tile0);
+    const int pos_end = min(L, (tile0 + ntiles) * kTile);
+
+    pdl_launch_dependents();  // the combine kernel waits for this grid's completion
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), kGroup);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    const uint32_t sbase = smem_u32(smem);
+    if (warp == kGroup) {
+        // ---------------- producer ----------------
+        // Positions [0, L) of the cache are not written by the prep kernel of
+        // this call (it appends at L), so the loads start at once, before the
+        // prep kernel is done.  The one exception is the tile holding position
+        // L - 1: the preceding call on this cache appended it, and a fused
+        // call (gqa_fused_kernel) lets its successor start before it
+        // completes.  That tile is loaded after this grid's wait, which
+        // returns once the prep kernel, and so everything before it, is done.
+        if (lane == 0) {
+            prefetch_tmap(&tmk);
+            prefetch_tmap(&tmv);
+            const int zc = b * nkv + g;
+            int it = 0;
+            bool waited = false;
+            for (; it < ntiles; it++) {
+                const int st = it % kStages, round = it / kStages;
+                if (round > 0 &&
+                    !mbar_wait_bounded(smem_u32(&empty[st]), (round - 1) & 1, abort_flag, err))
+                    break;
+                if (!waited && (tile0 + it) * kTile + kTile > L - 1) {
+                    pdl_wait();
+                    waited = true;
+                }
+                const uint32_t fb = smem_u32(&full[st]);
+                mbar_arrive_expect_tx(fb, kStageBytes);
+                const int p0 = (tile0 + it) * kTile;
+                const uint32_t kb = sbase + st * kStageBytes;
+#pragma unroll
+                for (int sub = 0; sub < 4; sub++) {
+                    tma_load_3d(kb + sub * kSubBytes, &tmk, sub * 64, p0, zc, fb);
+                    tma_load_3d(kb + kTileBytes + sub * kSubBytes, &tmv, sub * 64, p0, zc, fb);
+                }
+            }
+            // Do not leave while copies this CTA issued may still land.
+            for (int j = max(0, it - kStages); j < it; j++)
+                mbar_wait_bounded(smem_u32(&full[j % kStages]), (j / kStages) & 1, abort_flag, err);
+        }
+        return;
+    }
+
+    // ---------------- consumers: warp w owns positions [16w, 16w+16) of a tile ----
+    const int row = lane >> 2;          // A/C row: head (row & 3), hi/lo (row >> 2)
+    const int quad = lane & 3;
+    uint32_t qa[16][2];
+    pdl_wait();  // q comes from the prep kernel (the producer's K/V loads did not wait)
+    {
+        const int head = row & 3, hl = row >> 2;
+        const uint16_t* qr = q_bf + ((((size_t)b * nkv + g) * kGroup + head) * 2 + hl) * kD;
+#pragma unroll
+        for (int kk = 0; kk < 16; kk++) {
+            qa[kk][0] = *reinterpret_cast<const uint32_t*>(qr + kk * 16 + quad * 2);
+            qa[kk][1] = *reinterpret_cast<const uint32_t*>(qr + kk * 16 + 8 + quad * 2);
+        }
+    }
+    float o[32][2];
+#pragma unroll
+    for (int n = 0; n < 32; n++) o[n][0] = o[n][1] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+    attend_tiles(sbase, full, empty, abort_flag, err, qa, tile0, ntiles, pos_end, warp, lane, o, m_run,
+                 l_run);
 
     // ---- fold lo rows into hi rows, then merge the 4 warps through smem ----
 #pragma unroll
@@ -496,6 +520,321 @@ gqa_combine_kernel(const float* __restrict__ q_f32, const float* __restrict__ kn
     out[(size_t)bh * kD + d] = (o / lsum) * (1.0f / (1.0f + __expf(-gate)));
 }
 
+// ---------------------------------------------------------------------------
+// 4. one launch for small batches: prep + split-KV attention + combine.
+// A cluster of nsplit CTAs (grid.x, up to 16) owns one (sequence, KV head);
+// CTA r streams tiles [r*tps, (r+1)*tps) like gqa_attn, computes the 4 query
+// heads' q itself (RMSNorm(1+g), RoPE, 1/16) and keeps its merged partial in
+// shared memory.  After a cluster barrier, CTA r produces outputs
+// [r*1024/nsplit, (r+1)*1024/nsplit) of the group's 4 x 256 by reading every
+// CTA's partial through distributed shared memory, adding the new token in
+// f32 and the sigmoid gate.  CTA 0 appends the new k/v.  No workspace.
+//
+// Launched with programmatic stream serialisation, and it lets its successor
+// start once it has itself waited for its predecessor: a successor that is
+// the next decode call then loads its cache tiles while this call runs,
+// except the tile holding position L-1, which this call may be writing (the
+// append of a call on the same cache); that tile and every input are read
+// only after the successor's own wait, i.e. after this grid has completed.
+// ---------------------------------------------------------------------------
+constexpr int kFzQ = kStages * kStageBytes;        // q of the 4 heads, f32 [4][256]
+constexpr int kFzKn = kFzQ + kGroup * kD * 4;      // the new token's normed k, f32 [256]
+constexpr int kFzRes = kFzKn + kD * 4;             // this CTA's partial o [4][256]
+constexpr int kFzMl = kFzRes + kGroup * kD * 4;    // its m [4], l [4], then q.k_new [4]
+constexpr int kFzBars = kFzMl + 16 * 4;
+constexpr int kFusedSmem = kFzBars + 2 * kStages * 8 + 16 + 1024 /*align*/;
+constexpr int kFusedMaxSplit = 16;
+// outputs per consumer thread after the merge: 4 x 256 / (nsplit x 128), nsplit >= 2
+constexpr int kFusedPerThread = 4;
+
+__global__ void __launch_bounds__(160, 1)
+gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                 const float* __restrict__ q_gate, const float* __restrict__ k_new,
+                 const float* __restrict__ v_new, const float* __restrict__ q_norm,
+                 const float* __restrict__ k_norm, const float* __restrict__ rope_cos,
+                 const float* __restrict__ rope_sin, int64_t pos, uint16_t* __restrict__ kcache,
+                 uint16_t* __restrict__ vcache, int cap, const float* __restrict__ c_gate,
+                 const float* __restrict__ c_v, float* __restrict__ out, int tps, int kv_lo, int nkv,
+                 int b0, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    float* q_s = reinterpret_cast<float*>(smem + kFzQ);
+    float* kn_s = reinterpret_cast<float*>(smem + kFzKn);
+    float* res_o = reinterpret_cast<float*>(smem + kFzRes);
+    float* res_m = reinterpret_cast<float*>(smem + kFzMl);
+    float* res_l = res_m + kGroup;
+    float* s_new = res_l + kGroup;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kFzBars);
+    uint64_t* empty = full + kStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
+
+    const int split = blockIdx.x, nsplit = gridDim.x;  // split == rank in the cluster
+    const int gl = blockIdx.y, g = kv_lo + gl, b = b0 + blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int L = (int)pos;  // cached positions; the new token goes to index L
+    const int tile0 = split * tps;
+    const int ntiles_all = (L + kTile - 1) / kTile;
+    const int ntiles = max(0, min(tps, ntiles_all - tile0));
+    const int pos_end = min(L, (tile0 + ntiles) * kTile);
+    const int per = (kGroup * kD) / nsplit;  // outputs this CTA produces after the merge
+    float red_gate[kFusedPerThread], red_v[kFusedPerThread];
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), kGroup);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const uint32_t sbase = smem_u32(smem);
+
+    if (warp == kGroup) {
+        // ---------------- producer warp ----------------
+        const int zc = b * nkv + gl;
+        auto issue = [&](int it) {
+            const int st = it % kStages;
+            const uint32_t fb = smem_u32(&full[st]);
+            mbar_arrive_expect_tx(fb, kStageBytes);
+            const int p0 = (tile0 + it) * kTile;
+            const uint32_t kb = sbase + st * kStageBytes;
+#pragma unroll
+            for (int sub = 0; sub < 4; sub++) {
+                tma_load_3d(kb + sub * kSubBytes, &tmk, sub * 64, p0, zc, fb);
+                tma_load_3d(kb + kTileBytes + sub * kSubBytes, &tmv, sub * 64, p0, zc, fb);
+            }
+        };
+        int it = 0;
+        if (lane == 0) {
+            prefetch_tmap(&tmk);
+            prefetch_tmap(&tmv);
+            // before the wait: the first ring's tiles whose positions all lie below L - 1
+            for (; it < min(ntiles, kStages); it++) {
+                if ((tile0 + it) * kTile + kTile > L - 1) break;
+                issue(it);
+            }
+        }
+        it = __shfl_sync(0xffffffffu, it, 0);
+        pdl_wait();
+        // the new token's k: RMSNorm(1+g) + partial RoPE (gemv.rs:945-955); CTA 0 appends k, v
+        {
+            const float* src = k_new + ((size_t)b * kNumKVH + g) * kD;
+            float x[8];
+            float ss = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                x[i] = src[lane + 32 * i];
+                ss = fmaf(x[i], x[i], ss);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float inv = 1.0f / sqrtf(ss * (1.0f / kD) + 1e-6f);  // gemv.rs:591
+#pragma unroll
+            for (int i = 0; i < 8; i++) x[i] = x[i] * inv * (1.0f + k_norm[lane + 32 * i]);
+            const float c = rope_cos[pos * kHalfRot + lane];
+            const float s = rope_sin[pos * kHalfRot + lane];
+            const float x1 = x[0], x2 = x[1];
+            x[0] = x1 * c - x2 * s;
+            x[1] = x2 * c + x1 * s;
+#pragma unroll
+            for (int i = 0; i < 8; i++) kn_s[lane + 32 * i] = x[i];
+            if (split == 0) {
+                const size_t row = (((size_t)b * nkv + gl) * cap + pos) * kD;
+                const float* vs = v_new + ((size_t)b * kNumKVH + g) * kD;
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int e = lane + 32 * i;
+                    kcache[row + e] = bf16_bits_rn(x[i]);
+                    vcache[row + e] = bf16_bits_rn(vs[e]);
+                }
+            }
+        }
+        if (lane == 0) {
+            for (; it < ntiles; it++) {
+                const int round = it / kStages;
+                if (round > 0 &&
+                    !mbar_wait_bounded(smem_u32(&empty[it % kStages]), (round - 1) & 1, abort_flag, err))
+                    break;
+                issue(it);
+            }
+            // every copy this CTA issued has landed before the ring is reused below
+            for (int j = max(0, it - kStages); j < it; j++)
+                mbar_wait_bounded(smem_u32(&full[j % kStages]), (j / kStages) & 1, abort_flag, err);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- consumers ----------------
+        pdl_wait();  // q comes from the preceding kernel
+        pdl_launch_dependents();
+        // the gate logit and new v of the outputs this thread produces after
+        // the cluster merge, loaded now so they arrive while the tiles stream
+#pragma unroll
+        for (int u = 0; u < kFusedPerThread; u++) {
+            const int oi = threadIdx.x + u * (kGroup * 32);
+            if (oi >= per) break;
+            const int idx = split * per + oi;
+            const int head = idx / kD, d = idx % kD;
+            red_gate[u] = c_gate[((size_t)b * kNumH + g * kGroup + head) * 2 * kD + kD + d];
+            red_v[u] = c_v[((size_t)b * kNumKVH + g) * kD + d];
+        }
+        // q of query head g*4 + warp: RMSNorm(1+g), RoPE, scale 1/16 (gemv.rs:945-959), as in gqa_prep
+        {
+            const int h = g * kGroup + warp;
+            const float* src = q_gate + ((size_t)b * kNumH + h) * 2 * kD;
+            float x[8];
+            float ss = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                x[i] = src[lane + 32 * i];
+                ss = fmaf(x[i], x[i], ss);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float inv = 1.0f / sqrtf(ss * (1.0f / kD) + 1e-6f);
+#pragma unroll
+            for (int i = 0; i < 8; i++) x[i] = x[i] * inv * (1.0f + q_norm[lane + 32 * i]);
+            const float c = rope_cos[pos * kHalfRot + lane];
+            const float s = rope_sin[pos * kHalfRot + lane];
+            const float x1 = x[0], x2 = x[1];
+            x[0] = x1 * c - x2 * s;
+            x[1] = x2 * c + x1 * s;
+#pragma unroll
+            for (int i = 0; i < 8; i++) q_s[warp * kD + lane + 32 * i] = x[i] * 0.0625f;
+        }
+        named_bar_sync(1, kGroup * 32);
+        const int row = lane >> 2, quad = lane & 3;
+        uint32_t qa[16][2];
+        {
+            const int head = row & 3, hl = row >> 2;
+            const float* qr = q_s + head * kD;
+            auto part = [&](int e) -> uint32_t {  // bf16 hi (hl 0) or lo (hl 1) of q[e], q[e+1]
+                uint16_t r[2];
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const float qs = qr[e + j];
+                    const uint16_t hi = bf16_bits_rn(qs);
+                    r[j] = hl ? bf16_bits_rn(qs - bf16_bits_to_f32(hi)) : hi;
+                }
+                return pack_bf16(r[0], r[1]);
+            };
+#pragma unroll
+            for (int kk = 0; kk < 16; kk++) {
+                qa[kk][0] = part(kk * 16 + quad * 2);
+                qa[kk][1] = part(kk * 16 + 8 + quad * 2);
+            }
+        }
+        float o[32][2];
+#pragma unroll
+        for (int n = 0; n < 32; n++) o[n][0] = o[n][1] = 0.f;
+        float m_run = -INFINITY, l_run = 0.f;
+        attend_tiles(sbase, full, empty, abort_flag, err, qa, tile0, ntiles, pos_end, warp, lane, o, m_run,
+                     l_run);
+        // fold lo rows into hi rows; merge the 4 warps (stage buffers reused)
+#pragma unroll
+        for (int n = 0; n < 32; n++) {
+            o[n][0] += __shfl_xor_sync(0xffffffffu, o[n][0], 16);
+            o[n][1] += __shfl_xor_sync(0xffffffffu, o[n][1], 16);
+        }
+        named_bar_sync(1, kGroup * 32);  // all consumers are done with the stage buffers
+        // the 4 warps' partials, rows padded by 8 floats so the 16 lanes'
+        // float2 stores fall on distinct banks
+        constexpr int kRow = kD + 8;
+        float* mo = reinterpret_cast<float*>(smem);  // [4 warps][4 heads][kRow]
+        float* mm = mo + kGroup * kGroup * kRow;     // [4][4]
+        float* ml = mm + kGroup * kGroup;            // [4][4]
+        float* sc = ml + kGroup * kGroup;            // [4][4] scale of warp w's partial of head h
+        if (lane < 16) {
+            const int head = lane >> 2;
+            float* dst = mo + (warp * kGroup + head) * kRow + quad * 2;
+#pragma unroll
+            for (int n = 0; n < 32; n++) *reinterpret_cast<float2*>(dst + n * 8) = make_float2(o[n][0], o[n][1]);
+            if (quad == 0) {
+                mm[warp * kGroup + head] = m_run;
+                ml[warp * kGroup + head] = l_run;
+            }
+        }
+        named_bar_sync(1, kGroup * 32);
+        const int t = threadIdx.x;  // 0..127
+        if (t < kGroup) {  // head t: the CTA's maximum, sum and the 4 warps' scales
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kGroup; w++) M = fmaxf(M, mm[w * kGroup + t]);
+            float lsum = 0.f;
+#pragma unroll
+            for (int w = 0; w < kGroup; w++) {
+                const float mw = mm[w * kGroup + t];
+                const float f = (mw == -INFINITY) ? 0.f : exp2f((mw - M) * kLog2e);
+                sc[w * kGroup + t] = f;
+                lsum += f * ml[w * kGroup + t];
+            }
+            res_m[t] = M;
+            res_l[t] = (M == -INFINITY) ? 0.f : lsum;
+        }
+        named_bar_sync(1, kGroup * 32);
+#pragma unroll
+        for (int e = 0; e < (kGroup * kD) / 128; e++) {
+            const int idx = e * 128 + t;
+            const int head = idx / kD, d = idx % kD;
+            float acc = 0.f;
+#pragma unroll
+            for (int w = 0; w < kGroup; w++) acc = fmaf(sc[w * kGroup + head], mo[(w * kGroup + head) * kRow + d], acc);
+            res_o[head * kD + d] = acc;
+        }
+    }
+    // every CTA's partial (and this CTA's q and new k) is complete
+    cluster_sync_all();
+    if (warp < kGroup) {  // the new token's score for head `warp`: q . k_new in f32
+        float prod = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) prod = fmaf(q_s[warp * kD + lane + 32 * i], kn_s[lane + 32 * i], prod);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) prod += __shfl_xor_sync(0xffffffffu, prod, o);
+        if (lane == 0) s_new[warp] = prod;
+    }
+    __syncthreads();
+    // outputs [split*per, (split+1)*per) of the group's 4 x 256, thread t
+    // taking t, t + 128, ...: merge the nsplit partials, add the new token,
+    // apply the gate (gemv.rs:1008-1011)
+    if (warp < kGroup) {
+#pragma unroll
+        for (int u = 0; u < kFusedPerThread; u++) {
+            const int oi = threadIdx.x + u * (kGroup * 32);
+            if (oi >= per) break;
+            const int idx = split * per + oi;
+            const int head = idx / kD, d = idx % kD;
+            const float sn = s_new[head];
+            float mi[kFusedMaxSplit], oi_v[kFusedMaxSplit], li[kFusedMaxSplit];
+#pragma unroll
+            for (int i = 0; i < kFusedMaxSplit; i++) {
+                if (i < nsplit) {
+                    mi[i] = ld_dsmem_f32(res_m + head, (uint32_t)i);
+                    li[i] = ld_dsmem_f32(res_l + head, (uint32_t)i);
+                    oi_v[i] = ld_dsmem_f32(res_o + head * kD + d, (uint32_t)i);
+                } else {
+                    mi[i] = -INFINITY;
+                    li[i] = oi_v[i] = 0.f;
+                }
+            }
+            float M = sn;
+#pragma unroll
+            for (int i = 0; i < kFusedMaxSplit; i++) M = fmaxf(M, mi[i]);
+            const float wn = exp2f((sn - M) * kLog2e);
+            float acc = wn * red_v[u];
+            float lsum = wn;
+#pragma unroll
+            for (int i = 0; i < kFusedMaxSplit; i++) {
+                const float f = (mi[i] == -INFINITY) ? 0.f : exp2f((mi[i] - M) * kLog2e);
+                acc = fmaf(f, oi_v[i], acc);
+                lsum = fmaf(f, li[i], lsum);
+            }
+            out[(((size_t)b * nkv + gl) * kGroup + head) * kD + d] =
+                (acc / lsum) * (1.0f / (1.0f + __expf(-red_gate[u])));
+        }
+    }
+    cluster_sync_all();  // no CTA leaves while another reads its shared memory
+}
+
 }  // namespace
 
 // Workspace of a call on sequences [b0, b0 + nb) of a batch-`batch` cache
@@ -505,6 +844,62 @@ size_t gqa_decode_ws_bytes(int batch, int nkv, int64_t seq_len, int num_sms, int
     return ws_layout(batch, nkv, p.nsplit).total;
 }
 
+// CTAs per cluster of the fused kernel on this device: 16 where a cluster of
+// 16 such CTAs can be resident (a non-portable size), else 8; 0 if neither.
+// Decided once per device, so every call on a device merges its splits in
+// the same order.
+static int fused_splits(qm_ctx* ctx) {
+    static std::atomic<int> known[64];
+    const int dev = ctx->device;
+    if (dev >= 0 && dev < 64) {
+        const int k = known[dev].load(std::memory_order_acquire);
+        if (k != 0) return k > 0 ? k : 0;
+    }
+    int found = -1;
+    if (cudaFuncSetAttribute(gqa_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFusedSmem) ==
+            cudaSuccess &&
+        cudaFuncSetAttribute(gqa_fused_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+            cudaSuccess) {
+        for (int S : {16, 8}) {
+            cudaLaunchConfig_t c = {};
+            c.gridDim = dim3(S, 1, 1);
+            c.blockDim = dim3(160);
+            c.dynamicSmemBytes = kFusedSmem;
+            cudaLaunchAttribute a[1];
+            a[0].id = cudaLaunchAttributeClusterDimension;
+            a[0].val.clusterDim.x = S;
+            a[0].val.clusterDim.y = 1;
+            a[0].val.clusterDim.z = 1;
+            c.attrs = a;
+            c.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, gqa_fused_kernel, &c) == cudaSuccess && n >= 1) {
+                found = S;
+                break;
+            }
+        }
+    }
+    cudaGetLastError();  // a refused query leaves no sticky error behind
+    if (dev >= 0 && dev < 64) known[dev].store(found, std::memory_order_release);
+    return found > 0 ? found : 0;
+}
+
+// The fused kernel serves calls whose clusters fit in one wave and whose
+// context is short enough that a cluster's CTAs stream it as fast as the
+// three-kernel grid would.  QORA_MIXER_GQA_FUSED=0 turns it off, =1 drops the
+// context limit (tuning and tests).
+constexpr int kFusedAutoMaxTiles = 256;  // L <= 16384
+
+static bool use_fused(qm_ctx* ctx, int B, int nkv, int64_t L, int S) {
+    static const int mode = [] {
+        const char* e = getenv("QORA_MIXER_GQA_FUSED");
+        return e ? atoi(e) : -1;
+    }();
+    if (mode == 0 || S == 0) return false;
+    if ((int64_t)B * nkv * S > ctx->num_sms) return false;
+    return mode == 1 || (L + kTile - 1) / kTile <= kFusedAutoMaxTiles;
+}
+
 cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
                               const float* q_gate, const float* k_new, const float* v_new,
                               float* out, void* ws, size_t ws_bytes, int b0, int nb,
@@ -512,6 +907,45 @@ cudaError_t launch_gqa_decode(qm_ctx* ctx, const qm_gqa_params* prm, qm_kv* kv,
     const int B = nb < 0 ? kv->batch : nb;  // sequences [b0, b0 + B) of the cache
     const int64_t L = kv->seq_len;  // cached positions; the new token goes to index L
     const int nkv = kv->nkv;
+    const int S = fused_splits(ctx);
+    if (use_fused(ctx, B, nkv, L, S)) {
+        const float* c_gate = q_gate;
+        const float* c_v = v_new;
+        if (comb) {
+            if (comb->ready) {
+                const cudaError_t e = cudaStreamWaitEvent(ctx->stream, comb->ready, 0);
+                if (e != cudaSuccess) return e;
+            }
+            c_gate = comb->q_gate ? comb->q_gate : q_gate;
+            c_v = comb->v_new ? comb->v_new : v_new;
+        }
+        const int ntiles = (int)((L + kTile - 1) / kTile);
+        const int tps = (ntiles + S - 1) / S;
+        cudaLaunchAttribute at[2];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = S;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[1].val.programmaticStreamSerializationAllowed = 1;
+        cudaLaunchConfig_t c = {};
+        c.gridDim = dim3(S, nkv, B);
+        c.blockDim = dim3(160);
+        c.dynamicSmemBytes = kFusedSmem;
+        c.stream = ctx->stream;
+        c.attrs = at;
+        c.numAttrs = 2;
+        cudaError_t e;
+        {
+            TimedLaunch tl(ctx, "gqa_fused");
+            e = cudaLaunchKernelEx(&c, gqa_fused_kernel, kv->tmap_k, kv->tmap_v, q_gate, k_new, v_new,
+                                   prm->q_norm, prm->k_norm, prm->rope_cos, prm->rope_sin, L, kv->k, kv->v,
+                                   kv->capacity, c_gate, c_v, out, tps, kv->kv_lo, nkv, b0, ctx->d_err);
+        }
+        if (e == cudaSuccess) e = cudaGetLastError();
+        if (e == cudaSuccess) ctx->launches += 1;
+        return e;
+    }
     const Plan pl = plan_for(B, nkv, L, ctx->num_sms);
     const WsLayout w = ws_layout(kv->batch, nkv, pl.nsplit);  // indexed by absolute sequence
     if (w.total > ws_bytes) return cudaErrorInvalidValue;

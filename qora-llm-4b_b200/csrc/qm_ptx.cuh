@@ -331,5 +331,11 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
     return r;
 }
+// A float in the shared memory of CTA `rank` of this cluster (same offset as p).
+__device__ __forceinline__ float ld_dsmem_f32(const void* p, uint32_t rank) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(mapa_shared(smem_u32(p), rank)));
+    return v;
+}
 
 }  // namespace qm
