@@ -268,6 +268,125 @@ __device__ __forceinline__ void attend_tiles(uint32_t sbase, uint64_t* full, uin
 
 }
 
+// The same attention with the operands swapped, as the fused kernel runs it:
+// per warp and tile, S^T [16 positions x 8] = K [16 x 256] . Q^T, where the 8
+// columns are the 4 heads' q in bf16 hi (columns 0-3) and lo (4-7), so every
+// row of the 16-row MMA is a position (16 MMAs a tile instead of 32), and
+// O^T [256 dims x 8] += V^T [256 x 16 positions] . P^T (16 instead of 32).
+// Lane l holds scores of heads 2(q & 1) + j, j = 0, 1 (q = l & 3) at
+// positions l/4 and l/4 + 8 of its warp's 16, and its O^T accumulator columns
+// 2q, 2q+1 are the hi or lo parts of the same two heads, so the online
+// softmax rescales them in place.  P^T enters the MMA as the B operand: lane
+// l needs P at positions 2q, 2q+1, 2q+8, 2q+9 for column l/4, which 8
+// shuffles collect.  qb are the q B fragments (the same registers as the A
+// fragments of attend_tiles); oc[mt] holds dims 16mt + l/4 (c0, c1) and
+// 16mt + l/4 + 8 (c2, c3), columns 2q, 2q+1.
+__device__ __forceinline__ void attend_tiles_t(uint32_t sbase, uint64_t* full, uint64_t* empty,
+                                               volatile int* abort_flag, int* err, const uint32_t (&qb)[16][2],
+                                               int tile0, int ntiles, int pos_end, int warp, int lane,
+                                               float (&oc)[16][4], float (&m_run)[2], float (&l_run)[2]) {
+    const int quad = lane & 3, g8 = lane >> 2;
+    const int hsel = g8 & 3, hl = g8 >> 2;          // B column of this lane: head, hi (0) / lo (1)
+    const int src_a = (2 * quad) * 4 + (hsel >> 1);  // holder of positions 2q and 2q + 8
+    const int src_b = src_a + 4;                     // holder of positions 2q + 1 and 2q + 9
+    const int krow = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;  // ldmatrix rows (K, A operand)
+    const int kdim = (lane >> 4) * 8;
+    const int vrow = warp * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;  // ldmatrix.trans rows (V^T)
+    const int vdim = ((lane >> 3) & 1) * 8;
+    for (int it = 0; it < ntiles; it++) {
+        const int st = it % kStages, round = it / kStages;
+        const bool ok = mbar_wait_bounded(smem_u32(&full[st]), round & 1, abort_flag, err);
+        if (ok) {
+            const uint32_t kb = sbase + st * kStageBytes;
+            const uint32_t vb = kb + kTileBytes;
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int kk = 0; kk < 16; kk++) {
+                uint32_t r0, r1, r2, r3;
+                ldsm_x4(swz_addr(kb, krow, kk * 16 + kdim), r0, r1, r2, r3);
+                mma_bf16_16816(c, r0, r1, r2, r3, qb[kk][0], qb[kk][1]);
+            }
+            // hi + lo columns (lanes q and q ^ 2); s[j][i]: head 2(q&1)+j, position g8 + 8i
+            float s[2][2];
+            s[0][0] = c[0] + __shfl_xor_sync(0xffffffffu, c[0], 2);
+            s[1][0] = c[1] + __shfl_xor_sync(0xffffffffu, c[1], 2);
+            s[0][1] = c[2] + __shfl_xor_sync(0xffffffffu, c[2], 2);
+            s[1][1] = c[3] + __shfl_xor_sync(0xffffffffu, c[3], 2);
+            const int p0 = (tile0 + it) * kTile + warp * 16 + g8;
+#pragma unroll
+            for (int i = 0; i < 2; i++)
+                if (p0 + 8 * i >= pos_end) s[0][i] = s[1][i] = -INFINITY;
+            float p[2][2], corr[2];
+            bool rescale = false;
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                float tmax = fmaxf(s[j][0], s[j][1]);
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+                const float m_new = fmaxf(m_run[j], tmax);
+                const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+                corr[j] = exp2f((m_run[j] - m_use) * kLog2e);
+                p[j][0] = exp2f((s[j][0] - m_use) * kLog2e);
+                p[j][1] = exp2f((s[j][1] - m_use) * kLog2e);
+                float rs = p[j][0] + p[j][1];
+                rs += __shfl_xor_sync(0xffffffffu, rs, 4);
+                rs += __shfl_xor_sync(0xffffffffu, rs, 8);
+                rs += __shfl_xor_sync(0xffffffffu, rs, 16);
+                l_run[j] = l_run[j] * corr[j] + rs;
+                m_run[j] = m_new;
+                rescale |= corr[j] != 1.0f;
+            }
+            if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+                for (int mt = 0; mt < 16; mt++) {
+                    oc[mt][0] *= corr[0];
+                    oc[mt][1] *= corr[1];
+                    oc[mt][2] *= corr[0];
+                    oc[mt][3] *= corr[1];
+                }
+            }
+            // P^T fragment: column (hsel, hl) at positions 2q, 2q+1 (b0) and 2q+8, 2q+9 (b1)
+            const float a00 = __shfl_sync(0xffffffffu, p[0][0], src_a), a10 = __shfl_sync(0xffffffffu, p[1][0], src_a);
+            const float a01 = __shfl_sync(0xffffffffu, p[0][1], src_a), a11 = __shfl_sync(0xffffffffu, p[1][1], src_a);
+            const float b00 = __shfl_sync(0xffffffffu, p[0][0], src_b), b10 = __shfl_sync(0xffffffffu, p[1][0], src_b);
+            const float b01 = __shfl_sync(0xffffffffu, p[0][1], src_b), b11 = __shfl_sync(0xffffffffu, p[1][1], src_b);
+            const bool odd = hsel & 1;
+            const float pv[4] = {odd ? a10 : a00, odd ? b10 : b00, odd ? a11 : a01, odd ? b11 : b01};
+            uint16_t pb[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint16_t hi = bf16_bits_rn(pv[k]);
+                pb[k] = hl ? bf16_bits_rn(pv[k] - bf16_bits_to_f32(hi)) : hi;
+            }
+            const uint32_t pb0 = pack_bf16(pb[0], pb[1]), pb1 = pack_bf16(pb[2], pb[3]);
+            // rows at or past the end of the range: P is 0 there, but the cache may
+            // hold anything (NaN) and 0 * NaN would poison O, so those V rows become 0
+            const int wpos0 = (tile0 + it) * kTile + warp * 16;
+            if (wpos0 + 16 > pos_end) {
+                for (int e = lane; e < 16 * 32; e += 32) {
+                    const int i = e >> 5, cc = e & 31;
+                    if (wpos0 + i >= pos_end)
+                        asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(
+                                         swz_addr(vb, warp * 16 + i, cc * 8)),
+                                     "r"(0u)
+                                     : "memory");
+                }
+                __syncwarp();
+                fence_proxy_async_shared();  // before TMA refills this stage
+            }
+#pragma unroll
+            for (int mt = 0; mt < 16; mt++) {
+                uint32_t r0, r1, r2, r3;
+                ldsm_x4_t(swz_addr(vb, vrow, mt * 16 + vdim), r0, r1, r2, r3);
+                mma_bf16_16816(oc[mt], r0, r1, r2, r3, pb0, pb1);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty[st]));
+    }
+}
+
 __global__ void __launch_bounds__(160, 1)
 gqa_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                 const uint16_t* __restrict__ q_bf, float* __restrict__ part_o,
@@ -525,10 +644,11 @@ gqa_combine_kernel(const float* __restrict__ q_f32, const float* __restrict__ kn
 // A cluster of nsplit CTAs (grid.x, up to 16) owns one (sequence, KV head);
 // CTA r streams tiles [r*tps, (r+1)*tps) like gqa_attn, computes the 4 query
 // heads' q itself (RMSNorm(1+g), RoPE, 1/16) and keeps its merged partial in
-// shared memory.  After a cluster barrier, CTA r produces outputs
-// [r*1024/nsplit, (r+1)*1024/nsplit) of the group's 4 x 256 by reading every
-// CTA's partial through distributed shared memory, adding the new token in
-// f32 and the sigmoid gate.  CTA 0 appends the new k/v.  No workspace.
+// shared memory.  CTA r owns outputs [r*1024/nsplit, (r+1)*1024/nsplit) of
+// the group's 4 x 256: every CTA stores its partial of those outputs (and
+// its per-head maximum and sum) into CTA r's shared memory, and after one
+// cluster barrier CTA r merges them, adds the new token in f32 and applies
+// the sigmoid gate.  CTA 0 appends the new k/v.  No workspace.
 //
 // Launched with programmatic stream serialisation, and it lets its successor
 // start once it has itself waited for its predecessor: a successor that is
@@ -537,13 +657,14 @@ gqa_combine_kernel(const float* __restrict__ q_f32, const float* __restrict__ kn
 // append of a call on the same cache); that tile and every input are read
 // only after the successor's own wait, i.e. after this grid has completed.
 // ---------------------------------------------------------------------------
+constexpr int kFusedMaxSplit = 16;                 // CTAs per cluster at most
+constexpr int kQbRow = kD + 8;                     // bf16 q row, padded: conflict-free fragment loads
 constexpr int kFzQ = kStages * kStageBytes;        // q of the 4 heads, f32 [4][256]
-constexpr int kFzKn = kFzQ + kGroup * kD * 4;      // the new token's normed k, f32 [256]
-constexpr int kFzRes = kFzKn + kD * 4;             // this CTA's partial o [4][256]
-constexpr int kFzMl = kFzRes + kGroup * kD * 4;    // its m [4], l [4], then q.k_new [4]
-constexpr int kFzBars = kFzMl + 16 * 4;
+constexpr int kFzQb = kFzQ + kGroup * kD * 4;      // q as bf16 hi / lo [4 heads][2][kQbRow]
+constexpr int kFzRecv = kFzQb + kGroup * 2 * kQbRow * 2;  // received partials [nsplit][1024 / nsplit]
+constexpr int kFzMl = kFzRecv + kGroup * kD * 4;   // received (m, l) [16][2], then q.k_new [4]
+constexpr int kFzBars = kFzMl + (2 * kFusedMaxSplit + 4) * 4;
 constexpr int kFusedSmem = kFzBars + 2 * kStages * 8 + 16 + 1024 /*align*/;
-constexpr int kFusedMaxSplit = 16;
 // outputs per consumer thread after the merge: 4 x 256 / (nsplit x 128), nsplit >= 2
 constexpr int kFusedPerThread = 4;
 
@@ -559,11 +680,10 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     float* q_s = reinterpret_cast<float*>(smem + kFzQ);
-    float* kn_s = reinterpret_cast<float*>(smem + kFzKn);
-    float* res_o = reinterpret_cast<float*>(smem + kFzRes);
-    float* res_m = reinterpret_cast<float*>(smem + kFzMl);
-    float* res_l = res_m + kGroup;
-    float* s_new = res_l + kGroup;
+    uint16_t* q_b = reinterpret_cast<uint16_t*>(smem + kFzQb);
+    float* recv_o = reinterpret_cast<float*>(smem + kFzRecv);
+    float* recv_ml = reinterpret_cast<float*>(smem + kFzMl);
+    float* s_new = recv_ml + 2 * kFusedMaxSplit;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kFzBars);
     uint64_t* empty = full + kStages;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kStages);
@@ -588,6 +708,9 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         fence_barrier_init();
     }
     __syncthreads();
+    // every CTA of the cluster has started before any stores into another's
+    // shared memory (the matching wait comes just before the first such store)
+    cluster_arrive_relaxed();
     const uint32_t sbase = smem_u32(smem);
 
     if (warp == kGroup) {
@@ -637,8 +760,18 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             const float x1 = x[0], x2 = x[1];
             x[0] = x1 * c - x2 * s;
             x[1] = x2 * c + x1 * s;
+            // the new token's score q . k_new (f32) of the 4 heads, once their q is in
+            // shared memory (the consumers arrive on barrier 2 after writing it)
+            named_bar_sync(2, 5 * 32);
 #pragma unroll
-            for (int i = 0; i < 8; i++) kn_s[lane + 32 * i] = x[i];
+            for (int h = 0; h < kGroup; h++) {
+                float prod = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; i++) prod = fmaf(q_s[h * kD + lane + 32 * i], x[i], prod);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) prod += __shfl_xor_sync(0xffffffffu, prod, o);
+                if (lane == 0) s_new[h] = prod;
+            }
             if (split == 0) {
                 const size_t row = (((size_t)b * nkv + gl) * cap + pos) * kD;
                 const float* vs = v_new + ((size_t)b * kNumKVH + g) * kD;
@@ -663,8 +796,23 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
                 mbar_wait_bounded(smem_u32(&full[j % kStages]), (j / kStages) & 1, abort_flag, err);
         }
         __syncwarp();
+        cluster_wait();
     } else {
         // ---------------- consumers ----------------
+        {   // warm L2 with this call's small inputs before the wait (a prefetch
+            // reads nothing into registers, so it cannot see stale data)
+            const int t = threadIdx.x;
+            const float* qg = q_gate + ((size_t)b * kNumH + g * kGroup) * 2 * kD;  // 4 heads, 8 KB
+            if (t < 64) prefetch_l2(qg + t * 32);
+            else if (t < 72) prefetch_l2(q_norm + (t - 64) * 32);
+            else if (t < 80) prefetch_l2(k_norm + (t - 72) * 32);
+            else if (t < 88) prefetch_l2(k_new + ((size_t)b * kNumKVH + g) * kD + (t - 80) * 32);
+            else if (t < 96) prefetch_l2(c_v + ((size_t)b * kNumKVH + g) * kD + (t - 88) * 32);
+            else if (t == 96) prefetch_l2(rope_cos + pos * kHalfRot);
+            else if (t == 97) prefetch_l2(rope_sin + pos * kHalfRot);
+            else if (c_gate != q_gate && t < 98 + 32)
+                prefetch_l2(c_gate + ((size_t)b * kNumH + g * kGroup + (t - 98) / 8) * 2 * kD + kD + ((t - 98) % 8) * 32);
+        }
         pdl_wait();  // q comes from the preceding kernel
         pdl_launch_dependents();
         // the gate logit and new v of the outputs this thread produces after
@@ -700,61 +848,66 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             x[0] = x1 * c - x2 * s;
             x[1] = x2 * c + x1 * s;
 #pragma unroll
-            for (int i = 0; i < 8; i++) q_s[warp * kD + lane + 32 * i] = x[i] * 0.0625f;
-        }
-        named_bar_sync(1, kGroup * 32);
-        const int row = lane >> 2, quad = lane & 3;
-        uint32_t qa[16][2];
-        {
-            const int head = row & 3, hl = row >> 2;
-            const float* qr = q_s + head * kD;
-            auto part = [&](int e) -> uint32_t {  // bf16 hi (hl 0) or lo (hl 1) of q[e], q[e+1]
-                uint16_t r[2];
-#pragma unroll
-                for (int j = 0; j < 2; j++) {
-                    const float qs = qr[e + j];
-                    const uint16_t hi = bf16_bits_rn(qs);
-                    r[j] = hl ? bf16_bits_rn(qs - bf16_bits_to_f32(hi)) : hi;
-                }
-                return pack_bf16(r[0], r[1]);
-            };
-#pragma unroll
-            for (int kk = 0; kk < 16; kk++) {
-                qa[kk][0] = part(kk * 16 + quad * 2);
-                qa[kk][1] = part(kk * 16 + 8 + quad * 2);
+            for (int i = 0; i < 8; i++) {
+                const int e = lane + 32 * i;
+                const float qs = x[i] * 0.0625f;  // scale 1/sqrt(256), exact
+                const uint16_t hi = bf16_bits_rn(qs);
+                q_s[warp * kD + e] = qs;
+                q_b[(warp * 2 + 0) * kQbRow + e] = hi;
+                q_b[(warp * 2 + 1) * kQbRow + e] = bf16_bits_rn(qs - bf16_bits_to_f32(hi));
             }
         }
-        float o[32][2];
+        named_bar_sync(1, kGroup * 32);
+        asm volatile("bar.arrive 2, %0;" ::"n"(5 * 32) : "memory");  // q_s is ready for the producer warp
+        const int row = lane >> 2, quad = lane & 3;
+        uint32_t qa[16][2];
+        {   // column row & 3 (head), hi (row < 4) or lo
+            const uint16_t* qr = q_b + ((row & 3) * 2 + (row >> 2)) * kQbRow;
 #pragma unroll
-        for (int n = 0; n < 32; n++) o[n][0] = o[n][1] = 0.f;
-        float m_run = -INFINITY, l_run = 0.f;
-        attend_tiles(sbase, full, empty, abort_flag, err, qa, tile0, ntiles, pos_end, warp, lane, o, m_run,
-                     l_run);
-        // fold lo rows into hi rows; merge the 4 warps (stage buffers reused)
-#pragma unroll
-        for (int n = 0; n < 32; n++) {
-            o[n][0] += __shfl_xor_sync(0xffffffffu, o[n][0], 16);
-            o[n][1] += __shfl_xor_sync(0xffffffffu, o[n][1], 16);
+            for (int kk = 0; kk < 16; kk++) {
+                qa[kk][0] = *reinterpret_cast<const uint32_t*>(qr + kk * 16 + quad * 2);
+                qa[kk][1] = *reinterpret_cast<const uint32_t*>(qr + kk * 16 + 8 + quad * 2);
+            }
         }
+        float oc[16][4];
+#pragma unroll
+        for (int mt = 0; mt < 16; mt++) oc[mt][0] = oc[mt][1] = oc[mt][2] = oc[mt][3] = 0.f;
+        float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+        attend_tiles_t(sbase, full, empty, abort_flag, err, qa, tile0, ntiles, pos_end, warp, lane, oc, m_run,
+                       l_run);
+        // hi + lo columns: lanes q and q ^ 2 (q < 2 keeps the sums)
+#pragma unroll
+        for (int mt = 0; mt < 16; mt++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) oc[mt][k] += __shfl_xor_sync(0xffffffffu, oc[mt][k], 2);
         named_bar_sync(1, kGroup * 32);  // all consumers are done with the stage buffers
-        // the 4 warps' partials, rows padded by 8 floats so the 16 lanes'
-        // float2 stores fall on distinct banks
+        // the 4 warps' partials, rows padded by 8 floats so a store instruction's
+        // 16 lanes (4 heads' rows apart) fall on distinct banks
         constexpr int kRow = kD + 8;
         float* mo = reinterpret_cast<float*>(smem);  // [4 warps][4 heads][kRow]
         float* mm = mo + kGroup * kGroup * kRow;     // [4][4]
         float* ml = mm + kGroup * kGroup;            // [4][4]
         float* sc = ml + kGroup * kGroup;            // [4][4] scale of warp w's partial of head h
-        if (lane < 16) {
-            const int head = lane >> 2;
-            float* dst = mo + (warp * kGroup + head) * kRow + quad * 2;
+        if (quad < 2) {  // heads 2q, 2q + 1 at dims 16mt + lane/4 (+8)
+            const int g8 = lane >> 2;
+            float* d0 = mo + (warp * kGroup + 2 * quad) * kRow + g8;
+            float* d1 = d0 + kRow;
 #pragma unroll
-            for (int n = 0; n < 32; n++) *reinterpret_cast<float2*>(dst + n * 8) = make_float2(o[n][0], o[n][1]);
-            if (quad == 0) {
-                mm[warp * kGroup + head] = m_run;
-                ml[warp * kGroup + head] = l_run;
+            for (int mt = 0; mt < 16; mt++) {
+                d0[mt * 16] = oc[mt][0];
+                d1[mt * 16] = oc[mt][1];
+                d0[mt * 16 + 8] = oc[mt][2];
+                d1[mt * 16 + 8] = oc[mt][3];
+            }
+            if (g8 == 0) {
+                mm[warp * kGroup + 2 * quad] = m_run[0];
+                mm[warp * kGroup + 2 * quad + 1] = m_run[1];
+                ml[warp * kGroup + 2 * quad] = l_run[0];
+                ml[warp * kGroup + 2 * quad + 1] = l_run[1];
             }
         }
         named_bar_sync(1, kGroup * 32);
+        cluster_wait();
         const int t = threadIdx.x;  // 0..127
         if (t < kGroup) {  // head t: the CTA's maximum, sum and the 4 warps' scales
             float M = -INFINITY;
@@ -768,10 +921,13 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
                 sc[w * kGroup + t] = f;
                 lsum += f * ml[w * kGroup + t];
             }
-            res_m[t] = M;
-            res_l[t] = (M == -INFINITY) ? 0.f : lsum;
+            // (m, l) of head t to the CTAs that own its outputs
+            for (int r = t * kD / per; r < (t + 1) * kD / per; r++)
+                st_dsmem_v2(recv_ml + 2 * split, (uint32_t)r, M, (M == -INFINITY) ? 0.f : lsum);
         }
         named_bar_sync(1, kGroup * 32);
+        // this CTA's merged partial: output idx goes to CTA idx / per, which
+        // receives every CTA's partial of its outputs [nsplit][per]
 #pragma unroll
         for (int e = 0; e < (kGroup * kD) / 128; e++) {
             const int idx = e * 128 + t;
@@ -779,20 +935,11 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             float acc = 0.f;
 #pragma unroll
             for (int w = 0; w < kGroup; w++) acc = fmaf(sc[w * kGroup + head], mo[(w * kGroup + head) * kRow + d], acc);
-            res_o[head * kD + d] = acc;
+            st_dsmem_f32(recv_o + split * per + idx % per, (uint32_t)(idx / per), acc);
         }
     }
-    // every CTA's partial (and this CTA's q and new k) is complete
+    // every CTA's pushes have landed (and s_new, written by the producer warp, is visible)
     cluster_sync_all();
-    if (warp < kGroup) {  // the new token's score for head `warp`: q . k_new in f32
-        float prod = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; i++) prod = fmaf(q_s[warp * kD + lane + 32 * i], kn_s[lane + 32 * i], prod);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) prod += __shfl_xor_sync(0xffffffffu, prod, o);
-        if (lane == 0) s_new[warp] = prod;
-    }
-    __syncthreads();
     // outputs [split*per, (split+1)*per) of the group's 4 x 256, thread t
     // taking t, t + 128, ...: merge the nsplit partials, add the new token,
     // apply the gate (gemv.rs:1008-1011)
@@ -804,35 +951,29 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             const int idx = split * per + oi;
             const int head = idx / kD, d = idx % kD;
             const float sn = s_new[head];
-            float mi[kFusedMaxSplit], oi_v[kFusedMaxSplit], li[kFusedMaxSplit];
+            float M = sn;
+            float mi[kFusedMaxSplit], li[kFusedMaxSplit], ov[kFusedMaxSplit];
 #pragma unroll
             for (int i = 0; i < kFusedMaxSplit; i++) {
-                if (i < nsplit) {
-                    mi[i] = ld_dsmem_f32(res_m + head, (uint32_t)i);
-                    li[i] = ld_dsmem_f32(res_l + head, (uint32_t)i);
-                    oi_v[i] = ld_dsmem_f32(res_o + head * kD + d, (uint32_t)i);
-                } else {
-                    mi[i] = -INFINITY;
-                    li[i] = oi_v[i] = 0.f;
-                }
+                const bool in = i < nsplit;
+                mi[i] = in ? recv_ml[2 * i] : -INFINITY;
+                li[i] = in ? recv_ml[2 * i + 1] : 0.f;
+                ov[i] = in ? recv_o[i * per + oi] : 0.f;
+                M = fmaxf(M, mi[i]);
             }
-            float M = sn;
-#pragma unroll
-            for (int i = 0; i < kFusedMaxSplit; i++) M = fmaxf(M, mi[i]);
             const float wn = exp2f((sn - M) * kLog2e);
             float acc = wn * red_v[u];
             float lsum = wn;
 #pragma unroll
             for (int i = 0; i < kFusedMaxSplit; i++) {
                 const float f = (mi[i] == -INFINITY) ? 0.f : exp2f((mi[i] - M) * kLog2e);
-                acc = fmaf(f, oi_v[i], acc);
+                acc = fmaf(f, ov[i], acc);
                 lsum = fmaf(f, li[i], lsum);
             }
             out[(((size_t)b * nkv + gl) * kGroup + head) * kD + d] =
                 (acc / lsum) * (1.0f / (1.0f + __expf(-red_gate[u])));
         }
     }
-    cluster_sync_all();  // no CTA leaves while another reads its shared memory
 }
 
 }  // namespace

@@ -126,6 +126,11 @@ __device__ __forceinline__ bool in_bounds_rec(size_t off, size_t n, size_t size,
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Brings the 128-byte line holding p into L2 (no register result, no ordering).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -155,6 +160,16 @@ __device__ __forceinline__ void mma_bf16_top(float& d0, float& d1, uint32_t a0, 
         : "=f"(d0), "=f"(d1)
         : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(d0), "f"(d1), "f"(0.f),
           "f"(0.f));
+}
+
+// D += A(16x16) * B(16x8), bf16 inputs, f32 accumulate, all 16 rows.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
+        "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ uint16_t bf16_bits_rn(float x) {
@@ -325,11 +340,24 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// The two halves of cluster_sync_all, for code that arrives early and waits later.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 // The shared::cluster address of `addr` (a shared::cta address) in CTA `rank`.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
     uint32_t r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
     return r;
+}
+// Stores into the shared memory of CTA `rank` of this cluster (same offset as p).
+__device__ __forceinline__ void st_dsmem_f32(void* p, uint32_t rank, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(mapa_shared(smem_u32(p), rank)), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_dsmem_v2(void* p, uint32_t rank, float a, float b) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(mapa_shared(smem_u32(p), rank)), "f"(a), "f"(b)
+                 : "memory");
 }
 // A float in the shared memory of CTA `rank` of this cluster (same offset as p).
 __device__ __forceinline__ float ld_dsmem_f32(const void* p, uint32_t rank) {
