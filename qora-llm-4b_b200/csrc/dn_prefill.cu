@@ -40,6 +40,8 @@ namespace qm {
 
 int encode_rows_tmap(CUtensorMap* m, void* base, uint64_t inner, uint64_t rows, uint64_t planes,
                      uint32_t box_inner, uint32_t box_rows, bool fp16);
+int encode_f32_tmap(CUtensorMap* m, void* base, uint64_t inner, uint64_t rows, uint64_t planes,
+                    uint32_t box_inner, uint32_t box_rows);
 
 namespace {
 
@@ -180,13 +182,8 @@ __global__ void dn_conv_ring(const uint16_t* __restrict__ qkv, float* __restrict
 // ---------------------------------------------------------------------------
 // chunk kernels
 // ---------------------------------------------------------------------------
-constexpr uint32_t kNegA = 1u << 13;
 constexpr uint32_t kIdKK = umma_idesc_f16kind(128, 64, false, false, false);   // A K, B K
 constexpr uint32_t kIdW = umma_idesc_f16kind(128, 64, true, false, false);     // A MN, B K
-constexpr uint32_t kIdSW = umma_idesc_f16kind(128, 64, false, true, false) | kNegA;  // -A . B(MN)
-constexpr uint32_t kIdSQ = umma_idesc_f16kind(128, 64, false, false, false);
-constexpr uint32_t kIdUP = umma_idesc_f16kind(128, 64, false, false, false);
-constexpr uint32_t kIdUK = umma_idesc_f16kind(128, 128, false, true, false);   // A K, B MN
 
 __device__ __forceinline__ uint32_t h2bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
@@ -306,9 +303,10 @@ struct ChunkBars {
 //   MMA3  U~^T = V^T (T diag(b))^T        (compensated)
 // written to the workspace for the state pass: W^T fp16 [128 k][64 t],
 // U~^T f32 as [16][128 v][4] (float4 of 4 tokens per v, so the state pass
-// loads it with one bulk copy and reads it conflict-free), P' fp16 hi/lo
-// [64 t][64 s], and the decayed operands of the state products
-// Q~_t = e^G_t q_t (fp16) and K~_s = e^(G_63 - G_s) k_s (fp16 hi/lo), [64][128].
+// loads it with one bulk copy and reads it conflict-free) and P' fp16 hi/lo
+// [64 t][64 s]: 64 KB per (chunk, V head).  The decayed q and k the state
+// pass needs are formed there from the prep kernel's tiles, which the two V
+// heads of a QK head share in L2.
 // 102 KB of shared memory and 256 TMEM columns: two CTAs per SM.  Warps w and
 // w+4 share TMEM lane quarter w%4 and split the 64 columns of every TMEM tile.
 constexpr int kL_KQh = 0;              // [K;Q] hi: 2 boxes [128 rows x 64] fp16 (K rows 0-63,
@@ -334,9 +332,7 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
                const __grid_constant__ CUtensorMap tvh, const __grid_constant__ CUtensorMap tvl,
                const float* __restrict__ gin, const float* __restrict__ bin, int T, int nch,
                uint16_t* __restrict__ wt_out, float* __restrict__ ut_out,
-               uint16_t* __restrict__ ph_out, uint16_t* __restrict__ pl_out,
-               uint16_t* __restrict__ qt_out, uint16_t* __restrict__ kth_out,
-               uint16_t* __restrict__ ktl_out, int* err) {
+               uint16_t* __restrict__ ph_out, uint16_t* __restrict__ pl_out, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     float* sG = reinterpret_cast<float*>(smem + kL_Misc);
@@ -469,42 +465,6 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
             }
         }
     }
-    // ---- Q~ = e^G q (fp16) and K~ = e^(G63-G) k (fp16 hi/lo), from the hi/lo tiles ----
-    if (ok && QM_IN(item * kC * kHd, kC * kHd, (size_t)gridDim.x * gridDim.y * gridDim.z * kC * kHd, err)) {
-        const size_t rowbase = item * kC;
-#pragma unroll 2
-        for (int m = 0; m < 1024 / kLocalThreads; m++) {
-            const int o = tid + kLocalThreads * m, t = o >> 4, kc = o & 15;
-            const uint32_t off = (kc >> 3) * 16384 + sw128_off(t, kc & 7);
-            float v[8];
-            // Q rows sit 8 KB into each box
-            uint4 h = *reinterpret_cast<const uint4*>(smem + kL_KQh + 8192 + off);
-            uint4 l = *reinterpret_cast<const uint4*>(smem + kL_KQl + 8192 + off);
-            const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&hw[i]));
-                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&lw[i]));
-                v[2 * i] = (a.x + b.x) * eG[t];
-                v[2 * i + 1] = (a.y + b.y) * eG[t];
-            }
-            reinterpret_cast<uint4*>(qt_out + (rowbase + t) * kHd)[kc] = round8(v);
-            h = *reinterpret_cast<const uint4*>(smem + kL_KQh + off);
-            l = *reinterpret_cast<const uint4*>(smem + kL_KQl + off);
-            const uint32_t hk[4] = {h.x, h.y, h.z, h.w}, lk[4] = {l.x, l.y, l.z, l.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&hk[i]));
-                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&lk[i]));
-                v[2 * i] = (a.x + b.x) * eD[t];
-                v[2 * i + 1] = (a.y + b.y) * eD[t];
-            }
-            uint4 kh4, kl4;
-            split8(v, kh4, kl4);
-            reinterpret_cast<uint4*>(kth_out + (rowbase + t) * kHd)[kc] = kh4;
-            reinterpret_cast<uint4*>(ktl_out + (rowbase + t) * kHd)[kc] = kl4;
-        }
-    }
     tc_fence_before();
     __syncthreads();
 
@@ -633,69 +593,131 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
     }
 }
 
-// ---- 2b. state pass: one CTA (128 threads, lane = v row) per (V head, sequence) ----
+// ---- 2b. state pass: one CTA per (V head, sequence), 8 warps ----
 //
-// Per chunk c, with S0 the state entering it (f32 master in TMEM, fp16 copy in
-// shared memory as the A operand), Q~ = e^G Q and K~ = e^(G63-G) K:
-//   MMA4  U_acc = -S0 W^T                    MMA5  Y[c&1] = S0 Q~^T  (fp16)
-//   U = U~ + U_acc (f32) -> fp16 hi/lo
-//   MMA7  dS = U^T K~   (compensated)        MMA6  Y[c&1] += U^T P'^T (compensated)
-//   S_master = e^G63 S_master + dS (f32), and its fp16 copy for chunk c+1
-// The dependency chain per chunk is S copy -> MMA4 -> U -> MMA7 -> S copy;
-// MMA5, MMA6 and the output of chunk c-1 (y = Y[(c-1)&1], read while MMA7
-// runs) stay off it.  W^T, Q~ and U~ (one untiled bulk copy) are refetched
-// for chunk c+1 as soon as MMA4/MMA5 and the U step are done, K~ after MMA7,
-// and P' is double-buffered; the gates of chunk c+1 are read into registers
-// during chunk c.
-constexpr int kS_S0 = 0;            // S0 fp16 [128 v x 128 k]: 2 boxes [128 x 64]
-constexpr int kS_W = 32768;         // W^T [128 k x 64 t] fp16 (16 KB)
-constexpr int kS_Q = 49152;         // Q~ [64 t x 128 k] fp16: 2 boxes [64 x 64] (16 KB)
-constexpr int kS_Ut = 65536;        // U~^T f32 [16][128 v][4] (32 KB)
-constexpr int kS_P = 98304;         // P' hi, lo [64 t x 64 s] (8 KB each), x2 buffers (32 KB)
-constexpr int kS_Kh = 131072;       // K~ hi [64 s x 128 k]: 2 boxes [64 x 64]
-constexpr int kS_Kl = 147456;
-constexpr int kS_Uh = 163840;       // U^T hi [128 v x 64 s]
-constexpr int kS_Ul = 180224;
-constexpr int kS_Misc = 196608;     // [2] x (G, eG, eD, g): 8 x 64 f32; barriers
-constexpr int kStateSmem = kS_Misc + 8 * 64 * 4 + 128 + 1024;
-constexpr uint32_t kTmU2 = 0, kTmY = 64 /* x2 */, kTmDS = 256, kTmS = 384;
+// Per chunk c, with S0 the state entering it (f32 master in TMEM, and an fp16
+// copy in TMEM as the A operand), G the in-chunk cumulative log-decay,
+// D_s = e^(G63 - G_s) and q, k the prep kernel's fp16 hi/lo tiles:
+//   MMA4  U = U~ - S0 W^T  (U~ preloaded into U2[c&1])
+//   MMA7  S += (U diag D)^T k  (compensated; S pre-scaled by e^G63)
+//   MMA5  Y1 = S0 q_hi^T       MMA6  Y2 = U^T P'^T (compensated)
+//   y_t = e^G_t Y1_t + Y2_t;   S0 (fp16, TMEM buffer (c+1)&1) = S
+// The decays fold into the operands the chain already touches (the U step
+// scales U's columns before splitting it into fp16 hi/lo, the readout
+// scales Y1), so q and k are used as the prep kernel wrote them.
+// Warps 0-3 (lane = v row) run the chain MMA4 -> U step -> MMA7 -> S pass
+// (the fp16 S0 of the next chunk, and S scaled by that chunk's e^G63 for its
+// MMA7, in one read of S); thread 0 issues MMA4, MMA7 and the W^T and k
+// loads.  Warps 4-7 run beside it: each chunk's decays, U~ of the next chunk
+// into TMEM, the unscaled U hi/lo for MMA6, and y (staged in shared memory,
+// one TMA store per chunk); their thread 128 issues MMA5 / MMA6 and the q
+// and P' loads.  mbarriers hand over: u2_ready, dec_ready (warps 4-7 ->
+// thread 0); u_ready, s_read (thread 0 -> warps 4-7).
+constexpr int kS_W = 0;             // W^T [128 k x 64 t] fp16, x2 buffers (32 KB)
+constexpr int kS_Q = 32768;         // q hi [64 t x 128 k] fp16: 2 boxes [64 x 64], x2 buffers (32 KB)
+constexpr int kS_P = 65536;         // P' hi, lo [64 t x 64 s] (8 KB each) (16 KB)
+constexpr int kS_K = 81920;         // k hi, lo [64 s x 128 k] (16 KB each), x2 buffers (64 KB)
+constexpr int kS_Us = 147456;       // (U diag D)^T hi, lo [128 v x 64 s] (16 KB each)
+constexpr int kS_Uu = 180224;       // U^T hi, lo (16 KB each); y [64 t][128 v] f32 after MMA6
+constexpr int kS_Misc = 212992;     // [2] x (g, G, eG, eD): 8 x 64 f32; barriers
+constexpr int kStateSmem = kS_Misc + 8 * 64 * 4 + 256 + 1024;
+// TMEM columns: S f32 [0,128), S0 fp16 pairs x2 [128,256), U2 f32 x2 [256,384), Y1 [384,448), Y2 [448,512)
+constexpr uint32_t kTmS = 0, kTmS0h = 128, kTmU2 = 256, kTmY1 = 384, kTmY2 = 448;
+constexpr uint32_t kNegB = 1u << 14;
+constexpr uint32_t kIdSW = umma_idesc_f16kind(128, 64, false, true, false) | kNegB;  // A tmem, -B(MN)
+constexpr uint32_t kIdSQ = umma_idesc_f16kind(128, 64, false, false, false);
+constexpr uint32_t kIdUP = umma_idesc_f16kind(128, 64, false, false, false);
+constexpr uint32_t kIdUK = umma_idesc_f16kind(128, 128, false, true, false);   // A K, B MN
 
-struct StateBars {
-    uint64_t wqu_full, k_full, p_full[2], m4, m5, m7, mY;
+struct StateBars {  // the first 11 words are tracked by Pending (in this order)
+    uint64_t w_full[2], q_full[2], k_full[2], p_full;  // TMA
+    uint64_t m4, m7, mY, spare;                        // MMA completions
+    uint64_t u2_ready, dec_ready;                      // warps 4-7 -> thread 0 (128 arrivals)
+    uint64_t u_ready, s_read;                          // thread 0 -> warps 4-7 (1 arrival)
     uint32_t tmem_base;
     int abort_flag;
 };
 
-__global__ void __launch_bounds__(128, 1)
+// bar.red.and over named barrier `id` of `count` threads
+__device__ __forceinline__ bool named_bar_and(int id, int count, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
+// The issuing thread's record of barrier phases it started and has not yet
+// seen complete (one bit per barrier among the first 11 words of StateBars),
+// drained on the way out so nothing lands after the CTA ends.
+struct Pending {
+    uint64_t* base;
+    uint32_t out = 0, par = 0;
+    __device__ explicit Pending(uint64_t* b) : base(b) {}
+    __device__ void start(uint64_t* b, uint32_t parity) {
+        const uint32_t bit = 1u << (uint32_t)(b - base);
+        out |= bit;
+        par = parity ? (par | bit) : (par & ~bit);
+    }
+    __device__ void seen(uint64_t* b) { out &= ~(1u << (uint32_t)(b - base)); }
+    __device__ void drain() {
+        for (int i = 0; i < 11; i++)
+            if (out & (1u << i)) mbar_drain(smem_u32(base + i), (par >> i) & 1u);
+    }
+};
+
+// U (64 f32 of one v row, token order) -> fp16 hi/lo, K-major swizzled rows
+__device__ __forceinline__ void store_u_split(uint8_t* smem_hi, uint8_t* smem_lo, int row, const float* u) {
+#pragma unroll
+    for (int s = 0; s < kC; s += 8) {
+        uint4 h, l;
+        split8(u + s, h, l);
+        *reinterpret_cast<uint4*>(smem_hi + sw128_off(row, s >> 3)) = h;
+        *reinterpret_cast<uint4*>(smem_lo + sw128_off(row, s >> 3)) = l;
+    }
+}
+
+constexpr int kStateThreads = 256;  // warps 0-3: the recurrence; 4-7: beside it
+
+__global__ void __launch_bounds__(kStateThreads, 1)
 dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ CUtensorMap tph,
-               const __grid_constant__ CUtensorMap tpl, const __grid_constant__ CUtensorMap tqt,
-               const __grid_constant__ CUtensorMap tkth, const __grid_constant__ CUtensorMap tktl,
+               const __grid_constant__ CUtensorMap tpl, const __grid_constant__ CUtensorMap tqh,
+               const __grid_constant__ CUtensorMap tkh, const __grid_constant__ CUtensorMap tkl,
+               const __grid_constant__ CUtensorMap tyo,
                const float* __restrict__ ut_in, const float* __restrict__ gin,
-               float* __restrict__ S, float* __restrict__ y, int T, int nch, int* err) {
+               float* __restrict__ S, int T, int nch, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    float* misc = reinterpret_cast<float*>(smem + kS_Misc);
-    // per chunk parity p: sG = misc + p*256, eG = +64, eD = +128, sg = +192
+    float* misc = reinterpret_cast<float*>(smem + kS_Misc);  // slot s: g, G, eG, eD at misc + 256 s
     StateBars* bars = reinterpret_cast<StateBars*>(misc + 8 * 64);
     volatile int* abort_flag = &bars->abort_flag;
     const uint32_t sb = smem_u32(smem);
 
     const int vh = blockIdx.x, b = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
-    const int row = tid;  // TMEM lane = v row
+    const int row = tid & 127;  // TMEM lane = v row
+    const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
     const size_t plane_v = (size_t)b * kNumV + vh;
+    const int plane_qk = b * kNumQK + (vh >> 1);  // the prep kernel's q/k planes
     const size_t item0 = plane_v * nch;
 
     if (tid == 0) {
-        mbar_init(smem_u32(&bars->wqu_full), 1);
-        mbar_init(smem_u32(&bars->k_full), 1);
-        mbar_init(smem_u32(&bars->p_full[0]), 1);
-        mbar_init(smem_u32(&bars->p_full[1]), 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(smem_u32(&bars->w_full[i]), 1);
+            mbar_init(smem_u32(&bars->q_full[i]), 1);
+            mbar_init(smem_u32(&bars->k_full[i]), 1);
+        }
+        mbar_init(smem_u32(&bars->p_full), 1);
         mbar_init(smem_u32(&bars->m4), 1);
-        mbar_init(smem_u32(&bars->m5), 1);
         mbar_init(smem_u32(&bars->m7), 1);
         mbar_init(smem_u32(&bars->mY), 1);
+        mbar_init(smem_u32(&bars->u2_ready), 128);
+        mbar_init(smem_u32(&bars->dec_ready), 128);
+        mbar_init(smem_u32(&bars->u_ready), 1);
+        mbar_init(smem_u32(&bars->s_read), 1);
         bars->abort_flag = 0;
         fence_barrier_init();
     }
@@ -707,254 +729,188 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = bars->tmem_base;
-
-    // thread 0's record of the last phase it started on each barrier and not
-    // yet seen complete (drained on the way out of an aborted CTA)
-    bool out_[8] = {false, false, false, false, false, false, false, false};
-    uint32_t par_[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    uint64_t* const bar_list[8] = {&bars->wqu_full, &bars->k_full, &bars->p_full[0], &bars->p_full[1],
-                                   &bars->m4, &bars->m5, &bars->m7, &bars->mY};
-    auto started = [&](int i, int c) { out_[i] = true; par_[i] = (uint32_t)c & 1; };
-    auto seen = [&](int i) { out_[i] = false; };
-    enum { kWqu = 0, kK = 1, kP0 = 2, kM4 = 4, kM5 = 5, kM7 = 6, kMY = 7 };
-
-    auto issue_wqu = [&](int c) {  // W^T, Q~ and U~^T of chunk c
-        const uint32_t fb = smem_u32(&bars->wqu_full);
-        started(kWqu, c);
-        mbar_arrive_expect_tx(fb, 16384 + 16384 + 32768);
-        tma_load_3d(sb + kS_W, &twt, 0, 0, (int)(item0 + c), fb);
-        for (int hb = 0; hb < 2; hb++)
-            tma_load_3d(sb + kS_Q + hb * 8192, &tqt, hb * 64, 0, (int)(item0 + c), fb);
-        if (QM_IN((item0 + c) * kHd * kC, kHd * kC, (size_t)gridDim.x * gridDim.y * nch * kHd * kC, err))
-            bulk_load(sb + kS_Ut, ut_in + (item0 + c) * kHd * kC, 32768, fb);
+    Pending pend(&bars->w_full[0]);
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+        const bool w = mbar_wait_bounded(smem_u32(bar), parity, abort_flag, err);
+        if (w) pend.seen(bar);
+        return w;
     };
-    auto issue_k = [&](int c) {  // K~ hi/lo of chunk c
-        const uint32_t fb = smem_u32(&bars->k_full);
-        started(kK, c);
-        mbar_arrive_expect_tx(fb, 16384 * 2);
+
+    // ---- loads (thread 0: W^T, k; thread 128: q, P') ----
+    auto issue_w = [&](int c) {  // W^T of chunk c into buffer c & 1
+        uint64_t* fb = &bars->w_full[c & 1];
+        pend.start(fb, (c >> 1) & 1);
+        mbar_arrive_expect_tx(smem_u32(fb), 16384);
+        tma_load_3d(sb + kS_W + (c & 1) * 16384, &twt, 0, 0, (int)(item0 + c), smem_u32(fb));
+    };
+    auto issue_q = [&](int c) {  // q hi of chunk c into buffer c & 1
+        uint64_t* fb = &bars->q_full[c & 1];
+        pend.start(fb, (c >> 1) & 1);
+        mbar_arrive_expect_tx(smem_u32(fb), 16384);
+        for (int hb = 0; hb < 2; hb++)
+            tma_load_3d(sb + kS_Q + (c & 1) * 16384 + hb * 8192, &tqh, hb * 64, c * kC, plane_qk, smem_u32(fb));
+    };
+    auto issue_k = [&](int c) {  // k hi/lo of chunk c into buffer c & 1
+        uint64_t* fb = &bars->k_full[c & 1];
+        pend.start(fb, (c >> 1) & 1);
+        mbar_arrive_expect_tx(smem_u32(fb), 2 * 16384);
+        const uint32_t kb = sb + kS_K + (c & 1) * 32768;
         for (int hb = 0; hb < 2; hb++) {
-            tma_load_3d(sb + kS_Kh + hb * 8192, &tkth, hb * 64, 0, (int)(item0 + c), fb);
-            tma_load_3d(sb + kS_Kl + hb * 8192, &tktl, hb * 64, 0, (int)(item0 + c), fb);
+            tma_load_3d(kb + hb * 8192, &tkh, hb * 64, c * kC, plane_qk, smem_u32(fb));
+            tma_load_3d(kb + 16384 + hb * 8192, &tkl, hb * 64, c * kC, plane_qk, smem_u32(fb));
         }
     };
-    auto issue_p = [&](int c) {  // P' hi/lo of chunk c into buffer c & 1
-        const int buf = c & 1;
-        const uint32_t fb = smem_u32(&bars->p_full[buf]);
-        started(kP0 + buf, c >> 1);
-        mbar_arrive_expect_tx(fb, 8192 * 2);
-        tma_load_3d(sb + kS_P + buf * 16384, &tph, 0, 0, (int)(item0 + c), fb);
-        tma_load_3d(sb + kS_P + buf * 16384 + 8192, &tpl, 0, 0, (int)(item0 + c), fb);
+    auto issue_p = [&](int c) {  // P' hi/lo of chunk c
+        uint64_t* fb = &bars->p_full;
+        pend.start(fb, c & 1);
+        mbar_arrive_expect_tx(smem_u32(fb), 2 * 8192);
+        tma_load_3d(sb + kS_P, &tph, 0, 0, (int)(item0 + c), smem_u32(fb));
+        tma_load_3d(sb + kS_P + 8192, &tpl, 0, 0, (int)(item0 + c), smem_u32(fb));
     };
     if (tid == 0) {
-        issue_wqu(0);
+        issue_w(0);
         issue_k(0);
-        issue_p(0);
-        if (nch > 1) issue_p(1);
+        if (nch > 1) {
+            issue_w(1);
+            issue_k(1);
+        }
     }
-    float g_next = (tid < min(kC, T)) ? gin[plane_v * T + tid] : 0.f;  // gates of chunk 0
-
-    // ---- initial state: global f32 -> TMEM master and fp16 copy ----
+    if (tid == 128) {
+        issue_q(0);
+        if (nch > 1) issue_q(1);
+        issue_p(0);
+    }
     float* Sg = S + (QM_IN(plane_v * kHd * kHd, kHd * kHd, (size_t)gridDim.x * gridDim.y * kHd * kHd, err)
                          ? plane_v * kHd * kHd : 0);
-    {
-        const float* srow = Sg + (size_t)row * kHd;
+
+    if (warp < 4) {
+        // ================= warps 0-3: the recurrence =================
+        bool ok = mbar_wait_bounded(smem_u32(&bars->dec_ready), 0, abort_flag, err);
+        {   // initial state: global f32 -> its fp16 copy (S0 buffer 0) and, scaled by
+            // e^G63 of chunk 0 for MMA7, the TMEM master
+            const float* srow = Sg + (size_t)row * kHd;
+            const float decay = misc[128 + kC - 1];
 #pragma unroll 1
-        for (int c = 0; c < 4; c++) {
-            float v[32];
+            for (int h = 0; h < 2; h++) {
+                float pk[32];
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-                const float4 f = *reinterpret_cast<const float4*>(srow + c * 32 + i);
-                v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+                for (int cc = 0; cc < 2; cc++) {
+                    const int c = 2 * h + cc;
+                    float v[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        const float4 f = *reinterpret_cast<const float4*>(srow + c * 32 + i);
+                        v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; i++) pk[cc * 16 + i] = __uint_as_float(pack_f16x2_rn(v[2 * i], v[2 * i + 1]));
+#pragma unroll
+                    for (int i = 0; i < 32; i++) v[i] *= decay;
+                    tmem_st32(tm + lane_addr + kTmS + c * 32, v);
+                }
+                tmem_st32(tm + lane_addr + kTmS0h + h * 32, pk);
             }
-            tmem_st32(tm + lane_addr + kTmS + c * 32, v);
-#pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-                const int k = c * 32 + i;
-                *reinterpret_cast<uint4*>(smem + kS_S0 + (k >> 6) * 16384 + sw128_off(row, (k & 63) >> 3)) =
-                    round8(v + i);
-            }
+            tmem_st_wait();
         }
-        tmem_st_wait();
-    }
-    fence_proxy_async_shared();
-    tc_fence_before();
-    __syncthreads();
+        tc_fence_before();
+        ok = named_bar_and(1, 128, ok);
+        if (tid == 0) mbar_arrive(smem_u32(&bars->s_read));  // phase 0: S0 of chunk 0
 
-    // y of chunk c from Y[c&1] (lane v, coalesced per token); the caller has
-    // seen MMA6 of chunk c complete
-    auto write_y = [&](int c) {
-        const int t0 = c * kC, tc = min(kC, T - t0);
-        float yv[64];
-        tmem_ld32(tm + lane_addr + kTmY + (c & 1) * 64, yv);
-        tmem_ld32(tm + lane_addr + kTmY + (c & 1) * 64 + 32, yv + 32);
-        tmem_ld_wait();
-        float* yb = y + ((size_t)b * T + t0) * kVDim + (size_t)vh * kHd + row;
-        if (!QM_IN(((size_t)b * T + t0 + tc - 1) * kVDim + (size_t)vh * kHd + row, 1,
-                   (size_t)gridDim.y * T * kVDim, err))
-            return;
-#pragma unroll
-        for (int t = 0; t < kC; t++)
-            if (t < tc) yb[(size_t)t * kVDim] = yv[t];
-    };
-
-    bool ok = true;
-    for (int ci = 0; ci < nch && ok; ci++) {
-        const int p = ci & 1;
-        float* sGp = misc + p * 256;
-        float* eGp = sGp + 64;
-        float* eDp = sGp + 128;
-        float* sgp = sGp + 192;
-        if (tid < kC) sgp[tid] = g_next;
-        {  // gates of chunk ci+1, consumed next iteration
-            const int tn = (ci + 1) * kC;
-            g_next = (ci + 1 < nch && tid < min(kC, T - tn)) ? gin[plane_v * T + tn + tid] : 0.f;
-        }
-        __syncthreads();
-        if (warp == 0) chunk_decays(sgp, sGp, eGp, eDp, lane);
-
-        // ---- MMA4 (commit m4), MMA5 (commit m5) ----
-        if (tid == 0) {
-            if (mbar_wait_bounded(smem_u32(&bars->wqu_full), p, abort_flag, err)) {
-                seen(kWqu);
+        for (int ci = 0; ci < nch && ok; ci++) {
+            const int p = ci & 1;
+            // ---- MMA4: U2[p] (= U~) -= S0[p] W^T ----
+            if (tid == 0) {
+                const bool w = wait(&bars->w_full[p], (ci >> 1) & 1) && wait(&bars->u2_ready, p);
                 tc_fence_after();
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16_ss(tm + kTmU2, umma_sdesc(sb + kS_S0 + aoff, 16, 1024),
-                                 umma_sdesc(sb + kS_W + kk * 2048, 8192, 1024), kIdSW, kk > 0);
+                if (w) {
+                    for (int kk = 0; kk < 8; kk++)
+                        umma_f16_ts(tm + kTmU2 + p * 64, tm + kTmS0h + p * 64 + kk * 8,
+                                    umma_sdesc(sb + kS_W + p * 16384 + kk * 2048, 8192, 1024), kIdSW, 1u);
                 }
                 umma_commit(smem_u32(&bars->m4));
-                started(kM4, ci);
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16_ss(tm + kTmY + p * 64, umma_sdesc(sb + kS_S0 + aoff, 16, 1024),
-                                 umma_sdesc(sb + kS_Q + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
-                                 kIdSQ, kk > 0);
-                }
-            } else {
-                umma_commit(smem_u32(&bars->m4));
-                started(kM4, ci);
+                pend.start(&bars->m4, p);
             }
-            umma_commit(smem_u32(&bars->m5));
-            started(kM5, ci);
-        }
-        {
-            // every thread waits on the load barrier too: it reads U~ from shared memory
-            const bool w = mbar_wait_bounded(smem_u32(&bars->m4), p, abort_flag, err) &&
-                           mbar_wait_bounded(smem_u32(&bars->wqu_full), p, abort_flag, err);
-            if (w) seen(kM4);
-            ok = __syncthreads_and(ok && w && !*abort_flag) != 0;  // also publishes G, eG, eD
-        }
-        if (!ok) break;
-        tc_fence_after();
-        // MMA6 of chunk ci-1 read P' buffer (ci+1)&1 and finished before MMA4 of ci
-        if (tid == 0 && ci + 1 < nch && ci >= 1) issue_p(ci + 1);
-
-        // ---- U = U~ + U_acc -> fp16 hi/lo ----
-        {
-            float acc[64];
-            tmem_ld32(tm + lane_addr + kTmU2, acc);
-            tmem_ld32(tm + lane_addr + kTmU2 + 32, acc + 32);
-            const float4* ub = reinterpret_cast<const float4*>(smem + kS_Ut);
-            float ut[64];
-#pragma unroll
-            for (int t4 = 0; t4 < kC / 4; t4++) {
-                const float4 f = ub[t4 * kHd + row];
-                ut[4 * t4] = f.x; ut[4 * t4 + 1] = f.y; ut[4 * t4 + 2] = f.z; ut[4 * t4 + 3] = f.w;
+            {   // MMA5 and MMA6 of ci-1 are done: S0 buffer p^1 and U^T (unscaled) are free
+                bool w = mbar_wait_bounded(smem_u32(&bars->m4), p, abort_flag, err);
+                if (w && ci > 0) w = mbar_wait_bounded(smem_u32(&bars->mY), (ci - 1) & 1, abort_flag, err);
+                if (tid == 0 && w) pend.seen(&bars->m4);
+                ok = named_bar_and(1, 128, ok && w && !*abort_flag);
             }
-            tmem_ld_wait();
-#pragma unroll
-            for (int s = 0; s < kC; s += 8) {
-                float u8[8];
-#pragma unroll
-                for (int i = 0; i < 8; i++) u8[i] = acc[s + i] + ut[s + i];
-                uint4 h, l;
-                split8(u8, h, l);
-                *reinterpret_cast<uint4*>(smem + kS_Uh + sw128_off(row, s >> 3)) = h;
-                *reinterpret_cast<uint4*>(smem + kS_Ul + sw128_off(row, s >> 3)) = l;
-            }
-        }
-        if (tid == 0) {  // MMA5 must be done before W/Q~ are refilled and S0 is rewritten
-            if (mbar_wait_bounded(smem_u32(&bars->m5), p, abort_flag, err)) seen(kM5);
-        }
-        fence_proxy_async_shared();
-        tc_fence_before();
-        __syncthreads();
-
-        // ---- MMA7 (commit m7), MMA6 (commit mY); refetch W^T, Q~, U~ for chunk ci+1 ----
-        if (tid == 0) {
-            if (ci + 1 < nch && !*abort_flag) issue_wqu(ci + 1);
-            const bool kok = mbar_wait_bounded(smem_u32(&bars->k_full), p, abort_flag, err);
-            const bool pok = kok && mbar_wait_bounded(smem_u32(&bars->p_full[p]), (ci >> 1) & 1, abort_flag, err);
-            if (kok) seen(kK);
-            if (pok) seen(kP0 + p);
+            if (!ok) break;
             tc_fence_after();
-            if (kok) {
-                int n = 0;
-                for (int term = 0; term < 3; term++) {
-                    const uint32_t ua = sb + (term == 2 ? kS_Ul : kS_Uh);
-                    const uint32_t kb = sb + (term == 1 ? kS_Kl : kS_Kh);
-                    for (int kk = 0; kk < 4; kk++, n++)
-                        umma_bf16_ss(tm + kTmDS, umma_sdesc(ua + kk * 32, 16, 1024),
-                                     umma_sdesc(kb + kk * 2048, 8192, 1024), kIdUK, n > 0);
-                }
-            }
-            umma_commit(smem_u32(&bars->m7));
-            started(kM7, ci);
-            if (pok) {
-                const uint32_t pb = sb + kS_P + p * 16384;
-                for (int term = 0; term < 3; term++) {
-                    const uint32_t ua = sb + (term == 2 ? kS_Ul : kS_Uh);
-                    const uint32_t pbt = pb + (term == 1 ? 8192 : 0);
-                    for (int kk = 0; kk < 4; kk++)
-                        umma_bf16_ss(tm + kTmY + p * 64, umma_sdesc(ua + kk * 32, 16, 1024),
-                                     umma_sdesc(pbt + kk * 32, 16, 1024), kIdUP, 1u);
-                }
-            }
-            umma_commit(smem_u32(&bars->mY));
-            started(kMY, ci);
-        }
-        // outputs of chunk ci-1 while MMA7 runs (its MMA6 finished before MMA4 of ci)
-        if (ci > 0) write_y(ci - 1);
-        {
-            const bool w = mbar_wait_bounded(smem_u32(&bars->m7), p, abort_flag, err);
-            if (w) seen(kM7);
-            ok = __syncthreads_and(ok && w && !*abort_flag) != 0;
-        }
-        if (!ok) break;
-        tc_fence_after();
-        if (tid == 0 && ci + 1 < nch) issue_k(ci + 1);  // MMA7 has read K~
+            if (tid == 0 && ci + 2 < nch) issue_w(ci + 2);  // MMA4 has read W^T buffer p
 
-        // ---- S_master = e^G63 S_master + dS, and its fp16 copy for the next chunk ----
-        const float decay = eGp[kC - 1];
+            // ---- U step: (U diag D)^T -> fp16 hi/lo (MMA7 of chunk ci-1 is done with them) ----
+            {
+                float u[64];
+                tmem_ld32(tm + lane_addr + kTmU2 + p * 64, u);
+                tmem_ld32(tm + lane_addr + kTmU2 + p * 64 + 32, u + 32);
+                const float* eD = misc + p * 256 + 192;
+                tmem_ld_wait();
+#pragma unroll
+                for (int s = 0; s < kC; s++) u[s] *= eD[s];
+                store_u_split(smem + kS_Us, smem + kS_Us + 16384, row, u);
+            }
+            fence_proxy_async_shared();
+            tc_fence_before();
+            named_bar_sync(1, 128);
+
+            // ---- MMA7: S (pre-scaled by e^G63) += (U diag D)^T k ----
+            if (tid == 0) {
+                mbar_arrive(smem_u32(&bars->u_ready));  // U is read; the chunk's decays are consumed
+                const bool w = wait(&bars->k_full[p], (ci >> 1) & 1);
+                tc_fence_after();
+                if (w) {
+                    const uint32_t kb = sb + kS_K + p * 32768;
+                    for (int term = 0; term < 3; term++) {
+                        const uint32_t ua = sb + kS_Us + (term == 2 ? 16384 : 0);
+                        const uint32_t kt = kb + (term == 1 ? 16384 : 0);
+                        for (int kk = 0; kk < 4; kk++)
+                            umma_bf16_ss(tm + kTmS, umma_sdesc(ua + kk * 32, 16, 1024),
+                                         umma_sdesc(kt + kk * 2048, 8192, 1024), kIdUK, 1u);
+                    }
+                }
+                umma_commit(smem_u32(&bars->m7));
+                pend.start(&bars->m7, p);
+            }
+            {
+                const bool w = mbar_wait_bounded(smem_u32(&bars->m7), p, abort_flag, err);
+                if (tid == 0 && w) pend.seen(&bars->m7);
+                ok = named_bar_and(1, 128, ok && w && !*abort_flag);
+            }
+            if (!ok) break;
+            tc_fence_after();
+            if (tid == 0 && ci + 2 < nch) issue_k(ci + 2);  // MMA7 has read k buffer p
+
+            // ---- S pass: S0 of chunk ci+1 = fp16(S) into TMEM buffer p^1, and S scaled
+            // by e^G63 of chunk ci+1 for its MMA7 (its decays come with dec_ready) ----
+            if (ci + 1 < nch) {
+                ok = mbar_wait_bounded(smem_u32(&bars->dec_ready), (ci + 1) & 1, abort_flag, err);
+                const float decay = misc[((ci + 1) & 1) * 256 + 128 + kC - 1];
 #pragma unroll 1
-        for (int c = 0; c < 4; c++) {
-            float sv[32], dv[32];
-            tmem_ld32(tm + lane_addr + kTmS + c * 32, sv);
-            tmem_ld32(tm + lane_addr + kTmDS + c * 32, dv);
-            tmem_ld_wait();
+                for (int h = 0; h < 2; h++) {
+                    float sv[64], pk[32];
+                    tmem_ld32(tm + lane_addr + kTmS + h * 64, sv);
+                    tmem_ld32(tm + lane_addr + kTmS + h * 64 + 32, sv + 32);
+                    tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; i++) sv[i] = fmaf(sv[i], decay, dv[i]);
-            tmem_st32(tm + lane_addr + kTmS + c * 32, sv);
+                    for (int i = 0; i < 32; i++) pk[i] = __uint_as_float(pack_f16x2_rn(sv[2 * i], sv[2 * i + 1]));
+                    tmem_st32(tm + lane_addr + kTmS0h + (p ^ 1) * 64 + h * 32, pk);
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-                const int k = c * 32 + i;
-                *reinterpret_cast<uint4*>(smem + kS_S0 + (k >> 6) * 16384 + sw128_off(row, (k & 63) >> 3)) =
-                    round8(sv + i);
+                    for (int i = 0; i < 64; i++) sv[i] *= decay;
+                    tmem_st32(tm + lane_addr + kTmS + h * 64, sv);
+                    tmem_st32(tm + lane_addr + kTmS + h * 64 + 32, sv + 32);
+                }
+                tmem_st_wait();
             }
+            tc_fence_before();
+            named_bar_sync(1, 128);
+            if (tid == 0) mbar_arrive(smem_u32(&bars->s_read));  // phase ci+1: S0 of ci+1 written
+            ok = named_bar_and(1, 128, ok && !*abort_flag);
         }
-        tmem_st_wait();
-        fence_proxy_async_shared();
-        tc_fence_before();
-        __syncthreads();
-    }
-
-    // ---- outputs of the last chunk; final state back to global (f32) ----
-    if (ok) {
-        const bool w = mbar_wait_bounded(smem_u32(&bars->mY), (nch - 1) & 1, abort_flag, err);
-        if (w) seen(kMY);
-        tc_fence_after();
-        if (w) {
-            write_y(nch - 1);
+        // ---- final state back to global (f32); warps 4-7 write the last y ----
+        if (ok) {
+            tc_fence_after();
             float* srow = Sg + (size_t)row * kHd;
 #pragma unroll 1
             for (int c = 0; c < 4; c++) {
@@ -967,12 +923,145 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
                         make_float4(sv[i], sv[i + 1], sv[i + 2], sv[i + 3]);
             }
         }
+    } else {
+        // ================= warps 4-7: beside the chain =================
+        // Every thread here runs every step (the named barriers need all 128);
+        // after an abort the bounded waits return at once and the work is skipped.
+        const int at = tid - 128;
+        bool ok = true;
+        const float* ut_base = ut_in + item0 * kHd * kC;
+        const bool ut_in_range =
+            QM_IN(item0 * kHd * kC, (size_t)nch * kHd * kC, (size_t)gridDim.x * gridDim.y * nch * kHd * kC, err);
+        float ut[64];  // U~ of the next chunk for this thread's v row
+        auto load_ut = [&](int c) {
+            const float4* ub = reinterpret_cast<const float4*>(ut_base + (size_t)c * kHd * kC);
+#pragma unroll
+            for (int t4 = 0; t4 < kC / 4; t4++) {
+                const float4 f = ut_in_range ? ub[t4 * kHd + row] : make_float4(0.f, 0.f, 0.f, 0.f);
+                ut[4 * t4] = f.x; ut[4 * t4 + 1] = f.y; ut[4 * t4 + 2] = f.z; ut[4 * t4 + 3] = f.w;
+            }
+        };
+        auto store_ut = [&](int c) {  // U~ of chunk c into U2[c&1], then u2_ready
+            tmem_st32(tm + lane_addr + kTmU2 + (c & 1) * 64, ut);
+            tmem_st32(tm + lane_addr + kTmU2 + (c & 1) * 64 + 32, ut + 32);
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(smem_u32(&bars->u2_ready));
+        };
+        float g_next = 0.f;
+        auto load_g = [&](int c) {
+            const int t = c * kC + at;
+            g_next = (at < kC && c < nch && t < T) ? gin[plane_v * T + t] : 0.f;
+        };
+        auto decays = [&](int c) {  // the gates of chunk c (in g_next) -> slot c&1, then dec_ready
+            float* sgp = misc + (c & 1) * 256;
+            if (at < kC) sgp[at] = g_next;
+            named_bar_sync(2, 128);
+            if (warp == 4) chunk_decays(sgp, sgp + 64, sgp + 128, sgp + 192, lane);
+            named_bar_sync(2, 128);
+            mbar_arrive(smem_u32(&bars->dec_ready));
+        };
+        auto write_y = [&](int c) {  // y_t = e^G_t Y1_t + Y2_t, staged [64 t][128 v], one TMA store
+            const float* eG = misc + (c & 1) * 256 + 128;
+            float y1[64], y2[64];
+            tmem_ld32(tm + lane_addr + kTmY1, y1);
+            tmem_ld32(tm + lane_addr + kTmY1 + 32, y1 + 32);
+            tmem_ld32(tm + lane_addr + kTmY2, y2);
+            tmem_ld32(tm + lane_addr + kTmY2 + 32, y2 + 32);
+            tmem_ld_wait();
+            tc_fence_before();
+            float* ys = reinterpret_cast<float*>(smem + kS_Uu);
+#pragma unroll
+            for (int t = 0; t < kC; t++) ys[t * kHd + row] = fmaf(eG[t], y1[t], y2[t]);
+            fence_proxy_async_shared();
+            named_bar_sync(2, 128);
+            if (at == 0) {  // tokens past T are outside the tensor and not written
+                tma_store_3d(&tyo, sb + kS_Uu, vh * kHd, c * kC, b);
+                bulk_commit();
+            }
+        };
+        // ---- before chunk 0: its decays, U~ -> U2[0] ----
+        load_g(0);
+        load_ut(0);
+        decays(0);
+        load_g(1);
+        store_ut(0);
+        if (nch > 1) load_ut(1);
+
+        for (int ci = 0; ci < nch; ci++) {
+            const int p = ci & 1;
+            const bool more = ci + 1 < nch;
+            // ---- MMA5: Y1 = S0 q^T (Y of ci-1 was read out; its staged copy has
+            // been read by the TMA store before U^T is written there again) ----
+            bool qok = ok && wait(&bars->q_full[p], (ci >> 1) & 1);
+            if (at == 0) {
+                bulk_wait_read0();
+                qok = qok && mbar_wait_bounded(smem_u32(&bars->s_read), p, abort_flag, err);  // S0 of ci
+            }
+            tc_fence_before();
+            named_bar_sync(2, 128);
+            if (at == 0) {
+                tc_fence_after();
+                if (qok) {
+                    for (int kk = 0; kk < 8; kk++)
+                        umma_f16_ts(tm + kTmY1, tm + kTmS0h + p * 64 + kk * 8,
+                                    umma_sdesc(sb + kS_Q + p * 16384 + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
+                                    kIdSQ, kk > 0 ? 1u : 0u);
+                }
+            }
+            // ---- once the U step of ci is done: U^T hi/lo (unscaled) for MMA6 ----
+            const bool wu = mbar_wait_bounded(smem_u32(&bars->u_ready), p, abort_flag, err);
+            ok = ok && wu;
+            if (ok) {
+                tc_fence_after();
+                float u[64];
+                tmem_ld32(tm + lane_addr + kTmU2 + p * 64, u);
+                tmem_ld32(tm + lane_addr + kTmU2 + p * 64 + 32, u + 32);
+                tmem_ld_wait();
+                store_u_split(smem + kS_Uu, smem + kS_Uu + 16384, row, u);
+                fence_proxy_async_shared();
+            }
+            tc_fence_before();
+            named_bar_sync(2, 128);
+            if (at == 0) {
+                const bool pok = ok && wait(&bars->p_full, p);
+                tc_fence_after();
+                if (pok) {
+                    int n = 0;
+                    for (int term = 0; term < 3; term++) {
+                        const uint32_t ua = sb + kS_Uu + (term == 2 ? 16384 : 0);
+                        const uint32_t pbt = sb + kS_P + (term == 1 ? 8192 : 0);
+                        for (int kk = 0; kk < 4; kk++, n++)
+                            umma_bf16_ss(tm + kTmY2, umma_sdesc(ua + kk * 32, 16, 1024),
+                                         umma_sdesc(pbt + kk * 32, 16, 1024), kIdUP, n > 0 ? 1u : 0u);
+                    }
+                }
+                umma_commit(smem_u32(&bars->mY));  // MMA5 and MMA6 of ci
+                pend.start(&bars->mY, p);
+            }
+            if (more) {
+                decays(ci + 1);  // slot (ci+1)&1 was last read in chunk ci-1
+                load_g(ci + 2);
+                store_ut(ci + 1);  // U2[(ci+1)&1] was read in chunk ci-1
+                if (ci + 2 < nch) load_ut(ci + 2);
+            }
+            // ---- MMA5 / MMA6 done: next q and P' loads; S scaled for chunk ci+1 ----
+            const bool wy = ok && wait(&bars->mY, p);
+            ok = wy;
+            if (at == 0 && ok) {
+                if (more) issue_p(ci + 1);
+                if (ci + 2 < nch) issue_q(ci + 2);  // MMA5 of ci has read q buffer p
+            }
+            // ---- y of chunk ci (every operand thread takes part: named barrier) ----
+            tc_fence_after();
+            if (wy) write_y(ci);
+            else named_bar_sync(2, 128);
+            ok = ok && !*abort_flag;
+        }
+        if (at == 0) bulk_wait0();  // the last y stores have completed
     }
     // do not leave while copies or MMAs this CTA issued may still land
-    if (tid == 0) {
-        for (int i = 0; i < 8; i++)
-            if (out_[i]) mbar_drain(smem_u32(bar_list[i]), par_[i]);
-    }
+    pend.drain();
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -1007,10 +1096,9 @@ __global__ void dn_prefill_gate(const float* __restrict__ y, const float* __rest
 
 // Workspace: fp16 hi+lo planes of q, k (16 heads each) and v (32 heads); f32
 // g and beta [B*32][T]; per (sequence, V head, chunk) item the chunk-local
-// factors W^T fp16 [128][64], U~^T f32 [64][128], P' fp16 hi/lo [64][64],
-// Q~ fp16 [64][128] and K~ fp16 hi/lo [64][128].
+// factors W^T fp16 [128][64], U~^T f32 [64][128] and P' fp16 hi/lo [64][64].
 struct DnWs {
-    size_t qh, ql, kh, kl, vh, vl, g, be, wt, ut, ph, pl, qt, kth, ktl, total;
+    size_t qh, ql, kh, kl, vh, vl, g, be, wt, ut, ph, pl, total;
 };
 
 static DnWs dn_ws_layout(int B, int T) {
@@ -1031,9 +1119,6 @@ static DnWs dn_ws_layout(int B, int T) {
     w.ut = o; o = al(o + items * kHd * kC * 4);
     w.ph = o; o = al(o + items * kC * kC * 2);
     w.pl = o; o = al(o + items * kC * kC * 2);
-    w.qt = o; o = al(o + items * kC * kHd * 2);
-    w.kth = o; o = al(o + items * kC * kHd * 2);
-    w.ktl = o; o = al(o + items * kC * kHd * 2);
     w.total = o;
     return w;
 }
@@ -1060,9 +1145,6 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
     float* ut = reinterpret_cast<float*>(base + w.ut);
     uint16_t* ph = reinterpret_cast<uint16_t*>(base + w.ph);
     uint16_t* pl = reinterpret_cast<uint16_t*>(base + w.pl);
-    uint16_t* qt = reinterpret_cast<uint16_t*>(base + w.qt);
-    uint16_t* kth = reinterpret_cast<uint16_t*>(base + w.kth);
-    uint16_t* ktl = reinterpret_cast<uint16_t*>(base + w.ktl);
     {
         TimedLaunch tl(ctx, "dn_prefill_prep");
         const int nruns = (T + kPrepRun - 1) / kPrepRun;
@@ -1086,13 +1168,11 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
             return cudaErrorInvalidValue;
     }
     const uint64_t items = (uint64_t)B * kNumV * nch;
-    CUtensorMap mwt, mph, mpl, mqt, mkth, mktl;
+    CUtensorMap mwt, mph, mpl, myo;
     if (encode_rows_tmap(&mwt, wt, kC, kHd, items, 64, kHd, true) != QM_OK ||
         encode_rows_tmap(&mph, ph, kC, kC, items, 64, kC, true) != QM_OK ||
         encode_rows_tmap(&mpl, pl, kC, kC, items, 64, kC, true) != QM_OK ||
-        encode_rows_tmap(&mqt, qt, kHd, kC, items, 64, kC, true) != QM_OK ||
-        encode_rows_tmap(&mkth, kth, kHd, kC, items, 64, kC, true) != QM_OK ||
-        encode_rows_tmap(&mktl, ktl, kHd, kC, items, 64, kC, true) != QM_OK)
+        encode_f32_tmap(&myo, y, kVDim, (uint64_t)T, (uint64_t)B, kHd, kC) != QM_OK)
         return cudaErrorInvalidValue;
     static std::atomic<uint64_t> attr_local{0}, attr_state{0};
     e = set_smem_once(attr_local, ctx->device, dn_chunk_local, kLocalSmem);
@@ -1101,15 +1181,15 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
     {
         TimedLaunch tl(ctx, "dn_chunk_local");
         dn_chunk_local<<<dim3(kNumV, nch, B), kLocalThreads, kLocalSmem, s>>>(
-            m[0], m[1], m[2], m[3], m[4], m[5], g, be, T, nch, wt, ut, ph, pl, qt, kth, ktl, ctx->d_err);
+            m[0], m[1], m[2], m[3], m[4], m[5], g, be, T, nch, wt, ut, ph, pl, ctx->d_err);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     ctx->launches += 1;
     {
         TimedLaunch tl(ctx, "dn_chunk_state");
-        dn_chunk_state<<<dim3(kNumV, B), 128, kStateSmem, s>>>(mwt, mph, mpl, mqt, mkth, mktl, ut, g,
-                                                               st->s, y, T, nch, ctx->d_err);
+        dn_chunk_state<<<dim3(kNumV, B), kStateThreads, kStateSmem, s>>>(mwt, mph, mpl, m[0], m[2], m[3], myo, ut, g,
+                                                               st->s, T, nch, ctx->d_err);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;

@@ -174,6 +174,23 @@ int encode_rows_tmap(CUtensorMap* m, void* base, uint64_t inner, uint64_t rows, 
     return r == CUDA_SUCCESS ? QM_OK : QM_E_CUDA;
 }
 
+// 3-D f32 view {inner, rows, planes} (row-major), no swizzle: the plain
+// row-major tiles a TMA store writes from shared memory (out-of-range rows
+// are skipped).
+int encode_f32_tmap(CUtensorMap* m, void* base, uint64_t inner, uint64_t rows, uint64_t planes,
+                    uint32_t box_inner, uint32_t box_rows) {
+    auto enc = get_encode_tiled();
+    if (!enc) return QM_E_CUDA;
+    cuuint64_t dims[3] = {inner, rows, planes};
+    cuuint64_t strides[2] = {inner * 4, rows * inner * 4};
+    cuuint32_t box[3] = {box_inner, box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? QM_OK : QM_E_CUDA;
+}
+
 int make_kv_tmaps(qm_kv* kv) {
     kv->tmaps_ok = false;
     const int planes = kv->batch * kv->nkv;
