@@ -612,7 +612,10 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
 // into TMEM, the unscaled U hi/lo for MMA6, and y (staged in shared memory,
 // one TMA store per chunk); their thread 128 issues MMA5 / MMA6 and the q
 // and P' loads.  mbarriers hand over: u2_ready, dec_ready (warps 4-7 ->
-// thread 0); u_ready, s_read (thread 0 -> warps 4-7).
+// thread 0); u_ready, s_read (thread 0 -> warps 4-7).  dec_ready and s_read
+// are pairs used by chunk parity (phase c >> 1 for chunk c): either side may
+// publish a chunk's piece one chunk early without a phase running two ahead
+// of its waiter.
 constexpr int kS_W = 0;             // W^T [128 k x 64 t] fp16, x2 buffers (32 KB)
 constexpr int kS_Q = 32768;         // q hi [64 t x 128 k] fp16: 2 boxes [64 x 64], x2 buffers (32 KB)
 constexpr int kS_P = 65536;         // P' hi, lo [64 t x 64 s] (8 KB each) (16 KB)
@@ -632,8 +635,8 @@ constexpr uint32_t kIdUK = umma_idesc_f16kind(128, 128, false, true, false);   /
 struct StateBars {  // the first 11 words are tracked by Pending (in this order)
     uint64_t w_full[2], q_full[2], k_full[2], p_full;  // TMA
     uint64_t m4, m7, mY, spare;                        // MMA completions
-    uint64_t u2_ready, dec_ready;                      // warps 4-7 -> thread 0 (128 arrivals)
-    uint64_t u_ready, s_read;                          // thread 0 -> warps 4-7 (1 arrival)
+    uint64_t u2_ready, dec_ready[2];                   // warps 4-7 -> thread 0 (128 arrivals)
+    uint64_t u_ready, s_read[2];                       // thread 0 -> warps 4-7 (1 arrival)
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -715,9 +718,11 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         mbar_init(smem_u32(&bars->m7), 1);
         mbar_init(smem_u32(&bars->mY), 1);
         mbar_init(smem_u32(&bars->u2_ready), 128);
-        mbar_init(smem_u32(&bars->dec_ready), 128);
+        mbar_init(smem_u32(&bars->dec_ready[0]), 128);
+        mbar_init(smem_u32(&bars->dec_ready[1]), 128);
         mbar_init(smem_u32(&bars->u_ready), 1);
-        mbar_init(smem_u32(&bars->s_read), 1);
+        mbar_init(smem_u32(&bars->s_read[0]), 1);
+        mbar_init(smem_u32(&bars->s_read[1]), 1);
         bars->abort_flag = 0;
         fence_barrier_init();
     }
@@ -785,7 +790,7 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
 
     if (warp < 4) {
         // ================= warps 0-3: the recurrence =================
-        bool ok = mbar_wait_bounded(smem_u32(&bars->dec_ready), 0, abort_flag, err);
+        bool ok = mbar_wait_bounded(smem_u32(&bars->dec_ready[0]), 0, abort_flag, err);
         {   // initial state: global f32 -> its fp16 copy (S0 buffer 0) and, scaled by
             // e^G63 of chunk 0 for MMA7, the TMEM master
             const float* srow = Sg + (size_t)row * kHd;
@@ -814,7 +819,7 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         }
         tc_fence_before();
         ok = named_bar_and(1, 128, ok);
-        if (tid == 0) mbar_arrive(smem_u32(&bars->s_read));  // phase 0: S0 of chunk 0
+        if (tid == 0) mbar_arrive(smem_u32(&bars->s_read[0]));  // S0 of chunk 0
 
         for (int ci = 0; ci < nch && ok; ci++) {
             const int p = ci & 1;
@@ -885,7 +890,8 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
             // ---- S pass: S0 of chunk ci+1 = fp16(S) into TMEM buffer p^1, and S scaled
             // by e^G63 of chunk ci+1 for its MMA7 (its decays come with dec_ready) ----
             if (ci + 1 < nch) {
-                ok = mbar_wait_bounded(smem_u32(&bars->dec_ready), (ci + 1) & 1, abort_flag, err);
+                // dec_ready[c&1] completes once per two chunks: phase (c >> 1) for chunk c
+                ok = mbar_wait_bounded(smem_u32(&bars->dec_ready[(ci + 1) & 1]), ((ci + 1) >> 1) & 1, abort_flag, err);
                 const float decay = misc[((ci + 1) & 1) * 256 + 128 + kC - 1];
 #pragma unroll 1
                 for (int h = 0; h < 2; h++) {
@@ -905,7 +911,9 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
             }
             tc_fence_before();
             named_bar_sync(1, 128);
-            if (tid == 0) mbar_arrive(smem_u32(&bars->s_read));  // phase ci+1: S0 of ci+1 written
+            // S0 of ci+1 written: s_read[(ci+1)&1], whose previous phase (chunk ci-1)
+            // warps 4-7 consumed before they published U~ of chunk ci
+            if (tid == 0 && ci + 1 < nch) mbar_arrive(smem_u32(&bars->s_read[(ci + 1) & 1]));
             ok = named_bar_and(1, 128, ok && !*abort_flag);
         }
         // ---- final state back to global (f32); warps 4-7 write the last y ----
@@ -953,13 +961,13 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
             const int t = c * kC + at;
             g_next = (at < kC && c < nch && t < T) ? gin[plane_v * T + t] : 0.f;
         };
-        auto decays = [&](int c) {  // the gates of chunk c (in g_next) -> slot c&1, then dec_ready
+        auto decays = [&](int c) {  // the gates of chunk c (in g_next) -> slot c&1, then dec_ready[c&1]
             float* sgp = misc + (c & 1) * 256;
             if (at < kC) sgp[at] = g_next;
             named_bar_sync(2, 128);
             if (warp == 4) chunk_decays(sgp, sgp + 64, sgp + 128, sgp + 192, lane);
             named_bar_sync(2, 128);
-            mbar_arrive(smem_u32(&bars->dec_ready));
+            mbar_arrive(smem_u32(&bars->dec_ready[c & 1]));
         };
         auto write_y = [&](int c) {  // y_t = e^G_t Y1_t + Y2_t, staged [64 t][128 v], one TMA store
             const float* eG = misc + (c & 1) * 256 + 128;
@@ -991,12 +999,20 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         for (int ci = 0; ci < nch; ci++) {
             const int p = ci & 1;
             const bool more = ci + 1 < nch;
+            // ---- the decays of chunk ci+1 first: the S pass of chunk ci waits for them.
+            // Slot (ci+1)&1 was last read by the U step of ci-1 (u_ready of ci-1 seen)
+            // and by y of ci-1; dec_ready[(ci+1)&1] last completed for chunk ci-1,
+            // whose S pass waited for it before the U step of ci ----
+            if (more) {
+                decays(ci + 1);
+                load_g(ci + 2);
+            }
             // ---- MMA5: Y1 = S0 q^T (Y of ci-1 was read out; its staged copy has
             // been read by the TMA store before U^T is written there again) ----
             bool qok = ok && wait(&bars->q_full[p], (ci >> 1) & 1);
             if (at == 0) {
                 bulk_wait_read0();
-                qok = qok && mbar_wait_bounded(smem_u32(&bars->s_read), p, abort_flag, err);  // S0 of ci
+                qok = qok && mbar_wait_bounded(smem_u32(&bars->s_read[p]), (ci >> 1) & 1, abort_flag, err);  // S0 of ci
             }
             tc_fence_before();
             named_bar_sync(2, 128);
@@ -1040,8 +1056,6 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
                 pend.start(&bars->mY, p);
             }
             if (more) {
-                decays(ci + 1);  // slot (ci+1)&1 was last read in chunk ci-1
-                load_g(ci + 2);
                 store_ut(ci + 1);  // U2[(ci+1)&1] was read in chunk ci-1
                 if (ci + 2 < nch) load_ut(ci + 2);
             }
