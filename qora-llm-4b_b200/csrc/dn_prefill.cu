@@ -243,47 +243,57 @@ __device__ __forceinline__ void chunk_decays(const float* sg, float* sG, float* 
 // unit-lower-triangular inverse T of I + A (row stride kAStride floats):
 //   X_ij = sum_{k=j}^{i-1} A_ik T_kj   (kept in the unused upper block (j, i))
 //   T_ij = -T_ii X_ij                  (T_ii stored with zeros above its diagonal)
-// Each of the NT threads owns (4 - d) * 256 / NT elements; all trip counts
-// are compile-time so the shared-memory loads issue ahead of the FMAs.
+// A work item is 4 adjacent columns of one row of one block: float4 loads of
+// T / X rows serve all four, and a warp's 8 rows x 4 column groups read
+// distinct banks (rows are 68 floats apart).  (4 - D) * 64 items over NT
+// threads; all trip counts are compile-time.
 template <int D, int NT>
 __device__ __forceinline__ void tri_inverse_diagonal(const float* __restrict__ A, float* __restrict__ Tm,
                                                      int tid) {
     constexpr int kStride = 68;
-    constexpr int NOUT = (4 - D) * 256 / NT;
-#pragma unroll
-    for (int m = 0; m < NOUT; m++) {
-        const int o = tid + NT * m;
-        const int j = o >> 8, i = j + D, r = (o >> 4) & 15, c = o & 15;
+    constexpr int NITEM = (4 - D) * 64;
+    static_assert(NITEM <= NT, "one item per thread");
+    const bool active = tid < NITEM;
+    const int c4 = tid & 3, r = (tid >> 2) & 15, j = tid >> 6, i = j + D;
+    if (active) {
         const float* arow = A + (16 * i + r) * kStride + 16 * j;
-        const float* tcol = Tm + (16 * j) * kStride + 16 * j + c;
-        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        const float* tcol = Tm + (16 * j) * kStride + 16 * j + 4 * c4;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int u = 0; u < 16 * D; u += 4) {
             const float4 a = *reinterpret_cast<const float4*>(arow + u);
-            x[0] = fmaf(a.x, tcol[(u + 0) * kStride], x[0]);
-            x[1] = fmaf(a.y, tcol[(u + 1) * kStride], x[1]);
-            x[2] = fmaf(a.z, tcol[(u + 2) * kStride], x[2]);
-            x[3] = fmaf(a.w, tcol[(u + 3) * kStride], x[3]);
+            const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float4 t = *reinterpret_cast<const float4*>(tcol + (u + q) * kStride);
+                x.x = fmaf(av[q], t.x, x.x);
+                x.y = fmaf(av[q], t.y, x.y);
+                x.z = fmaf(av[q], t.z, x.z);
+                x.w = fmaf(av[q], t.w, x.w);
+            }
         }
-        Tm[(16 * j + r) * kStride + 16 * i + c] = (x[0] + x[1]) + (x[2] + x[3]);
+        *reinterpret_cast<float4*>(Tm + (16 * j + r) * kStride + 16 * i + 4 * c4) = x;
     }
     __syncthreads();
-#pragma unroll
-    for (int m = 0; m < NOUT; m++) {
-        const int o = tid + NT * m;
-        const int j = o >> 8, i = j + D, r = (o >> 4) & 15, c = o & 15;
+    if (active) {
         const float* trow = Tm + (16 * i + r) * kStride + 16 * i;
-        const float* xcol = Tm + (16 * j) * kStride + 16 * i + c;
-        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        const float* xcol = Tm + (16 * j) * kStride + 16 * i + 4 * c4;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int u = 0; u < 16; u += 4) {
             const float4 t = *reinterpret_cast<const float4*>(trow + u);
-            x[0] = fmaf(t.x, xcol[(u + 0) * kStride], x[0]);
-            x[1] = fmaf(t.y, xcol[(u + 1) * kStride], x[1]);
-            x[2] = fmaf(t.z, xcol[(u + 2) * kStride], x[2]);
-            x[3] = fmaf(t.w, xcol[(u + 3) * kStride], x[3]);
+            const float tv[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float4 xv = *reinterpret_cast<const float4*>(xcol + (u + q) * kStride);
+                x.x = fmaf(tv[q], xv.x, x.x);
+                x.y = fmaf(tv[q], xv.y, x.y);
+                x.z = fmaf(tv[q], xv.z, x.z);
+                x.w = fmaf(tv[q], xv.w, x.w);
+            }
         }
-        Tm[(16 * i + r) * kStride + 16 * j + c] = -((x[0] + x[1]) + (x[2] + x[3]));
+        *reinterpret_cast<float4*>(Tm + (16 * i + r) * kStride + 16 * j + 4 * c4) =
+            make_float4(-x.x, -x.y, -x.z, -x.w);
     }
     __syncthreads();
 }
@@ -356,26 +366,22 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
     const size_t plane_qk = (size_t)b * kNumQK + qk, plane_v = (size_t)b * kNumV + vh;
     const size_t item = ((size_t)b * kNumV + vh) * nch + ci;
 
-    if (tid == 0) {
-        mbar_init(smem_u32(&bars->load), 1);
-        mbar_init(smem_u32(&bars->mma), 1);
-        bars->abort_flag = 0;
-        fence_barrier_init();
+    // the gates first (a dependent global load), then the K/Q tiles as soon as
+    // the load barrier exists; both arrive while the CTA sets up
+    float g_own = 0.f, b_own = 0.f;
+    if (tid < tc) {
+        g_own = gin[plane_v * T + t0 + tid];
+        b_own = bin[plane_v * T + t0 + tid];
     }
-    if (warp == 0) {
-        tmem_alloc(smem_u32(&bars->tmem_base), 256);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tm = bars->tmem_base;
-
     // thread 0's record of the last phase it started on each barrier and not
     // yet seen complete (drained on the way out of an aborted CTA)
     bool ld_out = false, mm_out = false;
     uint32_t ld_par = 0, mm_par = 0;
     if (tid == 0) {
+        mbar_init(smem_u32(&bars->load), 1);
+        mbar_init(smem_u32(&bars->mma), 1);
+        bars->abort_flag = 0;
+        fence_barrier_init();
         const uint32_t lb = smem_u32(&bars->load);
         mbar_arrive_expect_tx(lb, 8 * 8192);
         ld_out = true;
@@ -386,12 +392,18 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
             tma_load_3d(sb + kL_KQl + hb * 16384 + 8192, &tql, hb * 64, t0, (int)plane_qk, lb);
         }
     }
-    if (tid < kC) {
-        const bool valid = tid < tc;
-        sg[tid] = valid ? gin[plane_v * T + t0 + tid] : 0.f;
-        sB[tid] = valid ? bin[plane_v * T + t0 + tid] : 0.f;
+    if (warp == 0) {
+        tmem_alloc(smem_u32(&bars->tmem_base), 256);
+        tmem_relinquish();
     }
+    if (tid < kC) {
+        sg[tid] = g_own;
+        sB[tid] = b_own;
+    }
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = bars->tmem_base;
     if (warp == 0) chunk_decays(sg, sG, eG, eD, lane);
     bool ok = mbar_wait_bounded(smem_u32(&bars->load), 0, abort_flag, err);
     if (ok) ld_out = false;
