@@ -513,8 +513,8 @@ def run_ours(args):
     if (ws > 1 and not args.no_head_sharded) or args.head_sharded:
         line["head_sharded"] = bench_head_sharded(ctx, ws, rank, args)
     if not args.no_prefill:
-        line["prefill_gqa"] = bench_gqa_prefill(ctx, ws, args.prefill_reps)
         line["prefill_dn"] = bench_dn_prefill(ctx, ws, args.prefill_reps)
+        line["prefill_gqa"] = bench_gqa_prefill(ctx, ws, args.prefill_reps)
     if not args.no_small:
         cpu = rank == 0 and ws == 1 and not args.no_cpu_baseline
         line["decode_config0"] = bench_config0(ctx, args.prefill_reps * 3, cpu=cpu)
