@@ -628,14 +628,16 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
 // are pairs used by chunk parity (phase c >> 1 for chunk c): either side may
 // publish a chunk's piece one chunk early without a phase running two ahead
 // of its waiter.
-constexpr int kS_W = 0;             // W^T [128 k x 64 t] fp16, x2 buffers (32 KB)
-constexpr int kS_Q = 32768;         // q hi [64 t x 128 k] fp16: 2 boxes [64 x 64], x2 buffers (32 KB)
-constexpr int kS_P = 65536;         // P' hi, lo [64 t x 64 s] (8 KB each) (16 KB)
-constexpr int kS_K = 81920;         // k hi, lo [64 s x 128 k] (16 KB each), x2 buffers (64 KB)
-constexpr int kS_Us = 147456;       // (U diag D)^T hi, lo [128 v x 64 s] (16 KB each)
-constexpr int kS_Uu = 180224;       // U^T hi, lo (16 KB each); y [64 t][128 v] f32 after MMA6
-constexpr int kS_Misc = 212992;     // [2] x (g, G, eG, eD): 8 x 64 f32; barriers
-constexpr int kStateSmem = kS_Misc + 8 * 64 * 4 + 256 + 1024;
+constexpr int kS_W = 0;             // W^T [128 k x 64 t] fp16 (16 KB)
+constexpr int kS_Q = 16384;         // q hi [64 t x 128 k] fp16: 2 boxes [64 x 64], x2 buffers (32 KB)
+constexpr int kS_P = 49152;         // P' hi, lo [64 t x 64 s] (8 KB each) (16 KB)
+constexpr int kS_K = 65536;         // k hi, lo [64 s x 128 k] (16 KB each), x2 buffers (64 KB)
+constexpr int kS_Us = 131072;       // (U diag D)^T hi, lo [128 v x 64 s] (16 KB each)
+constexpr int kS_Uu = 163840;       // U^T hi, lo (16 KB each)
+constexpr int kS_Y = 196608;        // y staging, half a chunk: [32 t][128 v] f32 (16 KB)
+constexpr int kS_Misc = 212992;     // [4] x (g, G, eG, eD): 16 x 64 f32; barriers
+constexpr int kMiscSlots = 4;       // chunk c's decays in slot c & 3
+constexpr int kStateSmem = kS_Misc + kMiscSlots * 4 * 64 * 4 + 256 + 1024;
 // TMEM columns: S f32 [0,128), S0 fp16 pairs x2 [128,256), U2 f32 x2 [256,384), Y1 [384,448), Y2 [448,512)
 constexpr uint32_t kTmS = 0, kTmS0h = 128, kTmU2 = 256, kTmY1 = 384, kTmY2 = 448;
 constexpr uint32_t kNegB = 1u << 14;
@@ -649,6 +651,7 @@ struct StateBars {  // the first 11 words are tracked by Pending (in this order)
     uint64_t m4, m7, mY, spare;                        // MMA completions
     uint64_t u2_ready, dec_ready[2];                   // warps 4-7 -> thread 0 (128 arrivals)
     uint64_t u_ready, s_read[2];                       // thread 0 -> warps 4-7 (1 arrival)
+    uint64_t y_free;                                   // warps 8-11 read Y out (128 arrivals)
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -695,7 +698,7 @@ __device__ __forceinline__ void store_u_split(uint8_t* smem_hi, uint8_t* smem_lo
     }
 }
 
-constexpr int kStateThreads = 256;  // warps 0-3: the recurrence; 4-7: beside it
+constexpr int kStateThreads = 384;  // warps 0-3: the recurrence; 4-7: beside it; 8-11: y
 
 __global__ void __launch_bounds__(kStateThreads, 1)
 dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ CUtensorMap tph,
@@ -707,7 +710,7 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     float* misc = reinterpret_cast<float*>(smem + kS_Misc);  // slot s: g, G, eG, eD at misc + 256 s
-    StateBars* bars = reinterpret_cast<StateBars*>(misc + 8 * 64);
+    StateBars* bars = reinterpret_cast<StateBars*>(misc + kMiscSlots * 256);
     volatile int* abort_flag = &bars->abort_flag;
     const uint32_t sb = smem_u32(smem);
 
@@ -735,6 +738,7 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         mbar_init(smem_u32(&bars->u_ready), 1);
         mbar_init(smem_u32(&bars->s_read[0]), 1);
         mbar_init(smem_u32(&bars->s_read[1]), 1);
+        mbar_init(smem_u32(&bars->y_free), 128);
         bars->abort_flag = 0;
         fence_barrier_init();
     }
@@ -754,11 +758,11 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
     };
 
     // ---- loads (thread 0: W^T, k; thread 128: q, P') ----
-    auto issue_w = [&](int c) {  // W^T of chunk c into buffer c & 1
-        uint64_t* fb = &bars->w_full[c & 1];
-        pend.start(fb, (c >> 1) & 1);
+    auto issue_w = [&](int c) {  // W^T of chunk c (one buffer: loaded as soon as MMA4 of c-1 is done)
+        uint64_t* fb = &bars->w_full[0];
+        pend.start(fb, c & 1);
         mbar_arrive_expect_tx(smem_u32(fb), 16384);
-        tma_load_3d(sb + kS_W + (c & 1) * 16384, &twt, 0, 0, (int)(item0 + c), smem_u32(fb));
+        tma_load_3d(sb + kS_W, &twt, 0, 0, (int)(item0 + c), smem_u32(fb));
     };
     auto issue_q = [&](int c) {  // q hi of chunk c into buffer c & 1
         uint64_t* fb = &bars->q_full[c & 1];
@@ -787,10 +791,7 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
     if (tid == 0) {
         issue_w(0);
         issue_k(0);
-        if (nch > 1) {
-            issue_w(1);
-            issue_k(1);
-        }
+        if (nch > 1) issue_k(1);
     }
     if (tid == 128) {
         issue_q(0);
@@ -837,12 +838,12 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
             const int p = ci & 1;
             // ---- MMA4: U2[p] (= U~) -= S0[p] W^T ----
             if (tid == 0) {
-                const bool w = wait(&bars->w_full[p], (ci >> 1) & 1) && wait(&bars->u2_ready, p);
+                const bool w = wait(&bars->w_full[0], p) && wait(&bars->u2_ready, p);
                 tc_fence_after();
                 if (w) {
                     for (int kk = 0; kk < 8; kk++)
                         umma_f16_ts(tm + kTmU2 + p * 64, tm + kTmS0h + p * 64 + kk * 8,
-                                    umma_sdesc(sb + kS_W + p * 16384 + kk * 2048, 8192, 1024), kIdSW, 1u);
+                                    umma_sdesc(sb + kS_W + kk * 2048, 8192, 1024), kIdSW, 1u);
                 }
                 umma_commit(smem_u32(&bars->m4));
                 pend.start(&bars->m4, p);
@@ -855,14 +856,14 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
             }
             if (!ok) break;
             tc_fence_after();
-            if (tid == 0 && ci + 2 < nch) issue_w(ci + 2);  // MMA4 has read W^T buffer p
+            if (tid == 0 && ci + 1 < nch) issue_w(ci + 1);  // MMA4 has read W^T
 
             // ---- U step: (U diag D)^T -> fp16 hi/lo (MMA7 of chunk ci-1 is done with them) ----
             {
                 float u[64];
                 tmem_ld32(tm + lane_addr + kTmU2 + p * 64, u);
                 tmem_ld32(tm + lane_addr + kTmU2 + p * 64 + 32, u + 32);
-                const float* eD = misc + p * 256 + 192;
+                const float* eD = misc + (ci & 3) * 256 + 192;
                 tmem_ld_wait();
 #pragma unroll
                 for (int s = 0; s < kC; s++) u[s] *= eD[s];
@@ -904,7 +905,7 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
             if (ci + 1 < nch) {
                 // dec_ready[c&1] completes once per two chunks: phase (c >> 1) for chunk c
                 ok = mbar_wait_bounded(smem_u32(&bars->dec_ready[(ci + 1) & 1]), ((ci + 1) >> 1) & 1, abort_flag, err);
-                const float decay = misc[((ci + 1) & 1) * 256 + 128 + kC - 1];
+                const float decay = misc[((ci + 1) & 3) * 256 + 128 + kC - 1];
 #pragma unroll 1
                 for (int h = 0; h < 2; h++) {
                     float sv[64], pk[32];
@@ -943,7 +944,7 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
                         make_float4(sv[i], sv[i + 1], sv[i + 2], sv[i + 3]);
             }
         }
-    } else {
+    } else if (warp < 8) {
         // ================= warps 4-7: beside the chain =================
         // Every thread here runs every step (the named barriers need all 128);
         // after an abort the bounded waits return at once and the work is skipped.
@@ -974,31 +975,12 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
             g_next = (at < kC && c < nch && t < T) ? gin[plane_v * T + t] : 0.f;
         };
         auto decays = [&](int c) {  // the gates of chunk c (in g_next) -> slot c&1, then dec_ready[c&1]
-            float* sgp = misc + (c & 1) * 256;
+            float* sgp = misc + (c & 3) * 256;
             if (at < kC) sgp[at] = g_next;
             named_bar_sync(2, 128);
             if (warp == 4) chunk_decays(sgp, sgp + 64, sgp + 128, sgp + 192, lane);
             named_bar_sync(2, 128);
             mbar_arrive(smem_u32(&bars->dec_ready[c & 1]));
-        };
-        auto write_y = [&](int c) {  // y_t = e^G_t Y1_t + Y2_t, staged [64 t][128 v], one TMA store
-            const float* eG = misc + (c & 1) * 256 + 128;
-            float y1[64], y2[64];
-            tmem_ld32(tm + lane_addr + kTmY1, y1);
-            tmem_ld32(tm + lane_addr + kTmY1 + 32, y1 + 32);
-            tmem_ld32(tm + lane_addr + kTmY2, y2);
-            tmem_ld32(tm + lane_addr + kTmY2 + 32, y2 + 32);
-            tmem_ld_wait();
-            tc_fence_before();
-            float* ys = reinterpret_cast<float*>(smem + kS_Uu);
-#pragma unroll
-            for (int t = 0; t < kC; t++) ys[t * kHd + row] = fmaf(eG[t], y1[t], y2[t]);
-            fence_proxy_async_shared();
-            named_bar_sync(2, 128);
-            if (at == 0) {  // tokens past T are outside the tensor and not written
-                tma_store_3d(&tyo, sb + kS_Uu, vh * kHd, c * kC, b);
-                bulk_commit();
-            }
         };
         // ---- before chunk 0: its decays, U~ -> U2[0] ----
         load_g(0);
@@ -1012,18 +994,17 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
             const int p = ci & 1;
             const bool more = ci + 1 < nch;
             // ---- the decays of chunk ci+1 first: the S pass of chunk ci waits for them.
-            // Slot (ci+1)&1 was last read by the U step of ci-1 (u_ready of ci-1 seen)
-            // and by y of ci-1; dec_ready[(ci+1)&1] last completed for chunk ci-1,
-            // whose S pass waited for it before the U step of ci ----
+            // Slot (ci+1)&3 was last read for chunk ci-3 (its y read out before MMA5 of
+            // ci-1 began); dec_ready[(ci+1)&1] last completed for chunk ci-1, whose S
+            // pass waited for it before the U step of ci ----
             if (more) {
                 decays(ci + 1);
                 load_g(ci + 2);
             }
-            // ---- MMA5: Y1 = S0 q^T (Y of ci-1 was read out; its staged copy has
-            // been read by the TMA store before U^T is written there again) ----
+            // ---- MMA5: Y1 = S0 q^T, once warps 8-11 have read Y of chunk ci-1 ----
             bool qok = ok && wait(&bars->q_full[p], (ci >> 1) & 1);
             if (at == 0) {
-                bulk_wait_read0();
+                if (ci > 0) qok = qok && mbar_wait_bounded(smem_u32(&bars->y_free), (ci - 1) & 1, abort_flag, err);
                 qok = qok && mbar_wait_bounded(smem_u32(&bars->s_read[p]), (ci >> 1) & 1, abort_flag, err);  // S0 of ci
             }
             tc_fence_before();
@@ -1071,20 +1052,59 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
                 store_ut(ci + 1);  // U2[(ci+1)&1] was read in chunk ci-1
                 if (ci + 2 < nch) load_ut(ci + 2);
             }
-            // ---- MMA5 / MMA6 done: next q and P' loads; S scaled for chunk ci+1 ----
+            // ---- MMA5 / MMA6 done (U^T hi/lo is free again): next q and P' loads ----
             const bool wy = ok && wait(&bars->mY, p);
-            ok = wy;
+            ok = wy && !*abort_flag;
             if (at == 0 && ok) {
                 if (more) issue_p(ci + 1);
                 if (ci + 2 < nch) issue_q(ci + 2);  // MMA5 of ci has read q buffer p
             }
-            // ---- y of chunk ci (every operand thread takes part: named barrier) ----
-            tc_fence_after();
-            if (wy) write_y(ci);
-            else named_bar_sync(2, 128);
-            ok = ok && !*abort_flag;
         }
-        if (at == 0) bulk_wait0();  // the last y stores have completed
+    } else {
+        // ================= warps 8-11: y =================
+        // Per chunk: wait for MMA5/MMA6, read Y1 and Y2 from TMEM, form
+        // y_t = e^G_t Y1_t + Y2_t (the decays are read before y_free releases Y,
+        // which bounds how far warps 4-7 can reuse their slot), then write it in
+        // two halves of 32 tokens through a 16 KB staging buffer and TMA stores
+        // (tokens past T lie outside the tensor map and are not written).
+        const int yt = tid - 256;
+        bool ok = true;
+        for (int ci = 0; ci < nch; ci++) {
+            const bool wy = ok && mbar_wait_bounded(smem_u32(&bars->mY), ci & 1, abort_flag, err);
+            ok = wy && !*abort_flag;
+            float yv[64];
+            if (wy) {
+                tc_fence_after();
+                float y2[64];
+                tmem_ld32(tm + lane_addr + kTmY1, yv);
+                tmem_ld32(tm + lane_addr + kTmY1 + 32, yv + 32);
+                tmem_ld32(tm + lane_addr + kTmY2, y2);
+                tmem_ld32(tm + lane_addr + kTmY2 + 32, y2 + 32);
+                tmem_ld_wait();
+                const float* eG = misc + (ci & 3) * 256 + 128;
+#pragma unroll
+                for (int t = 0; t < kC; t++) yv[t] = fmaf(eG[t], yv[t], y2[t]);
+            }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&bars->y_free));
+            float* ys = reinterpret_cast<float*>(smem + kS_Y);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                if (yt == 0) bulk_wait_read0();  // the previous store has read the buffer
+                named_bar_sync(3, 128);
+                if (wy) {
+#pragma unroll
+                    for (int t = 0; t < kC / 2; t++) ys[t * kHd + row] = yv[32 * h + t];
+                }
+                fence_proxy_async_shared();
+                named_bar_sync(3, 128);
+                if (yt == 0 && wy) {
+                    tma_store_3d(&tyo, sb + kS_Y, vh * kHd, ci * kC + 32 * h, b);
+                    bulk_commit();
+                }
+            }
+        }
+        if (yt == 0) bulk_wait0();  // the last y stores have completed
     }
     // do not leave while copies or MMAs this CTA issued may still land
     pend.drain();
@@ -1198,7 +1218,7 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
     if (encode_rows_tmap(&mwt, wt, kC, kHd, items, 64, kHd, true) != QM_OK ||
         encode_rows_tmap(&mph, ph, kC, kC, items, 64, kC, true) != QM_OK ||
         encode_rows_tmap(&mpl, pl, kC, kC, items, 64, kC, true) != QM_OK ||
-        encode_f32_tmap(&myo, y, kVDim, (uint64_t)T, (uint64_t)B, kHd, kC) != QM_OK)
+        encode_f32_tmap(&myo, y, kVDim, (uint64_t)T, (uint64_t)B, kHd, kC / 2) != QM_OK)
         return cudaErrorInvalidValue;
     static std::atomic<uint64_t> attr_local{0}, attr_state{0};
     e = set_smem_once(attr_local, ctx->device, dn_chunk_local, kLocalSmem);
