@@ -621,10 +621,12 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
 // (the fp16 S0 of the next chunk, and S scaled by that chunk's e^G63 for its
 // MMA7, in one read of S); thread 0 issues MMA4, MMA7 and the W^T and k
 // loads.  Warps 4-7 run beside it: each chunk's decays, U~ of the next chunk
-// into TMEM, the unscaled U hi/lo for MMA6, and y (staged in shared memory,
-// one TMA store per chunk); their thread 128 issues MMA5 / MMA6 and the q
-// and P' loads.  mbarriers hand over: u2_ready, dec_ready (warps 4-7 ->
-// thread 0); u_ready, s_read (thread 0 -> warps 4-7).  dec_ready and s_read
+// into TMEM, the unscaled U hi/lo for MMA6; their thread 128 issues MMA5 /
+// MMA6.  Warps 8-11 wait for those, write y (staged in shared memory, TMA
+// stores of half chunks) and their thread 256 issues the next q and P'
+// loads.  mbarriers hand over: u2_ready, dec_ready (warps 4-7 -> thread 0);
+// u_ready, s_read (thread 0 -> warps 4-7); y_free (warps 8-11 -> warps 4-7,
+// which also frees U^T hi/lo and q for reuse).  dec_ready and s_read
 // are pairs used by chunk parity (phase c >> 1 for chunk c): either side may
 // publish a chunk's piece one chunk early without a phase running two ahead
 // of its waiter.
@@ -1052,13 +1054,9 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
                 store_ut(ci + 1);  // U2[(ci+1)&1] was read in chunk ci-1
                 if (ci + 2 < nch) load_ut(ci + 2);
             }
-            // ---- MMA5 / MMA6 done (U^T hi/lo is free again): next q and P' loads ----
-            const bool wy = ok && wait(&bars->mY, p);
-            ok = wy && !*abort_flag;
-            if (at == 0 && ok) {
-                if (more) issue_p(ci + 1);
-                if (ci + 2 < nch) issue_q(ci + 2);  // MMA5 of ci has read q buffer p
-            }
+            // (the next q and P' loads are issued by warps 8-11 once MMA5/MMA6 are
+            // done; U^T hi/lo is rewritten only after y_free of ci, which follows them)
+            ok = ok && !*abort_flag;
         }
     } else {
         // ================= warps 8-11: y =================
@@ -1070,8 +1068,12 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         const int yt = tid - 256;
         bool ok = true;
         for (int ci = 0; ci < nch; ci++) {
-            const bool wy = ok && mbar_wait_bounded(smem_u32(&bars->mY), ci & 1, abort_flag, err);
+            const bool wy = ok && wait(&bars->mY, ci & 1);
             ok = wy && !*abort_flag;
+            if (yt == 0 && ok) {  // MMA6 of ci has read P', MMA5 of ci q buffer ci&1
+                if (ci + 1 < nch) issue_p(ci + 1);
+                if (ci + 2 < nch) issue_q(ci + 2);
+            }
             float yv[64];
             if (wy) {
                 tc_fence_after();
