@@ -320,19 +320,17 @@ struct ChunkBars {
 // 102 KB of shared memory and 256 TMEM columns: two CTAs per SM.  Warps w and
 // w+4 share TMEM lane quarter w%4 and split the 64 columns of every TMEM tile.
 constexpr int kL_KQh = 0;              // [K;Q] hi: 2 boxes [128 rows x 64] fp16 (K rows 0-63,
-constexpr int kL_KQl = 32768;          //   Q rows 64-127); after MMA1 the four Q quarters
-constexpr int kL_T1h = kL_KQh + 8192;  //   hold T' and T'' (hi/lo), 8 KB each
-constexpr int kL_T1l = kL_KQh + 24576;
-constexpr int kL_T2h = kL_KQl + 8192;
-constexpr int kL_T2l = kL_KQl + 24576;
+constexpr int kL_KQl = 32768;          //   Q rows 64-127); once MMA1 is done the four Q
+constexpr int kL_Vh = kL_KQh + 8192;   //   quarters take V hi / lo [64 t x 64 v] (the boxes
+constexpr int kL_Vl = kL_KQl + 8192;   //   of v columns 64-127 16 KB further on)
 constexpr int kAStride = 68;           // floats per A / T row (float4-aligned)
 constexpr int kL_A = 65536;            // A f32 [64][68] and T f32 [64][68] during the
-constexpr int kL_Tm = kL_A + 64 * kAStride * 4;  // solve, then V hi (2 boxes [64 x 64])
-constexpr int kL_Vh = 65536;           //   and V lo on top of them
-constexpr int kL_Vl = 81920;
+constexpr int kL_Tm = kL_A + 64 * kAStride * 4;  // solve, then T' hi/lo over A, T'' hi/lo over T
+constexpr int kL_T1h = kL_A, kL_T1l = kL_A + 8192, kL_T2h = kL_Tm, kL_T2l = kL_Tm + 8192;
 constexpr int kL_Misc = kL_Tm + 64 * kAStride * 4;  // G, beta, g, b e^G, e^G, e^(G63-G): 6 x 64 f32
 constexpr int kLocalSmem = kL_Misc + 6 * 64 * 4 + 64 + 1024;
-static_assert(kL_Vl + 16384 <= kL_Misc, "V fits over A and T");
+static_assert(kL_T1l + 8192 <= kL_Tm && kL_T2l + 8192 <= kL_Misc, "T' over A, T'' over T");
+static_assert(kL_Tm % 1024 == 0 && kL_T2l % 1024 == 0, "swizzled tiles on 1024-byte boundaries");
 constexpr uint32_t kTmKQ = 0, kTmW = 64, kTmU = 128;
 constexpr int kLocalThreads = 256;
 
@@ -429,6 +427,16 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
         ok = mbar_wait_bounded(smem_u32(&bars->mma), 0, abort_flag, err);
         if (ok) mm_out = false;
     }
+    if (ok && tid == 0) {  // MMA1 has read Q: V lands in its quarters during the solve
+        const uint32_t lb = smem_u32(&bars->load);
+        mbar_arrive_expect_tx(lb, 4 * 8192);
+        ld_out = true;
+        ld_par = 1;
+        for (int hb = 0; hb < 2; hb++) {
+            tma_load_3d(sb + kL_Vh + hb * 16384, &tvh, hb * 64, t0, (int)plane_v, lb);
+            tma_load_3d(sb + kL_Vl + hb * 16384, &tvl, hb * 64, t0, (int)plane_v, lb);
+        }
+    }
     ok = __syncthreads_and(ok) != 0;
     tc_fence_after();
 
@@ -510,9 +518,14 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
         tri_inverse_diagonal<1, kLocalThreads>(Amat, Tm, tid);
         tri_inverse_diagonal<2, kLocalThreads>(Amat, Tm, tid);
         tri_inverse_diagonal<3, kLocalThreads>(Amat, Tm, tid);
-        // T' = T diag(b e^G), T'' = T diag(b) as fp16 hi/lo [t][j] tiles (upper part zero)
-        for (int o = tid; o < kC * 8; o += kLocalThreads) {
-            const int t = o >> 3, jc = o & 7, j0 = jc * 8;
+        // T' = T diag(b e^G), T'' = T diag(b) as fp16 hi/lo [t][j] tiles (upper
+        // part zero), formed in registers and written over A and T once every
+        // thread has read its part of T
+        static_assert(kC * 8 == 2 * kLocalThreads, "two 8-column pieces of T a thread");
+        uint4 t1h[2], t1l[2], t2h[2], t2l[2];
+#pragma unroll
+        for (int it = 0; it < 2; it++) {
+            const int o = tid + it * kLocalThreads, t = o >> 3, j0 = (o & 7) * 8;
             float v1[8], v2[8];
 #pragma unroll
             for (int q = 0; q < 8; q++) {
@@ -521,29 +534,27 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
                 v1[q] = tv * sC1[j];
                 v2[q] = tv * sB[j];
             }
-            uint4 h, l;
-            split8(v1, h, l);
-            *reinterpret_cast<uint4*>(smem + kL_T1h + sw128_off(t, jc)) = h;
-            *reinterpret_cast<uint4*>(smem + kL_T1l + sw128_off(t, jc)) = l;
-            split8(v2, h, l);
-            *reinterpret_cast<uint4*>(smem + kL_T2h + sw128_off(t, jc)) = h;
-            *reinterpret_cast<uint4*>(smem + kL_T2l + sw128_off(t, jc)) = l;
+            split8(v1, t1h[it], t1l[it]);
+            split8(v2, t2h[it], t2l[it]);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < 2; it++) {
+            const int o = tid + it * kLocalThreads;
+            const uint32_t so = sw128_off(o >> 3, o & 7);
+            *reinterpret_cast<uint4*>(smem + kL_T1h + so) = t1h[it];
+            *reinterpret_cast<uint4*>(smem + kL_T1l + so) = t1l[it];
+            *reinterpret_cast<uint4*>(smem + kL_T2h + so) = t2h[it];
+            *reinterpret_cast<uint4*>(smem + kL_T2l + so) = t2l[it];
         }
     }
-    fence_proxy_async_shared();
+    fence_proxy_async_shared();  // the T tiles, for the tensor core
     tc_fence_before();
-    __syncthreads();  // A is dead from here: V lands on it
+    __syncthreads();
 
-    // ---- MMA2 (W^T) now; V load; MMA3 (U~^T) once V has landed ----
+    // ---- MMA2 (W^T) now, MMA3 (U~^T) once V has landed ----
     if (ok && tid == 0) {
         const uint32_t lb = smem_u32(&bars->load);
-        mbar_arrive_expect_tx(lb, 4 * 8192);
-        ld_out = true;
-        ld_par = 1;
-        for (int hb = 0; hb < 2; hb++) {
-            tma_load_3d(sb + kL_Vh + hb * 8192, &tvh, hb * 64, t0, (int)plane_v, lb);
-            tma_load_3d(sb + kL_Vl + hb * 8192, &tvl, hb * 64, t0, (int)plane_v, lb);
-        }
         tc_fence_after();
         int n = 0;
         for (int term = 0; term < 3; term++) {
@@ -561,7 +572,7 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
                 const uint32_t va = sb + (term == 2 ? kL_Vl : kL_Vh);
                 const uint32_t tb = sb + (term == 1 ? kL_T2l : kL_T2h);
                 for (int kk = 0; kk < 4; kk++, n++)
-                    umma_bf16_ss(tm + kTmU, umma_sdesc(va + kk * 2048, 8192, 1024),
+                    umma_bf16_ss(tm + kTmU, umma_sdesc(va + kk * 2048, 16384, 1024),
                                  umma_sdesc(tb + kk * 32, 16, 1024), kIdW, n > 0);
             }
         }
