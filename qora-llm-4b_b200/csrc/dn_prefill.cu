@@ -239,63 +239,42 @@ __device__ __forceinline__ void chunk_decays(const float* sg, float* sG, float* 
     }
 }
 
-// One block diagonal d (pairs (i, j) = (j + d, j), j = 0 .. 3-d) of the blocked
-// unit-lower-triangular inverse T of I + A (row stride kAStride floats):
-//   X_ij = sum_{k=j}^{i-1} A_ik T_kj   (kept in the unused upper block (j, i))
-//   T_ij = -T_ii X_ij                  (T_ii stored with zeros above its diagonal)
-// A work item is 4 adjacent columns of one row of one block: float4 loads of
-// T / X rows serve all four, and a warp's 8 rows x 4 column groups read
-// distinct banks (rows are 68 floats apart).  (4 - D) * 64 items over NT
-// threads; all trip counts are compile-time.
-template <int D, int NT>
-__device__ __forceinline__ void tri_inverse_diagonal(const float* __restrict__ A, float* __restrict__ Tm,
-                                                     int tid) {
-    constexpr int kStride = 68;
-    constexpr int NITEM = (4 - D) * 64;
-    static_assert(NITEM <= NT, "one item per thread");
-    const bool active = tid < NITEM;
-    const int c4 = tid & 3, r = (tid >> 2) & 15, j = tid >> 6, i = j + D;
-    if (active) {
-        const float* arow = A + (16 * i + r) * kStride + 16 * j;
-        const float* tcol = Tm + (16 * j) * kStride + 16 * j + 4 * c4;
-        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+// c (a 16 x 8 tile) += X[16 rows][k0, k1) Y[k0, k1)[8 columns] for f32 X and Y
+// in shared memory (row stride 68 floats), as three TF32 products per k-step
+// (lo.hi + hi.lo + hi.hi: about 22 significant bits, f32 range).  X rows and
+// Y columns start at the pointers; k0, k1 are multiples of 8.  Fragment loads
+// of X touch 32 distinct banks (rows 68 floats apart).
+__device__ __forceinline__ void mma3_tf32_tile(float (&c)[4], const float* __restrict__ X,
+                                               const float* __restrict__ Y, int k0, int k1, int lane) {
+    constexpr int S = 68;
+    const int g = lane >> 2, t = lane & 3;
+    for (int k = k0; k < k1; k += 8) {
+        const float af[4] = {X[g * S + k + t], X[(g + 8) * S + k + t], X[g * S + k + t + 4],
+                             X[(g + 8) * S + k + t + 4]};
+        const float bf[2] = {Y[(k + t) * S + g], Y[(k + t + 4) * S + g]};
+        uint32_t ah[4], al[4], bh[2], bl[2];
 #pragma unroll
-        for (int u = 0; u < 16 * D; u += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(arow + u);
-            const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const float4 t = *reinterpret_cast<const float4*>(tcol + (u + q) * kStride);
-                x.x = fmaf(av[q], t.x, x.x);
-                x.y = fmaf(av[q], t.y, x.y);
-                x.z = fmaf(av[q], t.z, x.z);
-                x.w = fmaf(av[q], t.w, x.w);
-            }
+        for (int i = 0; i < 4; i++) {
+            ah[i] = tf32_rna(af[i]);
+            al[i] = tf32_rna(af[i] - __uint_as_float(ah[i]));
         }
-        *reinterpret_cast<float4*>(Tm + (16 * j + r) * kStride + 16 * i + 4 * c4) = x;
-    }
-    __syncthreads();
-    if (active) {
-        const float* trow = Tm + (16 * i + r) * kStride + 16 * i;
-        const float* xcol = Tm + (16 * j) * kStride + 16 * i + 4 * c4;
-        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int u = 0; u < 16; u += 4) {
-            const float4 t = *reinterpret_cast<const float4*>(trow + u);
-            const float tv[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const float4 xv = *reinterpret_cast<const float4*>(xcol + (u + q) * kStride);
-                x.x = fmaf(tv[q], xv.x, x.x);
-                x.y = fmaf(tv[q], xv.y, x.y);
-                x.z = fmaf(tv[q], xv.z, x.z);
-                x.w = fmaf(tv[q], xv.w, x.w);
-            }
+        for (int i = 0; i < 2; i++) {
+            bh[i] = tf32_rna(bf[i]);
+            bl[i] = tf32_rna(bf[i] - __uint_as_float(bh[i]));
         }
-        *reinterpret_cast<float4*>(Tm + (16 * i + r) * kStride + 16 * j + 4 * c4) =
-            make_float4(-x.x, -x.y, -x.z, -x.w);
+        mma_tf32_1688(c, al[0], al[1], al[2], al[3], bh[0], bh[1]);
+        mma_tf32_1688(c, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+        mma_tf32_1688(c, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
     }
-    __syncthreads();
+}
+
+// stores s * c (a 16 x 8 accumulator tile) at Z (row stride 68 floats)
+__device__ __forceinline__ void store_tile_1688(float* __restrict__ Z, const float (&c)[4], float s, int lane) {
+    constexpr int S = 68;
+    const int g = lane >> 2, t = lane & 3;
+    *reinterpret_cast<float2*>(Z + g * S + 2 * t) = make_float2(s * c[0], s * c[1]);
+    *reinterpret_cast<float2*>(Z + (g + 8) * S + 2 * t) = make_float2(s * c[2], s * c[3]);
 }
 
 struct ChunkBars {
@@ -338,7 +317,7 @@ __global__ void __launch_bounds__(kLocalThreads, 2)
 dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ CUtensorMap tql,
                const __grid_constant__ CUtensorMap tkh, const __grid_constant__ CUtensorMap tkl,
                const __grid_constant__ CUtensorMap tvh, const __grid_constant__ CUtensorMap tvl,
-               const float* __restrict__ gin, const float* __restrict__ bin, int T, int nch,
+               const float* __restrict__ gin, const float* __restrict__ bin, int T, int nch, int B,
                uint16_t* __restrict__ wt_out, float* __restrict__ ut_out,
                uint16_t* __restrict__ ph_out, uint16_t* __restrict__ pl_out, int* err) {
     extern __shared__ uint8_t smem_raw[];
@@ -355,255 +334,330 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
     volatile int* abort_flag = &bars->abort_flag;
     const uint32_t sb = smem_u32(smem);
 
-    const int vh = blockIdx.x, ci = blockIdx.y, b = blockIdx.z, qk = vh >> 1;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quarter = warp & 3, half = warp >> 2;  // TMEM lanes 32*quarter.., columns 32*half..
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const int row = quarter * 32 + lane;              // TMEM lane = tile row
-    const int t0 = ci * kC, tc = min(kC, T - t0);
-    const size_t plane_qk = (size_t)b * kNumQK + qk, plane_v = (size_t)b * kNumV + vh;
-    const size_t item = ((size_t)b * kNumV + vh) * nch + ci;
+    const int nitems = B * kNumV * nch;
+    // work item L: V head L % 32 (the two V heads of a QK head side by side, so
+    // their K/Q tiles meet in L2), then chunk, then sequence
+    auto item_of = [&](int L, int& vh, int& ci, int& b) {
+        vh = L % kNumV;
+        ci = (L / kNumV) % nch;
+        b = L / (kNumV * nch);
+    };
+    auto load_kq = [&](int vh, int ci, int b) {  // thread 0
+        const uint32_t lb = smem_u32(&bars->load);
+        const int t0 = ci * kC, plane_qk = b * kNumQK + (vh >> 1);
+        mbar_arrive_expect_tx(lb, 8 * 8192);
+        for (int hb = 0; hb < 2; hb++) {
+            tma_load_3d(sb + kL_KQh + hb * 16384, &tkh, hb * 64, t0, plane_qk, lb);
+            tma_load_3d(sb + kL_KQl + hb * 16384, &tkl, hb * 64, t0, plane_qk, lb);
+            tma_load_3d(sb + kL_KQh + hb * 16384 + 8192, &tqh, hb * 64, t0, plane_qk, lb);
+            tma_load_3d(sb + kL_KQl + hb * 16384 + 8192, &tql, hb * 64, t0, plane_qk, lb);
+        }
+    };
+    auto load_gates = [&](int vh, int ci, int b, float& g, float& be) {
+        const int t = ci * kC + tid;
+        g = be = 0.f;
+        if (tid < kC && t < T) {
+            const size_t o = ((size_t)b * kNumV + vh) * T + t;
+            g = gin[o];
+            be = bin[o];
+        }
+    };
 
-    // the gates first (a dependent global load), then the K/Q tiles as soon as
-    // the load barrier exists; both arrive while the CTA sets up
+    // the first item's gates and K/Q tiles arrive while the CTA sets up; each
+    // later item's are requested as soon as the previous item's tensor-core
+    // work is done, and arrive during its outputs
+    int L = blockIdx.x;
     float g_own = 0.f, b_own = 0.f;
-    if (tid < tc) {
-        g_own = gin[plane_v * T + t0 + tid];
-        b_own = bin[plane_v * T + t0 + tid];
-    }
     // thread 0's record of the last phase it started on each barrier and not
     // yet seen complete (drained on the way out of an aborted CTA)
     bool ld_out = false, mm_out = false;
     uint32_t ld_par = 0, mm_par = 0;
-    if (tid == 0) {
-        mbar_init(smem_u32(&bars->load), 1);
-        mbar_init(smem_u32(&bars->mma), 1);
-        bars->abort_flag = 0;
-        fence_barrier_init();
-        const uint32_t lb = smem_u32(&bars->load);
-        mbar_arrive_expect_tx(lb, 8 * 8192);
-        ld_out = true;
-        for (int hb = 0; hb < 2; hb++) {
-            tma_load_3d(sb + kL_KQh + hb * 16384, &tkh, hb * 64, t0, (int)plane_qk, lb);
-            tma_load_3d(sb + kL_KQl + hb * 16384, &tkl, hb * 64, t0, (int)plane_qk, lb);
-            tma_load_3d(sb + kL_KQh + hb * 16384 + 8192, &tqh, hb * 64, t0, (int)plane_qk, lb);
-            tma_load_3d(sb + kL_KQl + hb * 16384 + 8192, &tql, hb * 64, t0, (int)plane_qk, lb);
+    {
+        int vh, ci, b;
+        item_of(L, vh, ci, b);
+        if (L < nitems) load_gates(vh, ci, b, g_own, b_own);
+        if (tid == 0) {
+            mbar_init(smem_u32(&bars->load), 1);
+            mbar_init(smem_u32(&bars->mma), 1);
+            bars->abort_flag = 0;
+            fence_barrier_init();
+            if (L < nitems) {
+                load_kq(vh, ci, b);
+                ld_out = true;
+            }
         }
     }
     if (warp == 0) {
         tmem_alloc(smem_u32(&bars->tmem_base), 256);
         tmem_relinquish();
     }
-    if (tid < kC) {
-        sg[tid] = g_own;
-        sB[tid] = b_own;
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = bars->tmem_base;
-    if (warp == 0) chunk_decays(sg, sG, eG, eD, lane);
-    bool ok = mbar_wait_bounded(smem_u32(&bars->load), 0, abort_flag, err);
-    if (ok) ld_out = false;
-    ok = __syncthreads_and(ok) != 0;  // also publishes sG
+    bool ok = true;
 
-    // ---- MMA1: [K;Q] K^T (compensated) -> TMEM KQ ----
-    if (ok && tid == 0) {
-        tc_fence_after();
-        int n = 0;
-        for (int term = 0; term < 3; term++) {
-            const uint32_t abase = sb + (term == 2 ? kL_KQl : kL_KQh);
-            const uint32_t bbase = sb + (term == 1 ? kL_KQl : kL_KQh);
-            for (int kk = 0; kk < 8; kk++, n++) {
-                const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                umma_bf16_ss(tm + kTmKQ, umma_sdesc(abase + off, 16, 1024),
-                             umma_sdesc(bbase + off, 16, 1024), kIdKK, n > 0);
-            }
-        }
-        umma_commit(smem_u32(&bars->mma));
-        mm_out = true;
-    }
-    if (ok) {
-        ok = mbar_wait_bounded(smem_u32(&bars->mma), 0, abort_flag, err);
-        if (ok) mm_out = false;
-    }
-    if (ok && tid == 0) {  // MMA1 has read Q: V lands in its quarters during the solve
-        const uint32_t lb = smem_u32(&bars->load);
-        mbar_arrive_expect_tx(lb, 4 * 8192);
-        ld_out = true;
-        ld_par = 1;
-        for (int hb = 0; hb < 2; hb++) {
-            tma_load_3d(sb + kL_Vh + hb * 16384, &tvh, hb * 64, t0, (int)plane_v, lb);
-            tma_load_3d(sb + kL_Vl + hb * 16384, &tvl, hb * 64, t0, (int)plane_v, lb);
-        }
-    }
-    ok = __syncthreads_and(ok) != 0;
-    tc_fence_after();
-
-    // ---- rows 0-63: A (f32, shared); rows 64-127: P' hi/lo (global); this
-    // thread's 32 columns [s0, s0 + 32) ----
-    if (ok) {
-        float kq[32];
-        const int s0 = half * 32;
-        tmem_ld32(tm + lane_addr + kTmKQ + s0, kq);
-        tmem_ld_wait();
-        if (row < kC) {
-            const int t = row;
-            const float Gt = sG[t], bt = sB[t];
-            float* arow = Amat + t * kAStride + s0;
-            if (QM_IN(t * kAStride + s0, 32, kC * kAStride, err))
-#pragma unroll
-            for (int i = 0; i < 32; i += 4) {
-                const int s = s0 + i;
-                float4 v;
-                v.x = (s + 0 < t) ? bt * ex2_approx(Gt - sG[s + 0]) * kq[i + 0] : 0.f;
-                v.y = (s + 1 < t) ? bt * ex2_approx(Gt - sG[s + 1]) * kq[i + 1] : 0.f;
-                v.z = (s + 2 < t) ? bt * ex2_approx(Gt - sG[s + 2]) * kq[i + 2] : 0.f;
-                v.w = (s + 3 < t) ? bt * ex2_approx(Gt - sG[s + 3]) * kq[i + 3] : 0.f;
-                *reinterpret_cast<float4*>(arow + i) = v;
-            }
-        } else {
-            const int t = row - kC;
-            const float Gt = sG[t];
-            const size_t items = (size_t)gridDim.x * gridDim.y * gridDim.z;
-            if (QM_IN((item * kC + t) * kC + s0, 32, items * kC * kC, err)) {
-                uint4* hrow = reinterpret_cast<uint4*>(ph_out + (item * kC + t) * kC + s0);
-                uint4* lrow = reinterpret_cast<uint4*>(pl_out + (item * kC + t) * kC + s0);
-#pragma unroll
-                for (int i = 0; i < 32; i += 8) {
-                    float p[8];
-#pragma unroll
-                    for (int q = 0; q < 8; q++) {
-                        const int s = s0 + i + q;
-                        p[q] = (s <= t) ? ex2_approx(Gt - sG[s]) * kq[i + q] : 0.f;
-                    }
-                    uint4 h, l;
-                    split8(p, h, l);
-                    hrow[i / 8] = h;
-                    lrow[i / 8] = l;
-                }
-            }
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-
-    // ---- T = (I + A)^-1, blocked by 16: diagonal blocks by forward substitution,
-    // then T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj by block diagonals i - j = 1, 2, 3
-    // (f32); the upper blocks of T's storage hold the partial sums X_ij ----
-    if (ok) {  // block-uniform
+    for (; L < nitems; L += gridDim.x) {
+        int vh, ci, b;
+        item_of(L, vh, ci, b);
+        const int t0 = ci * kC;
+        const size_t plane_v = (size_t)b * kNumV + vh;
+        const size_t item = ((size_t)b * kNumV + vh) * nch + ci;
         if (tid < kC) {
-            const int blk = tid >> 4, c = tid & 15, o = blk * 16;
-            float tc[16];
-#pragma unroll
-            for (int r = 0; r < 16; r++) {
-                const float* arow = Amat + (o + r) * kAStride + o;
-                float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-                for (int u = 0; u + 1 < r; u += 2) {
-                    a0 = fmaf(arow[u], tc[u], a0);
-                    a1 = fmaf(arow[u + 1], tc[u + 1], a1);
-                }
-                if (r & 1) a0 = fmaf(arow[r - 1], tc[r - 1], a0);
-                tc[r] = (r == c) ? 1.f : (r < c ? 0.f : -(a0 + a1));
-            }
-#pragma unroll
-            for (int r = 0; r < 16; r++) Tm[(o + r) * kAStride + o + c] = tc[r];
-        } else if (tid < 2 * kC) {
-            const int t = tid - kC;
-            sC1[t] = sB[t] * eG[t];
+            sg[tid] = g_own;
+            sB[tid] = b_own;
         }
         __syncthreads();
-        static_assert(kAStride == 68, "tri_inverse_diagonal assumes the A/T row stride");
-        tri_inverse_diagonal<1, kLocalThreads>(Amat, Tm, tid);
-        tri_inverse_diagonal<2, kLocalThreads>(Amat, Tm, tid);
-        tri_inverse_diagonal<3, kLocalThreads>(Amat, Tm, tid);
-        // T' = T diag(b e^G), T'' = T diag(b) as fp16 hi/lo [t][j] tiles (upper
-        // part zero), formed in registers and written over A and T once every
-        // thread has read its part of T
-        static_assert(kC * 8 == 2 * kLocalThreads, "two 8-column pieces of T a thread");
-        uint4 t1h[2], t1l[2], t2h[2], t2l[2];
-#pragma unroll
-        for (int it = 0; it < 2; it++) {
-            const int o = tid + it * kLocalThreads, t = o >> 3, j0 = (o & 7) * 8;
-            float v1[8], v2[8];
-#pragma unroll
-            for (int q = 0; q < 8; q++) {
-                const int j = j0 + q;
-                const float tv = (j <= t) ? Tm[t * kAStride + j] : 0.f;
-                v1[q] = tv * sC1[j];
-                v2[q] = tv * sB[j];
-            }
-            split8(v1, t1h[it], t1l[it]);
-            split8(v2, t2h[it], t2l[it]);
-        }
-        __syncthreads();
-#pragma unroll
-        for (int it = 0; it < 2; it++) {
-            const int o = tid + it * kLocalThreads;
-            const uint32_t so = sw128_off(o >> 3, o & 7);
-            *reinterpret_cast<uint4*>(smem + kL_T1h + so) = t1h[it];
-            *reinterpret_cast<uint4*>(smem + kL_T1l + so) = t1l[it];
-            *reinterpret_cast<uint4*>(smem + kL_T2h + so) = t2h[it];
-            *reinterpret_cast<uint4*>(smem + kL_T2l + so) = t2l[it];
-        }
-    }
-    fence_proxy_async_shared();  // the T tiles, for the tensor core
-    tc_fence_before();
-    __syncthreads();
-
-    // ---- MMA2 (W^T) now, MMA3 (U~^T) once V has landed ----
-    if (ok && tid == 0) {
-        const uint32_t lb = smem_u32(&bars->load);
-        tc_fence_after();
-        int n = 0;
-        for (int term = 0; term < 3; term++) {
-            const uint32_t ka = sb + (term == 2 ? kL_KQl : kL_KQh);
-            const uint32_t tb = sb + (term == 1 ? kL_T1l : kL_T1h);
-            for (int kk = 0; kk < 4; kk++, n++)
-                umma_bf16_ss(tm + kTmW, umma_sdesc(ka + kk * 2048, 16384, 1024),
-                             umma_sdesc(tb + kk * 32, 16, 1024), kIdW, n > 0);
-        }
-        if (mbar_wait_bounded(lb, 1, abort_flag, err)) {
-            ld_out = false;
+        if (warp == 0) chunk_decays(sg, sG, eG, eD, lane);
+        ok = mbar_wait_bounded(smem_u32(&bars->load), 0, abort_flag, err);
+        if (ok) ld_out = false;
+        ok = __syncthreads_and(ok) != 0;  // also publishes sG
+        if (!ok) break;
+        // ---- MMA1: [K;Q] K^T (compensated) -> TMEM KQ ----
+        if (ok && tid == 0) {
             tc_fence_after();
-            n = 0;
+            int n = 0;
             for (int term = 0; term < 3; term++) {
-                const uint32_t va = sb + (term == 2 ? kL_Vl : kL_Vh);
-                const uint32_t tb = sb + (term == 1 ? kL_T2l : kL_T2h);
+                const uint32_t abase = sb + (term == 2 ? kL_KQl : kL_KQh);
+                const uint32_t bbase = sb + (term == 1 ? kL_KQl : kL_KQh);
+                for (int kk = 0; kk < 8; kk++, n++) {
+                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    umma_bf16_ss(tm + kTmKQ, umma_sdesc(abase + off, 16, 1024),
+                                 umma_sdesc(bbase + off, 16, 1024), kIdKK, n > 0);
+                }
+            }
+            umma_commit(smem_u32(&bars->mma));
+            mm_out = true;
+        }
+        if (ok) {
+            ok = mbar_wait_bounded(smem_u32(&bars->mma), 0, abort_flag, err);
+            if (ok) mm_out = false;
+        }
+        if (ok && tid == 0) {  // MMA1 has read Q: V lands in its quarters during the solve
+            const uint32_t lb = smem_u32(&bars->load);
+            mbar_arrive_expect_tx(lb, 4 * 8192);
+            ld_out = true;
+            ld_par = 1;
+            for (int hb = 0; hb < 2; hb++) {
+                tma_load_3d(sb + kL_Vh + hb * 16384, &tvh, hb * 64, t0, (int)plane_v, lb);
+                tma_load_3d(sb + kL_Vl + hb * 16384, &tvl, hb * 64, t0, (int)plane_v, lb);
+            }
+        }
+        ok = __syncthreads_and(ok) != 0;
+        tc_fence_after();
+
+        // ---- rows 0-63: A (f32, shared); rows 64-127: P' hi/lo (global); this
+        // thread's 32 columns [s0, s0 + 32) ----
+        if (ok) {
+            float kq[32];
+            const int s0 = half * 32;
+            tmem_ld32(tm + lane_addr + kTmKQ + s0, kq);
+            tmem_ld_wait();
+            if (row < kC) {
+                const int t = row;
+                const float Gt = sG[t], bt = sB[t];
+                float* arow = Amat + t * kAStride + s0;
+                if (QM_IN(t * kAStride + s0, 32, kC * kAStride, err))
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                    const int s = s0 + i;
+                    float4 v;
+                    v.x = (s + 0 < t) ? bt * ex2_approx(Gt - sG[s + 0]) * kq[i + 0] : 0.f;
+                    v.y = (s + 1 < t) ? bt * ex2_approx(Gt - sG[s + 1]) * kq[i + 1] : 0.f;
+                    v.z = (s + 2 < t) ? bt * ex2_approx(Gt - sG[s + 2]) * kq[i + 2] : 0.f;
+                    v.w = (s + 3 < t) ? bt * ex2_approx(Gt - sG[s + 3]) * kq[i + 3] : 0.f;
+                    *reinterpret_cast<float4*>(arow + i) = v;
+                }
+            } else {
+                const int t = row - kC;
+                const float Gt = sG[t];
+                if (QM_IN((item * kC + t) * kC + s0, 32, (size_t)nitems * kC * kC, err)) {
+                    uint4* hrow = reinterpret_cast<uint4*>(ph_out + (item * kC + t) * kC + s0);
+                    uint4* lrow = reinterpret_cast<uint4*>(pl_out + (item * kC + t) * kC + s0);
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        float p[8];
+#pragma unroll
+                        for (int q = 0; q < 8; q++) {
+                            const int s = s0 + i + q;
+                            p[q] = (s <= t) ? ex2_approx(Gt - sG[s]) * kq[i + q] : 0.f;
+                        }
+                        uint4 h, l;
+                        split8(p, h, l);
+                        hrow[i / 8] = h;
+                        lrow[i / 8] = l;
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+
+        // ---- T = (I + A)^-1, blocked by 16: diagonal blocks by forward substitution
+        // (f32), then the blocks below them from products with T's known blocks ----
+        if (ok) {  // block-uniform
+            if (tid < kC) {
+                const int blk = tid >> 4, c = tid & 15, o = blk * 16;
+                float tc[16];
+#pragma unroll
+                for (int r = 0; r < 16; r++) {
+                    const float* arow = Amat + (o + r) * kAStride + o;
+                    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+                    for (int u = 0; u + 1 < r; u += 2) {
+                        a0 = fmaf(arow[u], tc[u], a0);
+                        a1 = fmaf(arow[u + 1], tc[u + 1], a1);
+                    }
+                    if (r & 1) a0 = fmaf(arow[r - 1], tc[r - 1], a0);
+                    tc[r] = (r == c) ? 1.f : (r < c ? 0.f : -(a0 + a1));
+                }
+#pragma unroll
+                for (int r = 0; r < 16; r++) Tm[(o + r) * kAStride + o + c] = tc[r];
+            } else if (tid < 2 * kC) {
+                const int t = tid - kC;
+                sC1[t] = sB[t] * eG[t];
+            }
+            __syncthreads();
+            // the off-diagonal blocks in two levels of 16 x 8 tensor-core tiles
+            // (3 x TF32).  Level 1, warps 0-3: for (i, j) = (1, 0), (3, 2),
+            // X_ij = A_ij T_jj (kept in the unused block (j, i)), then
+            // T_ij = -T_ii X_ij.  Level 2, 8 warps: with T_A, T_B the inverses
+            // of the leading and trailing 32 x 32 halves, X = A_BA T_A (kept in
+            // rows 0-31, columns 32-63), then T_BA = -T_B X.  k-steps that only
+            // meet T's zero upper part (whose storage holds the X's) are skipped.
+            static_assert(kAStride == 68, "mma3_tf32_tile assumes the A/T row stride");
+            constexpr int S = kAStride;
+            if (warp < 4) {
+                const int i = 2 * (warp >> 1) + 1, j = i - 1, h = warp & 1;
+                float c[4] = {0.f, 0.f, 0.f, 0.f};
+                mma3_tf32_tile(c, Amat + 16 * i * S + 16 * j, Tm + 16 * j * S + 16 * j + 8 * h, 8 * h, 16, lane);
+                store_tile_1688(Tm + 16 * j * S + 16 * i + 8 * h, c, 1.f, lane);
+            }
+            __syncthreads();
+            if (warp < 4) {
+                const int i = 2 * (warp >> 1) + 1, j = i - 1, h = warp & 1;
+                float c[4] = {0.f, 0.f, 0.f, 0.f};
+                mma3_tf32_tile(c, Tm + 16 * i * S + 16 * i, Tm + 16 * j * S + 16 * i + 8 * h, 0, 16, lane);
+                store_tile_1688(Tm + 16 * i * S + 16 * j + 8 * h, c, -1.f, lane);
+            }
+            __syncthreads();
+            {
+                const int rt = warp >> 2, ct = warp & 3;
+                float c[4] = {0.f, 0.f, 0.f, 0.f};
+                mma3_tf32_tile(c, Amat + (32 + 16 * rt) * S, Tm + 8 * ct, 8 * ct, 32, lane);
+                store_tile_1688(Tm + 16 * rt * S + 32 + 8 * ct, c, 1.f, lane);
+                __syncthreads();
+                c[0] = c[1] = c[2] = c[3] = 0.f;
+                mma3_tf32_tile(c, Tm + (32 + 16 * rt) * S + 32, Tm + 32 + 8 * ct, 0, rt ? 32 : 16, lane);
+                store_tile_1688(Tm + (32 + 16 * rt) * S + 8 * ct, c, -1.f, lane);
+            }
+            __syncthreads();
+            // T' = T diag(b e^G), T'' = T diag(b) as fp16 hi/lo [t][j] tiles (upper
+            // part zero), formed in registers and written over A and T once every
+            // thread has read its part of T
+            static_assert(kC * 8 == 2 * kLocalThreads, "two 8-column pieces of T a thread");
+            uint4 t1h[2], t1l[2], t2h[2], t2l[2];
+#pragma unroll
+            for (int it = 0; it < 2; it++) {
+                const int o = tid + it * kLocalThreads, t = o >> 3, j0 = (o & 7) * 8;
+                float v1[8], v2[8];
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    const int j = j0 + q;
+                    const float tv = (j <= t) ? Tm[t * kAStride + j] : 0.f;
+                    v1[q] = tv * sC1[j];
+                    v2[q] = tv * sB[j];
+                }
+                split8(v1, t1h[it], t1l[it]);
+                split8(v2, t2h[it], t2l[it]);
+            }
+            __syncthreads();
+#pragma unroll
+            for (int it = 0; it < 2; it++) {
+                const int o = tid + it * kLocalThreads;
+                const uint32_t so = sw128_off(o >> 3, o & 7);
+                *reinterpret_cast<uint4*>(smem + kL_T1h + so) = t1h[it];
+                *reinterpret_cast<uint4*>(smem + kL_T1l + so) = t1l[it];
+                *reinterpret_cast<uint4*>(smem + kL_T2h + so) = t2h[it];
+                *reinterpret_cast<uint4*>(smem + kL_T2l + so) = t2l[it];
+            }
+        }
+        fence_proxy_async_shared();  // the T tiles, for the tensor core
+        tc_fence_before();
+        __syncthreads();
+
+        // ---- MMA2 (W^T) now, MMA3 (U~^T) once V has landed ----
+        if (ok && tid == 0) {
+            const uint32_t lb = smem_u32(&bars->load);
+            tc_fence_after();
+            int n = 0;
+            for (int term = 0; term < 3; term++) {
+                const uint32_t ka = sb + (term == 2 ? kL_KQl : kL_KQh);
+                const uint32_t tb = sb + (term == 1 ? kL_T1l : kL_T1h);
                 for (int kk = 0; kk < 4; kk++, n++)
-                    umma_bf16_ss(tm + kTmU, umma_sdesc(va + kk * 2048, 16384, 1024),
+                    umma_bf16_ss(tm + kTmW, umma_sdesc(ka + kk * 2048, 16384, 1024),
                                  umma_sdesc(tb + kk * 32, 16, 1024), kIdW, n > 0);
             }
+            if (mbar_wait_bounded(lb, 1, abort_flag, err)) {
+                ld_out = false;
+                tc_fence_after();
+                n = 0;
+                for (int term = 0; term < 3; term++) {
+                    const uint32_t va = sb + (term == 2 ? kL_Vl : kL_Vh);
+                    const uint32_t tb = sb + (term == 1 ? kL_T2l : kL_T2h);
+                    for (int kk = 0; kk < 4; kk++, n++)
+                        umma_bf16_ss(tm + kTmU, umma_sdesc(va + kk * 2048, 16384, 1024),
+                                     umma_sdesc(tb + kk * 32, 16, 1024), kIdW, n > 0);
+                }
+            }
+            umma_commit(smem_u32(&bars->mma));  // also covers MMA2 when the V wait gave up
+            mm_out = true;
+            mm_par = 1;
         }
-        umma_commit(smem_u32(&bars->mma));  // also covers MMA2 when the V wait gave up
-        mm_out = true;
-        mm_par = 1;
-    }
-    if (ok) {
-        ok = mbar_wait_bounded(smem_u32(&bars->mma), 1, abort_flag, err);
-        if (ok) mm_out = false;
-    }
-    ok = __syncthreads_and(ok && !*abort_flag) != 0;
-    tc_fence_after();
+        if (ok) {
+            ok = mbar_wait_bounded(smem_u32(&bars->mma), 1, abort_flag, err);
+            if (ok) mm_out = false;
+        }
+        ok = __syncthreads_and(ok && !*abort_flag) != 0;
+        tc_fence_after();
+        if (!ok) break;
 
-    // ---- outputs: W^T row k (fp16), U~^T row v (f32, [t/4][v][4]); this
-    // thread's 32 tokens [32 half, 32 half + 32) ----
-    if (ok && QM_IN(item * kHd * kC, kHd * kC, (size_t)gridDim.x * gridDim.y * gridDim.z * kHd * kC, err)) {
-        float wv[32];
-        tmem_ld32(tm + lane_addr + kTmW + half * 32, wv);
-        tmem_ld_wait();
-        uint4* wrow = reinterpret_cast<uint4*>(wt_out + (item * kHd + row) * kC) + half * 4;
+        // the next item's K/Q tiles (the region is free: MMA2/3 are done) and gates
+        if (L + (int)gridDim.x < nitems) {
+            int vh2, ci2, b2;
+            item_of(L + gridDim.x, vh2, ci2, b2);
+            load_gates(vh2, ci2, b2, g_own, b_own);
+            if (tid == 0) {
+                load_kq(vh2, ci2, b2);
+                ld_out = true;
+                ld_par = 0;
+            }
+        }
+
+        // ---- outputs: W^T row k (fp16), U~^T row v (f32, [t/4][v][4]); this
+        // thread's 32 tokens [32 half, 32 half + 32) ----
+        if (QM_IN(item * kHd * kC, kHd * kC, (size_t)nitems * kHd * kC, err)) {
+            float wv[32];
+            tmem_ld32(tm + lane_addr + kTmW + half * 32, wv);
+            tmem_ld_wait();
+            uint4* wrow = reinterpret_cast<uint4*>(wt_out + (item * kHd + row) * kC) + half * 4;
 #pragma unroll
-        for (int t = 0; t < 32; t += 8) wrow[t / 8] = round8(wv + t);
-        float uv[32];
-        tmem_ld32(tm + lane_addr + kTmU + half * 32, uv);
-        tmem_ld_wait();
-        float4* ub = reinterpret_cast<float4*>(ut_out + item * kHd * kC);
+            for (int t = 0; t < 32; t += 8) wrow[t / 8] = round8(wv + t);
+            float uv[32];
+            tmem_ld32(tm + lane_addr + kTmU + half * 32, uv);
+            tmem_ld_wait();
+            float4* ub = reinterpret_cast<float4*>(ut_out + item * kHd * kC);
 #pragma unroll
-        for (int i = 0; i < 8; i++)
-            ub[(half * 8 + i) * kHd + row] = make_float4(uv[4 * i], uv[4 * i + 1], uv[4 * i + 2], uv[4 * i + 3]);
-    }
+            for (int i = 0; i < 8; i++)
+                ub[(half * 8 + i) * kHd + row] = make_float4(uv[4 * i], uv[4 * i + 1], uv[4 * i + 2], uv[4 * i + 3]);
+        }
+        tc_fence_before();
+    }  // items
+
     if (tid == 0) {
         if (ld_out) mbar_drain(smem_u32(&bars->load), ld_par);
         if (mm_out) mbar_drain(smem_u32(&bars->mma), mm_par);
@@ -1239,8 +1293,10 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
     if (e != cudaSuccess) return e;
     {
         TimedLaunch tl(ctx, "dn_chunk_local");
-        dn_chunk_local<<<dim3(kNumV, nch, B), kLocalThreads, kLocalSmem, s>>>(
-            m[0], m[1], m[2], m[3], m[4], m[5], g, be, T, nch, wt, ut, ph, pl, ctx->d_err);
+        const int nitems = B * kNumV * nch;  // persistent: two CTAs per SM walk the items
+        const int grid = std::min(nitems, 2 * std::max(ctx->num_sms, 1));
+        dn_chunk_local<<<grid, kLocalThreads, kLocalSmem, s>>>(m[0], m[1], m[2], m[3], m[4], m[5], g, be, T,
+                                                               nch, B, wt, ut, ph, pl, ctx->d_err);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
