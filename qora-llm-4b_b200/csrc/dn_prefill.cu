@@ -239,33 +239,58 @@ __device__ __forceinline__ void chunk_decays(const float* sg, float* sG, float* 
     }
 }
 
-// c (a 16 x 8 tile) += X[16 rows][k0, k1) Y[k0, k1)[8 columns] for f32 X and Y
-// in shared memory (row stride 68 floats), as three TF32 products per k-step
-// (lo.hi + hi.lo + hi.hi: about 22 significant bits, f32 range).  X rows and
-// Y columns start at the pointers; k0, k1 are multiples of 8.  Fragment loads
-// of X touch 32 distinct banks (rows 68 floats apart).
-__device__ __forceinline__ void mma3_tf32_tile(float (&c)[4], const float* __restrict__ X,
-                                               const float* __restrict__ Y, int k0, int k1, int lane) {
+// c (a 16 x 8 tile) = X[16 rows][k0, k0 + 8 NK) Y[k0, k0 + 8 NK)[8 columns] for
+// f32 X and Y in shared memory (row stride 68 floats), as three TF32 products
+// per k-step (hi.hi + hi.lo + lo.hi: about 22 significant bits, f32 range),
+// accumulated in three independent chains.  X rows and Y columns start at the
+// pointers; k0 is a multiple of 8.  Fragment loads of X touch 32 distinct
+// banks (rows 68 floats apart).
+template <int NK>
+__device__ __forceinline__ void mma3_tf32_tile_n(float (&c)[4], const float* __restrict__ X,
+                                                 const float* __restrict__ Y, int k0, int lane) {
     constexpr int S = 68;
     const int g = lane >> 2, t = lane & 3;
-    for (int k = k0; k < k1; k += 8) {
-        const float af[4] = {X[g * S + k + t], X[(g + 8) * S + k + t], X[g * S + k + t + 4],
-                             X[(g + 8) * S + k + t + 4]};
-        const float bf[2] = {Y[(k + t) * S + g], Y[(k + t + 4) * S + g]};
+    float af[NK][4], bf[NK][2];
+#pragma unroll
+    for (int s = 0; s < NK; s++) {
+        const int k = k0 + 8 * s;
+        af[s][0] = X[g * S + k + t];
+        af[s][1] = X[(g + 8) * S + k + t];
+        af[s][2] = X[g * S + k + t + 4];
+        af[s][3] = X[(g + 8) * S + k + t + 4];
+        bf[s][0] = Y[(k + t) * S + g];
+        bf[s][1] = Y[(k + t + 4) * S + g];
+    }
+    float ch[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < NK; s++) {
         uint32_t ah[4], al[4], bh[2], bl[2];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            ah[i] = tf32_rna(af[i]);
-            al[i] = tf32_rna(af[i] - __uint_as_float(ah[i]));
+            ah[i] = tf32_rna(af[s][i]);
+            al[i] = tf32_rna(af[s][i] - __uint_as_float(ah[i]));
         }
 #pragma unroll
         for (int i = 0; i < 2; i++) {
-            bh[i] = tf32_rna(bf[i]);
-            bl[i] = tf32_rna(bf[i] - __uint_as_float(bh[i]));
+            bh[i] = tf32_rna(bf[s][i]);
+            bl[i] = tf32_rna(bf[s][i] - __uint_as_float(bh[i]));
         }
-        mma_tf32_1688(c, al[0], al[1], al[2], al[3], bh[0], bh[1]);
-        mma_tf32_1688(c, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
-        mma_tf32_1688(c, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+        mma_tf32_1688(ch, ah[0], ah[1], ah[2], ah[3], bh[0], bh[1]);
+        mma_tf32_1688(c1, ah[0], ah[1], ah[2], ah[3], bl[0], bl[1]);
+        mma_tf32_1688(c2, al[0], al[1], al[2], al[3], bh[0], bh[1]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) c[i] = ch[i] + (c1[i] + c2[i]);
+}
+
+// the same over nk = 1 .. 4 k-steps (warp-uniform)
+__device__ __forceinline__ void mma3_tf32_tile(float (&c)[4], const float* __restrict__ X,
+                                               const float* __restrict__ Y, int k0, int k1, int lane) {
+    switch ((k1 - k0) >> 3) {
+        case 1: mma3_tf32_tile_n<1>(c, X, Y, k0, lane); break;
+        case 2: mma3_tf32_tile_n<2>(c, X, Y, k0, lane); break;
+        case 3: mma3_tf32_tile_n<3>(c, X, Y, k0, lane); break;
+        default: mma3_tf32_tile_n<4>(c, X, Y, k0, lane); break;
     }
 }
 
@@ -533,25 +558,24 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
             constexpr int S = kAStride;
             if (warp < 4) {
                 const int i = 2 * (warp >> 1) + 1, j = i - 1, h = warp & 1;
-                float c[4] = {0.f, 0.f, 0.f, 0.f};
+                float c[4];
                 mma3_tf32_tile(c, Amat + 16 * i * S + 16 * j, Tm + 16 * j * S + 16 * j + 8 * h, 8 * h, 16, lane);
                 store_tile_1688(Tm + 16 * j * S + 16 * i + 8 * h, c, 1.f, lane);
             }
             __syncthreads();
             if (warp < 4) {
                 const int i = 2 * (warp >> 1) + 1, j = i - 1, h = warp & 1;
-                float c[4] = {0.f, 0.f, 0.f, 0.f};
+                float c[4];
                 mma3_tf32_tile(c, Tm + 16 * i * S + 16 * i, Tm + 16 * j * S + 16 * i + 8 * h, 0, 16, lane);
                 store_tile_1688(Tm + 16 * i * S + 16 * j + 8 * h, c, -1.f, lane);
             }
             __syncthreads();
             {
                 const int rt = warp >> 2, ct = warp & 3;
-                float c[4] = {0.f, 0.f, 0.f, 0.f};
+                float c[4];
                 mma3_tf32_tile(c, Amat + (32 + 16 * rt) * S, Tm + 8 * ct, 8 * ct, 32, lane);
                 store_tile_1688(Tm + 16 * rt * S + 32 + 8 * ct, c, 1.f, lane);
                 __syncthreads();
-                c[0] = c[1] = c[2] = c[3] = 0.f;
                 mma3_tf32_tile(c, Tm + (32 + 16 * rt) * S + 32, Tm + 32 + 8 * ct, 0, rt ? 32 : 16, lane);
                 store_tile_1688(Tm + (32 + 16 * rt) * S + 8 * ct, c, -1.f, lane);
             }
