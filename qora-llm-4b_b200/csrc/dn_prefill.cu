@@ -520,7 +520,9 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
             }
         }
         tc_fence_before();
-        __syncthreads();
+        // A is complete once warps 0, 1, 4, 5 (its rows) meet; warps 2, 3, 6, 7
+        // go on writing P' while the diagonal blocks are solved
+        if (quarter < 2) named_bar_sync(1, 128);
 
         // ---- T = (I + A)^-1, blocked by 16: diagonal blocks by forward substitution
         // (f32), then the blocks below them from products with T's known blocks ----
@@ -542,8 +544,8 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
                 }
 #pragma unroll
                 for (int r = 0; r < 16; r++) Tm[(o + r) * kAStride + o + c] = tc[r];
-            } else if (tid < 2 * kC) {
-                const int t = tid - kC;
+            } else if (warp == 4 || warp == 5) {
+                const int t = tid - 2 * kC;
                 sC1[t] = sB[t] * eG[t];
             }
             __syncthreads();
