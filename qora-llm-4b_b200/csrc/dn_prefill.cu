@@ -717,10 +717,10 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
 // stores of half chunks) and their thread 256 issues the next q and P'
 // loads.  mbarriers hand over: u2_ready, dec_ready (warps 4-7 -> thread 0);
 // u_ready, s_read (thread 0 -> warps 4-7); y_free (warps 8-11 -> warps 4-7,
-// which also frees U^T hi/lo and q for reuse).  dec_ready and s_read
-// are pairs used by chunk parity (phase c >> 1 for chunk c): either side may
-// publish a chunk's piece one chunk early without a phase running two ahead
-// of its waiter.
+// which also frees U^T hi/lo and q for reuse).  u2_ready, dec_ready, s_read
+// and mY are pairs used by chunk parity (phase c >> 1 for chunk c): either
+// side may publish a chunk's piece one chunk early without a phase running
+// two ahead of its waiter.
 constexpr int kS_W = 0;             // W^T [128 k x 64 t] fp16 (16 KB)
 constexpr int kS_Q = 16384;         // q hi [64 t x 128 k] fp16: 2 boxes [64 x 64], x2 buffers (32 KB)
 constexpr int kS_P = 49152;         // P' hi, lo [64 t x 64 s] (8 KB each) (16 KB)
@@ -741,8 +741,8 @@ constexpr uint32_t kIdUK = umma_idesc_f16kind(128, 128, false, true, false);   /
 
 struct StateBars {  // the first 11 words are tracked by Pending (in this order)
     uint64_t w_full[2], q_full[2], k_full[2], p_full;  // TMA
-    uint64_t m4, m7, mY, spare;                        // MMA completions
-    uint64_t u2_ready, dec_ready[2];                   // warps 4-7 -> thread 0 (128 arrivals)
+    uint64_t m4, m7, mY[2];                            // MMA completions (mY: a chunk-parity pair)
+    uint64_t u2_ready[2], dec_ready[2];                // warps 4-7 -> thread 0 (128 arrivals)
     uint64_t u_ready, s_read[2];                       // thread 0 -> warps 4-7 (1 arrival)
     uint64_t y_free;                                   // warps 8-11 read Y out (128 arrivals)
     uint32_t tmem_base;
@@ -824,8 +824,10 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         mbar_init(smem_u32(&bars->p_full), 1);
         mbar_init(smem_u32(&bars->m4), 1);
         mbar_init(smem_u32(&bars->m7), 1);
-        mbar_init(smem_u32(&bars->mY), 1);
-        mbar_init(smem_u32(&bars->u2_ready), 128);
+        mbar_init(smem_u32(&bars->mY[0]), 1);
+        mbar_init(smem_u32(&bars->mY[1]), 1);
+        mbar_init(smem_u32(&bars->u2_ready[0]), 128);
+        mbar_init(smem_u32(&bars->u2_ready[1]), 128);
         mbar_init(smem_u32(&bars->dec_ready[0]), 128);
         mbar_init(smem_u32(&bars->dec_ready[1]), 128);
         mbar_init(smem_u32(&bars->u_ready), 1);
@@ -931,7 +933,7 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
             const int p = ci & 1;
             // ---- MMA4: U2[p] (= U~) -= S0[p] W^T ----
             if (tid == 0) {
-                const bool w = wait(&bars->w_full[0], p) && wait(&bars->u2_ready, p);
+                const bool w = wait(&bars->w_full[0], p) && wait(&bars->u2_ready[p], (ci >> 1) & 1);
                 tc_fence_after();
                 if (w) {
                     for (int kk = 0; kk < 8; kk++)
@@ -941,9 +943,8 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
                 umma_commit(smem_u32(&bars->m4));
                 pend.start(&bars->m4, p);
             }
-            {   // MMA5 and MMA6 of ci-1 are done: S0 buffer p^1 and U^T (unscaled) are free
-                bool w = mbar_wait_bounded(smem_u32(&bars->m4), p, abort_flag, err);
-                if (w && ci > 0) w = mbar_wait_bounded(smem_u32(&bars->mY), (ci - 1) & 1, abort_flag, err);
+            {
+                const bool w = mbar_wait_bounded(smem_u32(&bars->m4), p, abort_flag, err);
                 if (tid == 0 && w) pend.seen(&bars->m4);
                 ok = named_bar_and(1, 128, ok && w && !*abort_flag);
             }
@@ -996,8 +997,11 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
             // ---- S pass: S0 of chunk ci+1 = fp16(S) into TMEM buffer p^1, and S scaled
             // by e^G63 of chunk ci+1 for its MMA7 (its decays come with dec_ready) ----
             if (ci + 1 < nch) {
-                // dec_ready[c&1] completes once per two chunks: phase (c >> 1) for chunk c
+                // dec_ready[c&1] completes once per two chunks: phase (c >> 1) for chunk c;
+                // MMA5 of chunk ci-1 (mY) has read S0 buffer p^1
                 ok = mbar_wait_bounded(smem_u32(&bars->dec_ready[(ci + 1) & 1]), ((ci + 1) >> 1) & 1, abort_flag, err);
+                if (ok && ci > 0)
+                    ok = mbar_wait_bounded(smem_u32(&bars->mY[(ci - 1) & 1]), ((ci - 1) >> 1) & 1, abort_flag, err);
                 const float decay = misc[((ci + 1) & 3) * 256 + 128 + kC - 1];
 #pragma unroll 1
                 for (int h = 0; h < 2; h++) {
@@ -1055,12 +1059,12 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
                 ut[4 * t4] = f.x; ut[4 * t4 + 1] = f.y; ut[4 * t4 + 2] = f.z; ut[4 * t4 + 3] = f.w;
             }
         };
-        auto store_ut = [&](int c) {  // U~ of chunk c into U2[c&1], then u2_ready
+        auto store_ut = [&](int c) {  // U~ of chunk c into U2[c&1], then u2_ready[c&1]
             tmem_st32(tm + lane_addr + kTmU2 + (c & 1) * 64, ut);
             tmem_st32(tm + lane_addr + kTmU2 + (c & 1) * 64 + 32, ut + 32);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(smem_u32(&bars->u2_ready));
+            mbar_arrive(smem_u32(&bars->u2_ready[c & 1]));
         };
         float g_next = 0.f;
         auto load_g = [&](int c) {
@@ -1138,8 +1142,8 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
                                          umma_sdesc(pbt + kk * 32, 16, 1024), kIdUP, n > 0 ? 1u : 0u);
                     }
                 }
-                umma_commit(smem_u32(&bars->mY));  // MMA5 and MMA6 of ci
-                pend.start(&bars->mY, p);
+                umma_commit(smem_u32(&bars->mY[p]));  // MMA5 and MMA6 of ci
+                pend.start(&bars->mY[p], (ci >> 1) & 1);
             }
             if (more) {
                 store_ut(ci + 1);  // U2[(ci+1)&1] was read in chunk ci-1
@@ -1159,7 +1163,7 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         const int yt = tid - 256;
         bool ok = true;
         for (int ci = 0; ci < nch; ci++) {
-            const bool wy = ok && wait(&bars->mY, ci & 1);
+            const bool wy = ok && wait(&bars->mY[ci & 1], (ci >> 1) & 1);
             ok = wy && !*abort_flag;
             if (yt == 0 && ok) {  // MMA6 of ci has read P', MMA5 of ci q buffer ci&1
                 if (ci + 1 < nch) issue_p(ci + 1);
