@@ -147,12 +147,19 @@ qm_gemv_kernel(const __grid_constant__ GvArgs a) {
     __syncthreads();
 
     float acc[BT][CPL];
+    // Q4 at batch 1: the column sums as pairs for the packed f32x2 FMA (two
+    // products per instruction, each rounded as by fmaf; larger batches keep
+    // scalar sums, the pairs' register alignment would spill them)
+    constexpr bool kPacked = Q4 && BT == 1;
+    float2 acc2[BT][kPacked ? CPL / 2 : 1];
     float sxsum[BT];  // Q4: the lane's sum of s x over its rows (the -8 of every nibble)
 #pragma unroll
     for (int b = 0; b < BT; b++) {
         sxsum[b] = 0.f;
 #pragma unroll
         for (int i = 0; i < CPL; i++) acc[b][i] = 0.f;
+#pragma unroll
+        for (int i = 0; i < (kPacked ? CPL / 2 : 1); i++) acc2[b][i] = make_float2(0.f, 0.f);
     }
 
     for (int base = 0; base < nrs; base += R) {
@@ -177,16 +184,27 @@ qm_gemv_kernel(const __grid_constant__ GvArgs a) {
                 for (int wd = 0; wd < 4; wd++) {
                     const uint32_t halves[2] = {ww[wd], ww[wd] >> 16};
 #pragma unroll
-                    for (int hh = 0; hh < 2; hh++)
+                    for (int hh = 0; hh < 2; hh++) {
+                        // nibble 4 hh + jn of word wd (column 8 wd + 4 hh + jn of the lane's
+                        // 32) masked in place: the denormal q 2^(4 jn - 149)
+                        const uint32_t h = halves[hh];
+                        if constexpr (kPacked) {  // two columns an instruction
+                            const int c2 = 4 * wd + 2 * hh;
+                            acc2[0][c2] = __ffma2_rn(make_float2(__uint_as_float(h & 0xFu), __uint_as_float(h & 0xF0u)),
+                                                     make_float2(sxj[0][0], sxj[0][1]), acc2[0][c2]);
+                            acc2[0][c2 + 1] =
+                                __ffma2_rn(make_float2(__uint_as_float(h & 0xF00u), __uint_as_float(h & 0xF000u)),
+                                           make_float2(sxj[0][2], sxj[0][3]), acc2[0][c2 + 1]);
+                        } else {
 #pragma unroll
-                        for (int jn = 0; jn < 4; jn++) {
-                            // nibble 4 hh + jn of word wd (column 8 wd + 4 hh + jn of the lane's
-                            // 32) masked in place: the denormal q 2^(4 jn - 149)
-                            const float v = __uint_as_float(halves[hh] & (0xFu << (4 * jn)));
+                            for (int jn = 0; jn < 4; jn++) {
+                                const float v = __uint_as_float(h & (0xFu << (4 * jn)));
 #pragma unroll
-                            for (int b = 0; b < BT; b++)
-                                acc[b][8 * wd + 4 * hh + jn] = fmaf(v, sxj[b][jn], acc[b][8 * wd + 4 * hh + jn]);
+                                for (int b = 0; b < BT; b++)
+                                    acc[b][8 * wd + 4 * hh + jn] = fmaf(v, sxj[b][jn], acc[b][8 * wd + 4 * hh + jn]);
+                            }
                         }
+                    }
                 }
             } else {
                 float xv[BT];
@@ -206,6 +224,15 @@ qm_gemv_kernel(const __grid_constant__ GvArgs a) {
                 }
             }
         }
+    }
+    if constexpr (kPacked) {
+#pragma unroll
+        for (int b = 0; b < BT; b++)
+#pragma unroll
+            for (int i = 0; i < CPL / 2; i++) {
+                acc[b][2 * i] = acc2[b][i].x;
+                acc[b][2 * i + 1] = acc2[b][i].y;
+            }
     }
     // the two half-warps (same columns, other rows), then the 8 warps, each in
     // a fixed order
