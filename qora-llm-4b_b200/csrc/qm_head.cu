@@ -132,18 +132,27 @@ qm_rows_kernel(const void* __restrict__ data, const uint16_t* __restrict__ scale
                         if (Q4) {
                             // the nibble masked in place is the denormal q 2^(4j-149); times the
                             // prescaled x it is q x 2^-49 exactly, whatever j
-                            float part[4] = {0.f, 0.f, 0.f, 0.f};  // one chain per word: 4 independent FMA chains
+                            // one chain of column pairs per word (packed f32x2 FMA: two products an
+                            // instruction), 4 independent chains
+                            float2 part[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                                              make_float2(0.f, 0.f)};
 #pragma unroll
                             for (int wd = 0; wd < 4; wd++) {
                                 const uint32_t halves[2] = {ww[wd], ww[wd] >> 16};
 #pragma unroll
                                 for (int hh = 0; hh < 2; hh++)
 #pragma unroll
-                                    for (int jn = 0; jn < 4; jn++)
-                                        part[wd] = fmaf(__uint_as_float(halves[hh] & (0xFu << (4 * jn))),
-                                                        xv[8 * wd + 4 * hh + jn], part[wd]);
+                                    for (int jn = 0; jn < 4; jn += 2) {
+                                        const int e = 8 * wd + 4 * hh + jn;
+                                        part[wd] = __ffma2_rn(
+                                            make_float2(__uint_as_float(halves[hh] & (0xFu << (4 * jn))),
+                                                        __uint_as_float(halves[hh] & (0xF0u << (4 * jn)))),
+                                            make_float2(xv[e], xv[e + 1]), part[wd]);
+                                    }
                             }
-                            const float qx = ((part[0] + part[1]) + (part[2] + part[3])) * 562949953421312.0f;  // 2^49
+                            const float qx = (((part[0].x + part[0].y) + (part[1].x + part[1].y)) +
+                                              ((part[2].x + part[2].y) + (part[3].x + part[3].y))) *
+                                             562949953421312.0f;  // 2^49
                             const float xsum = xs[(b * C + c) * XS + CW];
                             const float sc = __half2float(__ushort_as_half((uint16_t)s[rr][Q4 ? i : 0]));
                             acc[b][rr] = fmaf(sc, fmaf(-8.0f, xsum, qx), acc[b][rr]);
