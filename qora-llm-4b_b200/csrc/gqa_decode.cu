@@ -299,13 +299,20 @@ __device__ __forceinline__ void attend_tiles_t(uint32_t sbase, uint64_t* full, u
         if (ok) {
             const uint32_t kb = sbase + st * kStageBytes;
             const uint32_t vb = kb + kTileBytes;
-            float c[4] = {0.f, 0.f, 0.f, 0.f};
+            // four independent accumulation chains over the 256 dims (a quarter of
+            // the dependent MMA latency), summed in a fixed order
+            float cq[4][4];
+#pragma unroll
+            for (int a = 0; a < 4; a++) cq[a][0] = cq[a][1] = cq[a][2] = cq[a][3] = 0.f;
 #pragma unroll
             for (int kk = 0; kk < 16; kk++) {
                 uint32_t r0, r1, r2, r3;
                 ldsm_x4(swz_addr(kb, krow, kk * 16 + kdim), r0, r1, r2, r3);
-                mma_bf16_16816(c, r0, r1, r2, r3, qb[kk][0], qb[kk][1]);
+                mma_bf16_16816(cq[kk & 3], r0, r1, r2, r3, qb[kk][0], qb[kk][1]);
             }
+            float c[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) c[i] = (cq[0][i] + cq[1][i]) + (cq[2][i] + cq[3][i]);
             // hi + lo columns (lanes q and q ^ 2); s[j][i]: head 2(q&1)+j, position g8 + 8i
             float s[2][2];
             s[0][0] = c[0] + __shfl_xor_sync(0xffffffffu, c[0], 2);
@@ -927,15 +934,26 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         }
         named_bar_sync(1, kGroup * 32);
         // this CTA's merged partial: output idx goes to CTA idx / per, which
-        // receives every CTA's partial of its outputs [nsplit][per]
+        // receives every CTA's partial of its outputs [nsplit][per]; four
+        // adjacent outputs a thread (one owner: per is a multiple of 4), one
+        // 16-byte store into the owner's shared memory
+        static_assert((kGroup * kD) % (4 * 128) == 0 && (kGroup * kD / kFusedMaxSplit) % 4 == 0,
+                      "four outputs a thread, never split between owners");
 #pragma unroll
-        for (int e = 0; e < (kGroup * kD) / 128; e++) {
-            const int idx = e * 128 + t;
+        for (int e = 0; e < (kGroup * kD) / (4 * 128); e++) {
+            const int idx = 4 * (e * 128 + t);
             const int head = idx / kD, d = idx % kD;
-            float acc = 0.f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int w = 0; w < kGroup; w++) acc = fmaf(sc[w * kGroup + head], mo[(w * kGroup + head) * kRow + d], acc);
-            st_dsmem_f32(recv_o + split * per + idx % per, (uint32_t)(idx / per), acc);
+            for (int w = 0; w < kGroup; w++) {
+                const float f = sc[w * kGroup + head];
+                const float4 m = *reinterpret_cast<const float4*>(&mo[(w * kGroup + head) * kRow + d]);
+                acc.x = fmaf(f, m.x, acc.x);
+                acc.y = fmaf(f, m.y, acc.y);
+                acc.z = fmaf(f, m.z, acc.z);
+                acc.w = fmaf(f, m.w, acc.w);
+            }
+            st_dsmem_v4(recv_o + split * per + idx % per, (uint32_t)(idx / per), acc);
         }
     }
     // every CTA's pushes have landed (and s_new, written by the producer warp, is visible)

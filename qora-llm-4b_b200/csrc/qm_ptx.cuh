@@ -389,6 +389,11 @@ __device__ __forceinline__ void st_dsmem_v2(void* p, uint32_t rank, float a, flo
     asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(mapa_shared(smem_u32(p), rank)), "f"(a), "f"(b)
                  : "memory");
 }
+__device__ __forceinline__ void st_dsmem_v4(void* p, uint32_t rank, float4 v) {  // p 16-byte aligned
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(mapa_shared(smem_u32(p), rank)),
+                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
 // A float in the shared memory of CTA `rank` of this cluster (same offset as p).
 __device__ __forceinline__ float ld_dsmem_f32(const void* p, uint32_t rank) {
     float v;
