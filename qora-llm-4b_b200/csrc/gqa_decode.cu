@@ -739,10 +739,20 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         if (lane == 0) {
             prefetch_tmap(&tmk);
             prefetch_tmap(&tmv);
-            // before the wait: the first ring's tiles whose positions all lie below L - 1
+            // before the wait: the first ring's tiles whose positions all lie below L - 1,
+            // and the later such tiles into L2 (their ring slots free up only after it)
             for (; it < min(ntiles, kStages); it++) {
                 if ((tile0 + it) * kTile + kTile > L - 1) break;
                 issue(it);
+            }
+            if (it == kStages) {
+                const size_t plane = ((size_t)b * nkv + gl) * cap;
+                for (int j = kStages; j < ntiles; j++) {
+                    const int p0 = (tile0 + j) * kTile;
+                    if (p0 + kTile > L - 1) break;
+                    bulk_prefetch_l2(kcache + (plane + p0) * kD, kTile * kD * 2);
+                    bulk_prefetch_l2(vcache + (plane + p0) * kD, kTile * kD * 2);
+                }
             }
         }
         it = __shfl_sync(0xffffffffu, it, 0);
