@@ -302,6 +302,12 @@ typedef struct qm_gqa_params {
  * QM_E_RANGE if seq_len >= capacity or seq_len >= max_pos.
  * Uses the context workspace for split-KV partials (grown on first use).
  * Cache rows at and past seq_len are never used, whatever they hold.
+ * The kernels run under programmatic dependent launch: the layer parameters
+ * (q_norm, k_norm, the RoPE rows) and the cache rows below seq_len - 1 may be
+ * read before they wait for the preceding kernel of the stream, q_gate,
+ * k_new, v_new and cache row seq_len - 1 only after it; so the kernel just
+ * before a call may write the call's inputs and append row seq_len - 1, not
+ * the parameters or older rows.
  */
 int qm_gqa_decode(qm_ctx* ctx, const qm_gqa_params* p, qm_kv* kv, const float* q_gate,
                   const float* k_new, const float* v_new, float* out);

@@ -756,6 +756,13 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             }
         }
         it = __shfl_sync(0xffffffffu, it, 0);
+        // the layer's parameters are read before the wait (they are not outputs of
+        // the preceding kernel), the new token's k only after it
+        float kn[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) kn[i] = k_norm[lane + 32 * i];
+        const float c = rope_cos[pos * kHalfRot + lane];
+        const float s = rope_sin[pos * kHalfRot + lane];
         pdl_wait();
         // the new token's k: RMSNorm(1+g) + partial RoPE (gemv.rs:945-955); CTA 0 appends k, v
         {
@@ -771,9 +778,7 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
             const float inv = 1.0f / sqrtf(ss * (1.0f / kD) + 1e-6f);  // gemv.rs:591
 #pragma unroll
-            for (int i = 0; i < 8; i++) x[i] = x[i] * inv * (1.0f + k_norm[lane + 32 * i]);
-            const float c = rope_cos[pos * kHalfRot + lane];
-            const float s = rope_sin[pos * kHalfRot + lane];
+            for (int i = 0; i < 8; i++) x[i] = x[i] * inv * (1.0f + kn[i]);
             const float x1 = x[0], x2 = x[1];
             x[0] = x1 * c - x2 * s;
             x[1] = x2 * c + x1 * s;
@@ -830,6 +835,12 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             else if (c_gate != q_gate && t < 98 + 32)
                 prefetch_l2(c_gate + ((size_t)b * kNumH + g * kGroup + (t - 98) / 8) * 2 * kD + kD + ((t - 98) % 8) * 32);
         }
+        // the layer's parameters before the wait (not outputs of the preceding kernel)
+        float qn[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) qn[i] = q_norm[lane + 32 * i];
+        const float rc = rope_cos[pos * kHalfRot + lane];
+        const float rs = rope_sin[pos * kHalfRot + lane];
         pdl_wait();  // q comes from the preceding kernel
         pdl_launch_dependents();
         // the gate logit and new v of the outputs this thread produces after
@@ -858,12 +869,10 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
             const float inv = 1.0f / sqrtf(ss * (1.0f / kD) + 1e-6f);
 #pragma unroll
-            for (int i = 0; i < 8; i++) x[i] = x[i] * inv * (1.0f + q_norm[lane + 32 * i]);
-            const float c = rope_cos[pos * kHalfRot + lane];
-            const float s = rope_sin[pos * kHalfRot + lane];
+            for (int i = 0; i < 8; i++) x[i] = x[i] * inv * (1.0f + qn[i]);
             const float x1 = x[0], x2 = x[1];
-            x[0] = x1 * c - x2 * s;
-            x[1] = x2 * c + x1 * s;
+            x[0] = x1 * rc - x2 * rs;
+            x[1] = x2 * rc + x1 * rs;
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 const int e = lane + 32 * i;
@@ -972,34 +981,43 @@ gqa_fused_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     // taking t, t + 128, ...: merge the nsplit partials, add the new token,
     // apply the gate (gemv.rs:1008-1011)
     if (warp < kGroup) {
+        // every output of this CTA belongs to one head (per divides 256): warp 0
+        // forms the head's maximum, the splits' weights and the sum once, in a
+        // fixed order; the stage buffers hold them (free since the pushes)
+        static_assert(kD % (kGroup * kD / kFusedMaxSplit) == 0 && kFusedMaxSplit <= 31, "one head per owner");
+        float* wsc = reinterpret_cast<float*>(smem);  // [i < nsplit]: split weights, [31]: new token, [30]: sum
+        const int head = (split * per) / kD;
+        if (warp == 0) {
+            const float sn = s_new[head];
+            const bool in = lane < nsplit;
+            const float mi = in ? recv_ml[2 * lane] : -INFINITY;
+            const float li = in ? recv_ml[2 * lane + 1] : 0.f;
+            float M = fmaxf(sn, mi);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            const float f = (mi == -INFINITY) ? 0.f : exp2f((mi - M) * kLog2e);
+            float ls = f * li;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+            const float wn = exp2f((sn - M) * kLog2e);
+            if (in) wsc[lane] = f;
+            if (lane == 0) {
+                wsc[31] = wn;
+                wsc[30] = ls + wn;
+            }
+        }
+        named_bar_sync(1, kGroup * 32);
 #pragma unroll
         for (int u = 0; u < kFusedPerThread; u++) {
             const int oi = threadIdx.x + u * (kGroup * 32);
             if (oi >= per) break;
-            const int idx = split * per + oi;
-            const int head = idx / kD, d = idx % kD;
-            const float sn = s_new[head];
-            float M = sn;
-            float mi[kFusedMaxSplit], li[kFusedMaxSplit], ov[kFusedMaxSplit];
+            const int d = (split * per + oi) % kD;
+            float acc = wsc[31] * red_v[u];
 #pragma unroll
-            for (int i = 0; i < kFusedMaxSplit; i++) {
-                const bool in = i < nsplit;
-                mi[i] = in ? recv_ml[2 * i] : -INFINITY;
-                li[i] = in ? recv_ml[2 * i + 1] : 0.f;
-                ov[i] = in ? recv_o[i * per + oi] : 0.f;
-                M = fmaxf(M, mi[i]);
-            }
-            const float wn = exp2f((sn - M) * kLog2e);
-            float acc = wn * red_v[u];
-            float lsum = wn;
-#pragma unroll
-            for (int i = 0; i < kFusedMaxSplit; i++) {
-                const float f = (mi[i] == -INFINITY) ? 0.f : exp2f((mi[i] - M) * kLog2e);
-                acc = fmaf(f, ov[i], acc);
-                lsum = fmaf(f, li[i], lsum);
-            }
+            for (int i = 0; i < kFusedMaxSplit; i++)
+                if (i < nsplit) acc = fmaf(wsc[i], recv_o[i * per + oi], acc);
             out[(((size_t)b * nkv + gl) * kGroup + head) * kD + d] =
-                (acc / lsum) * (1.0f / (1.0f + __expf(-red_gate[u])));
+                (acc / wsc[30]) * (1.0f / (1.0f + __expf(-red_gate[u])));
         }
     }
 }
