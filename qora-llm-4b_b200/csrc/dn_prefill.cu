@@ -308,21 +308,22 @@ struct ChunkBars {
     int abort_flag;
 };
 
-// ---- 2a. chunk-local WY factors: one CTA (8 warps) per (V head, chunk, sequence) ----
+// ---- 2a. chunk-local WY factors: persistent CTAs (8 warps, two per SM) walk
+// the (V head, chunk, sequence) items ----
 //
 // Everything in a chunk that does not depend on the state entering it:
 //   MMA1  [K;Q] K^T                       (compensated)  -> A (f32) and P'
-//   T = (I + A)^-1 by forward substitution, one column per thread (f32)
+//   T = (I + A)^-1 blocked by 16: the diagonal blocks by forward substitution
+//         (f32), the blocks below them as 3 x TF32 warp-level MMA tiles
 //   MMA2  W^T  = K^T (T diag(b e^G))^T    (compensated)
 //   MMA3  U~^T = V^T (T diag(b))^T        (compensated)
 // written to the workspace for the state pass: W^T fp16 [128 k][64 t],
 // U~^T f32 as [16][128 v][4] (float4 of 4 tokens per v, so the state pass
 // loads it with one bulk copy and reads it conflict-free) and P' fp16 hi/lo
-// [64 t][64 s]: 64 KB per (chunk, V head).  The decayed q and k the state
-// pass needs are formed there from the prep kernel's tiles, which the two V
-// heads of a QK head share in L2.
-// 102 KB of shared memory and 256 TMEM columns: two CTAs per SM.  Warps w and
-// w+4 share TMEM lane quarter w%4 and split the 64 columns of every TMEM tile.
+// [64 t][64 s]: 64 KB per (chunk, V head).  The state pass uses q and k as
+// the prep kernel wrote them (the two V heads of a QK head share them in L2).
+// 102 KB of shared memory and 256 TMEM columns a CTA.  Warps w and w+4 share
+// TMEM lane quarter w%4 and split the 64 columns of every TMEM tile.
 constexpr int kL_KQh = 0;              // [K;Q] hi: 2 boxes [128 rows x 64] fp16 (K rows 0-63,
 constexpr int kL_KQl = 32768;          //   Q rows 64-127); once MMA1 is done the four Q
 constexpr int kL_Vh = kL_KQh + 8192;   //   quarters take V hi / lo [64 t x 64 v] (the boxes
