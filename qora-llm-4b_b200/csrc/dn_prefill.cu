@@ -697,7 +697,7 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
     }
 }
 
-// ---- 2b. state pass: one CTA per (V head, sequence), 8 warps ----
+// ---- 2b. state pass: one CTA per (V head, sequence), 12 warps ----
 //
 // Per chunk c, with S0 the state entering it (f32 master in TMEM, and an fp16
 // copy in TMEM as the A operand), G the in-chunk cumulative log-decay,
