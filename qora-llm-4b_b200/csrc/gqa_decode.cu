@@ -323,28 +323,30 @@ __device__ __forceinline__ void attend_tiles_t(uint32_t sbase, uint64_t* full, u
 #pragma unroll
             for (int i = 0; i < 2; i++)
                 if (p0 + 8 * i >= pos_end) s[0][i] = s[1][i] = -INFINITY;
-            float p[2][2], corr[2];
-            bool rescale = false;
+            // Lazy rescaling: P is taken against the warp's reference maximum
+            // m_run, which moves (a reduction over the warp, then O and the sums
+            // rescaled) only when some score exceeds it by more than 2^8 in
+            // exp2 units; otherwise a tile costs no cross-lane reduction.  The
+            // sums stay per lane until the end (the result does not depend on
+            // the reference: numerator and denominator use the same one).
+            bool grow = false;
 #pragma unroll
-            for (int j = 0; j < 2; j++) {
-                float tmax = fmaxf(s[j][0], s[j][1]);
-                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
-                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
-                tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
-                const float m_new = fmaxf(m_run[j], tmax);
-                const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-                corr[j] = exp2f((m_run[j] - m_use) * kLog2e);
-                p[j][0] = exp2f((s[j][0] - m_use) * kLog2e);
-                p[j][1] = exp2f((s[j][1] - m_use) * kLog2e);
-                float rs = p[j][0] + p[j][1];
-                rs += __shfl_xor_sync(0xffffffffu, rs, 4);
-                rs += __shfl_xor_sync(0xffffffffu, rs, 8);
-                rs += __shfl_xor_sync(0xffffffffu, rs, 16);
-                l_run[j] = l_run[j] * corr[j] + rs;
-                m_run[j] = m_new;
-                rescale |= corr[j] != 1.0f;
-            }
-            if (__any_sync(0xffffffffu, rescale)) {
+            for (int j = 0; j < 2; j++)
+                grow |= (fmaxf(s[j][0], s[j][1]) - m_run[j]) * kLog2e > 8.0f;  // -inf - -inf: NaN, false
+            if (__any_sync(0xffffffffu, grow)) {
+                float corr[2];
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    float tmax = fmaxf(s[j][0], s[j][1]);
+                    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+                    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
+                    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 16));
+                    const float m_new = fmaxf(m_run[j], tmax);
+                    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+                    corr[j] = exp2f((m_run[j] - m_use) * kLog2e);  // m_run -inf: 0 (nothing to keep)
+                    l_run[j] *= corr[j];
+                    m_run[j] = m_new;
+                }
 #pragma unroll
                 for (int mt = 0; mt < 16; mt++) {
                     oc[mt][0] *= corr[0];
@@ -352,6 +354,14 @@ __device__ __forceinline__ void attend_tiles_t(uint32_t sbase, uint64_t* full, u
                     oc[mt][2] *= corr[0];
                     oc[mt][3] *= corr[1];
                 }
+            }
+            float p[2][2];
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const float m_use = (m_run[j] == -INFINITY) ? 0.f : m_run[j];
+                p[j][0] = exp2f((s[j][0] - m_use) * kLog2e);
+                p[j][1] = exp2f((s[j][1] - m_use) * kLog2e);
+                l_run[j] += p[j][0] + p[j][1];
             }
             // P^T fragment: column (hsel, hl) at positions 2q, 2q+1 (b0) and 2q+8, 2q+9 (b1)
             const float a00 = __shfl_sync(0xffffffffu, p[0][0], src_a), a10 = __shfl_sync(0xffffffffu, p[1][0], src_a);
@@ -391,6 +401,13 @@ __device__ __forceinline__ void attend_tiles_t(uint32_t sbase, uint64_t* full, u
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&empty[st]));
+    }
+    // the warp's sums over its 16 positions (lanes with the same heads)
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 4);
+        l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 8);
+        l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 16);
     }
 }
 
