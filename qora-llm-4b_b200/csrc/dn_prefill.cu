@@ -343,6 +343,7 @@ __global__ void __launch_bounds__(kLocalThreads, 2)
 dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ CUtensorMap tql,
                const __grid_constant__ CUtensorMap tkh, const __grid_constant__ CUtensorMap tkl,
                const __grid_constant__ CUtensorMap tvh, const __grid_constant__ CUtensorMap tvl,
+               const __grid_constant__ CUtensorMap tmw,
                const float* __restrict__ gin, const float* __restrict__ bin, int T, int nch, int B,
                uint16_t* __restrict__ wt_out, float* __restrict__ ut_out,
                uint16_t* __restrict__ ph_out, uint16_t* __restrict__ pl_out, int* err) {
@@ -437,6 +438,7 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
             sg[tid] = g_own;
             sB[tid] = b_own;
         }
+        if (tid == 0) bulk_wait_read0();  // the previous item's W^T store has read the A region
         __syncthreads();
         if (warp == 0) chunk_decays(sg, sG, eG, eD, lane);
         ok = mbar_wait_bounded(smem_u32(&bars->load), 0, abort_flag, err);
@@ -665,15 +667,24 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
             }
         }
 
-        // ---- outputs: W^T row k (fp16), U~^T row v (f32, [t/4][v][4]); this
-        // thread's 32 tokens [32 half, 32 half + 32) ----
-        if (QM_IN(item * kHd * kC, kHd * kC, (size_t)nitems * kHd * kC, err)) {
+        // ---- outputs: W^T row k (fp16) through the A region (free since MMA2/3)
+        // and one TMA store; U~^T row v (f32, [t/4][v][4]) straight to global.
+        // This thread's 32 tokens [32 half, 32 half + 32) ----
+        {
             float wv[32];
             tmem_ld32(tm + lane_addr + kTmW + half * 32, wv);
             tmem_ld_wait();
-            uint4* wrow = reinterpret_cast<uint4*>(wt_out + (item * kHd + row) * kC) + half * 4;
 #pragma unroll
-            for (int t = 0; t < 32; t += 8) wrow[t / 8] = round8(wv + t);
+            for (int t = 0; t < 32; t += 8)
+                *reinterpret_cast<uint4*>(smem + kL_A + sw128_off(row, half * 4 + t / 8)) = round8(wv + t);
+        }
+        fence_proxy_async_shared();
+        __syncthreads();
+        if (tid == 0 && QM_IN(item * kHd * kC, kHd * kC, (size_t)nitems * kHd * kC, err)) {
+            tma_store_3d(&tmw, sb + kL_A, 0, 0, (int)item);
+            bulk_commit();
+        }
+        if (QM_IN(item * kHd * kC, kHd * kC, (size_t)nitems * kHd * kC, err)) {
             float uv[32];
             tmem_ld32(tm + lane_addr + kTmU + half * 32, uv);
             tmem_ld_wait();
@@ -686,6 +697,7 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
     }  // items
 
     if (tid == 0) {
+        bulk_wait0();  // every W^T store has completed
         if (ld_out) mbar_drain(smem_u32(&bars->load), ld_par);
         if (mm_out) mbar_drain(smem_u32(&bars->mma), mm_par);
     }
@@ -1334,8 +1346,8 @@ cudaError_t launch_dn_prefill(qm_ctx* ctx, const qm_dn_params* p, qm_dn_state* s
         TimedLaunch tl(ctx, "dn_chunk_local");
         const int nitems = B * kNumV * nch;  // persistent: two CTAs per SM walk the items
         const int grid = std::min(nitems, 2 * std::max(ctx->num_sms, 1));
-        dn_chunk_local<<<grid, kLocalThreads, kLocalSmem, s>>>(m[0], m[1], m[2], m[3], m[4], m[5], g, be, T,
-                                                               nch, B, wt, ut, ph, pl, ctx->d_err);
+        dn_chunk_local<<<grid, kLocalThreads, kLocalSmem, s>>>(m[0], m[1], m[2], m[3], m[4], m[5], mwt, g, be,
+                                                               T, nch, B, wt, ut, ph, pl, ctx->d_err);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
