@@ -554,7 +554,7 @@ dn_decode_stream(const float* __restrict__ qkv, const float* __restrict__ a_in,
     // do not leave while copies this CTA issued may still land
     if (tid == 0)
         for (int i = 0; i < NB; i++)
-            if (pending[i] >= 0) mbar_drain(smem_u32(&full[i]), (pending[i] / NB) & 1);
+            if (pending[i] >= 0) mbar_drain(smem_u32(&full[i]), (pending[i] / NB) & 1, err);
 }
 
 template <int SPLIT, bool FUSED>

@@ -698,8 +698,8 @@ dn_chunk_local(const __grid_constant__ CUtensorMap tqh, const __grid_constant__ 
 
     if (tid == 0) {
         bulk_wait0();  // every W^T store has completed
-        if (ld_out) mbar_drain(smem_u32(&bars->load), ld_par);
-        if (mm_out) mbar_drain(smem_u32(&bars->mma), mm_par);
+        if (ld_out) mbar_drain(smem_u32(&bars->load), ld_par, err);
+        if (mm_out) mbar_drain(smem_u32(&bars->mma), mm_par, err);
     }
     tc_fence_before();
     __syncthreads();
@@ -787,9 +787,9 @@ struct Pending {
         par = parity ? (par | bit) : (par & ~bit);
     }
     __device__ void seen(uint64_t* b) { out &= ~(1u << (uint32_t)(b - base)); }
-    __device__ void drain() {
+    __device__ void drain(int* err) {
         for (int i = 0; i < 11; i++)
-            if (out & (1u << i)) mbar_drain(smem_u32(base + i), (par >> i) & 1u);
+            if (out & (1u << i)) mbar_drain(smem_u32(base + i), (par >> i) & 1u, err);
     }
 };
 
@@ -1225,7 +1225,7 @@ dn_chunk_state(const __grid_constant__ CUtensorMap twt, const __grid_constant__ 
         if (yt == 0) bulk_wait0();  // the last y stores have completed
     }
     // do not leave while copies or MMAs this CTA issued may still land
-    pend.drain();
+    pend.drain(err);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {

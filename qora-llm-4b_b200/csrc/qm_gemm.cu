@@ -140,7 +140,7 @@ qm_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restric
             }
             // every copy this thread issued has landed before the CTA can leave
             for (int i = issued - kGmStages > 0 ? issued - kGmStages : 0; i < issued; i++)
-                mbar_drain(smem_u32(&bars->x_full[i % kGmStages]), (i / kGmStages) & 1);
+                mbar_drain(smem_u32(&bars->x_full[i % kGmStages]), (i / kGmStages) & 1, err);
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issue
@@ -385,7 +385,7 @@ qm_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restric
     }
     // the MMA thread committed `done` on every path: once it completes, no
     // MMA still writes TMEM
-    if (warp == 1 && lane == 0) mbar_drain(smem_u32(&bars->done), 0);
+    if (warp == 1 && lane == 0) mbar_drain(smem_u32(&bars->done), 0, err);
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {

@@ -70,13 +70,18 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     }
 }
 
-// On the way out of an aborted CTA: wait (with the same limit, ignoring the
-// abort flag) for a phase whose copies or MMAs this CTA issued, so nothing
-// lands in shared memory or TMEM after the CTA has released them.
-__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+// On the way out of a CTA: wait (with the same limit, ignoring the abort
+// flag) for a phase whose copies or MMAs this CTA issued and did not see
+// complete, so nothing lands in shared memory or TMEM after the CTA has
+// released them.  Giving up sets the timeout bit of the error word, if given:
+// a phase that never completes means the CTA's own bookkeeping went wrong.
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity, int* err = nullptr) {
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > kWaitCycles) return;
+        if (clock64() - t0 > kWaitCycles) {
+            if (err) atomicOr(err, kErrTimeout);
+            return;
+        }
     }
 }
 
