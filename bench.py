@@ -567,6 +567,7 @@ def bench_gqa_prefill(ctx, ws, reps, B=4, T=32768):
         mx.gqa_prefill(prm, kv, T, qg, kk, vv, out)
     e1.record(stream)
     torch.cuda.synchronize()
+    ctx.sync()  # a device-side timeout in the timed calls fails the record instead of timing it
     call_ms = max_over_ranks(e0.elapsed_time(e1) / reps, ws)
     att_ms, att_n = ctx.kernel_time("gqa_prefill_attn")
     prep_ms, _ = ctx.kernel_time("gqa_prefill_prep")
@@ -873,6 +874,7 @@ def bench_dn_prefill(ctx, ws, reps, B=8, T=8192):
         e1.record(stream)
         torch.cuda.synchronize()
         tot += e0.elapsed_time(e1)
+    ctx.sync()  # a device-side timeout in the timed calls fails the record instead of timing it
     call_ms = max_over_ranks(tot / reps, ws)
     loc_ms, k_n = ctx.kernel_time("dn_chunk_local")
     sta_ms, _ = ctx.kernel_time("dn_chunk_state")
