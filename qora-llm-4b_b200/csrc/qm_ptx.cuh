@@ -56,13 +56,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait on phase `parity`.  Returns false (and sets the error word and
 // the CTA abort flag) when the limit passes or another warp already aborted.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
-                                                  volatile int* abort_flag, int* err) {
+                                                  volatile int* abort_flag, int* err,
+                                                  long long limit = kWaitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
         if (*abort_flag) return false;
         if (mbar_try_wait(bar, parity)) return true;
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > limit) {
             *abort_flag = 1;
             atomicOr(err, kErrTimeout);
             return false;

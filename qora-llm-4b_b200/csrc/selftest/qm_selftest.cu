@@ -162,10 +162,55 @@ umma_selftest_kernel(const __grid_constant__ CUtensorMap tma, const __grid_const
 }
 
 
+// Failure detection without a fault: 64 threads wait on an mbarrier nothing
+// arrives at, through the library's bounded wait with a short limit.  The
+// first thread to give up sets the error word and the CTA abort flag; the
+// others then return at once.  Records how many waits succeeded (none
+// should) and the longest wait in cycles.
+__global__ void wait_timeout_selftest_kernel(long long limit, int* err, int* n_true, long long* max_cycles) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag_s;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        abort_flag_s = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const long long t0 = clock64();
+    const bool ok = mbar_wait_bounded(smem_u32(&bar), 0, &abort_flag_s, err, limit);
+    const long long dt = clock64() - t0;
+    if (ok) atomicAdd(n_true, 1);
+    atomicMax(reinterpret_cast<unsigned long long*>(max_cycles), (unsigned long long)dt);
+}
+
 }  // namespace
 }  // namespace qm
 
 using namespace qm;
+
+// Runs wait_timeout_selftest_kernel with `limit` cycles; returns the error
+// word, the number of waits that succeeded and the longest wait.  The kernel
+// ends normally either way: a QM status other than QM_OK means the launch
+// itself failed.
+extern "C" int qm_selftest_wait_timeout(long long limit, int* err_word, int* n_true, long long* max_cycles) {
+    int* d = nullptr;
+    if (cudaMalloc(&d, 4 * sizeof(long long)) != cudaSuccess) return QM_E_OOM;
+    cudaMemset(d, 0, 4 * sizeof(long long));
+    int* d_err = d;
+    int* d_n = d + 2;
+    long long* d_max = reinterpret_cast<long long*>(d) + 2;
+    wait_timeout_selftest_kernel<<<1, 64>>>(limit, d_err, d_n, d_max);
+    cudaError_t e = cudaDeviceSynchronize();
+    long long h[4] = {0, 0, 0, 0};
+    cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    if (e != cudaSuccess) return QM_E_CUDA;
+    const int* hi = reinterpret_cast<const int*>(h);
+    *err_word = hi[0];
+    *n_true = hi[2];
+    *max_cycles = h[2];
+    return QM_OK;
+}
 
 // a [128x256], b [64x256], v [64x256], p [128x64] (device; all bf16, or all
 // fp16 when mode bit 0 is set; mode bit 1: the first product reads a from
