@@ -289,22 +289,54 @@ qm_gemv_kernel(const __grid_constant__ GvArgs a) {
     }
     __syncthreads();
     if (!last_cta) return;
+    // The last CTA's sum is spread over its warps so that few L2 round trips
+    // are in series: warp w adds the contiguous parts [w P/8, (w+1) P/8) of all
+    // T columns (lane: LC columns as float4s, the loads of 4 parts in flight),
+    // then the 8 warp sums are added in warp order through shared memory (the
+    // CTA-sum area, no longer read).  A fixed order: the result does not depend
+    // on which CTA finished last.
     const float* tp = a.partial + ((size_t)tile * a.parts * BT) * T;
+    constexpr int LC = T / 32;  // columns per lane: 16 Q4, 8 F16
+    float* wsum = red;          // [warps][BT][T]; fits the [warps][BT][16][PAD] area
+    const int pw0 = (a.parts * warp) / kGvWarps, pw1 = (a.parts * (warp + 1)) / kGvWarps;
+#pragma unroll
+    for (int b = 0; b < BT; b++) {
+        float4 s[LC / 4];
+#pragma unroll
+        for (int q = 0; q < LC / 4; q++) s[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int p = pw0; p < pw1; p += 4) {
+            float4 v[4][LC / 4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+#pragma unroll
+                for (int q = 0; q < LC / 4; q++)
+                    v[u][q] = p + u < pw1 ? __ldcg(reinterpret_cast<const float4*>(
+                                                tp + ((size_t)(p + u) * BT + b) * T + lane * LC) + q)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (p + u < pw1)
+#pragma unroll
+                    for (int q = 0; q < LC / 4; q++) {
+                        s[q].x += v[u][q].x;
+                        s[q].y += v[u][q].y;
+                        s[q].z += v[u][q].z;
+                        s[q].w += v[u][q].w;
+                    }
+        }
+#pragma unroll
+        for (int q = 0; q < LC / 4; q++)
+            *reinterpret_cast<float4*>(&wsum[((size_t)warp * BT + b) * T + lane * LC + 4 * q]) = s[q];
+    }
+    __syncthreads();
 #pragma unroll
     for (int b = 0; b < BT; b++)
 #pragma unroll
         for (int c = 0; c < CPT; c++) {
             const int col = c * kGvThreads + tid;
             float tot = 0.f;
-            for (int p0 = 0; p0 < a.parts; p0 += 16) {
-                float v[16];
 #pragma unroll
-                for (int u = 0; u < 16; u++)
-                    v[u] = p0 + u < a.parts ? __ldcg(&tp[((size_t)(p0 + u) * BT + b) * T + col]) : 0.f;
-#pragma unroll
-                for (int u = 0; u < 16; u++)
-                    if (p0 + u < a.parts) tot += v[u];
-            }
+            for (int w = 0; w < kGvWarps; w++) tot += wsum[((size_t)w * BT + b) * T + col];
             if (tcol + col < n) jb.y[(size_t)b * n + tcol + col] = tot;
         }
     if (tid == 0) a.count[tile] = 0;  // ready for the next launch
