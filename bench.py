@@ -491,12 +491,7 @@ def run_ours(args):
         "higher_is_better": True, "scaling": "strong" if args.strong else "weak",
         "vs_baseline": None, "dtype": "f32 state / bf16 KV (f32 math)",
         "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) states/caches, random-init params)",
-        "config": {"workload": WORKLOAD if ctx_len == CTX and B == B_PER_GPU else
-                   f"mixer-stack decode: 32 layers, ctx {ctx_len}, batch {B} (reduced case)",
-                   "global_batch": B * ws, "batch_per_gpu": B,
-                   "context": ctx_len, "layers": "24 DeltaNet + 8 GQA",
-                   "parallelism": f"sequence-sharded x{ws}, no collective",
-                   "l2": f"inputs larger than L2 ({attn_bytes(B, ctx_len) * 8 / 1e9:.1f} GB of KV per GPU)"},
+        "config": decode_config(ws, B, ctx_len),
         "e2e": e2e,
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "kernel": "gqa_attn (split-KV attention)",
@@ -1254,6 +1249,17 @@ def cpu_model():
     return "unknown"
 
 
+def decode_config(ws, B, ctx_len):
+    """The decode workload's config, the same in both arms: the reference arm
+    times a bounded sample of it (its cpu_baseline.sample says which)."""
+    return {"workload": WORKLOAD if ctx_len == CTX and B == B_PER_GPU else
+            f"mixer-stack decode: 32 layers, ctx {ctx_len}, batch {B} (reduced case)",
+            "global_batch": B * ws, "batch_per_gpu": B,
+            "context": ctx_len, "layers": "24 DeltaNet + 8 GQA",
+            "parallelism": f"sequence-sharded x{ws}, no collective",
+            "l2": f"inputs larger than L2 ({attn_bytes(B, ctx_len) * 8 / 1e9:.1f} GB of KV per GPU)"}
+
+
 def run_reference(args):
     ws, rank, local = dist_env()
     if rank != 0:
@@ -1275,7 +1281,8 @@ def run_reference(args):
     tot = sum(times)
     value = per_step * args.steps / tot
     sample = (f"{per_step} decode token(s) of one sequence per step through all 32 mixer layers at "
-              f"context {CTX} (the reference processes sequences one at a time); GQA heads on an "
+              f"context {CTX} (the reference processes sequences one at a time, so its rate over the "
+              f"{B_PER_GPU * ws} sequences is this one's); GQA heads on an "
               "OpenMP pool as rayon does (gemv.rs:963), DeltaNet heads serial with the AVX-512 "
               "head update (gemv.rs:817, simd.rs:292-362)")
     line = {
@@ -1284,8 +1291,7 @@ def run_reference(args):
         "ms_per_step": round(tot / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded)",
-        "config": {"workload": WORKLOAD, "global_batch": 1, "context": CTX,
-                   "parallelism": "CPU restatement of the reference (Rust not buildable here)"},
+        "config": decode_config(ws, B_PER_GPU, CTX),
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": min(16, orc.num_threads()),
                          "kind": "port", "sample": sample, "cpu": cpu_model()},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,

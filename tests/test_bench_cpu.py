@@ -30,6 +30,12 @@ def test_reference_arm_prints_one_contract_line():
     assert d["value"] > 0 and d["unit"] == "tok/s" and d["higher_is_better"] is True
     assert d["steps"] == 1 and d["warmup"] >= 3 and d["n_gpus"] == 1
     assert d["config"]["workload"].startswith("mixer-stack decode")
+    # the same config dict as the GPU arm's at this world size (a sample of it is timed)
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bm = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bm)
+    assert d["config"] == bm.decode_config(1, bm.B_PER_GPU, bm.CTX)
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["sample"] and cb["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
