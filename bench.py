@@ -14,7 +14,9 @@ value  = tokens/s of the whole job with inputs resident in HBM.
 e2e    = the same through the C ABI's _host entry points: every layer call
          copies its inputs from pinned host memory and its output back.
 roofline = the dominant kernel (split-KV GQA attention) against the
-         measured HBM copy bandwidth.
+         measured HBM copy bandwidth; its launch durations come from a second
+         timed pass of the same steps with CUDA events around every launch
+         (events between kernels serialise them, so `value`'s pass has none).
 cpu_baseline = the CPU restatement of the reference mixer path on a bounded
          sample (rank 0, N=1 only).
 
@@ -417,7 +419,8 @@ def run_ours(args):
     torch.cuda.set_device(local)
     B = args.batch if not args.strong else max(1, args.batch // ws)
     ctx_len = args.context
-    cap = ctx_len + 2 * (args.warmup + args.steps) + 16
+    # tokens appended: warm-up, the timed steps, the per-kernel pass, the e2e pass
+    cap = ctx_len + 3 * (args.warmup + args.steps) + 16
     ctx = qm.Ctx(local, stream=torch.cuda.current_stream())
     stack = Stack(ctx, B, cap, seed=rank, ctx_len=ctx_len)
     stream = torch.cuda.current_stream()
@@ -430,8 +433,6 @@ def run_ours(args):
     clocks = Clocks(local)
     clocks.start()
     time.sleep(1.0)  # let nvidia-smi start sampling before the timed region
-    ctx.set_timing(True)
-    L0 = stack.seq_len()
     n0 = ctx.launch_count()
     torch.cuda.synchronize()
     barrier(ws)
@@ -444,9 +445,22 @@ def run_ours(args):
     barrier(ws)
     launches = ctx.launch_count() - n0
     ms_local = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+
+    # ---- per-kernel durations: a second timed pass of the same K steps with
+    # the library's event pair around every launch (on the launching stream).
+    # An event between two kernels also keeps the second from starting early
+    # behind the first, so the step time above is taken without them. ----
+    L0 = stack.seq_len()
+    ctx.set_timing(True)
+    torch.cuda.synchronize()
+    barrier(ws)
+    for _ in range(args.steps):
+        stack.step()
+    torch.cuda.synchronize()
+    barrier(ws)
     ktimes = {k: ctx.kernel_time(k) for k in ("dn_decode", "gqa_prep", "gqa_attn", "gqa_combine")}
     ctx.set_timing(False)
-    clk = clocks.stop()
     ctx.sync()
     ms = max_over_ranks(ms_local, ws)
     ms_step = ms / args.steps
@@ -502,7 +516,10 @@ def run_ours(args):
                                         "of an ncu capture of a smaller case (profiles/traffic.json) x batch x "
                                         "positions") if att_traffic else None,
                      "algorithmic_bytes_per_launch": att_bytes,
-                     "avg_launch_us": round(att_ms / att_n * 1e3, 2)},
+                     "avg_launch_us": round(att_ms / att_n * 1e3, 2),
+                     "timing": ("CUDA events around every launch on the launching stream, over a second "
+                                "timed pass of the same steps (the step time is taken without them: an "
+                                "event between two kernels serialises them)")},
         "kernels": {
             k: {"launches_per_step": v[1] / args.steps, "ms_per_step": round(v[0] / args.steps, 4)}
             for k, v in ktimes.items()},
