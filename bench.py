@@ -14,7 +14,7 @@ value  = tokens/s of the whole job with inputs resident in HBM.
 e2e    = the same through the C ABI's _host entry points: every layer call
          copies its inputs from pinned host memory and its output back.
 roofline = the dominant kernel (split-KV GQA attention) against the
-         measured HBM copy bandwidth; its launch durations come from a second
+         measured HBM copy bandwidth; its launch durations come from a further
          timed pass of the same steps with CUDA events around every launch
          (events between kernels serialise them, so `value`'s pass has none).
 cpu_baseline = the CPU restatement of the reference mixer path on a bounded
@@ -447,37 +447,10 @@ def run_ours(args):
     ms_local = ev0.elapsed_time(ev1)
     clk = clocks.stop()
 
-    # ---- per-kernel durations: a second timed pass of the same K steps with
-    # the library's event pair around every launch (on the launching stream).
-    # An event between two kernels also keeps the second from starting early
-    # behind the first, so the step time above is taken without them. ----
-    L0 = stack.seq_len()
-    ctx.set_timing(True)
-    torch.cuda.synchronize()
-    barrier(ws)
-    for _ in range(args.steps):
-        stack.step()
-    torch.cuda.synchronize()
-    barrier(ws)
-    ktimes = {k: ctx.kernel_time(k) for k in ("dn_decode", "gqa_prep", "gqa_attn", "gqa_combine")}
-    ctx.set_timing(False)
-    ctx.sync()
     ms = max_over_ranks(ms_local, ws)
     ms_step = ms / args.steps
     tokens = B * ws * args.steps
     value = tokens / (ms / 1e3)
-
-    # ---- roofline of the dominant kernel (split-KV attention) ----
-    peak, peak_kind = load_peaks()
-    att_ms, att_n = ktimes["gqa_attn"]
-    L_avg = L0 + (args.steps - 1) / 2.0
-    att_bytes = attn_bytes(B, L_avg)
-    att_achieved = att_bytes / (att_ms / att_n / 1e3) / 1e9
-    dn_ms, dn_n = ktimes["dn_decode"]
-    dn_achieved = B * DN_BYTES_TOKEN / (dn_ms / dn_n / 1e3) / 1e9
-    traffic = load_traffic().get("gqa_attn_bytes_per_seq_pos")
-    att_traffic = traffic * B * L_avg if traffic else None
-    step_kernel_ms = sum(v[0] for v in ktimes.values()) / args.steps
 
     # ---- e2e through the _host entry points ----
     e2e = None
@@ -499,6 +472,34 @@ def run_ours(args):
         e2e = {"value": round(tokens / (e2e_ms / 1e3), 2), "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
+    # ---- per-kernel durations: a further timed pass of the same K steps with
+    # the library's event pair around every launch (on the launching stream),
+    # after the e2e pass so that it runs where it always did.  An event between
+    # two kernels also keeps the second from starting early behind the first,
+    # so the step time above is taken without them. ----
+    L0 = stack.seq_len()
+    ctx.set_timing(True)
+    torch.cuda.synchronize()
+    barrier(ws)
+    for _ in range(args.steps):
+        stack.step()
+    torch.cuda.synchronize()
+    barrier(ws)
+    ktimes = {k: ctx.kernel_time(k) for k in ("dn_decode", "gqa_prep", "gqa_attn", "gqa_combine")}
+    ctx.set_timing(False)
+    ctx.sync()
+    # ---- roofline of the dominant kernel (split-KV attention) ----
+    peak, peak_kind = load_peaks()
+    att_ms, att_n = ktimes["gqa_attn"]
+    L_avg = L0 + (args.steps - 1) / 2.0
+    att_bytes = attn_bytes(B, L_avg)
+    att_achieved = att_bytes / (att_ms / att_n / 1e3) / 1e9
+    dn_ms, dn_n = ktimes["dn_decode"]
+    dn_achieved = B * DN_BYTES_TOKEN / (dn_ms / dn_n / 1e3) / 1e9
+    traffic = load_traffic().get("gqa_attn_bytes_per_seq_pos")
+    att_traffic = traffic * B * L_avg if traffic else None
+    step_kernel_ms = sum(v[0] for v in ktimes.values()) / args.steps
+
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
@@ -517,7 +518,7 @@ def run_ours(args):
                                         "positions") if att_traffic else None,
                      "algorithmic_bytes_per_launch": att_bytes,
                      "avg_launch_us": round(att_ms / att_n * 1e3, 2),
-                     "timing": ("CUDA events around every launch on the launching stream, over a second "
+                     "timing": ("CUDA events around every launch on the launching stream, over a further "
                                 "timed pass of the same steps (the step time is taken without them: an "
                                 "event between two kernels serialises them)")},
         "kernels": {
