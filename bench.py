@@ -886,7 +886,6 @@ def bench_dn_prefill(ctx, ws, reps, B=8, T=8192):
         mx.dn_prefill(prm, st, T, qkv, a, bb, y)
     ctx.sync()
     barrier(ws)
-    ctx.set_timing(True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     tot = 0.0
     for _ in range(reps):
@@ -898,6 +897,14 @@ def bench_dn_prefill(ctx, ws, reps, B=8, T=8192):
         tot += e0.elapsed_time(e1)
     ctx.sync()  # a device-side timeout in the timed calls fails the record instead of timing it
     call_ms = max_over_ranks(tot / reps, ws)
+    # the per-kernel split from the same calls again with an event pair around
+    # every launch (events between the call's kernels would add gaps to call_ms)
+    ctx.set_timing(True)
+    for _ in range(reps):
+        st.reset()
+        mx.dn_prefill(prm, st, T, qkv, a, bb, y)
+    torch.cuda.synchronize()
+    ctx.sync()
     loc_ms, k_n = ctx.kernel_time("dn_chunk_local")
     sta_ms, _ = ctx.kernel_time("dn_chunk_state")
     prep_ms, _ = ctx.kernel_time("dn_prefill_prep")
