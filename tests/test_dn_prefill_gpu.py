@@ -149,9 +149,8 @@ def _oracle_prefill_heads(orc, c, qh, a, b, p, heads, groups=16):
 
 def test_config2_prefill(ctx, orc):
     """Config 2: batch 8 x 8192 tokens, chunk 64.  q/k/v raw inputs drawn on the
-    device (bf16).  Sequences 0 and 5 are checked in full — every token of all
-    32 V heads and all 32 final states — and every other sequence on one V
-    head, against the sequential recurrence."""
+    device (bf16).  Checked in full against the sequential recurrence: every
+    token of all 32 V heads and all 32 final states of all 8 sequences."""
     import torch
 
     import qora_mixer as qm
@@ -170,9 +169,8 @@ def test_config2_prefill(ctx, orc):
     qm.Mixer(ctx).dn_prefill(prm, st, T, qkv.view(torch.int16), dev(a), dev(b), y)
     ctx.sync()
     worst = 0.0
-    full = (0, 5)
     for bi in range(B):
-        heads = range(32) if bi in full else [(5 * bi + 3) % 32]
+        heads = range(32)
         qh = host(qkv[bi].view(torch.int16))
         yo, so = _oracle_prefill_heads(orc, c, qh, a[bi], b[bi], p, heads)
         s_g, _ = st.read(bi)
@@ -182,5 +180,4 @@ def test_config2_prefill(ctx, orc):
             es = refmath.rel_err(s_g[vh], so[vh])
             worst = max(worst, e, es)
             assert e <= TOL and es <= TOL, (bi, vh, e, es)
-    print(f"config 2 prefill: worst rel err (y and S; all heads of sequences {full}, "
-          f"one head of the others) {worst:.2e}")
+    print(f"config 2 prefill: worst rel err over y and S, all sequences and heads: {worst:.2e}")
