@@ -243,25 +243,41 @@ class Stack:
                 mx.gqa_decode(L["prm"], L["kv"], *L["in"], L["out"])
 
     def make_host_io(self):
-        """Pinned host copies of every layer's inputs and outputs (for e2e)."""
+        """Pinned host copies of every layer's inputs and outputs (for e2e),
+        and each layer's C-ABI call with its arguments bound once, as a
+        compiled caller holds them (the per-call Python argument conversion of
+        the ctypes mirror is not the library's cost)."""
+        import ctypes as C
+
         import torch
 
+        import qora_mixer as qm
+
+        lib = qm.lib()
         for L in self.layers:
             L["hin"] = [t.cpu().pin_memory() for t in L["in"]]
             L["hout"] = torch.empty(L["out"].shape, dtype=torch.float32).pin_memory()
+            hin = [t.data_ptr() for t in L["hin"]]
+            out = L["hout"].data_ptr()
+            if L["kind"] == "dn":
+                qkv, a, b, z = hin
+                L["host_call"] = (lib.qm_dn_decode_host,
+                                  (self.ctx.handle, C.byref(L["prm"]), L["st"].handle, qkv, a, b, None, z, out))
+            else:
+                L["host_call"] = (lib.qm_gqa_decode_host,
+                                  (self.ctx.handle, C.byref(L["prm"]), L["kv"].handle, *hin, out))
         h2d = sum(t.numel() * 4 for L in self.layers for t in L["hin"])
         d2h = sum(L["hout"].numel() * 4 for L in self.layers)
         return h2d, d2h
 
     def step_host(self):
-        mx = self.mx
+        """One step through qm_dn_decode_host / qm_gqa_decode_host: each call
+        returns once its output is in the pinned host buffer."""
         for L in self.layers:
-            hin = [t.numpy() for t in L["hin"]]
-            if L["kind"] == "dn":
-                qkv, a, b, z = hin
-                mx.dn_decode_host(L["prm"], L["st"], qkv, a, b, None, z, L["hout"].numpy())
-            else:
-                mx.gqa_decode_host(L["prm"], L["kv"], *hin, L["hout"].numpy())
+            fn, args = L["host_call"]
+            rc = fn(*args)
+            if rc != 0:
+                self.ctx.check(rc, "host-buffer layer call")
 
     def seq_len(self):
         return self.layers[3]["kv"].seq_len
