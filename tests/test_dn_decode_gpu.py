@@ -266,3 +266,57 @@ def test_host_variant_in_place_on_pinned_buffers(ctx, orc):
             np.testing.assert_array_equal(st_h.read(bi)[1], st_d.read(bi)[1])
     finally:
         ctx.set_host_direct(True)
+
+
+def test_host_staged_in_parts(ctx, orc):
+    """qm_ctx_set_host_parts: the staged qm_dn_decode_host cut into 1, 3 and 8
+    parts (overlapped copies and launches on three streams) matches the
+    device-buffer call within 1e-5 and the restatement within 1e-3, and
+    advances the same conv history; part counts outside 0..8 are refused."""
+    import torch
+
+    import qora_mixer as qm
+
+    B = 16
+    g = I.rng(853)
+    p = I.dn_layer_params(g)
+    keep = [dev(p["conv_w"]), dev(p["a_log"]), dev(p["dt_bias"]), dev(p["norm_gamma"])]
+    prm = qm.dn_params(*keep)
+    mx = qm.Mixer(ctx)
+    st_d, st_h = qm.DnState(ctx, B), qm.DnState(ctx, B)
+    c = orc.cfg_4b()
+    ost = [orc.DnState(c) for _ in range(B)]
+    try:
+        for parts in (1, 3, 8):
+            toks = I.dn_token_inputs(g, 1, B)
+            qkv, a, b, z = (np.ascontiguousarray(toks[k][:, 0]) for k in ("qkv", "a", "b", "z"))
+            y = torch.empty(B, 32, 128, device="cuda")
+            out = torch.empty(B, 4096, device="cuda")
+            mx.dn_decode(prm, st_d, dev(qkv), dev(a), dev(b), y, dev(z), out)
+            ctx.sync()
+            yh = torch.empty(B, 32, 128).pin_memory()
+            oh = torch.empty(B, 4096).pin_memory()
+            ctx.set_host_direct(False)
+            ctx.set_host_parts(parts, 0)
+            n0, c0 = ctx.launch_count(), ctx.host_calls()
+            mx.dn_decode_host(prm, st_h, _pinned(qkv), _pinned(a), _pinned(b), yh, _pinned(z), oh)
+            assert ctx.launch_count() - n0 == parts  # one decode launch a part
+            assert ctx.host_calls()[1] - c0[1] == 1  # staged
+            assert refmath.rel_err(yh.numpy(), host(y)) <= 1e-5
+            assert refmath.rel_err(oh.numpy(), host(out)) <= 1e-5
+            for bi in range(B):
+                yo, go = orc.dn_decode(c, ost[bi], qkv[bi], a[bi], b[bi], p["conv_w"], p["a_log"],
+                                       p["dt_bias"], use_avx512=False, z=z[bi], norm_gamma=p["norm_gamma"])
+                assert refmath.rel_err(yh.numpy()[bi], yo) <= TOL
+                assert refmath.rel_err(oh.numpy()[bi], go) <= TOL
+        for bi in (0, 7, 15):
+            np.testing.assert_array_equal(st_h.read(bi)[1], st_d.read(bi)[1])  # conv history, raw inputs
+        for bad in (9, -1):
+            with pytest.raises(qm.QmError) as e:
+                ctx.set_host_parts(bad, 0)
+            assert e.value.code == 1  # QM_E_ARG
+    finally:
+        ctx.set_host_parts(0, 0)
+        ctx.set_host_direct(True)
+        st_d.close()
+        st_h.close()

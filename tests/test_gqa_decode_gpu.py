@@ -237,3 +237,44 @@ def test_cache_rows_past_seq_len_may_hold_nan(ctx, orc):
         ref = orc.gqa_decode(c, okv[bi], tok["q_gate"][bi], tok["k_new"][bi], tok["v_new"][bi],
                              pr["q_norm"], pr["k_norm"], cos, sin)
         assert refmath.rel_err(o[bi], ref) <= TOL
+
+
+def test_host_staged_in_parts(ctx, orc):
+    """qm_ctx_set_host_parts: the staged qm_gqa_decode_host cut into 1, 3 and 8
+    parts matches the device-buffer call within 1e-3 and appends the same V
+    rows bit for bit and K rows within one bf16 rounding (a part of two
+    sequences takes the one-launch kernel, the whole batch the split-KV one)."""
+    import torch
+
+    import qora_mixer as qm
+
+    B, L = 16, 150
+    g, c, pr, cos, sin, K, V, okv, kvh, prm, keep = _setup(ctx, orc, B, L, L + 8, 861)
+    K2, V2 = K.clone(), V.clone()
+    kvd = qm.KvCache(ctx, B, L + 8, K2, V2)
+    kvd.seq_len = L
+    mx = qm.Mixer(ctx)
+    try:
+        for t, parts in enumerate((1, 3, 8)):
+            tok = I.gqa_token_inputs(g, B)
+            out = torch.empty(B, 16, 256, device="cuda")
+            mx.gqa_decode(prm, kvd, dev(tok["q_gate"]), dev(tok["k_new"]), dev(tok["v_new"]), out)
+            ctx.sync()
+            ins = [torch.from_numpy(np.ascontiguousarray(tok[k])).pin_memory()
+                   for k in ("q_gate", "k_new", "v_new")]
+            oh = torch.empty(B, 16, 256).pin_memory()
+            ctx.set_host_direct(False)
+            ctx.set_host_parts(0, parts)
+            c0 = ctx.host_calls()
+            mx.gqa_decode_host(prm, kvh, *ins, oh)
+            assert ctx.host_calls()[1] - c0[1] == 1  # staged
+            assert refmath.rel_err(oh.numpy(), host(out)) <= TOL
+            assert kvh.seq_len == L + 1 + t
+            np.testing.assert_array_equal(host(V[:, :, L + t]), host(V2[:, :, L + t]))
+            kh = I.bf16_bits_to_f32(host(K[:, :, L + t]))
+            kd = I.bf16_bits_to_f32(host(K2[:, :, L + t]))
+            assert np.all(np.abs(kh - kd) <= np.abs(kd) * 2.0 ** -8 + 1e-4)
+    finally:
+        ctx.set_host_parts(0, 0)
+        ctx.set_host_direct(True)
+        kvd.close()
