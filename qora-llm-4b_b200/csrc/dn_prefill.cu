@@ -49,12 +49,12 @@ constexpr int kC = 64;  // chunk length (tokens)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // ---------------------------------------------------------------------------
-// prep: one warp per (head-vector, run of 16 tokens, sequence); lane l owns
+// prep: one warp per (head-vector, run of kPrepRun tokens, sequence); lane l owns
 // the 4 channels 4l..4l+3 of the 128-channel head-vector (8-byte bf16 loads,
 // the conv history of those channels kept in registers along the run).
 // head-vectors 0..15 = q heads, 16..31 = k heads, 32..63 = v heads
 // ---------------------------------------------------------------------------
-constexpr int kPrepRun = 16;
+constexpr int kPrepRun = 12;  // tokens a warp (16: 0.65 ms on workload 2, 12 with 7 CTAs an SM: 0.62)
 constexpr int kPrepWarps = 4;  // warps per CTA
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
@@ -70,7 +70,7 @@ __device__ __forceinline__ float4 bf16x4_to_f32(uint2 u) {
                        __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
 }
 
-__global__ void __launch_bounds__(32 * kPrepWarps)
+__global__ void __launch_bounds__(32 * kPrepWarps, 7)
 dn_prefill_prep(const uint16_t* __restrict__ qkv, const float* __restrict__ a_in,
                 const float* __restrict__ b_in, const float* __restrict__ conv_w,
                 const float* __restrict__ a_log, const float* __restrict__ dt_bias,
