@@ -29,9 +29,9 @@
 // group) or 32 bytes of f16 (16 columns) per row.  Partial sums: the two
 // half-warps by shuffle, the 8 warps in shared memory, the CTAs of a tile
 // through a global scratch area: each CTA stores its partial, and the last
-// CTA of the tile to finish (a counter) adds all of them in part order and
-// writes y.  Every sum is in a fixed order: the result does not depend on
-// timing.  BT <= 4 sequences per launch; larger batches run in groups of 4.
+// CTA of the tile to finish (a counter) adds them (each warp a contiguous
+// eighth of the parts, then the warps in order) and writes y.  Every sum is
+// in a fixed order: the result does not depend on timing.  BT <= 4 sequences per launch; larger batches run in groups of 4.
 //
 // Q4 nibble without a shift or a conversion: the nibble q at bit 4j of a
 // 16-bit half of the word, masked in place and read as a float, is the
@@ -64,11 +64,13 @@ struct GvShape {
     static constexpr int pad = cpl + 4;       // shared-memory stride of a lane's columns
 };
 
-// rows in flight per stream (the most that fit 2 CTAs per SM without spills at
-// BT <= 2: Q4 takes 5 registers a row, F16 8)
+// rows in flight per stream (Q4 takes 5 registers a row, F16 8; at most what
+// fits 2 CTAs per SM without spills).  Measured at batch 1 over the 32 layers'
+// projections: Q4 6 rows 0.467 ms, 8 rows 0.472, 10-12 rows 0.489; F16 8 rows
+// 0.552, 6 rows 0.559, 12 rows 0.569
 template <bool Q4, int BT>
 struct GvDepth {
-    static constexpr int rows = BT == 1 ? 8 : (BT == 2 ? 6 : 4);
+    static constexpr int rows = BT == 1 ? (Q4 ? 6 : 8) : (BT == 2 ? 6 : 4);
 };
 
 struct GvJob {
